@@ -1,0 +1,381 @@
+"""Benchmark of the B200 int8 LM GEMM path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of one Qwen3-0.6B-shaped decoder layer's int8 linear set
+(q/k/v, o, gate/up, down with their RMSNorm/SiLU quantisers) over one batch
+of M = 2 x 200 tokens (a CFG pair), the int8 branch of LM::run_layer
+(cpp/src/model/lm.cpp:217-322) without attention.  Consecutive steps walk
+through 28 distinct random-init layers (440 MB of int8 weights, > L2), as a
+forward pass does, so every step's weights come from HBM.
+
+Metric: int8 tera-ops/s, ops = 2 * M * sum(N*K) = 12.58 G per step.  Under
+torchrun each rank runs the same per-GPU workload (utterance-parallel data
+parallelism: no data-path collective) and `value` is the whole-job total.
+
+`--impl reference` times the reference's own CPU implementation of the same
+layer step (oracle/_ref, built from the reference's sources) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_TOKENS = 400
+N_LAYERS = 28
+METRIC = "int8 LM GEMM TOPS (one decoder layer's linear set, M=2x200)"
+WORKLOAD = "config1: Qwen3-0.6B-shaped decoder layer linear set, int8, M=400"
+
+
+def env_int(k, d):
+    v = os.environ.get(k)
+    return int(v) if v not in (None, "") else d
+
+
+def config(world: int) -> dict:
+    return {
+        "workload": WORKLOAD,
+        "tokens_per_step": M_TOKENS,
+        "hidden": 1024, "qkv": "2048|1024|1024", "o": "2048->1024", "gate_up": "3072|3072",
+        "down": "3072->1024",
+        "layers_rotated": N_LAYERS,
+        "weights": "random int8 uniform[-127,127], scale |N(0,0.02)|/127, RMSNorm gains 1",
+        "l2": "inputs larger than L2: each step reads a different layer's 15.7 MB of weights, "
+              "28 layers = 440 MB",
+        "parallelism": f"dp{world} (utterance sharding, no collectives)",
+        "attention": "out of scope; o_proj consumes the q projection (identity stand-in)",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every `period` s."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report why, keep running
+            self.error = str(e)
+        self.period = period
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t.is_alive():
+            self._t.join()
+
+    def summary(self) -> dict:
+        names = sorted(k for k, bit in self.REASONS.items() if self.reasons & bit)
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        if self.error:
+            out["error"] = self.error
+        return out
+
+
+# --------------------------------------------------------------- roofline
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic() -> float | None:
+    """DRAM bytes per launch of the dominant GEMM from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gemm_gate_up_m400_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    return None
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import layer as LY
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    rng = np.random.default_rng(1000)
+    layers = [LY.LayerWeights.from_host(LY.random_layer_host(rng), dev) for _ in range(N_LAYERS)]
+    buf = LY.LayerBuffers(M_TOKENS, dev)
+    x0 = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32)).to(dev)
+    x = x0.clone()
+    ops_step = M_TOKENS * LY.ops_per_token()
+
+    # Eager warm-up sets the kernels' shared-memory attributes before capture.
+    for lw in layers[:2]:
+        LY.run(x, lw, buf)
+    torch.cuda.synchronize()
+    if ovb.device_status() != 0:
+        raise RuntimeError("device wait timed out during warm-up")
+
+    stream = torch.cuda.Stream(device=dev)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for lw in layers:  # one graph per layer step
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                LY.run(x, lw, buf)
+            graphs.append(g)
+        chain = torch.cuda.CUDAGraph()  # all 28 steps; x reset first (one 1.6 MB copy)
+        with torch.cuda.graph(chain, stream=stream):
+            x.copy_(x0)
+            for lw in layers:
+                LY.run(x, lw, buf)
+
+    def run_steps(n):
+        full, rest = divmod(n, N_LAYERS)
+        for _ in range(full):
+            chain.replay()
+        for i in range(rest):
+            graphs[i].replay()
+
+    with torch.cuda.stream(stream):
+        run_steps(args.warmup)
+    torch.cuda.synchronize()
+
+    # ---- timed region: exactly K steps
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            run_steps(args.steps)
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * args.steps * ops_step / (ms_max * 1e-3) / 1e12
+
+    # ---- dominant kernel, timed live: the gate|up sliced GEMM (N=6144, K=1024)
+    n_launch = max(N_LAYERS * 4, 112)
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    aq, asc = buf.qh
+    with torch.cuda.stream(stream):
+        ovb.rmsnorm_quantize_f32(x0, layers[0].post_ln, LY.RMS_EPS, out=buf.qh)
+        for i in range(N_LAYERS):  # warm
+            ovb.linear_s8_nk_packed_q_sliced(aq, asc, layers[i].gate_up, [buf.gate, buf.up])
+        k0.record(stream)
+        for i in range(n_launch):
+            ovb.linear_s8_nk_packed_q_sliced(aq, asc, layers[i % N_LAYERS].gate_up,
+                                             [buf.gate, buf.up])
+        k1.record(stream)
+    torch.cuda.synchronize()
+    gemm_us = k0.elapsed_time(k1) * 1e3 / n_launch
+    peaks = load_peaks()
+    N_gu, K_gu = 2 * LY.INTER, LY.HIDDEN
+    Kb = K_gu // 32
+    alg_bytes = (M_TOKENS * K_gu + M_TOKENS * Kb * 4 + N_gu * K_gu + N_gu * 4
+                 + M_TOKENS * N_gu * 4)
+    gemm_ops = 2 * M_TOKENS * N_gu * K_gu
+    achieved_gbs = alg_bytes / (gemm_us * 1e-6) / 1e9
+    # int8 MMA peak taken as 2x the measured dense bf16 rate (same tensor
+    # pipe, half the operand width); the HBM bound is the larger time here.
+    t_hbm = alg_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_int8 = gemm_ops / (2 * peaks["bf16_tflops"] * 1e12)
+    roofline = {
+        "kernel": "gemm_s8_tc (gate|up sliced, M=400, N=6144, K=1024)",
+        "bound": "hbm" if t_hbm >= t_int8 else "tensor",
+        "achieved": round(achieved_gbs, 1),
+        "peak": peaks["hbm_gbs"],
+        "unit": "GB/s",
+        "frac": round(achieved_gbs / peaks["hbm_gbs"], 4),
+        "peak_source": peaks["source"],
+        "algorithmic_bytes": alg_bytes,
+        "us_per_launch": round(gemm_us, 3),
+        "tensor_tops": round(gemm_ops / (gemm_us * 1e-6) / 1e12, 1),
+        "tensor_frac_of_2x_bf16": round(gemm_ops / (gemm_us * 1e-6) / 1e12
+                                        / (2 * peaks["bf16_tflops"]), 4),
+        "roofline_us": round(max(t_hbm, t_int8) * 1e6, 3),
+        "traffic": load_traffic(),
+    }
+
+    # ---- end to end through the public API with host buffers
+    xh_in = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
+    xh_in = xh_in.pin_memory()
+    xh_out = torch.empty_like(xh_in).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            x.copy_(xh_in, non_blocking=True)
+            graphs[i % N_LAYERS].replay()
+            xh_out.copy_(x, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    io_bytes = M_TOKENS * LY.HIDDEN * 4
+    e2e = {"value": world * args.steps * ops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+           "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
+           "ms_per_step": e2e_ms / args.steps}
+
+    status = ovb.device_status()
+    for g in graphs + [chain]:
+        g.reset()
+    if world > 1:
+        dist.destroy_process_group()
+    if status != 0:
+        raise RuntimeError(f"bounded device wait timed out (status {status})")
+
+    if rank != 0:
+        return None
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        import oracle.cpu_baseline as CB
+        r = CB.run(M=M_TOKENS, layers=4, budget_s=args.cpu_seconds)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 (s8 x s8 -> s32 per 32-k block, fp32 epilogue)",
+        "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
+        "config": config(world),
+        "impl": "ours",
+        "e2e": e2e,
+        "gpu_launches": args.steps * LY.KERNELS_PER_LAYER,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+    }
+
+
+# ---------------------------------------------------------- reference arm
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    import oracle.cpu_baseline as CB
+    # Bounded sample: at most K steps, at most ~budget seconds of CPU time.
+    r = CB.run(M=M_TOKENS, layers=4, max_steps=args.steps, budget_s=args.ref_seconds,
+               warmup=min(args.warmup, 3))
+    return {
+        "metric": METRIC,
+        "value": r["value"],
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": r["steps"],
+        "warmup": min(args.warmup, 3),
+        "ms_per_step": r["seconds"] * 1e3 / max(r["steps"], 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 (u8 x s8 VNNI per 32-k block, fp32 epilogue)",
+        "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
+        "config": config(world),
+        "impl": "reference",
+        "cpu_baseline": {"value": r["value"], "unit": "TOPS", "cores": r["cores"],
+                         "kind": r["kind"], "sample": r["sample"]},
+        "e2e": {"value": r["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=28000)
+    ap.add_argument("--warmup", type=int, default=280)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out = run_ours(args, rank, world, local_rank)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/* ovb200.h -- C ABI of the B200-native int8 LM GEMM path for OVNative.
+ *
+ * This library replaces, for the int8 LM projections only, the per-GEMM
+ * entry points of the reference's backend contract
+ * (cpp/include/ovnative/ov_gemm.h, namespace ov) and the cuBLAS calls of
+ * its CUDA LM runner (cpp/src/backend/cuda/cuda_lm.cu:984-989, :1023-1030).
+ * Every compute entry point takes DEVICE pointers and a cudaStream_t (passed
+ * as void*) and is stream-ordered; nothing here synchronises the device except
+ * ovb_weight_create/ovb_weight_concat/ovb_weight_destroy.
+ *
+ * Numerics are those of the reference's CPU AVX-VNNI path
+ * (cpp/src/backend/cpu/gemm.cpp:379-882, cpp/src/backend/cpu/ops_cpu.cpp:75-198):
+ *   - activations are quantised per row per 32-k block:
+ *       amax = max|a|, asc = amax/127, q = rne(a * (127/amax)) clamped to +-127;
+ *   - each 32-k block product P_b = sum q*w is an exact int32;
+ *   - the fp32 result is f = fma(P_b, asc_b, f) over b in order, then
+ *     o = f * wscale[n], then o = o + C_old when accumulating.
+ *   Following that order makes the fp32 output bit-identical to the
+ *   reference's.
+ *
+ * Activation buffers ("aq/asc"):
+ *   aq  : int8 q, row-major [M, Kp], Kp = 32*ceil(K/32), tail bytes zero.
+ *         With OVB_AQ_U8 a quantiser writes the reference's u8 form instead
+ *         (q + 128, tail bytes zero; gemm.cpp:423-427) -- for byte comparison
+ *         only, the GEMMs consume the int8 form.
+ *   asc : fp32 row-major [M, Kb], Kb = ceil(K/32).
+ *   Sizes: ovb_quant_bytes(M, K) bytes and ovb_quant_scales(M, K) floats
+ *   (s8_nk_quant_bytes / s8_nk_quant_scales, ov_gemm.h:95-96).
+ *
+ * Error convention (mirrors ovnative.h:19-23): every call returns OVB_OK or
+ * a negative status and leaves a message in ovb_last_error() (thread-local).
+ * Like the reference, M, N or K <= 0 is a no-op that returns OVB_OK
+ * (gemm.cpp:761, :779, :832).
+ *
+ * Thread safety: one weight handle may be used from several threads and
+ * streams at once (it is read-only after creation).  Calls that share output
+ * buffers must be ordered by the caller, as with the reference.
+ */
+#ifndef OVB200_H
+#define OVB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OVB_ABI_VERSION 1
+
+/* status codes: same values as OV_OK / OV_ERR_INVALID_ARG / OV_ERR_INTERNAL */
+#define OVB_OK 0
+#define OVB_ERR_INVALID_ARG (-1)
+#define OVB_ERR_INTERNAL (-4)
+
+/* weight layouts (OVW1 descriptor `layout`, weight-format.en.md / mat.cpp:69-106) */
+#define OVB_LAYOUT_NK 0 /* [N, K], one scale per output row (layout=0) */
+#define OVB_LAYOUT_KN 1 /* [K, N], one scale per output column (layout=1) */
+
+/* flags */
+#define OVB_SRC_DEVICE 1 /* ovb_weight_create: W and scale are device pointers */
+#define OVB_AQ_U8 1      /* quantisers: write reference u8 (q+128) instead of int8 */
+
+typedef struct ovb_weight ovb_weight;
+
+/* One output slice of a concatenated weight (ov::S8NkSlice, ov_gemm.h:105-108),
+ * with an explicit row stride for C. */
+typedef struct ovb_slice {
+  int64_t N;   /* columns of this slice, a positive multiple of 64 */
+  float* C;    /* device [M, ldc] */
+  int64_t ldc; /* >= N */
+} ovb_slice;
+
+int ovb_abi_version(void);
+const char* ovb_last_error(void);
+
+/* Per-launch device status of the last GEMM on this thread's device: 0 when
+ * every bounded wait inside the kernels completed.  Reading it synchronises
+ * the given stream. */
+int ovb_device_status(void* stream);
+
+/* --- sizes ------------------------------------------------------------ */
+/* replaces ov::s8_nk_quant_bytes (ov_gemm.h:95) */
+int64_t ovb_quant_bytes(int64_t M, int64_t K);
+/* replaces ov::s8_nk_quant_scales (ov_gemm.h:96) */
+int64_t ovb_quant_scales(int64_t M, int64_t K);
+
+/* --- weights ---------------------------------------------------------- */
+/* Build a device-resident weight from an int8 matrix in either OVW1 layout
+ * and its per-output-channel fp32 scale (N floats).  Replaces the load-time
+ * ov::s8_nk_pack (ov_gemm.h:60-63, gemm.cpp:584-621) and the CUDA runner's
+ * dequantise-at-load (cuda_lm.cu:840-873).  Host sources (the OVW1 mmap) are
+ * borrowed for the call only.  Synchronous. */
+int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const float* scale,
+                      int flags, void* stream, ovb_weight** out);
+/* Concatenate weights with the same K along N (q|k|v, gate|up).  Replaces
+ * combine_packed (lm.cpp:57-94).  The parts stay valid. */
+int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
+                      ovb_weight** out);
+int ovb_weight_destroy(ovb_weight* w);
+int ovb_weight_shape(const ovb_weight* w, int64_t* N, int64_t* K);
+/* Copy the device weight back as [N, K] int8 and its N scales (host pointers);
+ * used by tests to check the packers. */
+int ovb_weight_export(const ovb_weight* w, int8_t* W_nk, float* scale);
+
+/* --- activation quantisers (device pointers) --------------------------- */
+/* replaces ov::s8_nk_quantize (ov_gemm.h:97; gemm.cpp:379-430, :709-720).
+ * A is [M, K] with row stride lda >= K. */
+int ovb_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq, float* asc,
+                 int flags, void* stream);
+/* replaces ov::rmsnorm_quantize_f32 (ov_gemm.h:118-119; gemm.cpp:638-707) */
+int ovb_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w, float eps,
+                         void* aq, float* asc, int flags, void* stream);
+/* replaces ov::silu_mul_quantize_f32 (ov_gemm.h:84-85; ops_cpu.cpp:144-198,
+ * :1138-1168).  gate/up are [M, K] with row strides ldg / ldu. */
+int ovb_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
+                          const float* up, int64_t ldu, void* aq, float* asc, int flags,
+                          void* stream);
+
+/* --- GEMMs (device pointers) ------------------------------------------ */
+/* C[m, n] (+)= linear(aq, asc) with w.  accumulate = 0 replaces
+ * ov::linear_s8_nk_packed_q (ov_gemm.h:98-100); accumulate = 1 replaces
+ * ov::linear_s8_nk_packed_q_add (ov_gemm.h:78-80).  C is [M, ldc]. */
+int ovb_linear_q(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc, float* C,
+                 int64_t ldc, int accumulate, void* stream);
+/* One launch over a concatenated weight writing each slice to its own C.
+ * Replaces ov::linear_s8_nk_packed_q_sliced (ov_gemm.h:109-111). */
+int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
+                        const ovb_slice* slices, int n_slices, void* stream);
+/* fp32 activations in, quantised inside (two launches).  accumulate = 0
+ * replaces ov::linear_s8_nk_packed (ov_gemm.h:67-69); accumulate = 1
+ * replaces ov::linear_s8_nk_packed_add (ov_gemm.h:73-75).  `work` is a device
+ * scratch of at least ovb_linear_workspace_bytes(M, K) bytes, 256-byte
+ * aligned, owned by the caller (the reference's thread-local aq/asc vectors,
+ * gemm.cpp:835-839). */
+size_t ovb_linear_workspace_bytes(int64_t M, int64_t K);
+int ovb_linear(int64_t M, const ovb_weight* w, const float* A, int64_t lda, float* C,
+               int64_t ldc, int accumulate, void* work, size_t work_bytes, void* stream);
+
+/* Exact per-32-k block products P[m, n, b] (int32 [M, N, Kb]) of the same
+ * tensor-core mainloop, for parity checks of the integer arithmetic. */
+int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t* P,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OVB200_H */

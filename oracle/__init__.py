@@ -1,0 +1,314 @@
+"""CPU checkers for the int8 LM GEMM path.  TEST INFRASTRUCTURE ONLY.
+
+Two checkers live here, both driven through ctypes with numpy arrays:
+
+* ``port``  -- liboracle.so, the scalar C restatement in ovb_oracle.c of the
+  reference's CPU int8 path (cpp/src/backend/cpu/gemm.cpp:379-882 and
+  cpp/src/backend/cpu/ops_cpu.cpp:75-198).  Always available once built.
+* ``ref``   -- _ref/libovref.so, the reference's own gemm.cpp/ops_cpu.cpp
+  compiled from source by oracle/Makefile.  Its int8 quantised path needs an
+  AVX-VNNI host (cpu_vnni_available(), gemm.cpp:556-572); ``ref_vnni()`` says
+  whether it can run here.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this package.  The product (ovnative_b200) never does.
+
+Activation format of both checkers is the reference's: aq = u8 (q + 128)
+[M, Kb*32] with zero tail bytes, asc = fp32 [M, Kb], Kb = ceil(K/32).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_PORT_PATH = os.path.join(_HERE, "liboracle.so")
+_REF_PATH = os.path.join(_HERE, "_ref", "libovref.so")
+
+_i64 = C.c_int64
+_p = C.c_void_p
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data
+
+
+def kblocks(K: int) -> int:
+    return (K + 31) // 32
+
+
+# --------------------------------------------------------------------- port
+_port = None
+
+
+def port_lib():
+    global _port
+    if _port is None:
+        if not os.path.exists(_PORT_PATH):
+            raise RuntimeError(f"oracle port not built: {_PORT_PATH} (run make -C oracle)")
+        lib = C.CDLL(_PORT_PATH)
+        for name, args in {
+            "ovo_quantize_u8": [_i64, _i64, _p, _p, _p],
+            "ovo_rmsnorm_quantize_u8": [_i64, _i64, _p, _p, C.c_float, _p, _p],
+            "ovo_silu_mul_quantize_u8": [_i64, _i64, _p, _p, _p, _p],
+            "ovo_block_products": [_i64, _i64, _i64, _p, _p, _p],
+            "ovo_linear_q": [_i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, C.c_int],
+            "ovo_rmsnorm_into": [_p, _p, _p, _i64, _i64, C.c_float],
+            "ovo_silu_mul": [_p, _p, _p, _i64],
+        }.items():
+            f = getattr(lib, name)
+            f.argtypes = args
+            f.restype = None
+        _port = lib
+    return _port
+
+
+def _quant_out(M: int, K: int):
+    Kb = kblocks(K)
+    return np.zeros((M, Kb * 32), np.uint8), np.zeros((M, Kb), np.float32)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def quantize(A: np.ndarray):
+    """quantize_a_u8 (gemm.cpp:379-430) -> (aq u8 [M,Kp], asc f32 [M,Kb])."""
+    A = _f32(A)
+    M, K = A.shape
+    aq, asc = _quant_out(M, K)
+    port_lib().ovo_quantize_u8(M, K, _ptr(A), _ptr(aq), _ptr(asc))
+    return aq, asc
+
+
+def rmsnorm_quantize(x: np.ndarray, w: np.ndarray, eps: float):
+    """rmsnorm_quantize_avx2 (gemm.cpp:638-707)."""
+    x, w = _f32(x), _f32(w)
+    M, K = x.shape
+    aq, asc = _quant_out(M, K)
+    port_lib().ovo_rmsnorm_quantize_u8(M, K, _ptr(x), _ptr(w), eps, _ptr(aq), _ptr(asc))
+    return aq, asc
+
+
+def silu_mul_quantize(gate: np.ndarray, up: np.ndarray):
+    """silu_mul_quant_avx2 (ops_cpu.cpp:144-198)."""
+    gate, up = _f32(gate), _f32(up)
+    M, K = gate.shape
+    aq, asc = _quant_out(M, K)
+    port_lib().ovo_silu_mul_quantize_u8(M, K, _ptr(gate), _ptr(up), _ptr(aq), _ptr(asc))
+    return aq, asc
+
+
+def block_products(aq: np.ndarray, W_nk: np.ndarray, K: int) -> np.ndarray:
+    """Exact per-32-k int32 products P[m, n, b] (gemm.cpp:455-474)."""
+    aq = np.ascontiguousarray(aq, np.uint8)
+    W_nk = np.ascontiguousarray(W_nk, np.int8)
+    M, N = aq.shape[0], W_nk.shape[0]
+    P = np.zeros((M, N, kblocks(K)), np.int32)
+    port_lib().ovo_block_products(M, N, K, _ptr(aq), _ptr(W_nk), _ptr(P))
+    return P
+
+
+def linear_q(aq, asc, W_nk, wscale, K: int, C_in=None) -> np.ndarray:
+    """linear_s8_nk_packed_q / _q_add semantics (gemm.cpp:432-504).
+
+    W_nk is the [N, K] int8 weight, wscale its per-output-row scale.  With
+    C_in the result is added to it (residual epilogue)."""
+    aq = np.ascontiguousarray(aq, np.uint8)
+    asc = _f32(asc)
+    W_nk = np.ascontiguousarray(W_nk, np.int8)
+    wscale = _f32(wscale)
+    M, N = aq.shape[0], W_nk.shape[0]
+    if C_in is None:
+        out = np.zeros((M, N), np.float32)
+        acc = 0
+    else:
+        out = _f32(C_in).copy()
+        acc = 1
+    port_lib().ovo_linear_q(M, N, K, _ptr(aq), _ptr(asc), _ptr(W_nk), _ptr(wscale), _ptr(out), N,
+                            acc)
+    return out
+
+
+def rmsnorm_into(x, w, eps: float) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    port_lib().ovo_rmsnorm_into(_ptr(out), _ptr(x), _ptr(w), x.shape[0], x.shape[1], eps)
+    return out
+
+
+def silu_mul(gate, up) -> np.ndarray:
+    gate, up = _f32(gate), _f32(up)
+    out = np.empty_like(gate)
+    port_lib().ovo_silu_mul(_ptr(out), _ptr(gate), _ptr(up), gate.size)
+    return out
+
+
+# ---------------------------------------------------------------- reference
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(_REF_PATH)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise RuntimeError(f"reference library not built: {_REF_PATH}")
+        lib = C.CDLL(_REF_PATH)
+        sig = {
+            "ref_vnni_available": ([], C.c_int),
+            "ref_kernel_name": ([], C.c_char_p),
+            "ref_packed_bytes": ([_i64, _i64], _i64),
+            "ref_wsum_elems": ([_i64, _i64], _i64),
+            "ref_s8_nk_pack": ([_i64, _i64, _p, _p, _p], C.c_int),
+            "ref_s8_nk_quantize": ([_i64, _i64, _p, _p, _p], C.c_int),
+            "ref_rmsnorm_quantize": ([_i64, _i64, _p, _p, C.c_float, _p, _p], C.c_int),
+            "ref_silu_mul_quantize": ([_i64, _i64, _p, _p, _p, _p], C.c_int),
+            "ref_rmsnorm_into": ([_p, _p, _p, _i64, _i64, C.c_float], C.c_int),
+            "ref_silu_mul": ([_p, _p, _p, _i64], C.c_int),
+            "ref_linear_packed_q": ([_i64, _i64, _i64, _p, _p, _p, _p, _p, _p], C.c_int),
+            "ref_linear_packed_q_add": ([_i64, _i64, _i64, _p, _p, _p, _p, _p, _p], C.c_int),
+            "ref_linear_packed": ([_i64, _i64, _i64, _p, _p, _p, _p, _p], C.c_int),
+            "ref_linear_packed_add": ([_i64, _i64, _i64, _p, _p, _p, _p, _p], C.c_int),
+            "ref_linear_packed_q_sliced": ([_i64, _i64, _p, _p, _p, _p, _p, _p, _p, C.c_int],
+                                           C.c_int),
+            "ref_linear_s8_nk": ([_i64, _i64, _i64, _p, _p, _p, _p], C.c_int),
+        }
+        for name, (args, res) in sig.items():
+            f = getattr(lib, name)
+            f.argtypes = args
+            f.restype = res
+        _ref = lib
+    return _ref
+
+
+def ref_vnni() -> bool:
+    return ref_available() and bool(ref_lib().ref_vnni_available())
+
+
+def _chk(rc: int, what: str):
+    if rc != 0:
+        raise RuntimeError(f"reference {what} raised (AVX-VNNI missing or bad arguments)")
+
+
+class RefPacked:
+    """A [N, K] int8 weight packed by the reference's s8_nk_pack (gemm.cpp:584-621)."""
+
+    def __init__(self, W_nk: np.ndarray, wscale: np.ndarray):
+        lib = ref_lib()
+        self.W = np.ascontiguousarray(W_nk, np.int8)
+        self.N, self.K = self.W.shape
+        self.scale = _f32(wscale)
+        self.packed = np.zeros(lib.ref_packed_bytes(self.N, self.K), np.int8)
+        self.wsum = np.zeros(lib.ref_wsum_elems(self.N, self.K), np.int32)
+        _chk(lib.ref_s8_nk_pack(self.N, self.K, _ptr(self.W), _ptr(self.packed), _ptr(self.wsum)),
+             "s8_nk_pack")
+
+    def linear_q(self, aq, asc, C_in=None) -> np.ndarray:
+        aq = np.ascontiguousarray(aq, np.uint8)
+        asc = _f32(asc)
+        M = aq.shape[0]
+        lib = ref_lib()
+        if C_in is None:
+            out = np.zeros((M, self.N), np.float32)
+            _chk(lib.ref_linear_packed_q(M, self.N, self.K, _ptr(aq), _ptr(asc), _ptr(self.packed),
+                                         _ptr(self.wsum), _ptr(self.scale), _ptr(out)),
+                 "linear_s8_nk_packed_q")
+        else:
+            out = _f32(C_in).copy()
+            _chk(lib.ref_linear_packed_q_add(M, self.N, self.K, _ptr(aq), _ptr(asc),
+                                             _ptr(self.packed), _ptr(self.wsum), _ptr(self.scale),
+                                             _ptr(out)), "linear_s8_nk_packed_q_add")
+        return out
+
+    def linear(self, A, C_in=None) -> np.ndarray:
+        A = _f32(A)
+        M = A.shape[0]
+        lib = ref_lib()
+        if C_in is None:
+            out = np.zeros((M, self.N), np.float32)
+            _chk(lib.ref_linear_packed(M, self.N, self.K, _ptr(A), _ptr(self.packed),
+                                       _ptr(self.wsum), _ptr(self.scale), _ptr(out)),
+                 "linear_s8_nk_packed")
+        else:
+            out = _f32(C_in).copy()
+            _chk(lib.ref_linear_packed_add(M, self.N, self.K, _ptr(A), _ptr(self.packed),
+                                           _ptr(self.wsum), _ptr(self.scale), _ptr(out)),
+                 "linear_s8_nk_packed_add")
+        return out
+
+
+def ref_concat(parts: list[RefPacked]) -> RefPacked:
+    """combine_packed (lm.cpp:57-94): tiles concatenate, wsum interleaves per block."""
+    c = RefPacked.__new__(RefPacked)
+    c.W = np.concatenate([p.W for p in parts], 0)
+    c.N, c.K = c.W.shape
+    c.scale = np.concatenate([p.scale for p in parts])
+    c.packed = np.concatenate([p.packed for p in parts])
+    Kb = kblocks(c.K)
+    npads = [(p.N + 7) // 8 * 8 for p in parts]
+    c.wsum = np.concatenate([p.wsum.reshape(Kb, npad) for p, npad in zip(parts, npads)],
+                            1).reshape(-1).copy()
+    return c
+
+
+def ref_linear_q_sliced(packed: RefPacked, Ns: list[int], aq, asc) -> list[np.ndarray]:
+    aq = np.ascontiguousarray(aq, np.uint8)
+    asc = _f32(asc)
+    M = aq.shape[0]
+    outs = [np.zeros((M, n), np.float32) for n in Ns]
+    ns = (C.c_int64 * len(Ns))(*Ns)
+    cs = (C.c_void_p * len(Ns))(*[o.ctypes.data for o in outs])
+    _chk(ref_lib().ref_linear_packed_q_sliced(M, packed.K, _ptr(aq), _ptr(asc),
+                                              _ptr(packed.packed), _ptr(packed.wsum),
+                                              _ptr(packed.scale), C.cast(ns, C.c_void_p),
+                                              C.cast(cs, C.c_void_p), len(Ns)),
+         "linear_s8_nk_packed_q_sliced")
+    return outs
+
+
+def ref_quantize(A):
+    A = _f32(A)
+    M, K = A.shape
+    aq, asc = _quant_out(M, K)
+    _chk(ref_lib().ref_s8_nk_quantize(M, K, _ptr(A), _ptr(aq), _ptr(asc)), "s8_nk_quantize")
+    return aq, asc
+
+
+def ref_rmsnorm_quantize(x, w, eps: float):
+    x, w = _f32(x), _f32(w)
+    M, K = x.shape
+    aq, asc = _quant_out(M, K)
+    _chk(ref_lib().ref_rmsnorm_quantize(M, K, _ptr(x), _ptr(w), eps, _ptr(aq), _ptr(asc)),
+         "rmsnorm_quantize_f32")
+    return aq, asc
+
+
+def ref_silu_mul_quantize(gate, up):
+    gate, up = _f32(gate), _f32(up)
+    M, K = gate.shape
+    aq, asc = _quant_out(M, K)
+    _chk(ref_lib().ref_silu_mul_quantize(M, K, _ptr(gate), _ptr(up), _ptr(aq), _ptr(asc)),
+         "silu_mul_quantize_f32")
+    return aq, asc
+
+
+def ref_rmsnorm_into(x, w, eps: float):
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    _chk(ref_lib().ref_rmsnorm_into(_ptr(out), _ptr(x), _ptr(w), x.shape[0], x.shape[1], eps),
+         "rmsnorm_into_f32")
+    return out
+
+
+def ref_silu_mul(gate, up):
+    gate, up = _f32(gate), _f32(up)
+    out = np.empty_like(gate)
+    _chk(ref_lib().ref_silu_mul(_ptr(out), _ptr(gate), _ptr(up), gate.size), "silu_mul_f32")
+    return out

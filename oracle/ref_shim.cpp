@@ -1,0 +1,107 @@
+// ref_shim.cpp -- extern "C" entry points over the reference's own CPU GEMM
+// path, so Python tests can call it through ctypes.
+//
+// TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
+// the reference sources cpp/src/backend/cpu/gemm.cpp and ops_cpu.cpp (read in
+// place from the reference checkout, never copied) into oracle/_ref/libovref.so.
+// Each wrapper forwards to the ov:: function named in its comment
+// (declared in cpp/include/ovnative/ov_gemm.h and cpp/src/model/ops.h) and turns
+// C++ exceptions into a non-zero return.
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <vector>
+
+#include "model/ops.h"
+#include "ovnative/ov_gemm.h"
+
+#define REF_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception&) {
+    return 1;
+  }
+}
+}  // namespace
+
+REF_API int ref_vnni_available() { return ov::cpu_vnni_available() ? 1 : 0; }
+REF_API const char* ref_kernel_name() { return ov::cpu_kernel_name(); }
+REF_API int64_t ref_packed_bytes(int64_t N, int64_t K) { return ov::s8_nk_packed_bytes(N, K); }
+REF_API int64_t ref_wsum_elems(int64_t N, int64_t K) { return ov::s8_nk_wsum_elems(N, K); }
+
+// ov::s8_nk_pack (gemm.cpp:584-621)
+REF_API int ref_s8_nk_pack(int64_t N, int64_t K, const int8_t* W, int8_t* packed, int32_t* wsum) {
+  return guard([&] { ov::s8_nk_pack(N, K, W, packed, wsum); });
+}
+// ov::s8_nk_quantize (gemm.cpp:709-720)
+REF_API int ref_s8_nk_quantize(int64_t M, int64_t K, const float* A, uint8_t* aq, float* asc) {
+  return guard([&] { ov::s8_nk_quantize(M, K, A, aq, asc); });
+}
+// ov::rmsnorm_quantize_f32 (gemm.cpp:722-756)
+REF_API int ref_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
+                                 float eps, uint8_t* aq, float* asc) {
+  return guard([&] { ov::rmsnorm_quantize_f32(rows, cols, x, w, eps, aq, asc); });
+}
+// ov::silu_mul_quantize_f32 (ops_cpu.cpp:1138-1168)
+REF_API int ref_silu_mul_quantize(int64_t M, int64_t K, const float* gate, const float* up,
+                                  uint8_t* aq, float* asc) {
+  return guard([&] { ov::silu_mul_quantize_f32(M, K, gate, up, aq, asc); });
+}
+// ov::rmsnorm_into_f32 (ops_cpu.cpp:812-825)
+REF_API int ref_rmsnorm_into(float* dst, const float* src, const float* w, int64_t rows,
+                             int64_t cols, float eps) {
+  return guard([&] { ov::rmsnorm_into_f32(dst, src, w, rows, cols, eps); });
+}
+// ov::silu_mul_f32 (ops_cpu.cpp:834-839)
+REF_API int ref_silu_mul(float* out, const float* gate, const float* up, int64_t n) {
+  return guard([&] { ov::silu_mul_f32(out, gate, up, n); });
+}
+// ov::linear_s8_nk_packed_q (gemm.cpp:758-774)
+REF_API int ref_linear_packed_q(int64_t M, int64_t N, int64_t K, const uint8_t* aq,
+                                const float* asc, const int8_t* packed, const int32_t* wsum,
+                                const float* scale, float* C) {
+  return guard([&] { ov::linear_s8_nk_packed_q(M, N, K, aq, asc, packed, wsum, scale, C); });
+}
+// ov::linear_s8_nk_packed_q_add (gemm.cpp:847-862)
+REF_API int ref_linear_packed_q_add(int64_t M, int64_t N, int64_t K, const uint8_t* aq,
+                                    const float* asc, const int8_t* packed, const int32_t* wsum,
+                                    const float* scale, float* C) {
+  return guard([&] { ov::linear_s8_nk_packed_q_add(M, N, K, aq, asc, packed, wsum, scale, C); });
+}
+// ov::linear_s8_nk_packed (gemm.cpp:829-845)
+REF_API int ref_linear_packed(int64_t M, int64_t N, int64_t K, const float* A,
+                              const int8_t* packed, const int32_t* wsum, const float* scale,
+                              float* C) {
+  return guard([&] { ov::linear_s8_nk_packed(M, N, K, A, packed, wsum, scale, C); });
+}
+// ov::linear_s8_nk_packed_add (gemm.cpp:864-882)
+REF_API int ref_linear_packed_add(int64_t M, int64_t N, int64_t K, const float* A,
+                                  const int8_t* packed, const int32_t* wsum, const float* scale,
+                                  float* C) {
+  return guard([&] { ov::linear_s8_nk_packed_add(M, N, K, A, packed, wsum, scale, C); });
+}
+// ov::linear_s8_nk_packed_q_sliced (gemm.cpp:776-827); slice i has Ns[i] columns -> Cs[i].
+REF_API int ref_linear_packed_q_sliced(int64_t M, int64_t K, const uint8_t* aq, const float* asc,
+                                       const int8_t* packed, const int32_t* wsum,
+                                       const float* scale, const int64_t* Ns, float* const* Cs,
+                                       int n_slices) {
+  std::vector<ov::S8NkSlice> s(static_cast<size_t>(n_slices));
+  for (int i = 0; i < n_slices; ++i) {
+    s[static_cast<size_t>(i)].N = Ns[i];
+    s[static_cast<size_t>(i)].C = Cs[i];
+  }
+  return guard([&] {
+    ov::linear_s8_nk_packed_q_sliced(M, K, aq, asc, packed, wsum, scale, s.data(), n_slices);
+  });
+}
+// ov::linear_s8_nk (gemm.cpp:923-940): the AVX2 path with unquantised activations
+// that the reference runs on hosts without AVX-VNNI.
+REF_API int ref_linear_s8_nk(int64_t M, int64_t N, int64_t K, const float* A, const int8_t* W,
+                             const float* scale, float* C) {
+  return guard([&] { ov::linear_s8_nk(M, N, K, A, W, scale, C); });
+}

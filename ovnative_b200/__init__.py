@@ -1,0 +1,25 @@
+"""ovnative_b200 -- B200-native int8 LM GEMM path for OVNative.
+
+The product is libovb200.so (CUDA kernels for sm_100a behind the C ABI in
+include/ovb200.h).  This package loads it and mirrors the reference's
+ov_gemm.h interface on torch CUDA tensors (gemm.py), and adds the per-layer
+linear sequence of LM::run_layer (layer.py) used by the benchmark.
+"""
+from ._lib import LIB_PATH, OvbError, lib  # noqa: F401
+from .gemm import (  # noqa: F401
+    Weight,
+    block_products,
+    device_status,
+    empty_quant,
+    linear_s8_nk_packed,
+    linear_s8_nk_packed_add,
+    linear_s8_nk_packed_q,
+    linear_s8_nk_packed_q_add,
+    linear_s8_nk_packed_q_sliced,
+    rmsnorm_quantize_f32,
+    s8_nk_quant_bytes,
+    s8_nk_quant_scales,
+    s8_nk_quantize,
+    silu_mul_quantize_f32,
+    workspace_bytes,
+)

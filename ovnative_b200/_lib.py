@@ -1,0 +1,89 @@
+"""ctypes binding of libovb200.so (the C ABI declared in include/ovb200.h).
+
+The library is loaded from this package directory only; when it is missing
+or fails to load, every entry point raises -- there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libovb200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "ovb200.h")
+
+OVB_OK = 0
+OVB_ERR_INVALID_ARG = -1
+OVB_ERR_INTERNAL = -4
+OVB_LAYOUT_NK = 0
+OVB_LAYOUT_KN = 1
+OVB_SRC_DEVICE = 1
+OVB_AQ_U8 = 1
+
+_i64 = C.c_int64
+_p = C.c_void_p
+_int = C.c_int
+
+
+class Slice(C.Structure):
+    _fields_ = [("N", C.c_int64), ("C", C.c_void_p), ("ldc", C.c_int64)]
+
+
+# name -> (argtypes, restype)
+SIGNATURES = {
+    "ovb_abi_version": ([], _int),
+    "ovb_last_error": ([], C.c_char_p),
+    "ovb_device_status": ([_p], _int),
+    "ovb_quant_bytes": ([_i64, _i64], _i64),
+    "ovb_quant_scales": ([_i64, _i64], _i64),
+    "ovb_weight_create": ([_p, _int, _i64, _i64, _p, _int, _p, C.POINTER(_p)], _int),
+    "ovb_weight_concat": ([_p, _int, _p, C.POINTER(_p)], _int),
+    "ovb_weight_destroy": ([_p], _int),
+    "ovb_weight_shape": ([_p, C.POINTER(_i64), C.POINTER(_i64)], _int),
+    "ovb_weight_export": ([_p, _p, _p], _int),
+    "ovb_quantize": ([_i64, _i64, _p, _i64, _p, _p, _int, _p], _int),
+    "ovb_rmsnorm_quantize": ([_i64, _i64, _p, _p, C.c_float, _p, _p, _int, _p], _int),
+    "ovb_silu_mul_quantize": ([_i64, _i64, _p, _i64, _p, _i64, _p, _p, _int, _p], _int),
+    "ovb_linear_q": ([_i64, _p, _p, _p, _p, _i64, _int, _p], _int),
+    "ovb_linear_q_sliced": ([_i64, _p, _p, _p, C.POINTER(Slice), _int, _p], _int),
+    "ovb_linear_workspace_bytes": ([_i64, _i64], C.c_size_t),
+    "ovb_linear": ([_i64, _p, _p, _i64, _p, _i64, _int, _p, C.c_size_t, _p], _int),
+    "ovb_block_products": ([_i64, _p, _p, _p, _p], _int),
+}
+
+_lib = None
+
+
+class OvbError(RuntimeError):
+    """A non-OK status from the C ABI (OVB_ERR_INTERNAL and friends)."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"ovb status {status}: {msg}")
+        self.status = status
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is not built; run `python -m ovnative_b200.build` "
+                "(the CUDA extension is required, there is no CPU fallback)")
+        h = C.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            f = getattr(h, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = h
+    return _lib
+
+
+def check(status: int) -> None:
+    """Raise like the reference does: ValueError where it throws
+    std::invalid_argument / rejects arguments, RuntimeError otherwise."""
+    if status == OVB_OK:
+        return
+    msg = lib().ovb_last_error().decode(errors="replace")
+    if status == OVB_ERR_INVALID_ARG:
+        raise ValueError(msg)
+    raise OvbError(status, msg)

@@ -1,0 +1,433 @@
+// capi.cpp -- the extern "C" entry points declared in include/ovb200.h:
+// argument checks, weight handles, TMA descriptors, and kernel launches.
+//
+// Error behaviour mirrors the reference contract (ov_gemm.h / gemm.cpp):
+// M, N or K <= 0 is a silent no-op (gemm.cpp:761, :779, :832); a bad
+// argument that the reference rejects with std::invalid_argument /
+// std::runtime_error (e.g. gemm.cpp:786-788 for slice widths) returns
+// OVB_ERR_INVALID_ARG here; CUDA failures return OVB_ERR_INTERNAL.  The
+// message is kept per thread for ovb_last_error().
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ovb200.h"
+#include "ovb_internal.h"
+
+namespace ovb {
+
+namespace {
+thread_local std::string t_error;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+void set_error(const std::string& msg) { t_error = msg; }
+
+bool cuda_failed(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return false;
+  set_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return true;
+}
+
+int num_sms(int device) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  if (device >= static_cast<int>(cache.size())) cache.resize(static_cast<size_t>(device) + 1, 0);
+  if (cache[static_cast<size_t>(device)] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[static_cast<size_t>(device)] = n;
+  }
+  return cache[static_cast<size_t>(device)];
+}
+
+bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
+                    uint64_t stride_bytes, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+    return false;
+  }
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {32u, box_rows};
+  const cuuint32_t elem_strides[2] = {1u, 1u};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                        strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    std::snprintf(buf, sizeof buf,
+                  "cuTensorMapEncodeTiled failed (%d): rows=%llu row_bytes=%llu stride=%llu",
+                  static_cast<int>(r), static_cast<unsigned long long>(rows),
+                  static_cast<unsigned long long>(row_bytes),
+                  static_cast<unsigned long long>(stride_bytes));
+    set_error(buf);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace ovb
+
+using ovb::cuda_failed;
+using ovb::set_error;
+
+namespace {
+
+inline int64_t kblocks(int64_t K) { return (K + 31) / 32; }
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+int invalid(const std::string& msg) {
+  set_error(msg);
+  return OVB_ERR_INVALID_ARG;
+}
+
+int internal_err() { return OVB_ERR_INTERNAL; }
+
+bool ensure_weight_tmap(ovb_weight* w) {
+  if (w->tmap_ready) return true;
+  if (!ovb::encode_tmap_u8(&w->tmap_b, w->w, static_cast<uint64_t>(w->Kp),
+                           static_cast<uint64_t>(w->N), static_cast<uint64_t>(w->Kp),
+                           ovb::kBlockN))
+    return false;
+  w->tmap_ready = true;
+  return true;
+}
+
+// Common checks of a pre-quantised GEMM call.  Returns OVB_OK or a status.
+int check_q_args(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc) {
+  if (!w) return invalid("weight handle is null");
+  if (!aq || !asc) return invalid("aq/asc must be non-null");
+  if (!aligned(aq, 16)) return invalid("aq must be 16-byte aligned (TMA source)");
+  if (!aligned(asc, 4)) return invalid("asc must be 4-byte aligned");
+  if (M > (int64_t{1} << 31) - 1) return invalid("M exceeds 2^31-1");
+  int dev = 0;
+  if (cuda_failed(cudaGetDevice(&dev), "cudaGetDevice")) return OVB_ERR_INTERNAL;
+  if (dev != w->device) return invalid("weight lives on another device than the current one");
+  return OVB_OK;
+}
+
+int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc,
+             const ovb::SliceOut* slices, int n_slices, int accumulate, int32_t* products,
+             cudaStream_t s) {
+  ovb_weight* w = const_cast<ovb_weight*>(wc);
+  if (!ensure_weight_tmap(w)) return OVB_ERR_INTERNAL;
+  CUtensorMap tmap_a;
+  if (!ovb::encode_tmap_u8(&tmap_a, aq, static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(M),
+                           static_cast<uint64_t>(w->Kp), ovb::kBlockM))
+    return OVB_ERR_INTERNAL;
+  ovb::GemmArgs args{};
+  args.M = M;
+  args.N = w->N;
+  args.Kb = w->Kb;
+  args.asc = asc;
+  args.wscale = w->scale;
+  args.accumulate = accumulate;
+  args.n_slices = n_slices;
+  for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
+  args.products = products;
+  if (cuda_failed(ovb::launch_gemm(tmap_a, w->tmap_b, args, s), "gemm launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ovb_abi_version(void) { return OVB_ABI_VERSION; }
+
+const char* ovb_last_error(void) { return ovb::t_error.c_str(); }
+
+int ovb_device_status(void* stream) {
+  int st = 0;
+  if (cuda_failed(ovb::read_and_clear_status(&st, as_stream(stream)), "read device status"))
+    return OVB_ERR_INTERNAL;
+  return st;
+}
+
+int64_t ovb_quant_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return M * kblocks(K) * 32;
+}
+
+int64_t ovb_quant_scales(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return M * kblocks(K);
+}
+
+// ---------------------------------------------------------------- weights
+int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const float* scale,
+                      int flags, void* stream, ovb_weight** out) {
+  if (!out) return invalid("out is null");
+  *out = nullptr;
+  if (N <= 0 || K <= 0) return invalid("weight shape must be positive");
+  if (!W || !scale) return invalid("W/scale must be non-null");
+  if (layout != OVB_LAYOUT_NK && layout != OVB_LAYOUT_KN) return invalid("unknown layout");
+  if (N > (int64_t{1} << 31) - 1 || K > (int64_t{1} << 30))
+    return invalid("weight dimensions too large");
+  cudaStream_t s = as_stream(stream);
+  auto* w = new ovb_weight();
+  if (cuda_failed(cudaGetDevice(&w->device), "cudaGetDevice")) {
+    delete w;
+    return OVB_ERR_INTERNAL;
+  }
+  w->N = N;
+  w->K = K;
+  w->Kb = kblocks(K);
+  w->Kp = w->Kb * 32;
+  const size_t wbytes = static_cast<size_t>(N * w->Kp);
+  const size_t sbytes = static_cast<size_t>(N) * sizeof(float);
+  const size_t src_bytes = static_cast<size_t>(N * K);
+  int8_t* src_dev = nullptr;
+  bool ok = !cuda_failed(cudaMalloc(&w->w, wbytes), "cudaMalloc(weight)") &&
+            !cuda_failed(cudaMalloc(&w->scale, sbytes), "cudaMalloc(scale)");
+  const bool on_device = (flags & OVB_SRC_DEVICE) != 0;
+  if (ok) {
+    if (on_device) {
+      src_dev = const_cast<int8_t*>(W);
+      ok = !cuda_failed(cudaMemcpyAsync(w->scale, scale, sbytes, cudaMemcpyDeviceToDevice, s),
+                        "copy scale");
+    } else {
+      ok = !cuda_failed(cudaMalloc(&src_dev, src_bytes), "cudaMalloc(staging)") &&
+           !cuda_failed(cudaMemcpyAsync(src_dev, W, src_bytes, cudaMemcpyHostToDevice, s),
+                        "copy weight") &&
+           !cuda_failed(cudaMemcpyAsync(w->scale, scale, sbytes, cudaMemcpyHostToDevice, s),
+                        "copy scale");
+    }
+  }
+  if (ok) {
+    cudaError_t e = layout == OVB_LAYOUT_NK ? ovb::launch_pack_nk(src_dev, N, K, w->w, w->Kp, s)
+                                            : ovb::launch_pack_kn(src_dev, N, K, w->w, w->Kp, s);
+    ok = !cuda_failed(e, "pack weight") &&
+         !cuda_failed(cudaStreamSynchronize(s), "weight pack sync");
+  }
+  if (!on_device && src_dev) cudaFree(src_dev);
+  if (ok) ok = ensure_weight_tmap(w);
+  if (!ok) {
+    cudaFree(w->w);
+    cudaFree(w->scale);
+    delete w;
+    return OVB_ERR_INTERNAL;
+  }
+  *out = w;
+  return OVB_OK;
+}
+
+int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
+                      ovb_weight** out) {
+  if (!out) return invalid("out is null");
+  *out = nullptr;
+  if (!parts || n_parts <= 0) return invalid("no parts");
+  int64_t total = 0;
+  for (int i = 0; i < n_parts; ++i) {
+    if (!parts[i]) return invalid("null part");
+    if (parts[i]->K != parts[0]->K) return invalid("concat: parts differ in K");
+    if (parts[i]->device != parts[0]->device) return invalid("concat: parts on different devices");
+    total += parts[i]->N;
+  }
+  cudaStream_t s = as_stream(stream);
+  auto* w = new ovb_weight();
+  w->device = parts[0]->device;
+  w->N = total;
+  w->K = parts[0]->K;
+  w->Kb = parts[0]->Kb;
+  w->Kp = parts[0]->Kp;
+  bool ok = !cuda_failed(cudaMalloc(&w->w, static_cast<size_t>(total * w->Kp)), "cudaMalloc") &&
+            !cuda_failed(cudaMalloc(&w->scale, static_cast<size_t>(total) * 4), "cudaMalloc");
+  int64_t row = 0;
+  for (int i = 0; ok && i < n_parts; ++i) {
+    const ovb_weight* p = parts[i];
+    ok = !cuda_failed(cudaMemcpyAsync(w->w + row * w->Kp, p->w, static_cast<size_t>(p->N * p->Kp),
+                                      cudaMemcpyDeviceToDevice, s),
+                      "concat copy") &&
+         !cuda_failed(cudaMemcpyAsync(w->scale + row, p->scale, static_cast<size_t>(p->N) * 4,
+                                      cudaMemcpyDeviceToDevice, s),
+                      "concat copy");
+    row += p->N;
+  }
+  if (ok) ok = !cuda_failed(cudaStreamSynchronize(s), "concat sync") && ensure_weight_tmap(w);
+  if (!ok) {
+    cudaFree(w->w);
+    cudaFree(w->scale);
+    delete w;
+    return OVB_ERR_INTERNAL;
+  }
+  *out = w;
+  return OVB_OK;
+}
+
+int ovb_weight_destroy(ovb_weight* w) {
+  if (!w) return OVB_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(w->device);
+  cudaFree(w->w);
+  cudaFree(w->scale);
+  cudaSetDevice(prev);
+  delete w;
+  return OVB_OK;
+}
+
+int ovb_weight_shape(const ovb_weight* w, int64_t* N, int64_t* K) {
+  if (!w) return invalid("weight handle is null");
+  if (N) *N = w->N;
+  if (K) *K = w->K;
+  return OVB_OK;
+}
+
+int ovb_weight_export(const ovb_weight* w, int8_t* W_nk, float* scale) {
+  if (!w || !W_nk || !scale) return invalid("null argument");
+  if (cuda_failed(cudaMemcpy2D(W_nk, static_cast<size_t>(w->K), w->w, static_cast<size_t>(w->Kp),
+                               static_cast<size_t>(w->K), static_cast<size_t>(w->N),
+                               cudaMemcpyDeviceToHost),
+                  "export weight") ||
+      cuda_failed(cudaMemcpy(scale, w->scale, static_cast<size_t>(w->N) * 4,
+                             cudaMemcpyDeviceToHost),
+                  "export scale"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+// ------------------------------------------------------------- quantisers
+int ovb_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq, float* asc,
+                 int flags, void* stream) {
+  if (M <= 0 || K <= 0) return OVB_OK;
+  if (!A || !aq || !asc) return invalid("A/aq/asc must be non-null");
+  if (lda < K) return invalid("lda < K");
+  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(A, 4)) return invalid("misaligned buffer");
+  if (cuda_failed(ovb::launch_quantize(M, K, A, lda, aq, asc, flags & OVB_AQ_U8,
+                                       as_stream(stream)),
+                  "quantize launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w, float eps,
+                         void* aq, float* asc, int flags, void* stream) {
+  if (rows <= 0 || cols <= 0) return OVB_OK;
+  if (!x || !w || !aq || !asc) return invalid("x/w/aq/asc must be non-null");
+  if (cols > 24 * 1024) return invalid("rmsnorm_quantize: cols > 24576 not supported");
+  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(x, 4) || !aligned(w, 4))
+    return invalid("misaligned buffer");
+  if (cuda_failed(ovb::launch_rmsnorm_quantize(rows, cols, x, w, eps, aq, asc,
+                                               flags & OVB_AQ_U8, as_stream(stream)),
+                  "rmsnorm_quantize launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
+                          const float* up, int64_t ldu, void* aq, float* asc, int flags,
+                          void* stream) {
+  if (M <= 0 || K <= 0) return OVB_OK;
+  if (!gate || !up || !aq || !asc) return invalid("gate/up/aq/asc must be non-null");
+  if (ldg < K || ldu < K) return invalid("ldg/ldu < K");
+  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(gate, 4) || !aligned(up, 4))
+    return invalid("misaligned buffer");
+  if (cuda_failed(ovb::launch_silu_mul_quantize(M, K, gate, ldg, up, ldu, aq, asc,
+                                                flags & OVB_AQ_U8, as_stream(stream)),
+                  "silu_mul_quantize launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+// ------------------------------------------------------------------ GEMMs
+int ovb_linear_q(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc, float* C,
+                 int64_t ldc, int accumulate, void* stream) {
+  if (M <= 0) return OVB_OK;
+  int st = check_q_args(M, w, aq, asc);
+  if (st != OVB_OK) return st;
+  if (!C) return invalid("C is null");
+  if (ldc < w->N) return invalid("ldc < N");
+  const ovb::SliceOut so{0, w->N, C, ldc};
+  return run_gemm(M, w, aq, asc, &so, 1, accumulate ? 1 : 0, nullptr, as_stream(stream));
+}
+
+int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
+                        const ovb_slice* slices, int n_slices, void* stream) {
+  if (M <= 0 || n_slices <= 0) return OVB_OK;
+  int st = check_q_args(M, w, aq, asc);
+  if (st != OVB_OK) return st;
+  if (!slices) return invalid("slices is null");
+  if (n_slices > ovb::kMaxSlices) return invalid("at most 4 slices");
+  ovb::SliceOut so[ovb::kMaxSlices];
+  int64_t total = 0;
+  for (int i = 0; i < n_slices; ++i) {
+    // gemm.cpp:786-788: each slice N must be a positive multiple of 64.
+    if (slices[i].N <= 0 || slices[i].N % 64 != 0 || !slices[i].C)
+      return invalid("sliced GEMM: each slice N must be a positive multiple of 64");
+    if (slices[i].ldc < slices[i].N) return invalid("sliced GEMM: ldc < N");
+    so[i] = ovb::SliceOut{total, slices[i].N, slices[i].C, slices[i].ldc};
+    total += slices[i].N;
+  }
+  if (total != w->N) return invalid("sliced GEMM: slice widths do not add up to the weight's N");
+  return run_gemm(M, w, aq, asc, so, n_slices, 0, nullptr, as_stream(stream));
+}
+
+size_t ovb_linear_workspace_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  const size_t qb = static_cast<size_t>(ovb_quant_bytes(M, K));
+  return ((qb + 255) / 256) * 256 + static_cast<size_t>(ovb_quant_scales(M, K)) * 4;
+}
+
+int ovb_linear(int64_t M, const ovb_weight* w, const float* A, int64_t lda, float* C,
+               int64_t ldc, int accumulate, void* work, size_t work_bytes, void* stream) {
+  if (M <= 0) return OVB_OK;
+  if (!w) return invalid("weight handle is null");
+  if (!A || !C) return invalid("A/C must be non-null");
+  if (!work || !aligned(work, 256)) return invalid("work must be non-null and 256-byte aligned");
+  if (work_bytes < ovb_linear_workspace_bytes(M, w->K)) return invalid("work buffer too small");
+  if (lda < w->K) return invalid("lda < K");
+  if (ldc < w->N) return invalid("ldc < N");
+  const size_t qb = static_cast<size_t>(ovb_quant_bytes(M, w->K));
+  auto* aq = static_cast<int8_t*>(work);
+  auto* asc = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ((qb + 255) / 256) * 256);
+  int st = ovb_quantize(M, w->K, A, lda, aq, asc, 0, stream);
+  if (st != OVB_OK) return st;
+  return ovb_linear_q(M, w, aq, asc, C, ldc, accumulate, stream);
+}
+
+int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t* P,
+                       void* stream) {
+  if (M <= 0) return OVB_OK;
+  if (!w) return invalid("weight handle is null");
+  if (!aq || !P) return invalid("aq/P must be non-null");
+  if (!aligned(aq, 16)) return invalid("aq must be 16-byte aligned (TMA source)");
+  const ovb::SliceOut so{0, w->N, nullptr, w->N};
+  // asc is not read in this mode; pass a valid dummy pointer.
+  return run_gemm(M, w, aq, reinterpret_cast<const float*>(aq), &so, 1, 0, P,
+                  as_stream(stream));
+}
+
+}  // extern "C"

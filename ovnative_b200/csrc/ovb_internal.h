@@ -1,0 +1,80 @@
+// ovb_internal.h -- declarations shared by the translation units of
+// libovb200.so.  Not part of the public C ABI (include/ovb200.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+struct ovb_weight {
+  int device = 0;
+  int64_t N = 0;         // output channels
+  int64_t K = 0;         // input features
+  int64_t Kb = 0;        // ceil(K / 32)
+  int64_t Kp = 0;        // Kb * 32: row stride of `w` in bytes
+  int8_t* w = nullptr;   // device [N, Kp] int8, K-major, zero tail bytes
+  float* scale = nullptr;  // device [N] per-output-channel scale
+  // TMA descriptor of `w` for the GEMM's B tiles (box 32 B x kBlockN rows).
+  CUtensorMap tmap_b;
+  bool tmap_ready = false;
+};
+
+namespace ovb {
+
+// Rows / columns per GEMM output tile and pipeline depth.
+constexpr int kBlockM = 128;
+constexpr int kBlockN = 128;
+
+constexpr int kMaxSlices = 4;
+
+struct SliceOut {
+  int64_t n_begin;  // first global column of the slice
+  int64_t n_count;
+  float* C;
+  int64_t ldc;
+};
+
+struct GemmArgs {
+  int64_t M, N, Kb;
+  const float* asc;     // [M, Kb]
+  const float* wscale;  // [N]
+  int accumulate;
+  int n_slices;
+  SliceOut slices[kMaxSlices];
+  int32_t* products;    // when non-null: write P[m, n, b] instead of C
+};
+
+// Thread-local error message (ovb_last_error).
+void set_error(const std::string& msg);
+
+// CUDA error -> message; returns true when `e` is an error.
+bool cuda_failed(cudaError_t e, const char* what);
+
+// Encode a 2-D uint8 tensor map [rows, row_bytes] with a (32 B x box_rows)
+// box and 32-byte swizzle.  Returns false (and sets the error) on failure.
+bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
+                    uint64_t stride_bytes, uint32_t box_rows);
+
+int num_sms(int device);
+
+// Launchers (stream-ordered, return a cudaError_t from the launch).
+cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
+                            float* asc, int u8, cudaStream_t s);
+cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
+                                    float eps, void* aq, float* asc, int u8, cudaStream_t s);
+cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
+                                     const float* up, int64_t ldu, void* aq, float* asc, int u8,
+                                     cudaStream_t s);
+cudaError_t launch_pack_nk(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
+                           cudaStream_t s);
+cudaError_t launch_pack_kn(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
+                           cudaStream_t s);
+cudaError_t launch_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
+                        const GemmArgs& args, cudaStream_t s);
+
+// Device status word (0 = every bounded wait completed).
+cudaError_t read_and_clear_status(int* out, cudaStream_t s);
+
+}  // namespace ovb

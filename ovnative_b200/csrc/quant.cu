@@ -1,0 +1,301 @@
+// quant.cu -- per-row, per-32-k activation quantisers for the int8 GEMM.
+//
+// Three producers, each writing aq (int8 q, or the reference's u8 q+128 with
+// OVB_AQ_U8) and asc (fp32 block scales), bit-identical to the reference CPU
+// path:
+//   quantize_kernel          quantize_a_u8          gemm.cpp:379-430
+//   rmsnorm_quantize_kernel  rmsnorm_quantize_avx2  gemm.cpp:638-707
+//   silu_mul_quantize_kernel silu_mul_quant_avx2    ops_cpu.cpp:144-198
+//
+// All three are HBM-bound (about 4-8 bytes read and ~1 byte written per
+// element).  Every fp32 operation is an explicit round-to-nearest intrinsic so
+// that nvcc can neither contract nor reorder anything; denormals are kept
+// (no -ftz / fast-math on this file).
+#include <climits>
+
+#include "ovb_internal.h"
+
+namespace ovb {
+namespace {
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// _mm256_cvtps_epi32 under the default MXCSR: round to nearest even, and
+// 0x80000000 ("integer indefinite") for NaN or values outside int32.
+__device__ __forceinline__ int cvt_rne_x86(float v) {
+  if (!(v == v) || v >= 2147483648.0f || v < -2147483648.0f) return INT_MIN;
+  return __float2int_rn(v);
+}
+
+__device__ __forceinline__ uint32_t quant_byte(float v, float inv, bool u8) {
+  int z = cvt_rne_x86(__fmul_rn(v, inv));
+  z = z < -127 ? -127 : (z > 127 ? 127 : z);
+  return u8 ? static_cast<uint32_t>(z + 128) : static_cast<uint32_t>(z & 0xFF);
+}
+
+// Block scale and its reciprocal exactly as gemm.cpp:407-408.
+__device__ __forceinline__ void block_scales(float amax, float* scale, float* inv) {
+  *scale = __fdiv_rn(amax, 127.0f);
+  *inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+}
+
+// Quantise 8 consecutive values (the first `nv` valid, the rest padding -> 0).
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], int nv, float inv, bool u8) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t b = (i < nv) ? quant_byte(v[i], inv, u8) : 0u;
+    if (i < 4)
+      lo |= b << (8 * i);
+    else
+      hi |= b << (8 * (i - 4));
+  }
+  return make_uint2(lo, hi);
+}
+
+// Load 8 floats starting at p, the first nv of them valid (others 0).
+__device__ __forceinline__ void load8(const float* p, int nv, bool vec_ok, float (&v)[8]) {
+  if (nv == 8 && vec_ok) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (i < nv) ? __ldg(p + i) : 0.f;
+  }
+}
+
+// ------------------------------------------------------------ quantize
+// Four threads per 32-k block (8 values each); the block absmax is reduced
+// over the four with shuffles (max is order-independent, so this equals the
+// reference's 8-lane max followed by a scalar tail).
+__global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, const float* A,
+                                                       int64_t lda, uint8_t* aq, float* asc,
+                                                       int u8) {
+  const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
+  const int64_t total = M * Kb * 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const bool vec_ok = ((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t - lane < total;
+       t += stride) {
+    const bool valid = t < total;
+    const int64_t task = valid ? t >> 2 : 0;
+    const int sub = static_cast<int>(t & 3);
+    const int64_t row = task / Kb, b = task - row * Kb;
+    const int64_t k = b * 32 + sub * 8;
+    const int nv = valid ? static_cast<int>(imax64(0, imin64(8, K - k))) : 0;
+    float v[8];
+    load8(A + row * lda + k, nv, vec_ok, v);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    float scale, inv;
+    block_scales(amax, &scale, &inv);
+    if (valid) {
+      *reinterpret_cast<uint2*>(aq + row * Kp + k) = quant8(v, nv, inv, u8 != 0);
+      if (sub == 0) asc[row * Kb + b] = scale;
+    }
+  }
+}
+
+// ---------------------------------------------------- rmsnorm + quantize
+// One warp per row.  The row is staged in shared memory with coalesced
+// float4 loads; lanes 0..7 then run the reference's eight sequential FMA
+// chains (lane l: elements l, l+8, ...; gemm.cpp:655-658), every lane sums
+// the eight partials left to right plus the cols%8 tail (:661-663) and forms
+// scale = 1/sqrt(sum/cols + eps) (:664).  Each lane then quantises whole
+// 32-k blocks b = lane, lane+32, ... of (x*scale)*w (:672-704).
+__global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int64_t cols,
+                                                               const float* x, const float* w,
+                                                               float eps, uint8_t* aq,
+                                                               float* asc, int u8) {
+  extern __shared__ float srow_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  float* srow = srow_all + static_cast<int64_t>(warp) * cols;
+  const int64_t Kb = (cols + 31) / 32, Kp = Kb * 32;
+  const bool vec_ok = ((cols & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * warps + warp; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * warps) {
+    const float* row = x + r * cols;
+    if (vec_ok) {
+      for (int64_t i = lane * 4; i < cols; i += 128)
+        *reinterpret_cast<float4*>(srow + i) = __ldg(reinterpret_cast<const float4*>(row + i));
+    } else {
+      for (int64_t i = lane; i < cols; i += 32) srow[i] = __ldg(row + i);
+    }
+    __syncwarp();
+    const int64_t nvec = cols / 8;
+    float acc = 0.f;
+    if (lane < 8)
+      for (int64_t j = 0; j < nvec; ++j) {
+        const float v = srow[j * 8 + lane];
+        acc = __fmaf_rn(v, v, acc);
+      }
+    float sum = __shfl_sync(0xffffffffu, acc, 0);
+#pragma unroll
+    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, l));
+    for (int64_t i = nvec * 8; i < cols; ++i) sum = __fadd_rn(sum, __fmul_rn(srow[i], srow[i]));
+    const float scale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+    for (int64_t b = lane; b < Kb; b += 32) {
+      const int64_t k0 = b * 32;
+      const int kn = static_cast<int>(imin64(32, cols - k0));
+      float v[32];
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] = (i < kn) ? __fmul_rn(__fmul_rn(srow[k0 + i], scale), __ldg(w + k0 + i)) : 0.f;
+        amax = fmaxf(amax, fabsf(v[i]));
+      }
+      float bs, inv;
+      block_scales(amax, &bs, &inv);
+      asc[r * Kb + b] = bs;
+      uint8_t* q = aq + r * Kp + k0;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float v8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v8[i] = v[g * 8 + i];
+        const int nv = max(0, min(8, kn - g * 8));
+        *reinterpret_cast<uint2*>(q + g * 8) = quant8(v8, nv, inv, u8 != 0);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------- silu(gate)*up + quantize
+// exp256_ps (ops_cpu.cpp:75-92) for one lane, operation for operation:
+// clamp to [-87, 88], n = rne(x*log2e), r = x - n*ln2 (product, then
+// difference), degree-6 Horner with fused multiply-adds, times 2^n built in
+// the exponent field.
+__device__ __forceinline__ float exp_ref(float x) {
+  x = (x < 88.0f) ? x : 88.0f;
+  x = (x > -87.0f) ? x : -87.0f;
+  const float n = rintf(__fmul_rn(x, 1.4426950408889634f));
+  const float r = __fsub_rn(x, __fmul_rn(n, 0.6931471805599453f));
+  float p = 1.0f / 720;
+  p = __fmaf_rn(p, r, 1.0f / 120);
+  p = __fmaf_rn(p, r, 1.0f / 24);
+  p = __fmaf_rn(p, r, 1.0f / 6);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = __float2int_rn(n);
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+// silu_up8 (ops_cpu.cpp:138-142): (g / (1 + exp(0 - g))) * u.
+__device__ __forceinline__ float silu_up_vec(float g, float u) {
+  const float d = __fadd_rn(1.0f, exp_ref(__fsub_rn(0.0f, g)));
+  return __fmul_rn(__fdiv_rn(g, d), u);
+}
+
+// The scalar tail of a block (kn % 8 trailing elements, ops_cpu.cpp:166)
+// uses silu() with the C library's expf.  A correctly rounded exp is formed
+// here from the double-precision exp, which agrees with the host expf except
+// in the rare cases where the host's result is not correctly rounded.
+__device__ __forceinline__ float silu_up_tail(float g, float u) {
+  const float e = static_cast<float>(exp(static_cast<double>(-g)));
+  const float d = __fadd_rn(1.0f, e);
+  return __fmul_rn(__fdiv_rn(g, d), u);
+}
+
+__global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
+                                                                const float* gate, int64_t ldg,
+                                                                const float* up, int64_t ldu,
+                                                                uint8_t* aq, float* asc, int u8) {
+  const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
+  const int64_t total = M * Kb * 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const bool vg = ((ldg & 3) == 0) && ((reinterpret_cast<uintptr_t>(gate) & 15) == 0);
+  const bool vu = ((ldu & 3) == 0) && ((reinterpret_cast<uintptr_t>(up) & 15) == 0);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t - lane < total;
+       t += stride) {
+    const bool valid = t < total;
+    const int64_t task = valid ? t >> 2 : 0;
+    const int sub = static_cast<int>(t & 3);
+    const int64_t row = task / Kb, b = task - row * Kb;
+    const int64_t k = b * 32 + sub * 8;
+    const int nv = valid ? static_cast<int>(imax64(0, imin64(8, K - k))) : 0;
+    const int kn = static_cast<int>(imin64(32, K - b * 32));
+    // This thread's 8 values are in the block's vector body when they form a
+    // whole group of 8 inside the block (ops_cpu.cpp:163-165).
+    const bool body = (sub * 8 + 8) <= kn;
+    float g[8], u[8], v[8];
+    load8(gate + row * ldg + k, nv, vg, g);
+    load8(up + row * ldu + k, nv, vu, u);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = (i < nv) ? (body ? silu_up_vec(g[i], u[i]) : silu_up_tail(g[i], u[i])) : 0.f;
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    float scale, inv;
+    block_scales(amax, &scale, &inv);
+    if (valid) {
+      *reinterpret_cast<uint2*>(aq + row * Kp + k) = quant8(v, nv, inv, u8 != 0);
+      if (sub == 0) asc[row * Kb + b] = scale;
+    }
+  }
+}
+
+int grid_for(int64_t threads_needed) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t blocks = (threads_needed + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms(dev)) * 8;
+  return static_cast<int>(imax64(1, imin64(blocks, cap)));
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
+                            float* asc, int u8, cudaStream_t s) {
+  const int64_t Kb = (K + 31) / 32;
+  quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(M, K, A, lda,
+                                                       static_cast<uint8_t*>(aq), asc, u8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
+                                    float eps, void* aq, float* asc, int u8, cudaStream_t s) {
+  // One warp per row; shared memory holds one row per warp.
+  const int64_t row_bytes = cols * 4;
+  int warps = static_cast<int>(imin64(8, imax64(1, (96 * 1024) / row_bytes)));
+  const size_t smem = static_cast<size_t>(warps) * row_bytes;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(rmsnorm_quantize_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  const int64_t blocks = (rows + warps - 1) / warps;
+  const int grid = static_cast<int>(imin64(blocks, static_cast<int64_t>(num_sms(dev)) * 16));
+  rmsnorm_quantize_kernel<<<grid, warps * 32, smem, s>>>(rows, cols, x, w, eps,
+                                                         static_cast<uint8_t*>(aq), asc, u8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
+                                     const float* up, int64_t ldu, void* aq, float* asc, int u8,
+                                     cudaStream_t s) {
+  const int64_t Kb = (K + 31) / 32;
+  silu_mul_quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(
+      M, K, gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, u8);
+  return cudaGetLastError();
+}
+
+}  // namespace ovb

@@ -1,0 +1,272 @@
+"""Host-side mirror of the reference's GEMM backend contract for this path.
+
+The functions here carry the names and argument meaning of
+cpp/include/ovnative/ov_gemm.h (namespace ov) -- s8_nk_quantize,
+rmsnorm_quantize_f32, silu_mul_quantize_f32, linear_s8_nk_packed_q[_add],
+linear_s8_nk_packed_q_sliced, linear_s8_nk_packed[_add] -- but run on the
+B200 through the C ABI (include/ovb200.h).  Tensors are torch CUDA tensors
+(PyTorch is used for device memory and streams only); every call is ordered on
+torch's current stream.
+
+Error behaviour follows the reference: M/N/K <= 0 is a no-op
+(gemm.cpp:761, :779, :832), argument errors raise ValueError where the
+reference throws std::invalid_argument (gemm.cpp:786-788), and device or
+launch failures raise RuntimeError (std::runtime_error in the reference).
+
+Quantised activations: aq is int8 q (or the reference's u8 q+128 when
+``u8=True``, for byte comparison), [M, 32*ceil(K/32)], asc fp32 [M, ceil(K/32)].
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev_ptr(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor")
+    return t.data_ptr()
+
+
+def _rows_ok(t: torch.Tensor, name: str):
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with unit column stride")
+
+
+def kblocks(K: int) -> int:
+    return (K + 31) // 32
+
+
+def s8_nk_quant_bytes(M: int, K: int) -> int:
+    """ov::s8_nk_quant_bytes (ov_gemm.h:95)."""
+    return int(L.lib().ovb_quant_bytes(M, K))
+
+
+def s8_nk_quant_scales(M: int, K: int) -> int:
+    """ov::s8_nk_quant_scales (ov_gemm.h:96)."""
+    return int(L.lib().ovb_quant_scales(M, K))
+
+
+def empty_quant(M: int, K: int, device=None):
+    """Allocate (aq, asc) for M rows of K features."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    Kb = kblocks(K)
+    return (torch.empty((M, Kb * 32), dtype=torch.int8, device=dev),
+            torch.empty((M, Kb), dtype=torch.float32, device=dev))
+
+
+class Weight:
+    """A device-resident int8 weight with per-output-channel scales.
+
+    Built from either OVW1 layout: ``from_nk`` ([N, K], layout=0) or
+    ``from_kn`` ([K, N], layout=1).  Replaces ``Mat``'s packed VNNI tiles
+    (mat.cpp:88-104 / s8_nk_pack) and the CUDA runner's dequantised copies
+    (cuda_lm.cu:840-873).
+    """
+
+    def __init__(self, handle: int, N: int, K: int):
+        self._h = handle
+        self.N = N
+        self.K = K
+
+    @property
+    def handle(self) -> int:
+        if not self._h:
+            raise ValueError("weight was destroyed")
+        return self._h
+
+    @classmethod
+    def _create(cls, W, scale, layout: int, N: int, K: int) -> "Weight":
+        out = C.c_void_p()
+        if isinstance(W, torch.Tensor) and W.is_cuda:
+            W = W.contiguous()
+            scale = scale.to(device=W.device, dtype=torch.float32).contiguous()
+            st = L.lib().ovb_weight_create(W.data_ptr(), layout, N, K, scale.data_ptr(),
+                                           L.OVB_SRC_DEVICE, _stream(), C.byref(out))
+        else:
+            Wn = np.ascontiguousarray(W.cpu().numpy() if isinstance(W, torch.Tensor) else W,
+                                      dtype=np.int8)
+            sn = np.ascontiguousarray(scale.cpu().numpy() if isinstance(scale, torch.Tensor)
+                                      else scale, dtype=np.float32)
+            st = L.lib().ovb_weight_create(Wn.ctypes.data, layout, N, K, sn.ctypes.data, 0,
+                                           _stream(), C.byref(out))
+        L.check(st)
+        return cls(out.value, N, K)
+
+    @classmethod
+    def from_nk(cls, W, scale) -> "Weight":
+        N, K = W.shape
+        return cls._create(W, scale, L.OVB_LAYOUT_NK, N, K)
+
+    @classmethod
+    def from_kn(cls, W, scale) -> "Weight":
+        K, N = W.shape
+        return cls._create(W, scale, L.OVB_LAYOUT_KN, N, K)
+
+    @classmethod
+    def concat(cls, parts: list["Weight"]) -> "Weight":
+        """combine_packed (lm.cpp:57-94): q|k|v or gate|up along N."""
+        arr = (C.c_void_p * len(parts))(*[p.handle for p in parts])
+        out = C.c_void_p()
+        L.check(L.lib().ovb_weight_concat(C.cast(arr, C.c_void_p), len(parts), _stream(),
+                                          C.byref(out)))
+        return cls(out.value, sum(p.N for p in parts), parts[0].K)
+
+    def export(self):
+        """The device weight as ([N, K] int8, [N] fp32) numpy arrays."""
+        W = np.zeros((self.N, self.K), np.int8)
+        s = np.zeros(self.N, np.float32)
+        L.check(L.lib().ovb_weight_export(self.handle, W.ctypes.data, s.ctypes.data))
+        return W, s
+
+    def close(self):
+        if self._h:
+            L.lib().ovb_weight_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------ quantisers
+def _flags(u8: bool) -> int:
+    return L.OVB_AQ_U8 if u8 else 0
+
+
+def _quant_out(M, K, device, u8, out):
+    if out is not None:
+        return out
+    aq, asc = empty_quant(M, K, device)
+    if u8:
+        aq = aq.view(torch.uint8)
+    return aq, asc
+
+
+def s8_nk_quantize(A: torch.Tensor, u8: bool = False, out=None):
+    """ov::s8_nk_quantize (ov_gemm.h:97): per-row, per-32-k quantisation."""
+    _rows_ok(A, "A")
+    M, K = A.shape
+    aq, asc = _quant_out(M, K, A.device, u8, out)
+    L.check(L.lib().ovb_quantize(M, K, _dev_ptr(A), A.stride(0), _dev_ptr(aq), _dev_ptr(asc),
+                                 _flags(u8), _stream()))
+    return aq, asc
+
+
+def rmsnorm_quantize_f32(x: torch.Tensor, w: torch.Tensor, eps: float, u8: bool = False,
+                         out=None):
+    """ov::rmsnorm_quantize_f32 (ov_gemm.h:118-119)."""
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    M, K = x.shape
+    aq, asc = _quant_out(M, K, x.device, u8, out)
+    L.check(L.lib().ovb_rmsnorm_quantize(M, K, _dev_ptr(x), _dev_ptr(w.contiguous()), eps,
+                                         _dev_ptr(aq), _dev_ptr(asc), _flags(u8), _stream()))
+    return aq, asc
+
+
+def silu_mul_quantize_f32(gate: torch.Tensor, up: torch.Tensor, u8: bool = False, out=None):
+    """ov::silu_mul_quantize_f32 (ov_gemm.h:84-85)."""
+    _rows_ok(gate, "gate")
+    _rows_ok(up, "up")
+    M, K = gate.shape
+    aq, asc = _quant_out(M, K, gate.device, u8, out)
+    L.check(L.lib().ovb_silu_mul_quantize(M, K, _dev_ptr(gate), gate.stride(0), _dev_ptr(up),
+                                          up.stride(0), _dev_ptr(aq), _dev_ptr(asc), _flags(u8),
+                                          _stream()))
+    return aq, asc
+
+
+# ----------------------------------------------------------------- GEMMs
+def _out(M, w: Weight, C, device):
+    if C is None:
+        return torch.empty((M, w.N), dtype=torch.float32, device=device)
+    _rows_ok(C, "C")
+    return C
+
+
+def linear_s8_nk_packed_q(aq: torch.Tensor, asc: torch.Tensor, w: Weight, C=None):
+    """ov::linear_s8_nk_packed_q (ov_gemm.h:98-100): C = linear(aq, asc)."""
+    M = aq.shape[0]
+    C = _out(M, w, C, aq.device)
+    L.check(L.lib().ovb_linear_q(M, w.handle, _dev_ptr(aq), _dev_ptr(asc), _dev_ptr(C),
+                                 C.stride(0), 0, _stream()))
+    return C
+
+
+def linear_s8_nk_packed_q_add(aq: torch.Tensor, asc: torch.Tensor, w: Weight, C: torch.Tensor):
+    """ov::linear_s8_nk_packed_q_add (ov_gemm.h:78-80): C += linear(aq, asc)."""
+    _rows_ok(C, "C")
+    L.check(L.lib().ovb_linear_q(aq.shape[0], w.handle, _dev_ptr(aq), _dev_ptr(asc),
+                                 _dev_ptr(C), C.stride(0), 1, _stream()))
+    return C
+
+
+def linear_s8_nk_packed_q_sliced(aq: torch.Tensor, asc: torch.Tensor, w: Weight,
+                                 Cs: list[torch.Tensor]):
+    """ov::linear_s8_nk_packed_q_sliced (ov_gemm.h:109-111): one launch over a
+    concatenated weight, slice i written to Cs[i] ([M, N_i], N_i % 64 == 0)."""
+    for c in Cs:
+        _rows_ok(c, "C")
+    arr = (L.Slice * len(Cs))(*[L.Slice(c.shape[1], _dev_ptr(c), c.stride(0)) for c in Cs])
+    L.check(L.lib().ovb_linear_q_sliced(aq.shape[0], w.handle, _dev_ptr(aq), _dev_ptr(asc), arr,
+                                        len(Cs), _stream()))
+    return Cs
+
+
+def workspace_bytes(M: int, K: int) -> int:
+    return int(L.lib().ovb_linear_workspace_bytes(M, K))
+
+
+def _work(M, K, device, work):
+    need = workspace_bytes(M, K)
+    if work is None:
+        work = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+    return work, need
+
+
+def linear_s8_nk_packed(A: torch.Tensor, w: Weight, C=None, work=None):
+    """ov::linear_s8_nk_packed (ov_gemm.h:67-69): quantise A, then C = linear."""
+    _rows_ok(A, "A")
+    M = A.shape[0]
+    C = _out(M, w, C, A.device)
+    work, need = _work(M, w.K, A.device, work)
+    L.check(L.lib().ovb_linear(M, w.handle, _dev_ptr(A), A.stride(0), _dev_ptr(C), C.stride(0),
+                               0, _dev_ptr(work), work.numel(), _stream()))
+    return C
+
+
+def linear_s8_nk_packed_add(A: torch.Tensor, w: Weight, C: torch.Tensor, work=None):
+    """ov::linear_s8_nk_packed_add (ov_gemm.h:73-75): C += linear(quantise(A))."""
+    _rows_ok(A, "A")
+    _rows_ok(C, "C")
+    work, need = _work(A.shape[0], w.K, A.device, work)
+    L.check(L.lib().ovb_linear(A.shape[0], w.handle, _dev_ptr(A), A.stride(0), _dev_ptr(C),
+                               C.stride(0), 1, _dev_ptr(work), work.numel(), _stream()))
+    return C
+
+
+def block_products(aq: torch.Tensor, w: Weight) -> torch.Tensor:
+    """Exact int32 per-32-k block products P[m, n, b] from the tensor-core mainloop."""
+    M = aq.shape[0]
+    P = torch.empty((M, w.N, kblocks(w.K)), dtype=torch.int32, device=aq.device)
+    L.check(L.lib().ovb_block_products(M, w.handle, _dev_ptr(aq), _dev_ptr(P), _stream()))
+    return P
+
+
+def device_status() -> int:
+    """Status word of the bounded device waits (0 = all completed); clears it."""
+    st = L.lib().ovb_device_status(_stream())
+    if st < 0:
+        L.check(st)
+    return st

@@ -1,0 +1,114 @@
+"""The linear sequence of one OVNative LM decoder layer on the B200 path.
+
+Mirrors the int8 branch of LM::run_layer (cpp/src/model/lm.cpp:217-322):
+
+    1. rmsnorm_quantize_f32(x, input_ln)              lm.cpp:232
+    2. qkv sliced GEMM -> q [M,2048], k, v [M,1024]     lm.cpp:233-237
+    3. (q/k norm, RoPE, attention -> attn [M,2048])    lm.cpp:252-277  -- out of scope
+    4. o_proj.mul_add(attn, x): quantise + GEMM, += x   lm.cpp:281
+    5. rmsnorm_quantize_f32(x, post_ln)               lm.cpp:292
+    6. gate|up sliced GEMM -> gate, up [M,3072]         lm.cpp:293-297
+    7. silu_mul_quantize_f32(gate, up)                lm.cpp:310
+    8. down.mul_q_add -> x += ...                       lm.cpp:311
+
+Attention is not part of this path.  ``run`` takes the attention output as an
+argument; when it is omitted the q projection itself is fed to o_proj (an
+identity stand-in that keeps the data flow of a real layer without adding
+work).  All buffers are allocated once, so ``run`` can be captured in a CUDA
+graph.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import gemm as G
+
+HIDDEN = 1024
+N_HEADS, N_KV, HEAD_DIM = 16, 8, 128
+QD = N_HEADS * HEAD_DIM   # 2048
+KVD = N_KV * HEAD_DIM     # 1024
+INTER = 3072
+RMS_EPS = 1e-6
+
+# (name, N, K) of the seven projections of one layer
+SHAPES = [("q", QD, HIDDEN), ("k", KVD, HIDDEN), ("v", KVD, HIDDEN), ("o", HIDDEN, QD),
+          ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]
+
+
+def ops_per_token() -> int:
+    """2 * sum(N*K) over the seven projections: 31.46 M int8 ops per token."""
+    return 2 * sum(n * k for _, n, k in SHAPES)
+
+
+def random_layer_host(rng: np.random.Generator):
+    """Random int8 weights ([N, K], uniform in [-127, 127]) and per-channel
+    scales |N(0, 0.02)|/127 for the seven projections, RMSNorm gains 1."""
+    w = {}
+    for name, n, k in SHAPES:
+        W = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        s = (np.abs(rng.standard_normal(n)) * 0.02 / 127.0).astype(np.float32)
+        w[name] = (W, s)
+    w["input_ln"] = np.ones(HIDDEN, np.float32)
+    w["post_ln"] = np.ones(HIDDEN, np.float32)
+    return w
+
+
+@dataclass
+class LayerWeights:
+    qkv: G.Weight
+    o: G.Weight
+    gate_up: G.Weight
+    down: G.Weight
+    input_ln: torch.Tensor
+    post_ln: torch.Tensor
+
+    @classmethod
+    def from_host(cls, w: dict, device) -> "LayerWeights":
+        parts = {name: G.Weight.from_nk(*w[name]) for name, _, _ in SHAPES}
+        qkv = G.Weight.concat([parts["q"], parts["k"], parts["v"]])
+        gu = G.Weight.concat([parts["gate"], parts["up"]])
+        for name in ("q", "k", "v", "gate", "up"):
+            parts[name].close()
+        return cls(qkv=qkv, o=parts["o"], gate_up=gu, down=parts["down"],
+                   input_ln=torch.from_numpy(w["input_ln"]).to(device),
+                   post_ln=torch.from_numpy(w["post_ln"]).to(device))
+
+    def close(self):
+        for m in (self.qkv, self.o, self.gate_up, self.down):
+            m.close()
+
+
+class LayerBuffers:
+    """Activation buffers for M rows (allocated once)."""
+
+    def __init__(self, M: int, device):
+        f32 = dict(dtype=torch.float32, device=device)
+        self.M = M
+        self.q = torch.empty((M, QD), **f32)
+        self.k = torch.empty((M, KVD), **f32)
+        self.v = torch.empty((M, KVD), **f32)
+        self.gate = torch.empty((M, INTER), **f32)
+        self.up = torch.empty((M, INTER), **f32)
+        self.qh = G.empty_quant(M, HIDDEN, device)   # norm+quant of x
+        self.qo = G.empty_quant(M, QD, device)       # quant of attn
+        self.qi = G.empty_quant(M, INTER, device)    # silu*up quant
+
+
+def run(x: torch.Tensor, lw: LayerWeights, buf: LayerBuffers, attn: torch.Tensor | None = None):
+    """One layer's linear set on x [M, 1024] (updated in place, residual stream)."""
+    G.rmsnorm_quantize_f32(x, lw.input_ln, RMS_EPS, out=buf.qh)
+    G.linear_s8_nk_packed_q_sliced(*buf.qh, lw.qkv, [buf.q, buf.k, buf.v])
+    a = buf.q if attn is None else attn
+    G.s8_nk_quantize(a, out=buf.qo)
+    G.linear_s8_nk_packed_q_add(*buf.qo, lw.o, x)
+    G.rmsnorm_quantize_f32(x, lw.post_ln, RMS_EPS, out=buf.qh)
+    G.linear_s8_nk_packed_q_sliced(*buf.qh, lw.gate_up, [buf.gate, buf.up])
+    G.silu_mul_quantize_f32(buf.gate, buf.up, out=buf.qi)
+    G.linear_s8_nk_packed_q_add(*buf.qi, lw.down, x)
+    return x
+
+
+KERNELS_PER_LAYER = 8  # 4 quantisers + 4 GEMMs
