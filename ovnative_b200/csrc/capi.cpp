@@ -75,11 +75,11 @@ bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint
   }
   const cuuint64_t dims[2] = {row_bytes, rows};
   const cuuint64_t strides[1] = {stride_bytes};
-  const cuuint32_t box[2] = {32u, box_rows};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kStageK), box_rows};
   const cuuint32_t elem_strides[2] = {1u, 1u};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
                         strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];

@@ -16,16 +16,18 @@ struct ovb_weight {
   int64_t Kp = 0;        // Kb * 32: row stride of `w` in bytes
   int8_t* w = nullptr;   // device [N, Kp] int8, K-major, zero tail bytes
   float* scale = nullptr;  // device [N] per-output-channel scale
-  // TMA descriptor of `w` for the GEMM's B tiles (box 32 B x kBlockN rows).
+  // TMA descriptor of `w` for the GEMM's B tiles (box kStageK B x kBlockN rows).
   CUtensorMap tmap_b;
   bool tmap_ready = false;
 };
 
 namespace ovb {
 
-// Rows / columns per GEMM output tile and pipeline depth.
+// Rows / columns per GEMM output tile; bytes of K per TMA box (four 32-k
+// quantisation blocks, one 128-byte swizzle row).
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
+constexpr int kStageK = 128;
 
 constexpr int kMaxSlices = 4;
 
@@ -52,8 +54,9 @@ void set_error(const std::string& msg);
 // CUDA error -> message; returns true when `e` is an error.
 bool cuda_failed(cudaError_t e, const char* what);
 
-// Encode a 2-D uint8 tensor map [rows, row_bytes] with a (32 B x box_rows)
-// box and 32-byte swizzle.  Returns false (and sets the error) on failure.
+// Encode a 2-D uint8 tensor map [rows, row_bytes] with a (kStageK B x
+// box_rows) box and 128-byte swizzle.  Returns false (and sets the error) on
+// failure.
 bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
                     uint64_t stride_bytes, uint32_t box_rows);
 

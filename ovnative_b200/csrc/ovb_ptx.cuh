@@ -142,16 +142,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
-// 32-byte swizzle: rows of 32 bytes, 8-row groups 256 bytes apart
-// (SBO = 256 B, LBO unused = 1, layout type 6 = SWIZZLE_32B, descriptor
-// version 1 for sm_100).  `addr` must be 256-byte aligned.
-__device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t addr) {
+// 128-byte swizzle: rows of 128 bytes (four 32-k int8 blocks), 8-row groups
+// 1024 bytes apart (SBO = 1024 B, LBO unused = 1, layout type 2 =
+// SWIZZLE_128B, descriptor version 1 for sm_100).  The tile base must be
+// 1024-byte aligned; `koff` (0, 32, 64, 96) selects the 32-byte K slice of
+// the rows that one K = 32 MMA reads -- the hardware applies the swizzle to
+// the advanced address.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t base, uint32_t koff) {
   uint64_t d = 0;
-  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);  // start address, bits [0,14)
-  d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (ignored)
-  d |= static_cast<uint64_t>(256 >> 4) << 32;          // stride byte offset
-  d |= static_cast<uint64_t>(1) << 46;                 // version
-  d |= static_cast<uint64_t>(6) << 61;                 // SWIZZLE_32B
+  d |= static_cast<uint64_t>(((base + koff) & 0x3FFFFu) >> 4);  // start address, bits [0,14)
+  d |= static_cast<uint64_t>(1) << 16;                         // leading byte offset (ignored)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                 // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                         // version
+  d |= static_cast<uint64_t>(2) << 61;                         // SWIZZLE_128B
   return d;
 }
 
