@@ -137,6 +137,19 @@ size_t ovb_linear_workspace_bytes(int64_t M, int64_t K);
 int ovb_linear(int64_t M, const ovb_weight* w, const float* A, int64_t lda, float* C,
                int64_t ldc, int accumulate, void* work, size_t work_bytes, void* stream);
 
+/* ovb_linear for callers that cannot allocate device memory (a host whose
+ * device memory all belongs to its own pool, a latency-critical step that
+ * must not pay for cudaMalloc's device synchronisation, an FFI binding that
+ * cannot own a device buffer).  Same arguments and results as ovb_linear
+ * without `work`: the quantised activations go to an 8 MiB device array
+ * inside the library, one per device, held until the process exits.
+ * Sizes with ovb_linear_workspace_bytes(M, K) above 8 MiB return
+ * OVB_ERR_INVALID_ARG.  Calls that overlap on the GPU race on the array; the
+ * first call on a device sets up the array's address and should come before
+ * any stream capture.  No counterpart in the reference. */
+int ovb_linear_static(int64_t M, const ovb_weight* w, const float* A, int64_t lda, float* C,
+                      int64_t ldc, int accumulate, void* stream);
+
 /* Exact per-32-k block products P[m, n, b] (int32 [M, N, Kb]) of the same
  * tensor-core mainloop, for parity checks of the integer arithmetic. */
 int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t* P,
