@@ -12,12 +12,12 @@
 //
 // Mapping.  One quantisation block (32 k) is one tcgen05.mma.kind::i8 with
 // K = 32, M = 128 rows of activations, N = 128 output channels.  Each block's
-// int32 product lands in its own TMEM accumulator (a ring of four 128-column
-// buffers = all 512 TMEM columns), so the tensor core runs up to four blocks
-// ahead of the fp32 epilogue.  TMA moves 128-byte-wide boxes (four blocks of
-// K, 128-byte swizzle); each MMA's descriptor points at its 32-byte K slice.
+// int32 product lands in its own TMEM accumulator (four 128-column buffers =
+// all 512 TMEM columns), so the tensor core runs ahead of the fp32 epilogue.
+// TMA moves 128-byte-wide boxes (four blocks of K, 128-byte swizzle); each
+// MMA's descriptor points at its 32-byte K slice.
 //
-// Warp roles (608 threads, one CTA per SM, persistent over output tiles):
+// Warp roles (640 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A box (128 B x 128 rows of aq) and B box (128 B
 //               x 128 rows of the packed weight) per stage into a 4-stage ring;
 //   warp 1      TMEM allocator + MMA issuer (lane 0 issues, the whole warp
@@ -27,28 +27,32 @@
 //               block's int32 products and folds them into 32 fp32 running
 //               sums per thread; at the end of the tile it stages the values
 //               in shared memory and writes them row by row (coalesced) with
-//               wscale and the optional residual applied.  Four epilogue
-//               warps per SM sub-partition let one warp's barrier wait and
-//               TMEM load overlap the others' arithmetic;
+//               wscale and the optional residual applied;
 //   warp 18     stage watcher: waits for each TMA stage to land and hands it
-//               to the MMA warp.
+//               to the MMA warp;
+//   warp 19     TMEM poller: waits for each MMA to complete and releases
+//               the epilogue warps.
 //
 // Handshakes.  A thread that has tcgen05.mma operations in flight stalls on
 // any shared-memory access of its own (an mbarrier wait included) until
 // those MMAs have read their operands -- measured here at ~400 clocks per
 // access, six times the 64-clock issue interval of a 128x128x32 int8 MMA.
-// So the MMA warp never waits on an mbarrier inside its loop.  It meets the
+// So the MMA warp never waits on an mbarrier inside its loop: it meets the
 // stage watcher on named barrier kBarFull (bar.sync, 64 threads, lockstep)
-// once per stage.  TMEM holds four block accumulators as two slots of two
-// (kGroup blocks per handshake): the MMA warp commits a slot's barrier once
-// both of its blocks are issued, waits on named barrier kBarTmem + g
-// (bar.sync, 544 threads) before refilling slot g, and the sixteen epilogue
-// warps signal that slot with bar.arrive after reading it -- so while the
-// epilogue drains one slot the tensor core fills the other.  Each slot's
-// arrivals and syncs alternate strictly, and every participant executes its
-// full count on every path (on an error it keeps signalling without doing
-// work), so no named barrier can be left waiting.
+// once per stage.  TMEM holds four block accumulators (slots).  The MMA warp
+// commits slot g's mbarrier after its MMA; the poller waits on that mbarrier
+// and bar.arrives on kBarReady + g,
+// on which the sixteen epilogue warps bar.sync -- so only one warp polls and
+// the epilogue warps sleep until their data is there.  After reading slot g
+// the epilogue warps bar.arrive on kBarTmem + g, on which the MMA warp
+// bar.syncs before refilling it; the MMA warp in turn bar.arrives on
+// kBarIssued + g after each MMA, on which the poller bar.syncs before waiting.  Each named barrier's arrivals and syncs
+// alternate strictly, and every participant executes its full count on every
+// path (after an error it keeps signalling without doing work), so no named
+// barrier can be left waiting.
 //
+// Every mbarrier wait is bounded (ovb_wait); on a timeout the kernel records
+// a non-zero status in g_status and the remaining waits return at once.
 #include "ovb_internal.h"
 #include "ovb_ptx.cuh"
 
@@ -61,17 +65,18 @@ namespace {
 constexpr int kBlocksPerStage = kStageK / 32;  // quantisation blocks per TMA box
 constexpr int kStages = 4;
 constexpr int kAccBufs = 4;
-constexpr int kGroup = 2;                        // blocks per TMEM handshake
-constexpr int kGroups = kAccBufs / kGroup;      // TMEM group slots
+constexpr int kSlots = kAccBufs;            // one block accumulator per TMEM slot
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiWarps = 16;
 constexpr int kWatcherWarp = 2 + kEpiWarps;
-constexpr int kThreads = 32 * (3 + kEpiWarps);
+constexpr int kPollerWarp = kWatcherWarp + 1;
+constexpr int kThreads = 32 * (kPollerWarp + 1);
 // named barriers (0 is __syncthreads)
-constexpr int kBarFull = 1;  // stage landed: watcher warp + MMA warp
-constexpr int kBarTmem = 2;  // kBarTmem + g: TMEM group slot g free: epilogue warps + MMA warp
+constexpr int kBarFull = 1;                    // stage landed: watcher + MMA warp
+constexpr int kBarTmem = 2;                     // + g: slot g read: epilogue warps -> MMA warp
+constexpr int kBarIssued = kBarTmem + kSlots;   // + g: slot g's MMA issued: MMA warp -> poller
+constexpr int kBarReady = kBarIssued + kSlots;  // + g: slot g written: poller -> epilogue warps
 constexpr int kBarFullThreads = 64;
-constexpr int kBarTmemThreads = 32 * (kEpiWarps + 1);
 constexpr uint32_t kABytes = kBlockM * kStageK;
 constexpr uint32_t kBBytes = kBlockN * kStageK;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -84,6 +89,7 @@ constexpr uint32_t kStgBytes = 32 * kStgStride * 4;
 static_assert(kAccBufs * kBlockN <= static_cast<int>(kTmemCols), "TMEM ring too large");
 static_assert(kEpiCols == 32, "the epilogue reads one 32-column TMEM slice per block");
 static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "128B-swizzle tiles need 1 KB bases");
+static_assert(kBarReady + kSlots <= 16, "the hardware has 16 named barriers");
 
 // status codes recorded in g_status (bit flags)
 constexpr int kErrProducer = 1;
@@ -94,7 +100,7 @@ constexpr int kErrDrain = 8;
 struct Ctl {
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t tfull[kGroups];
+  uint64_t tfull[kSlots];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -116,9 +122,9 @@ __device__ __forceinline__ void fail(Ctl* ctl, int code) {
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
 }
 
-// Block scales of rows m for blocks b0..b0+3 (zero past Kb or for rows >= M).
-__device__ __forceinline__ float4 load_scales4(const float* asc_row, int64_t b0, int64_t Kb,
-                                               bool row_ok, bool vec) {
+// Block scales of row m for blocks b0..b0+3 (zero past Kb or for rows >= M).
+__device__ __forceinline__ float4 load_scales4(const float* asc_row, int b0, int Kb, bool row_ok,
+                                               bool vec) {
   if (!row_ok) return make_float4(0.f, 0.f, 0.f, 0.f);
   if (vec) return __ldg(reinterpret_cast<const float4*>(asc_row + b0));
   float v[4];
@@ -127,9 +133,34 @@ __device__ __forceinline__ float4 load_scales4(const float* asc_row, int64_t b0,
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
+// f[j] = fma((float)P[j], s, f[j]) for one 16-column half of a block
+// (columns 0..15 or 16..31 of the warp's slice) -- one exact int->fp32
+// conversion and one fused multiply-add per output, as the reference does.
+template <int kHalf>
+__device__ __forceinline__ void fold_half(float (&f)[32], const uint32_t (&r)[16], float s) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    f[kHalf * 16 + j] = __fmaf_rn(__int2float_rn(static_cast<int>(r[j])), s, f[kHalf * 16 + j]);
+}
+
+// The slot barriers:
+//   kBarTmem + g    the 16 epilogue warps arrive when slot g is read; the MMA
+//                   warp syncs before refilling it;
+//   kBarIssued + g  the MMA warp arrives once it has issued slot g's MMA; the
+//                   poller syncs before waiting for that MMA to complete;
+//   kBarReady + g   the poller arrives when slot g's MMA has completed; the
+//                   16 epilogue warps sync before reading the slot.
+// Every arrival on one of them happens after the previous generation of that
+// barrier has completed (each arrive follows, through the other two, the sync
+// of the generation before), so generations never merge -- also on the error
+// path, where a failed mbarrier wait lets the poller go on without data.  The
+// MMA warp never waits for the poller: an earlier version in which both synced
+// on one "free" barrier held every MMA until the poller had seen the previous
+// one complete, serialising them (~390 clocks per block).
+constexpr int kBarSlotThreads = 32 * (kEpiWarps + 1);
+constexpr int kBarIssuedThreads = 64;
+
 template <bool kProducts>
-// 19 warps: five share one SM sub-partition's 16K registers, so at most 96
-// registers per thread.
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_s8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -145,22 +176,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int64_t M = args.M, N = args.N, Kb = args.Kb;
-  const int64_t ksteps = (Kb + kBlocksPerStage - 1) / kBlocksPerStage;
+  const int64_t M = args.M, N = args.N;
+  const int Kb = static_cast<int>(args.Kb);
+  const int ksteps = (Kb + kBlocksPerStage - 1) / kBlocksPerStage;
   const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
   const int64_t n_tiles = (N + kBlockN - 1) / kBlockN;
   const int64_t tiles = m_tiles * n_tiles;
   const int64_t my_tiles =
       tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-  const int64_t tile_groups = (Kb + kGroup - 1) / kGroup;
-  const int64_t my_groups = my_tiles * tile_groups;  // TMEM handshakes of this CTA
+  const int64_t my_fills = my_tiles * Kb;  // TMEM slot fills (= MMAs) of this CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&ctl->full[s]), 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
     }
-    for (int g = 0; g < kGroups; ++g) mbar_init(smem_u32(&ctl->tfull[g]), 1);
+    for (int g = 0; g < kSlots; ++g) mbar_init(smem_u32(&ctl->tfull[g]), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -186,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
         const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
         const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * kBlockN);
-        for (int64_t j = 0; j < ksteps; ++j, ++st) {
+        for (int j = 0; j < ksteps; ++j, ++st) {
           const int s = static_cast<int>(st % kStages);
           const uint32_t ph = static_cast<uint32_t>((st / kStages) & 1);
           if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
@@ -197,9 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t full = smem_u32(&ctl->full[s]);
           const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * kStageBytes);
           mbar_arrive_expect_tx(full, kStageBytes);
-          const int32_t x = static_cast<int32_t>(j * kStageK);
-          tma_load_2d(sa, &tmap_a, x, m0, full);
-          tma_load_2d(sa + kABytes, &tmap_b, x, n0, full);
+          tma_load_2d(sa, &tmap_a, j * kStageK, m0, full);
+          tma_load_2d(sa + kABytes, &tmap_b, j * kStageK, n0, full);
         }
       }
       if (!ok) {
@@ -216,38 +246,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
-    // One K = 32 MMA per quantisation block, each into its own TMEM buffer.
+    // One K = 32 MMA per quantisation block into TMEM slot g = fill % 4.
     // The whole warp walks the loop (named barriers count warps); lane 0
-    // issues.  No shared-memory access happens here until the final drain.
+    // issues.  No shared-memory access here until the final drain.
     const uint32_t idesc = idesc_i8(kBlockM, kBlockN);
     int64_t st = 0, q = 0;
     for (int64_t t = 0; t < my_tiles; ++t) {
-      uint32_t sa = 0;
-      int s = 0;
-      for (int64_t b = 0; b < Kb; ++b) {
-        const int kk = static_cast<int>(b % kBlocksPerStage);
-        if (kk == 0) {
-          s = static_cast<int>(st % kStages);
-          named_sync(kBarFull, kBarFullThreads);  // stage s has landed
-          sa = smem_u32(smem + static_cast<size_t>(s) * kStageBytes);
+      for (int j = 0; j < ksteps; ++j, ++st) {
+        const int s = static_cast<int>(st % kStages);
+        named_sync(kBarFull, kBarFullThreads);  // stage s has landed
+        const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * kStageBytes);
+        const int nb = Kb - j * kBlocksPerStage < kBlocksPerStage ? Kb - j * kBlocksPerStage
+                                                                  : kBlocksPerStage;
+        for (int kk = 0; kk < nb; ++kk, ++q) {
+          const int g = static_cast<int>(q & (kSlots - 1));
+          if (q >= kSlots) named_sync(kBarTmem + g, kBarSlotThreads);  // slot g read
+          if (lane == 0) {
+            tc_fence_after();
+            mma_i8(tmem_base + static_cast<uint32_t>(g * kBlockN),
+                   sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
+                   sw128_kmajor_desc(sa + kABytes, static_cast<uint32_t>(kk * 32)), idesc, 0u);
+            tc_commit(smem_u32(&ctl->tfull[g]));
+          }
+          __syncwarp();
+          named_arrive(kBarIssued + g, kBarIssuedThreads);
         }
-        const int g = static_cast<int>(q % kGroups);
-        const int in_group = static_cast<int>(b % kGroup);
-        if (in_group == 0 && q >= kGroups) named_sync(kBarTmem + g, kBarTmemThreads);  // slot g read
-        if (lane == 0) {
-          tc_fence_after();
-          mma_i8(tmem_base + static_cast<uint32_t>((g * kGroup + in_group) * kBlockN),
-                 sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
-                 sw128_kmajor_desc(sa + kABytes, static_cast<uint32_t>(kk * 32)), idesc, 0u);
-        }
-        if (in_group == kGroup - 1 || b == Kb - 1) {
-          if (lane == 0) tc_commit(smem_u32(&ctl->tfull[g]));
-          ++q;
-        }
-        if (kk == kBlocksPerStage - 1 || b == Kb - 1) {
-          if (lane == 0) tc_commit(smem_u32(&ctl->empty[s]));
-          ++st;
-        }
+        if (lane == 0) tc_commit(smem_u32(&ctl->empty[s]));
         __syncwarp();
       }
     }
@@ -265,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // word reports the failure).
     int64_t st = 0;
     for (int64_t t = 0; t < my_tiles; ++t) {
-      for (int64_t j = 0; j < ksteps; ++j, ++st) {
+      for (int j = 0; j < ksteps; ++j, ++st) {
         const int s = static_cast<int>(st % kStages);
         const uint32_t ph = static_cast<uint32_t>((st / kStages) & 1);
         const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
@@ -273,79 +297,93 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_sync(kBarFull, kBarFullThreads);
       }
     }
+  } else if (warp == kPollerWarp) {
+    // -------------------------------------------------------- TMEM poller
+    for (int64_t q = 0; q < my_fills; ++q) {
+      const int g = static_cast<int>(q & (kSlots - 1));
+      named_sync(kBarIssued + g, kBarIssuedThreads);  // slot g's MMA has been issued
+      const uint32_t ph = static_cast<uint32_t>((q / kSlots) & 1);
+      const bool got = ovb_wait(smem_u32(&ctl->tfull[g]), ph, abort);
+      if (!__all_sync(0xffffffffu, got) && lane == 0) fail(ctl, kErrEpilogue);
+      named_arrive(kBarReady + g, kBarSlotThreads);
+    }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;          // TMEM lanes this warp may read
-    const int group = (warp - 2) >> 2;     // which 32 of the 128 tile columns
+    const int quarter = warp & 3;       // TMEM lanes this warp may read
+    const int cgroup = (warp - 2) >> 2;  // which 32 of the 128 tile columns
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const bool vec_asc =
         ((Kb & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.asc) & 15) == 0);
     float* stg = stg_all + (warp - 2) * (32 * kStgStride);
-    int64_t q = 0;  // TMEM groups consumed
-    bool ok = true;  // false after a failed wait: keep signalling, skip work
+    int64_t q = 0;  // TMEM slot fills consumed
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       const int64_t m0 = (tile % m_tiles) * kBlockM;
       const int64_t n0 = (tile / m_tiles) * kBlockN;
       const int64_t m = m0 + quarter * 32 + lane;
       const bool row_ok = m < M;
-      const float* asc_row = args.asc + (row_ok ? m : 0) * Kb;
-      const int64_t nc = n0 + group * kEpiCols;  // first column of this warp's slice
+      const float* asc_row = args.asc + (row_ok ? m : 0) * static_cast<int64_t>(Kb);
+      const int64_t nc = n0 + cgroup * kEpiCols;  // first column of this warp's slice
       float f[kEpiCols];
 #pragma unroll
       for (int j = 0; j < kEpiCols; ++j) f[j] = 0.f;
-      float4 sv_next =
-          kProducts ? make_float4(0.f, 0.f, 0.f, 0.f) : load_scales4(asc_row, 0, Kb, row_ok, vec_asc);
-      for (int64_t b0 = 0; b0 < Kb; b0 += 4) {
+      float4 sv_next = kProducts ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                 : load_scales4(asc_row, 0, Kb, row_ok, vec_asc);
+      // Software pipeline over half-blocks: while the low 16 columns of block
+      // b load from TMEM, the high 16 columns of block b-1 are folded in;
+      // while the high half of b loads, its low half is folded in.  The fold
+      // order per output is still b = 0, 1, 2, ...  (The TMEM load is as slow
+      // as the arithmetic; done back to back they do not overlap, because all
+      // epilogue warps reach each block at the same time.)
+      uint32_t r_lo[16], r_hi[16];
+      float s_prev = 0.f;
+      for (int b0 = 0; b0 < Kb; b0 += 4) {
         const float4 sv = sv_next;
         if (!kProducts && b0 + 4 < Kb) sv_next = load_scales4(asc_row, b0 + 4, Kb, row_ok, vec_asc);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          if (b0 + kk >= Kb) break;
-          const int64_t b = b0 + kk;
+          const int b = b0 + kk;
+          if (b >= Kb) break;
           const float s = kk == 0 ? sv.x : kk == 1 ? sv.y : kk == 2 ? sv.z : sv.w;
-          const int g = static_cast<int>(q % kGroups);
-          const int in_group = static_cast<int>(b % kGroup);
-          const bool last_in_group = in_group == kGroup - 1 || b == Kb - 1;
-          if (ok && in_group == 0) {
-            const uint32_t gph = static_cast<uint32_t>((q / kGroups) & 1);
-            const bool got = ovb_wait(smem_u32(&ctl->tfull[g]), gph, abort);
-            if (!__all_sync(0xffffffffu, got)) {
-              if (lane == 0) fail(ctl, kErrEpilogue);
-              ok = false;
-            }
-            if (ok) tc_fence_after();
+          const int g = static_cast<int>(q & (kSlots - 1));
+          named_sync(kBarReady + g, kBarSlotThreads);  // slot g holds block b
+          tc_fence_after();
+          const uint32_t taddr =
+              tmem_base + lane_off + static_cast<uint32_t>(g * kBlockN + cgroup * kEpiCols);
+          tmem_ld16(taddr, r_lo);
+          if constexpr (!kProducts) {
+            if (b > 0) fold_half<1>(f, r_hi, s_prev);  // block b-1, columns 16..31
           }
-          uint32_t r[32];
-          if (ok) {
-            tmem_ld32(tmem_base + lane_off +
-                          static_cast<uint32_t>((g * kGroup + in_group) * kBlockN + group * kEpiCols),
-                      r);
-            tc_wait_ld();
-          }
-          if (last_in_group) {
-            tc_fence_before();
-            // Slot g is free again; the MMA warp waits for this only when it
-            // will reuse the slot, i.e. not for the last kGroups groups.
-            if (q + kGroups < my_groups) named_arrive(kBarTmem + g, kBarTmemThreads);
-            ++q;
-          }
-          if (!ok) continue;
+          tc_wait_ld16(r_lo);
           if constexpr (kProducts) {
             if (row_ok) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
+              for (int j = 0; j < 16; ++j) {
                 const int64_t n = nc + j;
-                if (n < N) args.products[(m * N + n) * Kb + b] = static_cast<int32_t>(r[j]);
+                if (n < N) args.products[(m * N + n) * Kb + b] = static_cast<int32_t>(r_lo[j]);
               }
             }
-          } else {
+          }
+          tmem_ld16(taddr + 16, r_hi);
+          if constexpr (!kProducts) fold_half<0>(f, r_lo, s);  // block b, columns 0..15
+          tc_wait_ld16(r_hi);
+          tc_fence_before();
+          // Slot g is free again; the MMA warp waits for this only when it
+          // will refill the slot, i.e. not for the last kSlots fills.
+          if (q + kSlots < my_fills) named_arrive(kBarTmem + g, kBarSlotThreads);
+          ++q;
+          s_prev = s;
+          if constexpr (kProducts) {
+            if (row_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              f[j] = __fmaf_rn(__int2float_rn(static_cast<int>(r[j])), s, f[j]);
+              for (int j = 0; j < 16; ++j) {
+                const int64_t n = nc + 16 + j;
+                if (n < N) args.products[(m * N + n) * Kb + b] = static_cast<int32_t>(r_hi[j]);
+              }
+            }
           }
         }
       }
-      if (!ok) continue;
+      if constexpr (!kProducts) fold_half<1>(f, r_hi, s_prev);  // last block, columns 16..31
       if constexpr (!kProducts) {
         // Stage the warp's 32 x 32 block in shared memory, then write it out
         // row by row: each store instruction covers 128 contiguous bytes of
