@@ -114,13 +114,16 @@ int invalid(const std::string& msg) {
 
 int internal_err() { return OVB_ERR_INTERNAL; }
 
+// Tensor maps of the packed weight for every GEMM tile width.
 bool ensure_weight_tmap(ovb_weight* w) {
-  if (w->tmap_ready) return true;
-  if (!ovb::encode_tmap_u8(&w->tmap_b, w->w, static_cast<uint64_t>(w->Kp),
-                           static_cast<uint64_t>(w->N), static_cast<uint64_t>(w->Kp),
-                           ovb::kBlockN))
-    return false;
-  w->tmap_ready = true;
+  for (int i = 0; i < 3; ++i) {
+    if (w->tmap_ready[i]) continue;
+    if (!ovb::encode_tmap_u8(&w->tmap_b[i], w->w, static_cast<uint64_t>(w->Kp),
+                             static_cast<uint64_t>(w->N), static_cast<uint64_t>(w->Kp),
+                             static_cast<uint32_t>(ovb::kTileN[i])))
+      return false;
+    w->tmap_ready[i] = true;
+  }
   return true;
 }
 
@@ -156,7 +159,8 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
   args.n_slices = n_slices;
   for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
   args.products = products;
-  if (cuda_failed(ovb::launch_gemm(tmap_a, w->tmap_b, args, s), "gemm launch"))
+  const int tile = ovb::pick_tile(M, w->N, w->device);
+  if (cuda_failed(ovb::launch_gemm(tile, tmap_a, w->tmap_b[tile], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
 }

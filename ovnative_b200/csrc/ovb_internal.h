@@ -16,9 +16,10 @@ struct ovb_weight {
   int64_t Kp = 0;        // Kb * 32: row stride of `w` in bytes
   int8_t* w = nullptr;   // device [N, Kp] int8, K-major, zero tail bytes
   float* scale = nullptr;  // device [N] per-output-channel scale
-  // TMA descriptor of `w` for the GEMM's B tiles (box kStageK B x kBlockN rows).
-  CUtensorMap tmap_b;
-  bool tmap_ready = false;
+  // TMA descriptors of `w` for the GEMM's B tiles, one per tile width
+  // (box kStageK B x kTileN[i] rows), built on first use.
+  CUtensorMap tmap_b[3];
+  bool tmap_ready[3] = {false, false, false};
 };
 
 namespace ovb {
@@ -26,8 +27,9 @@ namespace ovb {
 // Rows / columns per GEMM output tile; bytes of K per TMA box (four 32-k
 // quantisation blocks, one 128-byte swizzle row).
 constexpr int kBlockM = 128;
-constexpr int kBlockN = 128;
 constexpr int kStageK = 128;
+// Output-tile widths the GEMM is built for (one kernel per width).
+constexpr int kTileN[3] = {128, 64, 32};
 
 constexpr int kMaxSlices = 4;
 
@@ -74,7 +76,10 @@ cudaError_t launch_pack_nk(const int8_t* src, int64_t N, int64_t K, int8_t* dst,
                            cudaStream_t s);
 cudaError_t launch_pack_kn(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
                            cudaStream_t s);
-cudaError_t launch_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
+// Index into kTileN of the tile width used for an M x N GEMM: the widest
+// one that still gives every SM a tile (OVB_GEMM_TILE_N overrides it).
+int pick_tile(int64_t M, int64_t N, int device);
+cudaError_t launch_gemm(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
                         const GemmArgs& args, cudaStream_t s);
 
 // Device status word (0 = every bounded wait completed).

@@ -125,6 +125,15 @@ __device__ __forceinline__ void tc_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 lanes x 8 consecutive 32-bit columns (see tmem_ld32).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
 // 32 lanes x 16 consecutive 32-bit columns (see tmem_ld32).  The registers
 // are written asynchronously: read them only after tc_wait_ld16(r).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -184,7 +193,7 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t base, uint32_t ko
 }
 
 // Instruction descriptor for kind::i8: s8 x s8 -> s32, both K-major,
-// M = 128, N = n.
+// M = m (64 or 128), N = n (a multiple of 16 up to 256 for M = 128).
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4)             // D format: S32
          | (1u << 7)           // A format: signed int8

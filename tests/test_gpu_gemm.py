@@ -188,3 +188,51 @@ def test_argument_errors(cuda):
     out = ovb.linear_s8_nk_packed_q(aq[:0], asc[:0], w)
     assert out.shape == (0, 192)
     assert ovb.device_status() == 0
+
+
+# K = 33, 96, 160, 1056: 2, 3, 5, 33 quantisation blocks, so the last TMEM
+# slot of a tile holds fewer blocks than the slot size (1, 2 or 4 by width).
+WIDTH_CASES = [(1, 8, 33), (127, 130, 96), (129, 257, 160), (300, 1000, 1056), (400, 1024, 2048)]
+
+
+@pytest.mark.parametrize("tile_n", [128, 64, 32])
+@pytest.mark.parametrize("M,N,K", WIDTH_CASES)
+def test_every_tile_width_bit_exact(cuda, monkeypatch, tile_n, M, N, K):
+    """The GEMM is built for output tiles 128, 64 and 32 columns wide; the
+    host picks one by shape.  Force each and check the plain, residual-add
+    and products outputs against the port."""
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    W = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    s = (np.abs(rng.standard_normal(N)) * 0.02 / 127 + 1e-6).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    w = ovb.Weight.from_nk(W, s)
+    aq, asc = ovb.s8_nk_quantize(dev(A, cuda))
+    aq_h, asc_h = O.quantize(A)
+    check_close_and_exact(host(ovb.linear_s8_nk_packed_q(aq, asc, w)),
+                          O.linear_q(aq_h, asc_h, W, s, K))
+    C = dev(C0, cuda)
+    ovb.linear_s8_nk_packed_q_add(aq, asc, w, C)
+    check_close_and_exact(host(C), O.linear_q(aq_h, asc_h, W, s, K, C_in=C0))
+    if M * N * ((K + 31) // 32) <= 4_000_000:
+        assert np.array_equal(host(ovb.block_products(aq, w)), O.block_products(aq_h, W, K))
+    assert ovb.device_status() == 0
+
+
+@pytest.mark.parametrize("tile_n", [64, 32])
+def test_narrow_tiles_sliced(cuda, golden, monkeypatch, tile_n):
+    """Sliced output (qkv / gate|up) with narrow tiles: slices are multiples
+    of 64 columns, so a warp's columns never straddle two slices."""
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    for i in range(3):
+        Ns = [int(n) for n in golden[f"sliced{i}_Ns"]]
+        parts = [ovb.Weight.from_nk(golden[f"sliced{i}_W{j}"], golden[f"sliced{i}_s{j}"])
+                 for j in range(len(Ns))]
+        wc = ovb.Weight.concat(parts)
+        A = dev(golden[f"sliced{i}_A"], cuda)
+        aq, asc = ovb.s8_nk_quantize(A)
+        Cs = [torch.full((A.shape[0], n), float("nan"), device=cuda) for n in Ns]
+        ovb.linear_s8_nk_packed_q_sliced(aq, asc, wc, Cs)
+        for j, c in enumerate(Cs):
+            check_close_and_exact(host(c), golden[f"sliced{i}_C{j}"])
