@@ -17,6 +17,12 @@
  *     o = f * wscale[n], then o = o + C_old when accumulating.
  *   Following that order makes the fp32 output bit-identical to the
  *   reference's.
+ * A weight created with OVB_WEIGHT_F16 instead runs the fp16 tensor-core
+ * mainloop: the same quantised activations, dequantised on the GPU to
+ * fp16(q * asc) and multiplied with the (exact) fp16 weights into one fp32
+ * accumulator.  Its outputs agree with the reference within relative L2
+ * ~3e-4 (contract: <= 1e-3, max-abs <= 1e-2 * rms), not bit for bit, and
+ * need |activations| < 65504.  ovb_block_products always uses the int8 path.
  *
  * Activation buffers ("aq/asc"):
  *   aq  : int8 q, row-major [M, Kp], Kp = 32*ceil(K/32), tail bytes zero.
@@ -59,7 +65,13 @@ extern "C" {
 
 /* flags */
 #define OVB_SRC_DEVICE 1 /* ovb_weight_create: W and scale are device pointers */
+#define OVB_WEIGHT_F16 2 /* ovb_weight_create: also keep an fp16 copy; GEMMs with this
+                            handle run the fp16 mainloop (see above).  No counterpart
+                            in the reference's CPU path; its CUDA runner multiplies
+                            dequantised fp16 weights (cuda_lm.cu:840-873). */
 #define OVB_AQ_U8 1      /* quantisers: write reference u8 (q+128) instead of int8 */
+#define OVB_AQ_F16 2     /* quantisers: write fp16(q * asc), [M, Kp] fp16 (2 bytes per
+                            element, 16-byte aligned), the input of ovb_linear_h */
 
 typedef struct ovb_weight ovb_weight;
 
@@ -74,9 +86,10 @@ typedef struct ovb_slice {
 int ovb_abi_version(void);
 const char* ovb_last_error(void);
 
-/* Per-launch device status of the last GEMM on this thread's device: 0 when
- * every bounded wait inside the kernels completed.  Reading it synchronises
- * the given stream. */
+/* Device status of the GEMMs since the last call, on this thread's device:
+ * 0 when every bounded wait inside the kernels completed.  Bit 16 reports an
+ * activation block beyond the fp16 range in the fp16 mainloop.  Reading it
+ * synchronises the given stream and clears it. */
 int ovb_device_status(void* stream);
 
 /* --- sizes ------------------------------------------------------------ */
@@ -94,7 +107,8 @@ int64_t ovb_quant_scales(int64_t M, int64_t K);
 int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const float* scale,
                       int flags, void* stream, ovb_weight** out);
 /* Concatenate weights with the same K along N (q|k|v, gate|up).  Replaces
- * combine_packed (lm.cpp:57-94).  The parts stay valid. */
+ * combine_packed (lm.cpp:57-94).  The parts stay valid.  The result has the
+ * fp16 copy (OVB_WEIGHT_F16) when every part has it. */
 int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
                       ovb_weight** out);
 int ovb_weight_destroy(ovb_weight* w);
@@ -127,6 +141,18 @@ int ovb_linear_q(int64_t M, const ovb_weight* w, const int8_t* aq, const float* 
  * Replaces ov::linear_s8_nk_packed_q_sliced (ov_gemm.h:109-111). */
 int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
                         const ovb_slice* slices, int n_slices, void* stream);
+
+/* The fp16 mainloop on already-dequantised activations: a16 is [M, Kp] fp16,
+ * fp16(q * asc) as written by a quantiser with OVB_AQ_F16; w must have been
+ * created with OVB_WEIGHT_F16.  Same outputs (slices, residual add) and
+ * tolerance as ovb_linear_q on such a handle, without converting the int8
+ * activations once per output tile.  No counterpart in the reference: it
+ * splits the reference's quantise+GEMM pair (s8_nk_quantize +
+ * linear_s8_nk_packed_q) at a different point. */
+int ovb_linear_h(int64_t M, const ovb_weight* w, const void* a16, float* C, int64_t ldc,
+                 int accumulate, void* stream);
+int ovb_linear_h_sliced(int64_t M, const ovb_weight* w, const void* a16, const ovb_slice* slices,
+                        int n_slices, void* stream);
 /* fp32 activations in, quantised inside (two launches).  accumulate = 0
  * replaces ov::linear_s8_nk_packed (ov_gemm.h:67-69); accumulate = 1
  * replaces ov::linear_s8_nk_packed_add (ov_gemm.h:73-75).  `work` is a device

@@ -11,6 +11,9 @@ from .gemm import (  # noqa: F401
     block_products,
     device_status,
     empty_quant,
+    empty_quant_f16,
+    linear_h,
+    linear_h_sliced,
     linear_s8_nk_packed,
     linear_s8_nk_packed_add,
     linear_s8_nk_packed_q,

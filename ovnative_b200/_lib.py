@@ -18,7 +18,9 @@ OVB_ERR_INTERNAL = -4
 OVB_LAYOUT_NK = 0
 OVB_LAYOUT_KN = 1
 OVB_SRC_DEVICE = 1
+OVB_WEIGHT_F16 = 2
 OVB_AQ_U8 = 1
+OVB_AQ_F16 = 2
 
 _i64 = C.c_int64
 _p = C.c_void_p
@@ -46,6 +48,8 @@ SIGNATURES = {
     "ovb_silu_mul_quantize": ([_i64, _i64, _p, _i64, _p, _i64, _p, _p, _int, _p], _int),
     "ovb_linear_q": ([_i64, _p, _p, _p, _p, _i64, _int, _p], _int),
     "ovb_linear_q_sliced": ([_i64, _p, _p, _p, C.POINTER(Slice), _int, _p], _int),
+    "ovb_linear_h": ([_i64, _p, _p, _p, _i64, _int, _p], _int),
+    "ovb_linear_h_sliced": ([_i64, _p, _p, C.POINTER(Slice), _int, _p], _int),
     "ovb_linear_workspace_bytes": ([_i64, _i64], C.c_size_t),
     "ovb_linear": ([_i64, _p, _p, _i64, _p, _i64, _int, _p, C.c_size_t, _p], _int),
     "ovb_linear_static": ([_i64, _p, _p, _i64, _p, _i64, _int, _p], _int),

@@ -66,32 +66,38 @@ int num_sms(int device) {
   return cache[static_cast<size_t>(device)];
 }
 
-bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
-                    uint64_t stride_bytes, uint32_t box_rows) {
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                    uint64_t inner, uint64_t rows, uint64_t stride_bytes, uint32_t box_inner,
+                    uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
     return false;
   }
-  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t dims[2] = {inner, rows};
   const cuuint64_t strides[1] = {stride_bytes};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kStageK), box_rows};
+  const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t elem_strides[2] = {1u, 1u};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
-                        strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     char buf[160];
     std::snprintf(buf, sizeof buf,
-                  "cuTensorMapEncodeTiled failed (%d): rows=%llu row_bytes=%llu stride=%llu",
+                  "cuTensorMapEncodeTiled failed (%d): rows=%llu inner=%llu stride=%llu",
                   static_cast<int>(r), static_cast<unsigned long long>(rows),
-                  static_cast<unsigned long long>(row_bytes),
+                  static_cast<unsigned long long>(inner),
                   static_cast<unsigned long long>(stride_bytes));
     set_error(buf);
     return false;
   }
   return true;
+}
+
+bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
+                    uint64_t stride_bytes, uint32_t box_rows) {
+  return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, rows, stride_bytes,
+                        static_cast<uint32_t>(kStageK), box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace ovb
@@ -105,6 +111,13 @@ inline int64_t kblocks(int64_t K) { return (K + 31) / 32; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+// Output form of a quantiser from its flags (0 int8, 1 u8, 2 fp16), or -1.
+int quant_mode(int flags) {
+  const int f = flags & (OVB_AQ_U8 | OVB_AQ_F16);
+  if (f == (OVB_AQ_U8 | OVB_AQ_F16)) return -1;
+  return f == OVB_AQ_F16 ? 2 : (f == OVB_AQ_U8 ? 1 : 0);
 }
 
 int invalid(const std::string& msg) {
@@ -125,6 +138,37 @@ bool ensure_weight_tmap(ovb_weight* w) {
     w->tmap_ready[i] = true;
   }
   return true;
+}
+
+// Tensor maps of the fp16 weight copy for every fp16-mainloop tile width.
+bool ensure_weight_tmap16(ovb_weight* w) {
+  if (!w->w16) return true;
+  for (int i = 0; i < 4; ++i) {
+    if (w->tmap16_ready[i]) continue;
+    if (!ovb::encode_tmap_2d(&w->tmap_w16[i], w->w16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->N),
+                             static_cast<uint64_t>(w->Kp) * 2, 64u,
+                             static_cast<uint32_t>(ovb::kTileNF[i]), CU_TENSOR_MAP_SWIZZLE_128B))
+      return false;
+    w->tmap16_ready[i] = true;
+  }
+  return true;
+}
+
+// Allocate and fill the fp16 copy of a packed weight.
+bool make_weight_f16(ovb_weight* w, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(w->N * w->Kp);
+  return !cuda_failed(cudaMalloc(&w->w16, n * 2), "cudaMalloc(fp16 weight)") &&
+         !cuda_failed(ovb::launch_widen_f16(w->w, static_cast<int64_t>(n), w->w16, s),
+                      "widen weight") &&
+         !cuda_failed(cudaStreamSynchronize(s), "widen sync") && ensure_weight_tmap16(w);
+}
+
+void free_weight(ovb_weight* w) {
+  cudaFree(w->w);
+  cudaFree(w->scale);
+  cudaFree(w->w16);
+  delete w;
 }
 
 // Common checks of a pre-quantised GEMM call.  Returns OVB_OK or a status.
@@ -150,6 +194,13 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
                            static_cast<uint64_t>(w->Kp), ovb::kBlockM))
     return OVB_ERR_INTERNAL;
   ovb::GemmArgs args{};
+  const bool f16 = w->w16 != nullptr && products == nullptr;
+  CUtensorMap tmap_a16;
+  if (f16 && !ovb::encode_tmap_2d(&tmap_a16, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                                  static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(M),
+                                  static_cast<uint64_t>(w->Kp), 64u,
+                                  static_cast<uint32_t>(ovb::kBlockM), CU_TENSOR_MAP_SWIZZLE_64B))
+    return OVB_ERR_INTERNAL;
   args.M = M;
   args.N = w->N;
   args.Kb = w->Kb;
@@ -159,9 +210,76 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
   args.n_slices = n_slices;
   for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
   args.products = products;
+  if (f16) {
+    if (!ensure_weight_tmap16(w)) return OVB_ERR_INTERNAL;
+    const int tile = ovb::pick_tile_f16(M, w->N, w->Kb, w->device);
+    if (cuda_failed(ovb::launch_gemm_f16(tile, tmap_a16, w->tmap_w16[tile], args, s),
+                    "gemm launch"))
+      return OVB_ERR_INTERNAL;
+    return OVB_OK;
+  }
   const int tile = ovb::pick_tile(M, w->N, w->device);
   if (cuda_failed(ovb::launch_gemm(tile, tmap_a, w->tmap_b[tile], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+// The plain fp16 mainloop on dequantised activations a16 [M, Kp] fp16.
+int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::SliceOut* slices,
+               int n_slices, int accumulate, cudaStream_t s) {
+  ovb_weight* w = const_cast<ovb_weight*>(wc);
+  if (!ensure_weight_tmap16(w)) return OVB_ERR_INTERNAL;
+  CUtensorMap tmap_a;
+  if (!ovb::encode_tmap_2d(&tmap_a, a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(M),
+                           static_cast<uint64_t>(w->Kp) * 2, 64u,
+                           static_cast<uint32_t>(ovb::kBlockM), CU_TENSOR_MAP_SWIZZLE_128B))
+    return OVB_ERR_INTERNAL;
+  ovb::GemmArgs args{};
+  args.M = M;
+  args.N = w->N;
+  args.Kb = w->Kb;
+  args.asc = nullptr;
+  args.wscale = w->scale;
+  args.accumulate = accumulate;
+  args.n_slices = n_slices;
+  for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
+  args.products = nullptr;
+  const int tile = ovb::pick_tile_h(M, w->N, w->Kb, w->device);
+  if (cuda_failed(ovb::launch_gemm_h(tile, tmap_a, w->tmap_w16[tile], args, s), "gemm launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+// Validate a slice list against a concatenated weight and convert it to
+// the kernels' form (first column of each slice).  Returns OVB_OK or a status.
+int build_slices(const ovb_weight* w, const ovb_slice* slices, int n_slices,
+                 ovb::SliceOut (&so)[ovb::kMaxSlices]) {
+  if (!slices) return invalid("slices is null");
+  if (n_slices > ovb::kMaxSlices) return invalid("at most 4 slices");
+  int64_t total = 0;
+  for (int i = 0; i < n_slices; ++i) {
+    // gemm.cpp:786-788: each slice N must be a positive multiple of 64.
+    if (slices[i].N <= 0 || slices[i].N % 64 != 0 || !slices[i].C)
+      return invalid("sliced GEMM: each slice N must be a positive multiple of 64");
+    if (slices[i].ldc < slices[i].N) return invalid("sliced GEMM: ldc < N");
+    so[i] = ovb::SliceOut{total, slices[i].N, slices[i].C, slices[i].ldc};
+    total += slices[i].N;
+  }
+  if (total != w->N) return invalid("sliced GEMM: slice widths do not add up to the weight's N");
+  return OVB_OK;
+}
+
+// Common checks of an ovb_linear_h call.
+int check_h_args(int64_t M, const ovb_weight* w, const void* a16) {
+  if (!w) return invalid("weight handle is null");
+  if (!w->w16) return invalid("ovb_linear_h needs a weight created with OVB_WEIGHT_F16");
+  if (!a16) return invalid("a16 is null");
+  if (!aligned(a16, 16)) return invalid("a16 must be 16-byte aligned (TMA source)");
+  if (M > (int64_t{1} << 31) - 1) return invalid("M exceeds 2^31-1");
+  int dev = 0;
+  if (cuda_failed(cudaGetDevice(&dev), "cudaGetDevice")) return OVB_ERR_INTERNAL;
+  if (dev != w->device) return invalid("weight lives on another device than the current one");
   return OVB_OK;
 }
 
@@ -174,9 +292,12 @@ int ovb_abi_version(void) { return OVB_ABI_VERSION; }
 const char* ovb_last_error(void) { return ovb::t_error.c_str(); }
 
 int ovb_device_status(void* stream) {
-  int st = 0;
-  if (cuda_failed(ovb::read_and_clear_status(&st, as_stream(stream)), "read device status"))
+  int st = 0, st16 = 0, stq = 0;
+  if (cuda_failed(ovb::read_and_clear_status(&st, as_stream(stream)), "read device status") ||
+      cuda_failed(ovb::read_and_clear_status_f16(&st16, as_stream(stream)), "read device status") ||
+      cuda_failed(ovb::read_and_clear_status_q(&stq, as_stream(stream)), "read device status"))
     return OVB_ERR_INTERNAL;
+  st |= st16 | stq;
   return st;
 }
 
@@ -238,10 +359,9 @@ int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const f
   }
   if (!on_device && src_dev) cudaFree(src_dev);
   if (ok) ok = ensure_weight_tmap(w);
+  if (ok && (flags & OVB_WEIGHT_F16)) ok = make_weight_f16(w, s);
   if (!ok) {
-    cudaFree(w->w);
-    cudaFree(w->scale);
-    delete w;
+    free_weight(w);
     return OVB_ERR_INTERNAL;
   }
   *out = w;
@@ -281,10 +401,11 @@ int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
     row += p->N;
   }
   if (ok) ok = !cuda_failed(cudaStreamSynchronize(s), "concat sync") && ensure_weight_tmap(w);
+  bool all_f16 = true;
+  for (int i = 0; i < n_parts; ++i) all_f16 = all_f16 && parts[i]->w16 != nullptr;
+  if (ok && all_f16) ok = make_weight_f16(w, s);
   if (!ok) {
-    cudaFree(w->w);
-    cudaFree(w->scale);
-    delete w;
+    free_weight(w);
     return OVB_ERR_INTERNAL;
   }
   *out = w;
@@ -296,10 +417,8 @@ int ovb_weight_destroy(ovb_weight* w) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(w->device);
-  cudaFree(w->w);
-  cudaFree(w->scale);
+  free_weight(w);
   cudaSetDevice(prev);
-  delete w;
   return OVB_OK;
 }
 
@@ -329,9 +448,11 @@ int ovb_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq, fl
   if (M <= 0 || K <= 0) return OVB_OK;
   if (!A || !aq || !asc) return invalid("A/aq/asc must be non-null");
   if (lda < K) return invalid("lda < K");
-  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(A, 4)) return invalid("misaligned buffer");
-  if (cuda_failed(ovb::launch_quantize(M, K, A, lda, aq, asc, flags & OVB_AQ_U8,
-                                       as_stream(stream)),
+  const int mode = quant_mode(flags);
+  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
+  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(A, 4))
+    return invalid("misaligned buffer");
+  if (cuda_failed(ovb::launch_quantize(M, K, A, lda, aq, asc, mode, as_stream(stream)),
                   "quantize launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
@@ -342,10 +463,12 @@ int ovb_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float
   if (rows <= 0 || cols <= 0) return OVB_OK;
   if (!x || !w || !aq || !asc) return invalid("x/w/aq/asc must be non-null");
   if (cols > 24 * 1024) return invalid("rmsnorm_quantize: cols > 24576 not supported");
-  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(x, 4) || !aligned(w, 4))
+  const int mode = quant_mode(flags);
+  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
+  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(x, 4) || !aligned(w, 4))
     return invalid("misaligned buffer");
-  if (cuda_failed(ovb::launch_rmsnorm_quantize(rows, cols, x, w, eps, aq, asc,
-                                               flags & OVB_AQ_U8, as_stream(stream)),
+  if (cuda_failed(ovb::launch_rmsnorm_quantize(rows, cols, x, w, eps, aq, asc, mode,
+                                               as_stream(stream)),
                   "rmsnorm_quantize launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
@@ -357,10 +480,13 @@ int ovb_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
   if (M <= 0 || K <= 0) return OVB_OK;
   if (!gate || !up || !aq || !asc) return invalid("gate/up/aq/asc must be non-null");
   if (ldg < K || ldu < K) return invalid("ldg/ldu < K");
-  if (!aligned(aq, 8) || !aligned(asc, 4) || !aligned(gate, 4) || !aligned(up, 4))
+  const int mode = quant_mode(flags);
+  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
+  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(gate, 4) ||
+      !aligned(up, 4))
     return invalid("misaligned buffer");
-  if (cuda_failed(ovb::launch_silu_mul_quantize(M, K, gate, ldg, up, ldu, aq, asc,
-                                                flags & OVB_AQ_U8, as_stream(stream)),
+  if (cuda_failed(ovb::launch_silu_mul_quantize(M, K, gate, ldg, up, ldu, aq, asc, mode,
+                                                as_stream(stream)),
                   "silu_mul_quantize launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
@@ -383,20 +509,32 @@ int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const 
   if (M <= 0 || n_slices <= 0) return OVB_OK;
   int st = check_q_args(M, w, aq, asc);
   if (st != OVB_OK) return st;
-  if (!slices) return invalid("slices is null");
-  if (n_slices > ovb::kMaxSlices) return invalid("at most 4 slices");
   ovb::SliceOut so[ovb::kMaxSlices];
-  int64_t total = 0;
-  for (int i = 0; i < n_slices; ++i) {
-    // gemm.cpp:786-788: each slice N must be a positive multiple of 64.
-    if (slices[i].N <= 0 || slices[i].N % 64 != 0 || !slices[i].C)
-      return invalid("sliced GEMM: each slice N must be a positive multiple of 64");
-    if (slices[i].ldc < slices[i].N) return invalid("sliced GEMM: ldc < N");
-    so[i] = ovb::SliceOut{total, slices[i].N, slices[i].C, slices[i].ldc};
-    total += slices[i].N;
-  }
-  if (total != w->N) return invalid("sliced GEMM: slice widths do not add up to the weight's N");
+  st = build_slices(w, slices, n_slices, so);
+  if (st != OVB_OK) return st;
   return run_gemm(M, w, aq, asc, so, n_slices, 0, nullptr, as_stream(stream));
+}
+
+int ovb_linear_h(int64_t M, const ovb_weight* w, const void* a16, float* C, int64_t ldc,
+                 int accumulate, void* stream) {
+  if (M <= 0) return OVB_OK;
+  int st = check_h_args(M, w, a16);
+  if (st != OVB_OK) return st;
+  if (!C) return invalid("C is null");
+  if (ldc < w->N) return invalid("ldc < N");
+  const ovb::SliceOut so{0, w->N, C, ldc};
+  return run_gemm_h(M, w, a16, &so, 1, accumulate ? 1 : 0, as_stream(stream));
+}
+
+int ovb_linear_h_sliced(int64_t M, const ovb_weight* w, const void* a16, const ovb_slice* slices,
+                        int n_slices, void* stream) {
+  if (M <= 0 || n_slices <= 0) return OVB_OK;
+  int st = check_h_args(M, w, a16);
+  if (st != OVB_OK) return st;
+  ovb::SliceOut so[ovb::kMaxSlices];
+  st = build_slices(w, slices, n_slices, so);
+  if (st != OVB_OK) return st;
+  return run_gemm_h(M, w, a16, so, n_slices, 0, as_stream(stream));
 }
 
 size_t ovb_linear_workspace_bytes(int64_t M, int64_t K) {

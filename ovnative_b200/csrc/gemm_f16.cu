@@ -1,0 +1,767 @@
+// gemm_f16.cu -- the fp16 tensor-core mainloop for weight handles created
+// with OVB_WEIGHT_F16: int8 x per-32-k-quantised activations, dequantised on
+// chip and multiplied with tcgen05.mma kind::f16 into one fp32 accumulator
+// per output tile.
+//
+// What it computes (the same contract as gemm.cpp:432-504, to tolerance):
+//   C[m,n] = wscale[n] * sum_k A'[m,k] * w[n,k]      (+ C[m,n] if accumulate)
+//   A'[m,k] = fp16(q[m,k] * asc[m, k/32])              (the dequantised activation)
+// The weights are exact in fp16 (|w| <= 127) and the products and sums are
+// exact-to-fp32 in the tensor core, so the only rounding beyond the
+// reference's fp32 arithmetic is that of A' to fp16: relative error
+// <= 2^-11 per element, ~3e-4 relative L2 on the outputs -- inside the
+// rel-L2 <= 1e-3 / max-abs <= 1e-2 * rms contract, but not bit-exact.  The
+// exact kernel (gemm_tc.cu) must read every 32-k block's int32 products out
+// of TMEM to fold them in the reference's order; that readout competes with
+// the MMAs for TMEM bandwidth and caps it near 700 clocks per 128x128 block.
+// Here TMEM is read once per tile.
+//
+// Data flow per stage (64 k = two quantisation blocks):
+//   TMA   A box: 64 B x 128 rows of aq (int8, 64-byte swizzle) and W box:
+//         64 fp16 x BN rows of the fp16 weight copy (128-byte swizzle) into a
+//         4-stage shared-memory ring (one mbarrier `full` per stage);
+//   conv  eight converter warps: thread (quarter, lane) owns activation row
+//         32*quarter + lane and one of the stage's two blocks; it reads its
+//         32 int8 from shared memory, forms fp16(q * asc) and stores the 16
+//         packed columns into the stage's A' slot in TMEM (tcgen05.st).
+//         (Sixteen converter warps, each with half the work, measured slower:
+//         the conversion is latency-bound, not bound by arithmetic);
+//   MMA   one thread issues four K = 16 MMAs per stage with A from TMEM and
+//         W from shared memory, accumulating into the tile's TMEM buffer;
+//         tcgen05.commit on `empty` releases the stage (smem and A' slot);
+//   epi   after the tile's last stage the MMA thread commits `tfull`; eight
+//         epilogue warps read the accumulator (32 columns per tcgen05.ld),
+//         stage it in shared memory and write rows coalesced with wscale and
+//         the optional residual applied.
+//
+// TMEM (512 columns): kAcc accumulator buffers of BN columns (two when they
+// fit beside the A' ring, so a tile's epilogue overlaps the next tile's
+// MMAs), then the A' ring (four stages x 32 columns).
+//
+// Handshakes.  The MMA thread never waits on an mbarrier inside its loop (a
+// thread with MMAs in flight stalls on its own shared-memory accesses):
+//   kBarStage + s  the converter warps and the MMA warp bar.sync once stage
+//                  s's A' is in TMEM (the converters waited on full[s], so
+//                  the W box has landed too), then the MMA warp issues;
+//   kBarDfree + d  the epilogue warps and the MMA warp bar.sync once
+//                  accumulator d is read, before the MMA warp reuses it.
+// Both sides of both barriers bar.sync (none only arrives), so no warp can
+// enter a barrier's next generation before the current one completed -- on
+// the error path too, where a failed mbarrier wait makes a warp skip its work
+// but not its barrier.  Converters therefore run at most one stage ahead of
+// the MMA warp, which is enough: a stage converts faster than its MMAs run.
+// The converters overwrite A' slot s for stage st only after full[s] of
+// stage st completed, and the producer issued that stage's copies only after
+// empty[s] of stage st - 4 (whose MMAs read the slot) -- so a slot is never
+// overwritten while an MMA may read it.  Every mbarrier wait is bounded
+// (ovb_wait).
+#include <cuda_fp16.h>
+
+#include <cstdlib>
+
+#include "ovb_internal.h"
+#include "ovb_ptx.cuh"
+
+namespace ovb {
+
+// Status word of this kernel's bounded waits (a device variable is private
+// to its translation unit without relocatable device code, so the fp16
+// mainloop keeps its own; ovb_device_status reports both).
+__device__ int g_status_f16;
+
+namespace {
+
+constexpr int kStageKF = 64;      // k per stage: two quantisation blocks
+constexpr int kStagesF = 4;
+constexpr int kConvWarps = 8;     // warps 2..9
+constexpr int kEpiWarpsF = 8;     // warps 10..17
+constexpr int kFirstConv = 2;
+constexpr int kFirstEpi = kFirstConv + kConvWarps;
+constexpr int kThreadsF = 32 * (kFirstEpi + kEpiWarpsF);
+constexpr uint32_t kTmemColsF = 512;
+constexpr int kAColsPerStage = kStageKF / 2;  // fp16 pairs per row
+constexpr uint32_t kABytesF = kBlockM * kStageKF;
+constexpr int kStgStrideF = 33;  // epilogue staging row stride (floats)
+// named barriers (0 is __syncthreads)
+constexpr int kBarStage = 1;                    // + s: converters -> MMA warp
+constexpr int kBarDfree = kBarStage + kStagesF;  // + d: epilogue -> MMA warp
+constexpr int kBarStageThreads = 32 * (kConvWarps + 1);
+constexpr int kBarDfreeThreads = 32 * (kEpiWarpsF + 1);
+static_assert(kBarDfree + 2 <= 16, "the hardware has 16 named barriers");
+static_assert(kABytesF % 1024 == 0, "stage bases stay 1 KB aligned");
+
+// status bits (the same meaning as gemm_tc.cu's)
+constexpr int kErrProducer = 1;
+constexpr int kErrConvert = 2;
+constexpr int kErrEpilogue = 4;
+constexpr int kErrDrain = 8;
+constexpr int kErrF16Range = 16;  // an activation block left the fp16 range
+
+struct CtlF {
+  uint64_t full[kStagesF];
+  uint64_t empty[kStagesF];
+  uint64_t tfull[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int BN>
+struct TileF {
+  static_assert(BN == 256 || BN == 128 || BN == 64 || BN == 32, "tile widths: 256..32");
+  static constexpr uint32_t kWBytes = BN * 128;  // 64 fp16 x BN rows
+  static constexpr uint32_t kStageBytes = kABytesF + kWBytes;
+  static constexpr int kAcc =
+      2 * BN + kStagesF * kAColsPerStage <= static_cast<int>(kTmemColsF) ? 2 : 1;
+  static constexpr int kACol0 = kAcc * BN;  // first column of the A' ring
+  static constexpr int kChunks = BN / 32;   // 32-column epilogue chunks
+  static constexpr uint32_t kStgBytes = 32 * kStgStrideF * 4;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStagesF) * kStageBytes +
+                                       static_cast<size_t>(kEpiWarpsF) * kStgBytes +
+                                       sizeof(CtlF);
+  static_assert(kACol0 + kStagesF * kAColsPerStage <= static_cast<int>(kTmemColsF),
+                "accumulators and A' ring exceed TMEM");
+  static_assert(kStageBytes % 1024 == 0, "stage bases stay 1 KB aligned");
+};
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void fail(CtlF* ctl, int code) {
+  atomicOr(&g_status_f16, code);
+  *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+}
+
+// Four signed int8 (one 32-bit word) -> two fp16x2 words holding
+// fp16(q * asc), asc given as hi + lo fp16 parts.  q is formed exactly:
+// the byte q + 128 placed under the fp16 exponent of 1024 reads as
+// 1024 + q + 128; subtracting 1152 leaves q.  Then q * hi + (q * lo) is
+// rounded once (fma), i.e. fp16(q * asc) up to the ~2^-22 relative
+// truncation of asc into hi + lo.
+__device__ __forceinline__ void dequant4(uint32_t x, __half2 s_hi, __half2 s_lo, uint32_t& out0,
+                                         uint32_t& out1) {
+  const uint32_t u = x ^ 0x80808080u;  // q + 128 per byte
+  const uint32_t b01 = __byte_perm(u, 0x64646464u, 0x4140);
+  const uint32_t b23 = __byte_perm(u, 0x64646464u, 0x4342);
+  const __half2 bias = __half2half2(__ushort_as_half(static_cast<unsigned short>(0x6480)));  // 1152
+  const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&b01), bias);
+  const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&b23), bias);
+  const __half2 r01 = __hfma2(q01, s_hi, __hmul2(q01, s_lo));
+  const __half2 r23 = __hfma2(q23, s_hi, __hmul2(q23, s_lo));
+  out0 = *reinterpret_cast<const uint32_t*>(&r01);
+  out1 = *reinterpret_cast<const uint32_t*>(&r23);
+}
+
+// Writes this lane's column of a warp's staged 32-column chunk (`stg` points
+// at the lane's column of row 0): o = stg * ws (+ C_old), row by row.  The residual loads of 8 rows are issued before
+// their stores, so their latencies overlap (the compiler cannot reorder a
+// load past a store it cannot prove distinct).
+__device__ __forceinline__ void store_rows(const float* stg, int stride, float* cbase,
+                                           int64_t ldc, int rows, float ws, int accumulate) {
+  for (int r0 = 0; r0 < rows; r0 += 8) {
+    float old[8];
+    if (accumulate) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) old[i] = r0 + i < rows ? cbase[(r0 + i) * ldc] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (r0 + i < rows) {
+        float o = __fmul_rn(stg[(r0 + i) * stride], ws);
+        if (accumulate) o = __fadd_rn(o, old[i]);
+        cbase[(r0 + i) * ldc] = o;
+      }
+    }
+  }
+}
+
+// The epilogue warps' loop over this CTA's tiles (both fp16 mainloops).
+// Warp (quarter, eh) reads TMEM lanes 32*quarter.. and the 32-column chunks
+// eh, eh+2, ... of accumulator d = t % kAcc (none for eh = 1 at BN = 32;
+// those warps still take part in every barrier).  Per tile: the chunks'
+// wscale values are fetched before the accumulator is ready (tfull[d]), the
+// TMEM load of the next chunk runs while the current one is stored, and
+// after the last chunk the warps bar.sync on dfree_bar + d with the MMA warp
+// (which syncs there before reusing accumulator d).
+template <int BN, int kAcc>
+__device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull,
+                                              volatile int* abort, uint32_t tmem_base,
+                                              float* stg, int quarter, int eh, int dfree_bar,
+                                              int64_t tiles, int64_t m_tiles, int64_t my_tiles) {
+  constexpr int kChunks = BN / 32;
+  constexpr int kMine = (kChunks + 1) / 2;  // chunks per warp (at most)
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  int64_t t = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    const int d = static_cast<int>(t % kAcc);
+    const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
+    const int64_t m0 = (tile % m_tiles) * kBlockM;
+    const int64_t n0 = (tile / m_tiles) * BN;
+    float wsv[kMine];
+#pragma unroll
+    for (int i = 0; i < kMine; ++i) {
+      const int64_t n = n0 + (eh + 2 * i) * 32 + lane;
+      wsv[i] = (eh + 2 * i < kChunks && n < N) ? __ldg(args.wscale + n) : 0.f;
+    }
+    const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0) {
+        atomicOr(&g_status_f16, kErrEpilogue);
+        *abort = 1;
+      }
+    } else {
+      tc_fence_after();
+      const int64_t r0 = m0 + quarter * 32;
+      const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
+      const uint32_t dcol = tmem_base + lane_off + static_cast<uint32_t>(d * BN);
+      uint32_t va[32], vb[32];
+      if (eh < kChunks) tmem_ld32(dcol + static_cast<uint32_t>(eh * 32), va);
+#pragma unroll
+      for (int i = 0; i < kMine; ++i) {
+        const int c = eh + 2 * i;
+        if (c >= kChunks) break;
+        uint32_t(&cur)[32] = (i & 1) ? vb : va;
+        uint32_t(&nxt)[32] = (i & 1) ? va : vb;
+        tc_wait_ld32(cur);
+        if (c + 2 < kChunks) tmem_ld32(dcol + static_cast<uint32_t>((c + 2) * 32), nxt);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[lane * kStgStrideF + j] = __uint_as_float(cur[j]);
+        __syncwarp();
+        const int64_t nc = n0 + c * 32;  // first column of the chunk
+        if (nc < N && rows > 0) {
+          // The chunk lies inside one output slice (slices are multiples of
+          // 64 columns, or a single slice covering all N).
+          int si = 0;
+#pragma unroll
+          for (int k = 1; k < kMaxSlices; ++k)
+            if (k < args.n_slices && nc >= args.slices[k].n_begin) si = k;
+          const SliceOut so = args.slices[si];
+          const int64_t local = nc - so.n_begin;
+          if (lane < so.n_count - local)
+            store_rows(stg + lane, kStgStrideF, so.C + r0 * so.ldc + local + lane, so.ldc, rows,
+                       wsv[i], args.accumulate);
+        }
+        __syncwarp();
+      }
+    }
+    tc_fence_before();
+    if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiWarpsF + 1));
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreadsF, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_w,
+                    const __grid_constant__ GemmArgs args) {
+  using T = TileF<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(kStagesF) * T::kStageBytes);
+  CtlF* ctl = reinterpret_cast<CtlF*>(reinterpret_cast<uint8_t*>(stg_all) +
+                                      static_cast<size_t>(kEpiWarpsF) * T::kStgBytes);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int64_t M = args.M, N = args.N;
+  const int Kb = static_cast<int>(args.Kb);
+  const int ksteps = (Kb + 1) / 2;  // stages per tile
+  const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int64_t my_tiles =
+      tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesF; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), kTmemColsF);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int64_t st = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
+        const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
+        for (int j = 0; j < ksteps; ++j, ++st) {
+          const int s = static_cast<int>(st % kStagesF);
+          const uint32_t ph = static_cast<uint32_t>((st / kStagesF) & 1);
+          if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
+            fail(ctl, kErrProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t full = smem_u32(&ctl->full[s]);
+          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+          mbar_arrive_expect_tx(full, T::kStageBytes);
+          tma_load_2d(sa, &tmap_a, j * kStageKF, m0, full);             // x in bytes (int8)
+          tma_load_2d(sa + kABytesF, &tmap_w, j * kStageKF, n0, full);  // x in fp16 elements
+        }
+      }
+      if (!ok) {
+        const int64_t first = st > kStagesF ? st - kStagesF : 0;
+        for (int64_t j = first; j < st; ++j) {
+          const int s = static_cast<int>(j % kStagesF);
+          const uint32_t ph = static_cast<uint32_t>((j / kStagesF) & 1);
+          volatile int never = 0;
+          ovb_wait(smem_u32(&ctl->full[s]), ph, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    const uint32_t idesc = idesc_f16(kBlockM, BN);
+    int64_t st = 0;
+    for (int64_t t = 0; t < my_tiles; ++t) {
+      const int d = static_cast<int>(t % T::kAcc);
+      if (t >= T::kAcc) named_sync(kBarDfree + d, kBarDfreeThreads);  // accumulator d read
+      const uint32_t dcol = tmem_base + static_cast<uint32_t>(d * BN);
+      for (int j = 0; j < ksteps; ++j, ++st) {
+        const int s = static_cast<int>(st % kStagesF);
+        named_sync(kBarStage + s, kBarStageThreads);  // A' of stage s in TMEM, W landed
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t acol =
+              tmem_base + static_cast<uint32_t>(T::kACol0 + s * kAColsPerStage);
+          const uint32_t sw = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes + kABytesF);
+#pragma unroll
+          for (int kk = 0; kk < kStageKF / 16; ++kk)
+            mma_f16_ts(dcol, acol + static_cast<uint32_t>(kk * 8),
+                       sw128_kmajor_desc(sw, static_cast<uint32_t>(kk * 32)), idesc,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&ctl->empty[s]));
+          if (j == ksteps - 1) tc_commit(smem_u32(&ctl->tfull[d]));
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(smem_u32(&ctl->drain));
+      volatile int never = 0;
+      if (!ovb_wait(smem_u32(&ctl->drain), 0u, &never)) atomicOr(&g_status_f16, kErrDrain);
+    }
+    __syncwarp();
+  } else if (warp < kFirstEpi) {
+    // ---------------------------------------------------------- converters
+    // TMEM lanes 32*quarter.. are the rows this warp may write; `half`
+    // picks the stage's first or second quantisation block.
+    const int quarter = warp & 3;
+    const int half = (warp - kFirstConv) >> 2;
+    const int r = quarter * 32 + lane;  // row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    int64_t st = 0;
+    bool range_ok = true;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int64_t m = (tile % m_tiles) * kBlockM + r;
+      const bool row_ok = m < M;
+      const float* asc_row = args.asc + (row_ok ? m : 0) * static_cast<int64_t>(Kb);
+      auto scale_of = [&](int j) -> float {
+        const int b = 2 * j + half;
+        return (row_ok && j < ksteps && b < Kb) ? __ldg(asc_row + b) : 0.f;
+      };
+      // One stage: wait for its TMA, dequantise this thread's 32 values
+      // into the stage's A' slot, meet the MMA warp.
+      auto do_stage = [&](float sc) {
+        const int s = static_cast<int>(st % kStagesF);
+        const uint32_t ph = static_cast<uint32_t>((st / kStagesF) & 1);
+        const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) fail(ctl, kErrConvert);
+        } else {
+          // Row r's 32 bytes of this block: 16-byte chunks 2*half and
+          // 2*half+1 of its 64-byte row, placed by the 64-byte swizzle at
+          // chunk c ^ ((r >> 1) & 3).
+          const uint8_t* arow = smem + static_cast<size_t>(s) * T::kStageBytes + r * 64;
+          const int sw = (r >> 1) & 3;
+          const uint4 c0 = *reinterpret_cast<const uint4*>(arow + (((2 * half) ^ sw) << 4));
+          const uint4 c1 = *reinterpret_cast<const uint4*>(arow + (((2 * half + 1) ^ sw) << 4));
+          if (sc * 127.f > 65504.f) range_ok = false;
+          const __half h_hi = __float2half_rn(sc);
+          const __half h_lo = __float2half_rn(sc - __half2float(h_hi));
+          const __half2 s_hi = __half2half2(h_hi), s_lo = __half2half2(h_lo);
+          uint32_t v[16];
+          dequant4(c0.x, s_hi, s_lo, v[0], v[1]);
+          dequant4(c0.y, s_hi, s_lo, v[2], v[3]);
+          dequant4(c0.z, s_hi, s_lo, v[4], v[5]);
+          dequant4(c0.w, s_hi, s_lo, v[6], v[7]);
+          dequant4(c1.x, s_hi, s_lo, v[8], v[9]);
+          dequant4(c1.y, s_hi, s_lo, v[10], v[11]);
+          dequant4(c1.z, s_hi, s_lo, v[12], v[13]);
+          dequant4(c1.w, s_hi, s_lo, v[14], v[15]);
+          tmem_st16(tmem_base + lane_off +
+                        static_cast<uint32_t>(T::kACol0 + s * kAColsPerStage + half * 16),
+                    v);
+          tc_wait_st();
+        }
+        tc_fence_before();
+        named_sync(kBarStage + s, kBarStageThreads);
+        ++st;
+      };
+      // Block scales of a group of four stages are loaded one group ahead
+      // into their own registers and indexed statically: no register with a
+      // load in flight is ever copied (a copy would wait for the load).
+      float cur[4], nxt[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) cur[u] = scale_of(u);
+      for (int j0 = 0; j0 < ksteps; j0 += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) nxt[u] = scale_of(j0 + 4 + u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u < ksteps) do_stage(cur[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) cur[u] = nxt[u];
+      }
+    }
+    if (!range_ok) atomicOr(&g_status_f16, kErrF16Range);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                               stg_all + (warp - kFirstEpi) * (32 * kStgStrideF), warp & 3,
+                               (warp - kFirstEpi) >> 2, kBarDfree, tiles, m_tiles, my_tiles);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemColsF);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The plain fp16 mainloop (ovb_linear_h): the activations arrive already
+// dequantised, fp16(q * asc) from a quantiser run with OVB_AQ_F16, so both
+// operands come from shared memory and no warp converts anything.  Warps:
+//   0  TMA producer: A box 64 fp16 x 128 rows and W box 64 fp16 x BN rows
+//      (both 128-byte swizzle) per 64-k stage into a 4-stage ring;
+//   1  TMEM allocator + MMA issuer: four K = 16 MMAs per stage;
+//   2  stage watcher: waits `full[s]` and meets the MMA warp on kBarFullH
+//      (bar.sync on both sides, so the MMA thread never waits on an
+//      mbarrier while it has MMAs in flight);
+//   3..10 epilogue (epilogue_loop), accumulators double-buffered in TMEM.
+constexpr int kStagesH = 4;
+constexpr int kFirstEpiH = 3;
+constexpr int kThreadsH = 32 * (kFirstEpiH + kEpiWarpsF);
+constexpr uint32_t kABytesH = kBlockM * kStageKF * 2;  // 16 KB
+constexpr int kBarFullH = 1;
+constexpr int kBarDfreeH = 2;  // + d
+
+struct CtlH {
+  uint64_t full[kStagesH];
+  uint64_t empty[kStagesH];
+  uint64_t tfull[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int BN>
+struct TileH {
+  static constexpr uint32_t kWBytes = BN * 128;
+  static constexpr uint32_t kStageBytes = kABytesH + kWBytes;
+  static constexpr int kAcc = 2;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStagesH) * kStageBytes +
+                                       static_cast<size_t>(kEpiWarpsF) * 32 * kStgStrideF * 4 +
+                                       sizeof(CtlH);
+  static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreadsH, 1)
+    gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                  const __grid_constant__ CUtensorMap tmap_w,
+                  const __grid_constant__ GemmArgs args) {
+  using T = TileH<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(kStagesH) * T::kStageBytes);
+  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) +
+                                      static_cast<size_t>(kEpiWarpsF) * 32 * kStgStrideF * 4);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const int Kb = static_cast<int>(args.Kb);
+  const int ksteps = (Kb + 1) / 2;
+  const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int64_t my_tiles =
+      tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesH; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), kTmemColsF);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int64_t st = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
+        const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
+        for (int j = 0; j < ksteps; ++j, ++st) {
+          const int s = static_cast<int>(st % kStagesH);
+          const uint32_t ph = static_cast<uint32_t>((st / kStagesH) & 1);
+          if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
+            atomicOr(&g_status_f16, kErrProducer);
+            *abort = 1;
+            ok = false;
+            break;
+          }
+          const uint32_t full = smem_u32(&ctl->full[s]);
+          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+          mbar_arrive_expect_tx(full, T::kStageBytes);
+          tma_load_2d(sa, &tmap_a, j * kStageKF, m0, full);            // x in fp16 elements
+          tma_load_2d(sa + kABytesH, &tmap_w, j * kStageKF, n0, full);
+        }
+      }
+      if (!ok) {
+        const int64_t first = st > kStagesH ? st - kStagesH : 0;
+        for (int64_t j = first; j < st; ++j) {
+          volatile int never = 0;
+          ovb_wait(smem_u32(&ctl->full[j % kStagesH]), static_cast<uint32_t>((j / kStagesH) & 1),
+                   &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    const uint32_t idesc = idesc_f16(kBlockM, BN);
+    int64_t st = 0;
+    for (int64_t t = 0; t < my_tiles; ++t) {
+      const int d = static_cast<int>(t % T::kAcc);
+      if (t >= T::kAcc) named_sync(kBarDfreeH + d, 32 * (kEpiWarpsF + 1));  // accumulator d read
+      const uint32_t dcol = tmem_base + static_cast<uint32_t>(d * BN);
+      for (int j = 0; j < ksteps; ++j, ++st) {
+        const int s = static_cast<int>(st % kStagesH);
+        named_sync(kBarFullH, 64);  // stage s has landed
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kStageKF / 16; ++kk)
+            mma_f16_ss(dcol, sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
+                       sw128_kmajor_desc(sa + kABytesH, static_cast<uint32_t>(kk * 32)), idesc,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&ctl->empty[s]));
+          if (j == ksteps - 1) tc_commit(smem_u32(&ctl->tfull[d]));
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(smem_u32(&ctl->drain));
+      volatile int never = 0;
+      if (!ovb_wait(smem_u32(&ctl->drain), 0u, &never)) atomicOr(&g_status_f16, kErrDrain);
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ----------------------------------------------------- stage watcher
+    // Exactly one bar.sync per stage, in lockstep with the MMA warp, also
+    // after a failed wait (the status word reports it).
+    int64_t st = 0;
+    for (int64_t t = 0; t < my_tiles; ++t) {
+      for (int j = 0; j < ksteps; ++j, ++st) {
+        const int s = static_cast<int>(st % kStagesH);
+        const uint32_t ph = static_cast<uint32_t>((st / kStagesH) & 1);
+        const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
+        if (!__all_sync(0xffffffffu, got) && lane == 0) {
+          atomicOr(&g_status_f16, kErrConvert);
+          *abort = 1;
+        }
+        named_sync(kBarFullH, 64);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                               stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                               (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemColsF);
+  }
+}
+
+template <int BN>
+cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                          const GemmArgs& args, cudaStream_t s) {
+  using T = TileH<BN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static thread_local int configured_dev = -1;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_h_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(T::kSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
+  gemm_h_kernel<BN><<<grid, kThreadsH, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_f16_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                            const GemmArgs& args, cudaStream_t s) {
+  using T = TileF<BN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static thread_local int configured_dev = -1;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_f16_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(T::kSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
+  gemm_f16_kernel<BN><<<grid, kThreadsF, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Cost of one output tile per 32-k block, by width (clocks): the slower of
+// the tensor core (a K = 16 fp16 MMA takes ~128 clocks at N = 256 and ~64 at
+// N <= 128) and the TMA feed (~65 B/clock per SM from L2 for 4 KB of A and
+// 64*BN B of fp16 weights per block), plus a fixed per-tile cost (pipeline
+// fill, epilogue).
+int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device) {
+  if (const char* e = std::getenv("OVB_GEMM_TILE_N")) {
+    const int v = std::atoi(e);
+    for (int i = 0; i < 4; ++i)
+      if (kTileNF[i] == v) return i;
+  }
+  static constexpr int64_t kPerBlock[4] = {315, 189, 133, 133};
+  const int64_t sms = num_sms(device);
+  const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
+  int best = 0;
+  int64_t best_cost = -1;
+  for (int i = 0; i < 4; ++i) {
+    const int64_t tiles = m_tiles * ((N + kTileNF[i] - 1) / kTileNF[i]);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * (2000 + Kb * kPerBlock[i]);
+    if (best_cost < 0 || cost < best_cost) {
+      best = i;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+// Tile width for the plain fp16 mainloop: per 64-k stage the slower of the
+// tensor core (4 MMAs: ~128 clocks each at N = 256, ~64 at N <= 128) and the
+// TMA feed (measured ~375 clocks for stages up to ~40 KB, ~100 B/clock per SM
+// beyond), plus a per-tile cost (prologue, epilogue stores) growing with BN.
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device) {
+  if (const char* e = std::getenv("OVB_GEMM_TILE_N")) {
+    const int v = std::atoi(e);
+    for (int i = 0; i < 4; ++i)
+      if (kTileNF[i] == v) return i;
+  }
+  static constexpr int64_t kPerStage[4] = {512, 375, 375, 375};
+  const int64_t sms = num_sms(device);
+  const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
+  const int64_t ksteps = (Kb + 1) / 2;
+  int best = 0;
+  int64_t best_cost = -1;
+  for (int i = 0; i < 4; ++i) {
+    const int64_t tiles = m_tiles * ((N + kTileNF[i] - 1) / kTileNF[i]);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * (2000 + 10 * kTileNF[i] + ksteps * kPerStage[i]);
+    if (best_cost < 0 || cost < best_cost) {
+      best = i;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                          const GemmArgs& args, cudaStream_t s) {
+  switch (tile) {
+    case 0: return launch_h_impl<256>(tmap_a, tmap_w, args, s);
+    case 1: return launch_h_impl<128>(tmap_a, tmap_w, args, s);
+    case 2: return launch_h_impl<64>(tmap_a, tmap_w, args, s);
+    case 3: return launch_h_impl<32>(tmap_a, tmap_w, args, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t read_and_clear_status_f16(int* out, cudaStream_t s) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_status_f16, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_status_f16, &zero, sizeof(int));
+}
+
+cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                            const GemmArgs& args, cudaStream_t s) {
+  switch (tile) {
+    case 0: return launch_f16_impl<256>(tmap_a, tmap_w, args, s);
+    case 1: return launch_f16_impl<128>(tmap_a, tmap_w, args, s);
+    case 2: return launch_f16_impl<64>(tmap_a, tmap_w, args, s);
+    case 3: return launch_f16_impl<32>(tmap_a, tmap_w, args, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ovb

@@ -436,6 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = m < M;
       const float* asc_row = args.asc + (row_ok ? m : 0) * static_cast<int64_t>(Kb);
       const int64_t nc = n0 + cgroup * E;  // first column of this warp's slice
+      // wscale of this lane's output column (see the stores below), fetched
+      // now so its latency hides behind the K loop.
+      const float ws_pre = (!kProducts && nc + lane % E < N) ? __ldg(args.wscale + nc + lane % E)
+                                                            : 0.f;
       float f[E];
 #pragma unroll
       for (int j = 0; j < E; ++j) f[j] = 0.f;
@@ -507,16 +511,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int cl = lane % E;       // column within the warp's slice
           const int rsub = lane / E;     // first row of this lane
           const bool col_ok = cl < so.n_count - local;
-          const float ws = col_ok ? __ldg(args.wscale + nc + cl) : 0.f;
+          const float ws = ws_pre;
           const int64_t r0 = m0 + quarter * 32;
           const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
           if (col_ok) {
+            // Rows rsub, rsub + 32/E, ...: the residual loads of 8 rows are
+            // issued before their stores so their latencies overlap.
+            constexpr int kStep = 32 / E;
             float* cbase = so.C + r0 * so.ldc + local + cl;
-            for (int rr = rsub; rr < rows; rr += 32 / E) {
-              float o = __fmul_rn(stg[rr * T::kStgStride + cl], ws);
-              float* cp = cbase + rr * so.ldc;
-              if (args.accumulate) o = __fadd_rn(o, *cp);
-              *cp = o;
+            for (int rr0 = rsub; rr0 < rows; rr0 += 8 * kStep) {
+              float old[8];
+              if (args.accumulate) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int rr = rr0 + i * kStep;
+                  old[i] = rr < rows ? cbase[rr * so.ldc] : 0.f;
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int rr = rr0 + i * kStep;
+                if (rr < rows) {
+                  float o = __fmul_rn(stg[rr * T::kStgStride + cl], ws);
+                  if (args.accumulate) o = __fadd_rn(o, old[i]);
+                  cbase[rr * so.ldc] = o;
+                }
+              }
             }
           }
         }

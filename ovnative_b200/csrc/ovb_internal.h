@@ -20,6 +20,12 @@ struct ovb_weight {
   // (box kStageK B x kTileN[i] rows), built on first use.
   CUtensorMap tmap_b[3];
   bool tmap_ready[3] = {false, false, false};
+  // Optional fp16 copy of `w` ([N, Kp], exact: |w| <= 127) for the fp16
+  // tensor-core mainloop, with its TMA descriptors per tile width
+  // (box 64 fp16 x kTileNF[i] rows).  Null unless created with OVB_WEIGHT_F16.
+  uint16_t* w16 = nullptr;
+  CUtensorMap tmap_w16[4];
+  bool tmap16_ready[4] = {false, false, false, false};
 };
 
 namespace ovb {
@@ -30,6 +36,9 @@ constexpr int kBlockM = 128;
 constexpr int kStageK = 128;
 // Output-tile widths the GEMM is built for (one kernel per width).
 constexpr int kTileN[3] = {128, 64, 32};
+
+// Output-tile widths of the fp16 mainloop.
+constexpr int kTileNF[4] = {256, 128, 64, 32};
 
 constexpr int kMaxSlices = 4;
 
@@ -65,17 +74,37 @@ bool encode_tmap_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint
 int num_sms(int device);
 
 // Launchers (stream-ordered, return a cudaError_t from the launch).
+// Quantisers.  mode: 0 = int8 q, 1 = reference u8 q+128, 2 = fp16(q * asc).
 cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
-                            float* asc, int u8, cudaStream_t s);
+                            float* asc, int mode, cudaStream_t s);
 cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
-                                    float eps, void* aq, float* asc, int u8, cudaStream_t s);
+                                    float eps, void* aq, float* asc, int mode, cudaStream_t s);
 cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
-                                     const float* up, int64_t ldu, void* aq, float* asc, int u8,
+                                     const float* up, int64_t ldu, void* aq, float* asc, int mode,
                                      cudaStream_t s);
+cudaError_t read_and_clear_status_q(int* out, cudaStream_t s);
 cudaError_t launch_pack_nk(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
                            cudaStream_t s);
 cudaError_t launch_pack_kn(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
                            cudaStream_t s);
+// General 2-D tensor map: dims {inner, rows} in elements, row stride in
+// bytes, box {box_inner, box_rows} elements.  Returns false (and sets the
+// error) on failure.
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                    uint64_t inner, uint64_t rows, uint64_t stride_bytes, uint32_t box_inner,
+                    uint32_t box_rows, CUtensorMapSwizzle swizzle);
+// int8 [n] -> fp16 [n] (exact for |v| <= 2048).
+cudaError_t launch_widen_f16(const int8_t* src, int64_t n, uint16_t* dst, cudaStream_t s);
+// Index into kTileNF of the tile width used by the fp16 mainloop.
+int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device);
+cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                            const GemmArgs& args, cudaStream_t s);
+cudaError_t read_and_clear_status_f16(int* out, cudaStream_t s);
+// The plain fp16 mainloop: A is fp16 [M, Kp] (dequantised activations).
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device);
+cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                          const GemmArgs& args, cudaStream_t s);
+
 // Index into kTileN of the tile width used for an M x N GEMM: the widest
 // one that still gives every SM a tile (OVB_GEMM_TILE_N overrides it).
 int pick_tile(int64_t M, int64_t N, int device);

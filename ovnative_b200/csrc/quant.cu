@@ -1,8 +1,10 @@
 // quant.cu -- per-row, per-32-k activation quantisers for the int8 GEMM.
 //
-// Three producers, each writing aq (int8 q, or the reference's u8 q+128 with
-// OVB_AQ_U8) and asc (fp32 block scales), bit-identical to the reference CPU
-// path:
+// Three producers, each writing asc (fp32 block scales) and aq in one of three
+// forms (`mode`): int8 q (0), the reference's u8 q+128 (1, OVB_AQ_U8), or the
+// dequantised activation fp16(q * asc) for the fp16 tensor-core mainloop (2,
+// OVB_AQ_F16; aq is then [M, Kp] fp16).  q and asc are bit-identical to the
+// reference CPU path:
 //   quantize_kernel          quantize_a_u8          gemm.cpp:379-430
 //   rmsnorm_quantize_kernel  rmsnorm_quantize_avx2  gemm.cpp:638-707
 //   silu_mul_quantize_kernel silu_mul_quant_avx2    ops_cpu.cpp:144-198
@@ -11,12 +13,23 @@
 // element).  Every fp32 operation is an explicit round-to-nearest intrinsic so
 // that nvcc can neither contract nor reorder anything; denormals are kept
 // (no -ftz / fast-math on this file).
+#include <cuda_fp16.h>
+
 #include <climits>
 
 #include "ovb_internal.h"
 
 namespace ovb {
+
+// Status of the fp16 output form: bit 16 = a dequantised activation left the
+// fp16 range (it would be stored as +-inf).  Reported by ovb_device_status.
+__device__ int g_status_q;
+
 namespace {
+
+constexpr int kModeU8 = 1;
+constexpr int kModeF16 = 2;
+constexpr int kErrF16Range = 16;
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
@@ -54,6 +67,41 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], int nv, float inv, 
   return make_uint2(lo, hi);
 }
 
+// fp16(q * scale) of 8 consecutive values (padding -> 0), packed in 16 bytes.
+__device__ __forceinline__ uint4 dequant8_f16(const float (&v)[8], int nv, float inv,
+                                              float scale) {
+  uint32_t w[4];
+  bool range_ok = true;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    float d[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (i + j < nv) {
+        int z = cvt_rne_x86(__fmul_rn(v[i + j], inv));
+        z = z < -127 ? -127 : (z > 127 ? 127 : z);
+        d[j] = __fmul_rn(static_cast<float>(z), scale);
+        range_ok = range_ok && fabsf(d[j]) <= 65504.f;
+      } else {
+        d[j] = 0.f;
+      }
+    }
+    const __half2 h = __floats2half2_rn(d[0], d[1]);
+    w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  if (!range_ok) atomicOr(&g_status_q, kErrF16Range);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Write the 8 quantised values of element k of a row in the chosen form.
+__device__ __forceinline__ void store8(uint8_t* aq, int64_t idx, const float (&v)[8], int nv,
+                                       float inv, float scale, int mode) {
+  if (mode == kModeF16)
+    *reinterpret_cast<uint4*>(aq + 2 * idx) = dequant8_f16(v, nv, inv, scale);
+  else
+    *reinterpret_cast<uint2*>(aq + idx) = quant8(v, nv, inv, mode == kModeU8);
+}
+
 // Load 8 floats starting at p, the first nv of them valid (others 0).
 __device__ __forceinline__ void load8(const float* p, int nv, bool vec_ok, float (&v)[8]) {
   if (nv == 8 && vec_ok) {
@@ -73,7 +121,7 @@ __device__ __forceinline__ void load8(const float* p, int nv, bool vec_ok, float
 // reference's 8-lane max followed by a scalar tail).
 __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, const float* A,
                                                        int64_t lda, uint8_t* aq, float* asc,
-                                                       int u8) {
+                                                       int mode) {
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
   const int64_t total = M * Kb * 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -97,7 +145,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, con
     float scale, inv;
     block_scales(amax, &scale, &inv);
     if (valid) {
-      *reinterpret_cast<uint2*>(aq + row * Kp + k) = quant8(v, nv, inv, u8 != 0);
+      store8(aq, row * Kp + k, v, nv, inv, scale, mode);
       if (sub == 0) asc[row * Kb + b] = scale;
     }
   }
@@ -113,7 +161,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, con
 __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int64_t cols,
                                                                const float* x, const float* w,
                                                                float eps, uint8_t* aq,
-                                                               float* asc, int u8) {
+                                                               float* asc, int mode) {
   extern __shared__ float srow_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -156,14 +204,13 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
       float bs, inv;
       block_scales(amax, &bs, &inv);
       asc[r * Kb + b] = bs;
-      uint8_t* q = aq + r * Kp + k0;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         float v8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v8[i] = v[g * 8 + i];
         const int nv = max(0, min(8, kn - g * 8));
-        *reinterpret_cast<uint2*>(q + g * 8) = quant8(v8, nv, inv, u8 != 0);
+        store8(aq, r * Kp + k0 + g * 8, v8, nv, inv, bs, mode);
       }
     }
     __syncwarp();
@@ -210,7 +257,8 @@ __device__ __forceinline__ float silu_up_tail(float g, float u) {
 __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
                                                                 const float* gate, int64_t ldg,
                                                                 const float* up, int64_t ldu,
-                                                                uint8_t* aq, float* asc, int u8) {
+                                                                uint8_t* aq, float* asc,
+                                                                int mode) {
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
   const int64_t total = M * Kb * 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -243,7 +291,7 @@ __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64
     float scale, inv;
     block_scales(amax, &scale, &inv);
     if (valid) {
-      *reinterpret_cast<uint2*>(aq + row * Kp + k) = quant8(v, nv, inv, u8 != 0);
+      store8(aq, row * Kp + k, v, nv, inv, scale, mode);
       if (sub == 0) asc[row * Kb + b] = scale;
     }
   }
@@ -260,15 +308,15 @@ int grid_for(int64_t threads_needed) {
 }  // namespace
 
 cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
-                            float* asc, int u8, cudaStream_t s) {
+                            float* asc, int mode, cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
   quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(M, K, A, lda,
-                                                       static_cast<uint8_t*>(aq), asc, u8);
+                                                       static_cast<uint8_t*>(aq), asc, mode);
   return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
-                                    float eps, void* aq, float* asc, int u8, cudaStream_t s) {
+                                    float eps, void* aq, float* asc, int mode, cudaStream_t s) {
   // One warp per row; shared memory holds one row per warp.
   const int64_t row_bytes = cols * 4;
   int warps = static_cast<int>(imin64(8, imax64(1, (96 * 1024) / row_bytes)));
@@ -285,17 +333,27 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
   const int64_t blocks = (rows + warps - 1) / warps;
   const int grid = static_cast<int>(imin64(blocks, static_cast<int64_t>(num_sms(dev)) * 16));
   rmsnorm_quantize_kernel<<<grid, warps * 32, smem, s>>>(rows, cols, x, w, eps,
-                                                         static_cast<uint8_t*>(aq), asc, u8);
+                                                         static_cast<uint8_t*>(aq), asc, mode);
   return cudaGetLastError();
 }
 
 cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
-                                     const float* up, int64_t ldu, void* aq, float* asc, int u8,
+                                     const float* up, int64_t ldu, void* aq, float* asc, int mode,
                                      cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
   silu_mul_quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(
-      M, K, gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, u8);
+      M, K, gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, mode);
   return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_status_q(int* out, cudaStream_t s) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_status_q, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_status_q, &zero, sizeof(int));
 }
 
 }  // namespace ovb

@@ -8,6 +8,8 @@
 // runner's dequantise-at-load (cuda_lm.cu:228-238, :840-873).  No wsum is
 // needed: the GEMM multiplies signed q by signed w directly, so there is no
 // +128 zero point to remove.
+#include <cuda_fp16.h>
+
 #include "ovb_internal.h"
 
 namespace ovb {
@@ -50,7 +52,31 @@ __global__ void pack_kn_kernel(const int8_t* __restrict__ src, int64_t N, int64_
   }
 }
 
+// int8 -> fp16 bit patterns, 16 values per thread (n is a multiple of 16:
+// rows of Kp = 32 * Kb bytes).  Integers |v| <= 2048 are exact in fp16.
+__global__ void widen_f16_kernel(const int8_t* __restrict__ src, int64_t n16,
+                                 uint16_t* __restrict__ dst) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int4 v = reinterpret_cast<const int4*>(src)[i];
+    const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    uint16_t h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) h[j] = __half_as_ushort(__short2half_rn(b[j]));
+    reinterpret_cast<int4*>(dst)[2 * i] = *reinterpret_cast<const int4*>(&h[0]);
+    reinterpret_cast<int4*>(dst)[2 * i + 1] = *reinterpret_cast<const int4*>(&h[8]);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_widen_f16(const int8_t* src, int64_t n, uint16_t* dst, cudaStream_t s) {
+  if (n % 16 != 0) return cudaErrorInvalidValue;
+  const int64_t n16 = n / 16;
+  const int grid = static_cast<int>(std::min<int64_t>((n16 + 255) / 256, 4096));
+  widen_f16_kernel<<<grid, 256, 0, s>>>(src, n16, dst);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_pack_nk(const int8_t* src, int64_t N, int64_t K, int8_t* dst, int64_t Kp,
                            cudaStream_t s) {

@@ -70,12 +70,17 @@ class Weight:
     ``from_kn`` ([K, N], layout=1).  Replaces ``Mat``'s packed VNNI tiles
     (mat.cpp:88-104 / s8_nk_pack) and the CUDA runner's dequantised copies
     (cuda_lm.cu:840-873).
+
+    ``f16=True`` (OVB_WEIGHT_F16) also keeps an fp16 copy, and the GEMMs on
+    this weight run the fp16 tensor-core mainloop: within rel-L2 ~3e-4 of
+    the reference instead of bit-exact, several times faster.
     """
 
-    def __init__(self, handle: int, N: int, K: int):
+    def __init__(self, handle: int, N: int, K: int, f16: bool = False):
         self._h = handle
         self.N = N
         self.K = K
+        self.f16 = f16
 
     @property
     def handle(self) -> int:
@@ -84,32 +89,33 @@ class Weight:
         return self._h
 
     @classmethod
-    def _create(cls, W, scale, layout: int, N: int, K: int) -> "Weight":
+    def _create(cls, W, scale, layout: int, N: int, K: int, f16: bool) -> "Weight":
         out = C.c_void_p()
+        flags = L.OVB_WEIGHT_F16 if f16 else 0
         if isinstance(W, torch.Tensor) and W.is_cuda:
             W = W.contiguous()
             scale = scale.to(device=W.device, dtype=torch.float32).contiguous()
             st = L.lib().ovb_weight_create(W.data_ptr(), layout, N, K, scale.data_ptr(),
-                                           L.OVB_SRC_DEVICE, _stream(), C.byref(out))
+                                           L.OVB_SRC_DEVICE | flags, _stream(), C.byref(out))
         else:
             Wn = np.ascontiguousarray(W.cpu().numpy() if isinstance(W, torch.Tensor) else W,
                                       dtype=np.int8)
             sn = np.ascontiguousarray(scale.cpu().numpy() if isinstance(scale, torch.Tensor)
                                       else scale, dtype=np.float32)
-            st = L.lib().ovb_weight_create(Wn.ctypes.data, layout, N, K, sn.ctypes.data, 0,
+            st = L.lib().ovb_weight_create(Wn.ctypes.data, layout, N, K, sn.ctypes.data, flags,
                                            _stream(), C.byref(out))
         L.check(st)
-        return cls(out.value, N, K)
+        return cls(out.value, N, K, f16)
 
     @classmethod
-    def from_nk(cls, W, scale) -> "Weight":
+    def from_nk(cls, W, scale, f16: bool = False) -> "Weight":
         N, K = W.shape
-        return cls._create(W, scale, L.OVB_LAYOUT_NK, N, K)
+        return cls._create(W, scale, L.OVB_LAYOUT_NK, N, K, f16)
 
     @classmethod
-    def from_kn(cls, W, scale) -> "Weight":
+    def from_kn(cls, W, scale, f16: bool = False) -> "Weight":
         K, N = W.shape
-        return cls._create(W, scale, L.OVB_LAYOUT_KN, N, K)
+        return cls._create(W, scale, L.OVB_LAYOUT_KN, N, K, f16)
 
     @classmethod
     def concat(cls, parts: list["Weight"]) -> "Weight":
@@ -118,7 +124,7 @@ class Weight:
         out = C.c_void_p()
         L.check(L.lib().ovb_weight_concat(C.cast(arr, C.c_void_p), len(parts), _stream(),
                                           C.byref(out)))
-        return cls(out.value, sum(p.N for p in parts), parts[0].K)
+        return cls(out.value, sum(p.N for p in parts), parts[0].K, all(p.f16 for p in parts))
 
     def export(self):
         """The device weight as ([N, K] int8, [N] fp32) numpy arrays."""
@@ -140,50 +146,65 @@ class Weight:
 
 
 # ------------------------------------------------------------ quantisers
-def _flags(u8: bool) -> int:
-    return L.OVB_AQ_U8 if u8 else 0
+def _flags(u8: bool, f16: bool = False) -> int:
+    if u8 and f16:
+        raise ValueError("u8 and f16 outputs are exclusive")
+    return (L.OVB_AQ_U8 if u8 else 0) | (L.OVB_AQ_F16 if f16 else 0)
 
 
-def _quant_out(M, K, device, u8, out):
+def empty_quant_f16(M: int, K: int, device=None):
+    """Allocate (a16, asc) for M rows: a16 is [M, Kp] fp16 (OVB_AQ_F16 form)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    Kb = kblocks(K)
+    return (torch.empty((M, Kb * 32), dtype=torch.float16, device=dev),
+            torch.empty((M, Kb), dtype=torch.float32, device=dev))
+
+
+def _quant_out(M, K, device, u8, out, f16=False):
     if out is not None:
         return out
+    if f16:
+        return empty_quant_f16(M, K, device)
     aq, asc = empty_quant(M, K, device)
     if u8:
         aq = aq.view(torch.uint8)
     return aq, asc
 
 
-def s8_nk_quantize(A: torch.Tensor, u8: bool = False, out=None):
-    """ov::s8_nk_quantize (ov_gemm.h:97): per-row, per-32-k quantisation."""
+def s8_nk_quantize(A: torch.Tensor, u8: bool = False, out=None, f16: bool = False):
+    """ov::s8_nk_quantize (ov_gemm.h:97): per-row, per-32-k quantisation.
+    ``f16=True`` writes the dequantised fp16(q * asc) instead of q (input of
+    linear_h)."""
     _rows_ok(A, "A")
     M, K = A.shape
-    aq, asc = _quant_out(M, K, A.device, u8, out)
+    aq, asc = _quant_out(M, K, A.device, u8, out, f16)
     L.check(L.lib().ovb_quantize(M, K, _dev_ptr(A), A.stride(0), _dev_ptr(aq), _dev_ptr(asc),
-                                 _flags(u8), _stream()))
+                                 _flags(u8, f16), _stream()))
     return aq, asc
 
 
 def rmsnorm_quantize_f32(x: torch.Tensor, w: torch.Tensor, eps: float, u8: bool = False,
-                         out=None):
+                         out=None, f16: bool = False):
     """ov::rmsnorm_quantize_f32 (ov_gemm.h:118-119)."""
     if not x.is_contiguous():
         raise ValueError("x must be contiguous")
     M, K = x.shape
-    aq, asc = _quant_out(M, K, x.device, u8, out)
+    aq, asc = _quant_out(M, K, x.device, u8, out, f16)
     L.check(L.lib().ovb_rmsnorm_quantize(M, K, _dev_ptr(x), _dev_ptr(w.contiguous()), eps,
-                                         _dev_ptr(aq), _dev_ptr(asc), _flags(u8), _stream()))
+                                         _dev_ptr(aq), _dev_ptr(asc), _flags(u8, f16), _stream()))
     return aq, asc
 
 
-def silu_mul_quantize_f32(gate: torch.Tensor, up: torch.Tensor, u8: bool = False, out=None):
+def silu_mul_quantize_f32(gate: torch.Tensor, up: torch.Tensor, u8: bool = False, out=None,
+                          f16: bool = False):
     """ov::silu_mul_quantize_f32 (ov_gemm.h:84-85)."""
     _rows_ok(gate, "gate")
     _rows_ok(up, "up")
     M, K = gate.shape
-    aq, asc = _quant_out(M, K, gate.device, u8, out)
+    aq, asc = _quant_out(M, K, gate.device, u8, out, f16)
     L.check(L.lib().ovb_silu_mul_quantize(M, K, _dev_ptr(gate), gate.stride(0), _dev_ptr(up),
-                                          up.stride(0), _dev_ptr(aq), _dev_ptr(asc), _flags(u8),
-                                          _stream()))
+                                          up.stride(0), _dev_ptr(aq), _dev_ptr(asc),
+                                          _flags(u8, f16), _stream()))
     return aq, asc
 
 
@@ -221,6 +242,26 @@ def linear_s8_nk_packed_q_sliced(aq: torch.Tensor, asc: torch.Tensor, w: Weight,
     arr = (L.Slice * len(Cs))(*[L.Slice(c.shape[1], _dev_ptr(c), c.stride(0)) for c in Cs])
     L.check(L.lib().ovb_linear_q_sliced(aq.shape[0], w.handle, _dev_ptr(aq), _dev_ptr(asc), arr,
                                         len(Cs), _stream()))
+    return Cs
+
+
+def linear_h(a16: torch.Tensor, w: Weight, C=None, accumulate: bool = False):
+    """The fp16 mainloop on dequantised activations (ovb_linear_h): a16 from a
+    quantiser with ``f16=True``, w created with ``f16=True``."""
+    M = a16.shape[0]
+    C = _out(M, w, C, a16.device)
+    L.check(L.lib().ovb_linear_h(M, w.handle, _dev_ptr(a16), _dev_ptr(C), C.stride(0),
+                                 1 if accumulate else 0, _stream()))
+    return C
+
+
+def linear_h_sliced(a16: torch.Tensor, w: Weight, Cs: list[torch.Tensor]):
+    """linear_h over a concatenated weight, slice i written to Cs[i]."""
+    for c in Cs:
+        _rows_ok(c, "C")
+    arr = (L.Slice * len(Cs))(*[L.Slice(c.shape[1], _dev_ptr(c), c.stride(0)) for c in Cs])
+    L.check(L.lib().ovb_linear_h_sliced(a16.shape[0], w.handle, _dev_ptr(a16), arr, len(Cs),
+                                        _stream()))
     return Cs
 
 

@@ -66,8 +66,10 @@ class LayerWeights:
     post_ln: torch.Tensor
 
     @classmethod
-    def from_host(cls, w: dict, device) -> "LayerWeights":
-        parts = {name: G.Weight.from_nk(*w[name]) for name, _, _ in SHAPES}
+    def from_host(cls, w: dict, device, f16: bool = False) -> "LayerWeights":
+        """``f16`` selects the fp16 tensor-core mainloop (OVB_WEIGHT_F16) for
+        all four GEMMs; otherwise they reproduce the reference bit for bit."""
+        parts = {name: G.Weight.from_nk(*w[name], f16=f16) for name, _, _ in SHAPES}
         qkv = G.Weight.concat([parts["q"], parts["k"], parts["v"]])
         gu = G.Weight.concat([parts["gate"], parts["up"]])
         for name in ("q", "k", "v", "gate", "up"):
@@ -82,26 +84,43 @@ class LayerWeights:
 
 
 class LayerBuffers:
-    """Activation buffers for M rows (allocated once)."""
+    """Activation buffers for M rows (allocated once).  ``f16`` holds the
+    quantisers' outputs in the dequantised fp16 form (OVB_AQ_F16) that the
+    fp16 mainloop (linear_h) reads."""
 
-    def __init__(self, M: int, device):
+    def __init__(self, M: int, device, f16: bool = False):
         f32 = dict(dtype=torch.float32, device=device)
         self.M = M
+        self.f16 = f16
         self.q = torch.empty((M, QD), **f32)
         self.k = torch.empty((M, KVD), **f32)
         self.v = torch.empty((M, KVD), **f32)
         self.gate = torch.empty((M, INTER), **f32)
         self.up = torch.empty((M, INTER), **f32)
-        self.qh = G.empty_quant(M, HIDDEN, device)   # norm+quant of x
-        self.qo = G.empty_quant(M, QD, device)       # quant of attn
-        self.qi = G.empty_quant(M, INTER, device)    # silu*up quant
+        alloc = G.empty_quant_f16 if f16 else G.empty_quant
+        self.qh = alloc(M, HIDDEN, device)   # norm+quant of x
+        self.qo = alloc(M, QD, device)       # quant of attn
+        self.qi = alloc(M, INTER, device)    # silu*up quant
 
 
 def run(x: torch.Tensor, lw: LayerWeights, buf: LayerBuffers, attn: torch.Tensor | None = None):
-    """One layer's linear set on x [M, 1024] (updated in place, residual stream)."""
+    """One layer's linear set on x [M, 1024] (updated in place, residual stream),
+    LM::run_layer's order (lm.cpp:217-322).  With fp16 buffers the quantisers
+    write fp16(q * asc) and the GEMMs run the plain fp16 mainloop; otherwise
+    int8 q + scales and the exact int8 mainloop."""
+    a = buf.q if attn is None else attn
+    if buf.f16:
+        G.rmsnorm_quantize_f32(x, lw.input_ln, RMS_EPS, out=buf.qh, f16=True)
+        G.linear_h_sliced(buf.qh[0], lw.qkv, [buf.q, buf.k, buf.v])
+        G.s8_nk_quantize(a, out=buf.qo, f16=True)
+        G.linear_h(buf.qo[0], lw.o, x, accumulate=True)
+        G.rmsnorm_quantize_f32(x, lw.post_ln, RMS_EPS, out=buf.qh, f16=True)
+        G.linear_h_sliced(buf.qh[0], lw.gate_up, [buf.gate, buf.up])
+        G.silu_mul_quantize_f32(buf.gate, buf.up, out=buf.qi, f16=True)
+        G.linear_h(buf.qi[0], lw.down, x, accumulate=True)
+        return x
     G.rmsnorm_quantize_f32(x, lw.input_ln, RMS_EPS, out=buf.qh)
     G.linear_s8_nk_packed_q_sliced(*buf.qh, lw.qkv, [buf.q, buf.k, buf.v])
-    a = buf.q if attn is None else attn
     G.s8_nk_quantize(a, out=buf.qo)
     G.linear_s8_nk_packed_q_add(*buf.qo, lw.o, x)
     G.rmsnorm_quantize_f32(x, lw.post_ln, RMS_EPS, out=buf.qh)

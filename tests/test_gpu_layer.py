@@ -73,3 +73,30 @@ def test_layer_graph_replay_matches_eager(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert xg.cpu().numpy().tobytes() == xe.cpu().numpy().tobytes()
+
+
+def test_layer_cfg1_f16_path_within_tolerance(cuda):
+    """The same layer on the fp16 mainloop (fp16 weight copies, quantisers in
+    the OVB_AQ_F16 form, ovb_linear_h): each GEMM output within the contract's
+    rel-L2 1e-3 of the reference, the residual stream too; the layer's own
+    contribution (x_out - x_in) within 1e-2 (two GEMMs deep, requantised)."""
+    rng = np.random.default_rng(2024)
+    M = 400
+    w = LY.random_layer_host(rng)
+    x = rng.standard_normal((M, LY.HIDDEN)).astype(np.float32)
+    lw = LY.LayerWeights.from_host(w, cuda, f16=True)
+    buf = LY.LayerBuffers(M, cuda, f16=True)
+    xd = torch.from_numpy(x).to(cuda)
+    LY.run(xd, lw, buf)
+    torch.cuda.synchronize()
+    want, q = oracle_layer(x, w)
+
+    def rel(a, b):
+        return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64)))
+
+    got_q = buf.q.cpu().numpy()
+    assert rel(got_q, q) <= 1e-3
+    got = xd.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel(got, want) <= 1e-3
+    assert rel(got - x, want - x) <= 1e-2
