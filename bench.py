@@ -13,6 +13,13 @@ Metric: int8 tera-ops/s, ops = 2 * M * sum(N*K) = 12.58 G per step.  Under
 torchrun each rank runs the same per-GPU workload (utterance-parallel data
 parallelism: no data-path collective) and `value` is the whole-job total.
 
+Numerics (--numerics): `fp16` (default) runs the fp16 tensor-core mainloop
+(weights with OVB_WEIGHT_F16, quantisers writing fp16(q*asc), ovb_linear_h),
+whose outputs meet the contract's rel-L2 <= 1e-3 / max-abs <= 1e-2*rms;
+`exact` runs the int8 mainloop that reproduces the reference bit for bit.
+The line always carries the other path's number as well (key `exact` or
+`fp16`), measured over the same steps right after the timed region.
+
 `--impl reference` times the reference's own CPU implementation of the same
 layer step (oracle/_ref, built from the reference's sources) on the host cores.
 """
@@ -126,16 +133,112 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def load_traffic() -> float | None:
+def load_traffic(f16: bool) -> float | None:
     """DRAM bytes per launch of the dominant GEMM from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gemm_gate_up_m400_traffic.json")
+    name = "gemm_h_gate_up_m400_traffic.json" if f16 else "gemm_gate_up_m400_traffic.json"
+    p = os.path.join(ROOT, "profiles", name)
     if os.path.exists(p):
         with open(p) as f:
             return float(json.load(f)["dram_bytes_per_launch"])
     return None
 
 
+DTYPE = {
+    "fp16": "fp16 x fp16 -> fp32 (int8 weights exact in fp16, activations fp16(q*asc))",
+    "exact": "int8 (s8 x s8 -> s32 per 32-k block, fp32 epilogue)",
+}
+NUMERICS = {
+    "fp16": "within rel-L2 <= 1e-3 / max-abs <= 1e-2*rms of the reference",
+    "exact": "bit-identical to the reference",
+}
+
+
+def gate_up_roofline(gemm_us: float, f16: bool) -> dict:
+    """Roofline of the gate|up GEMM (M=400, N=6144, K=1024) from its live
+    launch time.  Algorithmic bytes and ops are the path's own (s8 A + fp32
+    scales, int8 W, fp32 C); the bound is the slower of HBM and the tensor pipe
+    the kernel uses (dense bf16 for kind::f16; int8 taken as 2x bf16)."""
+    from ovnative_b200 import layer as LY
+    peaks = load_peaks()
+    N_gu, K_gu = 2 * LY.INTER, LY.HIDDEN
+    Kb = K_gu // 32
+    alg_bytes = (M_TOKENS * K_gu + M_TOKENS * Kb * 4 + N_gu * K_gu + N_gu * 4
+                 + M_TOKENS * N_gu * 4)
+    gemm_ops = 2 * M_TOKENS * N_gu * K_gu
+    tensor_peak = peaks["bf16_tflops"] * (1 if f16 else 2)
+    t_hbm = alg_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_tensor = gemm_ops / (tensor_peak * 1e12)
+    if t_tensor >= t_hbm:
+        achieved, peak, unit = gemm_ops / (gemm_us * 1e-6) / 1e12, tensor_peak, "TFLOP/s"
+    else:
+        achieved, peak, unit = alg_bytes / (gemm_us * 1e-6) / 1e9, peaks["hbm_gbs"], "GB/s"
+    return {
+        "kernel": ("gemm_h (fp16 mainloop" if f16 else "gemm_s8_tc (int8 mainloop")
+                  + ", gate|up sliced, M=400, N=6144, K=1024)",
+        "bound": "tensor" if t_tensor >= t_hbm else "hbm",
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "unit": unit,
+        "frac": round(achieved / peak, 4),
+        "peak_source": peaks["source"] + (" bf16 burst" if f16 else " 2x bf16 burst / hbm copy"),
+        "algorithmic_bytes": alg_bytes,
+        "algorithmic_ops": gemm_ops,
+        "us_per_launch": round(gemm_us, 3),
+        "roofline_us": round(max(t_hbm, t_tensor) * 1e6, 3),
+        "traffic": load_traffic(f16),
+    }
+
+
 # ---------------------------------------------------------------- our arm
+class LayerPath:
+    """28 layers' weights, buffers and CUDA graphs of one numerics path."""
+
+    def __init__(self, f16: bool, dev, stream, seed: int = 1000):
+        import torch
+
+        import ovnative_b200 as ovb
+        from ovnative_b200 import layer as LY
+        rng = np.random.default_rng(seed)
+        self.f16 = f16
+        self.layers = [LY.LayerWeights.from_host(LY.random_layer_host(rng), dev, f16=f16)
+                       for _ in range(N_LAYERS)]
+        self.buf = LY.LayerBuffers(M_TOKENS, dev, f16=f16)
+        self.x0 = torch.from_numpy(
+            rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32)).to(dev)
+        self.x = self.x0.clone()
+        # Eager warm-up sets the kernels' shared-memory attributes before capture.
+        for lw in self.layers[:2]:
+            LY.run(self.x, lw, self.buf)
+        torch.cuda.synchronize()
+        if ovb.device_status() != 0:
+            raise RuntimeError("device wait timed out during warm-up")
+        self.graphs = []
+        with torch.cuda.stream(stream):
+            for lw in self.layers:  # one graph per layer step
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    LY.run(self.x, lw, self.buf)
+                self.graphs.append(g)
+            self.chain = torch.cuda.CUDAGraph()  # all 28 steps; x reset first (1.6 MB)
+            with torch.cuda.graph(self.chain, stream=stream):
+                self.x.copy_(self.x0)
+                for lw in self.layers:
+                    LY.run(self.x, lw, self.buf)
+
+    def run_steps(self, n: int):
+        full, rest = divmod(n, N_LAYERS)
+        for _ in range(full):
+            self.chain.replay()
+        for i in range(rest):
+            self.graphs[i].replay()
+
+    def release(self):
+        for g in self.graphs + [self.chain]:
+            g.reset()
+        for lw in self.layers:
+            lw.close()
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -154,43 +257,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         if world > 1:
             dist.barrier()
 
-    rng = np.random.default_rng(1000)
-    layers = [LY.LayerWeights.from_host(LY.random_layer_host(rng), dev) for _ in range(N_LAYERS)]
-    buf = LY.LayerBuffers(M_TOKENS, dev)
-    x0 = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32)).to(dev)
-    x = x0.clone()
+    def max_over_ranks(ms: float) -> float:
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    f16 = args.numerics == "fp16"
+    stream = torch.cuda.Stream(device=dev)
+    path = LayerPath(f16, dev, stream)
+    layers, buf, x0, x = path.layers, path.buf, path.x0, path.x
+    graphs = path.graphs
     ops_step = M_TOKENS * LY.ops_per_token()
 
-    # Eager warm-up sets the kernels' shared-memory attributes before capture.
-    for lw in layers[:2]:
-        LY.run(x, lw, buf)
-    torch.cuda.synchronize()
-    if ovb.device_status() != 0:
-        raise RuntimeError("device wait timed out during warm-up")
-
-    stream = torch.cuda.Stream(device=dev)
-    graphs = []
     with torch.cuda.stream(stream):
-        for lw in layers:  # one graph per layer step
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                LY.run(x, lw, buf)
-            graphs.append(g)
-        chain = torch.cuda.CUDAGraph()  # all 28 steps; x reset first (one 1.6 MB copy)
-        with torch.cuda.graph(chain, stream=stream):
-            x.copy_(x0)
-            for lw in layers:
-                LY.run(x, lw, buf)
-
-    def run_steps(n):
-        full, rest = divmod(n, N_LAYERS)
-        for _ in range(full):
-            chain.replay()
-        for i in range(rest):
-            graphs[i].replay()
-
-    with torch.cuda.stream(stream):
-        run_steps(args.warmup)
+        path.run_steps(args.warmup)
     torch.cuda.synchronize()
 
     # ---- timed region: exactly K steps
@@ -201,16 +283,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     with ClockSampler(local_rank) as clk:
         with torch.cuda.stream(stream):
             ev0.record(stream)
-            run_steps(args.steps)
+            path.run_steps(args.steps)
             ev1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    ms = ev0.elapsed_time(ev1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1))
     value = world * args.steps * ops_step / (ms_max * 1e-3) / 1e12
 
     # ---- dominant kernel, timed live: the gate|up sliced GEMM (N=6144, K=1024),
@@ -219,49 +296,27 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     n_launch = 4 * N_LAYERS
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
-    aq, asc = buf.qh
     with torch.cuda.stream(stream):
-        ovb.rmsnorm_quantize_f32(x0, layers[0].post_ln, LY.RMS_EPS, out=buf.qh)
+        ovb.rmsnorm_quantize_f32(x0, layers[0].post_ln, LY.RMS_EPS, out=buf.qh, f16=f16)
         kg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(kg, stream=stream):
             for i in range(n_launch):
-                ovb.linear_s8_nk_packed_q_sliced(aq, asc, layers[i % N_LAYERS].gate_up,
-                                                 [buf.gate, buf.up])
+                if f16:
+                    ovb.linear_h_sliced(buf.qh[0], layers[i % N_LAYERS].gate_up,
+                                        [buf.gate, buf.up])
+                else:
+                    ovb.linear_s8_nk_packed_q_sliced(*buf.qh, layers[i % N_LAYERS].gate_up,
+                                                     [buf.gate, buf.up])
         kg.replay()  # warm
         k0.record(stream)
         kg.replay()
         k1.record(stream)
     torch.cuda.synchronize()
     gemm_us = k0.elapsed_time(k1) * 1e3 / n_launch
-    peaks = load_peaks()
-    N_gu, K_gu = 2 * LY.INTER, LY.HIDDEN
-    Kb = K_gu // 32
-    alg_bytes = (M_TOKENS * K_gu + M_TOKENS * Kb * 4 + N_gu * K_gu + N_gu * 4
-                 + M_TOKENS * N_gu * 4)
-    gemm_ops = 2 * M_TOKENS * N_gu * K_gu
-    achieved_gbs = alg_bytes / (gemm_us * 1e-6) / 1e9
-    # int8 MMA peak taken as 2x the measured dense bf16 rate (same tensor
-    # pipe, half the operand width); the HBM bound is the larger time here.
-    t_hbm = alg_bytes / (peaks["hbm_gbs"] * 1e9)
-    t_int8 = gemm_ops / (2 * peaks["bf16_tflops"] * 1e12)
-    roofline = {
-        "kernel": "gemm_s8_tc (gate|up sliced, M=400, N=6144, K=1024)",
-        "bound": "hbm" if t_hbm >= t_int8 else "tensor",
-        "achieved": round(achieved_gbs, 1),
-        "peak": peaks["hbm_gbs"],
-        "unit": "GB/s",
-        "frac": round(achieved_gbs / peaks["hbm_gbs"], 4),
-        "peak_source": peaks["source"],
-        "algorithmic_bytes": alg_bytes,
-        "us_per_launch": round(gemm_us, 3),
-        "tensor_tops": round(gemm_ops / (gemm_us * 1e-6) / 1e12, 1),
-        "tensor_frac_of_2x_bf16": round(gemm_ops / (gemm_us * 1e-6) / 1e12
-                                        / (2 * peaks["bf16_tflops"]), 4),
-        "roofline_us": round(max(t_hbm, t_int8) * 1e6, 3),
-        "traffic": load_traffic(),
-    }
+    roofline = gate_up_roofline(gemm_us, f16)
 
     # ---- end to end through the public API with host buffers
+    rng = np.random.default_rng(77)
     xh_in = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
     xh_in = xh_in.pin_memory()
     xh_out = torch.empty_like(xh_in).pin_memory()
@@ -289,8 +344,32 @@ def run_ours(args, rank: int, world: int, local_rank: int):
            "ms_per_step": e2e_ms / args.steps}
 
     status = ovb.device_status()
-    for g in graphs + [chain, kg]:
-        g.reset()
+    kg.reset()
+    path.release()
+
+    # ---- the other numerics path over the same K steps (reported, not headline)
+    other_line = None
+    if not args.skip_other:
+        other = LayerPath(not f16, dev, stream)
+        with torch.cuda.stream(stream):
+            other.run_steps(args.warmup)
+        barrier()
+        torch.cuda.synchronize()
+        o0 = torch.cuda.Event(enable_timing=True)
+        o1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            o0.record(stream)
+            other.run_steps(args.steps)
+            o1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        o_ms = max_over_ranks(o0.elapsed_time(o1))
+        status |= ovb.device_status()
+        other.release()
+        other_line = {"value": world * args.steps * ops_step / (o_ms * 1e-3) / 1e12,
+                      "unit": "TOPS", "ms_per_step": o_ms / args.steps,
+                      "numerics": NUMERICS["exact" if f16 else "fp16"]}
+
     if world > 1:
         dist.destroy_process_group()
     if status != 0:
@@ -314,10 +393,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "int8 (s8 x s8 -> s32 per 32-k block, fp32 epilogue)",
+        "dtype": DTYPE[args.numerics],
+        "numerics": NUMERICS[args.numerics],
         "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
         "config": config(world),
         "impl": "ours",
+        ("exact" if f16 else "fp16"): other_line,
         "e2e": e2e,
         "gpu_launches": args.steps * LY.KERNELS_PER_LAYER,
         "roofline": roofline,
@@ -365,6 +446,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--numerics", choices=["fp16", "exact"], default="fp16")
+    ap.add_argument("--skip-other", action="store_true",
+                    help="do not time the other numerics path (for profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
