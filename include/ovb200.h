@@ -111,6 +111,13 @@ int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const f
  * fp16 copy (OVB_WEIGHT_F16) when every part has it. */
 int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
                       ovb_weight** out);
+/* Gate|up weight for the fused SiLU*up GEMMs below: the two projections'
+ * rows interleaved in 32-row blocks (gate and up must have the same N, a
+ * multiple of 32, and K).  It keeps the fp16 copy when both parts have one.
+ * No counterpart in the reference (its gate_up is combine_packed, lm.cpp:57-94,
+ * followed by a separate silu_mul_quantize_f32). */
+int ovb_weight_gate_up(const ovb_weight* gate, const ovb_weight* up, void* stream,
+                       ovb_weight** out);
 int ovb_weight_destroy(ovb_weight* w);
 int ovb_weight_shape(const ovb_weight* w, int64_t* N, int64_t* K);
 /* Copy the device weight back as [N, K] int8 and its N scales (host pointers);
@@ -141,6 +148,21 @@ int ovb_linear_q(int64_t M, const ovb_weight* w, const int8_t* aq, const float* 
  * Replaces ov::linear_s8_nk_packed_q_sliced (ov_gemm.h:109-111). */
 int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
                         const ovb_slice* slices, int n_slices, void* stream);
+
+/* gate|up GEMM fused with silu_mul_quantize_f32 (ov_gemm.h:84-85): computes
+ * gate = x*Wg^T*sg and up = x*Wu^T*su exactly as ovb_linear_q would, then
+ * writes quantise(silu(gate) * up) -- the down projection's input -- in the
+ * form `flags` selects (0 int8 q / OVB_AQ_U8 / OVB_AQ_F16) into out
+ * [M, Kp_inter] and its scales into out_asc [M, inter/32], without writing
+ * gate and up.  w comes from ovb_weight_gate_up.  The _q form runs the int8
+ * mainloop and is bit-identical to the reference's two calls; the _h form
+ * takes fp16(q*asc) activations (OVB_WEIGHT_F16 weights) and runs the fp16
+ * mainloop (tolerance numerics).  Replaces linear_s8_nk_packed_q_sliced on
+ * gate|up plus silu_mul_quantize_f32 (lm.cpp:295-311). */
+int ovb_linear_q_silu(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
+                      void* out, float* out_asc, int flags, void* stream);
+int ovb_linear_h_silu(int64_t M, const ovb_weight* w, const void* a16, void* out,
+                      float* out_asc, int flags, void* stream);
 
 /* The fp16 mainloop on already-dequantised activations: a16 is [M, Kp] fp16,
  * fp16(q * asc) as written by a quantiser with OVB_AQ_F16; w must have been

@@ -13,7 +13,9 @@ from .gemm import (  # noqa: F401
     empty_quant,
     empty_quant_f16,
     linear_h,
+    linear_h_silu,
     linear_h_sliced,
+    linear_q_silu,
     linear_s8_nk_packed,
     linear_s8_nk_packed_add,
     linear_s8_nk_packed_q,

@@ -49,6 +49,9 @@ SIGNATURES = {
     "ovb_linear_q": ([_i64, _p, _p, _p, _p, _i64, _int, _p], _int),
     "ovb_linear_q_sliced": ([_i64, _p, _p, _p, C.POINTER(Slice), _int, _p], _int),
     "ovb_linear_h": ([_i64, _p, _p, _p, _i64, _int, _p], _int),
+    "ovb_linear_q_silu": ([_i64, _p, _p, _p, _p, _p, _int, _p], _int),
+    "ovb_linear_h_silu": ([_i64, _p, _p, _p, _p, _int, _p], _int),
+    "ovb_weight_gate_up": ([_p, _p, _p, C.POINTER(_p)], _int),
     "ovb_linear_h_sliced": ([_i64, _p, _p, C.POINTER(Slice), _int, _p], _int),
     "ovb_linear_workspace_bytes": ([_i64, _i64], C.c_size_t),
     "ovb_linear": ([_i64, _p, _p, _i64, _p, _i64, _int, _p, C.c_size_t, _p], _int),

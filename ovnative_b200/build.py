@@ -26,7 +26,7 @@ LIB = os.path.join(HERE, "libovb200.so")
 
 CU_SOURCES = ["quant.cu", "weights.cu", "gemm_tc.cu", "gemm_f16.cu", "linear_static.cu"]
 CXX_SOURCES = ["capi.cpp"]
-HEADERS = ["ovb_internal.h", "ovb_ptx.cuh"]
+HEADERS = ["ovb_internal.h", "ovb_ptx.cuh", "ovb_quant.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC",

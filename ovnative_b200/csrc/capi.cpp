@@ -184,9 +184,16 @@ int check_q_args(int64_t M, const ovb_weight* w, const int8_t* aq, const float* 
   return OVB_OK;
 }
 
+// Fused SiLU*up output of a gate|up GEMM (null: none).
+struct SiluOut {
+  void* out;
+  float* asc;
+  int mode;
+};
+
 int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc,
              const ovb::SliceOut* slices, int n_slices, int accumulate, int32_t* products,
-             cudaStream_t s) {
+             cudaStream_t s, const SiluOut* silu = nullptr) {
   ovb_weight* w = const_cast<ovb_weight*>(wc);
   if (!ensure_weight_tmap(w)) return OVB_ERR_INTERNAL;
   CUtensorMap tmap_a;
@@ -194,7 +201,8 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
                            static_cast<uint64_t>(w->Kp), ovb::kBlockM))
     return OVB_ERR_INTERNAL;
   ovb::GemmArgs args{};
-  const bool f16 = w->w16 != nullptr && products == nullptr;
+  // The fused SiLU*up epilogue and the block products run the int8 mainloop.
+  const bool f16 = w->w16 != nullptr && products == nullptr && silu == nullptr;
   CUtensorMap tmap_a16;
   if (f16 && !ovb::encode_tmap_2d(&tmap_a16, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8,
                                   static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(M),
@@ -210,6 +218,15 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
   args.n_slices = n_slices;
   for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
   args.products = products;
+  if (silu) {
+    args.silu_out = static_cast<uint8_t*>(silu->out);
+    args.silu_asc = silu->asc;
+    args.silu_mode = silu->mode;
+    args.silu_kp = w->glu_inter;
+    if (cuda_failed(ovb::launch_gemm(0, tmap_a, w->tmap_b[0], args, s), "gemm launch"))
+      return OVB_ERR_INTERNAL;
+    return OVB_OK;
+  }
   if (f16) {
     if (!ensure_weight_tmap16(w)) return OVB_ERR_INTERNAL;
     const int tile = ovb::pick_tile_f16(M, w->N, w->Kb, w->device);
@@ -226,7 +243,7 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
 
 // The plain fp16 mainloop on dequantised activations a16 [M, Kp] fp16.
 int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::SliceOut* slices,
-               int n_slices, int accumulate, cudaStream_t s) {
+               int n_slices, int accumulate, cudaStream_t s, const SiluOut* silu = nullptr) {
   ovb_weight* w = const_cast<ovb_weight*>(wc);
   if (!ensure_weight_tmap16(w)) return OVB_ERR_INTERNAL;
   CUtensorMap tmap_a;
@@ -245,7 +262,13 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
   args.n_slices = n_slices;
   for (int i = 0; i < n_slices; ++i) args.slices[i] = slices[i];
   args.products = nullptr;
-  const int tile = ovb::pick_tile_h(M, w->N, w->Kb, w->device);
+  if (silu) {
+    args.silu_out = static_cast<uint8_t*>(silu->out);
+    args.silu_asc = silu->asc;
+    args.silu_mode = silu->mode;
+    args.silu_kp = w->glu_inter;
+  }
+  const int tile = ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : 4);
   if (cuda_failed(ovb::launch_gemm_h(tile, tmap_a, w->tmap_w16[tile], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
@@ -267,6 +290,17 @@ int build_slices(const ovb_weight* w, const ovb_slice* slices, int n_slices,
     total += slices[i].N;
   }
   if (total != w->N) return invalid("sliced GEMM: slice widths do not add up to the weight's N");
+  return OVB_OK;
+}
+
+// Checks of a fused gate|up + SiLU*up call's weight and outputs.
+int check_silu_out(const ovb_weight* w, void* out, float* out_asc, int flags, int* mode) {
+  if (!w) return invalid("weight handle is null");
+  if (w->glu_inter <= 0) return invalid("the fused SiLU*up GEMM needs a gate|up weight (ovb_weight_gate_up)");
+  if (!out || !out_asc) return invalid("out/out_asc must be non-null");
+  *mode = quant_mode(flags);
+  if (*mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
+  if (!aligned(out, 16) || !aligned(out_asc, 4)) return invalid("misaligned output buffer");
   return OVB_OK;
 }
 
@@ -412,6 +446,51 @@ int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
   return OVB_OK;
 }
 
+int ovb_weight_gate_up(const ovb_weight* gate, const ovb_weight* up, void* stream,
+                       ovb_weight** out) {
+  if (!out) return invalid("out is null");
+  *out = nullptr;
+  if (!gate || !up) return invalid("gate/up handle is null");
+  if (gate->N != up->N || gate->K != up->K) return invalid("gate_up: gate and up differ in shape");
+  if (gate->N % 32 != 0) return invalid("gate_up: N must be a multiple of 32");
+  if (gate->device != up->device) return invalid("gate_up: parts on different devices");
+  cudaStream_t s = as_stream(stream);
+  auto* w = new ovb_weight();
+  w->device = gate->device;
+  w->N = 2 * gate->N;
+  w->K = gate->K;
+  w->Kb = gate->Kb;
+  w->Kp = gate->Kp;
+  w->glu_inter = gate->N;
+  const int64_t blocks = gate->N / 32;
+  // Rows interleaved in 32-row blocks: out block 2j = gate block j, 2j+1 = up block j.
+  auto interleave = [&](void* dst, const void* g, const void* u, size_t row_bytes) {
+    const size_t blk = 32 * row_bytes;
+    return !cuda_failed(cudaMemcpy2DAsync(dst, 2 * blk, g, blk, blk, static_cast<size_t>(blocks),
+                                          cudaMemcpyDeviceToDevice, s),
+                        "gate_up interleave") &&
+           !cuda_failed(cudaMemcpy2DAsync(static_cast<uint8_t*>(dst) + blk, 2 * blk, u, blk, blk,
+                                          static_cast<size_t>(blocks), cudaMemcpyDeviceToDevice, s),
+                        "gate_up interleave");
+  };
+  bool ok = !cuda_failed(cudaMalloc(&w->w, static_cast<size_t>(w->N * w->Kp)), "cudaMalloc") &&
+            !cuda_failed(cudaMalloc(&w->scale, static_cast<size_t>(w->N) * 4), "cudaMalloc");
+  if (ok) ok = interleave(w->w, gate->w, up->w, static_cast<size_t>(w->Kp));
+  if (ok) ok = interleave(w->scale, gate->scale, up->scale, 4);
+  if (ok && gate->w16 && up->w16) {
+    ok = !cuda_failed(cudaMalloc(&w->w16, static_cast<size_t>(w->N * w->Kp) * 2), "cudaMalloc") &&
+         interleave(w->w16, gate->w16, up->w16, static_cast<size_t>(w->Kp) * 2);
+  }
+  if (ok) ok = !cuda_failed(cudaStreamSynchronize(s), "gate_up sync") && ensure_weight_tmap(w) &&
+               ensure_weight_tmap16(w);
+  if (!ok) {
+    free_weight(w);
+    return OVB_ERR_INTERNAL;
+  }
+  *out = w;
+  return OVB_OK;
+}
+
 int ovb_weight_destroy(ovb_weight* w) {
   if (!w) return OVB_OK;
   int prev = 0;
@@ -513,6 +592,32 @@ int ovb_linear_q_sliced(int64_t M, const ovb_weight* w, const int8_t* aq, const 
   st = build_slices(w, slices, n_slices, so);
   if (st != OVB_OK) return st;
   return run_gemm(M, w, aq, asc, so, n_slices, 0, nullptr, as_stream(stream));
+}
+
+int ovb_linear_q_silu(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc,
+                      void* out, float* out_asc, int flags, void* stream) {
+  if (M <= 0) return OVB_OK;
+  int st = check_q_args(M, w, aq, asc);
+  if (st != OVB_OK) return st;
+  int mode = 0;
+  st = check_silu_out(w, out, out_asc, flags, &mode);
+  if (st != OVB_OK) return st;
+  const ovb::SliceOut so{0, w->N, nullptr, 0};
+  const SiluOut silu{out, out_asc, mode};
+  return run_gemm(M, w, aq, asc, &so, 1, 0, nullptr, as_stream(stream), &silu);
+}
+
+int ovb_linear_h_silu(int64_t M, const ovb_weight* w, const void* a16, void* out,
+                      float* out_asc, int flags, void* stream) {
+  if (M <= 0) return OVB_OK;
+  int st = check_h_args(M, w, a16);
+  if (st != OVB_OK) return st;
+  int mode = 0;
+  st = check_silu_out(w, out, out_asc, flags, &mode);
+  if (st != OVB_OK) return st;
+  const ovb::SliceOut so{0, w->N, nullptr, 0};
+  const SiluOut silu{out, out_asc, mode};
+  return run_gemm_h(M, w, a16, &so, 1, 0, as_stream(stream), &silu);
 }
 
 int ovb_linear_h(int64_t M, const ovb_weight* w, const void* a16, float* C, int64_t ldc,

@@ -61,6 +61,7 @@
 
 #include "ovb_internal.h"
 #include "ovb_ptx.cuh"
+#include "ovb_quant.cuh"
 
 namespace ovb {
 
@@ -183,8 +184,9 @@ __device__ __forceinline__ void store_rows(const float* stg, int stride, float* 
 // wscale values are fetched before the accumulator is ready (tfull[d]), the
 // TMEM load of the next chunk runs while the current one is stored, and
 // after the last chunk the warps bar.sync on dfree_bar + d with the MMA warp
-// (which syncs there before reusing accumulator d).
-template <int BN, int kAcc>
+// (which syncs there before reusing accumulator d).  kPipe = false loads one
+// chunk at a time (for kernels short of registers).
+template <int BN, int kAcc, bool kPipe = true>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull,
                                               volatile int* abort, uint32_t tmem_base,
                                               float* stg, int quarter, int eh, int dfree_bar,
@@ -223,10 +225,11 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
       for (int i = 0; i < kMine; ++i) {
         const int c = eh + 2 * i;
         if (c >= kChunks) break;
-        uint32_t(&cur)[32] = (i & 1) ? vb : va;
-        uint32_t(&nxt)[32] = (i & 1) ? va : vb;
+        uint32_t(&cur)[32] = (kPipe && (i & 1)) ? vb : va;
+        uint32_t(&nxt)[32] = (kPipe && (i & 1)) ? va : vb;
+        if (!kPipe && i > 0) tmem_ld32(dcol + static_cast<uint32_t>(c * 32), cur);
         tc_wait_ld32(cur);
-        if (c + 2 < kChunks) tmem_ld32(dcol + static_cast<uint32_t>((c + 2) * 32), nxt);
+        if (kPipe && c + 2 < kChunks) tmem_ld32(dcol + static_cast<uint32_t>((c + 2) * 32), nxt);
 #pragma unroll
         for (int j = 0; j < 32; ++j) stg[lane * kStgStrideF + j] = __uint_as_float(cur[j]);
         __syncwarp();
@@ -250,6 +253,92 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     tc_fence_before();
     if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiWarpsF + 1));
   }
+}
+
+// silu(g) * u for the fp16 mainloop's fused epilogue, which owes the
+// contract's tolerance rather than the reference's bits: the hardware's
+// approximate exponential and division (CUDA's __expf / __fdividef, relative
+// error ~1e-6, far below the fp16 rounding of the activations).
+__device__ __forceinline__ float silu_up_fast(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+// The epilogue loop of the fused SiLU*up mode (gate|up weight, rows
+// interleaved in 32-row blocks): chunk 2p of a tile is gate block
+// J = n0/64 + p, chunk 2p+1 the up block J.  The kEpiW epilogue warps are
+// kEpiW/4 per TMEM lane quarter; warp (quarter, eh) takes the pairs
+// p = eh, eh + kEpiW/4, ...: each thread holds one row's 32 gate and 32 up
+// accumulators, forms g = D_g * wscale and u = D_u * wscale per column, then
+// v = silu(g) * u (silu_mul_quantize_f32's formula, ops_cpu.cpp:144-198, with
+// fast exp/division) and quantises the whole 32-column block of its row.
+template <int BN, int kAcc, int kEpiW>
+__device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_t* tfull,
+                                                   volatile int* abort, uint32_t tmem_base,
+                                                   int quarter, int eh, int dfree_bar,
+                                                   int64_t tiles, int64_t m_tiles,
+                                                   int64_t my_tiles) {
+  constexpr int kPairs = BN / 64;
+  constexpr int kPerQ = kEpiW / 4;  // warps per lane quarter
+  constexpr int kMine = (kPairs + kPerQ - 1) / kPerQ;
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const int64_t esz = args.silu_mode == 2 ? 2 : 1;
+  bool range_bad = false;
+  int64_t t = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+    const int d = static_cast<int>(t % kAcc);
+    const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
+    const int64_t m0 = (tile % m_tiles) * kBlockM;
+    const int64_t n0 = (tile / m_tiles) * BN;
+    float wsg[kMine], wsu[kMine];
+#pragma unroll
+    for (int i = 0; i < kMine; ++i) {
+      const int64_t ng = n0 + (eh + kPerQ * i) * 64 + lane;
+      const bool ok = eh + kPerQ * i < kPairs && ng + 32 < N;
+      wsg[i] = ok ? __ldg(args.wscale + ng) : 0.f;
+      wsu[i] = ok ? __ldg(args.wscale + ng + 32) : 0.f;
+    }
+    const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0) {
+        atomicOr(&g_status_f16, kErrEpilogue);
+        *abort = 1;
+      }
+    } else {
+      tc_fence_after();
+      const int64_t m = m0 + quarter * 32 + lane;
+      const uint32_t dcol = tmem_base + lane_off + static_cast<uint32_t>(d * BN);
+#pragma unroll
+      for (int i = 0; i < kMine; ++i) {
+        const int p = eh + kPerQ * i;
+        if (p >= kPairs) break;
+        uint32_t vg[32], vu[32];
+        tmem_ld32(dcol + static_cast<uint32_t>(p * 64), vg);
+        tmem_ld32(dcol + static_cast<uint32_t>(p * 64 + 32), vu);
+        tc_wait_ld32(vg);
+        tc_wait_ld32(vu);
+        // All lanes form v (the shuffles need the whole warp); rows past M
+        // and columns past N are not stored.
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float g = __fmul_rn(__uint_as_float(vg[j]), __shfl_sync(0xffffffffu, wsg[i], j));
+          const float u = __fmul_rn(__uint_as_float(vu[j]), __shfl_sync(0xffffffffu, wsu[i], j));
+          v[j] = silu_up_fast(g, u);
+        }
+        if (n0 + p * 64 < N && m < M) {
+          const int64_t J = n0 / 64 + p;
+          const float sc = quant_block32(v, args.silu_out + (m * args.silu_kp + J * 32) * esz,
+                                         args.silu_mode, &range_bad);
+          args.silu_asc[m * (args.silu_kp / 32) + J] = sc;
+        }
+      }
+    }
+    tc_fence_before();
+    if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiW + 1));
+  }
+  if (range_bad) atomicOr(&g_status_f16, kErrF16Range);
 }
 
 template <int BN>
@@ -440,9 +529,10 @@ __global__ void __launch_bounds__(kThreadsF, 1)
     if (!range_ok) atomicOr(&g_status_f16, kErrF16Range);
   } else {
     // ------------------------------------------------------------ epilogue
-    epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                               stg_all + (warp - kFirstEpi) * (32 * kStgStrideF), warp & 3,
-                               (warp - kFirstEpi) >> 2, kBarDfree, tiles, m_tiles, my_tiles);
+    epilogue_loop<BN, T::kAcc, false>(args, ctl->tfull, abort, tmem_base,
+                                      stg_all + (warp - kFirstEpi) * (32 * kStgStrideF), warp & 3,
+                                      (warp - kFirstEpi) >> 2, kBarDfree, tiles, m_tiles,
+                                      my_tiles);
   }
 
   tc_fence_before();
@@ -466,7 +556,11 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 //   3..10 epilogue (epilogue_loop), accumulators double-buffered in TMEM.
 constexpr int kStagesH = 4;
 constexpr int kFirstEpiH = 3;
-constexpr int kThreadsH = 32 * (kFirstEpiH + kEpiWarpsF);
+// Epilogue warps: 8 for plain outputs (each stages 32x32 chunks in shared
+// memory); 16 for the fused SiLU*up epilogue, which is arithmetic-heavy and
+// needs no staging.
+template <bool kSilu>
+constexpr int epi_warps_h() { return kSilu ? 16 : kEpiWarpsF; }
 constexpr uint32_t kABytesH = kBlockM * kStageKF * 2;  // 16 KB
 constexpr int kBarFullH = 1;
 constexpr int kBarDfreeH = 2;  // + d
@@ -480,30 +574,31 @@ struct CtlH {
   int abort;
 };
 
-template <int BN>
+template <int BN, bool kSilu>
 struct TileH {
   static constexpr uint32_t kWBytes = BN * 128;
   static constexpr uint32_t kStageBytes = kABytesH + kWBytes;
   static constexpr int kAcc = 2;
+  static constexpr int kEpiW = epi_warps_h<kSilu>();
+  static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
+  static constexpr size_t kStgAll = kSilu ? 0 : static_cast<size_t>(kEpiW) * 32 * kStgStrideF * 4;
   static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStagesH) * kStageBytes +
-                                       static_cast<size_t>(kEpiWarpsF) * 32 * kStgStrideF * 4 +
-                                       sizeof(CtlH);
+                                       kStgAll + sizeof(CtlH);
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN>
-__global__ void __launch_bounds__(kThreadsH, 1)
+template <int BN, bool kSilu>
+__global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
     gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ GemmArgs args) {
-  using T = TileH<BN>;
+  using T = TileH<BN, kSilu>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(kStagesH) * T::kStageBytes);
-  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) +
-                                      static_cast<size_t>(kEpiWarpsF) * 32 * kStgStrideF * 4);
+  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -577,7 +672,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     int64_t st = 0;
     for (int64_t t = 0; t < my_tiles; ++t) {
       const int d = static_cast<int>(t % T::kAcc);
-      if (t >= T::kAcc) named_sync(kBarDfreeH + d, 32 * (kEpiWarpsF + 1));  // accumulator d read
+      if (t >= T::kAcc) named_sync(kBarDfreeH + d, 32 * (T::kEpiW + 1));  // accumulator d read
       const uint32_t dcol = tmem_base + static_cast<uint32_t>(d * BN);
       for (int j = 0; j < ksteps; ++j, ++st) {
         const int s = static_cast<int>(st % kStagesH);
@@ -621,9 +716,15 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                               stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                               (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles);
+    if constexpr (kSilu) {
+      epilogue_silu_loop<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, warp & 3,
+                                                (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
+                                                m_tiles, my_tiles);
+    } else {
+      epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                                 stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles);
+    }
   }
 
   tc_fence_before();
@@ -634,15 +735,15 @@ __global__ void __launch_bounds__(kThreadsH, 1)
   }
 }
 
-template <int BN>
+template <int BN, bool kSilu>
 cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  using T = TileH<BN>;
+  using T = TileH<BN, kSilu>;
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_h_kernel<BN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_h_kernel<BN, kSilu>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(T::kSmemBytes));
     if (e != cudaSuccess) return e;
@@ -650,7 +751,7 @@ cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  gemm_h_kernel<BN><<<grid, kThreadsH, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
+  gemm_h_kernel<BN, kSilu><<<grid, T::kThreads, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
   return cudaGetLastError();
 }
 
@@ -708,10 +809,10 @@ int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device) {
 // tensor core (4 MMAs: ~128 clocks each at N = 256, ~64 at N <= 128) and the
 // TMA feed (measured ~375 clocks for stages up to ~40 KB, ~100 B/clock per SM
 // beyond), plus a per-tile cost (prologue, epilogue stores) growing with BN.
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device) {
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_widths) {
   if (const char* e = std::getenv("OVB_GEMM_TILE_N")) {
     const int v = std::atoi(e);
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < n_widths; ++i)
       if (kTileNF[i] == v) return i;
   }
   static constexpr int64_t kPerStage[4] = {512, 375, 375, 375};
@@ -720,7 +821,7 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device) {
   const int64_t ksteps = (Kb + 1) / 2;
   int best = 0;
   int64_t best_cost = -1;
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < n_widths; ++i) {
     const int64_t tiles = m_tiles * ((N + kTileNF[i] - 1) / kTileNF[i]);
     const int64_t waves = (tiles + sms - 1) / sms;
     const int64_t cost = waves * (2000 + 10 * kTileNF[i] + ksteps * kPerStage[i]);
@@ -734,11 +835,19 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device) {
 
 cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
+  if (args.silu_out) {
+    switch (tile) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
+      case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);
+      case 1: return launch_h_impl<128, true>(tmap_a, tmap_w, args, s);
+      case 2: return launch_h_impl<64, true>(tmap_a, tmap_w, args, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (tile) {
-    case 0: return launch_h_impl<256>(tmap_a, tmap_w, args, s);
-    case 1: return launch_h_impl<128>(tmap_a, tmap_w, args, s);
-    case 2: return launch_h_impl<64>(tmap_a, tmap_w, args, s);
-    case 3: return launch_h_impl<32>(tmap_a, tmap_w, args, s);
+    case 0: return launch_h_impl<256, false>(tmap_a, tmap_w, args, s);
+    case 1: return launch_h_impl<128, false>(tmap_a, tmap_w, args, s);
+    case 2: return launch_h_impl<64, false>(tmap_a, tmap_w, args, s);
+    case 3: return launch_h_impl<32, false>(tmap_a, tmap_w, args, s);
     default: return cudaErrorInvalidValue;
   }
 }

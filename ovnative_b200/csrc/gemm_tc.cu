@@ -61,6 +61,7 @@
 
 #include "ovb_internal.h"
 #include "ovb_ptx.cuh"
+#include "ovb_quant.cuh"
 
 namespace ovb {
 
@@ -92,6 +93,15 @@ constexpr int kErrProducer = 1;
 constexpr int kErrMma = 2;
 constexpr int kErrEpilogue = 4;
 constexpr int kErrDrain = 8;
+constexpr int kErrF16Range = 16;  // fused SiLU*up output beyond the fp16 range
+
+// Kernel modes: C = wscale * sum (+ C), the int32 block products, or the
+// fused SiLU*up + quantise epilogue of a gate|up weight (BN = 128 only).
+constexpr int kModePlain = 0;
+constexpr int kModeProducts = 1;
+constexpr int kModeSilu = 2;
+constexpr int kBarSilu = kBarReady + kSlots;  // all epilogue warps, fused SiLU*up
+static_assert(kBarSilu < 16, "the hardware has 16 named barriers");
 
 struct Ctl {
   uint64_t full[kStages];
@@ -263,13 +273,15 @@ __device__ __forceinline__ void store_products(int32_t* products, int64_t m, int
 constexpr int kBarSlotThreads = 32 * (kEpiWarps + 1);
 constexpr int kBarIssuedThreads = 64;
 
-template <int BN, bool kProducts>
+template <int BN, int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_s8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ GemmArgs args) {
   using T = Tile<BN>;
   constexpr int G = T::kG;
+  constexpr bool kProducts = kMode == kModeProducts;
+  static_assert(kMode != kModeSilu || BN == 128, "the fused SiLU*up epilogue needs BN = 128");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -491,7 +503,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if constexpr (!kProducts) {
+      if constexpr (kMode == kModeSilu) {
+        fold_half<BN, 1>(f, r_hi, sc_prev, nv_prev);  // last slot, half 1
+        // Fused SiLU*up (silu_mul_quantize_f32, ops_cpu.cpp:144-198, on the
+        // gate|up outputs).  Column group c of the tile is gate block (c even)
+        // or up block (c odd) J = n0/64 + c/2 of the interleaved weight.  Each
+        // warp forms its outputs o = f * wscale exactly as the plain GEMM
+        // writes them; the up warp stages o, and the gate warp with the same
+        // rows (warp + 4) forms v = silu(g) * u for its 32 columns -- one
+        // whole quantisation block of the row -- and quantises it.
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) o[j] = __fmul_rn(f[j], __shfl_sync(0xffffffffu, ws_pre, j));
+        if (cgroup & 1) {
+#pragma unroll
+          for (int j = 0; j < E; ++j) stg[lane * T::kStgStride + j] = o[j];
+        }
+        named_sync(kBarSilu, 32 * kEpiWarps);
+        if (!(cgroup & 1) && nc < N && row_ok) {
+          const float* ustg = stg + 4 * (32 * T::kStgStride);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = silu_up_vec(o[j], ustg[lane * T::kStgStride + j]);
+          const int64_t J = n0 / 64 + cgroup / 2;
+          const int64_t esz = args.silu_mode == 2 ? 2 : 1;
+          bool bad = false;
+          const float sc = quant_block32(v, args.silu_out + (m * args.silu_kp + J * 32) * esz,
+                                         args.silu_mode, &bad);
+          args.silu_asc[m * (args.silu_kp / 32) + J] = sc;
+          if (bad) atomicOr(&g_status, kErrF16Range);
+        }
+        named_sync(kBarSilu, 32 * kEpiWarps);  // staging free for the next tile
+      } else if constexpr (!kProducts) {
         fold_half<BN, 1>(f, r_hi, sc_prev, nv_prev);  // last slot, half 1
         // Stage the warp's 32 x E block in shared memory, then write it out
         // row-wise: each store instruction covers 32 / E rows of E
@@ -553,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool kProducts>
+template <int BN, int kMode>
 cudaError_t launch_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
                         const GemmArgs& args, cudaStream_t s) {
   using T = Tile<BN>;
@@ -561,7 +604,7 @@ cudaError_t launch_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_s8_tc_kernel<BN, kProducts>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_s8_tc_kernel<BN, kMode>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(T::kSmemBytes));
     if (e != cudaSuccess) return e;
@@ -569,17 +612,17 @@ cudaError_t launch_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  gemm_s8_tc_kernel<BN, kProducts><<<grid, kThreads, T::kSmemBytes, s>>>(tmap_a, tmap_b, args);
+  gemm_s8_tc_kernel<BN, kMode><<<grid, kThreads, T::kSmemBytes, s>>>(tmap_a, tmap_b, args);
   return cudaGetLastError();
 }
 
-template <bool kProducts>
+template <int kMode>
 cudaError_t launch_width(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
                          const GemmArgs& args, cudaStream_t s) {
   switch (tile) {
-    case 0: return launch_impl<128, kProducts>(tmap_a, tmap_b, args, s);
-    case 1: return launch_impl<64, kProducts>(tmap_a, tmap_b, args, s);
-    case 2: return launch_impl<32, kProducts>(tmap_a, tmap_b, args, s);
+    case 0: return launch_impl<128, kMode>(tmap_a, tmap_b, args, s);
+    case 1: return launch_impl<64, kMode>(tmap_a, tmap_b, args, s);
+    case 2: return launch_impl<32, kMode>(tmap_a, tmap_b, args, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -615,8 +658,12 @@ int pick_tile(int64_t M, int64_t N, int device) {
 
 cudaError_t launch_gemm(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
                         const GemmArgs& args, cudaStream_t s) {
-  if (args.products) return launch_width<true>(tile, tmap_a, tmap_b, args, s);
-  return launch_width<false>(tile, tmap_a, tmap_b, args, s);
+  if (args.silu_out) {
+    if (tile != 0) return cudaErrorInvalidValue;  // the fused epilogue is built for BN = 128
+    return launch_impl<128, kModeSilu>(tmap_a, tmap_b, args, s);
+  }
+  if (args.products) return launch_width<kModeProducts>(tile, tmap_a, tmap_b, args, s);
+  return launch_width<kModePlain>(tile, tmap_a, tmap_b, args, s);
 }
 
 cudaError_t read_and_clear_status(int* out, cudaStream_t s) {

@@ -26,6 +26,10 @@ struct ovb_weight {
   uint16_t* w16 = nullptr;
   CUtensorMap tmap_w16[4];
   bool tmap16_ready[4] = {false, false, false, false};
+  // Gate|up weight for the fused SiLU*up epilogue (ovb_weight_gate_up): rows
+  // are gate and up interleaved in 32-row blocks (gate 32j.., up 32j.., ...);
+  // glu_inter = N / 2 is the intermediate width.  0 for other weights.
+  int64_t glu_inter = 0;
 };
 
 namespace ovb {
@@ -57,6 +61,14 @@ struct GemmArgs {
   int n_slices;
   SliceOut slices[kMaxSlices];
   int32_t* products;    // when non-null: write P[m, n, b] instead of C
+  // Fused SiLU*up epilogue (gate|up weights): when silu_out is non-null the
+  // kernel writes quantise(silu(gate) * up) instead of C -- form silu_mode
+  // (0 int8 q, 1 u8, 2 fp16 q*asc) into silu_out [M, silu_kp] and the block
+  // scales into silu_asc [M, silu_kp / 32].
+  uint8_t* silu_out;
+  float* silu_asc;
+  int silu_mode;
+  int64_t silu_kp;
 };
 
 // Thread-local error message (ovb_last_error).
@@ -101,7 +113,8 @@ cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorM
                             const GemmArgs& args, cudaStream_t s);
 cudaError_t read_and_clear_status_f16(int* out, cudaStream_t s);
 // The plain fp16 mainloop: A is fp16 [M, Kp] (dequantised activations).
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device);
+// n_widths: consider the first n entries of kTileNF (3 = BN >= 64).
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_widths = 4);
 cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s);
 

@@ -18,6 +18,7 @@
 #include <climits>
 
 #include "ovb_internal.h"
+#include "ovb_quant.cuh"
 
 namespace ovb {
 
@@ -33,39 +34,6 @@ constexpr int kErrF16Range = 16;
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
-
-// _mm256_cvtps_epi32 under the default MXCSR: round to nearest even, and
-// 0x80000000 ("integer indefinite") for NaN or values outside int32.
-__device__ __forceinline__ int cvt_rne_x86(float v) {
-  if (!(v == v) || v >= 2147483648.0f || v < -2147483648.0f) return INT_MIN;
-  return __float2int_rn(v);
-}
-
-__device__ __forceinline__ uint32_t quant_byte(float v, float inv, bool u8) {
-  int z = cvt_rne_x86(__fmul_rn(v, inv));
-  z = z < -127 ? -127 : (z > 127 ? 127 : z);
-  return u8 ? static_cast<uint32_t>(z + 128) : static_cast<uint32_t>(z & 0xFF);
-}
-
-// Block scale and its reciprocal exactly as gemm.cpp:407-408.
-__device__ __forceinline__ void block_scales(float amax, float* scale, float* inv) {
-  *scale = __fdiv_rn(amax, 127.0f);
-  *inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-}
-
-// Quantise 8 consecutive values (the first `nv` valid, the rest padding -> 0).
-__device__ __forceinline__ uint2 quant8(const float (&v)[8], int nv, float inv, bool u8) {
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t b = (i < nv) ? quant_byte(v[i], inv, u8) : 0u;
-    if (i < 4)
-      lo |= b << (8 * i);
-    else
-      hi |= b << (8 * (i - 4));
-  }
-  return make_uint2(lo, hi);
-}
 
 // fp16(q * scale) of 8 consecutive values (padding -> 0), packed in 16 bytes.
 __device__ __forceinline__ uint4 dequant8_f16(const float (&v)[8], int nv, float inv,
@@ -91,6 +59,40 @@ __device__ __forceinline__ uint4 dequant8_f16(const float (&v)[8], int nv, float
   }
   if (!range_ok) atomicOr(&g_status_q, kErrF16Range);
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The same for 4 consecutive values (4 bytes of q, or 8 bytes of fp16).
+__device__ __forceinline__ void store4(uint8_t* aq, int64_t idx, const float (&v)[4], int nv,
+                                       float inv, float scale, int mode) {
+  if (mode == kModeF16) {
+    uint32_t w[2];
+    bool range_ok = true;
+#pragma unroll
+    for (int i = 0; i < 4; i += 2) {
+      float d[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        if (i + j < nv) {
+          int z = cvt_rne_x86(__fmul_rn(v[i + j], inv));
+          z = z < -127 ? -127 : (z > 127 ? 127 : z);
+          d[j] = __fmul_rn(static_cast<float>(z), scale);
+          range_ok = range_ok && fabsf(d[j]) <= 65504.f;
+        } else {
+          d[j] = 0.f;
+        }
+      }
+      const __half2 h = __floats2half2_rn(d[0], d[1]);
+      w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    if (!range_ok) atomicOr(&g_status_q, kErrF16Range);
+    *reinterpret_cast<uint2*>(aq + 2 * idx) = make_uint2(w[0], w[1]);
+  } else {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      word |= ((i < nv) ? quant_byte(v[i], inv, mode == kModeU8) : 0u) << (8 * i);
+    *reinterpret_cast<uint32_t*>(aq + idx) = word;
+  }
 }
 
 // Write the 8 quantised values of element k of a row in the chosen form.
@@ -151,13 +153,54 @@ __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, con
   }
 }
 
+// Copy n floats from global src to shared dst with `threads` threads (this
+// one is `tid`): 16-byte loads when aligned, eight loads in flight per thread
+// before their stores.
+__device__ __forceinline__ void stage_row(const float* __restrict__ src, int64_t n, float* dst,
+                                          int tid, int threads) {
+  const bool vec = ((n & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  if (vec) {
+    const int64_t n4 = n / 4;
+    for (int64_t i0 = tid; i0 < n4; i0 += 8 * static_cast<int64_t>(threads)) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + u * static_cast<int64_t>(threads);
+        v[u] = i < n4 ? __ldg(reinterpret_cast<const float4*>(src) + i) : make_float4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + u * static_cast<int64_t>(threads);
+        if (i < n4) reinterpret_cast<float4*>(dst)[i] = v[u];
+      }
+    }
+  } else {
+    for (int64_t i0 = tid; i0 < n; i0 += 8 * static_cast<int64_t>(threads)) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + u * static_cast<int64_t>(threads);
+        v[u] = i < n ? __ldg(src + i) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + u * static_cast<int64_t>(threads);
+        if (i < n) dst[i] = v[u];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------- rmsnorm + quantize
 // One warp per row.  The row is staged in shared memory with coalesced
 // float4 loads; lanes 0..7 then run the reference's eight sequential FMA
 // chains (lane l: elements l, l+8, ...; gemm.cpp:655-658), every lane sums
 // the eight partials left to right plus the cols%8 tail (:661-663) and forms
-// scale = 1/sqrt(sum/cols + eps) (:664).  Each lane then quantises whole
-// 32-k blocks b = lane, lane+32, ... of (x*scale)*w (:672-704).
+// scale = 1/sqrt(sum/cols + eps) (:664).  The warp then quantises
+// (x*scale)*w (:672-704) four 32-k blocks at a time: eight lanes per block,
+// four consecutive elements per lane (one 16-byte shared-memory and gain
+// load each), the block absmax reduced over the eight lanes with shuffles
+// (max is order-independent, so this equals the reference's).
 __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int64_t cols,
                                                                const float* x, const float* w,
                                                                float eps, uint8_t* aq,
@@ -166,21 +209,21 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   float* srow = srow_all + static_cast<int64_t>(warp) * cols;
+  // The gain vector, staged once per block (after the rows' slots).  Loads
+  // are issued in batches of 8 before their stores so their latencies overlap.
+  float* sw = srow_all + static_cast<int64_t>(warps) * cols;
+  stage_row(w, cols, sw, threadIdx.x, blockDim.x);
+  __syncthreads();
   const int64_t Kb = (cols + 31) / 32, Kp = Kb * 32;
   const bool vec_ok = ((cols & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * warps + warp; r < rows;
        r += static_cast<int64_t>(gridDim.x) * warps) {
-    const float* row = x + r * cols;
-    if (vec_ok) {
-      for (int64_t i = lane * 4; i < cols; i += 128)
-        *reinterpret_cast<float4*>(srow + i) = __ldg(reinterpret_cast<const float4*>(row + i));
-    } else {
-      for (int64_t i = lane; i < cols; i += 32) srow[i] = __ldg(row + i);
-    }
+    stage_row(x + r * cols, cols, srow, lane, 32);
     __syncwarp();
     const int64_t nvec = cols / 8;
     float acc = 0.f;
     if (lane < 8)
+#pragma unroll 8
       for (int64_t j = 0; j < nvec; ++j) {
         const float v = srow[j * 8 + lane];
         acc = __fmaf_rn(v, v, acc);
@@ -191,26 +234,40 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
     for (int64_t i = nvec * 8; i < cols; ++i) sum = __fadd_rn(sum, __fmul_rn(srow[i], srow[i]));
     const float scale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
-    for (int64_t b = lane; b < Kb; b += 32) {
-      const int64_t k0 = b * 32;
-      const int kn = static_cast<int>(imin64(32, cols - k0));
-      float v[32];
+    const int sub = lane & 7;  // this lane's quarter-of-a-quarter of the block
+#pragma unroll 2
+    for (int64_t b0 = 0; b0 < Kb; b0 += 4) {
+      const int64_t b = b0 + (lane >> 3);
+      const int64_t k = b * 32 + sub * 4;
+      const int nv = b < Kb ? static_cast<int>(imax64(0, imin64(4, cols - k))) : 0;
+      float xv[4], wv[4];
+      if (nv == 4 && vec_ok) {
+        const float4 a = *reinterpret_cast<const float4*>(srow + k);
+        const float4 c = *reinterpret_cast<const float4*>(sw + k);
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+        wv[0] = c.x; wv[1] = c.y; wv[2] = c.z; wv[3] = c.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xv[i] = i < nv ? srow[k + i] : 0.f;
+          wv[i] = i < nv ? sw[k + i] : 0.f;
+        }
+      }
+      float v[4];
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        v[i] = (i < kn) ? __fmul_rn(__fmul_rn(srow[k0 + i], scale), __ldg(w + k0 + i)) : 0.f;
+      for (int i = 0; i < 4; ++i) {
+        v[i] = (i < nv) ? __fmul_rn(__fmul_rn(xv[i], scale), wv[i]) : 0.f;
         amax = fmaxf(amax, fabsf(v[i]));
       }
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
       float bs, inv;
       block_scales(amax, &bs, &inv);
-      asc[r * Kb + b] = bs;
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        float v8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v8[i] = v[g * 8 + i];
-        const int nv = max(0, min(8, kn - g * 8));
-        store8(aq, r * Kp + k0 + g * 8, v8, nv, inv, bs, mode);
+      if (b < Kb) {
+        if (sub == 0) asc[r * Kb + b] = bs;
+        store4(aq, r * Kp + k, v, nv, inv, bs, mode);
       }
     }
     __syncwarp();
@@ -218,42 +275,6 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
 }
 
 // ------------------------------------------------- silu(gate)*up + quantize
-// exp256_ps (ops_cpu.cpp:75-92) for one lane, operation for operation:
-// clamp to [-87, 88], n = rne(x*log2e), r = x - n*ln2 (product, then
-// difference), degree-6 Horner with fused multiply-adds, times 2^n built in
-// the exponent field.
-__device__ __forceinline__ float exp_ref(float x) {
-  x = (x < 88.0f) ? x : 88.0f;
-  x = (x > -87.0f) ? x : -87.0f;
-  const float n = rintf(__fmul_rn(x, 1.4426950408889634f));
-  const float r = __fsub_rn(x, __fmul_rn(n, 0.6931471805599453f));
-  float p = 1.0f / 720;
-  p = __fmaf_rn(p, r, 1.0f / 120);
-  p = __fmaf_rn(p, r, 1.0f / 24);
-  p = __fmaf_rn(p, r, 1.0f / 6);
-  p = __fmaf_rn(p, r, 0.5f);
-  p = __fmaf_rn(p, r, 1.0f);
-  p = __fmaf_rn(p, r, 1.0f);
-  const int ni = __float2int_rn(n);
-  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
-}
-
-// silu_up8 (ops_cpu.cpp:138-142): (g / (1 + exp(0 - g))) * u.
-__device__ __forceinline__ float silu_up_vec(float g, float u) {
-  const float d = __fadd_rn(1.0f, exp_ref(__fsub_rn(0.0f, g)));
-  return __fmul_rn(__fdiv_rn(g, d), u);
-}
-
-// The scalar tail of a block (kn % 8 trailing elements, ops_cpu.cpp:166)
-// uses silu() with the C library's expf.  A correctly rounded exp is formed
-// here from the double-precision exp, which agrees with the host expf except
-// in the rare cases where the host's result is not correctly rounded.
-__device__ __forceinline__ float silu_up_tail(float g, float u) {
-  const float e = static_cast<float>(exp(static_cast<double>(-g)));
-  const float d = __fadd_rn(1.0f, e);
-  return __fmul_rn(__fdiv_rn(g, d), u);
-}
-
 __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
                                                                 const float* gate, int64_t ldg,
                                                                 const float* up, int64_t ldu,
@@ -317,10 +338,14 @@ cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, v
 
 cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
                                     float eps, void* aq, float* asc, int mode, cudaStream_t s) {
-  // One warp per row; shared memory holds one row per warp.
+  // One warp per row; shared memory holds one row per warp.  Fewer warps per
+  // block when there are few rows, so that the rows spread over all SMs.
   const int64_t row_bytes = cols * 4;
-  int warps = static_cast<int>(imin64(8, imax64(1, (96 * 1024) / row_bytes)));
-  const size_t smem = static_cast<size_t>(warps) * row_bytes;
+  int dev0 = 0;
+  cudaGetDevice(&dev0);
+  const int64_t per_block = imax64(1, rows / (2 * static_cast<int64_t>(num_sms(dev0))));
+  int warps = static_cast<int>(imin64(imin64(8, per_block), imax64(1, (96 * 1024) / row_bytes)));
+  const size_t smem = static_cast<size_t>(warps + 1) * row_bytes;  // rows + the gain vector
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -126,6 +126,16 @@ class Weight:
                                           C.byref(out)))
         return cls(out.value, sum(p.N for p in parts), parts[0].K, all(p.f16 for p in parts))
 
+    @classmethod
+    def gate_up(cls, gate: "Weight", up: "Weight") -> "Weight":
+        """gate|up interleaved in 32-row blocks for the fused SiLU*up GEMMs
+        (ovb_weight_gate_up)."""
+        out = C.c_void_p()
+        L.check(L.lib().ovb_weight_gate_up(gate.handle, up.handle, _stream(), C.byref(out)))
+        w = cls(out.value, 2 * gate.N, gate.K, gate.f16 and up.f16)
+        w.glu = True
+        return w
+
     def export(self):
         """The device weight as ([N, K] int8, [N] fp32) numpy arrays."""
         W = np.zeros((self.N, self.K), np.int8)
@@ -263,6 +273,36 @@ def linear_h_sliced(a16: torch.Tensor, w: Weight, Cs: list[torch.Tensor]):
     L.check(L.lib().ovb_linear_h_sliced(a16.shape[0], w.handle, _dev_ptr(a16), arr, len(Cs),
                                         _stream()))
     return Cs
+
+
+def _silu_out(M, w: Weight, device, u8, f16, out):
+    if out is not None:
+        return out
+    inter = w.N // 2
+    if f16:
+        return empty_quant_f16(M, inter, device)
+    aq, asc = empty_quant(M, inter, device)
+    return (aq.view(torch.uint8) if u8 else aq), asc
+
+
+def linear_q_silu(aq: torch.Tensor, asc: torch.Tensor, w: Weight, out=None, u8: bool = False,
+                  f16: bool = False):
+    """gate|up GEMM fused with silu_mul_quantize_f32 on the int8 mainloop
+    (bit-identical to the two reference calls).  Returns (q or fp16, scales)."""
+    M = aq.shape[0]
+    q, sc = _silu_out(M, w, aq.device, u8, f16, out)
+    L.check(L.lib().ovb_linear_q_silu(M, w.handle, _dev_ptr(aq), _dev_ptr(asc), _dev_ptr(q),
+                                      _dev_ptr(sc), _flags(u8, f16), _stream()))
+    return q, sc
+
+
+def linear_h_silu(a16: torch.Tensor, w: Weight, out=None, u8: bool = False, f16: bool = True):
+    """The same on the fp16 mainloop (a16 = fp16(q*asc) activations)."""
+    M = a16.shape[0]
+    q, sc = _silu_out(M, w, a16.device, u8, f16, out)
+    L.check(L.lib().ovb_linear_h_silu(M, w.handle, _dev_ptr(a16), _dev_ptr(q), _dev_ptr(sc),
+                                      _flags(u8, f16), _stream()))
+    return q, sc
 
 
 def workspace_bytes(M: int, K: int) -> int:

@@ -66,12 +66,17 @@ class LayerWeights:
     post_ln: torch.Tensor
 
     @classmethod
-    def from_host(cls, w: dict, device, f16: bool = False) -> "LayerWeights":
+    def from_host(cls, w: dict, device, f16: bool = False, fused: bool = True) -> "LayerWeights":
         """``f16`` selects the fp16 tensor-core mainloop (OVB_WEIGHT_F16) for
-        all four GEMMs; otherwise they reproduce the reference bit for bit."""
+        all four GEMMs; otherwise they reproduce the reference bit for bit.
+        ``fused`` builds gate|up for the fused SiLU*up GEMM (run); otherwise a
+        plain concatenation (run_unfused)."""
         parts = {name: G.Weight.from_nk(*w[name], f16=f16) for name, _, _ in SHAPES}
         qkv = G.Weight.concat([parts["q"], parts["k"], parts["v"]])
-        gu = G.Weight.concat([parts["gate"], parts["up"]])
+        if fused:
+            gu = G.Weight.gate_up(parts["gate"], parts["up"])
+        else:
+            gu = G.Weight.concat([parts["gate"], parts["up"]])
         for name in ("q", "k", "v", "gate", "up"):
             parts[name].close()
         return cls(qkv=qkv, o=parts["o"], gate_up=gu, down=parts["down"],
@@ -115,8 +120,7 @@ def run(x: torch.Tensor, lw: LayerWeights, buf: LayerBuffers, attn: torch.Tensor
         G.s8_nk_quantize(a, out=buf.qo, f16=True)
         G.linear_h(buf.qo[0], lw.o, x, accumulate=True)
         G.rmsnorm_quantize_f32(x, lw.post_ln, RMS_EPS, out=buf.qh, f16=True)
-        G.linear_h_sliced(buf.qh[0], lw.gate_up, [buf.gate, buf.up])
-        G.silu_mul_quantize_f32(buf.gate, buf.up, out=buf.qi, f16=True)
+        G.linear_h_silu(buf.qh[0], lw.gate_up, out=buf.qi, f16=True)  # gate|up + SiLU*up quant
         G.linear_h(buf.qi[0], lw.down, x, accumulate=True)
         return x
     G.rmsnorm_quantize_f32(x, lw.input_ln, RMS_EPS, out=buf.qh)
@@ -124,10 +128,38 @@ def run(x: torch.Tensor, lw: LayerWeights, buf: LayerBuffers, attn: torch.Tensor
     G.s8_nk_quantize(a, out=buf.qo)
     G.linear_s8_nk_packed_q_add(*buf.qo, lw.o, x)
     G.rmsnorm_quantize_f32(x, lw.post_ln, RMS_EPS, out=buf.qh)
-    G.linear_s8_nk_packed_q_sliced(*buf.qh, lw.gate_up, [buf.gate, buf.up])
-    G.silu_mul_quantize_f32(buf.gate, buf.up, out=buf.qi)
+    G.linear_q_silu(*buf.qh, lw.gate_up, out=buf.qi)  # gate|up + SiLU*up quant, bit-exact
     G.linear_s8_nk_packed_q_add(*buf.qi, lw.down, x)
     return x
 
 
-KERNELS_PER_LAYER = 8  # 4 quantisers + 4 GEMMs
+def run_unfused(x: torch.Tensor, lw_cat, buf: LayerBuffers, attn: torch.Tensor | None = None):
+    """The same layer with the reference's separate gate|up GEMM and
+    silu_mul_quantize call (lw_cat.gate_up a plain concatenation): used by the
+    tests to check the fused epilogue against the unfused sequence."""
+    a = buf.q if attn is None else attn
+    kw = dict(f16=True) if buf.f16 else {}
+    G.rmsnorm_quantize_f32(x, lw_cat.input_ln, RMS_EPS, out=buf.qh, **kw)
+    if buf.f16:
+        G.linear_h_sliced(buf.qh[0], lw_cat.qkv, [buf.q, buf.k, buf.v])
+    else:
+        G.linear_s8_nk_packed_q_sliced(*buf.qh, lw_cat.qkv, [buf.q, buf.k, buf.v])
+    G.s8_nk_quantize(a, out=buf.qo, **kw)
+    if buf.f16:
+        G.linear_h(buf.qo[0], lw_cat.o, x, accumulate=True)
+    else:
+        G.linear_s8_nk_packed_q_add(*buf.qo, lw_cat.o, x)
+    G.rmsnorm_quantize_f32(x, lw_cat.post_ln, RMS_EPS, out=buf.qh, **kw)
+    if buf.f16:
+        G.linear_h_sliced(buf.qh[0], lw_cat.gate_up, [buf.gate, buf.up])
+    else:
+        G.linear_s8_nk_packed_q_sliced(*buf.qh, lw_cat.gate_up, [buf.gate, buf.up])
+    G.silu_mul_quantize_f32(buf.gate, buf.up, out=buf.qi, **kw)
+    if buf.f16:
+        G.linear_h(buf.qi[0], lw_cat.down, x, accumulate=True)
+    else:
+        G.linear_s8_nk_packed_q_add(*buf.qi, lw_cat.down, x)
+    return x
+
+
+KERNELS_PER_LAYER = 7  # 3 quantisers + 4 GEMMs (gate|up fused with SiLU*up quantise)
