@@ -12,6 +12,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -50,6 +51,14 @@ bool cuda_failed(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return false;
   set_error(std::string(what) + ": " + cudaGetErrorString(e));
   return true;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("OVB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int num_sms(int device) {

@@ -387,6 +387,8 @@ __global__ void __launch_bounds__(kThreadsF, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  pdl_wait();  // the preceding kernel's outputs (A, residual C) are complete
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 //      (bar.sync on both sides, so the MMA thread never waits on an
 //      mbarrier while it has MMAs in flight);
 //   3..10 epilogue (epilogue_loop), accumulators double-buffered in TMEM.
-constexpr int kStagesH = 4;
+constexpr int kMaxStagesH = 8;
 constexpr int kFirstEpiH = 3;
 // Epilogue warps: 8 for plain outputs (each stages 32x32 chunks in shared
 // memory); 16 for the fused SiLU*up epilogue, which is arithmetic-heavy and
@@ -566,8 +568,8 @@ constexpr int kBarFullH = 1;
 constexpr int kBarDfreeH = 2;  // + d
 
 struct CtlH {
-  uint64_t full[kStagesH];
-  uint64_t empty[kStagesH];
+  uint64_t full[kMaxStagesH];
+  uint64_t empty[kMaxStagesH];
   uint64_t tfull[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -582,8 +584,14 @@ struct TileH {
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
   static constexpr size_t kStgAll = kSilu ? 0 : static_cast<size_t>(kEpiW) * 32 * kStgStrideF * 4;
-  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStagesH) * kStageBytes +
+  // As many stages as fit (a deeper ring hides more TMA latency; narrow
+  // tiles have small stages), at most kMaxStagesH.
+  static constexpr int kStagesFit =
+      static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
+  static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes +
                                        kStgAll + sizeof(CtlH);
+  static_assert(kStages >= 3, "too few pipeline stages");
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -597,7 +605,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(kStagesH) * T::kStageBytes);
+  float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(T::kStages) * T::kStageBytes);
   CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
   volatile int* abort = &ctl->abort;
 
@@ -613,7 +621,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
       tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStagesH; ++s) {
+    for (int s = 0; s < T::kStages; ++s) {
       mbar_init(smem_u32(&ctl->full[s]), 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
     }
@@ -632,6 +640,8 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  pdl_wait();  // the preceding kernel's outputs (A, residual C) are complete
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -642,8 +652,8 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
         const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
         const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
         for (int j = 0; j < ksteps; ++j, ++st) {
-          const int s = static_cast<int>(st % kStagesH);
-          const uint32_t ph = static_cast<uint32_t>((st / kStagesH) & 1);
+          const int s = static_cast<int>(st % T::kStages);
+          const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
           if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
             atomicOr(&g_status_f16, kErrProducer);
             *abort = 1;
@@ -658,10 +668,10 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
         }
       }
       if (!ok) {
-        const int64_t first = st > kStagesH ? st - kStagesH : 0;
+        const int64_t first = st > T::kStages ? st - T::kStages : 0;
         for (int64_t j = first; j < st; ++j) {
           volatile int never = 0;
-          ovb_wait(smem_u32(&ctl->full[j % kStagesH]), static_cast<uint32_t>((j / kStagesH) & 1),
+          ovb_wait(smem_u32(&ctl->full[j % T::kStages]), static_cast<uint32_t>((j / T::kStages) & 1),
                    &never);
         }
       }
@@ -675,7 +685,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
       if (t >= T::kAcc) named_sync(kBarDfreeH + d, 32 * (T::kEpiW + 1));  // accumulator d read
       const uint32_t dcol = tmem_base + static_cast<uint32_t>(d * BN);
       for (int j = 0; j < ksteps; ++j, ++st) {
-        const int s = static_cast<int>(st % kStagesH);
+        const int s = static_cast<int>(st % T::kStages);
         named_sync(kBarFullH, 64);  // stage s has landed
         if (lane == 0) {
           tc_fence_after();
@@ -704,8 +714,8 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
     int64_t st = 0;
     for (int64_t t = 0; t < my_tiles; ++t) {
       for (int j = 0; j < ksteps; ++j, ++st) {
-        const int s = static_cast<int>(st % kStagesH);
-        const uint32_t ph = static_cast<uint32_t>((st / kStagesH) & 1);
+        const int s = static_cast<int>(st % T::kStages);
+        const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
         const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
         if (!__all_sync(0xffffffffu, got) && lane == 0) {
           atomicOr(&g_status_f16, kErrConvert);
@@ -751,8 +761,8 @@ cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  gemm_h_kernel<BN, kSilu><<<grid, T::kThreads, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
-  return cudaGetLastError();
+  return launch_pdl(gemm_h_kernel<BN, kSilu>, dim3(grid), dim3(T::kThreads), T::kSmemBytes, s,
+                    tmap_a, tmap_w, args);
 }
 
 template <int BN>
@@ -771,8 +781,8 @@ cudaError_t launch_f16_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  gemm_f16_kernel<BN><<<grid, kThreadsF, T::kSmemBytes, s>>>(tmap_a, tmap_w, args);
-  return cudaGetLastError();
+  return launch_pdl(gemm_f16_kernel<BN>, dim3(grid), dim3(kThreadsF), T::kSmemBytes, s, tmap_a,
+                    tmap_w, args);
 }
 
 }  // namespace

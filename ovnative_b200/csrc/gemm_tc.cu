@@ -324,6 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  pdl_wait();  // the preceding kernel's outputs (aq, asc, residual C) are complete
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -612,8 +614,8 @@ cudaError_t launch_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  gemm_s8_tc_kernel<BN, kMode><<<grid, kThreads, T::kSmemBytes, s>>>(tmap_a, tmap_b, args);
-  return cudaGetLastError();
+  return launch_pdl(gemm_s8_tc_kernel<BN, kMode>, dim3(grid), dim3(kThreads), T::kSmemBytes, s,
+                    tmap_a, tmap_b, args);
 }
 
 template <int kMode>

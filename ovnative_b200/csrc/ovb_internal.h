@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 
 struct ovb_weight {
   int device = 0;
@@ -33,6 +34,27 @@ struct ovb_weight {
 };
 
 namespace ovb {
+
+// Launch `kernel` on stream s with programmatic dependent launch (the kernel
+// itself orders its memory accesses after the preceding grid with
+// griddepcontrol.wait), unless the environment sets OVB_PDL=0.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Rows / columns per GEMM output tile; bytes of K per TMA box (four 32-k
 // quantisation blocks, one 128-byte swizzle row).

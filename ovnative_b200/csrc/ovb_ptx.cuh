@@ -18,6 +18,19 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ------------------------------------------------ programmatic launch
+// Kernels are launched with programmatic stream serialisation (launch_pdl):
+// the next kernel in the stream may start before this one ends.  Every
+// kernel calls pdl_wait() before its first global-memory access (it returns
+// once the preceding grid has completed and its writes are visible) and then
+// pdl_launch_dependents(), which lets the next grid launch once every CTA of
+// this one has started.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

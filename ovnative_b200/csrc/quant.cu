@@ -18,6 +18,7 @@
 #include <climits>
 
 #include "ovb_internal.h"
+#include "ovb_ptx.cuh"
 #include "ovb_quant.cuh"
 
 namespace ovb {
@@ -124,6 +125,8 @@ __device__ __forceinline__ void load8(const float* p, int nv, bool vec_ok, float
 __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, const float* A,
                                                        int64_t lda, uint8_t* aq, float* asc,
                                                        int mode) {
+  pdl_wait();  // the producer of this kernel's input is complete
+  pdl_launch_dependents();
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
   const int64_t total = M * Kb * 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -205,6 +208,8 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
                                                                const float* x, const float* w,
                                                                float eps, uint8_t* aq,
                                                                float* asc, int mode) {
+  pdl_wait();  // the producer of this kernel's input is complete
+  pdl_launch_dependents();
   extern __shared__ float srow_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -274,12 +279,95 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
   }
 }
 
+// The same for rows of at most 1024 elements (cols % 4 == 0, 16-byte aligned
+// x and w) -- the LM's hidden size.  Lane l's quantisation positions are
+// k = 128*i + 4*l, i < 8, exactly the positions it loads when staging the
+// row, so the row and the gains stay in registers: the gains are loaded
+// once per warp together with its first row, and shared memory only feeds
+// the reference-ordered sum of squares.
+constexpr int kSmallIters = 8;  // 8 x 128 = 1024 elements per row
+
+__global__ void __launch_bounds__(256) rmsnorm_quantize_small_kernel(
+    int64_t rows, int64_t cols, const float* x, const float* w, float eps, uint8_t* aq,
+    float* asc, int mode) {
+  pdl_wait();  // the producer of this kernel's input is complete
+  pdl_launch_dependents();
+  extern __shared__ float srow_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  float* srow = srow_all + static_cast<int64_t>(warp) * cols;
+  const int64_t Kb = (cols + 31) / 32, Kp = Kb * 32;
+  float4 wr[kSmallIters];
+#pragma unroll
+  for (int i = 0; i < kSmallIters; ++i) {
+    const int64_t k = 128 * i + 4 * lane;
+    wr[i] = k < cols ? __ldg(reinterpret_cast<const float4*>(w + k)) : make_float4(0, 0, 0, 0);
+  }
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * warps + warp; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * warps) {
+    const float* row = x + r * cols;
+    float4 xr[kSmallIters];
+#pragma unroll
+    for (int i = 0; i < kSmallIters; ++i) {
+      const int64_t k = 128 * i + 4 * lane;
+      xr[i] = k < cols ? __ldg(reinterpret_cast<const float4*>(row + k)) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < kSmallIters; ++i) {
+      const int64_t k = 128 * i + 4 * lane;
+      if (k < cols) *reinterpret_cast<float4*>(srow + k) = xr[i];
+    }
+    __syncwarp();
+    const int64_t nvec = cols / 8;
+    float acc = 0.f;
+    if (lane < 8)
+#pragma unroll 8
+      for (int64_t j = 0; j < nvec; ++j) {
+        const float v = srow[j * 8 + lane];
+        acc = __fmaf_rn(v, v, acc);
+      }
+    float sum = __shfl_sync(0xffffffffu, acc, 0);
+#pragma unroll
+    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, l));
+    for (int64_t i = nvec * 8; i < cols; ++i) sum = __fadd_rn(sum, __fmul_rn(srow[i], srow[i]));
+    const float scale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+#pragma unroll
+    for (int i = 0; i < kSmallIters; ++i) {
+      const int64_t b = 4 * i + (lane >> 3);
+      const int64_t k = 128 * i + 4 * lane;
+      const int nv = k < cols ? 4 : 0;  // cols % 4 == 0
+      const float xv[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
+      const float wv[4] = {wr[i].x, wr[i].y, wr[i].z, wr[i].w};
+      float v[4];
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = (j < nv) ? __fmul_rn(__fmul_rn(xv[j], scale), wv[j]) : 0.f;
+        amax = fmaxf(amax, fabsf(v[j]));
+      }
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      float bs, inv;
+      block_scales(amax, &bs, &inv);
+      if (b < Kb) {
+        if ((lane & 7) == 0) asc[r * Kb + b] = bs;
+        store4(aq, r * Kp + k, v, nv, inv, bs, mode);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // ------------------------------------------------- silu(gate)*up + quantize
 __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
                                                                 const float* gate, int64_t ldg,
                                                                 const float* up, int64_t ldu,
                                                                 uint8_t* aq, float* asc,
                                                                 int mode) {
+  pdl_wait();  // the producer of this kernel's input is complete
+  pdl_launch_dependents();
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
   const int64_t total = M * Kb * 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -331,9 +419,8 @@ int grid_for(int64_t threads_needed) {
 cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
                             float* asc, int mode, cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
-  quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(M, K, A, lda,
-                                                       static_cast<uint8_t*>(aq), asc, mode);
-  return cudaGetLastError();
+  return launch_pdl(quantize_kernel, dim3(grid_for(M * Kb * 4)), dim3(256), 0, s, M, K, A, lda,
+                    static_cast<uint8_t*>(aq), asc, mode);
 }
 
 cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
@@ -357,18 +444,24 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
   }
   const int64_t blocks = (rows + warps - 1) / warps;
   const int grid = static_cast<int>(imin64(blocks, static_cast<int64_t>(num_sms(dev)) * 16));
-  rmsnorm_quantize_kernel<<<grid, warps * 32, smem, s>>>(rows, cols, x, w, eps,
-                                                         static_cast<uint8_t*>(aq), asc, mode);
-  return cudaGetLastError();
+  const bool small = cols <= 128 * kSmallIters && (cols & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  if (small) {
+    return launch_pdl(rmsnorm_quantize_small_kernel, dim3(grid), dim3(warps * 32),
+                      static_cast<size_t>(warps) * row_bytes, s, rows, cols, x, w, eps,
+                      static_cast<uint8_t*>(aq), asc, mode);
+  }
+  return launch_pdl(rmsnorm_quantize_kernel, dim3(grid), dim3(warps * 32), smem, s, rows, cols, x, w,
+                    eps, static_cast<uint8_t*>(aq), asc, mode);
 }
 
 cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
                                      const float* up, int64_t ldu, void* aq, float* asc, int mode,
                                      cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
-  silu_mul_quantize_kernel<<<grid_for(M * Kb * 4), 256, 0, s>>>(
-      M, K, gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, mode);
-  return cudaGetLastError();
+  return launch_pdl(silu_mul_quantize_kernel, dim3(grid_for(M * Kb * 4)), dim3(256), 0, s, M, K,
+                    gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, mode);
 }
 
 cudaError_t read_and_clear_status_q(int* out, cudaStream_t s) {

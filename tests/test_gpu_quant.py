@@ -66,7 +66,8 @@ def test_silu_mul_quantize_golden(cuda, golden, i):
     assert_same(host(asc), golden[f"silu{i}_asc"])
 
 
-@pytest.mark.parametrize("M,K", [(400, 1024), (400, 2048), (1400, 1024), (129, 3072), (1, 1)])
+@pytest.mark.parametrize("M,K", [(400, 1024), (400, 2048), (1400, 1024), (129, 3072), (1, 1),
+                                 (64, 1000), (7, 96), (3, 4), (5, 1020), (2, 1028)])
 def test_quantizers_lm_shapes_vs_port(cuda, M, K):
     rng = np.random.default_rng(M * 7 + K)
     A = (rng.standard_normal((M, K)) * 4).astype(np.float32)
