@@ -133,13 +133,15 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def load_traffic(f16: bool) -> float | None:
-    """DRAM bytes per launch of the dominant GEMM from the committed ncu summary."""
-    name = "gemm_h_gate_up_m400_traffic.json" if f16 else "gemm_gate_up_m400_traffic.json"
-    p = os.path.join(ROOT, "profiles", name)
+def load_traffic(gemm: str, f16: bool) -> float | None:
+    """DRAM bytes per launch of one of the step's GEMMs (ncu dram__bytes_read
+    + dram__bytes_write) from the committed summary, or None."""
+    p = os.path.join(ROOT, "profiles", "gemm_traffic_m400.json")
     if os.path.exists(p):
         with open(p) as f:
-            return float(json.load(f)["dram_bytes_per_launch"])
+            d = json.load(f)
+        v = d.get("fp16" if f16 else "exact", {}).get(gemm)
+        return float(v) if v is not None else None
     return None
 
 
@@ -153,28 +155,25 @@ NUMERICS = {
 }
 
 
-def gate_up_roofline(gemm_us: float, f16: bool) -> dict:
-    """Roofline of the gate|up GEMM (M=400, N=6144, K=1024) from its live
-    launch time.  Algorithmic bytes and ops are the path's own (s8 A + fp32
-    scales, int8 W, fp32 C); the bound is the slower of HBM and the tensor pipe
-    the kernel uses (dense bf16 for kind::f16; int8 taken as 2x bf16)."""
-    from ovnative_b200 import layer as LY
+def gemm_roofline(name: str, kernel: str, M: int, N: int, K: int, residual: bool,
+                  out_bytes: int, gemm_us: float, f16: bool) -> dict:
+    """Roofline of one GEMM of the step from its live launch time.
+    Algorithmic bytes: s8 A + fp32 block scales (1.125*M*K), int8 W (N*K),
+    fp32 wscale (4N), the output (`out_bytes`) and the residual read
+    (4*M*N when accumulating).  The bound is the slower of HBM and the
+    tensor pipe the kernel uses (dense bf16 for kind::f16; int8 = 2x bf16)."""
     peaks = load_peaks()
-    N_gu, K_gu = 2 * LY.INTER, LY.HIDDEN
-    Kb = K_gu // 32
-    alg_bytes = (M_TOKENS * K_gu + M_TOKENS * Kb * 4 + N_gu * K_gu + N_gu * 4
-                 + M_TOKENS * N_gu * 4)
-    gemm_ops = 2 * M_TOKENS * N_gu * K_gu
+    alg_bytes = int(1.125 * M * K) + N * K + 4 * N + out_bytes + (4 * M * N if residual else 0)
+    ops = 2 * M * N * K
     tensor_peak = peaks["bf16_tflops"] * (1 if f16 else 2)
     t_hbm = alg_bytes / (peaks["hbm_gbs"] * 1e9)
-    t_tensor = gemm_ops / (tensor_peak * 1e12)
+    t_tensor = ops / (tensor_peak * 1e12)
     if t_tensor >= t_hbm:
-        achieved, peak, unit = gemm_ops / (gemm_us * 1e-6) / 1e12, tensor_peak, "TFLOP/s"
+        achieved, peak, unit = ops / (gemm_us * 1e-6) / 1e12, tensor_peak, "TFLOP/s"
     else:
         achieved, peak, unit = alg_bytes / (gemm_us * 1e-6) / 1e9, peaks["hbm_gbs"], "GB/s"
     return {
-        "kernel": ("gemm_h (fp16 mainloop" if f16 else "gemm_s8_tc (int8 mainloop")
-                  + ", gate|up sliced, M=400, N=6144, K=1024)",
+        "kernel": f"{kernel} ({name}, M={M}, N={N}, K={K})",
         "bound": "tensor" if t_tensor >= t_hbm else "hbm",
         "achieved": round(achieved, 1),
         "peak": peak,
@@ -182,10 +181,10 @@ def gate_up_roofline(gemm_us: float, f16: bool) -> dict:
         "frac": round(achieved / peak, 4),
         "peak_source": peaks["source"] + (" bf16 burst" if f16 else " 2x bf16 burst / hbm copy"),
         "algorithmic_bytes": alg_bytes,
-        "algorithmic_ops": gemm_ops,
+        "algorithmic_ops": ops,
         "us_per_launch": round(gemm_us, 3),
         "roofline_us": round(max(t_hbm, t_tensor) * 1e6, 3),
-        "traffic": load_traffic(f16),
+        "traffic": load_traffic(name, f16),
     }
 
 
@@ -290,30 +289,56 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     ms_max = max_over_ranks(ev0.elapsed_time(ev1))
     value = world * args.steps * ops_step / (ms_max * 1e-3) / 1e12
 
-    # ---- dominant kernel, timed live: the gate|up sliced GEMM (N=6144, K=1024),
-    # launches captured in a CUDA graph so host launch cost is not timed,
-    # weights rotating over the 28 layers (L2-cold).
-    n_launch = 4 * N_LAYERS
-    k0 = torch.cuda.Event(enable_timing=True)
-    k1 = torch.cuda.Event(enable_timing=True)
+    # ---- the step's four GEMMs, each timed live: launches captured in a CUDA
+    # graph so host launch cost is not timed, weights rotating over the 28
+    # layers (L2-cold).  `roofline` is the one with the largest share.
+    H, QKV, INTER = LY.HIDDEN, LY.QD + 2 * LY.KVD, LY.INTER
+    kern = "gemm_h (fp16 mainloop)" if f16 else "gemm_s8_tc (int8 mainloop)"
+    aq = buf.qh[0]
+    xr = x0.clone()
+    gemms = {
+        # name: (launch(i), N, K, residual, output bytes)
+        "qkv": ((lambda i: ovb.linear_h_sliced(aq, layers[i].qkv, [buf.q, buf.k, buf.v])) if f16
+                else (lambda i: ovb.linear_s8_nk_packed_q_sliced(*buf.qh, layers[i].qkv,
+                                                                 [buf.q, buf.k, buf.v])),
+                QKV, H, False, 4 * M_TOKENS * QKV),
+        "o": ((lambda i: ovb.linear_h(buf.qo[0], layers[i].o, xr, accumulate=True)) if f16
+              else (lambda i: ovb.linear_s8_nk_packed_q_add(*buf.qo, layers[i].o, xr)),
+              H, LY.QD, True, 4 * M_TOKENS * H),
+        "gate_up+silu": ((lambda i: ovb.linear_h_silu(aq, layers[i].gate_up, out=buf.qi,
+                                                      f16=True)) if f16
+                         else (lambda i: ovb.linear_q_silu(*buf.qh, layers[i].gate_up,
+                                                           out=buf.qi)),
+                         2 * INTER, H, False,
+                         M_TOKENS * INTER * (2 if f16 else 1) + 4 * M_TOKENS * INTER // 32),
+        "down": ((lambda i: ovb.linear_h(buf.qi[0], layers[i].down, xr, accumulate=True)) if f16
+                 else (lambda i: ovb.linear_s8_nk_packed_q_add(*buf.qi, layers[i].down, xr)),
+                 H, INTER, True, 4 * M_TOKENS * H),
+    }
+    n_launch = 2 * N_LAYERS
+    per_gemm = []
     with torch.cuda.stream(stream):
         ovb.rmsnorm_quantize_f32(x0, layers[0].post_ln, LY.RMS_EPS, out=buf.qh, f16=f16)
-        kg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(kg, stream=stream):
-            for i in range(n_launch):
-                if f16:
-                    ovb.linear_h_sliced(buf.qh[0], layers[i % N_LAYERS].gate_up,
-                                        [buf.gate, buf.up])
-                else:
-                    ovb.linear_s8_nk_packed_q_sliced(*buf.qh, layers[i % N_LAYERS].gate_up,
-                                                     [buf.gate, buf.up])
-        kg.replay()  # warm
-        k0.record(stream)
-        kg.replay()
-        k1.record(stream)
+        ovb.s8_nk_quantize(buf.q, out=buf.qo, f16=f16)
+        for name, (fn, N_g, K_g, res, ob) in gemms.items():
+            kg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(kg, stream=stream):
+                for i in range(n_launch):
+                    fn(i % N_LAYERS)
+            kg.replay()  # warm
+            k0 = torch.cuda.Event(enable_timing=True)
+            k1 = torch.cuda.Event(enable_timing=True)
+            k0.record(stream)
+            kg.replay()
+            k1.record(stream)
+            k1.synchronize()
+            gemm_us = k0.elapsed_time(k1) * 1e3 / n_launch
+            kg.reset()
+            per_gemm.append(gemm_roofline(name, kern, M_TOKENS, N_g, K_g, res, ob, gemm_us, f16))
     torch.cuda.synchronize()
-    gemm_us = k0.elapsed_time(k1) * 1e3 / n_launch
-    roofline = gate_up_roofline(gemm_us, f16)
+    roofline = dict(max(per_gemm, key=lambda r: r["us_per_launch"]))
+    roofline["all_gemms"] = [{k: r[k] for k in ("kernel", "us_per_launch", "bound", "achieved",
+                                                "unit", "frac", "traffic")} for r in per_gemm]
 
     # ---- end to end through the public API with host buffers
     rng = np.random.default_rng(77)
@@ -344,7 +369,6 @@ def run_ours(args, rank: int, world: int, local_rank: int):
            "ms_per_step": e2e_ms / args.steps}
 
     status = ovb.device_status()
-    kg.reset()
     path.release()
 
     # ---- the other numerics path over the same K steps (reported, not headline)
