@@ -277,8 +277,9 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
     args.silu_mode = silu->mode;
     args.silu_kp = w->glu_inter;
   }
-  const int tile = ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : 4);
-  if (cuda_failed(ovb::launch_gemm_h(tile, tmap_a, w->tmap_w16[tile], args, s), "gemm launch"))
+  const int config = ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : 7);
+  const int width = ovb::kHConfigs[config].width;
+  if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
 }

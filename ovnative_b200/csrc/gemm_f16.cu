@@ -572,53 +572,185 @@ struct CtlH {
   uint64_t empty[kMaxStagesH];
   uint64_t tfull[2];
   uint64_t drain;
+  uint64_t recv;  // split-K: partner partials have arrived (cluster scope)
   uint32_t tmem_base;
   int abort;
 };
 
-template <int BN, bool kSilu>
+// kSplit > 1: the CTAs of a kSplit-CTA cluster share one output tile and
+// split its k-stages; each owns BN / kSplit columns of the tile and receives
+// the other ranks' partial accumulators for them in `recv`
+// [kSplit - 1][128 rows][kRecvStride floats] of its shared memory.
+template <int BN, bool kSilu, int kSplit = 1>
 struct TileH {
+  static_assert(kSplit == 1 || (!kSilu && (BN / kSplit) % 32 == 0), "split-K layout");
   static constexpr uint32_t kWBytes = BN * 128;
   static constexpr uint32_t kStageBytes = kABytesH + kWBytes;
   static constexpr int kAcc = 2;
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
   static constexpr size_t kStgAll = kSilu ? 0 : static_cast<size_t>(kEpiW) * 32 * kStgStrideF * 4;
+  static constexpr int kOwn = BN / kSplit;     // columns owned per rank
+  static constexpr int kRecvStride = kOwn + 4;  // floats; 16-byte rows, conflict-free v4 access
+  static constexpr size_t kRecvBytes =
+      kSplit > 1 ? static_cast<size_t>(kSplit - 1) * kBlockM * kRecvStride * 4 : 0;
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
   // tiles have small stages), at most kMaxStagesH.
-  static constexpr int kStagesFit =
-      static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
+  static constexpr int kStagesFit = static_cast<int>(
+      (227 * 1024 - 1024 - kStgAll - kRecvBytes - sizeof(CtlH)) / kStageBytes);
   static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
   static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes +
-                                       kStgAll + sizeof(CtlH);
+                                       kStgAll + kRecvBytes + sizeof(CtlH);
   static_assert(kStages >= 3, "too few pipeline stages");
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, bool kSilu>
-__global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
+// The split-K epilogue (one tile per cluster).  Warp (quarter, eh) handles
+// the 32-column chunks c = eh, eh+2, ... of rows 32*quarter..: a chunk owned
+// by another rank o is sent -- this thread's row of the partial accumulator,
+// 32 floats -- into o's `recv` slot for this rank with shared::cluster
+// stores, then a release-arrive on o's `recv` mbarrier.  For an owned chunk
+// the thread waits (bounded, cluster-scope acquire) until every partner's
+// rows have arrived, sums the partials in rank order 0, 1, ..., kSplit-1
+// (deterministic) and writes o = sum * wscale (+ C) like the plain epilogue.
+template <int BN, int kSplit>
+__device__ __forceinline__ void epilogue_split(const GemmArgs& args, CtlH* ctl,
+                                               volatile int* abort, uint32_t tmem_base,
+                                               float* stg, const float* recv, int quarter,
+                                               int eh, int rank, int64_t tile, int64_t m_tiles) {
+  using T = TileH<BN, false, kSplit>;
+  constexpr int kChunks = BN / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const int64_t m0 = (tile % m_tiles) * kBlockM;
+  const int64_t n0 = (tile / m_tiles) * BN;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const bool got = ovb_wait(smem_u32(&ctl->tfull[0]), 0u, abort);
+  if (!__all_sync(0xffffffffu, got) && lane == 0) {
+    atomicOr(&g_status_f16, kErrEpilogue);
+    *abort = 1;
+  }
+  tc_fence_after();
+  // 1. Send the partials of the chunks other ranks own (also after a failed
+  //    wait, so that every arrival the owners count is made).
+#pragma unroll
+  for (int c = eh; c < kChunks; c += 2) {
+    const int o = (c * 32) / T::kOwn;
+    if (o == rank) continue;
+    uint32_t v[32];
+    tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(c * 32), v);
+    tc_wait_ld32(v);
+    const int slot = rank < o ? rank : rank - 1;
+    const uint32_t local =
+        smem_u32(recv + (static_cast<size_t>(slot) * kBlockM + row) * T::kRecvStride +
+                 (c * 32 - o * T::kOwn));
+    const uint32_t remote = mapa_shared(local, static_cast<uint32_t>(o));
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      st_cluster_v4(remote + j * 4, __uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                    __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+    mbar_arrive_remote(mapa_shared(smem_u32(&ctl->recv), static_cast<uint32_t>(o)));
+  }
+  // 2. The owned chunks: wait for the partners, sum in rank order, store.
+  bool mine = false;
+#pragma unroll
+  for (int c = eh; c < kChunks; c += 2) mine = mine || ((c * 32) / T::kOwn == rank);
+  if (!mine) return;
+  const bool all_in = ovb_wait_cluster(smem_u32(&ctl->recv), 0u, abort);
+  if (!__all_sync(0xffffffffu, all_in)) {
+    if (lane == 0) {
+      atomicOr(&g_status_f16, kErrEpilogue);
+      *abort = 1;
+    }
+    return;
+  }
+  const int64_t r0 = m0 + quarter * 32;
+  const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
+#pragma unroll
+  for (int c = eh; c < kChunks; c += 2) {
+    if ((c * 32) / T::kOwn != rank) continue;
+    uint32_t v[32];
+    tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(c * 32), v);
+    tc_wait_ld32(v);
+    const int col = c * 32 - rank * T::kOwn;
+    float sum[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+    for (int r = 0; r < kSplit; ++r) {
+      if (r == rank) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          sum[j] = r == 0 ? __uint_as_float(v[j]) : __fadd_rn(sum[j], __uint_as_float(v[j]));
+      } else {
+        const int slot = r < rank ? r : r - 1;
+        const float* src =
+            recv + (static_cast<size_t>(slot) * kBlockM + row) * T::kRecvStride + col;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 p = *reinterpret_cast<const float4*>(src + j);
+          const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) sum[j + q] = r == 0 ? pv[q] : __fadd_rn(sum[j + q], pv[q]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stg[lane * kStgStrideF + j] = sum[j];
+    __syncwarp();
+    const int64_t nc = n0 + c * 32;
+    if (nc < N && rows > 0) {
+      int si = 0;
+#pragma unroll
+      for (int k = 1; k < kMaxSlices; ++k)
+        if (k < args.n_slices && nc >= args.slices[k].n_begin) si = k;
+      const SliceOut so = args.slices[si];
+      const int64_t local = nc - so.n_begin;
+      if (lane < so.n_count - local) {
+        const float ws = __ldg(args.wscale + nc + lane);
+        store_rows(stg + lane, kStgStrideF, so.C + r0 * so.ldc + local + lane, so.ldc, rows, ws,
+                   args.accumulate);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <int BN, bool kSilu, int kSplit>
+__global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ GemmArgs args) {
-  using T = TileH<BN, kSilu>;
+  using T = TileH<BN, kSilu, kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(T::kStages) * T::kStageBytes);
-  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
+  float* recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
+  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(recv) + T::kRecvBytes);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N;
   const int Kb = static_cast<int>(args.Kb);
-  const int ksteps = (Kb + 1) / 2;
   const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
   const int64_t n_tiles = (N + BN - 1) / BN;
   const int64_t tiles = m_tiles * n_tiles;
+  // Split-K: one tile per cluster (grid = tiles * kSplit); rank r runs the
+  // k-stages [j_begin, j_end).  Otherwise a persistent grid over the tiles.
+  const int rank = kSplit > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  // Rank r gets stages [r*S/kSplit, (r+1)*S/kSplit): at least one each,
+  // since the host launches split-K only when S >= kSplit.
+  const int all_steps = (Kb + 1) / 2;
+  const int j_begin = kSplit > 1 ? (rank * all_steps) / kSplit : 0;
+  const int j_end = kSplit > 1 ? ((rank + 1) * all_steps) / kSplit : all_steps;
+  const int ksteps = j_end - j_begin;
+  const int64_t tile0 = kSplit > 1 ? static_cast<int64_t>(blockIdx.x) / kSplit : blockIdx.x;
+  const int64_t tile_step = kSplit > 1 ? tiles : static_cast<int64_t>(gridDim.x);
   const int64_t my_tiles =
-      tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+      tiles > tile0 ? (kSplit > 1 ? 1 : (tiles - tile0 + tile_step - 1) / tile_step) : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::kStages; ++s) {
@@ -627,6 +759,10 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
     }
     for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
+    // Split-K: every sender thread of every partner arrives once per owned
+    // chunk: (kSplit - 1) ranks x (owned chunks) x 4 lane quarters x 32.
+    mbar_init(smem_u32(&ctl->recv),
+              kSplit > 1 ? static_cast<uint32_t>((kSplit - 1) * (T::kOwn / 32) * 128) : 1u);
     ctl->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmap_a);
@@ -638,6 +774,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kSplit > 1) cluster_sync();  // partners' `recv` barriers are initialised
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   pdl_wait();  // the preceding kernel's outputs (A, residual C) are complete
@@ -648,10 +785,11 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
     if (lane == 0) {
       int64_t st = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int64_t tile = tile0; tile < tiles && ok; tile += tile_step) {
         const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
         const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
-        for (int j = 0; j < ksteps; ++j, ++st) {
+        for (int jj = 0; jj < ksteps; ++jj, ++st) {
+          const int j = j_begin + jj;
           const int s = static_cast<int>(st % T::kStages);
           const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
           if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
@@ -726,7 +864,12 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    if constexpr (kSilu) {
+    if constexpr (kSplit > 1) {
+      if (my_tiles > 0)
+        epilogue_split<BN, kSplit>(args, ctl, abort, tmem_base,
+                                   stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), recv,
+                                   warp & 3, (warp - kFirstEpiH) >> 2, rank, tile0, m_tiles);
+    } else if constexpr (kSilu) {
       epilogue_silu_loop<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, warp & 3,
                                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
                                                 m_tiles, my_tiles);
@@ -739,30 +882,53 @@ __global__ void __launch_bounds__(TileH<BN, kSilu>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // Split-K: no CTA leaves (releasing its shared memory) while a partner may
+  // still store into it or arrive on its barrier.
+  if constexpr (kSplit > 1) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemColsF);
   }
 }
 
-template <int BN, bool kSilu>
+template <int BN, bool kSilu, int kSplit = 1>
 cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  using T = TileH<BN, kSilu>;
+  using T = TileH<BN, kSilu, kSplit>;
+  auto* kernel = gemm_h_kernel<BN, kSilu, kSplit>;
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_h_kernel<BN, kSilu>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(T::kSmemBytes));
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
-  return launch_pdl(gemm_h_kernel<BN, kSilu>, dim3(grid), dim3(T::kThreads), T::kSmemBytes, s,
-                    tmap_a, tmap_w, args);
+  if constexpr (kSplit == 1) {
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
+    return launch_pdl(kernel, dim3(grid), dim3(T::kThreads), T::kSmemBytes, s, tmap_a, tmap_w,
+                      args);
+  } else {
+    // One tile per kSplit-CTA cluster; every rank needs at least one stage.
+    if ((args.Kb + 1) / 2 < kSplit) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * kSplit));
+    cfg.blockDim = dim3(T::kThreads);
+    cfg.dynamicSmemBytes = T::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_w, args);
+  }
 }
 
 template <int BN>
@@ -819,22 +985,36 @@ int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device) {
 // tensor core (4 MMAs: ~128 clocks each at N = 256, ~64 at N <= 128) and the
 // TMA feed (measured ~375 clocks for stages up to ~40 KB, ~100 B/clock per SM
 // beyond), plus a per-tile cost (prologue, epilogue stores) growing with BN.
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_widths) {
-  if (const char* e = std::getenv("OVB_GEMM_TILE_N")) {
-    const int v = std::atoi(e);
-    for (int i = 0; i < n_widths; ++i)
-      if (kTileNF[i] == v) return i;
+// Split-K configurations (kHConfigs[4..6]) need at least this many 64-k
+// stages per rank to pay for the partial-sum exchange.
+constexpr int kMinStagesPerRank = 4;
+
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_configs) {
+  const int64_t ksteps = (Kb + 1) / 2;
+  const char* et = std::getenv("OVB_GEMM_TILE_N");
+  const char* es = std::getenv("OVB_GEMM_SPLIT_K");
+  if (et || es) {
+    const int bn = et ? std::atoi(et) : 0;
+    const int sp = es ? std::atoi(es) : 1;
+    for (int i = 0; i < n_configs; ++i)
+      if ((bn == 0 || kTileNF[kHConfigs[i].width] == bn) && kHConfigs[i].split == sp &&
+          ksteps >= static_cast<int64_t>(kHConfigs[i].split))
+        return i;
   }
   static constexpr int64_t kPerStage[4] = {512, 375, 375, 375};
   const int64_t sms = num_sms(device);
   const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
-  const int64_t ksteps = (Kb + 1) / 2;
   int best = 0;
   int64_t best_cost = -1;
-  for (int i = 0; i < n_widths; ++i) {
-    const int64_t tiles = m_tiles * ((N + kTileNF[i] - 1) / kTileNF[i]);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const int64_t cost = waves * (2000 + 10 * kTileNF[i] + ksteps * kPerStage[i]);
+  for (int i = 0; i < n_configs; ++i) {
+    const int w = kHConfigs[i].width, sp = kHConfigs[i].split;
+    if (sp > 1 && ksteps < static_cast<int64_t>(sp) * kMinStagesPerRank) continue;
+    const int64_t tiles = m_tiles * ((N + kTileNF[w] - 1) / kTileNF[w]);
+    const int64_t ctas = tiles * sp;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const int64_t stages = (ksteps + sp - 1) / sp;
+    const int64_t cost = waves * (2000 + 10 * kTileNF[w] + stages * kPerStage[w] +
+                                  (sp > 1 ? 1500 : 0));
     if (best_cost < 0 || cost < best_cost) {
       best = i;
       best_cost = cost;
@@ -843,21 +1023,24 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_widths) {
   return best;
 }
 
-cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
   if (args.silu_out) {
-    switch (tile) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
+    switch (config) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
       case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);
       case 1: return launch_h_impl<128, true>(tmap_a, tmap_w, args, s);
       case 2: return launch_h_impl<64, true>(tmap_a, tmap_w, args, s);
       default: return cudaErrorInvalidValue;
     }
   }
-  switch (tile) {
+  switch (config) {  // kHConfigs
     case 0: return launch_h_impl<256, false>(tmap_a, tmap_w, args, s);
     case 1: return launch_h_impl<128, false>(tmap_a, tmap_w, args, s);
     case 2: return launch_h_impl<64, false>(tmap_a, tmap_w, args, s);
     case 3: return launch_h_impl<32, false>(tmap_a, tmap_w, args, s);
+    case 4: return launch_h_impl<64, false, 2>(tmap_a, tmap_w, args, s);
+    case 5: return launch_h_impl<128, false, 2>(tmap_a, tmap_w, args, s);
+    case 6: return launch_h_impl<128, false, 4>(tmap_a, tmap_w, args, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -63,8 +63,15 @@ constexpr int kStageK = 128;
 // Output-tile widths the GEMM is built for (one kernel per width).
 constexpr int kTileN[3] = {128, 64, 32};
 
-// Output-tile widths of the fp16 mainloop.
+// Output-tile widths of the fp16 mainloops.
 constexpr int kTileNF[4] = {256, 128, 64, 32};
+// Configurations of the plain fp16 mainloop: tile width (index into
+// kTileNF) and split-K factor (a cluster of `split` CTAs per output tile).
+struct HConfig {
+  int width;
+  int split;
+};
+constexpr HConfig kHConfigs[7] = {{0, 1}, {1, 1}, {2, 1}, {3, 1}, {2, 2}, {1, 2}, {1, 4}};
 
 constexpr int kMaxSlices = 4;
 
@@ -135,8 +142,9 @@ cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorM
                             const GemmArgs& args, cudaStream_t s);
 cudaError_t read_and_clear_status_f16(int* out, cudaStream_t s);
 // The plain fp16 mainloop: A is fp16 [M, Kp] (dequantised activations).
-// n_widths: consider the first n entries of kTileNF (3 = BN >= 64).
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_widths = 4);
+// Returns an index into kHConfigs; n_configs limits the choice to the first
+// n entries (3 = BN >= 64 without split-K, for the fused SiLU*up epilogue).
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_configs = 7);
 cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s);
 

@@ -226,3 +226,50 @@ def test_quantiser_f16_range_flag(cuda):
     ovb.s8_nk_quantize(A, f16=True)
     assert ovb.device_status() == 16
     assert ovb.device_status() == 0
+
+
+# ------------------------------------------- split-K clusters (fp16 mainloop)
+SPLIT_SHAPES = [(400, 1024, 3072), (129, 320, 1056), (300, 1000, 256), (1, 128, 512),
+                (400, 1024, 2048)]
+
+
+@pytest.mark.parametrize("tile_n,split", [(64, 2), (128, 2), (128, 4)])
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+def test_linear_h_split_k(cuda, monkeypatch, tile_n, split, M, N, K):
+    """K split over a cluster of `split` CTAs per output tile; each rank sums
+    its partners' partials in rank order.  1056 gives 17 k-stages (uneven
+    per rank), 256 gives 4 (one per rank at split 4)."""
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    monkeypatch.setenv("OVB_GEMM_SPLIT_K", str(split))
+    rng = np.random.default_rng(M * 5 + N + K + split)
+    A, W, s = case(rng, M, N, K)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    w = ovb.Weight.from_nk(W, s, f16=True)
+    a16, _ = ovb.s8_nk_quantize(dev(A, cuda), f16=True)
+    aq_h, asc_h = O.quantize(A)
+    got = host(ovb.linear_h(a16, w))
+    check_tolerance(got, O.linear_q(aq_h, asc_h, W, s, K))
+    # deterministic: the partial sums are added in a fixed order
+    assert host(ovb.linear_h(a16, w)).tobytes() == got.tobytes()
+    C = dev(C0, cuda)
+    ovb.linear_h(a16, w, C, accumulate=True)
+    check_tolerance(host(C), O.linear_q(aq_h, asc_h, W, s, K, C_in=C0))
+    assert ovb.device_status() == 0
+    w.close()
+
+
+@pytest.mark.parametrize("split", [2, 4])
+def test_linear_h_split_k_sliced(cuda, golden, monkeypatch, split):
+    monkeypatch.setenv("OVB_GEMM_TILE_N", "128")
+    monkeypatch.setenv("OVB_GEMM_SPLIT_K", str(split))
+    for i in range(3):
+        Ns = [int(n) for n in golden[f"sliced{i}_Ns"]]
+        parts = [ovb.Weight.from_nk(golden[f"sliced{i}_W{j}"], golden[f"sliced{i}_s{j}"], f16=True)
+                 for j in range(len(Ns))]
+        wc = ovb.Weight.concat(parts)
+        a16, _ = ovb.s8_nk_quantize(dev(golden[f"sliced{i}_A"], cuda), f16=True)
+        Cs = [torch.full((a16.shape[0], n), float("nan"), device=cuda) for n in Ns]
+        ovb.linear_h_sliced(a16, wc, Cs)
+        for j, c in enumerate(Cs):
+            check_tolerance(host(c), golden[f"sliced{i}_C{j}"])
+    assert ovb.device_status() == 0
