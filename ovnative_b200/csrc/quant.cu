@@ -63,9 +63,10 @@ __device__ __forceinline__ uint4 dequant8_f16(const float (&v)[8], int nv, float
 }
 
 // The same for 4 consecutive values (4 bytes of q, or 8 bytes of fp16).
+template <int kMode>
 __device__ __forceinline__ void store4(uint8_t* aq, int64_t idx, const float (&v)[4], int nv,
-                                       float inv, float scale, int mode) {
-  if (mode == kModeF16) {
+                                       float inv, float scale) {
+  if constexpr (kMode == kModeF16) {
     uint32_t w[2];
     bool range_ok = true;
 #pragma unroll
@@ -91,18 +92,19 @@ __device__ __forceinline__ void store4(uint8_t* aq, int64_t idx, const float (&v
     uint32_t word = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      word |= ((i < nv) ? quant_byte(v[i], inv, mode == kModeU8) : 0u) << (8 * i);
+      word |= ((i < nv) ? quant_byte(v[i], inv, kMode == kModeU8) : 0u) << (8 * i);
     *reinterpret_cast<uint32_t*>(aq + idx) = word;
   }
 }
 
 // Write the 8 quantised values of element k of a row in the chosen form.
+template <int kMode>
 __device__ __forceinline__ void store8(uint8_t* aq, int64_t idx, const float (&v)[8], int nv,
-                                       float inv, float scale, int mode) {
-  if (mode == kModeF16)
+                                       float inv, float scale) {
+  if constexpr (kMode == kModeF16)
     *reinterpret_cast<uint4*>(aq + 2 * idx) = dequant8_f16(v, nv, inv, scale);
   else
-    *reinterpret_cast<uint2*>(aq + idx) = quant8(v, nv, inv, mode == kModeU8);
+    *reinterpret_cast<uint2*>(aq + idx) = quant8(v, nv, inv, kMode == kModeU8);
 }
 
 // Load 8 floats starting at p, the first nv of them valid (others 0).
@@ -122,9 +124,9 @@ __device__ __forceinline__ void load8(const float* p, int nv, bool vec_ok, float
 // Four threads per 32-k block (8 values each); the block absmax is reduced
 // over the four with shuffles (max is order-independent, so this equals the
 // reference's 8-lane max followed by a scalar tail).
+template <int kMode>
 __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, const float* A,
-                                                       int64_t lda, uint8_t* aq, float* asc,
-                                                       int mode) {
+                                                       int64_t lda, uint8_t* aq, float* asc) {
   pdl_wait();  // the producer of this kernel's input is complete
   pdl_launch_dependents();
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, con
     float scale, inv;
     block_scales(amax, &scale, &inv);
     if (valid) {
-      store8(aq, row * Kp + k, v, nv, inv, scale, mode);
+      store8<kMode>(aq, row * Kp + k, v, nv, inv, scale);
       if (sub == 0) asc[row * Kb + b] = scale;
     }
   }
@@ -204,10 +206,11 @@ __device__ __forceinline__ void stage_row(const float* __restrict__ src, int64_t
 // four consecutive elements per lane (one 16-byte shared-memory and gain
 // load each), the block absmax reduced over the eight lanes with shuffles
 // (max is order-independent, so this equals the reference's).
+template <int kMode>
 __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int64_t cols,
                                                                const float* x, const float* w,
                                                                float eps, uint8_t* aq,
-                                                               float* asc, int mode) {
+                                                               float* asc) {
   pdl_wait();  // the producer of this kernel's input is complete
   pdl_launch_dependents();
   extern __shared__ float srow_all[];
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
       block_scales(amax, &bs, &inv);
       if (b < Kb) {
         if (sub == 0) asc[r * Kb + b] = bs;
-        store4(aq, r * Kp + k, v, nv, inv, bs, mode);
+        store4<kMode>(aq, r * Kp + k, v, nv, inv, bs);
       }
     }
     __syncwarp();
@@ -280,65 +283,73 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
 }
 
 // The same for rows of at most 1024 elements (cols % 4 == 0, 16-byte aligned
-// x and w) -- the LM's hidden size.  Lane l's quantisation positions are
-// k = 128*i + 4*l, i < 8, exactly the positions it loads when staging the
-// row, so the row and the gains stay in registers: the gains are loaded
-// once per warp together with its first row, and shared memory only feeds
-// the reference-ordered sum of squares.
-constexpr int kSmallIters = 8;  // 8 x 128 = 1024 elements per row
+// x and w) -- the LM's hidden size -- with one 128-thread block (4 warps) per
+// row, so that the quantisation, serial within a warp, is spread over four:
+// all threads stage the row in shared memory; lanes 0..7 of warp 0 run the
+// reference-ordered sum of squares and publish the scale; then warp q
+// quantises the groups i = 2q, 2q+1 (128 elements each: eight lanes per
+// 32-k block, four elements per lane, as in the general kernel).
+constexpr int kSmallCols = 1024;
+constexpr int kSmallThreads = 128;
 
-__global__ void __launch_bounds__(256) rmsnorm_quantize_small_kernel(
+template <int kMode>
+__global__ void __launch_bounds__(kSmallThreads) rmsnorm_quantize_small_kernel(
     int64_t rows, int64_t cols, const float* x, const float* w, float eps, uint8_t* aq,
-    float* asc, int mode) {
+    float* asc) {
   pdl_wait();  // the producer of this kernel's input is complete
   pdl_launch_dependents();
-  extern __shared__ float srow_all[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  float* srow = srow_all + static_cast<int64_t>(warp) * cols;
+  __shared__ __align__(16) float srow[kSmallCols];
+  __shared__ float s_scale;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t Kb = (cols + 31) / 32, Kp = Kb * 32;
-  float4 wr[kSmallIters];
-#pragma unroll
-  for (int i = 0; i < kSmallIters; ++i) {
-    const int64_t k = 128 * i + 4 * lane;
-    wr[i] = k < cols ? __ldg(reinterpret_cast<const float4*>(w + k)) : make_float4(0, 0, 0, 0);
-  }
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * warps + warp; r < rows;
-       r += static_cast<int64_t>(gridDim.x) * warps) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* row = x + r * cols;
-    float4 xr[kSmallIters];
+    // Each thread's two float4 of the row (positions 128*i + 4*lane of its
+    // warp's groups), kept in registers for the quantisation.
+    float4 xr[2], wr[2];
 #pragma unroll
-    for (int i = 0; i < kSmallIters; ++i) {
-      const int64_t k = 128 * i + 4 * lane;
-      xr[i] = k < cols ? __ldg(reinterpret_cast<const float4*>(row + k)) : make_float4(0, 0, 0, 0);
+    for (int u = 0; u < 2; ++u) {
+      const int64_t k = 128 * (2 * warp + u) + 4 * lane;
+      xr[u] = k < cols ? __ldg(reinterpret_cast<const float4*>(row + k)) : make_float4(0, 0, 0, 0);
+      wr[u] = k < cols ? __ldg(reinterpret_cast<const float4*>(w + k)) : make_float4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int i = 0; i < kSmallIters; ++i) {
-      const int64_t k = 128 * i + 4 * lane;
-      if (k < cols) *reinterpret_cast<float4*>(srow + k) = xr[i];
+    for (int u = 0; u < 2; ++u) {
+      const int64_t k = 128 * (2 * warp + u) + 4 * lane;
+      if (k < cols) *reinterpret_cast<float4*>(srow + k) = xr[u];
     }
-    __syncwarp();
-    const int64_t nvec = cols / 8;
-    float acc = 0.f;
-    if (lane < 8)
-#pragma unroll 8
-      for (int64_t j = 0; j < nvec; ++j) {
-        const float v = srow[j * 8 + lane];
-        acc = __fmaf_rn(v, v, acc);
+    __syncthreads();
+    if (warp == 0) {
+      const int64_t nvec = cols / 8;
+      float acc = 0.f;
+      if (lane < 8) {
+        for (int64_t j0 = 0; j0 < nvec; j0 += 16) {
+          float t[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) t[u] = j0 + u < nvec ? srow[(j0 + u) * 8 + lane] : 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+            if (j0 + u < nvec) acc = __fmaf_rn(t[u], t[u], acc);
+        }
       }
-    float sum = __shfl_sync(0xffffffffu, acc, 0);
+      float sum = __shfl_sync(0xffffffffu, acc, 0);
 #pragma unroll
-    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, l));
-    for (int64_t i = nvec * 8; i < cols; ++i) sum = __fadd_rn(sum, __fmul_rn(srow[i], srow[i]));
-    const float scale =
-        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+      for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, l));
+      for (int64_t i = nvec * 8; i < cols; ++i) sum = __fadd_rn(sum, __fmul_rn(srow[i], srow[i]));
+      if (lane == 0)
+        s_scale =
+            __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
 #pragma unroll
-    for (int i = 0; i < kSmallIters; ++i) {
+    for (int u = 0; u < 2; ++u) {
+      const int i = 2 * warp + u;
       const int64_t b = 4 * i + (lane >> 3);
       const int64_t k = 128 * i + 4 * lane;
       const int nv = k < cols ? 4 : 0;  // cols % 4 == 0
-      const float xv[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
-      const float wv[4] = {wr[i].x, wr[i].y, wr[i].z, wr[i].w};
+      const float xv[4] = {xr[u].x, xr[u].y, xr[u].z, xr[u].w};
+      const float wv[4] = {wr[u].x, wr[u].y, wr[u].z, wr[u].w};
       float v[4];
       float amax = 0.f;
 #pragma unroll
@@ -353,19 +364,19 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_small_kernel(
       block_scales(amax, &bs, &inv);
       if (b < Kb) {
         if ((lane & 7) == 0) asc[r * Kb + b] = bs;
-        store4(aq, r * Kp + k, v, nv, inv, bs, mode);
+        store4<kMode>(aq, r * Kp + k, v, nv, inv, bs);
       }
     }
-    __syncwarp();
+    __syncthreads();  // srow and s_scale are reused by the next row
   }
 }
 
 // ------------------------------------------------- silu(gate)*up + quantize
+template <int kMode>
 __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
                                                                 const float* gate, int64_t ldg,
                                                                 const float* up, int64_t ldu,
-                                                                uint8_t* aq, float* asc,
-                                                                int mode) {
+                                                                uint8_t* aq, float* asc) {
   pdl_wait();  // the producer of this kernel's input is complete
   pdl_launch_dependents();
   const int64_t Kb = (K + 31) / 32, Kp = Kb * 32;
@@ -400,7 +411,7 @@ __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64
     float scale, inv;
     block_scales(amax, &scale, &inv);
     if (valid) {
-      store8(aq, row * Kp + k, v, nv, inv, scale, mode);
+      store8<kMode>(aq, row * Kp + k, v, nv, inv, scale);
       if (sub == 0) asc[row * Kb + b] = scale;
     }
   }
@@ -419,8 +430,13 @@ int grid_for(int64_t threads_needed) {
 cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq,
                             float* asc, int mode, cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
-  return launch_pdl(quantize_kernel, dim3(grid_for(M * Kb * 4)), dim3(256), 0, s, M, K, A, lda,
-                    static_cast<uint8_t*>(aq), asc, mode);
+  const dim3 grid(grid_for(M * Kb * 4));
+  auto* q8 = static_cast<uint8_t*>(aq);
+  switch (mode) {
+    case 0: return launch_pdl(quantize_kernel<0>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    case 1: return launch_pdl(quantize_kernel<1>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    default: return launch_pdl(quantize_kernel<2>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+  }
 }
 
 cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w,
@@ -437,31 +453,56 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(rmsnorm_quantize_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
+    for (auto* k : {rmsnorm_quantize_kernel<0>, rmsnorm_quantize_kernel<1>,
+                    rmsnorm_quantize_kernel<2>}) {
+      cudaError_t e =
+          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) return e;
+    }
     configured_dev = dev;
   }
   const int64_t blocks = (rows + warps - 1) / warps;
   const int grid = static_cast<int>(imin64(blocks, static_cast<int64_t>(num_sms(dev)) * 16));
-  const bool small = cols <= 128 * kSmallIters && (cols & 3) == 0 &&
+  const bool small = cols <= kSmallCols && (cols & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(w) & 15) == 0;
   if (small) {
-    return launch_pdl(rmsnorm_quantize_small_kernel, dim3(grid), dim3(warps * 32),
-                      static_cast<size_t>(warps) * row_bytes, s, rows, cols, x, w, eps,
-                      static_cast<uint8_t*>(aq), asc, mode);
+    const int sgrid = static_cast<int>(imin64(rows, static_cast<int64_t>(num_sms(dev)) * 16));
+    auto* q8s = static_cast<uint8_t*>(aq);
+    switch (mode) {
+      case 0: return launch_pdl(rmsnorm_quantize_small_kernel<0>, dim3(sgrid), dim3(kSmallThreads),
+                                0, s, rows, cols, x, w, eps, q8s, asc);
+      case 1: return launch_pdl(rmsnorm_quantize_small_kernel<1>, dim3(sgrid), dim3(kSmallThreads),
+                                0, s, rows, cols, x, w, eps, q8s, asc);
+      default: return launch_pdl(rmsnorm_quantize_small_kernel<2>, dim3(sgrid),
+                                 dim3(kSmallThreads), 0, s, rows, cols, x, w, eps, q8s, asc);
+    }
   }
-  return launch_pdl(rmsnorm_quantize_kernel, dim3(grid), dim3(warps * 32), smem, s, rows, cols, x, w,
-                    eps, static_cast<uint8_t*>(aq), asc, mode);
+  auto* q8 = static_cast<uint8_t*>(aq);
+  switch (mode) {
+    case 0: return launch_pdl(rmsnorm_quantize_kernel<0>, dim3(grid), dim3(warps * 32), smem, s,
+                              rows, cols, x, w, eps, q8, asc);
+    case 1: return launch_pdl(rmsnorm_quantize_kernel<1>, dim3(grid), dim3(warps * 32), smem, s,
+                              rows, cols, x, w, eps, q8, asc);
+    default: return launch_pdl(rmsnorm_quantize_kernel<2>, dim3(grid), dim3(warps * 32), smem, s,
+                               rows, cols, x, w, eps, q8, asc);
+  }
 }
 
 cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
                                      const float* up, int64_t ldu, void* aq, float* asc, int mode,
                                      cudaStream_t s) {
   const int64_t Kb = (K + 31) / 32;
-  return launch_pdl(silu_mul_quantize_kernel, dim3(grid_for(M * Kb * 4)), dim3(256), 0, s, M, K,
-                    gate, ldg, up, ldu, static_cast<uint8_t*>(aq), asc, mode);
+  const dim3 grid(grid_for(M * Kb * 4));
+  auto* q8 = static_cast<uint8_t*>(aq);
+  switch (mode) {
+    case 0: return launch_pdl(silu_mul_quantize_kernel<0>, grid, dim3(256), 0, s, M, K, gate, ldg,
+                              up, ldu, q8, asc);
+    case 1: return launch_pdl(silu_mul_quantize_kernel<1>, grid, dim3(256), 0, s, M, K, gate, ldg,
+                              up, ldu, q8, asc);
+    default: return launch_pdl(silu_mul_quantize_kernel<2>, grid, dim3(256), 0, s, M, K, gate, ldg,
+                               up, ldu, q8, asc);
+  }
 }
 
 cudaError_t read_and_clear_status_q(int* out, cudaStream_t s) {
