@@ -75,6 +75,32 @@ int num_sms(int device) {
   return cache[static_cast<size_t>(device)];
 }
 
+namespace {
+std::mutex g_ws_mu;
+std::vector<float*> g_split_ws;  // per device; kept for the life of the process
+}  // namespace
+
+bool ensure_split_workspace(int device) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  if (device >= static_cast<int>(g_split_ws.size()))
+    g_split_ws.resize(static_cast<size_t>(device) + 1, nullptr);
+  float*& ws = g_split_ws[static_cast<size_t>(device)];
+  if (ws) return true;
+  void* p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(kSplitSlots) * kSplitSlotBytes) != cudaSuccess) {
+    cudaGetLastError();  // without a workspace the GEMMs run without split-K
+    return false;
+  }
+  ws = static_cast<float*>(p);
+  return true;
+}
+
+float* split_workspace(int device) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  return device < static_cast<int>(g_split_ws.size()) ? g_split_ws[static_cast<size_t>(device)]
+                                                      : nullptr;
+}
+
 bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                     uint64_t inner, uint64_t rows, uint64_t stride_bytes, uint32_t box_inner,
                     uint32_t box_rows, CUtensorMapSwizzle swizzle) {
@@ -167,6 +193,7 @@ bool ensure_weight_tmap16(ovb_weight* w) {
 // Allocate and fill the fp16 copy of a packed weight.
 bool make_weight_f16(ovb_weight* w, cudaStream_t s) {
   const size_t n = static_cast<size_t>(w->N * w->Kp);
+  ovb::ensure_split_workspace(w->device);  // optional: split-K configs need it
   return !cuda_failed(cudaMalloc(&w->w16, n * 2), "cudaMalloc(fp16 weight)") &&
          !cuda_failed(ovb::launch_widen_f16(w->w, static_cast<int64_t>(n), w->w16, s),
                       "widen weight") &&
@@ -277,7 +304,11 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
     args.silu_mode = silu->mode;
     args.silu_kp = w->glu_inter;
   }
-  const int config = ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : 7);
+  args.split_ws = ovb::split_workspace(w->device);
+  // configs 0..3 are plain, 4..6 split-K (which needs the workspace), and the
+  // fused SiLU*up epilogue takes BN >= 64 without split-K (0..2)
+  const int config =
+      ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : (args.split_ws ? 7 : 4));
   const int width = ovb::kHConfigs[config].width;
   if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;

@@ -82,7 +82,10 @@ constexpr int kThreadsF = 32 * (kFirstEpi + kEpiWarpsF);
 constexpr uint32_t kTmemColsF = 512;
 constexpr int kAColsPerStage = kStageKF / 2;  // fp16 pairs per row
 constexpr uint32_t kABytesF = kBlockM * kStageKF;
-constexpr int kStgStrideF = 33;  // epilogue staging row stride (floats)
+// Epilogue staging row stride (floats): 16-byte rows, so that both the
+// row-per-lane float4 writes and the 4-rows-per-instruction float4 reads of
+// a 32x32 chunk are free of bank conflicts.
+constexpr int kStgStrideF = 36;
 // named barriers (0 is __syncthreads)
 constexpr int kBarStage = 1;                    // + s: converters -> MMA warp
 constexpr int kBarDfree = kBarStage + kStagesF;  // + d: epilogue -> MMA warp
@@ -154,10 +157,21 @@ __device__ __forceinline__ void dequant4(uint32_t x, __half2 s_hi, __half2 s_lo,
   out1 = *reinterpret_cast<const uint32_t*>(&r23);
 }
 
-// Writes this lane's column of a warp's staged 32-column chunk (`stg` points
-// at the lane's column of row 0): o = stg * ws (+ C_old), row by row.  The residual loads of 8 rows are issued before
-// their stores, so their latencies overlap (the compiler cannot reorder a
-// load past a store it cannot prove distinct).
+// Stage row `lane` of a warp's 32x32 accumulator chunk (one TMEM lane per
+// thread) in shared memory, row stride kStgStrideF.
+__device__ __forceinline__ void stage_chunk(float* stg, const uint32_t (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(stg + lane * kStgStrideF + 4 * q) =
+        make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                    __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+}
+
+// Scalar path of store_chunk: lane l writes column l, row by row.  The
+// residual loads of 8 rows are issued before their stores, so their
+// latencies overlap (the compiler cannot reorder a load past a store it
+// cannot prove distinct).
 __device__ __forceinline__ void store_rows(const float* stg, int stride, float* cbase,
                                            int64_t ldc, int rows, float ws, int accumulate) {
   for (int r0 = 0; r0 < rows; r0 += 8) {
@@ -175,6 +189,106 @@ __device__ __forceinline__ void store_rows(const float* stg, int stride, float* 
       }
     }
   }
+}
+
+// Lane l's residual values of a chunk for the float4 path: rows
+// 4*it + l/8 (it in [it0, it0 + kN)), columns 4*(l%8) .. +3; zeros outside
+// rows / ncols.  The whole-float4 loads are predicated, not branched, so that
+// all of them are in flight together; ragged last columns load singly.
+template <int kN>
+__device__ __forceinline__ void load_residual(const float* cbase, int64_t ldc, int rows, int ncols,
+                                              int it0, float4 (&old)[kN]) {
+  const int lane = threadIdx.x & 31;
+  const int c4 = (lane & 7) * 4;
+  const bool full = c4 + 3 < ncols;
+#pragma unroll
+  for (int i = 0; i < kN; ++i) {
+    const int r = (it0 + i) * 4 + (lane >> 3);
+    const bool ok = full && r < rows;
+    old[i] = ld_f4_if(cbase + (ok ? r * ldc + c4 : 0), ok);
+  }
+  if (!full && c4 < ncols) {
+#pragma unroll
+    for (int i = 0; i < kN; ++i) {
+      const int r = (it0 + i) * 4 + (lane >> 3);
+      if (r < rows) {
+        const float* src = cbase + r * ldc + c4;
+        old[i].x = src[0];
+        if (c4 + 1 < ncols) old[i].y = src[1];
+        if (c4 + 2 < ncols) old[i].z = src[2];
+      }
+    }
+  }
+}
+
+// o = v * ws (+ old) for four columns, the reference's epilogue order.
+__device__ __forceinline__ float4 scale_add4(float4 v, const float (&ws)[4], float4 old,
+                                             int accumulate) {
+  v.x = __fmul_rn(v.x, ws[0]);
+  v.y = __fmul_rn(v.y, ws[1]);
+  v.z = __fmul_rn(v.z, ws[2]);
+  v.w = __fmul_rn(v.w, ws[3]);
+  if (accumulate) {
+    v.x = __fadd_rn(v.x, old.x);
+    v.y = __fadd_rn(v.y, old.y);
+    v.z = __fadd_rn(v.z, old.z);
+    v.w = __fadd_rn(v.w, old.w);
+  }
+  return v;
+}
+
+// Write o (four columns of row r) to cbase + r * ldc + c4, clipped to ncols.
+__device__ __forceinline__ void put4(float* cbase, int64_t ldc, int r, int c4, int ncols,
+                                     float4 o) {
+  float* dst = cbase + r * ldc + c4;
+  if (c4 + 3 < ncols) {
+    *reinterpret_cast<float4*>(dst) = o;
+  } else {
+    if (c4 < ncols) dst[0] = o.x;
+    if (c4 + 1 < ncols) dst[1] = o.y;
+    if (c4 + 2 < ncols) dst[2] = o.z;
+  }
+}
+
+// Lane l's four wscale values (columns 4*(l%8) ..) from the per-lane values
+// wl (lane l holds column l's).  All 32 lanes must call it.
+__device__ __forceinline__ void gather_ws4(float wl, float (&ws)[4]) {
+  const int c4 = ((threadIdx.x & 31) & 7) * 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ws[j] = __shfl_sync(0xffffffffu, wl, c4 + j);
+}
+
+// Write a warp's staged 32x32 chunk to C: o = acc * ws[col] (+ C_old) for
+// the first `rows` rows and `ncols` columns at cbase (row stride ldc).
+// Float4 path (C rows 16-byte aligned: vec): lane l handles rows 4*it + l/8
+// and columns 4*(l%8) .. +3, i.e. four 128-byte row segments per warp
+// instruction, with the whole residual chunk loaded before the first store.
+// Otherwise the scalar path.  All 32 lanes must call it; wl as in gather_ws4.
+__device__ __forceinline__ void store_chunk(const float* stg, float* cbase, int64_t ldc, int rows,
+                                            int ncols, float wl, int accumulate, bool vec) {
+  const int lane = threadIdx.x & 31;
+  float ws[4];
+  gather_ws4(wl, ws);
+  if (!vec) {
+    if (lane < ncols) store_rows(stg + lane, kStgStrideF, cbase + lane, ldc, rows, wl, accumulate);
+    return;
+  }
+  const int c4 = (lane & 7) * 4;
+  float4 old[8];
+  if (accumulate) load_residual<8>(cbase, ldc, rows, ncols, 0, old);
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    if (r < rows && c4 < ncols) {
+      const float4 v = *reinterpret_cast<const float4*>(stg + r * kStgStrideF + c4);
+      put4(cbase, ldc, r, c4, ncols, scale_add4(v, ws, old[it], accumulate));
+    }
+  }
+}
+
+// True when every row of the slice's C is 16-byte aligned (float4 stores).
+__device__ __forceinline__ bool rows_aligned(const SliceOut& so) {
+  return (reinterpret_cast<uintptr_t>(so.C) & 15) == 0 && (so.ldc & 3) == 0;
 }
 
 // The epilogue warps' loop over this CTA's tiles (both fp16 mainloops).
@@ -230,8 +344,7 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
         if (!kPipe && i > 0) tmem_ld32(dcol + static_cast<uint32_t>(c * 32), cur);
         tc_wait_ld32(cur);
         if (kPipe && c + 2 < kChunks) tmem_ld32(dcol + static_cast<uint32_t>((c + 2) * 32), nxt);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) stg[lane * kStgStrideF + j] = __uint_as_float(cur[j]);
+        stage_chunk(stg, cur);
         __syncwarp();
         const int64_t nc = n0 + c * 32;  // first column of the chunk
         if (nc < N && rows > 0) {
@@ -243,9 +356,9 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
             if (k < args.n_slices && nc >= args.slices[k].n_begin) si = k;
           const SliceOut so = args.slices[si];
           const int64_t local = nc - so.n_begin;
-          if (lane < so.n_count - local)
-            store_rows(stg + lane, kStgStrideF, so.C + r0 * so.ldc + local + lane, so.ldc, rows,
-                       wsv[i], args.accumulate);
+          const int ncols = static_cast<int>(so.n_count - local < 32 ? so.n_count - local : 32);
+          store_chunk(stg, so.C + r0 * so.ldc + local, so.ldc, rows, ncols, wsv[i],
+                      args.accumulate, rows_aligned(so));
         }
         __syncwarp();
       }
@@ -572,15 +685,18 @@ struct CtlH {
   uint64_t empty[kMaxStagesH];
   uint64_t tfull[2];
   uint64_t drain;
-  uint64_t recv;  // split-K: partner partials have arrived (cluster scope)
   uint32_t tmem_base;
   int abort;
+  uint32_t my_sm;  // split-K: %smid of this CTA (its workspace slot)
 };
 
 // kSplit > 1: the CTAs of a kSplit-CTA cluster share one output tile and
-// split its k-stages; each owns BN / kSplit columns of the tile and receives
-// the other ranks' partial accumulators for them in `recv`
-// [kSplit - 1][128 rows][kRecvStride floats] of its shared memory.
+// split its k-stages; rank r owns the columns [r * kOwn, (r + 1) * kOwn) of
+// the tile and receives the other ranks' partial accumulators for them in
+// its SM's slot of the split-K workspace (global memory, L2-resident):
+// [kSplit - 1 senders][128 rows][kOwn floats].  A split-K CTA needs more
+// than half of the SM's shared memory, so no two of them share an SM (or a
+// workspace slot).
 template <int BN, bool kSilu, int kSplit = 1>
 struct TileH {
   static_assert(kSplit == 1 || (!kSilu && (BN / kSplit) % 32 == 0), "split-K layout");
@@ -590,51 +706,56 @@ struct TileH {
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
   static constexpr size_t kStgAll = kSilu ? 0 : static_cast<size_t>(kEpiW) * 32 * kStgStrideF * 4;
-  static constexpr int kOwn = BN / kSplit;     // columns owned per rank
-  static constexpr int kRecvStride = kOwn + 4;  // floats; 16-byte rows, conflict-free v4 access
-  static constexpr size_t kRecvBytes =
-      kSplit > 1 ? static_cast<size_t>(kSplit - 1) * kBlockM * kRecvStride * 4 : 0;
+  static constexpr int kOwn = BN / kSplit;  // columns owned per rank
+  static constexpr size_t kPartialFloats = static_cast<size_t>(kBlockM) * kOwn;  // per sender
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
   // tiles have small stages), at most kMaxStagesH.
-  static constexpr int kStagesFit = static_cast<int>(
-      (227 * 1024 - 1024 - kStgAll - kRecvBytes - sizeof(CtlH)) / kStageBytes);
+  static constexpr int kStagesFit =
+      static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
   static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
-  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes +
-                                       kStgAll + kRecvBytes + sizeof(CtlH);
+  static constexpr size_t kSmemBytes =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kStgAll + sizeof(CtlH);
   static_assert(kStages >= 3, "too few pipeline stages");
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kSplit == 1 || kSmemBytes > 116 * 1024, "a split-K CTA must have its SM alone");
+  static_assert(kSplit == 1 || (kSplit - 1) * kPartialFloats * 4 <= kSplitSlotBytes,
+                "split-K workspace slot");
 };
 
-// The split-K epilogue (one tile per cluster).  Warp (quarter, eh) handles
-// the 32-column chunks c = eh, eh+2, ... of rows 32*quarter..: a chunk owned
-// by another rank o is sent -- this thread's row of the partial accumulator,
-// 32 floats -- into o's `recv` slot for this rank with shared::cluster
-// stores, then a release-arrive on o's `recv` mbarrier.  For an owned chunk
-// the thread waits (bounded, cluster-scope acquire) until every partner's
-// rows have arrived, sums the partials in rank order 0, 1, ..., kSplit-1
-// (deterministic) and writes o = sum * wscale (+ C) like the plain epilogue.
+// The split-K epilogue (one tile per cluster), in two phases around a
+// cluster barrier that every thread of the cluster executes.  Warp
+// (quarter, eh) handles the 32-column chunks c = eh, eh+2, ... of rows
+// 32*quarter..; rank o = c*32 / kOwn owns chunk c.
+// Phase 1 (split_send): a chunk another rank owns is staged in shared memory
+// and written with coalesced float4 stores into the owner's workspace slot,
+// sender slot (rank < o ? rank : rank - 1).
+// Phase 2 (split_finish, after barrier.cluster arrive.release / wait.acquire,
+// which makes those global stores visible cluster-wide): for an owned chunk
+// the partials are summed in rank order 0, 1, ..., kSplit-1 (deterministic),
+// then o = sum * wscale (+ C) as in the plain epilogue.
 template <int BN, int kSplit>
-__device__ __forceinline__ void epilogue_split(const GemmArgs& args, CtlH* ctl,
-                                               volatile int* abort, uint32_t tmem_base,
-                                               float* stg, const float* recv, int quarter,
-                                               int eh, int rank, int64_t tile, int64_t m_tiles) {
+__device__ __forceinline__ void split_send(const GemmArgs& args, CtlH* ctl, volatile int* abort,
+                                           uint32_t tmem_base, float* stg, int quarter, int eh,
+                                           int rank) {
   using T = TileH<BN, false, kSplit>;
   constexpr int kChunks = BN / 32;
   const int lane = threadIdx.x & 31;
-  const int64_t M = args.M, N = args.N;
-  const int64_t m0 = (tile % m_tiles) * kBlockM;
-  const int64_t n0 = (tile / m_tiles) * BN;
-  const int row = quarter * 32 + lane;
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  // The other ranks' SMs (workspace slots), read before the accumulator is
+  // ready.  Every rank is alive until it has passed the cluster barrier,
+  // which it cannot do before this rank arrives there.
+  uint32_t peer[kSplit];
+#pragma unroll
+  for (int r = 0; r < kSplit; ++r)
+    peer[r] = ld_cluster_u32(mapa_shared(smem_u32(&ctl->my_sm), static_cast<uint32_t>(r)));
   const bool got = ovb_wait(smem_u32(&ctl->tfull[0]), 0u, abort);
   if (!__all_sync(0xffffffffu, got) && lane == 0) {
     atomicOr(&g_status_f16, kErrEpilogue);
     *abort = 1;
   }
   tc_fence_after();
-  // 1. Send the partials of the chunks other ranks own (also after a failed
-  //    wait, so that every arrival the owners count is made).
+  const int c4 = (lane & 7) * 4;
 #pragma unroll
   for (int c = eh; c < kChunks; c += 2) {
     const int o = (c * 32) / T::kOwn;
@@ -642,76 +763,127 @@ __device__ __forceinline__ void epilogue_split(const GemmArgs& args, CtlH* ctl,
     uint32_t v[32];
     tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(c * 32), v);
     tc_wait_ld32(v);
-    const int slot = rank < o ? rank : rank - 1;
-    const uint32_t local =
-        smem_u32(recv + (static_cast<size_t>(slot) * kBlockM + row) * T::kRecvStride +
-                 (c * 32 - o * T::kOwn));
-    const uint32_t remote = mapa_shared(local, static_cast<uint32_t>(o));
+    stage_chunk(stg, v);
+    __syncwarp();
+    uint32_t sm = 0;
 #pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      st_cluster_v4(remote + j * 4, __uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                    __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-    mbar_arrive_remote(mapa_shared(smem_u32(&ctl->recv), static_cast<uint32_t>(o)));
-  }
-  // 2. The owned chunks: wait for the partners, sum in rank order, store.
-  bool mine = false;
+    for (int r = 0; r < kSplit; ++r)
+      if (r == o) sm = peer[r];
+    if (sm < static_cast<uint32_t>(kSplitSlots)) {
+      const int slot = rank < o ? rank : rank - 1;
+      float* dst = args.split_ws + static_cast<size_t>(sm) * (kSplitSlotBytes / 4) +
+                   static_cast<size_t>(slot) * T::kPartialFloats +
+                   static_cast<size_t>(quarter * 32) * T::kOwn + (c * 32 - o * T::kOwn);
 #pragma unroll
-  for (int c = eh; c < kChunks; c += 2) mine = mine || ((c * 32) / T::kOwn == rank);
-  if (!mine) return;
-  const bool all_in = ovb_wait_cluster(smem_u32(&ctl->recv), 0u, abort);
-  if (!__all_sync(0xffffffffu, all_in)) {
-    if (lane == 0) {
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        *reinterpret_cast<float4*>(dst + r * T::kOwn + c4) =
+            *reinterpret_cast<const float4*>(stg + r * kStgStrideF + c4);
+      }
+    } else if (lane == 0) {
       atomicOr(&g_status_f16, kErrEpilogue);
-      *abort = 1;
     }
-    return;
+    __syncwarp();
   }
+}
+
+// Both warps of a lane quarter (eh = 0, 1) reduce each owned chunk, warp eh
+// the rows 16*eh .. 16*eh + 15 of the quarter (row groups it = 4*eh ..
+// 4*eh + 3), so that every residual and partial load of a thread is issued
+// in one predicated batch before the sums.
+template <int BN, int kSplit>
+__device__ __forceinline__ void split_finish(const GemmArgs& args, CtlH* ctl,
+                                             uint32_t tmem_base, float* stg, int quarter, int eh,
+                                             int rank, int64_t tile, int64_t m_tiles) {
+  using T = TileH<BN, false, kSplit>;
+  constexpr int kOC = T::kOwn / 32;  // chunks owned per rank
+  constexpr int kP = kSplit - 1;     // partials per element from the other ranks
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const int64_t m0 = (tile % m_tiles) * kBlockM;
+  const int64_t n0 = (tile / m_tiles) * BN;
   const int64_t r0 = m0 + quarter * 32;
   const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const uint32_t sm = ctl->my_sm;
+  const bool have = sm < static_cast<uint32_t>(kSplitSlots);
+  const int c4 = (lane & 7) * 4;
+  const int it0 = eh * 4;
 #pragma unroll
-  for (int c = eh; c < kChunks; c += 2) {
-    if ((c * 32) / T::kOwn != rank) continue;
+  for (int k = 0; k < kOC; ++k) {
+    const int c = rank * kOC + k;  // chunk of the tile
+    const int64_t nc = n0 + c * 32;
+    if (nc >= N || rows <= 0) continue;  // uniform per warp
+    int si = 0;
+#pragma unroll
+    for (int q = 1; q < kMaxSlices; ++q)
+      if (q < args.n_slices && nc >= args.slices[q].n_begin) si = q;
+    const SliceOut so = args.slices[si];
+    const int64_t local = nc - so.n_begin;
+    const int ncols = static_cast<int>(so.n_count - local < 32 ? so.n_count - local : 32);
+    float* cbase = so.C + r0 * so.ldc + local;
+    const bool vec = rows_aligned(so);
+    const float* part = args.split_ws + static_cast<size_t>(have ? sm : 0) * (kSplitSlotBytes / 4) +
+                        static_cast<size_t>(quarter * 32) * T::kOwn + k * 32 + c4;
+    // One batch of loads: the residual (float4 path) and the partials.
+    float4 old[4];
+    if (vec && args.accumulate) {
+      load_residual<4>(cbase, so.ldc, rows, ncols, it0, old);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) old[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float4 pr[kP][4];
+#pragma unroll
+    for (int sl = 0; sl < kP; ++sl)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        pr[sl][i] = ld_f4_cg_if(part + static_cast<size_t>(sl) * T::kPartialFloats +
+                                    ((it0 + i) * 4 + (lane >> 3)) * T::kOwn,
+                                have);
+    const float wl = lane < ncols ? __ldg(args.wscale + nc + lane) : 0.f;
+    float ws[4];
+    gather_ws4(wl, ws);
     uint32_t v[32];
     tmem_ld32(tmem_base + lane_off + static_cast<uint32_t>(c * 32), v);
     tc_wait_ld32(v);
-    const int col = c * 32 - rank * T::kOwn;
-    float sum[32];
+    stage_chunk(stg, v);
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
-    for (int r = 0; r < kSplit; ++r) {
-      if (r == rank) {
+    for (int i = 0; i < 4; ++i) {
+      const int r = (it0 + i) * 4 + (lane >> 3);
+      float* own_p = stg + r * kStgStrideF + c4;
+      const float4 own = *reinterpret_cast<const float4*>(own_p);
+      // Ranks in order 0 .. kSplit-1; rank q's partial is in sender slot
+      // q (q < rank) or q - 1 (q > rank).
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          sum[j] = r == 0 ? __uint_as_float(v[j]) : __fadd_rn(sum[j], __uint_as_float(v[j]));
-      } else {
-        const int slot = r < rank ? r : r - 1;
-        const float* src =
-            recv + (static_cast<size_t>(slot) * kBlockM + row) * T::kRecvStride + col;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 p = *reinterpret_cast<const float4*>(src + j);
-          const float pv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) sum[j + q] = r == 0 ? pv[q] : __fadd_rn(sum[j + q], pv[q]);
+      for (int q = 0; q < kSplit; ++q) {
+        float4 p = own;
+        if (q < kP && q < rank) p = pr[q < kP ? q : 0][i];
+        if (q >= 1 && q > rank) p = pr[q >= 1 ? q - 1 : 0][i];
+        if (q == 0) {
+          sum = p;
+        } else {
+          sum.x = __fadd_rn(sum.x, p.x);
+          sum.y = __fadd_rn(sum.y, p.y);
+          sum.z = __fadd_rn(sum.z, p.z);
+          sum.w = __fadd_rn(sum.w, p.w);
         }
       }
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) stg[lane * kStgStrideF + j] = sum[j];
-    __syncwarp();
-    const int64_t nc = n0 + c * 32;
-    if (nc < N && rows > 0) {
-      int si = 0;
-#pragma unroll
-      for (int k = 1; k < kMaxSlices; ++k)
-        if (k < args.n_slices && nc >= args.slices[k].n_begin) si = k;
-      const SliceOut so = args.slices[si];
-      const int64_t local = nc - so.n_begin;
-      if (lane < so.n_count - local) {
-        const float ws = __ldg(args.wscale + nc + lane);
-        store_rows(stg + lane, kStgStrideF, so.C + r0 * so.ldc + local + lane, so.ldc, rows, ws,
-                   args.accumulate);
+      if (vec) {
+        if (r < rows && c4 < ncols)
+          put4(cbase, so.ldc, r, c4, ncols, scale_add4(sum, ws, old[i], args.accumulate));
+      } else {
+        *reinterpret_cast<float4*>(own_p) = sum;
       }
+    }
+    if (!vec) {  // scalar path: this warp's 16 rows, lane = column
+      __syncwarp();
+      const int rows_w = rows - 16 * eh < 16 ? rows - 16 * eh : 16;
+      if (lane < ncols && rows_w > 0)
+        store_rows(stg + 16 * eh * kStgStrideF + lane, kStgStrideF, cbase + 16 * eh * so.ldc + lane,
+                   so.ldc, rows_w, wl, args.accumulate);
     }
     __syncwarp();
   }
@@ -727,8 +899,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(T::kStages) * T::kStageBytes);
-  float* recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
-  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(recv) + T::kRecvBytes);
+  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -759,11 +930,8 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     }
     for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
-    // Split-K: every sender thread of every partner arrives once per owned
-    // chunk: (kSplit - 1) ranks x (owned chunks) x 4 lane quarters x 32.
-    mbar_init(smem_u32(&ctl->recv),
-              kSplit > 1 ? static_cast<uint32_t>((kSplit - 1) * (T::kOwn / 32) * 128) : 1u);
     ctl->abort = 0;
+    ctl->my_sm = sm_id();  // read by the cluster's other ranks after cluster_sync
     fence_mbar_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_w);
@@ -774,7 +942,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (kSplit > 1) cluster_sync();  // partners' `recv` barriers are initialised
+  if constexpr (kSplit > 1) cluster_sync();  // every rank has started; my_sm is set
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   pdl_wait();  // the preceding kernel's outputs (A, residual C) are complete
@@ -866,9 +1034,9 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     // ------------------------------------------------------------ epilogue
     if constexpr (kSplit > 1) {
       if (my_tiles > 0)
-        epilogue_split<BN, kSplit>(args, ctl, abort, tmem_base,
-                                   stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), recv,
-                                   warp & 3, (warp - kFirstEpiH) >> 2, rank, tile0, m_tiles);
+        split_send<BN, kSplit>(args, ctl, abort, tmem_base,
+                               stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                               (warp - kFirstEpiH) >> 2, rank);
     } else if constexpr (kSilu) {
       epilogue_silu_loop<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, warp & 3,
                                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
@@ -880,11 +1048,18 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     }
   }
 
+  if constexpr (kSplit > 1) {
+    // Every rank's partials are in their owners' workspace slots (release /
+    // acquire at cluster scope covers the global stores); then the owners
+    // reduce.  Executed by every thread of the cluster.
+    cluster_sync();
+    if (warp >= kFirstEpiH && my_tiles > 0)
+      split_finish<BN, kSplit>(args, ctl, tmem_base,
+                               stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                               (warp - kFirstEpiH) >> 2, rank, tile0, m_tiles);
+  }
   tc_fence_before();
   __syncthreads();
-  // Split-K: no CTA leaves (releasing its shared memory) while a partner may
-  // still store into it or arrive on its barrier.
-  if constexpr (kSplit > 1) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemColsF);

@@ -56,6 +56,24 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// The same launch without the PDL attribute, for the quantisers: they
+// start only after the preceding GEMM has finished.  (With PDL their blocks
+// became resident and waited on the SMs while the GEMM ran, which slowed the
+// RMSNorm-quantise + GEMM pair of the layer by ~3.8 us at M = 400.)  Their
+// own griddepcontrol.launch_dependents still lets the next GEMM start early.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_plain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Rows / columns per GEMM output tile; bytes of K per TMA box (four 32-k
 // quantisation blocks, one 128-byte swizzle row).
 constexpr int kBlockM = 128;
@@ -98,7 +116,21 @@ struct GemmArgs {
   float* silu_asc;
   int silu_mode;
   int64_t silu_kp;
+  // Split-K workspace of the device (fp16 mainloop, kSplit > 1 configs):
+  // kSplitSlots slots of kSplitSlotBytes, slot i used only by the CTA
+  // running on the SM with %smid == i.
+  float* split_ws;
 };
+
+// The split-K workspace: one slot per SM id (%smid < kSplitSlots), each large
+// enough for the partial accumulators an owner CTA receives, (kSplit - 1) x
+// 128 rows x (BN / kSplit) floats, at most 3 x 128 x 32 x 4 bytes.
+constexpr int kSplitSlots = 256;
+constexpr size_t kSplitSlotBytes = 48 * 1024;
+// The device's split-K workspace (allocated with its first fp16 weight), or
+// null when none could be allocated -- then no split-K config is launched.
+float* split_workspace(int device);
+bool ensure_split_workspace(int device);
 
 // Thread-local error message (ovb_last_error).
 void set_error(const std::string& msg);

@@ -74,32 +74,45 @@ __device__ __forceinline__ bool ovb_wait(uint32_t bar, uint32_t parity, volatile
   }
 }
 
-// Bounded wait with cluster-scope acquire: sees shared-memory writes that
-// other CTAs of the cluster made before their release-arrive on this barrier.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
+// 16-byte global load that only happens when `pred` holds (else zeros);
+// predicated rather than branched, so that a batch of them is in flight
+// together.  The .cg form reads through L2 only (data written by other SMs
+// in this kernel).
+__device__ __forceinline__ float4 ld_f4_if(const float* p, bool pred) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q ld.global.v4.f32 {%0, %1, %2, %3}, [%4];\n\t}"
+      : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w)
+      : "l"(p), "r"(static_cast<int>(pred))
       : "memory");
-  return ok != 0;
+  return v;
 }
-
-__device__ __forceinline__ bool ovb_wait_cluster(uint32_t bar, uint32_t parity,
-                                                 volatile int* abort) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) return false;
-  }
+__device__ __forceinline__ float4 ld_f4_cg_if(const float* p, bool pred) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];\n\t}"
+      : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w)
+      : "l"(p), "r"(static_cast<int>(pred))
+      : "memory");
+  return v;
 }
 
 // ------------------------------------------------------ thread-block clusters
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+// Load one 32-bit word from shared memory of the cluster (mapa address).
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -120,18 +133,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
-
-// Arrive (release, cluster scope) on an mbarrier in another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
-               : "memory");
 }
 
 // ------------------------------------------------------------------- TMA

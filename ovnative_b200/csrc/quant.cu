@@ -433,9 +433,9 @@ cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, v
   const dim3 grid(grid_for(M * Kb * 4));
   auto* q8 = static_cast<uint8_t*>(aq);
   switch (mode) {
-    case 0: return launch_pdl(quantize_kernel<0>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
-    case 1: return launch_pdl(quantize_kernel<1>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
-    default: return launch_pdl(quantize_kernel<2>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    case 0: return launch_plain(quantize_kernel<0>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    case 1: return launch_plain(quantize_kernel<1>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    default: return launch_plain(quantize_kernel<2>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
   }
 }
 
@@ -470,21 +470,21 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
     const int sgrid = static_cast<int>(imin64(rows, static_cast<int64_t>(num_sms(dev)) * 16));
     auto* q8s = static_cast<uint8_t*>(aq);
     switch (mode) {
-      case 0: return launch_pdl(rmsnorm_quantize_small_kernel<0>, dim3(sgrid), dim3(kSmallThreads),
+      case 0: return launch_plain(rmsnorm_quantize_small_kernel<0>, dim3(sgrid), dim3(kSmallThreads),
                                 0, s, rows, cols, x, w, eps, q8s, asc);
-      case 1: return launch_pdl(rmsnorm_quantize_small_kernel<1>, dim3(sgrid), dim3(kSmallThreads),
+      case 1: return launch_plain(rmsnorm_quantize_small_kernel<1>, dim3(sgrid), dim3(kSmallThreads),
                                 0, s, rows, cols, x, w, eps, q8s, asc);
-      default: return launch_pdl(rmsnorm_quantize_small_kernel<2>, dim3(sgrid),
+      default: return launch_plain(rmsnorm_quantize_small_kernel<2>, dim3(sgrid),
                                  dim3(kSmallThreads), 0, s, rows, cols, x, w, eps, q8s, asc);
     }
   }
   auto* q8 = static_cast<uint8_t*>(aq);
   switch (mode) {
-    case 0: return launch_pdl(rmsnorm_quantize_kernel<0>, dim3(grid), dim3(warps * 32), smem, s,
+    case 0: return launch_plain(rmsnorm_quantize_kernel<0>, dim3(grid), dim3(warps * 32), smem, s,
                               rows, cols, x, w, eps, q8, asc);
-    case 1: return launch_pdl(rmsnorm_quantize_kernel<1>, dim3(grid), dim3(warps * 32), smem, s,
+    case 1: return launch_plain(rmsnorm_quantize_kernel<1>, dim3(grid), dim3(warps * 32), smem, s,
                               rows, cols, x, w, eps, q8, asc);
-    default: return launch_pdl(rmsnorm_quantize_kernel<2>, dim3(grid), dim3(warps * 32), smem, s,
+    default: return launch_plain(rmsnorm_quantize_kernel<2>, dim3(grid), dim3(warps * 32), smem, s,
                                rows, cols, x, w, eps, q8, asc);
   }
 }
@@ -496,11 +496,11 @@ cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, in
   const dim3 grid(grid_for(M * Kb * 4));
   auto* q8 = static_cast<uint8_t*>(aq);
   switch (mode) {
-    case 0: return launch_pdl(silu_mul_quantize_kernel<0>, grid, dim3(256), 0, s, M, K, gate, ldg,
+    case 0: return launch_plain(silu_mul_quantize_kernel<0>, grid, dim3(256), 0, s, M, K, gate, ldg,
                               up, ldu, q8, asc);
-    case 1: return launch_pdl(silu_mul_quantize_kernel<1>, grid, dim3(256), 0, s, M, K, gate, ldg,
+    case 1: return launch_plain(silu_mul_quantize_kernel<1>, grid, dim3(256), 0, s, M, K, gate, ldg,
                               up, ldu, q8, asc);
-    default: return launch_pdl(silu_mul_quantize_kernel<2>, grid, dim3(256), 0, s, M, K, gate, ldg,
+    default: return launch_plain(silu_mul_quantize_kernel<2>, grid, dim3(256), 0, s, M, K, gate, ldg,
                                up, ldu, q8, asc);
   }
 }

@@ -273,3 +273,30 @@ def test_linear_h_split_k_sliced(cuda, golden, monkeypatch, split):
         for j, c in enumerate(Cs):
             check_tolerance(host(c), golden[f"sliced{i}_C{j}"])
     assert ovb.device_status() == 0
+
+
+# C rows that are not 16-byte aligned take the epilogue's scalar store path
+# (the float4 path needs C and ldc multiples of 4 floats).
+@pytest.mark.parametrize("offset,pad", [(1, 0), (0, 3), (2, 5)])
+@pytest.mark.parametrize("tile_n,split", [(128, 1), (32, 1), (64, 2), (128, 4)])
+def test_linear_h_unaligned_c(cuda, monkeypatch, offset, pad, tile_n, split):
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    monkeypatch.setenv("OVB_GEMM_SPLIT_K", str(split))
+    M, N, K = 150, 256, 1024
+    rng = np.random.default_rng(offset * 7 + pad + tile_n + split)
+    A, W, s = case(rng, M, N, K)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    w = ovb.Weight.from_nk(W, s, f16=True)
+    a16, _ = ovb.s8_nk_quantize(dev(A, cuda), f16=True)
+    aq_h, asc_h = O.quantize(A)
+    buf = torch.full((M, N + offset + pad), float("nan"), device=cuda)
+    C = buf[:, offset:offset + N]
+    ovb.linear_h(a16, w, C)
+    check_tolerance(host(C), O.linear_q(aq_h, asc_h, W, s, K))
+    # the columns around the view are untouched
+    assert torch.isnan(buf[:, :offset]).all() and torch.isnan(buf[:, offset + N:]).all()
+    C.copy_(dev(C0, cuda))
+    ovb.linear_h(a16, w, C, accumulate=True)
+    check_tolerance(host(C), O.linear_q(aq_h, asc_h, W, s, K, C_in=C0))
+    assert ovb.device_status() == 0
+    w.close()
