@@ -376,6 +376,62 @@ __device__ __forceinline__ float silu_up_fast(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
+// Quantise the 32 SiLU outputs of one row's block with the block's absmax
+// rule (gemm.cpp:379-430) into form kQMode (0 int8 q, 1 u8 q + 128, 2 fp16
+// q * scale) at `dst` (shared memory, 32 or 64 bytes, 16-byte chunks
+// XOR-swizzled by `sw`); returns the block scale.  |v * inv| <= 127 for finite
+// v (inv = 127 / amax), so only NaN needs the x86 rule (-> -127), and an fp16
+// value can overflow only if 127 * scale does.
+template <int kQMode>
+__device__ __forceinline__ float quant_row32(const float (&v)[32], uint8_t* dst, int sw,
+                                            bool* range_bad) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  float scale, inv;
+  block_scales(amax, &scale, &inv);
+  int z[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float t = __fmul_rn(v[i], inv);
+    int q = __float2int_rn(t);
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    z[i] = (t == t) ? q : -127;
+  }
+  if constexpr (kQMode == 2) {
+    if (fabsf(__fmul_rn(127.0f, scale)) > 65504.f) *range_bad = true;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const __half2 x = __floats2half2_rn(__fmul_rn(static_cast<float>(z[8 * c + 2 * h]), scale),
+                                            __fmul_rn(static_cast<float>(z[8 * c + 2 * h + 1]), scale));
+        w[h] = *reinterpret_cast<const uint32_t*>(&x);
+      }
+      *reinterpret_cast<uint4*>(dst + 16 * (c ^ sw)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int q = z[16 * c + 4 * h + b];
+          word |= (kQMode == 1 ? static_cast<uint32_t>(q + 128) : static_cast<uint32_t>(q & 0xFF))
+                  << (8 * b);
+        }
+        w[h] = word;
+      }
+      *reinterpret_cast<uint4*>(dst + 16 * (c ^ (sw & 1))) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  return scale;
+}
+
 // The epilogue loop of the fused SiLU*up mode (gate|up weight, rows
 // interleaved in 32-row blocks): chunk 2p of a tile is gate block
 // J = n0/64 + p, chunk 2p+1 the up block J.  The kEpiW epilogue warps are
@@ -383,20 +439,27 @@ __device__ __forceinline__ float silu_up_fast(float g, float u) {
 // p = eh, eh + kEpiW/4, ...: each thread holds one row's 32 gate and 32 up
 // accumulators, forms g = D_g * wscale and u = D_u * wscale per column, then
 // v = silu(g) * u (silu_mul_quantize_f32's formula, ops_cpu.cpp:144-198, with
-// fast exp/division) and quantises the whole 32-column block of its row.
-template <int BN, int kAcc, int kEpiW>
+// fast exp/division) and quantises the whole 32-column block of its row into
+// the warp's staging rows `stg` (32 rows x 64 bytes, 16-byte chunks swizzled
+// so that both the row-per-lane writes and the reads below are free of bank
+// conflicts), from where each store instruction writes whole row segments
+// of 32 / (row bytes / 16) rows.  kQMode is the output form (silu_mode).
+template <int BN, int kAcc, int kEpiW, int kQMode>
 __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_t* tfull,
                                                    volatile int* abort, uint32_t tmem_base,
-                                                   int quarter, int eh, int dfree_bar,
-                                                   int64_t tiles, int64_t m_tiles,
+                                                   uint8_t* stg, int quarter, int eh,
+                                                   int dfree_bar, int64_t tiles, int64_t m_tiles,
                                                    int64_t my_tiles) {
   constexpr int kPairs = BN / 64;
   constexpr int kPerQ = kEpiW / 4;  // warps per lane quarter
   constexpr int kMine = (kPairs + kPerQ - 1) / kPerQ;
+  constexpr int kRowBytes = kQMode == 2 ? 64 : 32;  // one block of a row
+  constexpr int kChunks = kRowBytes / 16;
+  constexpr int kRowsPerStore = 32 / kChunks;
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N;
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-  const int64_t esz = args.silu_mode == 2 ? 2 : 1;
+  const int64_t row_stride = args.silu_kp * (kQMode == 2 ? 2 : 1);  // bytes
   bool range_bad = false;
   int64_t t = 0;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
@@ -420,7 +483,7 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
       }
     } else {
       tc_fence_after();
-      const int64_t m = m0 + quarter * 32 + lane;
+      const int64_t rbase = m0 + quarter * 32;  // first row of this warp
       const uint32_t dcol = tmem_base + lane_off + static_cast<uint32_t>(d * BN);
 #pragma unroll
       for (int i = 0; i < kMine; ++i) {
@@ -440,12 +503,22 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
           const float u = __fmul_rn(__uint_as_float(vu[j]), __shfl_sync(0xffffffffu, wsu[i], j));
           v[j] = silu_up_fast(g, u);
         }
-        if (n0 + p * 64 < N && m < M) {
-          const int64_t J = n0 / 64 + p;
-          const float sc = quant_block32(v, args.silu_out + (m * args.silu_kp + J * 32) * esz,
-                                         args.silu_mode, &range_bad);
-          args.silu_asc[m * (args.silu_kp / 32) + J] = sc;
+        if (n0 + p * 64 >= N) continue;  // uniform per warp
+        const int64_t J = n0 / 64 + p;
+        const float sc = quant_row32<kQMode>(v, stg + lane * 64, (lane >> 1) & 3, &range_bad);
+        if (rbase + lane < M) args.silu_asc[(rbase + lane) * (args.silu_kp / 32) + J] = sc;
+        __syncwarp();
+        uint8_t* out = args.silu_out + rbase * row_stride + J * kRowBytes;
+#pragma unroll
+        for (int it = 0; it < 32 / kRowsPerStore; ++it) {
+          const int r = it * kRowsPerStore + lane / kChunks;
+          const int c = lane % kChunks;
+          const int sw = kQMode == 2 ? ((r >> 1) & 3) : ((r >> 1) & 1);
+          if (rbase + r < M)
+            *reinterpret_cast<uint4*>(out + r * row_stride + 16 * c) =
+                *reinterpret_cast<const uint4*>(stg + r * 64 + 16 * (c ^ sw));
         }
+        __syncwarp();
       }
     }
     tc_fence_before();
@@ -705,7 +778,9 @@ struct TileH {
   static constexpr int kAcc = 2;
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
-  static constexpr size_t kStgAll = kSilu ? 0 : static_cast<size_t>(kEpiW) * 32 * kStgStrideF * 4;
+  // epilogue staging: 32 x 32 fp32 chunks, or 32 rows x 64 bytes of the
+  // fused SiLU*up epilogue's quantised output
+  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4);
   static constexpr int kOwn = BN / kSplit;  // columns owned per rank
   static constexpr size_t kPartialFloats = static_cast<size_t>(kBlockM) * kOwn;  // per sender
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
@@ -1038,9 +1113,22 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
                                stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
                                (warp - kFirstEpiH) >> 2, rank);
     } else if constexpr (kSilu) {
-      epilogue_silu_loop<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, warp & 3,
-                                                (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
-                                                m_tiles, my_tiles);
+      uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
+      const int q = warp & 3, e = (warp - kFirstEpiH) >> 2;
+      switch (args.silu_mode) {  // the output form, a compile-time constant in the loop
+        case 0:
+          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 0>(args, ctl->tfull, abort, tmem_base, stg, q,
+                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
+          break;
+        case 1:
+          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 1>(args, ctl->tfull, abort, tmem_base, stg, q,
+                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
+          break;
+        default:
+          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 2>(args, ctl->tfull, abort, tmem_base, stg, q,
+                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
+          break;
+      }
     } else {
       epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
                                  stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
