@@ -341,32 +341,77 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                                 "unit", "frac", "traffic")} for r in per_gemm]
 
     # ---- end to end through the public API with host buffers
+    # Every step copies its own input from pinned host memory and reads its
+    # result back.  Serial: copy in, step, copy out on one stream.  Pipelined
+    # (the reported value): double-buffered, host->device copies on one copy
+    # stream and device->host on another, overlapping the neighbouring
+    # steps' compute -- how a serving loop drives the layer.
     rng = np.random.default_rng(77)
-    xh_in = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
-    xh_in = xh_in.pin_memory()
-    xh_out = torch.empty_like(xh_in).pin_memory()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
+    h_in = [torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
+            .pin_memory() for _ in range(2)]
+    h_out = [torch.empty_like(h_in[0]).pin_memory() for _ in range(2)]
+    d_in = [torch.empty_like(x) for _ in range(2)]
+    d_out = [torch.empty_like(x) for _ in range(2)]
+    s_in = torch.cuda.Stream(device=dev)
+    s_out = torch.cuda.Stream(device=dev)
+
+    def timed_e2e(pipelined: bool) -> float:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        barrier()
+        torch.cuda.synchronize()
         e0.record(stream)
-        for i in range(args.steps):
-            x.copy_(xh_in, non_blocking=True)
-            graphs[i % N_LAYERS].replay()
-            xh_out.copy_(x, non_blocking=True)
+        if not pipelined:
+            with torch.cuda.stream(stream):
+                for i in range(args.steps):
+                    x.copy_(h_in[0], non_blocking=True)
+                    graphs[i % N_LAYERS].replay()
+                    h_out[0].copy_(x, non_blocking=True)
+        else:
+            s_in.wait_event(e0)
+            s_out.wait_event(e0)
+            for i in range(args.steps):
+                b = i % 2
+                with torch.cuda.stream(s_in):
+                    if i >= 2:
+                        s_in.wait_event(ev_comp[b])  # step i-2 has consumed d_in[b]
+                    d_in[b].copy_(h_in[b], non_blocking=True)
+                    ev_in[b].record(s_in)
+                with torch.cuda.stream(stream):
+                    stream.wait_event(ev_in[b])
+                    if i >= 2:
+                        stream.wait_event(ev_out[b])  # step i-2's result has left d_out[b]
+                    x.copy_(d_in[b], non_blocking=True)
+                    graphs[i % N_LAYERS].replay()
+                    d_out[b].copy_(x, non_blocking=True)
+                    ev_comp[b].record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_comp[b])
+                    h_out[b].copy_(d_out[b], non_blocking=True)
+                    ev_out[b].record(s_out)
+            for b in range(min(2, args.steps)):
+                stream.wait_event(ev_out[b])
         e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    e2e_serial_ms = timed_e2e(False)
+    e2e_ms = timed_e2e(True)
     io_bytes = M_TOKENS * LY.HIDDEN * 4
     e2e = {"value": world * args.steps * ops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
            "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
-           "ms_per_step": e2e_ms / args.steps}
+           "ms_per_step": e2e_ms / args.steps,
+           "mode": "pipelined: double-buffered copies on two copy streams overlap compute",
+           "serial_ms_per_step": e2e_serial_ms / args.steps}
 
     status = ovb.device_status()
     path.release()

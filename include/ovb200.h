@@ -68,7 +68,11 @@ extern "C" {
 #define OVB_WEIGHT_F16 2 /* ovb_weight_create: also keep an fp16 copy; GEMMs with this
                             handle run the fp16 mainloop (see above).  No counterpart
                             in the reference's CPU path; its CUDA runner multiplies
-                            dequantised fp16 weights (cuda_lm.cu:840-873). */
+                            dequantised fp16 weights (cuda_lm.cu:840-873).  The first
+                            such weight on a device also allocates the library's
+                            split-K workspace there (12 MiB, one slot per SM, kept
+                            until exit; safe for concurrent streams).  Without it the
+                            fp16 GEMMs run without split-K. */
 #define OVB_AQ_U8 1      /* quantisers: write reference u8 (q+128) instead of int8 */
 #define OVB_AQ_F16 2     /* quantisers: write fp16(q * asc), [M, Kp] fp16 (2 bytes per
                             element, 16-byte aligned), the input of ovb_linear_h */
