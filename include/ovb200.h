@@ -207,6 +207,31 @@ int ovb_linear_static(int64_t M, const ovb_weight* w, const float* A, int64_t ld
 int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t* P,
                        void* stream);
 
+/* The guided (classifier-free guidance) argmax pass of a TTS step, on device
+ * pointers: for every codebook c < codebooks and target frame t < target_len,
+ * with the cond row at token cond_seq - target_len + t of `cond` and the
+ * uncond row at token t of `uncond` (both planes token-major [seq,
+ * codebooks * vocab] fp32):
+ *   lp_c, lp_u = log_softmax of the two rows;
+ *   mix = log_softmax(lp_c + guidance * (lp_c - lp_u))   (mix = lp_c if guidance == 0);
+ *   mix[mask_id] = -inf (no token is masked if mask_id is outside [0, vocab));
+ *   pred[c * target_len + t] = first argmax of mix;
+ *   scores[c * target_len + t] = max(mix) - c * layer_penalty.
+ * Replaces the reference's CPU loop (cpp/src/model/tts.cpp:291-326, log_softmax
+ * :91-101) and its CUDA guided_sample_kernel (cpp/src/backend/cuda/
+ * cuda_lm.cu:679-758, called by LmRunnerSampleThunk :1228-1262) behind
+ * LM::CudaSampleFn (cpp/src/model/lm.h:106-108; that hook copies pred/scores
+ * back to the host -- see INTEGRATION.md).  pred and scores are device
+ * arrays of codebooks * target_len.  target_len <= 0 or codebooks <= 0
+ * returns OVB_OK without work; cond_seq / uncond_seq < target_len is
+ * OVB_ERR_INVALID_ARG.  Log-probabilities agree with the CPU loop to a few
+ * ulps (its sums run left to right, these in a warp tree), so pred agrees
+ * except where two tokens' scores tie within rounding. */
+int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int uncond_seq,
+                      int codebooks, int vocab, int target_len, float guidance,
+                      float layer_penalty, int mask_id, int32_t* pred, float* scores,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,8 @@ def port_lib():
             "ovo_linear_q": [_i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, C.c_int],
             "ovo_rmsnorm_into": [_p, _p, _p, _i64, _i64, C.c_float],
             "ovo_silu_mul": [_p, _p, _p, _i64],
+            "ovo_guided_sample": [_p, C.c_int, _p, C.c_int, C.c_int, C.c_int, C.c_float,
+                                  C.c_float, C.c_int, C.c_int, _p, _p, _p],
         }.items():
             f = getattr(lib, name)
             f.argtypes = args
@@ -312,3 +314,26 @@ def ref_silu_mul(gate, up):
     out = np.empty_like(gate)
     _chk(ref_lib().ref_silu_mul(_ptr(out), _ptr(gate), _ptr(up), gate.size), "silu_mul_f32")
     return out
+
+
+# ------------------------------------------------------------- sampler
+def guided_sample(cond: np.ndarray, uncond: np.ndarray, T: int, C_books: int, guidance: float,
+                  penalty: float, mask_id: int = 1024, in_place: bool = False):
+    """The guidance + argmax loop of cpp/src/model/tts.cpp:291-326 on
+    token-major planes cond [cond_seq, C*V], uncond [uncond_seq, C*V].
+    in_place=True reproduces the reference's in-place log_softmax of the mix
+    (tts.cpp:313); False gives the log-probabilities it intends.  Returns
+    (pred int32 [C, T], scores float32 [C, T]).  Restatement only (parity
+    unpinned: no reference test or callable reference function covers it)."""
+    cond = _f32(cond)
+    uncond = _f32(uncond)
+    V = cond.shape[1] // C_books
+    assert cond.shape[1] == uncond.shape[1] == C_books * V
+    assert cond.shape[0] >= T and uncond.shape[0] >= T
+    pred = np.zeros((C_books, T), np.int32)
+    scores = np.zeros((C_books, T), np.float32)
+    scratch = np.zeros(4 * V, np.float32)
+    port_lib().ovo_guided_sample(_ptr(cond), cond.shape[0], _ptr(uncond), C_books, V, T,
+                                 guidance, penalty, mask_id, 1 if in_place else 0, _ptr(pred),
+                                 _ptr(scores), _ptr(scratch))
+    return pred, scores

@@ -10,8 +10,15 @@
  * source into oracle/_ref/libovref.so by oracle/Makefile) and against the
  * committed golden vectors in tests/golden/.
  *
+ * Exception: ovo_guided_sample (the sampler, cpp/src/model/tts.cpp:91-101,
+ * :291-326) is a restatement only -- parity unpinned.  The reference's loop
+ * lives inside a Pipeline method and its log_softmax in an anonymous
+ * namespace, so neither can be called on its own, and no reference test or
+ * golden vector covers it.
+ *
  * Reference files cited below are paths inside the OVNative project
- * (cpp/src/backend/cpu/gemm.cpp, cpp/src/backend/cpu/ops_cpu.cpp).
+ * (cpp/src/backend/cpu/gemm.cpp, cpp/src/backend/cpu/ops_cpu.cpp,
+ * cpp/src/model/tts.cpp).
  *
  * Numerics follow the reference operation for operation:
  *   - every product, sum and quotient is a separately rounded IEEE fp32 op
@@ -248,5 +255,71 @@ OVO_API void ovo_silu_mul(float* out, const float* gate, const float* up, int64_
   for (; i < n; ++i) {
     const float d = 1.f + expf(-gate[i]);
     out[i] = (gate[i] / d) * up[i];
+  }
+}
+
+/* ------------------------------------------------ guided argmax (sampler)
+ * log_softmax: cpp/src/model/tts.cpp:91-101, operation for operation (max
+ * as std::max(m, x) = m < x ? x : m; exp values summed left to right; then
+ * x - lse).  `out` may be `x`, as in the reference's call at tts.cpp:313 --
+ * its third loop then reads the exp values the second loop stored. */
+static void log_softmax_ref(const float* x, int n, float* out) {
+  float m = -INFINITY;
+  for (int i = 0; i < n; ++i) m = (m < x[i]) ? x[i] : m;
+  float sum = 0.f;
+  for (int i = 0; i < n; ++i) {
+    out[i] = expf(x[i] - m);
+    sum += out[i];
+  }
+  const float lse = logf(sum) + m;
+  for (int i = 0; i < n; ++i) out[i] = x[i] - lse;
+}
+
+/* The per-step guidance + argmax loop, cpp/src/model/tts.cpp:291-326 (the
+ * non-B2 plane layout: cond row at token cond_seq - T + t, uncond row at
+ * token t of its own plane, both [seq, C * V]).  in_place != 0 reproduces
+ * the reference's in-place log_softmax of the mix (tts.cpp:313, scores
+ * exp(mix - max) - lse); in_place == 0 gives the log-probabilities that
+ * call intends, which the reference's CUDA kernel computes
+ * (cpp/src/backend/cuda/cuda_lm.cu:717-740).  pred is the same either way.
+ * mask_id outside [0, V) masks nothing.  scratch: 4 * V floats. */
+OVO_API void ovo_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
+                               int V, int T, float guidance, float penalty, int mask_id,
+                               int in_place, int32_t* pred, float* scores, float* scratch) {
+  float* lp_c = scratch;
+  float* lp_u = scratch + V;
+  float* mix = scratch + 2 * (int64_t)V;
+  float* mix2 = scratch + 3 * (int64_t)V;
+  const int64_t CV = (int64_t)C * V;
+  for (int64_t idx = 0; idx < (int64_t)C * T; ++idx) {
+    const int c = (int)(idx / T);
+    const int t = (int)(idx - (int64_t)c * T);
+    const float* lc = cond + ((int64_t)cond_seq - T + t) * CV + (int64_t)c * V;
+    const float* lu = uncond + (int64_t)t * CV + (int64_t)c * V;
+    log_softmax_ref(lc, V, lp_c);
+    log_softmax_ref(lu, V, lp_u);
+    float* lp_mix = mix;
+    if (guidance != 0.f) {
+      for (int v = 0; v < V; ++v) mix[v] = lp_c[v] + guidance * (lp_c[v] - lp_u[v]);
+      if (in_place) {
+        log_softmax_ref(mix, V, mix);
+      } else {
+        log_softmax_ref(mix, V, mix2);
+        lp_mix = mix2;
+      }
+    } else {
+      memcpy(mix, lp_c, sizeof(float) * (size_t)V);
+    }
+    if (mask_id >= 0 && mask_id < V) lp_mix[mask_id] = -INFINITY;
+    int best = 0;
+    float best_val = -INFINITY;
+    for (int v = 0; v < V; ++v) {
+      if (lp_mix[v] > best_val) {
+        best_val = lp_mix[v];
+        best = v;
+      }
+    }
+    pred[idx] = best;
+    scores[idx] = best_val - (float)c * penalty;
   }
 }

@@ -3,7 +3,8 @@
 The product is libovb200.so (CUDA kernels for sm_100a behind the C ABI in
 include/ovb200.h).  This package loads it and mirrors the reference's
 ov_gemm.h interface on torch CUDA tensors (gemm.py), and adds the per-layer
-linear sequence of LM::run_layer (layer.py) used by the benchmark.
+linear sequence of LM::run_layer (layer.py) used by the benchmark, and the
+guided argmax pass of the TTS step (sampler.py).
 """
 from ._lib import LIB_PATH, OvbError, lib  # noqa: F401
 from .gemm import (  # noqa: F401
@@ -28,3 +29,4 @@ from .gemm import (  # noqa: F401
     silu_mul_quantize_f32,
     workspace_bytes,
 )
+from .sampler import guided_sample  # noqa: F401

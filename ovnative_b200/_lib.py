@@ -57,6 +57,8 @@ SIGNATURES = {
     "ovb_linear": ([_i64, _p, _p, _i64, _p, _i64, _int, _p, C.c_size_t, _p], _int),
     "ovb_linear_static": ([_i64, _p, _p, _i64, _p, _i64, _int, _p], _int),
     "ovb_block_products": ([_i64, _p, _p, _p, _p], _int),
+    "ovb_guided_sample": ([_p, _int, _p, _int, _int, _int, _int, C.c_float, C.c_float, _int,
+                           _p, _p, _p], _int),
 }
 
 _lib = None

@@ -718,4 +718,25 @@ int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t
                   as_stream(stream));
 }
 
+int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int uncond_seq,
+                      int codebooks, int vocab, int target_len, float guidance,
+                      float layer_penalty, int mask_id, int32_t* pred, float* scores,
+                      void* stream) {
+  if (target_len <= 0 || codebooks <= 0) return OVB_OK;
+  if (!cond || !uncond || !pred || !scores) return invalid("cond/uncond/pred/scores must be non-null");
+  if (vocab <= 0) return invalid("vocab must be positive");
+  if (cond_seq < target_len || uncond_seq < target_len)
+    return invalid("cond_seq and uncond_seq must be >= target_len");
+  if (!aligned(cond, 4) || !aligned(uncond, 4) || !aligned(pred, 4) || !aligned(scores, 4))
+    return invalid("misaligned sampler buffer");
+  if (static_cast<int64_t>(codebooks) * target_len > (int64_t{1} << 31) - 1)
+    return invalid("codebooks * target_len exceeds 2^31-1");
+  if (cuda_failed(ovb::launch_guided_sample(cond, cond_seq, uncond, codebooks, vocab, target_len,
+                                            guidance, layer_penalty, mask_id, pred, scores,
+                                            as_stream(stream)),
+                  "guided sample launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
 }  // extern "C"

@@ -168,6 +168,10 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtyp
                     uint32_t box_rows, CUtensorMapSwizzle swizzle);
 // int8 [n] -> fp16 [n] (exact for |v| <= 2048).
 cudaError_t launch_widen_f16(const int8_t* src, int64_t n, uint16_t* dst, cudaStream_t s);
+// The guided argmax pass (sampler.cu): one warp per (codebook, frame) row.
+cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
+                                 int V, int T, float guidance, float penalty, int mask_id,
+                                 int32_t* pred, float* scores, cudaStream_t s);
 // Index into kTileNF of the tile width used by the fp16 mainloop.
 int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device);
 cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,

@@ -1,0 +1,44 @@
+"""The guided (classifier-free guidance) argmax pass of a TTS step
+(ovb_guided_sample) on torch CUDA tensors.
+
+Mirrors the accelerator hook LM::CudaSampleFn (cpp/src/model/lm.h:106-108):
+the reference's CPU loop cpp/src/model/tts.cpp:291-326 computes, for every
+codebook c and target frame t,
+
+    lp_c, lp_u = log_softmax(cond row), log_softmax(uncond row)
+    mix = log_softmax(lp_c + g * (lp_c - lp_u))      (mix = lp_c if g == 0)
+    mix[mask_id] = -inf; pred = argmax(mix); score = max(mix) - c * layer_penalty
+
+with the cond row at token cond_seq - T + t and the uncond row at token t of
+token-major [seq, C * V] logits planes.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+MASK_ID = 1024  # the audio vocabulary's mask token (cpp/src/model/tts.cpp:17)
+
+
+def guided_sample(cond: torch.Tensor, uncond: torch.Tensor, target_len: int, codebooks: int,
+                  guidance: float, layer_penalty: float, mask_id: int = MASK_ID,
+                  pred: torch.Tensor | None = None, scores: torch.Tensor | None = None):
+    """cond [cond_seq, codebooks * V] and uncond [uncond_seq, codebooks * V],
+    fp32 CUDA, rows contiguous.  Returns (pred int32, scores fp32), each
+    [codebooks, target_len] (index c * target_len + t)."""
+    for name, t in (("cond", cond), ("uncond", uncond)):
+        if not t.is_cuda or t.dtype != torch.float32 or t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 2-D float32 CUDA tensor")
+    if cond.shape[1] != uncond.shape[1] or cond.shape[1] % codebooks:
+        raise ValueError("cond/uncond widths must both be codebooks * vocab")
+    V = cond.shape[1] // codebooks
+    if pred is None:
+        pred = torch.empty((codebooks, target_len), dtype=torch.int32, device=cond.device)
+    if scores is None:
+        scores = torch.empty((codebooks, target_len), dtype=torch.float32, device=cond.device)
+    L.check(L.lib().ovb_guided_sample(cond.data_ptr(), cond.shape[0], uncond.data_ptr(),
+                                      uncond.shape[0], codebooks, V, target_len, float(guidance),
+                                      float(layer_penalty), mask_id, pred.data_ptr(),
+                                      scores.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    return pred, scores
