@@ -597,7 +597,16 @@ def main():
     ap.add_argument("--numerics", choices=["fp16", "exact"], default="fp16")
     ap.add_argument("--skip-other", action="store_true",
                     help="do not time the other numerics path (for profiling runs)")
+    ap.add_argument("--sampler-only", action="store_true",
+                    help="only time the guided sampler (one plane set, 8 launches; for "
+                         "profiling runs) and print its entry")
     args = ap.parse_args()
+    if args.sampler_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(time_sampler(dev, torch.cuda.Stream(device=dev), launches=8, sets=1)),
+              flush=True)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     rank = env_int("RANK", 0)
