@@ -132,6 +132,18 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// First row / column of output tile `tile` (tiles are numbered m-fastest).
+// 32-bit arithmetic: a 64-bit division is a long dependent software
+// sequence (~0.4 us on a kernel's critical path); the launchers keep the
+// tile count below 2^31.
+__device__ __forceinline__ void tile_origin(int64_t tile, int64_t m_tiles, int bn, int64_t* m0,
+                                            int64_t* n0) {
+  const uint32_t t = static_cast<uint32_t>(tile), mt = static_cast<uint32_t>(m_tiles);
+  const uint32_t q = t / mt;
+  *m0 = static_cast<int64_t>(t - q * mt) * kBlockM;
+  *n0 = static_cast<int64_t>(q) * bn;
+}
+
 __device__ __forceinline__ void fail(CtlF* ctl, int code) {
   atomicOr(&g_status_f16, code);
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
@@ -314,8 +326,8 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
     const int d = static_cast<int>(t % kAcc);
     const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
-    const int64_t m0 = (tile % m_tiles) * kBlockM;
-    const int64_t n0 = (tile / m_tiles) * BN;
+    int64_t m0, n0;
+    tile_origin(tile, m_tiles, BN, &m0, &n0);
     float wsv[kMine];
 #pragma unroll
     for (int i = 0; i < kMine; ++i) {
@@ -465,8 +477,8 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
     const int d = static_cast<int>(t % kAcc);
     const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
-    const int64_t m0 = (tile % m_tiles) * kBlockM;
-    const int64_t n0 = (tile / m_tiles) * BN;
+    int64_t m0, n0;
+    tile_origin(tile, m_tiles, BN, &m0, &n0);
     float wsg[kMine], wsu[kMine];
 #pragma unroll
     for (int i = 0; i < kMine; ++i) {
@@ -582,8 +594,9 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       int64_t st = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
-        const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
+        int64_t m0l, n0l;
+        tile_origin(tile, m_tiles, BN, &m0l, &n0l);
+        const int32_t m0 = static_cast<int32_t>(m0l), n0 = static_cast<int32_t>(n0l);
         for (int j = 0; j < ksteps; ++j, ++st) {
           const int s = static_cast<int>(st % kStagesF);
           const uint32_t ph = static_cast<uint32_t>((st / kStagesF) & 1);
@@ -653,7 +666,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
     int64_t st = 0;
     bool range_ok = true;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-      const int64_t m = (tile % m_tiles) * kBlockM + r;
+      const int64_t m = static_cast<int64_t>(static_cast<uint32_t>(tile) % static_cast<uint32_t>(m_tiles)) * kBlockM + r;
       const bool row_ok = m < M;
       const float* asc_row = args.asc + (row_ok ? m : 0) * static_cast<int64_t>(Kb);
       auto scale_of = [&](int j) -> float {
@@ -875,8 +888,8 @@ __device__ __forceinline__ void split_finish(const GemmArgs& args, CtlH* ctl,
   constexpr int kP = kSplit - 1;     // partials per element from the other ranks
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N;
-  const int64_t m0 = (tile % m_tiles) * kBlockM;
-  const int64_t n0 = (tile / m_tiles) * BN;
+  int64_t m0, n0;
+  tile_origin(tile, m_tiles, BN, &m0, &n0);
   const int64_t r0 = m0 + quarter * 32;
   const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -1029,13 +1042,15 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
       int64_t st = 0;
       bool ok = true;
       for (int64_t tile = tile0; tile < tiles && ok; tile += tile_step) {
-        const int32_t m0 = static_cast<int32_t>((tile % m_tiles) * kBlockM);
-        const int32_t n0 = static_cast<int32_t>((tile / m_tiles) * BN);
+        int64_t m0l, n0l;
+        tile_origin(tile, m_tiles, BN, &m0l, &n0l);
+        const int32_t m0 = static_cast<int32_t>(m0l), n0 = static_cast<int32_t>(n0l);
         for (int jj = 0; jj < ksteps; ++jj, ++st) {
           const int j = j_begin + jj;
           const int s = static_cast<int>(st % T::kStages);
           const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
-          if (!ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
+          // The ring's first pass needs no wait: those stages were never used.
+          if (st >= T::kStages && !ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
             atomicOr(&g_status_f16, kErrProducer);
             *abort = 1;
             ok = false;
@@ -1169,6 +1184,7 @@ cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
     configured_dev = dev;
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
+  if (tiles * 4 > INT32_MAX) return cudaErrorInvalidValue;  // 32-bit tile arithmetic
   if constexpr (kSplit == 1) {
     const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
     return launch_pdl(kernel, dim3(grid), dim3(T::kThreads), T::kSmemBytes, s, tmap_a, tmap_w,
@@ -1209,6 +1225,7 @@ cudaError_t launch_f16_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w
     configured_dev = dev;
   }
   const int64_t tiles = ((args.M + kBlockM - 1) / kBlockM) * ((args.N + BN - 1) / BN);
+  if (tiles * 4 > INT32_MAX) return cudaErrorInvalidValue;  // 32-bit tile arithmetic
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
   return launch_pdl(gemm_f16_kernel<BN>, dim3(grid), dim3(kThreadsF), T::kSmemBytes, s, tmap_a,
                     tmap_w, args);
