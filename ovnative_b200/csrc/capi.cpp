@@ -305,10 +305,10 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
     args.silu_kp = w->glu_inter;
   }
   args.split_ws = ovb::split_workspace(w->device);
-  // configs 0..3 are plain, 4..6 split-K (which needs the workspace), and the
-  // fused SiLU*up epilogue takes BN >= 64 without split-K (0..2)
-  const int config =
-      ovb::pick_tile_h(M, w->N, w->Kb, w->device, silu ? 3 : (args.split_ws ? 7 : 4));
+  // split-K configurations need the workspace; the fused SiLU*up epilogue
+  // takes BN >= 64 without split-K
+  const int config = ovb::pick_tile_h(
+      M, w->N, w->Kb, w->device, silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit));
   const int width = ovb::kHConfigs[config].width;
   if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;

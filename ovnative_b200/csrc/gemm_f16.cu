@@ -316,14 +316,15 @@ template <int BN, int kAcc, bool kPipe = true>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull,
                                               volatile int* abort, uint32_t tmem_base,
                                               float* stg, int quarter, int eh, int dfree_bar,
-                                              int64_t tiles, int64_t m_tiles, int64_t my_tiles) {
+                                              int64_t tiles, int64_t m_tiles, int64_t my_tiles,
+                                              int64_t tile_first, int64_t tile_step) {
   constexpr int kChunks = BN / 32;
   constexpr int kMine = (kChunks + 1) / 2;  // chunks per warp (at most)
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N;
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
   int64_t t = 0;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+  for (int64_t tile = tile_first; tile < tiles; tile += tile_step, ++t) {
     const int d = static_cast<int>(t % kAcc);
     const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
     int64_t m0, n0;
@@ -461,7 +462,8 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
                                                    volatile int* abort, uint32_t tmem_base,
                                                    uint8_t* stg, int quarter, int eh,
                                                    int dfree_bar, int64_t tiles, int64_t m_tiles,
-                                                   int64_t my_tiles) {
+                                                   int64_t my_tiles, int64_t tile_first,
+                                                   int64_t tile_step) {
   constexpr int kPairs = BN / 64;
   constexpr int kPerQ = kEpiW / 4;  // warps per lane quarter
   constexpr int kMine = (kPairs + kPerQ - 1) / kPerQ;
@@ -474,7 +476,7 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
   const int64_t row_stride = args.silu_kp * (kQMode == 2 ? 2 : 1);  // bytes
   bool range_bad = false;
   int64_t t = 0;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+  for (int64_t tile = tile_first; tile < tiles; tile += tile_step, ++t) {
     const int d = static_cast<int>(t % kAcc);
     const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
     int64_t m0, n0;
@@ -537,6 +539,33 @@ __device__ __forceinline__ void epilogue_silu_loop(const GemmArgs& args, uint64_
     if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiW + 1));
   }
   if (range_bad) atomicOr(&g_status_f16, kErrF16Range);
+}
+
+// epilogue_silu_loop with the output form args.silu_mode as a compile-time
+// constant; the staging rows are the warp's 32 x 64 bytes at `stg`.
+template <int BN, int kAcc, int kEpiW>
+__device__ __forceinline__ void silu_epilogue(const GemmArgs& args, uint64_t* tfull,
+                                              volatile int* abort, uint32_t tmem_base,
+                                              uint8_t* stg, int quarter, int eh, int dfree_bar,
+                                              int64_t tiles, int64_t m_tiles, int64_t my_tiles,
+                                              int64_t tile_first, int64_t tile_step) {
+  switch (args.silu_mode) {
+    case 0:
+      epilogue_silu_loop<BN, kAcc, kEpiW, 0>(args, tfull, abort, tmem_base, stg, quarter, eh,
+                                             dfree_bar, tiles, m_tiles, my_tiles, tile_first,
+                                             tile_step);
+      break;
+    case 1:
+      epilogue_silu_loop<BN, kAcc, kEpiW, 1>(args, tfull, abort, tmem_base, stg, quarter, eh,
+                                             dfree_bar, tiles, m_tiles, my_tiles, tile_first,
+                                             tile_step);
+      break;
+    default:
+      epilogue_silu_loop<BN, kAcc, kEpiW, 2>(args, tfull, abort, tmem_base, stg, quarter, eh,
+                                             dfree_bar, tiles, m_tiles, my_tiles, tile_first,
+                                             tile_step);
+      break;
+  }
 }
 
 template <int BN>
@@ -733,7 +762,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
     epilogue_loop<BN, T::kAcc, false>(args, ctl->tfull, abort, tmem_base,
                                       stg_all + (warp - kFirstEpi) * (32 * kStgStrideF), warp & 3,
                                       (warp - kFirstEpi) >> 2, kBarDfree, tiles, m_tiles,
-                                      my_tiles);
+                                      my_tiles, blockIdx.x, gridDim.x);
   }
 
   tc_fence_before();
@@ -1129,25 +1158,14 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
                                (warp - kFirstEpiH) >> 2, rank);
     } else if constexpr (kSilu) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
-      const int q = warp & 3, e = (warp - kFirstEpiH) >> 2;
-      switch (args.silu_mode) {  // the output form, a compile-time constant in the loop
-        case 0:
-          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 0>(args, ctl->tfull, abort, tmem_base, stg, q,
-                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
-          break;
-        case 1:
-          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 1>(args, ctl->tfull, abort, tmem_base, stg, q,
-                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
-          break;
-        default:
-          epilogue_silu_loop<BN, T::kAcc, T::kEpiW, 2>(args, ctl->tfull, abort, tmem_base, stg, q,
-                                                       e, kBarDfreeH, tiles, m_tiles, my_tiles);
-          break;
-      }
+      silu_epilogue<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
+                                           (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles,
+                                           my_tiles, blockIdx.x, gridDim.x);
     } else {
       epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
                                  stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles);
+                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles,
+                                 blockIdx.x, gridDim.x);
     }
   }
 
@@ -1210,6 +1228,218 @@ cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair fp16 mainloop (tcgen05 cta_group::2).  Two CTAs of a 2-CTA
+// cluster compute one 256 x BN output tile: rank r TMA-loads its 128 rows of
+// A' and rows [r * BN/2, (r + 1) * BN/2) of the W tile into its own shared
+// memory; the leader (rank 0) issues tcgen05.mma.cta_group::2 with M = 256,
+// which reads both CTAs' operands (each W half once, shared by both SMs'
+// tensor cores), and each CTA's TMEM receives its 128 rows x BN columns.
+// This halves the W bytes each SM loads per tile, the mainloop's bound at
+// M = 400 (L2-to-SM traffic).
+//   - Both CTAs' loads complete on the leader's `full[s]` barrier, which the
+//     leader alone arms with both CTAs' bytes (its producer); the peer's
+//     producer waits only on its own `empty[s]`.
+//   - The leader's commits arrive on `empty[s]` and `tfull` of both CTAs
+//     (multicast to cluster ranks 0 and 1).
+//   - TMEM is allocated and freed collectively by warp 1 of both CTAs.
+// One tile per cluster; the epilogues are the single-CTA ones on the CTA's
+// 128-row tile (a virtual 128-row tiling of 2 * m_pairs row tiles).
+template <int BN, bool kSilu>
+struct TileH2 {
+  static_assert(BN == 256 || BN == 128, "pair tile widths");
+  static constexpr uint32_t kWBytes = (BN / 2) * 128;  // this CTA's half of the W rows
+  static constexpr uint32_t kStageBytes = kABytesH + kWBytes;
+  static constexpr int kEpiW = epi_warps_h<kSilu>();
+  static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
+  static constexpr size_t kStgAll =
+      static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4);
+  static constexpr int kStagesFit =
+      static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
+  static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
+  static constexpr size_t kSmemBytes =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kStgAll + sizeof(CtlH);
+  static_assert(kStages >= 3, "too few pipeline stages");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kStageBytes % 1024 == 0, "stage bases stay 1 KB aligned");
+};
+
+template <int BN, bool kSilu>
+__global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
+    gemm_h2_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ GemmArgs args) {
+  using T = TileH2<BN, kSilu>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* stg_all = reinterpret_cast<float*>(smem + static_cast<size_t>(T::kStages) * T::kStageBytes);
+  CtlH* ctl = reinterpret_cast<CtlH*>(reinterpret_cast<uint8_t*>(stg_all) + T::kStgAll);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const int Kb = static_cast<int>(args.Kb);
+  const int rank = static_cast<int>(cluster_ctarank());  // 0: leader, 1: peer
+  const int64_t m_pairs = (M + 2 * kBlockM - 1) / (2 * kBlockM);
+  const uint32_t pair = blockIdx.x >> 1;
+  const uint32_t pm = pair % static_cast<uint32_t>(m_pairs);
+  const uint32_t pn = pair / static_cast<uint32_t>(m_pairs);
+  const int32_t a_row = static_cast<int32_t>((2 * pm + rank) * kBlockM);
+  const int32_t w_row = static_cast<int32_t>(pn * BN + rank * (BN / 2));
+  const int64_t m_tiles_v = 2 * m_pairs;  // the epilogue's 128-row tiling
+  const int64_t vtile = static_cast<int64_t>(pn) * m_tiles_v + 2 * pm + rank;
+  const int ksteps = (Kb + 1) / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::kStages; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&ctl->tmem_base), kTmemColsF);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised and their TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  pdl_wait();  // the preceding kernel's outputs (A, residual C) are complete
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // --------------------------------------------------- producer (both CTAs)
+    if (lane == 0) {
+      bool ok = true;
+      int st = 0;
+      for (; st < ksteps; ++st) {
+        const int s = st % T::kStages;
+        const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
+        // The ring's first pass needs no wait: those stages were never used.
+        if (st >= T::kStages && !ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
+          atomicOr(&g_status_f16, kErrProducer);
+          *abort = 1;
+          ok = false;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&ctl->full[s]), 2 * T::kStageBytes);
+        const uint32_t bar = mapa_shared(smem_u32(&ctl->full[s]), 0u);  // the leader's
+        const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+        tma_load_2d_pair(sa, &tmap_a, st * kStageKF, a_row, bar);
+        tma_load_2d_pair(sa + kABytesH, &tmap_w, st * kStageKF, w_row, bar);
+      }
+      if (!ok && rank == 0) {  // let the loads in flight land before the CTA can exit
+        const int first = st > T::kStages ? st - T::kStages : 0;
+        for (int j = first; j < st; ++j) {
+          volatile int never = 0;
+          ovb_wait(smem_u32(&ctl->full[j % T::kStages]),
+                   static_cast<uint32_t>((j / T::kStages) & 1), &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA (leader)
+    if (rank == 0) {
+      const uint32_t idesc = idesc_f16(2 * kBlockM, BN);
+      for (int st = 0; st < ksteps; ++st) {
+        const int s = st % T::kStages;
+        named_sync(kBarFullH, 64);  // stage s of both CTAs has landed
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kStageKF / 16; ++kk)
+            mma_f16_ss_pair(tmem_base, sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
+                            sw128_kmajor_desc(sa + kABytesH, static_cast<uint32_t>(kk * 32)),
+                            idesc, (st > 0 || kk > 0) ? 1u : 0u);
+          tc_commit_pair(smem_u32(&ctl->empty[s]), 0x3);
+          if (st == ksteps - 1) tc_commit_pair(smem_u32(&ctl->tfull[0]), 0x3);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------- stage watcher (leader)
+    if (rank == 0) {
+      for (int st = 0; st < ksteps; ++st) {
+        const int s = st % T::kStages;
+        const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
+        const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
+        if (!__all_sync(0xffffffffu, got) && lane == 0) {
+          atomicOr(&g_status_f16, kErrConvert);
+          *abort = 1;
+        }
+        named_sync(kBarFullH, 64);
+      }
+    }
+  } else {
+    // ------------------------------------------------- epilogue (both CTAs)
+    if constexpr (kSilu) {
+      uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
+      silu_epilogue<BN, 1, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
+                                     (warp - kFirstEpiH) >> 2, kBarDfreeH, vtile + 1, m_tiles_v,
+                                     1, vtile, 1);
+    } else {
+      epilogue_loop<BN, 1>(args, ctl->tfull, abort, tmem_base,
+                           stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                           (warp - kFirstEpiH) >> 2, kBarDfreeH, vtile + 1, m_tiles_v, 1, vtile,
+                           1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // Neither CTA frees its TMEM or shared memory while the pair's MMAs or the
+  // other CTA may still use them (the epilogues waited for the last MMA).
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemColsF);
+  }
+}
+
+template <int BN, bool kSilu>
+cudaError_t launch_h2_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
+                           const GemmArgs& args, cudaStream_t s) {
+  using T = TileH2<BN, kSilu>;
+  auto* kernel = gemm_h2_kernel<BN, kSilu>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static thread_local int configured_dev = -1;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(T::kSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  const int64_t pairs = ((args.M + 2 * kBlockM - 1) / (2 * kBlockM)) * ((args.N + BN - 1) / BN);
+  if (pairs * 8 > INT32_MAX) return cudaErrorInvalidValue;  // 32-bit tile arithmetic
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(T::kThreads);
+  cfg.dynamicSmemBytes = T::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_w, args);
+}
+
 template <int BN>
 cudaError_t launch_f16_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                             const GemmArgs& args, cudaStream_t s) {
@@ -1261,46 +1491,61 @@ int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device) {
   return best;
 }
 
-// Tile width for the plain fp16 mainloop: per 64-k stage the slower of the
-// tensor core (4 MMAs: ~128 clocks each at N = 256, ~64 at N <= 128) and the
-// TMA feed (measured ~375 clocks for stages up to ~40 KB, ~100 B/clock per SM
-// beyond), plus a per-tile cost (prologue, epilogue stores) growing with BN.
-// Split-K configurations (kHConfigs[4..6]) need at least this many 64-k
-// stages per rank to pay for the partial-sum exchange.
+// Split-K configurations need at least this many 64-k stages per rank to pay
+// for the partial-sum exchange.
 constexpr int kMinStagesPerRank = 4;
 
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_configs) {
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) {
   const int64_t ksteps = (Kb + 1) / 2;
   const char* et = std::getenv("OVB_GEMM_TILE_N");
   const char* es = std::getenv("OVB_GEMM_SPLIT_K");
-  if (et || es) {
+  const char* ep = std::getenv("OVB_GEMM_PAIR");
+  if (et || es || ep) {
     const int bn = et ? std::atoi(et) : 0;
     const int sp = es ? std::atoi(es) : 1;
-    for (int i = 0; i < n_configs; ++i)
-      if ((bn == 0 || kTileNF[kHConfigs[i].width] == bn) && kHConfigs[i].split == sp &&
-          ksteps >= static_cast<int64_t>(kHConfigs[i].split))
+    const int pr = ep ? std::atoi(ep) : 0;
+    for (int i = 0; i < kNumHConfigs; ++i)
+      if (((allowed >> i) & 1u) && (bn == 0 || h_tile_n(i) == bn) && kHConfigs[i].split == sp &&
+          kHConfigs[i].pair == pr && ksteps >= static_cast<int64_t>(kHConfigs[i].split))
         return i;
   }
-  static constexpr int64_t kPerStage[4] = {512, 375, 375, 375};
+  // Cost in SM clocks, fitted to graph timings at M = 400 and 1400: a fixed
+  // part (launch, prologue, first load; more for a CTA pair), the epilogue
+  // (per output column of the CTA; the fused SiLU*up one is heavier), and per
+  // 64-k stage the slower of the tensor pipe (four K = 16 MMAs) and shared
+  // memory at ~128 B per clock, which carries the stage twice (TMA write, MMA
+  // read; a pair CTA writes half of W but serves it to both tensor cores),
+  // plus the split-K exchange; whole waves of CTAs.  CTA pairs run one tile
+  // per cluster (no epilogue overlap), so they are only used in one wave.
   const int64_t sms = num_sms(device);
+  const bool silu = allowed == kHSilu;
   const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
-  int best = 0;
+  int best = -1;
   int64_t best_cost = -1;
-  for (int i = 0; i < n_configs; ++i) {
-    const int w = kHConfigs[i].width, sp = kHConfigs[i].split;
-    if (sp > 1 && ksteps < static_cast<int64_t>(sp) * kMinStagesPerRank) continue;
-    const int64_t tiles = m_tiles * ((N + kTileNF[w] - 1) / kTileNF[w]);
-    const int64_t ctas = tiles * sp;
+  for (int i = 0; i < kNumHConfigs; ++i) {
+    if (!((allowed >> i) & 1u)) continue;
+    const HConfig& c = kHConfigs[i];
+    const int64_t bn = h_tile_n(i);
+    if (c.split > 1 && ksteps < static_cast<int64_t>(c.split) * kMinStagesPerRank) continue;
+    const int64_t n_tiles = (N + bn - 1) / bn;
+    const int64_t ctas =
+        c.pair ? 2 * ((m_tiles + 1) / 2) * n_tiles : m_tiles * n_tiles * c.split;
     const int64_t waves = (ctas + sms - 1) / sms;
-    const int64_t stages = (ksteps + sp - 1) / sp;
-    const int64_t cost = waves * (2000 + 10 * kTileNF[w] + stages * kPerStage[w] +
-                                  (sp > 1 ? 1500 : 0));
+    if (c.pair && waves > 1) continue;
+    const int64_t box = kTileNF[c.width];  // W rows this CTA loads per stage
+    const int64_t smem = c.pair ? (16384 + box * 128) + (16384 + bn * 128)
+                                : 2 * (16384 + box * 128);
+    const int64_t mma = 4 * (bn <= 128 ? 64 : 128);
+    const int64_t per_stage = (mma > smem / 128 ? mma : smem / 128) + (c.pair ? 30 : 0);
+    const int64_t stages = (ksteps + c.split - 1) / c.split;
+    const int64_t cost = waves * (3000 + (c.pair ? 600 : 0) + (silu ? 38 : 29) * (bn / c.split) +
+                                  stages * per_stage + (c.split > 1 ? 4000 : 0));
     if (best_cost < 0 || cost < best_cost) {
       best = i;
       best_cost = cost;
     }
   }
-  return best;
+  return best < 0 ? 0 : best;
 }
 
 cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
@@ -1310,6 +1555,8 @@ cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorM
       case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);
       case 1: return launch_h_impl<128, true>(tmap_a, tmap_w, args, s);
       case 2: return launch_h_impl<64, true>(tmap_a, tmap_w, args, s);
+      case 7: return launch_h2_impl<256, true>(tmap_a, tmap_w, args, s);
+      case 8: return launch_h2_impl<128, true>(tmap_a, tmap_w, args, s);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -1321,6 +1568,8 @@ cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorM
     case 4: return launch_h_impl<64, false, 2>(tmap_a, tmap_w, args, s);
     case 5: return launch_h_impl<128, false, 2>(tmap_a, tmap_w, args, s);
     case 6: return launch_h_impl<128, false, 4>(tmap_a, tmap_w, args, s);
+    case 7: return launch_h2_impl<256, false>(tmap_a, tmap_w, args, s);
+    case 8: return launch_h2_impl<128, false>(tmap_a, tmap_w, args, s);
     default: return cudaErrorInvalidValue;
   }
 }

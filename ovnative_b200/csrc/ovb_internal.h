@@ -83,13 +83,24 @@ constexpr int kTileN[3] = {128, 64, 32};
 
 // Output-tile widths of the fp16 mainloops.
 constexpr int kTileNF[4] = {256, 128, 64, 32};
-// Configurations of the plain fp16 mainloop: tile width (index into
-// kTileNF) and split-K factor (a cluster of `split` CTAs per output tile).
+// Configurations of the plain fp16 mainloop: the W box (index into kTileNF:
+// rows of W each CTA loads per stage), the split-K factor (a cluster of
+// `split` CTAs per output tile) and CTA pairs (`pair`: a 2-CTA cluster runs
+// cta_group::2 MMAs on a 256-row tile twice the box wide).
 struct HConfig {
   int width;
   int split;
+  int pair;
 };
-constexpr HConfig kHConfigs[7] = {{0, 1}, {1, 1}, {2, 1}, {3, 1}, {2, 2}, {1, 2}, {1, 4}};
+constexpr HConfig kHConfigs[9] = {{0, 1, 0}, {1, 1, 0}, {2, 1, 0}, {3, 1, 0}, {2, 2, 0},
+                                  {1, 2, 0}, {1, 4, 0}, {1, 1, 1}, {2, 1, 1}};
+constexpr int kNumHConfigs = 9;
+// Output-tile width of configuration c.
+constexpr int h_tile_n(int c) { return kTileNF[kHConfigs[c].width] * (kHConfigs[c].pair ? 2 : 1); }
+// Allowed-configuration masks for pick_tile_h.
+constexpr unsigned kHAll = (1u << kNumHConfigs) - 1;
+constexpr unsigned kHNoSplit = 0x18Fu;  // 0-3 and the pairs 7, 8
+constexpr unsigned kHSilu = 0x187u;     // BN >= 64 without split-K: 0-2, 7, 8
 
 constexpr int kMaxSlices = 4;
 
@@ -178,9 +189,10 @@ cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorM
                             const GemmArgs& args, cudaStream_t s);
 cudaError_t read_and_clear_status_f16(int* out, cudaStream_t s);
 // The plain fp16 mainloop: A is fp16 [M, Kp] (dequantised activations).
-// Returns an index into kHConfigs; n_configs limits the choice to the first
-// n entries (3 = BN >= 64 without split-K, for the fused SiLU*up epilogue).
-int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, int n_configs = 7);
+// Returns an index into kHConfigs among the configurations in `allowed`
+// (a bit mask: kHAll, kHNoSplit without a split-K workspace, kHSilu for the
+// fused SiLU*up epilogue).
+int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed = kHAll);
 cudaError_t launch_gemm_h(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s);
 

@@ -300,3 +300,53 @@ def test_linear_h_unaligned_c(cuda, monkeypatch, offset, pad, tile_n, split):
     check_tolerance(host(C), O.linear_q(aq_h, asc_h, W, s, K, C_in=C0))
     assert ovb.device_status() == 0
     w.close()
+
+
+# ------------------------------------ CTA pairs (tcgen05 cta_group::2, M = 256)
+PAIR_SHAPES = [(400, 1024, 1024), (129, 320, 1056), (300, 4096, 1024), (1, 256, 64),
+               (1400, 6144, 1024), (600, 1000, 256)]
+
+
+@pytest.mark.parametrize("tile_n", [256, 128])
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_linear_h_pair(cuda, monkeypatch, tile_n, M, N, K):
+    """A 2-CTA cluster computes a 256-row tile with cta_group::2 MMAs, each
+    CTA loading half of the W tile.  300 rows leave the second pair's peer
+    CTA without rows; 1400 x 6144 needs several waves of clusters."""
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    monkeypatch.setenv("OVB_GEMM_PAIR", "1")
+    rng = np.random.default_rng(M * 3 + N + K + tile_n)
+    A, W, s = case(rng, M, N, K)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    w = ovb.Weight.from_nk(W, s, f16=True)
+    a16, _ = ovb.s8_nk_quantize(dev(A, cuda), f16=True)
+    aq_h, asc_h = O.quantize(A)
+    got = host(ovb.linear_h(a16, w))
+    check_tolerance(got, O.linear_q(aq_h, asc_h, W, s, K))
+    assert host(ovb.linear_h(a16, w)).tobytes() == got.tobytes()  # deterministic
+    C = dev(C0, cuda)
+    ovb.linear_h(a16, w, C, accumulate=True)
+    check_tolerance(host(C), O.linear_q(aq_h, asc_h, W, s, K, C_in=C0))
+    # unaligned C rows take the epilogue's scalar path
+    buf = torch.full((M, N + 3), float("nan"), device=cuda)
+    ovb.linear_h(a16, w, buf[:, 1:N + 1])
+    check_tolerance(host(buf[:, 1:N + 1]), O.linear_q(aq_h, asc_h, W, s, K))
+    assert torch.isnan(buf[:, 0]).all() and torch.isnan(buf[:, N + 1:]).all()
+    assert ovb.device_status() == 0
+    w.close()
+
+
+def test_linear_h_pair_sliced(cuda, golden, monkeypatch):
+    monkeypatch.setenv("OVB_GEMM_TILE_N", "128")
+    monkeypatch.setenv("OVB_GEMM_PAIR", "1")
+    for i in range(3):
+        Ns = [int(n) for n in golden[f"sliced{i}_Ns"]]
+        parts = [ovb.Weight.from_nk(golden[f"sliced{i}_W{j}"], golden[f"sliced{i}_s{j}"], f16=True)
+                 for j in range(len(Ns))]
+        wc = ovb.Weight.concat(parts)
+        a16, _ = ovb.s8_nk_quantize(dev(golden[f"sliced{i}_A"], cuda), f16=True)
+        Cs = [torch.full((a16.shape[0], n), float("nan"), device=cuda) for n in Ns]
+        ovb.linear_h_sliced(a16, wc, Cs)
+        for j, c in enumerate(Cs):
+            check_tolerance(host(c), golden[f"sliced{i}_C{j}"])
+    assert ovb.device_status() == 0

@@ -63,9 +63,11 @@ def test_q_silu_bit_exact_vs_reference(cuda, M, inter, K):
     assert ovb.device_status() == 0
 
 
-@pytest.mark.parametrize("tile_n", [256, 128, 64])
-@pytest.mark.parametrize("M,inter,K", [(1, 64, 64), (129, 256, 96), (400, 3072, 1024)])
-def test_h_silu_agrees_with_unfused_fp16_sequence(cuda, monkeypatch, tile_n, M, inter, K):
+# (tile width, CTA pair): the single-CTA widths and the cta_group::2 pairs.
+@pytest.mark.parametrize("tile_n,pair", [(256, 0), (128, 0), (64, 0), (256, 1), (128, 1)])
+@pytest.mark.parametrize("M,inter,K", [(1, 64, 64), (129, 256, 96), (400, 3072, 1024),
+                                       (300, 640, 1056)])
+def test_h_silu_agrees_with_unfused_fp16_sequence(cuda, monkeypatch, tile_n, pair, M, inter, K):
     rng = np.random.default_rng(3 * M + inter + K)
     (Wg, sg, Wu, su), g, u = weights(rng, inter, K, True)
     gu = ovb.Weight.gate_up(g, u)
@@ -78,8 +80,10 @@ def test_h_silu_agrees_with_unfused_fp16_sequence(cuda, monkeypatch, tile_n, M, 
     for f16_out in (True, False):
         want_q, want_s = ovb.silu_mul_quantize_f32(gate, up, f16=f16_out)
         monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+        monkeypatch.setenv("OVB_GEMM_PAIR", str(pair))
         q, sc = ovb.linear_h_silu(a16, gu, f16=f16_out)
         monkeypatch.delenv("OVB_GEMM_TILE_N")
+        monkeypatch.delenv("OVB_GEMM_PAIR")
         got_s, ref_s = host(sc).astype(np.float64), host(want_s).astype(np.float64)
         assert np.all(np.abs(got_s - ref_s) <= 1e-5 * np.abs(ref_s) + 1e-30)
         if f16_out:
