@@ -350,30 +350,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # i-1's result from buffer (i-1)%3 on two copy streams, so the copies
     # overlap the compute and each step is one graph launch.
     rng = np.random.default_rng(77)
-    h_in = [torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
-            .pin_memory() for _ in range(3)]
-    h_out = [torch.empty_like(h_in[0]).pin_memory() for _ in range(3)]
-    d_x = [torch.empty_like(x) for _ in range(3)]
-    s_in = torch.cuda.Stream(device=dev)
-    s_out = torch.cuda.Stream(device=dev)
-    step_graphs = {}
-    with torch.cuda.stream(stream):
-        for lid, lw in enumerate(path.layers):
-            for r in range(3):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    s_in.wait_stream(stream)
-                    s_out.wait_stream(stream)
-                    with torch.cuda.stream(s_in):  # step i+1's input
-                        d_x[(r + 1) % 3].copy_(h_in[(r + 1) % 3], non_blocking=True)
-                    with torch.cuda.stream(s_out):  # step i-1's result
-                        h_out[(r + 2) % 3].copy_(d_x[(r + 2) % 3], non_blocking=True)
-                    LY.run(d_x[r], lw, path.buf)  # step i, in place
-                    stream.wait_stream(s_in)
-                    stream.wait_stream(s_out)
-                step_graphs[(lid, r)] = g
-        for r in range(3):  # warm
-            step_graphs[(0, r)].replay()
+    h_in0 = torch.from_numpy(rng.standard_normal((M_TOKENS, LY.HIDDEN)).astype(np.float32))
+    h_in0 = h_in0.pin_memory()
+    h_out0 = torch.empty_like(h_in0).pin_memory()
+    pipe = LY.StepPipeline(path.layers, path.buf, M_TOKENS, dev, stream)
+    for r in range(3):
+        pipe.host_in[r].copy_(h_in0)
+    pipe.start()
+    for r in range(3):  # warm
+        pipe.step(r, 0)
     torch.cuda.synchronize()
 
     def timed_e2e(pipelined: bool) -> float:
@@ -385,15 +370,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         with torch.cuda.stream(stream):
             if not pipelined:
                 for i in range(args.steps):
-                    x.copy_(h_in[0], non_blocking=True)
+                    x.copy_(h_in0, non_blocking=True)
                     graphs[i % N_LAYERS].replay()
-                    h_out[0].copy_(x, non_blocking=True)
+                    h_out0.copy_(x, non_blocking=True)
             else:
-                d_x[0].copy_(h_in[0], non_blocking=True)  # step 0's input
+                pipe.start()
                 for i in range(args.steps):
-                    step_graphs[(i % N_LAYERS, i % 3)].replay()
-                last = (args.steps - 1) % 3
-                h_out[last].copy_(d_x[last], non_blocking=True)  # the last step's result
+                    pipe.step(i, i % N_LAYERS)
+                pipe.finish(args.steps - 1)
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -416,8 +400,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
            "serial_ms_per_step": e2e_serial_ms / args.steps}
 
     status = ovb.device_status()
-    for g in step_graphs.values():
-        g.reset()
+    pipe.release()
     path.release()
     sampler = time_sampler(dev, stream) if world == 1 else None
     status |= ovb.device_status()

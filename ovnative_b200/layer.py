@@ -163,3 +163,68 @@ def run_unfused(x: torch.Tensor, lw_cat, buf: LayerBuffers, attn: torch.Tensor |
 
 
 KERNELS_PER_LAYER = 7  # 3 quantisers + 4 GEMMs (gate|up fused with SiLU*up quantise)
+
+
+class StepPipeline:
+    """Drives layer steps over inputs in pinned host memory with the copies
+    overlapping the compute, as a serving loop does.
+
+    Three device buffers rotate: step i runs in place on buffer i % 3, and the
+    CUDA graph of step i (one per (layer, rotation)) also copies step i+1's
+    input from ``host_in[(i+1) % 3]`` into its buffer and step i-1's result
+    from its buffer into ``host_out[(i-1) % 3]``, on two copy streams.  So
+    every step is one graph launch; step i's input must be in
+    ``host_in[i % 3]`` when step i-1 starts (step 0's when ``start`` is
+    called), and its result is in ``host_out[i % 3]`` once step i+1 (or
+    ``finish``) has completed on the stream.
+    """
+
+    def __init__(self, layers: list[LayerWeights], buf: LayerBuffers, M: int, device,
+                 stream: torch.cuda.Stream):
+        self.stream = stream
+        self.host_in = [torch.empty((M, HIDDEN), dtype=torch.float32).pin_memory()
+                        for _ in range(3)]
+        self.host_out = [torch.empty((M, HIDDEN), dtype=torch.float32).pin_memory()
+                         for _ in range(3)]
+        self.dev = [torch.empty((M, HIDDEN), dtype=torch.float32, device=device)
+                    for _ in range(3)]
+        s_in = torch.cuda.Stream(device=device)
+        s_out = torch.cuda.Stream(device=device)
+        self.graphs = {}
+        with torch.cuda.stream(stream):
+            for lid, lw in enumerate(layers):
+                for r in range(3):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        s_in.wait_stream(stream)
+                        s_out.wait_stream(stream)
+                        with torch.cuda.stream(s_in):  # step i+1's input
+                            self.dev[(r + 1) % 3].copy_(self.host_in[(r + 1) % 3],
+                                                        non_blocking=True)
+                        with torch.cuda.stream(s_out):  # step i-1's result
+                            self.host_out[(r + 2) % 3].copy_(self.dev[(r + 2) % 3],
+                                                             non_blocking=True)
+                        run(self.dev[r], lw, buf)  # step i, in place
+                        stream.wait_stream(s_in)
+                        stream.wait_stream(s_out)
+                    self.graphs[(lid, r)] = g
+
+    def start(self):
+        """Copy step 0's input (host_in[0]) to the device."""
+        with torch.cuda.stream(self.stream):
+            self.dev[0].copy_(self.host_in[0], non_blocking=True)
+
+    def step(self, i: int, layer: int):
+        """Enqueue step i on the layer with index `layer`."""
+        with torch.cuda.stream(self.stream):
+            self.graphs[(layer, i % 3)].replay()
+
+    def finish(self, last: int):
+        """Copy the last step's result to host_out[last % 3]."""
+        with torch.cuda.stream(self.stream):
+            self.host_out[last % 3].copy_(self.dev[last % 3], non_blocking=True)
+
+    def release(self):
+        for g in self.graphs.values():
+            g.reset()
+        self.graphs = {}

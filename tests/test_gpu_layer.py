@@ -100,3 +100,42 @@ def test_layer_cfg1_f16_path_within_tolerance(cuda):
     assert np.isfinite(got).all()
     assert rel(got, want) <= 1e-3
     assert rel(got - x, want - x) <= 1e-2
+
+
+@pytest.mark.parametrize("f16", [True, False])
+def test_step_pipeline_matches_direct_steps(cuda, f16):
+    """StepPipeline (the serving loop bench.py's e2e line uses: copies of the
+    next input and the previous result inside each step's graph, three device
+    buffers in rotation) returns exactly what running each step directly
+    returns, for distinct inputs and layers per step."""
+    rng = np.random.default_rng(31 + f16)
+    M, n_layers, steps = 200, 2, 7
+    layers = [LY.LayerWeights.from_host(LY.random_layer_host(rng), cuda, f16=f16)
+              for _ in range(n_layers)]
+    buf = LY.LayerBuffers(M, cuda, f16=f16)
+    xs = [rng.standard_normal((M, LY.HIDDEN)).astype(np.float32) for _ in range(steps)]
+    want = []
+    for i, xi in enumerate(xs):
+        x = torch.from_numpy(xi).to(cuda)
+        LY.run(x, layers[i % n_layers], buf)
+        want.append(x.cpu().numpy())
+    stream = torch.cuda.Stream(device=cuda)
+    pipe = LY.StepPipeline(layers, buf, M, cuda, stream)
+    got = []
+    pipe.host_in[0].copy_(torch.from_numpy(xs[0]))
+    pipe.start()
+    for i in range(steps):
+        # step i+1's input must be in place before step i starts
+        if i + 1 < steps:
+            stream.synchronize()
+            pipe.host_in[(i + 1) % 3].copy_(torch.from_numpy(xs[i + 1]))
+        pipe.step(i, i % n_layers)
+        if i >= 1:  # step i-1's result is out once step i has completed
+            stream.synchronize()
+            got.append(pipe.host_out[(i - 1) % 3].numpy().copy())
+    pipe.finish(steps - 1)
+    stream.synchronize()
+    got.append(pipe.host_out[(steps - 1) % 3].numpy().copy())
+    for i in range(steps):
+        assert np.array_equal(got[i], want[i]), f"step {i}"
+    pipe.release()
