@@ -91,10 +91,20 @@ int ovb_abi_version(void);
 const char* ovb_last_error(void);
 
 /* Device status of the GEMMs since the last call, on this thread's device:
- * 0 when every bounded wait inside the kernels completed.  Bit 16 reports an
- * activation block beyond the fp16 range in the fp16 mainloop.  Reading it
+ * 0 when every bounded wait inside the kernels completed.  Bits 1, 2, 4, 8:
+ * a wait of the producer, stage watcher / converter, epilogue or drain gave
+ * up (~1 s limit; the kernel then ends early and its outputs are invalid,
+ * the context stays usable).  Bit 16 reports an activation block beyond the
+ * fp16 range in the fp16 mainloop; bit 64 the self-test below.  Reading it
  * synchronises the given stream and clears it. */
 int ovb_device_status(void* stream);
+
+/* Failure-detection self-test: launches a kernel whose bounded mbarrier
+ * wait can never complete (nothing arrives on the barrier).  The wait gives
+ * up after its limit (~1 s), the kernel ends normally and the next
+ * ovb_device_status reports bit 64.  No GPU fault or hang is involved.  No
+ * counterpart in the reference. */
+int ovb_selftest_wait_timeout(void* stream);
 
 /* --- sizes ------------------------------------------------------------ */
 /* replaces ov::s8_nk_quant_bytes (ov_gemm.h:95) */

@@ -36,6 +36,7 @@ SIGNATURES = {
     "ovb_abi_version": ([], _int),
     "ovb_last_error": ([], C.c_char_p),
     "ovb_device_status": ([_p], _int),
+    "ovb_selftest_wait_timeout": ([_p], _int),
     "ovb_quant_bytes": ([_i64, _i64], _i64),
     "ovb_quant_scales": ([_i64, _i64], _i64),
     "ovb_weight_create": ([_p, _int, _i64, _i64, _p, _int, _p, C.POINTER(_p)], _int),

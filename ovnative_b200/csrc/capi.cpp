@@ -718,6 +718,12 @@ int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t
                   as_stream(stream));
 }
 
+int ovb_selftest_wait_timeout(void* stream) {
+  if (cuda_failed(ovb::launch_wait_selftest(as_stream(stream)), "wait self-test launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
 int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int uncond_seq,
                       int codebooks, int vocab, int target_len, float guidance,
                       float layer_penalty, int mask_id, int32_t* pred, float* scores,

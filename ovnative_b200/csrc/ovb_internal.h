@@ -179,6 +179,8 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtyp
                     uint32_t box_rows, CUtensorMapSwizzle swizzle);
 // int8 [n] -> fp16 [n] (exact for |v| <= 2048).
 cudaError_t launch_widen_f16(const int8_t* src, int64_t n, uint16_t* dst, cudaStream_t s);
+// A kernel whose bounded wait cannot complete (status bit 64 after ~1 s).
+cudaError_t launch_wait_selftest(cudaStream_t s);
 // The guided argmax pass (sampler.cu): one warp per (codebook, frame) row.
 cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
                                  int V, int T, float guidance, float penalty, int mask_id,

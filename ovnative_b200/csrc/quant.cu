@@ -32,6 +32,7 @@ namespace {
 constexpr int kModeU8 = 1;
 constexpr int kModeF16 = 2;
 constexpr int kErrF16Range = 16;
+constexpr int kErrSelftest = 64;  // the wait self-test's deliberate timeout
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
@@ -503,6 +504,27 @@ cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, in
     default: return launch_plain(silu_mul_quantize_kernel<2>, grid, dim3(256), 0, s, M, K, gate, ldg,
                                up, ldu, q8, asc);
   }
+}
+
+namespace {
+// One mbarrier that nothing ever arrives on, waited on with the kernels'
+// bounded wait (ovb_wait): the wait gives up at its limit (~1 s at the SM
+// clock), thread 0 records kErrSelftest, and the kernel ends normally.
+__global__ void wait_selftest_kernel() {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int never = 0;
+  const bool got = ovb_wait(smem_u32(&bar), 0u, &never);
+  if (!got && threadIdx.x == 0) atomicOr(&g_status_q, kErrSelftest);
+}
+}  // namespace
+
+cudaError_t launch_wait_selftest(cudaStream_t s) {
+  return launch_plain(wait_selftest_kernel, dim3(1), dim3(32), 0, s);
 }
 
 cudaError_t read_and_clear_status_q(int* out, cudaStream_t s) {
