@@ -403,6 +403,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     pipe.release()
     path.release()
     sampler = time_sampler(dev, stream) if world == 1 else None
+    attention = time_attention(dev, stream) if world == 1 else None
     status |= ovb.device_status()
 
     # ---- the other numerics path over the same K steps (reported, not headline)
@@ -442,6 +443,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
         if sampler is not None:
             sampler["cpu_baseline"] = sampler_cpu_baseline()
+        if attention is not None:
+            attention["cpu_baseline"] = attention_cpu_baseline()
     return {
         "metric": METRIC,
         "value": value,
@@ -464,6 +467,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "roofline": roofline,
         "cpu_baseline": cpu,
         "sampler": sampler,
+        "attention": attention,
         "clocks": clk.summary(),
     }
 
@@ -542,6 +546,106 @@ def sampler_cpu_baseline(budget_s: float = 1.0) -> dict:
             "sample": f"{n} x {C * T_s} rows in {sec:.2f} s, scaled to {C * sp['target_len']} rows"}
 
 
+# ------------------------------------------------------------ attention
+# The attention of one layer at config 3's length: a CFG pair of 700-token
+# segments (cond, uncond) with the reference's 0 / -1e30 padding bias, 16
+# query heads over 8 kv heads of 128 dims.
+ATTENTION = {"segments": [700, 700], "n_heads": 16, "n_kv": 8, "head_dim": 128,
+             "pad_keys": 8}
+
+
+def _attention_inputs(dev, gen, sets):
+    import torch
+    at = ATTENTION
+    T = sum(at["segments"])
+    H, KV, Dh = at["n_heads"], at["n_kv"], at["head_dim"]
+    segs, r0 = [], 0
+    for rows in at["segments"]:
+        bias = torch.zeros((rows, rows), device=dev)
+        bias[:, :at["pad_keys"]] = -1e30
+        segs.append((bias, rows, r0 * H * Dh, r0 * KV * Dh))
+        r0 += rows
+    qs = [torch.randn((T, H * Dh), device=dev, generator=gen) for _ in range(sets)]
+    ks = [torch.randn((T, KV * Dh), device=dev, generator=gen) for _ in range(sets)]
+    vs = [torch.randn((T, KV * Dh), device=dev, generator=gen) for _ in range(sets)]
+    return qs, ks, vs, segs
+
+
+def attention_flops() -> int:
+    """Algorithmic FLOPs of one layer's attention: 2 S^2 D for q k^T and
+    2 S^2 D for p v, per segment and query head."""
+    at = ATTENTION
+    return sum(4 * s * s * at["head_dim"] * at["n_heads"] for s in at["segments"])
+
+
+def time_attention(dev, stream, launches: int = 32, sets: int = 4) -> dict:
+    """Device time per ovb_attention launch, CUDA events around a graph of
+    `launches` launches rotating over `sets` q/k/v sets (4 x 34 MB > L2)."""
+    import torch
+    import ovnative_b200 as ovb
+    at = ATTENTION
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17)
+    qs, ks, vs, segs = _attention_inputs(dev, gen, sets)
+    outs = [torch.empty_like(q) for q in qs]
+    scale = 1.0 / float(np.sqrt(at["head_dim"]))
+
+    def one(i):
+        j = i % sets
+        ovb.attention(qs[j], ks[j], vs[j], segs, at["n_heads"], at["n_kv"], scale, out=outs[j])
+
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            one(i)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(launches):
+                one(i)
+        g.replay()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / launches
+    del g
+    flops = attention_flops()
+    peaks = load_peaks()
+    achieved = flops / (us * 1e-6) / 1e12
+    return {"kernel": "attention_kernel (one CTA per segment x head x 128 query rows; "
+                      "tcgen05 kind::f16, S and P v in TMEM)",
+            "config": dict(at), "us_per_launch": us, "bound": "tensor",
+            "algorithmic_flops": flops, "achieved": achieved, "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+            "peak_source": peaks["source"], "l2": "4 q/k/v sets rotated, 137 MB > L2"}
+
+
+def attention_cpu_baseline(budget_s: float = 1.0) -> dict:
+    """The reference's own ov::attention_head_f32 (oracle/_ref, one thread)
+    on a bounded sample -- whole (segment, head) units of ATTENTION -- scaled
+    to one layer's 32 units."""
+    import oracle as O
+    at = ATTENTION
+    S, Dh = at["segments"][0], at["head_dim"]
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((S, Dh)).astype(np.float32)
+    k = rng.standard_normal((S, Dh)).astype(np.float32)
+    v = rng.standard_normal((S, Dh)).astype(np.float32)
+    bias = np.zeros((S, S), dtype=np.float32)
+    bias[:, :at["pad_keys"]] = -1e30
+    ref = O.ref_available()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n == 0:
+        O.attention(q, k, v, [(bias, S, 0, 0)], 1, 1, Dh, 1.0 / float(np.sqrt(Dh)), use_ref=ref)
+        n += 1
+    sec = time.perf_counter() - t0
+    units = len(at["segments"]) * at["n_heads"]
+    return {"us_per_step": sec / n * units * 1e6, "cores": 1,
+            "kind": "reference" if ref else "port",
+            "sample": f"{n} (segment, head) units of {S} rows in {sec:.2f} s, scaled to {units}"}
+
+
 # ---------------------------------------------------------- reference arm
 def run_reference(args, rank: int, world: int):
     if rank != 0:
@@ -584,6 +688,8 @@ def main():
     ap.add_argument("--numerics", choices=["fp16", "exact"], default="fp16")
     ap.add_argument("--skip-other", action="store_true",
                     help="do not time the other numerics path (for profiling runs)")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="only time the attention (one q/k/v set, 8 launches; for ncu)")
     ap.add_argument("--sampler-only", action="store_true",
                     help="only time the guided sampler (one plane set, 8 launches; for "
                          "profiling runs) and print its entry")
@@ -592,6 +698,12 @@ def main():
         import torch
         dev = torch.device("cuda", 0)
         print(json.dumps(time_sampler(dev, torch.cuda.Stream(device=dev), launches=8, sets=1)),
+              flush=True)
+        return
+    if args.attention_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(time_attention(dev, torch.cuda.Stream(device=dev), launches=8, sets=1)),
               flush=True)
         return
     if args.warmup < 3:

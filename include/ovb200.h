@@ -95,7 +95,8 @@ const char* ovb_last_error(void);
  * a wait of the producer, stage watcher / converter, epilogue or drain gave
  * up (~1 s limit; the kernel then ends early and its outputs are invalid,
  * the context stays usable).  Bit 16 reports an activation block beyond the
- * fp16 range in the fp16 mainloop; bit 64 the self-test below.  Reading it
+ * fp16 range in the fp16 mainloop; bit 32 a wait of the attention kernel;
+ * bit 64 the self-test below.  Reading it
  * synchronises the given stream and clears it. */
 int ovb_device_status(void* stream);
 
@@ -231,7 +232,7 @@ int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t
  * :91-101) and its CUDA guided_sample_kernel (cpp/src/backend/cuda/
  * cuda_lm.cu:679-758, called by LmRunnerSampleThunk :1228-1262) behind
  * LM::CudaSampleFn (cpp/src/model/lm.h:106-108; that hook copies pred/scores
- * back to the host -- see INTEGRATION.md).  pred and scores are device
+ * back to the host).  pred and scores are device
  * arrays of codebooks * target_len.  target_len <= 0 or codebooks <= 0
  * returns OVB_OK without work; cond_seq / uncond_seq < target_len is
  * OVB_ERR_INVALID_ARG.  Log-probabilities agree with the CPU loop to a few
@@ -241,6 +242,34 @@ int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int 
                       int codebooks, int vocab, int target_len, float guidance,
                       float layer_penalty, int mask_id, int32_t* pred, float* scores,
                       void* stream);
+
+/* One attention segment, as the reference's AttnSegment (cpp/src/model/
+ * lm.h:46-51): `rows` query rows starting at element offset q_off of q/out,
+ * attending to the `rows` keys / values starting at element offset kv_off of
+ * k/v, with an optional additive bias [rows, rows] (row-major, device). */
+typedef struct ovb_attn_segment {
+  const float* bias;
+  int32_t rows;
+  int64_t q_off;
+  int64_t kv_off;
+} ovb_attn_segment;
+
+/* The attention of one layer on device pointers: for each segment and query
+ * head h < n_heads (kv head h / (n_heads / n_kv)),
+ *   out[s, h] = softmax_t(q[s, h] . k[t, kv] * scale + bias[s, t]) v[t, kv],
+ * a row whose scores are all below -1e29 (fully masked) giving zeros --
+ * ov::attention_head_f32 (cpp/src/backend/cpu/ops_cpu.cpp:907-943) over the
+ * loop of LM::run_layer (cpp/src/model/lm.cpp:256-274); the reference's CUDA
+ * runner does the same in cpp/src/backend/cuda/cuda_lm.cu:434-606.  Row s of
+ * head h of q and out is at element q_off + s * q_stride + h * head_dim; of
+ * k / v at kv_off + t * kv_stride + kv * head_dim.  head_dim must be 128;
+ * q/k/v/out 16-byte aligned; strides and offsets multiples of 4 elements;
+ * at most 64 segments.  The products run on the tensor cores with fp16
+ * inputs and fp32 accumulation: the output agrees with the fp32 reference
+ * to ~1e-3 relative.  n_segs == 0 returns OVB_OK without work. */
+int ovb_attention(const float* q, const float* k, const float* v, float* out, int64_t q_stride,
+                  int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                  const ovb_attn_segment* segs, int n_segs, void* stream);
 
 #ifdef __cplusplus
 }

@@ -181,6 +181,8 @@ def ref_lib():
             "ref_linear_packed_q_sliced": ([_i64, _i64, _p, _p, _p, _p, _p, _p, _p, C.c_int],
                                            C.c_int),
             "ref_linear_s8_nk": ([_i64, _i64, _i64, _p, _p, _p, _p], C.c_int),
+            "ref_attention_head": ([_p, _i64, _p, _p, _i64, _p, C.c_int, C.c_int, C.c_float,
+                                    _p, _i64], C.c_int),
         }
         for name, (args, res) in sig.items():
             f = getattr(lib, name)
@@ -337,3 +339,50 @@ def guided_sample(cond: np.ndarray, uncond: np.ndarray, T: int, C_books: int, gu
                                  guidance, penalty, mask_id, 1 if in_place else 0, _ptr(pred),
                                  _ptr(scores), _ptr(scratch))
     return pred, scores
+
+
+# ----------------------------------------------------------- attention
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, segs, n_heads: int, n_kv: int,
+              D: int, scale: float, use_ref: bool | None = None) -> np.ndarray:
+    """The reference's attention loop (cpp/src/model/lm.cpp:256-274): for each
+    segment (bias [rows, rows] or None, rows, q_off, kv_off -- element offsets
+    as in AttnSegment, lm.h:46-51) and query head h (kv head h / group),
+    ov::attention_head_f32 (ops_cpu.cpp:907-943) on q [T, n_heads*D],
+    k/v [T, n_kv*D], into out [T, n_heads*D].  Runs the reference library
+    when it is built (use_ref None/True), else a float64 numpy restatement of
+    the same formula."""
+    q = _f32(q)
+    k = _f32(k)
+    v = _f32(v)
+    QD, KVD = n_heads * D, n_kv * D
+    out = np.zeros_like(q)
+    group = n_heads // n_kv
+    ref = ref_available() if use_ref is None else use_ref
+    for bias, rows, q_off, kv_off in segs:
+        b = None if bias is None else _f32(bias)
+        for h in range(n_heads):
+            kv = h // group
+            qo = q_off + h * D
+            ko = kv_off + kv * D
+            if ref:
+                base_q = q.ctypes.data + 4 * qo
+                base_k = k.ctypes.data + 4 * ko
+                base_v = v.ctypes.data + 4 * ko
+                base_o = out.ctypes.data + 4 * qo
+                _chk(ref_lib().ref_attention_head(base_q, QD, base_k, base_v, KVD,
+                                                  None if b is None else _ptr(b), rows, D,
+                                                  scale, base_o, QD), "attention_head_f32")
+            else:
+                Q = np.stack([q.reshape(-1)[qo + i * QD: qo + i * QD + D] for i in range(rows)])
+                K = np.stack([k.reshape(-1)[ko + i * KVD: ko + i * KVD + D] for i in range(rows)])
+                V = np.stack([v.reshape(-1)[ko + i * KVD: ko + i * KVD + D] for i in range(rows)])
+                sc = (Q.astype(np.float64) @ K.astype(np.float64).T) * scale
+                if b is not None:
+                    sc = sc + b.astype(np.float64)
+                m = sc.max(axis=1, keepdims=True)
+                p = np.exp(sc - m)
+                o = (p / p.sum(axis=1, keepdims=True)) @ V.astype(np.float64)
+                o[m[:, 0] < -1e29] = 0.0
+                for i in range(rows):
+                    out.reshape(-1)[qo + i * QD: qo + i * QD + D] = o[i]
+    return out

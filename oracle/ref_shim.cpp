@@ -105,3 +105,13 @@ REF_API int ref_linear_s8_nk(int64_t M, int64_t N, int64_t K, const float* A, co
                              const float* scale, float* C) {
   return guard([&] { ov::linear_s8_nk(M, N, K, A, W, scale, C); });
 }
+
+// ov::attention_head_f32 (ops_cpu.cpp:907-943): one head of one attention
+// segment, softmax(q k^T * scale + bias) v with fully masked rows -> 0.
+REF_API int ref_attention_head(const float* q, int64_t q_stride, const float* k, const float* v,
+                               int64_t kv_stride, const float* bias, int S, int D, float scale,
+                               float* out, int64_t out_stride) {
+  return guard([&] {
+    ov::attention_head_f32(q, q_stride, k, v, kv_stride, bias, S, D, scale, out, out_stride);
+  });
+}

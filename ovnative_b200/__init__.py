@@ -4,7 +4,8 @@ The product is libovb200.so (CUDA kernels for sm_100a behind the C ABI in
 include/ovb200.h).  This package loads it and mirrors the reference's
 ov_gemm.h interface on torch CUDA tensors (gemm.py), and adds the per-layer
 linear sequence of LM::run_layer (layer.py) used by the benchmark, and the
-guided argmax pass of the TTS step (sampler.py).
+guided argmax pass of the TTS step (sampler.py) and the attention of a layer
+(attention.py).
 """
 from ._lib import LIB_PATH, OvbError, lib  # noqa: F401
 from .gemm import (  # noqa: F401
@@ -29,4 +30,5 @@ from .gemm import (  # noqa: F401
     silu_mul_quantize_f32,
     workspace_bytes,
 )
+from .attention import attention  # noqa: F401
 from .sampler import guided_sample  # noqa: F401

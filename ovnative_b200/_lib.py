@@ -31,6 +31,12 @@ class Slice(C.Structure):
     _fields_ = [("N", C.c_int64), ("C", C.c_void_p), ("ldc", C.c_int64)]
 
 
+class AttnSegment(C.Structure):
+    """ovb_attn_segment (the reference's AttnSegment, cpp/src/model/lm.h:46-51)."""
+    _fields_ = [("bias", C.c_void_p), ("rows", C.c_int32), ("q_off", C.c_int64),
+                ("kv_off", C.c_int64)]
+
+
 # name -> (argtypes, restype)
 SIGNATURES = {
     "ovb_abi_version": ([], _int),
@@ -60,6 +66,8 @@ SIGNATURES = {
     "ovb_block_products": ([_i64, _p, _p, _p, _p], _int),
     "ovb_guided_sample": ([_p, _int, _p, _int, _int, _int, _int, C.c_float, C.c_float, _int,
                            _p, _p, _p], _int),
+    "ovb_attention": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
+                       C.POINTER(AttnSegment), _int, _p], _int),
 }
 
 _lib = None

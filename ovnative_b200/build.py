@@ -24,7 +24,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libovb200.so")
 
-CU_SOURCES = ["quant.cu", "weights.cu", "gemm_tc.cu", "gemm_f16.cu", "linear_static.cu", "sampler.cu"]
+CU_SOURCES = ["quant.cu", "weights.cu", "gemm_tc.cu", "gemm_f16.cu", "linear_static.cu", "sampler.cu",
+              "attention.cu"]
 CXX_SOURCES = ["capi.cpp"]
 HEADERS = ["ovb_internal.h", "ovb_ptx.cuh", "ovb_quant.cuh"]
 

@@ -367,12 +367,13 @@ int ovb_abi_version(void) { return OVB_ABI_VERSION; }
 const char* ovb_last_error(void) { return ovb::t_error.c_str(); }
 
 int ovb_device_status(void* stream) {
-  int st = 0, st16 = 0, stq = 0;
+  int st = 0, st16 = 0, stq = 0, sta = 0;
   if (cuda_failed(ovb::read_and_clear_status(&st, as_stream(stream)), "read device status") ||
       cuda_failed(ovb::read_and_clear_status_f16(&st16, as_stream(stream)), "read device status") ||
-      cuda_failed(ovb::read_and_clear_status_q(&stq, as_stream(stream)), "read device status"))
+      cuda_failed(ovb::read_and_clear_status_q(&stq, as_stream(stream)), "read device status") ||
+      cuda_failed(ovb::read_and_clear_status_att(&sta, as_stream(stream)), "read device status"))
     return OVB_ERR_INTERNAL;
-  st |= st16 | stq;
+  st |= st16 | stq | sta;
   return st;
 }
 
@@ -741,6 +742,53 @@ int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int 
                                             guidance, layer_penalty, mask_id, pred, scores,
                                             as_stream(stream)),
                   "guided sample launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_attention(const float* q, const float* k, const float* v, float* out, int64_t q_stride,
+                  int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                  const ovb_attn_segment* segs, int n_segs, void* stream) {
+  if (n_segs == 0) return OVB_OK;
+  if (n_segs < 0 || n_segs > ovb::kAttMaxSegs) return invalid("n_segs must be in [0, 64]");
+  if (!segs || !q || !k || !v || !out) return invalid("q/k/v/out/segs must be non-null");
+  if (head_dim != 128) return invalid("head_dim must be 128");
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0)
+    return invalid("n_heads must be a positive multiple of n_kv");
+  if (q_stride < int64_t{n_heads} * head_dim || kv_stride < int64_t{n_kv} * head_dim)
+    return invalid("row strides must cover every head");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) ||
+      q_stride % 4 != 0 || kv_stride % 4 != 0)
+    return invalid("q/k/v/out must be 16-byte aligned with strides a multiple of 4");
+  ovb::AttnArgs a = {};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.q_stride = q_stride;
+  a.kv_stride = kv_stride;
+  a.n_heads = n_heads;
+  a.group = n_heads / n_kv;
+  a.scale = scale;
+  int64_t blocks = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    const ovb_attn_segment& g = segs[i];
+    if (g.rows < 0 || g.q_off < 0 || g.kv_off < 0) return invalid("negative segment field");
+    if (g.q_off % 4 != 0 || g.kv_off % 4 != 0)
+      return invalid("segment offsets must be multiples of 4");
+    if (g.rows == 0) continue;
+    ovb::AttnSeg& d = a.segs[a.n_segs++];
+    d.bias = g.bias;
+    d.q_off = g.q_off;
+    d.kv_off = g.kv_off;
+    d.rows = g.rows;
+    d.qblock0 = static_cast<int>(blocks);
+    blocks += (g.rows + 127) / 128;
+    if (blocks * n_heads > (int64_t{1} << 31) - 1) return invalid("too many query blocks");
+  }
+  if (blocks == 0) return OVB_OK;
+  if (cuda_failed(ovb::launch_attention(a, static_cast<int>(blocks), as_stream(stream)),
+                  "attention launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
 }

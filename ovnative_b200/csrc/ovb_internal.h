@@ -185,6 +185,32 @@ cudaError_t launch_wait_selftest(cudaStream_t s);
 cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
                                  int V, int T, float guidance, float penalty, int mask_id,
                                  int32_t* pred, float* scores, cudaStream_t s);
+// Attention (attention.cu).  One segment as the kernel sees it: the
+// reference's AttnSegment (bias, rows, q_off, kv_off; element offsets) plus
+// the index of its first 128-row query block in the launch.
+constexpr int kAttMaxSegs = 64;
+struct AttnSeg {
+  const float* bias;  // [rows, rows] additive, or null
+  int64_t q_off;      // element offset of the segment's first query row
+  int64_t kv_off;     // element offset of its first key / value row
+  int rows;
+  int qblock0;
+};
+struct AttnArgs {
+  const float* q;  // [*, q_stride]: head h at column h * 128
+  const float* k;  // [*, kv_stride]: kv head j at column j * 128
+  const float* v;
+  float* out;      // laid out like q
+  int64_t q_stride;
+  int64_t kv_stride;
+  int n_heads;
+  int group;       // query heads per kv head
+  int n_segs;
+  float scale;
+  AttnSeg segs[kAttMaxSegs];
+};
+cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s);
+cudaError_t read_and_clear_status_att(int* out, cudaStream_t s);
 // Index into kTileNF of the tile width used by the fp16 mainloop.
 int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device);
 cudaError_t launch_gemm_f16(int tile, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
