@@ -12,6 +12,8 @@
 #include <exception>
 #include <vector>
 
+#include <xmmintrin.h>
+
 #include "model/ops.h"
 #include "ovnative/ov_gemm.h"
 
@@ -107,11 +109,18 @@ REF_API int ref_linear_s8_nk(int64_t M, int64_t N, int64_t K, const float* A, co
 }
 
 // ov::attention_head_f32 (ops_cpu.cpp:907-943): one head of one attention
-// segment, softmax(q k^T * scale + bias) v with fully masked rows -> 0.
+// segment, softmax(q k^T * scale + bias) v with fully masked rows -> 0.  Its
+// AVX2 kernels switch the calling thread to flush-to-zero / denormals-are-zero
+// (ops_cpu.cpp:335, :738, as LM::forward does for every worker, lm.cpp:347-348);
+// the caller's MXCSR is restored afterwards so that the checkers that run
+// later in the same process keep IEEE denormals.
 REF_API int ref_attention_head(const float* q, int64_t q_stride, const float* k, const float* v,
                                int64_t kv_stride, const float* bias, int S, int D, float scale,
                                float* out, int64_t out_stride) {
-  return guard([&] {
+  const unsigned csr = _mm_getcsr();
+  const int rc = guard([&] {
     ov::attention_head_f32(q, q_stride, k, v, kv_stride, bias, S, D, scale, out, out_stride);
   });
+  _mm_setcsr(csr);
+  return rc;
 }
