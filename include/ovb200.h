@@ -95,7 +95,8 @@ const char* ovb_last_error(void);
  * a wait of the producer, stage watcher / converter, epilogue or drain gave
  * up (~1 s limit; the kernel then ends early and its outputs are invalid,
  * the context stays usable).  Bit 16 reports an activation block beyond the
- * fp16 range in the fp16 mainloop; bit 32 a wait of the attention kernel;
+ * fp16 range in the fp16 mainloop, or a q/k/v value beyond it in the
+ * attention; bit 32 a wait of the attention kernel;
  * bit 64 the self-test below.  Reading it
  * synchronises the given stream and clears it. */
 int ovb_device_status(void* stream);
@@ -264,9 +265,12 @@ typedef struct ovb_attn_segment {
  * head h of q and out is at element q_off + s * q_stride + h * head_dim; of
  * k / v at kv_off + t * kv_stride + kv * head_dim.  head_dim must be 128;
  * q/k/v/out 16-byte aligned; strides and offsets multiples of 4 elements;
- * at most 64 segments.  The products run on the tensor cores with fp16
- * inputs and fp32 accumulation: the output agrees with the fp32 reference
- * to ~1e-3 relative.  n_segs == 0 returns OVB_OK without work. */
+ * every head of a segment's rows within one row of the 2-D view
+ * ((q_off % q_stride) + n_heads * 128 <= q_stride, likewise for k/v); at
+ * most 64 segments.  The products run on the tensor cores with fp16 inputs
+ * and fp32 accumulation: the output agrees with the fp32 reference to ~1e-3
+ * relative; a q/k/v value beyond the fp16 range sets ovb_device_status bit
+ * 16.  n_segs == 0 (or only empty segments) returns OVB_OK without work. */
 int ovb_attention(const float* q, const float* k, const float* v, float* out, int64_t q_stride,
                   int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
                   const ovb_attn_segment* segs, int n_segs, void* stream);

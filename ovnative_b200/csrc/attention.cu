@@ -1,6 +1,7 @@
 // attention.cu -- the attention of one OVNative LM layer on the tensor cores:
-// for every attention segment (one half of a CFG pair: its q/k/v rows, an
-// additive bias [rows, rows] or none) and query head h (kv head h / group),
+// for every attention segment (one half of a CFG pair, or one batch row: its
+// q/k/v rows and an additive bias [rows, rows] or none) and query head h (kv
+// head h / group),
 //
 //   out = softmax(q k^T * scale + bias) v,  rows whose scores are all below
 //   -1e29 (fully masked) -> 0,
@@ -10,18 +11,25 @@
 // lm.cpp:256-274; the reference's CUDA runner uses a SIMT fp32 kernel,
 // cpp/src/backend/cuda/cuda_lm.cu:434-606).  head_dim is 128.
 //
-// One CTA of 128 threads per (segment, head, block of 128 query rows); thread
-// r owns query row r, i.e. TMEM lane r.  Q, K and V^T tiles are converted to
-// fp16 and stored in shared memory in the 128-byte-swizzled K-major layout
-// the MMA reads (two 64-wide K chunks per 128 x 128 tile).  Two passes over
-// the key tiles (128 keys each):
-//   1. S = Q K^T (tcgen05.mma kind::f16, fp32 in TMEM); each thread folds its
-//      row into a running max and sum of exp (the softmax statistics);
-//   2. S again (skipped with a single key tile), P = exp(S - max) / sum in
-//      fp16 written into TMEM, O += P V with P as the A operand from TMEM.
-// The two passes cost a second Q K^T instead of rescaling O in TMEM.  The
-// fp16 inputs make the result agree with the fp32 reference to ~1e-3
-// relative (the fp16 GEMM path's own rounding is 2^-11 per element).
+// One CTA of 512 threads per (segment, head, block of 128 query rows).  Warp
+// w reads TMEM lanes 32 (w % 4) .. + 31 (the rows) and column group w / 4: a
+// quarter of the tile's keys and of O's columns; the four threads of a row
+// combine their maxima and sums through shared memory.  Per tile of 128 keys:
+//   - TMA brings the fp32 K and V tiles (128 x 128, 64 KB each) into staging
+//     shared memory one tile ahead of their use;
+//   - the threads convert them to fp16: K into the 128-byte-swizzled K-major
+//     layout the MMA reads, V transposed (keys along K), keys past the
+//     segment zeroed;
+//   - S = Q K^T (tcgen05.mma kind::f16, fp32 in TMEM);
+//   - each thread turns its row of S into scaled, biased scores, moves its
+//     softmax reference point m when the tile's maximum exceeds it by more
+//     than 8 (then rescaling its running sum and its row of O in TMEM), and
+//     writes P = exp(score - m) as fp16 into TMEM;
+//   - O += P V with P as the A operand from TMEM.
+// Finally O / sum goes to the output.  Keeping m up to 8 below the running
+// maximum bounds P by e^8 (well inside fp16) and skips most rescales; the
+// result is the same softmax.  The fp16 operands make the output agree with
+// the fp32 reference to ~1e-3 relative (2^-11 rounding per element).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -37,30 +45,39 @@ __device__ int g_status_att;
 
 namespace {
 
-constexpr int kErrAttWait = 32;  // an MMA-completion wait gave up
+constexpr int kErrAttRange = 16;  // an input beyond the fp16 range (or NaN)
+constexpr int kErrAttWait = 32;   // a TMA or MMA-completion wait gave up
 constexpr int kAttD = 128;
 constexpr int kAttRows = 128;     // query rows per CTA = TMEM lanes
 constexpr int kAttKeys = 128;     // keys per tile
-constexpr int kAttThreads = 128;
-constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one fp16 operand tile
+#ifndef OVB_ATT_THREADS
+#define OVB_ATT_THREADS 256
+#endif
+constexpr int kAttThreads = OVB_ATT_THREADS;
+constexpr int kCG = kAttThreads / 128;   // column groups (threads per row)
+constexpr int kGCols = kAttKeys / kCG;   // S / O columns per thread
+static_assert(kGCols % 32 == 0, "whole 32-column TMEM chunks per thread");
+constexpr float kRescale = 8.f;   // move m once a tile's max exceeds it by this
+constexpr uint32_t kF16Tile = 128 * 128 * 2;  // one fp16 operand tile
+constexpr uint32_t kF32Tile = 128 * 128 * 4;  // one fp32 staging tile (TMA box)
+constexpr uint32_t kOffQ = 0, kOffK = kF16Tile, kOffV = 2 * kF16Tile;
+constexpr uint32_t kOffStK = 3 * kF16Tile, kOffStV = kOffStK + kF32Tile;
+constexpr uint32_t kOffCtl = kOffStV + kF32Tile;
 constexpr uint32_t kColS = 0, kColP = 128, kColO = 256, kTmemCols = 512;
 
 struct AttnCtl {
-  uint64_t mma;  // one arrival per committed MMA group
+  uint64_t ld_k;   // TMA: K tile (phase i = tile i)
+  uint64_t ld_v;   // TMA: Q (phase 0), then V tile i (phase i + 1)
+  uint64_t mma_s;  // S = Q K^T of tile i complete (phase i)
+  uint64_t mma_o;  // O += P V of tile i complete (phase i)
   uint32_t tmem_base;
   int abort;
 };
+constexpr size_t kAttSmem = 1024 + kOffCtl + sizeof(AttnCtl);
+static_assert(kAttSmem <= 227 * 1024, "attention shared memory");
 
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// 8 fp16 values of row r, K columns c8 .. c8+7 (c8 a multiple of 8) of a
-// 128 x 128 operand stored as two K chunks of [128 rows][64 fp16] with the
-// 128-byte swizzle (16-byte chunk j of row r at position j ^ (r % 8)).
-__device__ __forceinline__ void put8(uint8_t* tile, int r, int c8, uint4 v) {
-  const int chunk = c8 >> 6, j = (c8 & 63) >> 3;
-  *reinterpret_cast<uint4*>(tile + chunk * (kTileBytes / 2) + r * 128 + ((j ^ (r & 7)) << 4)) = v;
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -68,43 +85,66 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Rows [row0, row0 + 128) (beyond `rows`: zeros) x 128 columns of a
-// row-major fp32 matrix (row stride `stride`) into `tile` as fp16.  Each warp
-// reads two 512-byte rows per step.
-__device__ __forceinline__ void stage_rows(uint8_t* tile, const float* src, int64_t stride,
-                                           int row0, int rows) {
-#pragma unroll 4
-  for (int i = threadIdx.x; i < 128 * 16; i += kAttThreads) {
-    const int r = i >> 4, c8 = (i & 15) * 8;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-    if (row0 + r < rows) {
-      const float* p = src + static_cast<int64_t>(row0 + r) * stride + c8;
-      a = *reinterpret_cast<const float4*>(p);
-      b = *reinterpret_cast<const float4*>(p + 4);
-    }
-    put8(tile, r, c8, make_uint4(pack2(a.x, a.y), pack2(a.z, a.w), pack2(b.x, b.y),
-                                 pack2(b.z, b.w)));
-  }
+__device__ __forceinline__ bool in_f16(float x) { return fabsf(x) <= 65504.f; }
+
+// Byte offset of fp16 element (r, c) of a 128 x 128 operand stored as two K
+// chunks of [128 rows][64 fp16] with the 128-byte swizzle (16-byte chunk j of
+// row r at position j ^ (r % 8)).
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return static_cast<uint32_t>((c >> 6) * (kF16Tile / 2) + r * 128 +
+                               ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
 }
 
-// V^T of key rows [row0, row0 + 128): tile row d holds v[row0 .. row0+127][d]
-// (keys along K).  Lane l reads dimension 32*q + l of 8 consecutive keys, so
-// every load instruction of a warp is one 128-byte segment of a key row.
-__device__ __forceinline__ void stage_vt(uint8_t* tile, const float* v, int64_t stride, int row0,
-                                         int rows) {
+// Rows of a row-major fp32 staging tile [128][128] into an fp16 operand
+// tile, rows >= valid as zeros.  Warp w converts rows w, w + 16, ...; lane l
+// columns 4l .. 4l + 3 (one 512-byte row per warp instruction, no bank
+// conflicts).  Returns false if a value is beyond the fp16 range.
+__device__ __forceinline__ bool convert_rows(uint8_t* dst, const float* st, int valid) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int item = warp; item < 4 * 16; item += kAttThreads / 32) {
-    const int q = item & 3, kg = item >> 2;  // dimension quarter, key group of 8
-    const int d = 32 * q + lane;
+  const int c4 = lane * 4;
+  bool ok = true;
+#pragma unroll
+  for (int r = warp; r < kAttKeys; r += kAttThreads / 32) {
+    float4 a = *reinterpret_cast<const float4*>(st + r * kAttD + c4);
+    if (r >= valid) a = make_float4(0.f, 0.f, 0.f, 0.f);
+    ok = ok && in_f16(a.x) && in_f16(a.y) && in_f16(a.z) && in_f16(a.w);
+    *reinterpret_cast<uint2*>(dst + sw_off(r, c4)) = make_uint2(pack2(a.x, a.y), pack2(a.z, a.w));
+  }
+  return ok;
+}
+
+// V^T of a row-major fp32 staging tile [128 keys][128 dims]: thread (g, d)
+// writes groups of 8 keys g, g + kCG, ... of row d of the operand (keys along
+// K), keys >= valid as zeros.  Each load instruction of a warp reads 32
+// consecutive floats of one key row.
+__device__ __forceinline__ bool convert_vt(uint8_t* dst, const float* st, int valid) {
+  const int d = threadIdx.x & (kAttD - 1), g = threadIdx.x / kAttD;
+  bool ok = true;
+#pragma unroll
+  for (int kg = g; kg < kAttKeys / 8; kg += kCG) {
     float x[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int t = row0 + kg * 8 + j;
-      x[j] = t < rows ? v[static_cast<int64_t>(t) * stride + d] : 0.f;
+      const int t = kg * 8 + j;
+      x[j] = t < valid ? st[t * kAttD + d] : 0.f;
+      ok = ok && in_f16(x[j]);
     }
-    put8(tile, d, kg * 8, make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]),
-                                     pack2(x[6], x[7])));
+    *reinterpret_cast<uint4*>(dst + sw_off(d, kg * 8)) =
+        make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
   }
+  return ok;
+}
+
+// 32 consecutive fp32 TMEM columns of this warp's 32 lanes <- r.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  uint32_t a[16], b[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    a[j] = r[j];
+    b[j] = r[16 + j];
+  }
+  tmem_st16(taddr, a);
+  tmem_st16(taddr + 16, b);
 }
 
 }  // namespace
@@ -114,12 +154,18 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* qs = smem;
-  uint8_t* ks = qs + kTileBytes;
-  uint8_t* vt = ks + kTileBytes;
-  AttnCtl* ctl = reinterpret_cast<AttnCtl*>(vt + kTileBytes);
+  AttnCtl* ctl = reinterpret_cast<AttnCtl*>(smem + kOffCtl);
+  const float* stk = reinterpret_cast<const float*>(smem + kOffStK);
+  const float* stv = reinterpret_cast<const float*>(smem + kOffStV);
+  // float [kCG][128] for combining the four threads of a row: the fp16 K
+  // tile, free from the completion of S = Q K^T until the next tile's
+  // conversion (and after the last tile).
+  float* red = reinterpret_cast<float*>(smem + kOffK);
+  const uint32_t sbase = smem_u32(smem);
   volatile int* abort = &ctl->abort;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rloc = (warp & 3) * 32 + lane;  // this thread's row (TMEM lane)
+  const int cg = warp >> 2;                 // its column group
 
   // (segment, query block, head) of this CTA
   const int head = static_cast<int>(blockIdx.x % static_cast<unsigned>(args.n_heads));
@@ -127,17 +173,18 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   int si = 0;
   for (int i = 1; i < args.n_segs; ++i)
     if (qb >= args.segs[i].qblock0) si = i;
-  const AttnSeg sg = args.segs[si];
+  const AttnSeg& sg = args.segs[si];
   const int row0 = (qb - sg.qblock0) * kAttRows;
   const int S = sg.rows;
   const int kv = head / args.group;
-  const float* qbase = args.q + sg.q_off + static_cast<int64_t>(head) * kAttD;
-  const float* kbase = args.k + sg.kv_off + static_cast<int64_t>(kv) * kAttD;
-  const float* vbase = args.v + sg.kv_off + static_cast<int64_t>(kv) * kAttD;
   const int ntiles = (S + kAttKeys - 1) / kAttKeys;
+  const int kx = sg.kv_x + kv * kAttD;
 
   if (tid == 0) {
-    mbar_init(smem_u32(&ctl->mma), 1);
+    mbar_init(smem_u32(&ctl->ld_k), 1);
+    mbar_init(smem_u32(&ctl->ld_v), 1);
+    mbar_init(smem_u32(&ctl->mma_s), 1);
+    mbar_init(smem_u32(&ctl->mma_o), 1);
     ctl->abort = 0;
     fence_mbar_init();
   }
@@ -145,144 +192,207 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     tmem_alloc(smem_u32(&ctl->tmem_base), kTmemCols);
     tmem_relinquish();
   }
-  stage_rows(qs, qbase, args.q_stride, row0, S);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t idesc = idesc_f16(kAttRows, kAttKeys);
-  uint32_t phase = 0;
-  bool ok = true;
-  // Wait for the last committed MMA group; after one wait gives up, every
-  // later wait of the CTA returns at once (the outputs are then invalid and
-  // status bit 32 is set).
-  auto wait_mma = [&]() {
-    if (!ovb_wait(smem_u32(&ctl->mma), phase, abort)) {
+  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  const uint32_t s_col = tmem + lane_off + kColS + static_cast<uint32_t>(cg * kGCols);
+  const uint32_t p_col = tmem + lane_off + kColP + static_cast<uint32_t>(cg * kGCols / 2);
+  const uint32_t o_col = tmem + lane_off + kColO + static_cast<uint32_t>(cg * kGCols);
+  uint32_t ph_k = 0, ph_v = 0, ph_s = 0, ph_o = 0;
+  bool ok = true, in_range = true;
+  auto wait = [&](uint64_t* bar, uint32_t& phase) {
+    if (!ovb_wait(smem_u32(bar), phase, abort)) {
       ok = false;
       *abort = 1;
     }
     phase ^= 1u;
   };
 
-  // S = Q K^T for the staged key tile, then wait for it (all threads).
-  auto qk = [&]() {
+  if (tid == 0) {
+    mbar_arrive_expect_tx(smem_u32(&ctl->ld_v), kF32Tile);
+    tma_load_2d(sbase + kOffStV, &args.tm_q, sg.q_x + head * kAttD, sg.q_y + row0,
+                smem_u32(&ctl->ld_v));
+    mbar_arrive_expect_tx(smem_u32(&ctl->ld_k), kF32Tile);
+    tma_load_2d(sbase + kOffStK, &args.tm_k, kx, sg.kv_y, smem_u32(&ctl->ld_k));
+  }
+  wait(&ctl->ld_v, ph_v);
+  in_range = convert_rows(smem + kOffQ, stv, S - row0) && in_range;
+  __syncthreads();  // staging of V free again
+  if (tid == 0) {
+    mbar_arrive_expect_tx(smem_u32(&ctl->ld_v), kF32Tile);
+    tma_load_2d(sbase + kOffStV, &args.tm_v, kx, sg.kv_y, smem_u32(&ctl->ld_v));
+  }
+
+  const int row = row0 + rloc;
+  const bool row_ok = row < S;
+  const float* brow = sg.bias ? sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S : nullptr;
+  // (S % 4 == 0 with a 16-byte aligned base: every row and every 4-key group
+  // of a tile is 16-byte aligned and lies wholly inside or past the row)
+  const bool bias_vec = !sg.bias || ((S & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.bias) & 15) == 0);
+  float m = -INFINITY;   // softmax reference point (running max - 8 <= m <= running max)
+  float mt = -INFINITY;  // running maximum of this thread's scores (fully-masked test)
+  float l = 0.f;         // this thread's part of the sum of exp(score - m)
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int valid = S - t * kAttKeys;
+    wait(&ctl->ld_k, ph_k);
+    in_range = convert_rows(smem + kOffK, stk, valid) && in_range;
+    if (t > 0) wait(&ctl->mma_o, ph_o);  // P V of the previous tile done: V^T and P free
+    wait(&ctl->ld_v, ph_v);
+    in_range = convert_vt(smem + kOffV, stv, valid) && in_range;
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();  // operands staged, staging buffers free
     if (tid == 0) {
+      if (t + 1 < ntiles) {
+        const int ky = sg.kv_y + (t + 1) * kAttKeys;
+        mbar_arrive_expect_tx(smem_u32(&ctl->ld_k), kF32Tile);
+        tma_load_2d(sbase + kOffStK, &args.tm_k, kx, ky, smem_u32(&ctl->ld_k));
+        mbar_arrive_expect_tx(smem_u32(&ctl->ld_v), kF32Tile);
+        tma_load_2d(sbase + kOffStV, &args.tm_v, kx, ky, smem_u32(&ctl->ld_v));
+      }
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < kAttD / 16; ++kk) {
-        const uint32_t off = static_cast<uint32_t>((kk >> 2) * (kTileBytes / 2));
-        const uint32_t kb = static_cast<uint32_t>((kk & 3) * 32);
-        mma_f16_ss(tmem + kColS, sw128_kmajor_desc(smem_u32(qs) + off, kb),
-                   sw128_kmajor_desc(smem_u32(ks) + off, kb), idesc, kk > 0 ? 1u : 0u);
+        const uint32_t off = static_cast<uint32_t>((kk >> 2) * (kF16Tile / 2) + (kk & 3) * 32);
+        mma_f16_ss(tmem + kColS, sw128_kmajor_desc(sbase + kOffQ, off),
+                   sw128_kmajor_desc(sbase + kOffK, off), idesc_f16(kAttRows, kAttKeys),
+                   kk > 0 ? 1u : 0u);
       }
-      tc_commit(smem_u32(&ctl->mma));
+      tc_commit(smem_u32(&ctl->mma_s));
     }
-    wait_mma();
+    // this thread's bias values of the tile, loaded while the MMA runs: 16-byte
+    // loads when every bias row starts 16-byte aligned, else one float each
+    const int key0 = t * kAttKeys + cg * kGCols;
+    float bias[kGCols];
+    if (bias_vec) {
+#pragma unroll
+      for (int j = 0; j < kGCols; j += 4) {
+        const float4 b = ld_f4_if(brow + key0 + j, brow != nullptr && key0 + j < S);
+        bias[j] = b.x;
+        bias[j + 1] = b.y;
+        bias[j + 2] = b.z;
+        bias[j + 3] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGCols; ++j) bias[j] = key0 + j < S ? brow[key0 + j] : 0.f;
+    }
+    wait(&ctl->mma_s, ph_s);
     tc_fence_after();
-  };
 
-  // This thread's scores of key tile `t` (chunk c of 32 keys), scaled, biased
-  // and masked past the segment.
-  const int row = row0 + tid;
-  const bool row_ok = row < S;
-  const float* brow = sg.bias ? sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S : nullptr;
-  auto scores = [&](int t, int c, float (&x)[32]) {
-    uint32_t u[32];
-    tmem_ld32(tmem + lane_off + kColS + static_cast<uint32_t>(c * 32), u);
-    tc_wait_ld32(u);
+    // scores (scaled, biased, -inf past the segment) back into S; tile max
+    float tmax = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int key = t * kAttKeys + c * 32 + j;
-      float s = __fmul_rn(__uint_as_float(u[j]), args.scale);
-      if (brow && key < S) s = __fadd_rn(s, brow[key]);
-      x[j] = key < S ? s : -INFINITY;
+    for (int c = 0; c < kGCols / 32; ++c) {
+      uint32_t u[32];
+      tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u);
+      tc_wait_ld32(u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int key = key0 + c * 32 + j;
+        float x = __fadd_rn(__fmul_rn(__uint_as_float(u[j]), args.scale), bias[c * 32 + j]);
+        x = key < S ? x : -INFINITY;
+        tmax = fmaxf(tmax, x);
+        u[j] = __float_as_uint(x);
+      }
+      tmem_st32(s_col + static_cast<uint32_t>(c * 32), u);
     }
-  };
-
-  // ---- pass 1: running max and sum of exp per row
-  float m = -INFINITY, l = 0.f;
-  for (int t = 0; t < ntiles; ++t) {
-    stage_rows(ks, kbase, args.kv_stride, t * kAttKeys, S);
-    fence_proxy_async();
+    mt = fmaxf(mt, tmax);
+    red[cg * kAttRows + rloc] = tmax;
     __syncthreads();
-    qk();
-    for (int c = 0; c < kAttKeys / 32; ++c) {
-      float x[32];
-      scores(t, c, x);
-      float cm = m;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) cm = fmaxf(cm, x[j]);
-      if (cm > -INFINITY) {
-        float sum = 0.f;
+    for (int g = 0; g < kCG; ++g) tmax = fmaxf(tmax, red[g * kAttRows + rloc]);
+    float factor = 1.f;
+    if (tmax > m + kRescale) {  // also the first finite tile max (m = -inf)
+      factor = m == -INFINITY ? 0.f : __expf(__fsub_rn(m, tmax));
+      l = __fmul_rn(l, factor);
+      m = tmax;
+    }
+    tc_wait_st();
+    if (t > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sum = __fadd_rn(sum, __expf(__fsub_rn(x[j], cm)));
-        l = __fadd_rn(__fmul_rn(l, __expf(__fsub_rn(m, cm))), sum);
-        m = cm;
+      for (int c = 0; c < kGCols / 32; ++c) {
+        uint32_t u[32];
+        tmem_ld32(o_col + static_cast<uint32_t>(c * 32), u);
+        tc_wait_ld32(u);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__fmul_rn(__uint_as_float(u[j]), factor));
+        tmem_st32(o_col + static_cast<uint32_t>(c * 32), u);
       }
     }
-    tc_fence_before();
-    __syncthreads();  // the key tile and S are reused
-  }
-  const bool masked = !(m >= -1e29f);  // the reference's fully masked rows -> 0
-  const float inv_l = masked || l <= 0.f ? 0.f : __fdividef(1.f, l);
-
-  // ---- pass 2: P = exp(S - m) / l into TMEM, O += P V
-  for (int t = 0; t < ntiles; ++t) {
-    if (ntiles > 1) stage_rows(ks, kbase, args.kv_stride, t * kAttKeys, S);
-    stage_vt(vt, vbase, args.kv_stride, t * kAttKeys, S);
-    fence_proxy_async();
-    __syncthreads();
-    if (ntiles > 1) qk();
-    for (int c = 0; c < kAttKeys / 32; ++c) {
-      float x[32];
-      scores(t, c, x);
-      uint32_t pk[16];
+    const float mexp = m == -INFINITY ? 0.f : m;
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        pk[j] = pack2(__fmul_rn(__expf(__fsub_rn(x[2 * j], m)), inv_l),
-                      __fmul_rn(__expf(__fsub_rn(x[2 * j + 1], m)), inv_l));
-      tmem_st16(tmem + lane_off + kColP + static_cast<uint32_t>(c * 16), pk);
+    for (int c = 0; c < kGCols / 32; ++c) {
+      uint32_t u[32];
+      tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u);
+      tc_wait_ld32(u);
+      uint32_t pk[16];
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float p0 = __expf(__fsub_rn(__uint_as_float(u[2 * j]), mexp));
+        const float p1 = __expf(__fsub_rn(__uint_as_float(u[2 * j + 1]), mexp));
+        sum = __fadd_rn(sum, __fadd_rn(p0, p1));
+        pk[j] = pack2(p0, p1);
+      }
+      l = __fadd_rn(l, sum);
+      tmem_st16(p_col + static_cast<uint32_t>(c * 16), pk);
     }
     tc_wait_st();
     tc_fence_before();
-    __syncthreads();  // P of every row is in TMEM
+    __syncthreads();  // P and the rescaled O of every row are in TMEM
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < kAttKeys / 16; ++kk) {
-        const uint32_t off = static_cast<uint32_t>((kk >> 2) * (kTileBytes / 2));
-        const uint32_t kb = static_cast<uint32_t>((kk & 3) * 32);
+        const uint32_t off = static_cast<uint32_t>((kk >> 2) * (kF16Tile / 2) + (kk & 3) * 32);
         mma_f16_ts(tmem + kColO, tmem + kColP + static_cast<uint32_t>(kk * 8),
-                   sw128_kmajor_desc(smem_u32(vt) + off, kb), idesc_f16(kAttRows, kAttD),
+                   sw128_kmajor_desc(sbase + kOffV, off), idesc_f16(kAttRows, kAttD),
                    (t > 0 || kk > 0) ? 1u : 0u);
       }
-      tc_commit(smem_u32(&ctl->mma));
+      tc_commit(smem_u32(&ctl->mma_o));
     }
-    wait_mma();
-    tc_fence_after();
-    __syncthreads();  // V^T, the key tile, S and P are reused
   }
+  wait(&ctl->mma_o, ph_o);
+  tc_fence_after();
 
-  // ---- O (already normalised) to the output rows
-  if (tid == 0 && (!ok || *abort)) atomicOr(&g_status_att, kErrAttWait);
-  float* orow = args.out + sg.q_off + static_cast<int64_t>(head) * kAttD +
+  // ---- the row's total sum and maximum, then O / l to the output rows
+  red[cg * kAttRows + rloc] = l;
+  __syncthreads();
+  float lsum = 0.f;
+#pragma unroll
+  for (int g = 0; g < kCG; ++g) lsum = __fadd_rn(lsum, red[g * kAttRows + rloc]);
+  __syncthreads();
+  red[cg * kAttRows + rloc] = mt;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kCG; ++g) mt = fmaxf(mt, red[g * kAttRows + rloc]);
+  const bool masked = !(mt >= -1e29f);  // the reference's fully masked rows -> 0
+  const float inv_l = masked || !(lsum > 0.f) ? 0.f : __frcp_rn(lsum);
+  float* orow = args.out + sg.q_off + static_cast<int64_t>(head) * kAttD + cg * kGCols +
                 static_cast<int64_t>(row_ok ? row : 0) * args.q_stride;
-  for (int c = 0; c < kAttD / 32; ++c) {
+#pragma unroll
+  for (int c = 0; c < kGCols / 32; ++c) {
     uint32_t u[32];
-    tmem_ld32(tmem + lane_off + kColO + static_cast<uint32_t>(c * 32), u);
+    tmem_ld32(o_col + static_cast<uint32_t>(c * 32), u);
     tc_wait_ld32(u);
     if (row_ok) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4*>(orow + c * 32 + j) =
-            masked ? make_float4(0.f, 0.f, 0.f, 0.f)
-                   : make_float4(__uint_as_float(u[j]), __uint_as_float(u[j + 1]),
-                                 __uint_as_float(u[j + 2]), __uint_as_float(u[j + 3]));
+            make_float4(__fmul_rn(__uint_as_float(u[j]), inv_l),
+                        __fmul_rn(__uint_as_float(u[j + 1]), inv_l),
+                        __fmul_rn(__uint_as_float(u[j + 2]), inv_l),
+                        __fmul_rn(__uint_as_float(u[j + 3]), inv_l));
     }
   }
+  if (!in_range) atomicOr(&g_status_att, kErrAttRange);
   tc_fence_before();
   __syncthreads();
+  if (tid == 0 && (!ok || *abort)) atomicOr(&g_status_att, kErrAttWait);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -290,21 +400,20 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 }
 
 cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s) {
-  constexpr size_t kSmem = 1024 + 3 * kTileBytes + sizeof(AttnCtl) + 20 * 1024;  // 1 CTA / SM
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmem));
+                                         static_cast<int>(kAttSmem));
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   // Plain launch: TMEM is allocated at entry, before any wait on the
   // preceding grid could be placed.
   return launch_plain(attention_kernel, dim3(static_cast<unsigned>(total_qblocks * args.n_heads)),
-                    dim3(kAttThreads), kSmem, s, args);
+                      dim3(kAttThreads), kAttSmem, s, args);
 }
 
 cudaError_t read_and_clear_status_att(int* out, cudaStream_t s) {

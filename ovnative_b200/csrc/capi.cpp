@@ -760,33 +760,52 @@ int ovb_attention(const float* q, const float* k, const float* v, float* out, in
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) ||
       q_stride % 4 != 0 || kv_stride % 4 != 0)
     return invalid("q/k/v/out must be 16-byte aligned with strides a multiple of 4");
+  if (q_stride > (int64_t{1} << 30) || kv_stride > (int64_t{1} << 30))
+    return invalid("row strides too large");
   ovb::AttnArgs a = {};
-  a.q = q;
-  a.k = k;
-  a.v = v;
   a.out = out;
   a.q_stride = q_stride;
-  a.kv_stride = kv_stride;
   a.n_heads = n_heads;
   a.group = n_heads / n_kv;
   a.scale = scale;
-  int64_t blocks = 0;
+  int64_t blocks = 0, q_rows = 1, kv_rows = 1;
   for (int i = 0; i < n_segs; ++i) {
     const ovb_attn_segment& g = segs[i];
     if (g.rows < 0 || g.q_off < 0 || g.kv_off < 0) return invalid("negative segment field");
     if (g.q_off % 4 != 0 || g.kv_off % 4 != 0)
       return invalid("segment offsets must be multiples of 4");
     if (g.rows == 0) continue;
+    const int64_t qx = g.q_off % q_stride, qy = g.q_off / q_stride;
+    const int64_t kx = g.kv_off % kv_stride, ky = g.kv_off / kv_stride;
+    // every head of every row must lie within one row of the 2-D view
+    if (qx + int64_t{n_heads} * head_dim > q_stride || kx + int64_t{n_kv} * head_dim > kv_stride)
+      return invalid("segment offset leaves no room for every head within a row");
+    if (qy + g.rows > (int64_t{1} << 31) - 1 - 128 || ky + g.rows > (int64_t{1} << 31) - 1 - 128)
+      return invalid("segment rows too large");
     ovb::AttnSeg& d = a.segs[a.n_segs++];
     d.bias = g.bias;
     d.q_off = g.q_off;
-    d.kv_off = g.kv_off;
     d.rows = g.rows;
     d.qblock0 = static_cast<int>(blocks);
+    d.q_x = static_cast<int>(qx);
+    d.q_y = static_cast<int>(qy);
+    d.kv_x = static_cast<int>(kx);
+    d.kv_y = static_cast<int>(ky);
+    q_rows = std::max(q_rows, qy + g.rows);
+    kv_rows = std::max(kv_rows, ky + g.rows);
     blocks += (g.rows + 127) / 128;
     if (blocks * n_heads > (int64_t{1} << 31) - 1) return invalid("too many query blocks");
   }
   if (blocks == 0) return OVB_OK;
+  // fp32 views {row stride, rows} with a 128 x 128 box; rows past the last
+  // segment read as zeros.
+  if (!ovb::encode_tmap_2d(&a.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q_stride, q_rows,
+                           q_stride * 4, 128, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !ovb::encode_tmap_2d(&a.tm_k, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kv_stride, kv_rows,
+                           kv_stride * 4, 128, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !ovb::encode_tmap_2d(&a.tm_v, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, kv_stride, kv_rows,
+                           kv_stride * 4, 128, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return OVB_ERR_INTERNAL;
   if (cuda_failed(ovb::launch_attention(a, static_cast<int>(blocks), as_stream(stream)),
                   "attention launch"))
     return OVB_ERR_INTERNAL;

@@ -186,23 +186,25 @@ cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* u
                                  int V, int T, float guidance, float penalty, int mask_id,
                                  int32_t* pred, float* scores, cudaStream_t s);
 // Attention (attention.cu).  One segment as the kernel sees it: the
-// reference's AttnSegment (bias, rows, q_off, kv_off; element offsets) plus
-// the index of its first 128-row query block in the launch.
+// reference's AttnSegment (bias, rows, q_off, kv_off; element offsets), the
+// same offsets as (column, row) coordinates of the q and k/v tensor maps,
+// and the index of its first 128-row query block in the launch.
 constexpr int kAttMaxSegs = 64;
 struct AttnSeg {
   const float* bias;  // [rows, rows] additive, or null
   int64_t q_off;      // element offset of the segment's first query row
-  int64_t kv_off;     // element offset of its first key / value row
   int rows;
   int qblock0;
+  int q_x, q_y;       // q_off = q_y * q_stride + q_x
+  int kv_x, kv_y;     // kv_off = kv_y * kv_stride + kv_x
 };
 struct AttnArgs {
-  const float* q;  // [*, q_stride]: head h at column h * 128
-  const float* k;  // [*, kv_stride]: kv head j at column j * 128
-  const float* v;
-  float* out;      // laid out like q
+  // fp32 2-D maps of q and k / v: {row stride, rows} elements, box 128 x 128
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  float* out;      // laid out like q: head h of row s at q_off + s * q_stride + h * 128
   int64_t q_stride;
-  int64_t kv_stride;
   int n_heads;
   int group;       // query heads per kv head
   int n_segs;

@@ -89,7 +89,9 @@ def test_abi_rejects_bad_arguments(kw):
 def test_abi_rejects_bad_segments():
     import ovnative_b200._lib as L
     for seg in (L.AttnSegment(None, -1, 0, 0), L.AttnSegment(None, 4, 2, 0),
-                L.AttnSegment(None, 4, 0, -4)):
+                L.AttnSegment(None, 4, 0, -4),
+                L.AttnSegment(None, 4, 4, 0),     # head 1 would wrap into the next row
+                L.AttnSegment(None, 4, 0, 132)):
         arr = (L.AttnSegment * 1)(seg)
         assert _call(segs=C.cast(arr, C.POINTER(L.AttnSegment))) == L.OVB_ERR_INVALID_ARG
 

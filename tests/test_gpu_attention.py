@@ -112,3 +112,53 @@ def test_many_segments(cuda):
     q, k, v, segs = make_case(rng, rows, 4, 2, masked_rows=(0,))
     scale = 0.09
     compare(run(q, k, v, segs, 4, 2, scale, cuda), O.attention(q, k, v, segs, 4, 2, D, scale))
+
+
+def test_strided_views_with_column_offset(cuda):
+    """q / k / v as column windows of wider row-major buffers (row stride
+    larger than the heads, segment offsets not at column 0), through the C
+    ABI directly."""
+    import ctypes as C
+    import ovnative_b200._lib as L
+    rng = np.random.default_rng(21)
+    seg_rows = (140, 70)
+    q, k, v, segs = make_case(rng, seg_rows, 8, 2, masked_rows=(4,), pad_keys=3)
+    T, QD, KVD = q.shape[0], q.shape[1], k.shape[1]
+    qpad, kvpad = 256, 132
+    qb = np.zeros((T, QD + qpad), np.float32)
+    kb = np.zeros((T, KVD + kvpad), np.float32)
+    vb = np.zeros((T, KVD + kvpad), np.float32)
+    qb[:, qpad:] = q
+    kb[:, kvpad:] = k
+    vb[:, kvpad:] = v
+    tq, tk, tv = (torch.from_numpy(x).to(cuda) for x in (qb, kb, vb))
+    out = torch.zeros_like(tq)
+    biases = [torch.from_numpy(b).to(cuda) for b, _, _, _ in segs]
+    arr = (L.AttnSegment * len(segs))()
+    r0 = 0
+    for i, (_, rows, _, _) in enumerate(segs):
+        arr[i] = L.AttnSegment(biases[i].data_ptr(), rows, r0 * (QD + qpad) + qpad,
+                               r0 * (KVD + kvpad) + kvpad)
+        r0 += rows
+    L.check(L.lib().ovb_attention(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), out.data_ptr(),
+                                  QD + qpad, KVD + kvpad, 8, 2, D, 0.07,
+                                  C.cast(arr, C.POINTER(L.AttnSegment)), len(segs),
+                                  torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert ovb.device_status() == 0
+    got = out.cpu().numpy()
+    assert not got[:, :qpad].any()
+    compare(got[:, qpad:], O.attention(q, k, v, segs, 8, 2, D, 0.07))
+
+
+def test_fp16_range_flag(cuda):
+    """A value beyond the fp16 range sets status bit 16 (and is cleared by
+    the read)."""
+    rng = np.random.default_rng(8)
+    q, k, v, segs = make_case(rng, (40,), 2, 1)
+    k[3, 5] = 1e5
+    tq, tk, tv = (torch.from_numpy(x).to(cuda) for x in (q, k, v))
+    ovb.attention(tq, tk, tv, [(None, 40, 0, 0)], 2, 1, 0.05)
+    torch.cuda.synchronize()
+    assert ovb.device_status() == 16
+    assert ovb.device_status() == 0
