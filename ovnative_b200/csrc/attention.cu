@@ -45,7 +45,7 @@ __device__ int g_status_att;
 
 namespace {
 
-constexpr int kErrAttRange = 16;  // an input beyond the fp16 range (or NaN)
+constexpr int kErrAttRange = 16;  // an input beyond the fp16 range
 constexpr int kErrAttWait = 32;   // a TMA or MMA-completion wait gave up
 constexpr int kAttD = 128;
 constexpr int kAttRows = 128;     // query rows per CTA = TMEM lanes
@@ -85,8 +85,6 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ bool in_f16(float x) { return fabsf(x) <= 65504.f; }
-
 // Byte offset of fp16 element (r, c) of a 128 x 128 operand stored as two K
 // chunks of [128 rows][64 fp16] with the 128-byte swizzle (16-byte chunk j of
 // row r at position j ^ (r % 8)).
@@ -96,43 +94,50 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
 }
 
 // Rows of a row-major fp32 staging tile [128][128] into an fp16 operand
-// tile, rows >= valid as zeros.  Warp w converts rows w, w + 16, ...; lane l
-// columns 4l .. 4l + 3 (one 512-byte row per warp instruction, no bank
-// conflicts).  Returns false if a value is beyond the fp16 range.
-__device__ __forceinline__ bool convert_rows(uint8_t* dst, const float* st, int valid) {
+// tile, rows >= valid as zeros.  Warp w converts rows w, w + kAttThreads/32,
+// ...; lane l columns 4l .. 4l + 3 (one 512-byte row per warp instruction, no
+// bank conflicts).  Returns the largest |value| converted (NaN ignored).
+__device__ __forceinline__ float convert_rows(uint8_t* dst, const float* st, int valid) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c4 = lane * 4;
-  bool ok = true;
+  float amax = 0.f;
 #pragma unroll
   for (int r = warp; r < kAttKeys; r += kAttThreads / 32) {
     float4 a = *reinterpret_cast<const float4*>(st + r * kAttD + c4);
     if (r >= valid) a = make_float4(0.f, 0.f, 0.f, 0.f);
-    ok = ok && in_f16(a.x) && in_f16(a.y) && in_f16(a.z) && in_f16(a.w);
+    amax = fmaxf(fmaxf(amax, fabsf(a.x)), fmaxf(fabsf(a.y), fmaxf(fabsf(a.z), fabsf(a.w))));
     *reinterpret_cast<uint2*>(dst + sw_off(r, c4)) = make_uint2(pack2(a.x, a.y), pack2(a.z, a.w));
   }
-  return ok;
+  return amax;
 }
 
-// V^T of a row-major fp32 staging tile [128 keys][128 dims]: thread (g, d)
-// writes groups of 8 keys g, g + kCG, ... of row d of the operand (keys along
-// K), keys >= valid as zeros.  Each load instruction of a warp reads 32
-// consecutive floats of one key row.
-__device__ __forceinline__ bool convert_vt(uint8_t* dst, const float* st, int valid) {
-  const int d = threadIdx.x & (kAttD - 1), g = threadIdx.x / kAttD;
-  bool ok = true;
+// V^T of a row-major fp32 staging tile [128 keys][128 dims]: thread (g, p)
+// writes rows 2p and 2p + 1 of the operand (keys along K) for the groups of
+// 8 keys g, g + kCG', ... (kCG' = kAttThreads / 64), keys >= valid as zeros.
+// Each 8-byte load instruction of a warp reads 256 consecutive bytes of one
+// key row.  Returns the largest |value| converted.
+__device__ __forceinline__ float convert_vt(uint8_t* dst, const float* st, int valid) {
+  constexpr int kGroups = kAttThreads / 64;
+  const int p = threadIdx.x & 63, g = threadIdx.x >> 6;
+  float amax = 0.f;
 #pragma unroll
-  for (int kg = g; kg < kAttKeys / 8; kg += kCG) {
-    float x[8];
+  for (int kg = g; kg < kAttKeys / 8; kg += kGroups) {
+    float2 x[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int t = kg * 8 + j;
-      x[j] = t < valid ? st[t * kAttD + d] : 0.f;
-      ok = ok && in_f16(x[j]);
+      x[j] = t < valid ? *reinterpret_cast<const float2*>(st + t * kAttD + 2 * p)
+                       : make_float2(0.f, 0.f);
+      amax = fmaxf(amax, fmaxf(fabsf(x[j].x), fabsf(x[j].y)));
     }
-    *reinterpret_cast<uint4*>(dst + sw_off(d, kg * 8)) =
-        make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+    *reinterpret_cast<uint4*>(dst + sw_off(2 * p, kg * 8)) =
+        make_uint4(pack2(x[0].x, x[1].x), pack2(x[2].x, x[3].x), pack2(x[4].x, x[5].x),
+                   pack2(x[6].x, x[7].x));
+    *reinterpret_cast<uint4*>(dst + sw_off(2 * p + 1, kg * 8)) =
+        make_uint4(pack2(x[0].y, x[1].y), pack2(x[2].y, x[3].y), pack2(x[4].y, x[5].y),
+                   pack2(x[6].y, x[7].y));
   }
-  return ok;
+  return amax;
 }
 
 // 32 consecutive fp32 TMEM columns of this warp's 32 lanes <- r.
@@ -201,7 +206,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const uint32_t p_col = tmem + lane_off + kColP + static_cast<uint32_t>(cg * kGCols / 2);
   const uint32_t o_col = tmem + lane_off + kColO + static_cast<uint32_t>(cg * kGCols);
   uint32_t ph_k = 0, ph_v = 0, ph_s = 0, ph_o = 0;
-  bool ok = true, in_range = true;
+  bool ok = true;
+  float amax = 0.f;  // largest |q|, |k|, |v| converted (fp16 range check)
   auto wait = [&](uint64_t* bar, uint32_t& phase) {
     if (!ovb_wait(smem_u32(bar), phase, abort)) {
       ok = false;
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     tma_load_2d(sbase + kOffStK, &args.tm_k, kx, sg.kv_y, smem_u32(&ctl->ld_k));
   }
   wait(&ctl->ld_v, ph_v);
-  in_range = convert_rows(smem + kOffQ, stv, S - row0) && in_range;
+  amax = fmaxf(amax, convert_rows(smem + kOffQ, stv, S - row0));
   __syncthreads();  // staging of V free again
   if (tid == 0) {
     mbar_arrive_expect_tx(smem_u32(&ctl->ld_v), kF32Tile);
@@ -237,11 +243,29 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 
   for (int t = 0; t < ntiles; ++t) {
     const int valid = S - t * kAttKeys;
+    // this thread's bias values of the tile, issued first so that they land
+    // during the conversions and the MMA: 16-byte loads when every bias row
+    // starts 16-byte aligned, else one float each
+    const int key0 = t * kAttKeys + cg * kGCols;
+    float bias[kGCols];
+    if (bias_vec) {
+#pragma unroll
+      for (int j = 0; j < kGCols; j += 4) {
+        const float4 b = ld_f4_if(brow + key0 + j, brow != nullptr && key0 + j < S);
+        bias[j] = b.x;
+        bias[j + 1] = b.y;
+        bias[j + 2] = b.z;
+        bias[j + 3] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGCols; ++j) bias[j] = key0 + j < S ? brow[key0 + j] : 0.f;
+    }
     wait(&ctl->ld_k, ph_k);
-    in_range = convert_rows(smem + kOffK, stk, valid) && in_range;
+    amax = fmaxf(amax, convert_rows(smem + kOffK, stk, valid));
     if (t > 0) wait(&ctl->mma_o, ph_o);  // P V of the previous tile done: V^T and P free
     wait(&ctl->ld_v, ph_v);
-    in_range = convert_vt(smem + kOffV, stv, valid) && in_range;
+    amax = fmaxf(amax, convert_vt(smem + kOffV, stv, valid));
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();  // operands staged, staging buffers free
@@ -262,23 +286,6 @@ __global__ void __launch_bounds__(kAttThreads, 1)
                    kk > 0 ? 1u : 0u);
       }
       tc_commit(smem_u32(&ctl->mma_s));
-    }
-    // this thread's bias values of the tile, loaded while the MMA runs: 16-byte
-    // loads when every bias row starts 16-byte aligned, else one float each
-    const int key0 = t * kAttKeys + cg * kGCols;
-    float bias[kGCols];
-    if (bias_vec) {
-#pragma unroll
-      for (int j = 0; j < kGCols; j += 4) {
-        const float4 b = ld_f4_if(brow + key0 + j, brow != nullptr && key0 + j < S);
-        bias[j] = b.x;
-        bias[j + 1] = b.y;
-        bias[j + 2] = b.z;
-        bias[j + 3] = b.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kGCols; ++j) bias[j] = key0 + j < S ? brow[key0 + j] : 0.f;
     }
     wait(&ctl->mma_s, ph_s);
     tc_fence_after();
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
                         __fmul_rn(__uint_as_float(u[j + 3]), inv_l));
     }
   }
-  if (!in_range) atomicOr(&g_status_att, kErrAttRange);
+  if (amax > 65504.f) atomicOr(&g_status_att, kErrAttRange);
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && (!ok || *abort)) atomicOr(&g_status_att, kErrAttWait);
