@@ -261,7 +261,8 @@ typedef struct ovb_attn_segment {
  * a row whose scores are all below -1e29 (fully masked) giving zeros --
  * ov::attention_head_f32 (cpp/src/backend/cpu/ops_cpu.cpp:907-943) over the
  * loop of LM::run_layer (cpp/src/model/lm.cpp:256-274); the reference's CUDA
- * runner does the same in cpp/src/backend/cuda/cuda_lm.cu:434-606.  Row s of
+ * runner does the same with a SIMT kernel or TF32 cuBLAS (cpp/src/backend/
+ * cuda/cuda_lm.cu:393-421, :423-606, dispatched at :1132-1145).  Row s of
  * head h of q and out is at element q_off + s * q_stride + h * head_dim; of
  * k / v at kv_off + t * kv_stride + kv * head_dim.  head_dim must be 128;
  * q/k/v/out 16-byte aligned; strides and offsets multiples of 4 elements;

@@ -8,8 +8,9 @@
 //
 // as ov::attention_head_f32 computes it (cpp/src/backend/cpu/ops_cpu.cpp:
 // 907-943, called per (segment, head) by LM::run_layer, cpp/src/model/
-// lm.cpp:256-274; the reference's CUDA runner uses a SIMT fp32 kernel,
-// cpp/src/backend/cuda/cuda_lm.cu:434-606).  head_dim is 128.
+// lm.cpp:256-274; the reference's CUDA runner dispatches between a SIMT fp32
+// kernel and TF32 strided-batched cuBLAS, cpp/src/backend/cuda/cuda_lm.cu:
+// 393-421, :423-606, :1132-1145).  head_dim is 128.
 //
 // One CTA of 512 threads per (segment, head, block of 128 query rows).  Warp
 // w reads TMEM lanes 32 (w % 4) .. + 31 (the rows) and column group w / 4: a
