@@ -546,6 +546,102 @@ def sampler_cpu_baseline(budget_s: float = 1.0) -> dict:
             "sample": f"{n} x {C * T_s} rows in {sec:.2f} s, scaled to {C * sp['target_len']} rows"}
 
 
+# ------------------------------------------------------------ GEMM M-sweep
+# Config 4's isolated GEMM sweep: every LM projection shape at M = 16 ... 8192,
+# both mainloops, weights rotating over enough copies to exceed L2.
+SWEEP_SHAPES = {"q": (2048, 1024, False), "k/v": (1024, 1024, False), "o": (1024, 2048, True),
+                "gate/up": (3072, 1024, False), "down": (1024, 3072, True),
+                "qkv": (4096, 1024, False), "gate_up": (6144, 1024, False),
+                "heads": (8200, 1024, False)}
+SWEEP_M = (16, 64, 256, 1024, 4096, 8192)
+
+
+def time_gemm_sweep(dev, stream, f16: bool, shapes=None, ms=SWEEP_M) -> list:
+    """Device time per launch of one GEMM (CUDA events around a graph of
+    launches) for every shape and M; weights rotate over copies totalling
+    more than 150 MB so that every launch reads its weight from HBM."""
+    import torch
+    import ovnative_b200 as ovb
+    out = []
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    kern = "gemm_h (fp16 mainloop)" if f16 else "gemm_s8_tc (int8 mainloop)"
+    for name, (N, K, res) in (shapes or SWEEP_SHAPES).items():
+        n_w = max(2, -(-150_000_000 // (N * K * (3 if f16 else 1))))
+        ws = []
+        for _ in range(n_w):
+            W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=gen)
+            sc = torch.rand((N,), device=dev, generator=gen) * (0.02 / 127)
+            ws.append(ovb.Weight.from_nk(W, sc, f16=f16))
+            del W
+        for M in ms:
+            A = torch.randn((M, K), device=dev, generator=gen)
+            aq = ovb.s8_nk_quantize(A, f16=f16)
+            C = torch.zeros((M, N), device=dev)
+            if f16:
+                fn = lambda w: ovb.linear_h(aq[0], w, C, accumulate=res)  # noqa: E731
+            elif res:
+                fn = lambda w: ovb.linear_s8_nk_packed_q_add(aq[0], aq[1], w, C)  # noqa: E731
+            else:
+                fn = lambda w: ovb.linear_s8_nk_packed_q(aq[0], aq[1], w, C)  # noqa: E731
+            launches = max(2 * n_w, 8)
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    fn(ws[i % n_w])
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(launches):
+                        fn(ws[i % n_w])
+                g.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / launches
+            g.reset()
+            r = gemm_roofline(name, kern, M, N, K, res, 4 * M * N, us, f16)
+            out.append({"shape": name, "M": M, "N": N, "K": K, "us": r["us_per_launch"],
+                        "tops": round(2 * M * N * K / (us * 1e-6) / 1e12, 1),
+                        "bound": r["bound"], "frac": r["frac"], "roofline_us": r["roofline_us"]})
+            del A, aq, C
+        for w in ws:
+            w.close()
+    if ovb.device_status() != 0:
+        raise RuntimeError("bounded device wait timed out in the GEMM sweep")
+    return out
+
+
+def sweep_cpu_baseline(points, budget_s: float = 0.15) -> dict:
+    """The reference's own int8 GEMM (linear_s8_nk_packed_q, AVX-VNNI,
+    OpenMP on all host cores, through oracle/_ref) at every (shape, M) of the
+    sweep: one warm-up call, then calls until `budget_s` (at least one);
+    microseconds per call by (shape, M)."""
+    import oracle as O
+    if not O.ref_vnni():
+        return {"unavailable": "the host has no AVX-VNNI (or oracle/_ref is not built)"}
+    rng = np.random.default_rng(7)
+    out, packed = {}, {}
+    for name, M in points:
+        N, K, res = SWEEP_SHAPES[name]
+        if name not in packed:
+            W = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+            packed[name] = O.RefPacked(W, (np.abs(rng.standard_normal(N)) * 0.02 / 127)
+                                       .astype(np.float32))
+        pk = packed[name]
+        aq, asc = O.ref_quantize(rng.standard_normal((M, K)).astype(np.float32))
+        C0 = np.zeros((M, N), np.float32) if res else None
+        pk.linear_q(aq, asc, C0)
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget_s:
+            pk.linear_q(aq, asc, C0)
+            n += 1
+        out[f"{name}@{M}"] = round((time.perf_counter() - t0) / n * 1e6, 1)
+    return {"us": out, "cores": os.cpu_count(), "kind": "reference",
+            "what": "linear_s8_nk_packed_q[_add] (AVX-VNNI, OpenMP), activations pre-quantised"}
+
+
 # ------------------------------------------------------------ attention
 # The attention of one layer at config 3's length: a CFG pair of 700-token
 # segments (cond, uncond) with the reference's 0 / -1e30 padding bias, 16
@@ -688,6 +784,8 @@ def main():
     ap.add_argument("--numerics", choices=["fp16", "exact"], default="fp16")
     ap.add_argument("--skip-other", action="store_true",
                     help="do not time the other numerics path (for profiling runs)")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="only time the isolated GEMM M-sweep of config 4 (both mainloops)")
     ap.add_argument("--attention-only", action="store_true",
                     help="only time the attention (one q/k/v set, 8 launches; for ncu)")
     ap.add_argument("--sampler-only", action="store_true",
@@ -699,6 +797,17 @@ def main():
         dev = torch.device("cuda", 0)
         print(json.dumps(time_sampler(dev, torch.cuda.Stream(device=dev), launches=8, sets=1)),
               flush=True)
+        return
+    if args.gemm_sweep:
+        import torch
+        dev = torch.device("cuda", 0)
+        st = torch.cuda.Stream(device=dev)
+        res = {"gemm_sweep": {"fp16": time_gemm_sweep(dev, st, True),
+                              "exact": time_gemm_sweep(dev, st, False)},
+               "peaks": load_peaks(), "l2": "weights rotate over > 150 MB of copies",
+               "cpu_baseline": sweep_cpu_baseline([(n, m) for n in SWEEP_SHAPES
+                                                   for m in SWEEP_M])}
+        print(json.dumps(res), flush=True)
         return
     if args.attention_only:
         import torch
