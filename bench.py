@@ -404,6 +404,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     path.release()
     sampler = time_sampler(dev, stream) if world == 1 else None
     attention = time_attention(dev, stream) if world == 1 else None
+    weight_load = time_weight_load(dev) if world == 1 and not args.no_cpu_baseline else None
     status |= ovb.device_status()
 
     # ---- the other numerics path over the same K steps (reported, not headline)
@@ -468,6 +469,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "cpu_baseline": cpu,
         "sampler": sampler,
         "attention": attention,
+        "weight_load": weight_load,
         "clocks": clk.summary(),
     }
 
@@ -642,6 +644,90 @@ def sweep_cpu_baseline(points, budget_s: float = 0.15) -> dict:
             "what": "linear_s8_nk_packed_q[_add] (AVX-VNNI, OpenMP), activations pre-quantised"}
 
 
+# ------------------------------------------------------------ weight load
+def time_weight_load(dev, layers: int = 28) -> dict:
+    """Load time of a synthetic checkpoint's int8 linear weights: a
+    `layers`-layer OVW1 file of int8 [N, K] tensors (the reference's
+    --int8-layout nk files; 440 MB at 28 layers), page cache warm.  Ours:
+    ovb_ovw1_open + ovb_ovw1_weight per tensor (copy as stored, pack and
+    widen to fp16 on the device), synchronised.  Reference: the host repack
+    make_linear does per tensor (ov::s8_nk_pack into VNNI tiles + wsum,
+    cpp/src/model/mat.cpp:95-101), one host thread as in the reference
+    loader, on the same mapped payloads."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    import oracle as O
+    from ovnative_b200 import ovw1
+    from ovnative_b200 import layer as LY
+    rng = np.random.default_rng(11)
+    shapes = [("q", LY.QD, LY.HIDDEN), ("k", LY.KVD, LY.HIDDEN), ("v", LY.KVD, LY.HIDDEN),
+              ("o", LY.HIDDEN, LY.QD), ("gate", LY.INTER, LY.HIDDEN),
+              ("up", LY.INTER, LY.HIDDEN), ("down", LY.HIDDEN, LY.INTER)]
+    base = {n: rng.integers(-127, 128, size=(N, K), dtype=np.int8) for n, N, K in shapes}
+    ts = []
+    for li in range(layers):
+        for n, N, K in shapes:
+            ts.append((f"llm.layers.{li}.{n}_proj.weight", base[n], 0,
+                       (np.abs(rng.standard_normal(N)) * 0.02 / 127).astype(np.float32)))
+    nbytes = sum(t[1].nbytes for t in ts)
+    d = tempfile.mkdtemp(prefix="ovb_load_")
+    try:
+        path = os.path.join(d, "synthetic-int8-nk.ovw")
+        ovw1.write(path, ts)
+        with ovw1.OVW1File(path) as f:  # warm the page cache and the CUDA context
+            for name, *_ in ts:
+                f.array(name).sum()
+        torch.cuda.synchronize()
+        names = [t[0] for t in ts]
+
+        def load_batch():
+            with ovw1.OVW1File(path) as f:
+                ws = f.weights(names, f16=True)
+                torch.cuda.synchronize()
+            return ws
+
+        def load_one_by_one():
+            with ovw1.OVW1File(path) as f:
+                ws = [f.weight(name, f16=True) for name in names]
+                torch.cuda.synchronize()
+            return ws
+
+        def timed(fn, reps=3):
+            ts_ = []
+            for _ in range(reps):
+                t0 = time.perf_counter()
+                ws = fn()
+                ts_.append(time.perf_counter() - t0)
+                for w in ws:
+                    w.close()
+            return float(np.median(ts_))
+
+        ours = timed(load_batch)
+        one_by_one = timed(load_one_by_one, reps=1)
+        ref = None
+        if O.ref_available():
+            reps = []
+            for _ in range(3):
+                with ovw1.OVW1File(path) as f:
+                    t0 = time.perf_counter()
+                    for name in names:
+                        O.RefPacked(f.array(name), f.scales(name))
+                    reps.append(time.perf_counter() - t0)
+            ref = float(np.median(reps))
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"what": f"{len(ts)} int8 [N, K] linear tensors of a {layers}-layer OVW1 file "
+                    "(page cache warm)",
+            "bytes": nbytes, "ms": round(ours * 1e3, 1), "GB/s": round(nbytes / ours / 1e9, 2),
+            "one_by_one_ms": round(one_by_one * 1e3, 1), "fp16_copy": True,
+            "cpu_baseline": None if ref is None else {
+                "ms": round(ref * 1e3, 1), "cores": 1, "kind": "reference",
+                "what": "ov::s8_nk_pack per tensor (make_linear's host repack)"}}
+
+
 # ------------------------------------------------------------ attention
 # The attention of one layer at config 3's length: a CFG pair of 700-token
 # segments (cond, uncond) with the reference's 0 / -1e30 padding bias, 16
@@ -786,6 +872,8 @@ def main():
                     help="do not time the other numerics path (for profiling runs)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="only time the isolated GEMM M-sweep of config 4 (both mainloops)")
+    ap.add_argument("--load-only", action="store_true",
+                    help="only time loading a synthetic OVW1 checkpoint's int8 weights")
     ap.add_argument("--attention-only", action="store_true",
                     help="only time the attention (one q/k/v set, 8 launches; for ncu)")
     ap.add_argument("--sampler-only", action="store_true",
@@ -808,6 +896,10 @@ def main():
                "cpu_baseline": sweep_cpu_baseline([(n, m) for n in SWEEP_SHAPES
                                                    for m in SWEEP_M])}
         print(json.dumps(res), flush=True)
+        return
+    if args.load_only:
+        import torch
+        print(json.dumps(time_weight_load(torch.device("cuda", 0))), flush=True)
         return
     if args.attention_only:
         import torch

@@ -122,6 +122,24 @@ int64_t ovb_quant_scales(int64_t M, int64_t K);
  * borrowed for the call only.  Synchronous. */
 int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const float* scale,
                       int flags, void* stream, ovb_weight** out);
+/* One host (or, with OVB_SRC_DEVICE, device) source of ovb_weight_create_batch. */
+typedef struct ovb_weight_src {
+  const int8_t* W;     /* layout 0: [N, K]; layout 1: [K, N] */
+  int layout;
+  int64_t N;
+  int64_t K;
+  const float* scale;  /* [N] per-output-channel scales */
+} ovb_weight_src;
+
+/* ovb_weight_create for n weights at once (a checkpoint's linear layers):
+ * one device allocation holds all of them (freed with the last of the n
+ * handles), every payload is copied and packed before a single
+ * synchronisation.  flags: OVB_WEIGHT_F16 and/or OVB_SRC_DEVICE.  On error
+ * no handle is returned.  No counterpart in the reference (its loader packs
+ * tensor by tensor on the host, mat.cpp:69-106). */
+int ovb_weight_create_batch(const ovb_weight_src* srcs, int n, int flags, void* stream,
+                            ovb_weight** out);
+
 /* Concatenate weights with the same K along N (q|k|v, gate|up).  Replaces
  * combine_packed (lm.cpp:57-94).  The parts stay valid.  The result has the
  * fp16 copy (OVB_WEIGHT_F16) when every part has it. */
@@ -275,6 +293,63 @@ typedef struct ovb_attn_segment {
 int ovb_attention(const float* q, const float* k, const float* v, float* out, int64_t q_stride,
                   int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
                   const ovb_attn_segment* segs, int n_segs, void* stream);
+
+/* ------------------------------------------------------------------ OVW1
+ * The reference's weight file (docs/weight-format.en.md), read the way its
+ * loader reads it (ov::WeightFile::Open, cpp/src/core/weight_file.cpp:124-206:
+ * one read-only mapping, header and index validated, tensors by name), so
+ * that int8 linear weights go from the mapping straight into the device
+ * layout: ovb_ovw1_weight replaces make_linear's host repack into VNNI tiles
+ * (cpp/src/model/mat.cpp:69-106, gemm.cpp:584-621) and the CUDA runner's
+ * fp32 expansion of every int8 tensor (LmRunner::weight, cuda_lm.cu:840-873).
+ * Pointers in ovb_ovw1_tensor point into the mapping and stay valid until
+ * ovb_ovw1_close.  Errors are OVB_ERR_INVALID_ARG with the reference loader's
+ * messages ("OVW1: bad magic (not an OVW1 file)", "... out of bounds",
+ * "size mismatch for ...", "tensor not found: ..."). */
+typedef struct ovb_ovw1 ovb_ovw1;
+
+typedef struct ovb_ovw1_tensor {
+  const char* name;     /* NUL-terminated copy, owned by the file handle */
+  int32_t name_len;
+  int32_t dtype;        /* 0 f32, 1 int8, 2 f16, 3 int64 */
+  int32_t ndim;         /* 0..4 */
+  int32_t layout;       /* 0 row-major as stored, 1 transposed linear weight [K, N] */
+  int32_t quant;        /* 1: per-output-channel symmetric int8 with `scales` */
+  int64_t dims[4];      /* shape in the stored layout */
+  const void* data;     /* payload in the mapping */
+  int64_t nbytes;
+  const float* scales;  /* n_scales fp32 scales in the mapping, or NULL */
+  int64_t n_scales;
+  uint32_t crc;         /* stored CRC32 of the payload */
+} ovb_ovw1_tensor;
+
+/* WeightFile::Open (weight_file.cpp:124-206). */
+int ovb_ovw1_open(const char* path, ovb_ovw1** out);
+/* WeightFile::Release (weight_file.cpp:77-94); NULL is a no-op. */
+int ovb_ovw1_close(ovb_ovw1* f);
+/* Number of tensors (0 for NULL). */
+int64_t ovb_ovw1_count(const ovb_ovw1* f);
+/* The header's dtype_mode, flags and n_params (any output may be NULL). */
+int ovb_ovw1_header(const ovb_ovw1* f, uint32_t* dtype_mode, uint64_t* flags, uint64_t* n_params);
+/* Tensor i in file order. */
+int ovb_ovw1_tensor_at(const ovb_ovw1* f, int64_t i, ovb_ovw1_tensor* out);
+/* WeightFile::Get (weight_file.cpp:208-218): OVB_ERR_INVALID_ARG when absent. */
+int ovb_ovw1_find(const ovb_ovw1* f, const char* name, ovb_ovw1_tensor* out);
+/* WeightFile::ComputeCrc (weight_file.cpp:220-222): CRC32 (IEEE) of the
+ * payload as mapped; compare with ovb_ovw1_tensor.crc. */
+int ovb_ovw1_crc(const ovb_ovw1* f, const char* name, uint32_t* computed);
+/* make_linear (mat.cpp:69-106) for an int8 weight with per-output-channel
+ * scales, either layout (1: [K, N], 0: [N, K]), packed on the device by
+ * ovb_weight_create; flags 0 or OVB_WEIGHT_F16.  Other tensors are
+ * OVB_ERR_INVALID_ARG (fp32 linear weights are not on this path). */
+int ovb_ovw1_weight(const ovb_ovw1* f, const char* name, int flags, void* stream,
+                    ovb_weight** out);
+/* ovb_ovw1_weight for n tensors at once through ovb_weight_create_batch (one
+ * device allocation, one synchronisation).  This is the loader fast path: a
+ * checkpoint's int8 linear layers go from the file to the device layout
+ * without a host repack. */
+int ovb_ovw1_weights(const ovb_ovw1* f, const char* const* names, int n, int flags,
+                     void* stream, ovb_weight** out);
 
 #ifdef __cplusplus
 }

@@ -183,6 +183,7 @@ def ref_lib():
             "ref_linear_s8_nk": ([_i64, _i64, _i64, _p, _p, _p, _p], C.c_int),
             "ref_attention_head": ([_p, _i64, _p, _p, _i64, _p, C.c_int, C.c_int, C.c_float,
                                     _p, _i64], C.c_int),
+            "ref_ovw1_tensor": ([C.c_char_p, C.c_char_p, _p, _p, C.c_char_p, C.c_int], C.c_int),
         }
         for name, (args, res) in sig.items():
             f = getattr(lib, name)
@@ -386,3 +387,19 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, segs, n_heads: int, n
                 for i in range(rows):
                     out.reshape(-1)[qo + i * QD: qo + i * QD + D] = o[i]
     return out
+
+
+def ref_ovw1_tensor(path: str, name: str):
+    """The reference's own OVW1 loader (ov::WeightFile::Open + Get + ComputeCrc,
+    cpp/src/core/weight_file.cpp:124-222, built into oracle/_ref) on one
+    tensor: (info dict, None) or (None, the loader's error message)."""
+    info = np.zeros(10, np.int64)
+    crc = np.zeros(2, np.uint32)
+    err = C.create_string_buffer(512)
+    rc = ref_lib().ref_ovw1_tensor(path.encode(), name.encode(), info.ctypes.data,
+                                   crc.ctypes.data, err, 512)
+    if rc != 0:
+        return None, err.value.decode()
+    return {"dtype": int(info[0]), "ndim": int(info[1]), "layout": int(info[2]),
+            "quant": int(info[3]), "dims": [int(x) for x in info[4:8]], "nbytes": int(info[8]),
+            "n_scales": int(info[9]), "crc": int(crc[0]), "crc_computed": int(crc[1])}, None

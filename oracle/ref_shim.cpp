@@ -2,7 +2,8 @@
 // path, so Python tests can call it through ctypes.
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
-// the reference sources cpp/src/backend/cpu/gemm.cpp and ops_cpu.cpp (read in
+// the reference sources cpp/src/backend/cpu/gemm.cpp, ops_cpu.cpp and
+// cpp/src/core/weight_file.cpp (read in
 // place from the reference checkout, never copied) into oracle/_ref/libovref.so.
 // Each wrapper forwards to the ov:: function named in its comment
 // (declared in cpp/include/ovnative/ov_gemm.h and cpp/src/model/ops.h) and turns
@@ -16,6 +17,7 @@
 
 #include "model/ops.h"
 #include "ovnative/ov_gemm.h"
+#include "ovnative/ov_weights.h"
 
 #define REF_API extern "C" __attribute__((visibility("default")))
 
@@ -123,4 +125,33 @@ REF_API int ref_attention_head(const float* q, int64_t q_stride, const float* k,
   });
   _mm_setcsr(csr);
   return rc;
+}
+
+// ov::WeightFile::Open + Get + ComputeCrc (cpp/src/core/weight_file.cpp:124-222):
+// the reference loader's view of one tensor of an OVW1 file.  info[] =
+// {dtype, ndim, transposed, quantized, dims[0..3], nbytes, n_scales,
+// data offset in the file, scales offset (or -1)}; crc[] = {stored,
+// computed}.  Returns 0, or 1 with the loader's exception message in err.
+REF_API int ref_ovw1_tensor(const char* path, const char* name, int64_t* info, uint32_t* crc,
+                            char* err, int err_len) {
+  try {
+    ov::WeightFile wf = ov::WeightFile::Open(path);
+    const ov::Tensor& t = wf.Get(name);
+    info[0] = static_cast<int64_t>(t.dtype);
+    info[1] = t.shape.ndim;
+    info[2] = t.transposed ? 1 : 0;
+    info[3] = t.quantized ? 1 : 0;
+    for (int k = 0; k < 4; ++k) info[4 + k] = t.shape.dims[k];
+    info[8] = t.nbytes;
+    info[9] = t.n_scales;
+    crc[0] = wf.StoredCrc(t);
+    crc[1] = wf.ComputeCrc(t);
+    return 0;
+  } catch (const std::exception& e) {
+    if (err && err_len > 0) {
+      std::strncpy(err, e.what(), static_cast<size_t>(err_len) - 1);
+      err[err_len - 1] = 0;
+    }
+    return 1;
+  }
 }

@@ -31,6 +31,20 @@ class Slice(C.Structure):
     _fields_ = [("N", C.c_int64), ("C", C.c_void_p), ("ldc", C.c_int64)]
 
 
+class WeightSrc(C.Structure):
+    """ovb_weight_src: one source of ovb_weight_create_batch."""
+    _fields_ = [("W", C.c_void_p), ("layout", C.c_int), ("N", C.c_int64), ("K", C.c_int64),
+                ("scale", C.c_void_p)]
+
+
+class Ovw1Tensor(C.Structure):
+    """ovb_ovw1_tensor: one tensor of a mapped OVW1 file."""
+    _fields_ = [("name", C.c_char_p), ("name_len", C.c_int32), ("dtype", C.c_int32),
+                ("ndim", C.c_int32), ("layout", C.c_int32), ("quant", C.c_int32),
+                ("dims", C.c_int64 * 4), ("data", C.c_void_p), ("nbytes", C.c_int64),
+                ("scales", C.c_void_p), ("n_scales", C.c_int64), ("crc", C.c_uint32)]
+
+
 class AttnSegment(C.Structure):
     """ovb_attn_segment (the reference's AttnSegment, cpp/src/model/lm.h:46-51)."""
     _fields_ = [("bias", C.c_void_p), ("rows", C.c_int32), ("q_off", C.c_int64),
@@ -66,6 +80,17 @@ SIGNATURES = {
     "ovb_block_products": ([_i64, _p, _p, _p, _p], _int),
     "ovb_guided_sample": ([_p, _int, _p, _int, _int, _int, _int, C.c_float, C.c_float, _int,
                            _p, _p, _p], _int),
+    "ovb_ovw1_open": ([C.c_char_p, C.POINTER(_p)], _int),
+    "ovb_ovw1_close": ([_p], _int),
+    "ovb_ovw1_count": ([_p], _i64),
+    "ovb_ovw1_header": ([_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
+                         C.POINTER(C.c_uint64)], _int),
+    "ovb_ovw1_tensor_at": ([_p, _i64, C.POINTER(Ovw1Tensor)], _int),
+    "ovb_ovw1_find": ([_p, C.c_char_p, C.POINTER(Ovw1Tensor)], _int),
+    "ovb_ovw1_crc": ([_p, C.c_char_p, C.POINTER(C.c_uint32)], _int),
+    "ovb_ovw1_weight": ([_p, C.c_char_p, _int, _p, C.POINTER(_p)], _int),
+    "ovb_ovw1_weights": ([_p, C.POINTER(C.c_char_p), _int, _int, _p, C.POINTER(_p)], _int),
+    "ovb_weight_create_batch": ([C.POINTER(WeightSrc), _int, _int, _p, C.POINTER(_p)], _int),
     "ovb_attention": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
                        C.POINTER(AttnSegment), _int, _p], _int),
 }

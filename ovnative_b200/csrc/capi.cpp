@@ -201,10 +201,12 @@ bool make_weight_f16(ovb_weight* w, cudaStream_t s) {
 }
 
 void free_weight(ovb_weight* w) {
-  cudaFree(w->w);
-  cudaFree(w->scale);
-  cudaFree(w->w16);
-  delete w;
+  if (!w->arena) {
+    cudaFree(w->w);
+    cudaFree(w->scale);
+    cudaFree(w->w16);
+  }
+  delete w;  // a batch's arena is freed with its last weight
 }
 
 // Common checks of a pre-quantised GEMM call.  Returns OVB_OK or a status.
@@ -441,6 +443,109 @@ int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const f
     return OVB_ERR_INTERNAL;
   }
   *out = w;
+  return OVB_OK;
+}
+
+int ovb_weight_create_batch(const ovb_weight_src* srcs, int n, int flags, void* stream,
+                            ovb_weight** out) {
+  if (!out) return invalid("out is null");
+  if (n <= 0) return n == 0 ? OVB_OK : invalid("n must be >= 0");
+  if (!srcs) return invalid("srcs is null");
+  for (int i = 0; i < n; ++i) out[i] = nullptr;
+  if ((flags & ~(OVB_WEIGHT_F16 | OVB_SRC_DEVICE)) != 0) return invalid("unknown flags");
+  const bool f16 = (flags & OVB_WEIGHT_F16) != 0;
+  const bool on_device = (flags & OVB_SRC_DEVICE) != 0;
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  size_t arena_bytes = 0, staging_bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    const ovb_weight_src& w = srcs[i];
+    if (!w.W || !w.scale) return invalid("W/scale must be non-null");
+    if (w.N <= 0 || w.K <= 0) return invalid("weight shape must be positive");
+    if (w.layout != OVB_LAYOUT_NK && w.layout != OVB_LAYOUT_KN) return invalid("unknown layout");
+    if (w.N > (int64_t{1} << 31) - 1 || w.K > (int64_t{1} << 30))
+      return invalid("weight dimensions too large");
+    const size_t wb = static_cast<size_t>(w.N * kblocks(w.K) * 32);
+    arena_bytes += up(wb) + up(static_cast<size_t>(w.N) * 4) + (f16 ? up(wb * 2) : 0);
+    if (!on_device) staging_bytes += up(static_cast<size_t>(w.N * w.K));
+  }
+  int device = 0;
+  if (cuda_failed(cudaGetDevice(&device), "cudaGetDevice")) return OVB_ERR_INTERNAL;
+  cudaStream_t s = as_stream(stream);
+  uint8_t* arena = nullptr;
+  uint8_t* staging = nullptr;
+  if (cuda_failed(cudaMalloc(&arena, arena_bytes), "cudaMalloc(weight arena)")) return OVB_ERR_INTERNAL;
+  std::shared_ptr<void> hold(arena, [device](void* p) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaFree(p);
+    cudaSetDevice(prev);
+  });
+  if (staging_bytes && cuda_failed(cudaMalloc(&staging, staging_bytes), "cudaMalloc(staging)"))
+    return OVB_ERR_INTERNAL;
+  if (f16) ovb::ensure_split_workspace(device);  // optional: split-K configs need it
+  // Copies first (host payloads, as stored), then every pack / widen kernel;
+  // one synchronisation at the end.
+  std::vector<ovb_weight*> ws(static_cast<size_t>(n), nullptr);
+  bool ok = true;
+  size_t a_off = 0, s_off = 0;
+  std::vector<const int8_t*> src_dev(static_cast<size_t>(n));
+  for (int i = 0; i < n && ok; ++i) {
+    const ovb_weight_src& src = srcs[i];
+    auto* w = new ovb_weight();
+    ws[static_cast<size_t>(i)] = w;
+    w->device = device;
+    w->arena = hold;
+    w->N = src.N;
+    w->K = src.K;
+    w->Kb = kblocks(src.K);
+    w->Kp = w->Kb * 32;
+    const size_t wb = static_cast<size_t>(w->N * w->Kp);
+    w->w = reinterpret_cast<int8_t*>(arena + a_off);
+    a_off += up(wb);
+    w->scale = reinterpret_cast<float*>(arena + a_off);
+    a_off += up(static_cast<size_t>(w->N) * 4);
+    if (f16) {
+      w->w16 = reinterpret_cast<uint16_t*>(arena + a_off);
+      a_off += up(wb * 2);
+    }
+    const size_t sb = static_cast<size_t>(w->N) * sizeof(float);
+    if (on_device) {
+      src_dev[static_cast<size_t>(i)] = src.W;
+      ok = !cuda_failed(cudaMemcpyAsync(w->scale, src.scale, sb, cudaMemcpyDeviceToDevice, s),
+                        "copy scale");
+    } else {
+      int8_t* d = reinterpret_cast<int8_t*>(staging + s_off);
+      s_off += up(static_cast<size_t>(src.N * src.K));
+      src_dev[static_cast<size_t>(i)] = d;
+      ok = !cuda_failed(cudaMemcpyAsync(d, src.W, static_cast<size_t>(src.N * src.K),
+                                        cudaMemcpyHostToDevice, s), "copy weight") &&
+           !cuda_failed(cudaMemcpyAsync(w->scale, src.scale, sb, cudaMemcpyHostToDevice, s),
+                        "copy scale");
+    }
+  }
+  for (int i = 0; i < n && ok; ++i) {
+    ovb_weight* w = ws[static_cast<size_t>(i)];
+    const int8_t* d = src_dev[static_cast<size_t>(i)];
+    cudaError_t e = srcs[i].layout == OVB_LAYOUT_NK
+                        ? ovb::launch_pack_nk(d, w->N, w->K, w->w, w->Kp, s)
+                        : ovb::launch_pack_kn(d, w->N, w->K, w->w, w->Kp, s);
+    ok = !cuda_failed(e, "pack weight");
+    if (ok && f16)
+      ok = !cuda_failed(ovb::launch_widen_f16(w->w, w->N * w->Kp, w->w16, s), "widen weight");
+  }
+  if (ok) ok = !cuda_failed(cudaStreamSynchronize(s), "weight batch sync");
+  if (staging) cudaFree(staging);
+  for (int i = 0; i < n && ok; ++i) {
+    ovb_weight* w = ws[static_cast<size_t>(i)];
+    ok = ensure_weight_tmap(w) && ensure_weight_tmap16(w);
+  }
+  if (!ok) {
+    for (ovb_weight* w : ws)
+      if (w) free_weight(w);
+    return OVB_ERR_INTERNAL;
+  }
+  for (int i = 0; i < n; ++i) out[i] = ws[static_cast<size_t>(i)];
   return OVB_OK;
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <string>
 #include <utility>
 
@@ -27,6 +28,9 @@ struct ovb_weight {
   uint16_t* w16 = nullptr;
   CUtensorMap tmap_w16[4];
   bool tmap16_ready[4] = {false, false, false, false};
+  // Set for weights made by ovb_weight_create_batch: w, scale and w16 are
+  // sub-ranges of one device allocation, freed with the batch's last weight.
+  std::shared_ptr<void> arena;
   // Gate|up weight for the fused SiLU*up epilogue (ovb_weight_gate_up): rows
   // are gate and up interleaved in 32-row blocks (gate 32j.., up 32j.., ...);
   // glu_inter = N / 2 is the intermediate width.  0 for other weights.

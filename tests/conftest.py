@@ -18,6 +18,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
 
 
+@pytest.fixture
+def repo_tmp(request):
+    """A scratch directory inside the repository (git-ignored `.test_tmp/`),
+    removed after the test, so that file-writing tests stay in the tree."""
+    import shutil
+    import uuid
+    d = os.path.join(ROOT, ".test_tmp", f"{request.node.name[:40]}-{uuid.uuid4().hex[:8]}")
+    os.makedirs(d)
+    yield __import__("pathlib").Path(d)
+    shutil.rmtree(d, ignore_errors=True)
+
+
 @pytest.fixture(scope="session")
 def golden():
     with np.load(os.path.join(GOLDEN, "gemm_path.npz")) as z:
