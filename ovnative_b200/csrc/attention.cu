@@ -22,6 +22,9 @@
 //     layout the MMA reads, V transposed (keys along K), keys past the
 //     segment zeroed;
 //   - S = Q K^T (tcgen05.mma kind::f16, fp32 in TMEM);
+//   - the tile's bias, loaded by whole rows (coalesced) while the operands
+//     are converted, is staged in the K staging buffer (the next K tile's
+//     TMA waits until the scores are read);
 //   - each thread turns its row of S into scaled, biased scores, moves its
 //     softmax reference point m when the tile's maximum exceeds it by more
 //     than 8 (then rescaling its running sum and its row of O in TMEM), and
@@ -234,33 +237,42 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 
   const int row = row0 + rloc;
   const bool row_ok = row < S;
-  const float* brow = sg.bias ? sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S : nullptr;
-  // (S % 4 == 0 with a 16-byte aligned base: every row and every 4-key group
-  // of a tile is 16-byte aligned and lies wholly inside or past the row)
-  const bool bias_vec = !sg.bias || ((S & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.bias) & 15) == 0);
+  const bool has_bias = sg.bias != nullptr;
+  // (S % 4 == 0 with a 16-byte aligned base: every bias row and every 4-key
+  // group of a tile is 16-byte aligned and lies wholly inside or past the row)
+  const bool bias_vec = (S & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.bias) & 15) == 0;
+  // The bias tile [128 rows][128 keys] staged in the K staging buffer as
+  // 16-byte chunks, chunk c of row r at position c ^ (r % 8): the eight rows
+  // that a quarter-warp reads at one key group fall in distinct banks.
+  float4* bst = reinterpret_cast<float4*>(smem + kOffStK);
+  constexpr int kWarps = kAttThreads / 32;
+  constexpr int kBRows = kAttRows / kWarps;  // bias rows each warp loads per tile
   float m = -INFINITY;   // softmax reference point (running max - 8 <= m <= running max)
   float mt = -INFINITY;  // running maximum of this thread's scores (fully-masked test)
   float l = 0.f;         // this thread's part of the sum of exp(score - m)
 
   for (int t = 0; t < ntiles; ++t) {
     const int valid = S - t * kAttKeys;
-    // this thread's bias values of the tile, issued first so that they land
-    // during the conversions and the MMA: 16-byte loads when every bias row
-    // starts 16-byte aligned, else one float each
-    const int key0 = t * kAttKeys + cg * kGCols;
-    float bias[kGCols];
-    if (bias_vec) {
+    // The tile's bias, loaded by whole rows (warp w rows w, w + kWarps, ...;
+    // lane l keys 4l .. 4l + 3: one 512-byte row per warp instruction) while
+    // the conversions and the MMA run.
+    float4 bv[kBRows];
+    if (has_bias) {
+      const int kb = t * kAttKeys + lane * 4;
 #pragma unroll
-      for (int j = 0; j < kGCols; j += 4) {
-        const float4 b = ld_f4_if(brow + key0 + j, brow != nullptr && key0 + j < S);
-        bias[j] = b.x;
-        bias[j + 1] = b.y;
-        bias[j + 2] = b.z;
-        bias[j + 3] = b.w;
+      for (int i = 0; i < kBRows; ++i) {
+        const int r = row0 + warp + i * kWarps;
+        const bool in = r < S;
+        const float* p = sg.bias + static_cast<int64_t>(in ? r : 0) * S + kb;
+        if (bias_vec) {
+          bv[i] = ld_f4_if(p, in && kb < S);
+        } else {
+          bv[i].x = in && kb < S ? p[0] : 0.f;
+          bv[i].y = in && kb + 1 < S ? p[1] : 0.f;
+          bv[i].z = in && kb + 2 < S ? p[2] : 0.f;
+          bv[i].w = in && kb + 3 < S ? p[3] : 0.f;
+        }
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kGCols; ++j) bias[j] = key0 + j < S ? brow[key0 + j] : 0.f;
     }
     wait(&ctl->ld_k, ph_k);
     amax = fmaxf(amax, convert_rows(smem + kOffK, stk, valid));
@@ -273,8 +285,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     if (tid == 0) {
       if (t + 1 < ntiles) {
         const int ky = sg.kv_y + (t + 1) * kAttKeys;
-        mbar_arrive_expect_tx(smem_u32(&ctl->ld_k), kF32Tile);
-        tma_load_2d(sbase + kOffStK, &args.tm_k, kx, ky, smem_u32(&ctl->ld_k));
+        if (!has_bias) {  // with a bias, K's staging holds it until the scores are read
+          mbar_arrive_expect_tx(smem_u32(&ctl->ld_k), kF32Tile);
+          tma_load_2d(sbase + kOffStK, &args.tm_k, kx, ky, smem_u32(&ctl->ld_k));
+        }
         mbar_arrive_expect_tx(smem_u32(&ctl->ld_v), kF32Tile);
         tma_load_2d(sbase + kOffStV, &args.tm_v, kx, ky, smem_u32(&ctl->ld_v));
       }
@@ -288,10 +302,19 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       }
       tc_commit(smem_u32(&ctl->mma_s));
     }
+    if (has_bias) {
+#pragma unroll
+      for (int i = 0; i < kBRows; ++i) {
+        const int r = warp + i * kWarps;
+        bst[r * (kAttKeys / 4) + (lane ^ (r & 7))] = bv[i];
+      }
+      __syncthreads();  // the bias tile is staged
+    }
     wait(&ctl->mma_s, ph_s);
     tc_fence_after();
 
     // scores (scaled, biased, -inf past the segment) back into S; tile max
+    const int key0 = t * kAttKeys + cg * kGCols;
     float tmax = -INFINITY;
 #pragma unroll
     for (int c = 0; c < kGCols / 32; ++c) {
@@ -299,18 +322,32 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u);
       tc_wait_ld32(u);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int key = key0 + c * 32 + j;
-        float x = __fadd_rn(__fmul_rn(__uint_as_float(u[j]), args.scale), bias[c * 32 + j]);
-        x = key < S ? x : -INFINITY;
-        tmax = fmaxf(tmax, x);
-        u[j] = __float_as_uint(x);
+      for (int j = 0; j < 32; j += 4) {
+        const int kc = (cg * kGCols + c * 32 + j) >> 2;  // key group within the tile
+        const float4 b = has_bias ? bst[rloc * (kAttKeys / 4) + (kc ^ (rloc & 7))]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + c * 32 + j + e;
+          float x = __fmul_rn(__uint_as_float(u[j + e]), args.scale);
+          if (has_bias) x = __fadd_rn(x, bb[e]);
+          x = key < S ? x : -INFINITY;
+          tmax = fmaxf(tmax, x);
+          u[j + e] = __float_as_uint(x);
+        }
       }
       tmem_st32(s_col + static_cast<uint32_t>(c * 32), u);
     }
     mt = fmaxf(mt, tmax);
     red[cg * kAttRows + rloc] = tmax;
-    __syncthreads();
+    __syncthreads();  // also: every thread has read its bias
+    if (has_bias && tid == 0 && t + 1 < ntiles) {
+      fence_proxy_async();
+      mbar_arrive_expect_tx(smem_u32(&ctl->ld_k), kF32Tile);
+      tma_load_2d(sbase + kOffStK, &args.tm_k, kx, sg.kv_y + (t + 1) * kAttKeys,
+                  smem_u32(&ctl->ld_k));
+    }
 #pragma unroll
     for (int g = 0; g < kCG; ++g) tmax = fmaxf(tmax, red[g * kAttRows + rloc]);
     float factor = 1.f;
