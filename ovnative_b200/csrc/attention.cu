@@ -12,10 +12,11 @@
 // kernel and TF32 strided-batched cuBLAS, cpp/src/backend/cuda/cuda_lm.cu:
 // 393-421, :423-606, :1132-1145).  head_dim is 128.
 //
-// One CTA of 512 threads per (segment, head, block of 128 query rows).  Warp
-// w reads TMEM lanes 32 (w % 4) .. + 31 (the rows) and column group w / 4: a
-// quarter of the tile's keys and of O's columns; the four threads of a row
-// combine their maxima and sums through shared memory.  Per tile of 128 keys:
+// One CTA of 256 threads (OVB_ATT_THREADS) per (segment, head, block of 128
+// query rows).  Warp w reads TMEM lanes 32 (w % 4) .. + 31 (the rows) and
+// column group w / 4: half of the tile's keys and of O's columns; the two
+// threads of a row combine their maxima and sums through shared memory.  Per
+// tile of 128 keys:
 //   - TMA brings the fp32 K and V tiles (128 x 128, 64 KB each) into staging
 //     shared memory one tile ahead of their use;
 //   - the threads convert them to fp16: K into the 128-byte-swizzled K-major
