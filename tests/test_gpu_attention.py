@@ -162,3 +162,29 @@ def test_fp16_range_flag(cuda):
     torch.cuda.synchronize()
     assert ovb.device_status() == 16
     assert ovb.device_status() == 0
+
+
+@pytest.mark.parametrize("slope", [0.1, -0.1, 0.03])
+def test_rescale_paths(cuda, slope):
+    """A bias rising along the keys by 12.8 per 128-key tile moves the softmax
+    reference point (and rescales O in TMEM) on every tile; a falling one
+    keeps the first tile's maximum; 3.8 per tile stays under the rescale
+    threshold for several tiles."""
+    rng = np.random.default_rng(int(abs(slope) * 1000) + (slope > 0))
+    S = 700
+    q, k, v, _ = make_case(rng, (S,), 4, 2)
+    bias = np.broadcast_to((slope * np.arange(S)).astype(np.float32), (S, S)).copy()
+    bias[:, 5] = -1e30
+    segs = [(bias, S, 0, 0)]
+    scale = 1.0 / np.sqrt(D)
+    compare(run(q, k, v, segs, 4, 2, scale, cuda), O.attention(q, k, v, segs, 4, 2, D, scale))
+
+
+def test_long_segment(cuda):
+    """1500 rows: 12 key tiles and 12 query blocks per head."""
+    rng = np.random.default_rng(15)
+    q, k, v, segs = make_case(rng, (1500,), 4, 1, masked_rows=(7,), pad_keys=11)
+    scale = 1.0 / np.sqrt(D)
+    got = run(q, k, v, segs, 4, 1, scale, cuda)
+    compare(got, O.attention(q, k, v, segs, 4, 1, D, scale))
+    assert not got[7].any()
