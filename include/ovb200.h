@@ -96,7 +96,8 @@ const char* ovb_last_error(void);
  * up (~1 s limit; the kernel then ends early and its outputs are invalid,
  * the context stays usable).  Bit 16 reports an activation block beyond the
  * fp16 range in the fp16 mainloop, or a q/k/v value beyond it in the
- * attention; bit 32 a wait of the attention kernel;
+ * attention; bit 32 a wait of the attention kernel; bit 128 a token or
+ * codebook id outside its embedding table (ovb_lm_*);
  * bit 64 the self-test below.  Reading it
  * synchronises the given stream and clears it. */
 int ovb_device_status(void* stream);
@@ -350,6 +351,43 @@ int ovb_ovw1_weight(const ovb_ovw1* f, const char* name, int flags, void* stream
  * without a host repack. */
 int ovb_ovw1_weights(const ovb_ovw1* f, const char* const* names, int n, int flags,
                      void* stream, ovb_weight** out);
+
+/* ------------------------------------------------------------------ LM
+ * The whole LM forward on the device, built from an OVW1 checkpoint: the
+ * reference's LM (cpp/src/model/lm.h:52-140, lm.cpp) for the accelerator
+ * hook LM::CudaForwardFn (lm.h:91-96) and the ragged
+ * CFG forward.  Linear weights (q/k/v/o, gate/up/down, audio_heads) must be
+ * int8 with per-output-channel scales, either orientation; embeddings int8
+ * with row scales or fp32; head_dim 128; LMConfig's rms_eps 1e-6 and
+ * rope_theta 1e6.  flags: 0 runs the bit-exact int8 mainloop, OVB_WEIGHT_F16
+ * the fp16 one.  One model per (thread, device); its forward buffers grow on
+ * demand (ovb_lm_reserve sizes them ahead, e.g. before a stream capture). */
+typedef struct ovb_lm ovb_lm;
+int ovb_lm_create(const char* ovw1_path, int flags, void* stream, ovb_lm** out);
+int ovb_lm_destroy(ovb_lm* m);
+/* {n_layers, hidden, n_heads, n_kv_heads, head_dim, inter, vocab,
+ *  audio_vocab, n_codebooks} */
+int ovb_lm_config(const ovb_lm* m, int64_t* cfg);
+int ovb_lm_reserve(ovb_lm* m, int64_t rows, int64_t mask_elems);
+/* LM::forward_cfg (lm.cpp:403-454) on host buffers: input_ids [C, rows]
+ * (rows = cond_seq + uncond_seq, codebook-major), audio_mask [rows],
+ * cond_attn [cond_seq, cond_seq], uncond_attn [uncond_seq, uncond_seq],
+ * position [rows]; logits [rows, C*V] token-major.  Synchronous. */
+int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* ids,
+                       const uint8_t* audio_mask, const uint8_t* cond_attn,
+                       const uint8_t* uncond_attn, const int64_t* pos, float* logits,
+                       void* stream);
+/* The same on device inputs, stream-ordered (no synchronisation); the logits
+ * stay on the device, at ovb_lm_logits(m) (LM::CudaLogitsFn, lm.h:95). */
+int ovb_lm_forward_cfg_device(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* ids,
+                              const uint8_t* audio_mask, const uint8_t* cond_attn,
+                              const uint8_t* uncond_attn, const int64_t* pos, void* stream);
+const float* ovb_lm_logits(const ovb_lm* m);
+/* LM::forward (lm.cpp:343-401) with CudaForwardFn's arguments on host
+ * buffers: input_ids [B, C, S], audio_mask [B, S], attn_mask [B, S, S],
+ * position [B, S]; logits [B, C, S, V].  batch <= 64.  Synchronous. */
+int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint8_t* audio_mask,
+                   const uint8_t* attn_mask, const int64_t* pos, float* logits, void* stream);
 
 #ifdef __cplusplus
 }

@@ -184,6 +184,10 @@ def ref_lib():
             "ref_attention_head": ([_p, _i64, _p, _p, _i64, _p, C.c_int, C.c_int, C.c_float,
                                     _p, _i64], C.c_int),
             "ref_ovw1_tensor": ([C.c_char_p, C.c_char_p, _p, _p, C.c_char_p, C.c_int], C.c_int),
+            "ref_lm_create": ([C.c_char_p, C.c_int, C.c_char_p, C.c_int], _p),
+            "ref_lm_destroy": ([_p], None),
+            "ref_lm_forward_cfg": ([_p, C.c_int, C.c_int, _p, _p, _p, _p, _p, _p], C.c_int),
+            "ref_lm_forward": ([_p, C.c_int, C.c_int, _p, _p, _p, _p, _p], C.c_int),
         }
         for name, (args, res) in sig.items():
             f = getattr(lib, name)
@@ -403,3 +407,51 @@ def ref_ovw1_tensor(path: str, name: str):
     return {"dtype": int(info[0]), "ndim": int(info[1]), "layout": int(info[2]),
             "quant": int(info[3]), "dims": [int(x) for x in info[4:8]], "nbytes": int(info[8]),
             "n_scales": int(info[9]), "crc": int(crc[0]), "crc_computed": int(crc[1])}, None
+
+
+class RefLM:
+    """The reference's own LM (cpp/src/model/lm.h:52-140, lm.cpp, built into
+    oracle/_ref) on an OVW1 file: LMConfig defaults except n_layers."""
+
+    def __init__(self, path: str, n_layers: int):
+        self._h = None
+        err = C.create_string_buffer(512)
+        h = ref_lib().ref_lm_create(path.encode(), n_layers, err, 512)
+        if not h:
+            raise RuntimeError(f"reference LM: {err.value.decode()}")
+        self._h = h
+        self.C, self.V = 8, 1025
+
+    def close(self):
+        if self._h:
+            ref_lib().ref_lm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward_cfg(self, ids, amask, cond_attn, uncond_attn, pos) -> np.ndarray:
+        """LM::forward_cfg: ids [C, rows] int64, amask [rows] u8, cond/uncond
+        masks u8, pos [rows] int64 -> logits [rows, C*V]."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        rows = ids.shape[1]
+        cs, us = cond_attn.shape[0], uncond_attn.shape[0]
+        out = np.zeros((rows, self.C * self.V), np.float32)
+        args = [np.ascontiguousarray(a) for a in (amask, cond_attn, uncond_attn)]
+        pos = np.ascontiguousarray(pos, np.int64)
+        _chk(ref_lib().ref_lm_forward_cfg(self._h, cs, us, _ptr(ids), _ptr(args[0]), _ptr(args[1]),
+                                          _ptr(args[2]), _ptr(pos), _ptr(out)), "LM::forward_cfg")
+        return out
+
+    def forward(self, ids, amask, attn, pos) -> np.ndarray:
+        """LM::forward: ids [B, C, S], amask [B, S], attn [B, S, S], pos [B, S]
+        -> logits [B, C, S, V]."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        B, _, S = ids.shape
+        out = np.zeros((B, self.C, S, self.V), np.float32)
+        a = np.ascontiguousarray(amask, np.uint8)
+        m = np.ascontiguousarray(attn, np.uint8)
+        pos = np.ascontiguousarray(pos, np.int64)
+        _chk(ref_lib().ref_lm_forward(self._h, B, S, _ptr(ids), _ptr(a), _ptr(m), _ptr(pos),
+                                      _ptr(out)), "LM::forward")
+        return out

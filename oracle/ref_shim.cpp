@@ -2,8 +2,8 @@
 // path, so Python tests can call it through ctypes.
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
-// the reference sources cpp/src/backend/cpu/gemm.cpp, ops_cpu.cpp and
-// cpp/src/core/weight_file.cpp (read in
+// the reference sources cpp/src/backend/cpu/gemm.cpp, ops_cpu.cpp,
+// cpp/src/core/weight_file.cpp and cpp/src/model/lm.cpp + mat.cpp (read in
 // place from the reference checkout, never copied) into oracle/_ref/libovref.so.
 // Each wrapper forwards to the ov:: function named in its comment
 // (declared in cpp/include/ovnative/ov_gemm.h and cpp/src/model/ops.h) and turns
@@ -15,6 +15,9 @@
 
 #include <xmmintrin.h>
 
+#include <memory>
+
+#include "model/lm.h"
 #include "model/ops.h"
 #include "ovnative/ov_gemm.h"
 #include "ovnative/ov_weights.h"
@@ -154,4 +157,62 @@ REF_API int ref_ovw1_tensor(const char* path, const char* name, int64_t* info, u
     }
     return 1;
   }
+}
+
+// The reference's LM (cpp/src/model/lm.h:52-140) over an OVW1 file: LMConfig
+// defaults except n_layers.  The WeightFile outlives the LM (its tensors point
+// into the mapping).  The forwards switch every OpenMP worker to flush-to-zero
+// (lm.cpp:347-348, :412-413); the caller's MXCSR is put back on all of them
+// afterwards so that later checkers keep IEEE denormals.
+namespace {
+struct RefLm {
+  ov::WeightFile wf;
+  std::unique_ptr<ov::LM> lm;
+};
+template <class F>
+int with_csr(F&& f) {
+  const unsigned csr = _mm_getcsr();
+  const int rc = guard(f);
+#pragma omp parallel
+  { _mm_setcsr(csr); }
+  _mm_setcsr(csr);
+  return rc;
+}
+}  // namespace
+
+REF_API void* ref_lm_create(const char* path, int n_layers, char* err, int err_len) {
+  try {
+    auto r = std::make_unique<RefLm>();
+    r->wf = ov::WeightFile::Open(path);
+    ov::LMConfig cfg;
+    cfg.n_layers = n_layers;
+    r->lm = std::make_unique<ov::LM>(r->wf, cfg);
+    return r.release();
+  } catch (const std::exception& e) {
+    if (err && err_len > 0) {
+      std::strncpy(err, e.what(), static_cast<size_t>(err_len) - 1);
+      err[err_len - 1] = 0;
+    }
+    return nullptr;
+  }
+}
+
+REF_API void ref_lm_destroy(void* h) { delete static_cast<RefLm*>(h); }
+
+// LM::forward_cfg (lm.cpp:403-454)
+REF_API int ref_lm_forward_cfg(void* h, int cond_seq, int uncond_seq, const int64_t* ids,
+                               const uint8_t* amask, const uint8_t* cond_attn,
+                               const uint8_t* uncond_attn, const int64_t* pos, float* logits) {
+  return with_csr([&] {
+    static_cast<RefLm*>(h)->lm->forward_cfg(cond_seq, uncond_seq, ids, amask, cond_attn,
+                                            uncond_attn, pos, logits);
+  });
+}
+
+// LM::forward (lm.cpp:343-401)
+REF_API int ref_lm_forward(void* h, int batch, int seq, const int64_t* ids, const uint8_t* amask,
+                           const uint8_t* attn, const int64_t* pos, float* logits) {
+  return with_csr([&] {
+    static_cast<RefLm*>(h)->lm->forward(batch, seq, ids, amask, attn, pos, logits);
+  });
 }

@@ -91,6 +91,14 @@ SIGNATURES = {
     "ovb_ovw1_weight": ([_p, C.c_char_p, _int, _p, C.POINTER(_p)], _int),
     "ovb_ovw1_weights": ([_p, C.POINTER(C.c_char_p), _int, _int, _p, C.POINTER(_p)], _int),
     "ovb_weight_create_batch": ([C.POINTER(WeightSrc), _int, _int, _p, C.POINTER(_p)], _int),
+    "ovb_lm_create": ([C.c_char_p, _int, _p, C.POINTER(_p)], _int),
+    "ovb_lm_destroy": ([_p], _int),
+    "ovb_lm_config": ([_p, C.POINTER(_i64)], _int),
+    "ovb_lm_reserve": ([_p, _i64, _i64], _int),
+    "ovb_lm_logits": ([_p], _p),
+    "ovb_lm_forward_cfg": ([_p, _int, _int, _p, _p, _p, _p, _p, _p, _p], _int),
+    "ovb_lm_forward_cfg_device": ([_p, _int, _int, _p, _p, _p, _p, _p, _p], _int),
+    "ovb_lm_forward": ([_p, _int, _int, _p, _p, _p, _p, _p, _p], _int),
     "ovb_attention": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
                        C.POINTER(AttnSegment), _int, _p], _int),
 }

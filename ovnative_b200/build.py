@@ -25,8 +25,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libovb200.so")
 
 CU_SOURCES = ["quant.cu", "weights.cu", "gemm_tc.cu", "gemm_f16.cu", "linear_static.cu", "sampler.cu",
-              "attention.cu"]
-CXX_SOURCES = ["capi.cpp", "ovw1.cpp"]
+              "attention.cu", "lm_ops.cu"]
+CXX_SOURCES = ["capi.cpp", "ovw1.cpp", "lm.cpp"]
 HEADERS = ["ovb_internal.h", "ovb_ptx.cuh", "ovb_quant.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -369,13 +369,14 @@ int ovb_abi_version(void) { return OVB_ABI_VERSION; }
 const char* ovb_last_error(void) { return ovb::t_error.c_str(); }
 
 int ovb_device_status(void* stream) {
-  int st = 0, st16 = 0, stq = 0, sta = 0;
+  int st = 0, st16 = 0, stq = 0, sta = 0, stl = 0;
   if (cuda_failed(ovb::read_and_clear_status(&st, as_stream(stream)), "read device status") ||
       cuda_failed(ovb::read_and_clear_status_f16(&st16, as_stream(stream)), "read device status") ||
       cuda_failed(ovb::read_and_clear_status_q(&stq, as_stream(stream)), "read device status") ||
-      cuda_failed(ovb::read_and_clear_status_att(&sta, as_stream(stream)), "read device status"))
+      cuda_failed(ovb::read_and_clear_status_att(&sta, as_stream(stream)), "read device status") ||
+      cuda_failed(ovb::read_and_clear_status_lm(&stl, as_stream(stream)), "read device status"))
     return OVB_ERR_INTERNAL;
-  st |= st16 | stq | sta;
+  st |= st16 | stq | sta | stl;
   return st;
 }
 

@@ -1,0 +1,164 @@
+// lm_ops.cu -- the steps of the LM forward that are not GEMMs, quantisers or
+// attention: the embedding gather, the attention-mask bias, the per-head
+// RMSNorm + RoPE of q and k, and the logits permute of the batched forward.
+// They are what LM::forward / LM::forward_cfg (cpp/src/model/lm.cpp:343-454)
+// run between the hot-path kernels, so that a whole forward stays on the
+// device (ovb_lm_*, lm.cpp in this directory).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "ovb_internal.h"
+
+namespace ovb {
+
+__device__ int g_status_lm;
+
+namespace {
+
+constexpr int kErrLmIndex = 128;  // a token / codebook id outside its table (row left zero)
+
+// One row of an embedding table as Emb::gather reads it (mat.cpp:52-66):
+// int8 entries times the row's scale, or fp32 entries.
+__device__ __forceinline__ float emb_at(const EmbTable& t, int64_t row, int c) {
+  if (t.i8) return __fmul_rn(static_cast<float>(t.i8[row * t.cols + c]), t.scale[row]);
+  return t.f32[row * t.cols + c];
+}
+
+}  // namespace
+
+// LM::embed / embed_cfg (lm.cpp:178-215): row r of the packed batch (batch
+// row b = r / seq, position s = r % seq) takes the token embedding of
+// ids[b][0][s] when mask[r] is 0, else the sum over codebooks c of the audio
+// embeddings of ids[b][c][s] + offsets[c], accumulated in codebook order from
+// 0.  ids are [B][C][seq] (forward_cfg: B = 1, seq = rows).  One block per
+// row; an id outside its table leaves the row zero and sets status bit 128.
+__global__ void embed_kernel(const int64_t* ids, const uint8_t* mask, const int64_t* offsets,
+                             int C, int seq, EmbTable tok, EmbTable aud, float* out, int H) {
+  const int64_t r = blockIdx.x;
+  const int64_t b = r / seq, s = r % seq;
+  const int64_t* base = ids + b * C * seq;
+  float* o = out + r * H;
+  if (!mask[r]) {
+    const int64_t id = base[s];
+    const bool ok = id >= 0 && id < tok.rows;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) o[c] = ok ? emb_at(tok, id, c) : 0.f;
+    if (!ok && threadIdx.x == 0) atomicOr(&g_status_lm, kErrLmIndex);
+    return;
+  }
+  bool ok = true;
+  for (int cb = 0; cb < C; ++cb) {
+    const int64_t id = base[static_cast<int64_t>(cb) * seq + s] + offsets[cb];
+    ok = ok && id >= 0 && id < aud.rows;
+  }
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float acc = 0.f;
+    if (ok)
+      for (int cb = 0; cb < C; ++cb)
+        acc = __fadd_rn(acc, emb_at(aud, base[static_cast<int64_t>(cb) * seq + s] + offsets[cb], c));
+    o[c] = acc;
+  }
+  if (!ok && threadIdx.x == 0) atomicOr(&g_status_lm, kErrLmIndex);
+}
+
+// bias = attn ? 0 : -1e30 (lm.cpp:365, :431-434).
+__global__ void mask_bias_kernel(const uint8_t* attn, int64_t n, float* bias) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    bias[i] = attn[i] ? 0.f : -1e30f;
+}
+
+// qk_norm_rope_f32 (ops_cpu.cpp:945-1013) for head_dim 128: each head vector
+// v of q (n_heads per row) and k (n_kv per row) is RMS-normalised with its
+// weight, then rotated by the position's angles:
+//   scale = 1 / sqrt(sum(v^2) / D + eps);  a = (v[i] scale) w[i],
+//   b = (v[i+64] scale) w[i+64];  v[i] = a cos - b sin;  v[i+64] = b cos + a sin,
+// angle = pos * inv_freq[i], inv_freq[i] = (float) theta^(-2i/D) computed on
+// the host as the reference does.  One warp per head vector; lane l holds
+// elements l, l+32, l+64, l+96.  The sum of squares runs in a warp tree and
+// cos / sin are CUDA's (not glibc's): results agree to a few ulps.
+__global__ void qk_norm_rope_kernel(float* q, float* k, const float* qw, const float* kw,
+                                    const int64_t* pos, const float* inv_freq, int64_t rows,
+                                    int n_heads, int n_kv, float eps) {
+  constexpr int D = 128, half = 64;
+  const int64_t gw = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int per_row = n_heads + n_kv;
+  if (gw >= rows * per_row) return;
+  const int64_t r = gw / per_row;
+  const int h = static_cast<int>(gw % per_row);
+  float* v = h < n_heads ? q + (r * n_heads + h) * D : k + (r * n_kv + (h - n_heads)) * D;
+  const float* w = h < n_heads ? qw : kw;
+  float x[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = v[lane + 32 * j];
+  float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                        __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  const float scale =
+      __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(D)), eps)));
+  const float p = static_cast<float>(pos[r]);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = lane + 32 * j;  // 0 .. 63
+    const float angle = __fmul_rn(p, inv_freq[i]);
+    const float cs = cosf(angle), sn = sinf(angle);
+    const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
+    const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
+    v[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+    v[i + half] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+  }
+}
+
+// [B*S, C*V] -> [B, C, S, V] (lm.cpp:387-398).  One block per (b, s) row.
+__global__ void permute_logits_kernel(const float* src, float* dst, int S, int C, int V) {
+  const int64_t r = blockIdx.x;
+  const int64_t b = r / S, s = r % S;
+  const float* in = src + r * C * static_cast<int64_t>(V);
+  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(C) * V; i += blockDim.x) {
+    const int64_t c = i / V, t = i % V;
+    dst[((b * C + c) * S + s) * V + t] = in[i];
+  }
+}
+
+cudaError_t launch_embed(const int64_t* ids, const uint8_t* mask, const int64_t* offsets, int C,
+                         int64_t rows, int seq, const EmbTable& tok, const EmbTable& aud,
+                         float* out, int H, cudaStream_t s) {
+  return launch_plain(embed_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s, ids,
+                      mask, offsets, C, seq, tok, aud, out, H);
+}
+
+cudaError_t launch_mask_bias(const uint8_t* attn, int64_t n, float* bias, cudaStream_t s) {
+  const int64_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  return launch_plain(mask_bias_kernel, dim3(static_cast<unsigned>(blocks > 0 ? blocks : 1)),
+                      dim3(256), 0, s, attn, n, bias);
+}
+
+cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float* kw,
+                                const int64_t* pos, const float* inv_freq, int64_t rows,
+                                int n_heads, int n_kv, float eps, cudaStream_t s) {
+  const int64_t warps = rows * (n_heads + n_kv);
+  const int64_t blocks = (warps + 7) / 8;
+  return launch_plain(qk_norm_rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+                      q, k, qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
+}
+
+cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,
+                                  cudaStream_t s) {
+  return launch_plain(permute_logits_kernel, dim3(static_cast<unsigned>(B * S)), dim3(256), 0, s,
+                      src, dst, S, C, V);
+}
+
+cudaError_t read_and_clear_status_lm(int* out, cudaStream_t s) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_status_lm, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_status_lm, &zero, sizeof(int));
+}
+
+}  // namespace ovb

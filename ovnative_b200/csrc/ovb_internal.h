@@ -216,6 +216,25 @@ struct AttnArgs {
   AttnSeg segs[kAttMaxSegs];
 };
 cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s);
+// LM forward steps (lm_ops.cu).  An embedding table on the device: int8
+// rows with one fp32 scale per row, or fp32 rows.
+struct EmbTable {
+  const int8_t* i8;
+  const float* scale;
+  const float* f32;
+  int64_t rows;
+  int64_t cols;
+};
+cudaError_t launch_embed(const int64_t* ids, const uint8_t* mask, const int64_t* offsets, int C,
+                         int64_t rows, int seq, const EmbTable& tok, const EmbTable& aud,
+                         float* out, int H, cudaStream_t s);
+cudaError_t launch_mask_bias(const uint8_t* attn, int64_t n, float* bias, cudaStream_t s);
+cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float* kw,
+                                const int64_t* pos, const float* inv_freq, int64_t rows,
+                                int n_heads, int n_kv, float eps, cudaStream_t s);
+cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,
+                                  cudaStream_t s);
+cudaError_t read_and_clear_status_lm(int* out, cudaStream_t s);
 cudaError_t read_and_clear_status_att(int* out, cudaStream_t s);
 // Index into kTileNF of the tile width used by the fp16 mainloop.
 int pick_tile_f16(int64_t M, int64_t N, int64_t Kb, int device);

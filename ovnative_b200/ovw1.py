@@ -173,3 +173,47 @@ class OVW1File:
         N = t.dims[1] if t.layout == 1 else t.dims[0]
         K = t.dims[0] if t.layout == 1 else t.dims[1]
         return Weight(out.value, int(N), int(K), f16)
+
+
+def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden: int = 1024,
+              n_heads: int = 16, n_kv: int = 8, inter: int = 3072, audio_vocab: int = 1025,
+              codebooks: int = 8) -> None:
+    """A random-weight checkpoint of the reference LM's shape and tensor names
+    (cpp/src/model/lm.cpp:96-141): int8 [N, K] linear weights with
+    per-output-channel scales |N(0, 0.02)| / 127 (the --int8-layout nk
+    encoding, audio heads int8 as well), int8 embedding tables with row
+    scales, RMSNorm gains 1 + N(0, 0.05), codebook offsets c * audio_vocab."""
+    rng = np.random.default_rng(seed)
+    D = 128
+
+    def lin(N, K):
+        return (rng.integers(-127, 128, size=(N, K), dtype=np.int8),
+                (np.abs(rng.standard_normal(N)) * 0.02 / 127 + 1e-6).astype(np.float32))
+
+    def gain(n):
+        return (1 + 0.05 * rng.standard_normal(n)).astype(np.float32)
+
+    ts = []
+    W, s = lin(vocab, hidden)
+    ts.append(("llm.embed_tokens.weight", W, 0, (s * 40).astype(np.float32)))
+    W, s = lin(codebooks * audio_vocab, hidden)
+    ts.append(("audio_embeddings.weight", W, 0, (s * 40).astype(np.float32)))
+    W, s = lin(codebooks * audio_vocab, hidden)
+    ts.append(("audio_heads.weight", W, 0, s))
+    ts.append(("llm.norm.weight", gain(hidden), 0, None))
+    ts.append(("codebook_layer_offsets",
+               (np.arange(codebooks, dtype=np.int64) * audio_vocab), 0, None))
+    QD, KVD = n_heads * D, n_kv * D
+    for i in range(n_layers):
+        p = f"llm.layers.{i}."
+        ts.append((p + "input_layernorm.weight", gain(hidden), 0, None))
+        ts.append((p + "post_attention_layernorm.weight", gain(hidden), 0, None))
+        ts.append((p + "self_attn.q_norm.weight", gain(D), 0, None))
+        ts.append((p + "self_attn.k_norm.weight", gain(D), 0, None))
+        for name, N, K in (("self_attn.q_proj", QD, hidden), ("self_attn.k_proj", KVD, hidden),
+                           ("self_attn.v_proj", KVD, hidden), ("self_attn.o_proj", hidden, QD),
+                           ("mlp.gate_proj", inter, hidden), ("mlp.up_proj", inter, hidden),
+                           ("mlp.down_proj", hidden, inter)):
+            W, s = lin(N, K)
+            ts.append((p + name + ".weight", W, 0, s))
+    write(path, ts)

@@ -1,0 +1,110 @@
+"""The whole LM forward on the device (ovb_lm_*, from an OVW1 checkpoint)
+against the reference's own LM forward (cpp/src/model/lm.cpp, oracle/_ref)
+on the same random checkpoint and inputs -- the end-to-end pin, judged as the
+reference's own LM test judges an int8 forward (cpp/tests/test_lm.cpp:
+198-231: cosine, mean |delta| and argmax agreement over every (row,
+codebook) position), with tighter bounds: both sides run the same int8
+arithmetic, and only the attention (fp16 operands), RoPE (CUDA's cos/sin)
+and the fp16 mainloop (when selected) differ."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import ovnative_b200 as ovb
+from ovnative_b200 import lm as LM
+from ovnative_b200 import ovw1
+from tests.test_lm_oracle import C, V, cfg_inputs
+
+pytestmark = pytest.mark.gpu
+
+LAYERS, VOCAB = 2, 512
+
+
+@pytest.fixture(scope="module")
+def model_path(tmp_path_factory):
+    import os
+    import shutil
+
+    from tests.conftest import ROOT
+    d = os.path.join(ROOT, ".test_tmp", "gpu_lm")
+    os.makedirs(d, exist_ok=True)
+    p = os.path.join(d, "lm2.ovw")
+    ovw1.random_lm(p, n_layers=LAYERS, vocab=VOCAB, seed=7)
+    yield p
+    shutil.rmtree(d, ignore_errors=True)
+
+
+def metrics(got, want):
+    g = got.reshape(-1, V).astype(np.float64)
+    w = want.reshape(-1, V).astype(np.float64)
+    cos = float((g * w).sum() / (np.linalg.norm(g) * np.linalg.norm(w)))
+    mean = float(np.abs(g - w).mean())
+    agree = float((g.argmax(1) == w.argmax(1)).mean())
+    return cos, mean, agree
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_forward_cfg_matches_reference(cuda, model_path, f16):
+    rng = np.random.default_rng(11)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 150, 97, VOCAB)
+    want = O.RefLM(model_path, LAYERS).forward_cfg(ids, amask, cond, unc, pos)
+    m = LM.LM(model_path, f16=f16)
+    assert m.config["n_layers"] == LAYERS and m.config["vocab"] == VOCAB
+    got = m.forward_cfg(ids, amask, cond, unc, pos)
+    cos, mean, agree = metrics(got, want)
+    print(f"f16={f16} cos={cos:.8f} mean={mean:.3e} agree={agree:.4f}")
+    assert np.isfinite(got).all()
+    assert cos > (0.9999 if f16 else 0.99999)
+    assert mean < 0.02 * float(np.abs(want).mean())
+    assert agree >= (0.97 if f16 else 0.99)
+    assert ovb.device_status() == 0
+    m.close()
+
+
+def test_forward_batched_matches_reference(cuda, model_path):
+    rng = np.random.default_rng(12)
+    B, S = 2, 90
+    ids = rng.integers(0, V, size=(B, C, S)).astype(np.int64)
+    amask = np.ones((B, S), np.uint8)
+    amask[:, :10] = 0
+    ids[:, 0, :10] = rng.integers(0, VOCAB, size=(B, 10))
+    attn = np.ones((B, S, S), np.uint8)
+    attn[1, :, :4] = 0
+    pos = np.tile(np.arange(S, dtype=np.int64), (B, 1))
+    want = O.RefLM(model_path, LAYERS).forward(ids, amask, attn, pos)
+    m = LM.LM(model_path)
+    got = m.forward(ids, amask, attn, pos)
+    assert got.shape == (B, C, S, V)
+    cos, mean, agree = metrics(got, want)
+    print(f"batched cos={cos:.8f} mean={mean:.3e} agree={agree:.4f}")
+    assert cos > 0.99999 and agree >= 0.99
+    assert ovb.device_status() == 0
+    m.close()
+
+
+def test_device_forward_equals_host_forward(cuda, model_path):
+    rng = np.random.default_rng(13)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 64, 40, VOCAB)
+    m = LM.LM(model_path)
+    host = m.forward_cfg(ids, amask, cond, unc, pos)
+    t = [torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in (ids, amask, cond, unc, pos)]
+    dev = m.forward_cfg_device(*t)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dev.cpu().numpy(), host)
+    m.close()
+
+
+def test_bad_ids_flagged_not_faulted(cuda, model_path):
+    """A token id outside the table leaves its row zero and sets status bit
+    128 instead of reading out of bounds."""
+    rng = np.random.default_rng(14)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 30, 20, VOCAB)
+    ids[0, 3] = VOCAB + 5  # a text row (amask 0)
+    m = LM.LM(model_path)
+    with pytest.raises(Exception, match="status 128"):
+        m.forward_cfg(ids, amask, cond, unc, pos)
+    assert ovb.device_status() == 0
+    m.close()

@@ -1,0 +1,54 @@
+"""The reference's own LM (cpp/src/model/lm.cpp, built into oracle/_ref) on a
+random checkpoint written by ovnative_b200.ovw1.random_lm: the reference
+loads the file (so the writer produces what its LM expects) and its two
+forwards agree with each other where the reference says they must (the
+ragged CFG forward equals the batched one on the conditional rows,
+lm.h:71-76)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from ovnative_b200 import ovw1
+
+pytestmark = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+
+C, V = 8, 1025
+
+
+def cfg_inputs(rng, cs, us, vocab, n_text=12, pad=2):
+    rows = cs + us
+    ids = rng.integers(0, V, size=(C, rows)).astype(np.int64)
+    amask = np.ones(rows, np.uint8)
+    amask[:n_text] = 0
+    ids[0, :n_text] = rng.integers(0, vocab, size=n_text)
+    cond = np.ones((cs, cs), np.uint8)
+    cond[:, :pad] = 0          # padded keys
+    unc = np.ones((us, us), np.uint8)
+    pos = np.concatenate([np.arange(cs), np.arange(us)]).astype(np.int64)
+    return ids, amask, cond, unc, pos
+
+
+def test_reference_lm_runs_on_written_checkpoint(repo_tmp):
+    p = str(repo_tmp / "lm2.ovw")
+    ovw1.random_lm(p, n_layers=2, vocab=512, seed=1)
+    ref = O.RefLM(p, 2)
+    rng = np.random.default_rng(2)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 40, 24, 512)
+    logits = ref.forward_cfg(ids, amask, cond, unc, pos)
+    assert logits.shape == (64, C * V) and np.isfinite(logits).all()
+    assert logits.std() > 0.05
+    # forward(B=1) over the conditional rows alone gives the same cond logits
+    ids_b = ids[:, :40][None]
+    lb = ref.forward(ids_b, amask[None, :40], cond[None], pos[None, :40])
+    np.testing.assert_allclose(lb[0].transpose(1, 0, 2).reshape(40, C * V), logits[:40],
+                               rtol=1e-4, atol=1e-4)
+    ref.close()
+
+
+def test_reference_lm_rejects_missing_layers(repo_tmp):
+    p = str(repo_tmp / "lm1.ovw")
+    ovw1.random_lm(p, n_layers=1, vocab=64, seed=3)
+    with pytest.raises(RuntimeError, match="tensor not found"):
+        O.RefLM(p, 2)
