@@ -405,6 +405,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     sampler = time_sampler(dev, stream) if world == 1 else None
     attention = time_attention(dev, stream) if world == 1 else None
     weight_load = time_weight_load(dev) if world == 1 and not args.no_cpu_baseline else None
+    lm_forward = (time_lm_forward(dev, stream, f16) if world == 1 and not args.no_cpu_baseline
+                  else None)
     status |= ovb.device_status()
 
     # ---- the other numerics path over the same K steps (reported, not headline)
@@ -470,6 +472,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "sampler": sampler,
         "attention": attention,
         "weight_load": weight_load,
+        "lm_forward": lm_forward,
         "clocks": clk.summary(),
     }
 
@@ -728,6 +731,103 @@ def time_weight_load(dev, layers: int = 28) -> dict:
                 "what": "ov::s8_nk_pack per tensor (make_linear's host repack)"}}
 
 
+# ------------------------------------------------------------ LM forward
+# BASELINE configs 2 and 3: the full 28-layer LM forward of a CFG pair
+# (cond + uncond rows of S tokens each) with random-init int8 weights.
+LM_CONFIGS = {"config2": 300, "config3": 700}
+
+
+def _lm_inputs(rng, S, vocab, n_text=40):
+    C, V = 8, 1025
+    rows = 2 * S
+    ids = rng.integers(0, V, size=(C, rows)).astype(np.int64)
+    amask = np.ones(rows, np.uint8)
+    amask[:n_text] = 0  # the conditional prompt's text ids
+    ids[0, :n_text] = rng.integers(0, vocab, size=n_text)
+    cond = np.ones((S, S), np.uint8)
+    unc = np.ones((S, S), np.uint8)
+    pos = np.concatenate([np.arange(S), np.arange(S)]).astype(np.int64)
+    return ids, amask, cond, unc, pos
+
+
+def time_lm_forward(dev, stream, f16: bool, layers: int = 28, vocab: int = 151676,
+                    reps: int = 8) -> dict:
+    """LM forward tokens/s (cond + uncond rows per forward / time) at configs
+    2 and 3 through ovb_lm: device-resident inputs, the forward captured in
+    one CUDA graph, CUDA events around `reps` replays; e2e through
+    ovb_lm_forward_cfg (host inputs in, host logits out, synchronous).  The
+    reference's own LM::forward_cfg (oracle/_ref, OpenMP on all host cores)
+    runs the same checkpoint and inputs on a bounded sample (one forward per
+    config after one warm-up)."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    import oracle as O
+    import ovnative_b200 as ovb
+    from ovnative_b200 import lm as LM
+    from ovnative_b200 import ovw1
+    d = tempfile.mkdtemp(prefix="ovb_lm_")
+    out = {"layers": layers, "numerics": "fp16" if f16 else "exact", "vocab": vocab,
+           "data": "synthetic (random-init int8 weights and embeddings, random ids)"}
+    try:
+        path = os.path.join(d, "lm.ovw")
+        ovw1.random_lm(path, n_layers=layers, vocab=vocab, seed=21)
+        m = LM.LM(path, f16=f16)
+        rng = np.random.default_rng(22)
+        ref = O.RefLM(path, layers) if O.ref_available() else None
+        for name, S in LM_CONFIGS.items():
+            ids, amask, cond, unc, pos = _lm_inputs(rng, S, vocab)
+            rows = 2 * S
+            m.reserve(rows, 2 * S * S)
+            t = [torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+                 for a in (ids, amask, cond, unc, pos)]
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    m.forward_cfg_device(*t)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    m.forward_cfg_device(*t)
+                g.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            g.reset()
+            # end to end: host inputs, host logits
+            m.forward_cfg(ids, amask, cond, unc, pos)
+            t0 = time.perf_counter()
+            for _ in range(3):
+                m.forward_cfg(ids, amask, cond, unc, pos)
+            e2e_ms = (time.perf_counter() - t0) / 3 * 1e3
+            entry = {"rows": rows, "ms": round(ms, 3), "tokens_per_s": round(rows / ms * 1e3, 1),
+                     "e2e_ms": round(e2e_ms, 3),
+                     "e2e_tokens_per_s": round(rows / e2e_ms * 1e3, 1)}
+            if ref is not None:
+                ref.forward_cfg(ids, amask, cond, unc, pos)
+                t0 = time.perf_counter()
+                ref.forward_cfg(ids, amask, cond, unc, pos)
+                rs = time.perf_counter() - t0
+                entry["cpu_baseline"] = {"ms": round(rs * 1e3, 1),
+                                         "tokens_per_s": round(rows / rs, 1),
+                                         "cores": os.cpu_count(), "kind": "reference",
+                                         "what": "LM::forward_cfg (AVX-VNNI int8, OpenMP)"}
+            out[name] = entry
+        if ovb.device_status() != 0:
+            raise RuntimeError("bounded device wait timed out in the LM forward")
+        m.close()
+        if ref is not None:
+            ref.close()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return out
+
+
 # ------------------------------------------------------------ attention
 # The attention of one layer at config 3's length: a CFG pair of 700-token
 # segments (cond, uncond) with the reference's 0 / -1e30 padding bias, 16
@@ -872,6 +972,8 @@ def main():
                     help="do not time the other numerics path (for profiling runs)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="only time the isolated GEMM M-sweep of config 4 (both mainloops)")
+    ap.add_argument("--lm-only", action="store_true",
+                    help="only time the 28-layer LM forward at configs 2 and 3")
     ap.add_argument("--load-only", action="store_true",
                     help="only time loading a synthetic OVW1 checkpoint's int8 weights")
     ap.add_argument("--attention-only", action="store_true",
@@ -896,6 +998,12 @@ def main():
                "cpu_baseline": sweep_cpu_baseline([(n, m) for n in SWEEP_SHAPES
                                                    for m in SWEEP_M])}
         print(json.dumps(res), flush=True)
+        return
+    if args.lm_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(time_lm_forward(dev, torch.cuda.Stream(device=dev),
+                                         args.numerics == "fp16")), flush=True)
         return
     if args.load_only:
         import torch
