@@ -52,3 +52,54 @@ def test_reference_lm_rejects_missing_layers(repo_tmp):
     ovw1.random_lm(p, n_layers=1, vocab=64, seed=3)
     with pytest.raises(RuntimeError, match="tensor not found"):
         O.RefLM(p, 2)
+
+
+def _create(path):
+    import ctypes as Cc
+
+    from ovnative_b200 import _lib as L
+    h = Cc.c_void_p()
+    rc = L.lib().ovb_lm_create(path.encode(), 0, None, Cc.byref(h))
+    return rc, L.lib().ovb_last_error().decode()
+
+
+def test_lm_create_rejects_bad_checkpoints(repo_tmp):
+    """ovb_lm_create's checks run before any device call (so on the CPU):
+    a missing file, a file without layers, and fp32 audio heads (not on the
+    int8 path) are invalid arguments with a message."""
+    from ovnative_b200 import _lib as L
+    rc, msg = _create(str(repo_tmp / "absent.ovw"))
+    assert rc == L.OVB_ERR_INVALID_ARG and "cannot open" in msg
+    p = str(repo_tmp / "norm_only.ovw")
+    ovw1.write(p, [("llm.norm.weight", np.ones(1024, np.float32), 0, None)])
+    rc, msg = _create(p)
+    assert rc == L.OVB_ERR_INVALID_ARG and "llm.layers.0" in msg
+    # a one-layer checkpoint whose audio heads are fp32 [K, N] (the reference's
+    # default conversion)
+    full = str(repo_tmp / "lm1.ovw")
+    ovw1.random_lm(full, n_layers=1, vocab=64, seed=5)
+    with ovw1.OVW1File(full) as f:
+        ts = []
+        for name in f.names():
+            a = np.array(f.array(name))
+            sc = f.scales(name)
+            if name == "audio_heads.weight":
+                ts.append((name, np.zeros((1024, 8200), np.float32), 1, None))
+            else:
+                ts.append((name, a, f.info(name).layout, None if sc is None else np.array(sc)))
+    p = str(repo_tmp / "fp32_heads.ovw")
+    ovw1.write(p, ts)
+    rc, msg = _create(p)
+    assert rc == L.OVB_ERR_INVALID_ARG and "audio_heads.weight" in msg
+
+
+def test_lm_entry_points_reject_null_model():
+    from ovnative_b200 import _lib as L
+    lib = L.lib()
+    assert lib.ovb_lm_forward_cfg(None, 4, 4, None, None, None, None, None, None, None) == \
+        L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_lm_forward(None, 1, 4, None, None, None, None, None, None) == \
+        L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_lm_reserve(None, 4, 16) == L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_lm_destroy(None) == L.OVB_OK
+    assert lib.ovb_lm_logits(None) is None
