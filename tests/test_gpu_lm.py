@@ -24,7 +24,7 @@ LAYERS, VOCAB = 2, 512
 
 
 @pytest.fixture(scope="module")
-def model_path(tmp_path_factory):
+def model_path():
     import os
     import shutil
 
