@@ -75,40 +75,47 @@ __global__ void mask_bias_kernel(const uint8_t* attn, int64_t n, float* bias) {
 //   scale = 1 / sqrt(sum(v^2) / D + eps);  a = (v[i] scale) w[i],
 //   b = (v[i+64] scale) w[i+64];  v[i] = a cos - b sin;  v[i+64] = b cos + a sin,
 // angle = pos * inv_freq[i], inv_freq[i] = (float) theta^(-2i/D) computed on
-// the host as the reference does.  One warp per head vector; lane l holds
-// elements l, l+32, l+64, l+96.  The sum of squares runs in a warp tree and
-// cos / sin are CUDA's (not glibc's): results agree to a few ulps.
+// the host as the reference does.  One block per row: its 64 cos / sin pairs
+// are computed once into shared memory (as the reference tabulates them per
+// row), then each warp normalises and rotates head vectors of the row; lane l
+// holds elements l, l+32, l+64, l+96.  The sum of squares runs in a warp tree
+// and cos / sin are CUDA's (not glibc's): results agree to a few ulps.
 __global__ void qk_norm_rope_kernel(float* q, float* k, const float* qw, const float* kw,
                                     const int64_t* pos, const float* inv_freq, int64_t rows,
                                     int n_heads, int n_kv, float eps) {
   constexpr int D = 128, half = 64;
-  const int64_t gw = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int per_row = n_heads + n_kv;
-  if (gw >= rows * per_row) return;
-  const int64_t r = gw / per_row;
-  const int h = static_cast<int>(gw % per_row);
-  float* v = h < n_heads ? q + (r * n_heads + h) * D : k + (r * n_kv + (h - n_heads)) * D;
-  const float* w = h < n_heads ? qw : kw;
-  float x[4];
+  __shared__ float cs_s[half], sn_s[half];
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  if (threadIdx.x < half) {
+    const float angle = __fmul_rn(static_cast<float>(pos[r]), inv_freq[threadIdx.x]);
+    cs_s[threadIdx.x] = cosf(angle);
+    sn_s[threadIdx.x] = sinf(angle);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = static_cast<int>(blockDim.x >> 5);
+  for (int h = warp; h < n_heads + n_kv; h += nw) {
+    float* v = h < n_heads ? q + (r * n_heads + h) * D : k + (r * n_kv + (h - n_heads)) * D;
+    const float* w = h < n_heads ? qw : kw;
+    float x[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = v[lane + 32 * j];
-  float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
-                        __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+    for (int j = 0; j < 4; ++j) x[j] = v[lane + 32 * j];
+    float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                          __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-  const float scale =
-      __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(D)), eps)));
-  const float p = static_cast<float>(pos[r]);
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float scale =
+        __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(D)), eps)));
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int i = lane + 32 * j;  // 0 .. 63
-    const float angle = __fmul_rn(p, inv_freq[i]);
-    const float cs = cosf(angle), sn = sinf(angle);
-    const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
-    const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
-    v[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-    v[i + half] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+    for (int j = 0; j < 2; ++j) {
+      const int i = lane + 32 * j;  // 0 .. 63
+      const float cs = cs_s[i], sn = sn_s[i];
+      const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
+      const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
+      v[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+      v[i + half] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+    }
   }
 }
 
@@ -139,10 +146,8 @@ cudaError_t launch_mask_bias(const uint8_t* attn, int64_t n, float* bias, cudaSt
 cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float* kw,
                                 const int64_t* pos, const float* inv_freq, int64_t rows,
                                 int n_heads, int n_kv, float eps, cudaStream_t s) {
-  const int64_t warps = rows * (n_heads + n_kv);
-  const int64_t blocks = (warps + 7) / 8;
-  return launch_plain(qk_norm_rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
-                      q, k, qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
+  return launch_plain(qk_norm_rope_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s, q,
+                      k, qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
 }
 
 cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,
