@@ -184,6 +184,8 @@ def ref_lib():
             "ref_attention_head": ([_p, _i64, _p, _p, _i64, _p, C.c_int, C.c_int, C.c_float,
                                     _p, _i64], C.c_int),
             "ref_ovw1_tensor": ([C.c_char_p, C.c_char_p, _p, _p, C.c_char_p, C.c_int], C.c_int),
+            "ref_attention_layer": ([_p, _p, _p, _p, _i64, _i64, C.c_int, C.c_int, C.c_int,
+                                     C.c_float, _p, _p, _p, _p, C.c_int], C.c_int),
             "ref_lm_create": ([C.c_char_p, C.c_int, C.c_char_p, C.c_int], _p),
             "ref_lm_destroy": ([_p], None),
             "ref_lm_forward_cfg": ([_p, C.c_int, C.c_int, _p, _p, _p, _p, _p, _p], C.c_int),
@@ -455,3 +457,24 @@ class RefLM:
         _chk(ref_lib().ref_lm_forward(self._h, B, S, _ptr(ids), _ptr(a), _ptr(m), _ptr(pos),
                                       _ptr(out)), "LM::forward")
         return out
+
+
+def attention_layer(q: np.ndarray, k: np.ndarray, v: np.ndarray, segs, n_heads: int, n_kv: int,
+                    D: int, scale: float) -> np.ndarray:
+    """The reference's attention loop of LM::run_layer (cpp/src/model/lm.cpp:
+    256-274) as it runs there: ov::attention_head_f32 for every (segment, kv
+    head, query head) in one OpenMP loop over the host cores (oracle/_ref).
+    Same arguments and result as `attention`."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.zeros_like(q)
+    n = len(segs)
+    biases = [None if b is None else _f32(b) for b, _, _, _ in segs]
+    bp = (C.c_void_p * n)(*[None if b is None else b.ctypes.data for b in biases])
+    rows = np.array([r for _, r, _, _ in segs], np.int32)
+    qo = np.array([o for _, _, o, _ in segs], np.int64)
+    ko = np.array([o for _, _, _, o in segs], np.int64)
+    _chk(ref_lib().ref_attention_layer(_ptr(q), _ptr(k), _ptr(v), _ptr(out), n_heads * D,
+                                       n_kv * D, n_heads, n_kv, D, scale, C.cast(bp, C.c_void_p),
+                                       _ptr(rows), _ptr(qo), _ptr(ko), n),
+         "attention loop of LM::run_layer")
+    return out

@@ -159,6 +159,38 @@ REF_API int ref_ovw1_tensor(const char* path, const char* name, int64_t* info, u
   }
 }
 
+// The attention of one layer as LM::run_layer runs it (lm.cpp:256-274):
+// ov::attention_head_f32 for every (segment, kv head, query head of the
+// group) in one OpenMP loop, head h at column h*D of q/out, kv head h/group
+// at column kv*D of k/v.  The worker threads' MXCSR is restored afterwards
+// (the AVX2 kernels turn on flush-to-zero).
+REF_API int ref_attention_layer(const float* q, const float* k, const float* v, float* out,
+                                int64_t QD, int64_t KVD, int NH, int NKV, int D, float scale,
+                                const float* const* bias, const int* rows, const int64_t* q_off,
+                                const int64_t* kv_off, int n_segs) {
+  const unsigned csr = _mm_getcsr();
+  const int group = NH / NKV;
+  int bad = 0;
+#pragma omp parallel for collapse(3) schedule(static) reduction(| : bad)
+  for (int seg = 0; seg < n_segs; ++seg) {
+    for (int kv = 0; kv < NKV; ++kv) {
+      for (int g = 0; g < group; ++g) {
+        const int h = kv * group + g;
+        const int64_t qo = q_off[seg] + static_cast<int64_t>(h) * D;
+        const int64_t ko = kv_off[seg] + static_cast<int64_t>(kv) * D;
+        bad |= guard([&] {
+          ov::attention_head_f32(q + qo, QD, k + ko, v + ko, KVD, bias[seg], rows[seg], D, scale,
+                                 out + qo, QD);
+        });
+      }
+    }
+  }
+#pragma omp parallel
+  { _mm_setcsr(csr); }
+  _mm_setcsr(csr);
+  return bad;
+}
+
 // The reference's LM (cpp/src/model/lm.h:52-140) over an OVW1 file: LMConfig
 // defaults except n_layers.  The WeightFile outlives the LM (its tensors point
 // into the mapping).  The forwards switch every OpenMP worker to flush-to-zero

@@ -101,3 +101,16 @@ def test_abi_no_work_is_ok():
     assert _call(n_segs=0, q=0) == L.OVB_OK
     arr = (L.AttnSegment * 2)(L.AttnSegment(None, 0, 0, 0), L.AttnSegment(None, 0, 256, 128))
     assert _call(segs=C.cast(arr, C.POINTER(L.AttnSegment)), n_segs=2) == L.OVB_OK
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+def test_reference_layer_loop_equals_per_head_calls():
+    """oracle.attention_layer (the OpenMP loop of LM::run_layer over the
+    reference's attention_head_f32, the bench's CPU baseline) gives the same
+    bytes as calling attention_head_f32 head by head."""
+    rng = np.random.default_rng(9)
+    q, k, v, segs = make_case(rng, (130, 61, 7), 8, 2, masked_rows=(2,), pad_keys=3)
+    segs[1] = (None,) + segs[1][1:]
+    a = O.attention(q, k, v, segs, 8, 2, D, 0.07, use_ref=True)
+    b = O.attention_layer(q, k, v, segs, 8, 2, D, 0.07)
+    assert a.tobytes() == b.tobytes()
