@@ -532,23 +532,38 @@ def time_sampler(dev, stream, launches: int = 64, sets: int = 4) -> dict:
 
 
 def sampler_cpu_baseline(budget_s: float = 1.0) -> dict:
-    """The C restatement of the reference's CPU loop (oracle port, one thread)
-    on a bounded sample of rows, scaled to one step of SAMPLER."""
+    """The C restatement of the reference's CPU loop (oracle port) on one
+    whole step of SAMPLER, its frames split into one slice per host core and
+    the slices run on concurrent threads (the ctypes calls release the GIL),
+    as the reference's loop runs its rows in parallel: one warm-up step, then
+    steps until `budget_s` (at least one)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     import oracle as O
     sp = SAMPLER
-    C, V = sp["codebooks"], sp["vocab"]
-    T_s = 16
+    C, V, T = sp["codebooks"], sp["vocab"], sp["target_len"]
     rng = np.random.default_rng(3)
-    cond = (rng.standard_normal((T_s, C * V)) * 3).astype(np.float32)
-    unc = (rng.standard_normal((T_s, C * V)) * 3).astype(np.float32)
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < budget_s:
-        O.guided_sample(cond, unc, T_s, C, sp["guidance"], sp["layer_penalty"], sp["mask_id"])
-        n += 1
-    sec = time.perf_counter() - t0
-    us_step = sec / (n * C * T_s) * C * sp["target_len"] * 1e6
-    return {"us_per_step": us_step, "cores": 1, "kind": "port",
-            "sample": f"{n} x {C * T_s} rows in {sec:.2f} s, scaled to {C * sp['target_len']} rows"}
+    cond = (rng.standard_normal((sp["cond_seq"], C * V)) * 3).astype(np.float32)
+    unc = (rng.standard_normal((sp["uncond_seq"], C * V)) * 3).astype(np.float32)
+    cores = os.cpu_count() or 1
+    bounds = np.linspace(0, T, min(cores, T) + 1).astype(int)
+    off = sp["cond_seq"] - T  # the cond plane's target rows start here
+
+    def part(i):
+        t0, t1 = int(bounds[i]), int(bounds[i + 1])
+        return O.guided_sample(cond[off + t0:off + t1], unc[t0:t1], t1 - t0, C, sp["guidance"],
+                               sp["layer_penalty"], sp["mask_id"])
+
+    with ThreadPoolExecutor(max_workers=len(bounds) - 1) as ex:
+        list(ex.map(part, range(len(bounds) - 1)))
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget_s:
+            list(ex.map(part, range(len(bounds) - 1)))
+            n += 1
+        sec = time.perf_counter() - t0
+    return {"us_per_step": sec / n * 1e6, "cores": len(bounds) - 1, "kind": "port",
+            "sample": f"{n} whole steps ({C} x {T} rows) in {sec:.2f} s, frames split over "
+                      f"{len(bounds) - 1} threads"}
 
 
 # ------------------------------------------------------------ GEMM M-sweep
