@@ -192,7 +192,11 @@ def ref_lib():
             "ref_lm_forward": ([_p, C.c_int, C.c_int, _p, _p, _p, _p, _p], C.c_int),
         }
         for name, (args, res) in sig.items():
-            f = getattr(lib, name)
+            # a library built before a wrapper was added lacks its symbol: that
+            # wrapper fails when called, the others keep working
+            f = getattr(lib, name, None)
+            if f is None:
+                continue
             f.argtypes = args
             f.restype = res
         _ref = lib
