@@ -930,7 +930,7 @@ def attention_cpu_baseline(budget_s: float = 1.0) -> dict:
     H, KV, Dh = at["n_heads"], at["n_kv"], at["head_dim"]
     rng = np.random.default_rng(5)
     scale = 1.0 / float(np.sqrt(Dh))
-    if O.ref_available():
+    if O.ref_available() and hasattr(O.ref_lib(), "ref_attention_layer"):
         T = sum(at["segments"])
         q = rng.standard_normal((T, H * Dh)).astype(np.float32)
         k = rng.standard_normal((T, KV * Dh)).astype(np.float32)
