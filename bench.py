@@ -75,9 +75,10 @@ class ClockSampler:
         "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period: float = 0.01):
+    def __init__(self, cuda_index: int, period: float = 0.01):
         self.samples = []
         self.reasons = 0
+        self.pci_bus_id = None
         self.max_mhz = None
         self._stop = threading.Event()
         self._h = None
@@ -86,7 +87,10 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            # NVML numbers GPUs in PCI order and ignores CUDA_VISIBLE_DEVICES:
+            # find the handle by the CUDA device's PCI bus id.
+            self.pci_bus_id = _pci_bus_id(cuda_index)
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(self.pci_bus_id.encode())
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
         except Exception as e:  # NVML missing: report why, keep running
             self.error = str(e)
@@ -118,9 +122,19 @@ class ClockSampler:
         names = sorted(k for k, bit in self.REASONS.items() if self.reasons & bit)
         out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        if self.pci_bus_id:
+            out["pci_bus_id"] = self.pci_bus_id
         if self.error:
             out["error"] = self.error
         return out
+
+
+def _pci_bus_id(cuda_index: int) -> str:
+    """PCI bus id of CUDA device `cuda_index` in NVML's form
+    (domain:bus:device.function)."""
+    import torch
+    p = torch.cuda.get_device_properties(cuda_index)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
 
 
 # --------------------------------------------------------------- roofline

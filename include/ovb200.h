@@ -227,9 +227,12 @@ int ovb_linear(int64_t M, const ovb_weight* w, const float* A, int64_t lda, floa
  * without `work`: the quantised activations go to an 8 MiB device array
  * inside the library, one per device, held until the process exits.
  * Sizes with ovb_linear_workspace_bytes(M, K) above 8 MiB return
- * OVB_ERR_INVALID_ARG.  Calls that overlap on the GPU race on the array; the
- * first call on a device sets up the array's address and should come before
- * any stream capture.  No counterpart in the reference. */
+ * OVB_ERR_INVALID_ARG.  Arguments are checked before anything is enqueued.
+ * Calls that overlap on the GPU race on the array.  The first call in each
+ * CUDA context (the device's primary context, a context the host binds
+ * through the driver API, or the new context after cudaDeviceReset) looks up
+ * the array's address in that context and should come before any stream
+ * capture in it.  No counterpart in the reference. */
 int ovb_linear_static(int64_t M, const ovb_weight* w, const float* A, int64_t lda, float* C,
                       int64_t ldc, int accumulate, void* stream);
 

@@ -101,6 +101,26 @@ class RefLayer:
         return O.linear_q(aq, asc, *self.w["down"], INTER, x)
 
 
+def host_cpu() -> dict:
+    """The host CPU as the reference's baseline reports it: model name (from
+    /proc/cpuinfo, as lscpu shows it) and whether it has AVX-VNNI, which
+    decides the reference's int8 path (gemm.cpp:556-572)."""
+    model, flags = None, set()
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k = k.strip()
+                if k == "model name" and model is None:
+                    model = v.strip()
+                elif k == "flags" and not flags:
+                    flags = set(v.split())
+    except OSError:
+        pass
+    return {"cpu_model": model, "avx_vnni": "avx_vnni" in flags,
+            "avx512_vnni": "avx512_vnni" in flags, "logical_cpus": os.cpu_count()}
+
+
 def pick_mode() -> tuple[str, str]:
     """(mode, kind): what the reference itself would run on this host."""
     if O.ref_available():
@@ -143,4 +163,5 @@ def run(M: int = 400, layers: int = 4, max_steps: int = 1 << 30, budget_s: float
         "sample": f"{steps} layer steps (M={M}, {layers} weight sets) in {dt:.2f} s; {label}",
         "steps": steps,
         "seconds": dt,
+        "host": host_cpu(),
     }

@@ -73,7 +73,6 @@ def build(force: bool = False, verbose: bool = False) -> str:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError(f"nvcc failed on {src}")
     if force or _stale(LIB, objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"]
         cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs]
         if verbose:
             print(" ".join(cmd))

@@ -28,9 +28,16 @@
 //   - The array keeps the last call's contents.  Nothing needs clearing: the
 //     quantiser writes every aq byte (tail padding included) and every scale
 //     before the GEMM reads them.
-//   - The first call on a device looks up the array's device address (with
-//     that device current) and caches it.  Make that first call before any
-//     CUDA stream capture on the device.
+//   - Arguments are checked before anything is enqueued: a rejected call
+//     leaves the array (and any ordered call still reading it) untouched.
+//   - The first call in a CUDA context looks up the array's device address
+//     (cudaGetSymbolAddress, with that context current) and caches it under
+//     the context's unique id.  A symbol's address belongs to a context, so a
+//     host that binds its own driver-API context, or a process that calls
+//     cudaDeviceReset and continues in a new context, gets a fresh lookup
+//     rather than a stale address.  Make the first call in each context
+//     before any CUDA stream capture in it.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -43,34 +50,79 @@
 namespace {
 
 constexpr size_t kStaticScratchBytes = size_t{8} << 20;
-constexpr int kMaxDevices = 64;
+constexpr int kCacheEntries = 64;
 
 // The scratch itself.  In host code this name is only a stand-in for the
 // symbol; the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_linear_scratch[kStaticScratchBytes];
 
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_linear_scratch on the current device (looked up once
-// per device).  Returns OVB_OK or a status with ovb_last_error() set.
+template <class Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPointByVersion(name, &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
+// Unique id of the calling thread's current CUDA context (0 with none).
+bool current_context_id(unsigned long long* id) {
+  static const CtxGetCurrentFn get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  *id = 0;
+  if (!get_current || !get_id) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return false;
+  if (!ctx) return true;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+struct CacheEntry {
+  unsigned long long ctx_id;
+  void* addr;
+};
+std::mutex g_scratch_mu;
+CacheEntry g_cache[kCacheEntries] = {};
+int g_cache_next = 0;
+
+// Device address of g_linear_scratch in the current context (looked up once
+// per context).  Returns OVB_OK or a status with ovb_last_error() set.
 int scratch_address(void** out) {
-  int dev = 0;
-  if (ovb::cuda_failed(cudaGetDevice(&dev), "cudaGetDevice")) return OVB_ERR_INTERNAL;
-  if (dev < 0 || dev >= kMaxDevices) {
-    ovb::set_error("ovb_linear_static: device index beyond the supported 64");
+  unsigned long long id = 0;
+  if (!current_context_id(&id)) {
+    ovb::set_error("ovb_linear_static: cannot identify the current CUDA context");
     return OVB_ERR_INTERNAL;
   }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    if (ovb::cuda_failed(cudaGetSymbolAddress(&p, g_linear_scratch),
-                         "cudaGetSymbolAddress(static scratch)"))
-      return OVB_ERR_INTERNAL;
-    g_scratch_addr[dev] = p;
+  if (id != 0)
+    for (const CacheEntry& e : g_cache)
+      if (e.ctx_id == id && e.addr) {
+        *out = e.addr;
+        return OVB_OK;
+      }
+  // With no context current yet, this lookup creates the device's primary
+  // context; its id is read afterwards.
+  void* p = nullptr;
+  if (ovb::cuda_failed(cudaGetSymbolAddress(&p, g_linear_scratch),
+                       "cudaGetSymbolAddress(static scratch)"))
+    return OVB_ERR_INTERNAL;
+  if (id == 0 && (!current_context_id(&id) || id == 0)) {
+    ovb::set_error("ovb_linear_static: no CUDA context after the symbol lookup");
+    return OVB_ERR_INTERNAL;
   }
-  *out = g_scratch_addr[dev];
+  g_cache[g_cache_next] = {id, p};
+  g_cache_next = (g_cache_next + 1) % kCacheEntries;
+  *out = p;
   return OVB_OK;
+}
+
+int invalid(const char* msg) {
+  ovb::set_error(msg);
+  return OVB_ERR_INVALID_ARG;
 }
 
 }  // namespace
@@ -78,20 +130,25 @@ int scratch_address(void** out) {
 extern "C" int ovb_linear_static(int64_t M, const ovb_weight* w, const float* A, int64_t lda,
                                  float* C, int64_t ldc, int accumulate, void* stream) {
   if (M <= 0) return OVB_OK;
-  if (!w) {
-    ovb::set_error("weight handle is null");
-    return OVB_ERR_INVALID_ARG;
-  }
-  const size_t need = ovb_linear_workspace_bytes(M, w->K);
-  if (need > kStaticScratchBytes) {
-    char buf[200];
+  // Every check comes before the first enqueue (see the rules above).
+  if (!w) return invalid("weight handle is null");
+  if (!A || !C) return invalid("A/C must be non-null");
+  if (w->K <= 0 || w->N <= 0) return invalid("weight has no elements");
+  if (lda < w->K) return invalid("lda < K");
+  if (ldc < w->N) return invalid("ldc < N");
+  // Bound M before any size arithmetic, so that a huge M cannot wrap the
+  // byte count below the limit: a row needs 32 * Kb quantised bytes and
+  // Kb fp32 scales.
+  const int64_t kb = (w->K + 31) / 32;
+  const int64_t max_rows = static_cast<int64_t>(kStaticScratchBytes / (36 * static_cast<size_t>(kb)));
+  const size_t need = M <= max_rows ? ovb_linear_workspace_bytes(M, w->K) : 0;
+  if (M > max_rows || need > kStaticScratchBytes) {
+    char buf[240];
     std::snprintf(buf, sizeof buf,
-                  "ovb_linear_static: M=%lld x K=%lld needs %zu bytes of scratch, above the "
-                  "%zu-byte static limit; use ovb_linear with a workspace",
-                  static_cast<long long>(M), static_cast<long long>(w->K), need,
-                  kStaticScratchBytes);
-    ovb::set_error(buf);
-    return OVB_ERR_INVALID_ARG;
+                  "ovb_linear_static: M=%lld x K=%lld needs more than the %zu-byte static "
+                  "scratch; use ovb_linear with a workspace",
+                  static_cast<long long>(M), static_cast<long long>(w->K), kStaticScratchBytes);
+    return invalid(buf);
   }
   void* scratch = nullptr;
   int st = scratch_address(&scratch);

@@ -214,7 +214,9 @@ int ovb_ovw1_open(const char* path, ovb_ovw1** out) {
     t.nbytes = static_cast<int64_t>(d.nbytes);
     t.crc = static_cast<uint32_t>(d.hash & 0xFFFFFFFFu);
     if (d.quant == 1) {
-      if (d.aux_off + static_cast<uint64_t>(d.aux_n) * 4 > size) return reject("scales out of bounds");
+      // Written so that no sum can wrap: a huge aux_off is out of bounds too.
+      if (d.aux_off > size || static_cast<uint64_t>(d.aux_n) * 4 > size - d.aux_off)
+        return reject("scales out of bounds");
       t.scales = reinterpret_cast<const float*>(cbase + d.aux_off);
       t.n_scales = d.aux_n;
     }

@@ -56,3 +56,17 @@ def test_noop_and_argument_errors_without_device():
         L.OVB_ERR_INVALID_ARG
     with pytest.raises(ValueError):
         L.check(L.OVB_ERR_INVALID_ARG)
+
+
+def test_static_linear_checks_arguments_before_the_device():
+    """ovb_linear_static rejects a null weight and null A/C before it looks
+    up its device array or enqueues anything (no GPU here)."""
+    lib = L.lib()
+    assert lib.ovb_linear_static(0, None, None, 0, None, 0, 0, None) == L.OVB_OK
+    assert lib.ovb_linear_static(4, None, None, 0, None, 0, 0, None) == L.OVB_ERR_INVALID_ARG
+    assert b"null" in lib.ovb_last_error()
+    # A non-null handle is not read before the A/C check.
+    fake = C.create_string_buffer(4096)
+    assert lib.ovb_linear_static(4, C.addressof(fake), None, 0, None, 0, 0, None) == \
+        L.OVB_ERR_INVALID_ARG
+    assert b"A/C" in lib.ovb_last_error()

@@ -138,6 +138,19 @@ def test_rejects_like_the_reference(repo_tmp, case, msg):
         assert ref_err is not None and ref_err == str(e.value)
 
 
+def test_rejects_wrapping_scale_offset(repo_tmp):
+    """A scales offset so large that offset + bytes wraps past 2^64 is out of
+    bounds (not compared with the reference loader, whose check is a plain
+    sum)."""
+    b = _file(repo_tmp, np.random.default_rng(2))
+    d1 = _desc_off(b, 1)
+    struct.pack_into("<Q", b, d1 + 56, (1 << 64) - 8)
+    p = repo_tmp / "wrap.ovw"
+    p.write_bytes(bytes(b))
+    with pytest.raises(ValueError, match="scales out of bounds"):
+        ovw1.OVW1File(str(p))
+
+
 def test_missing_file_and_tensor(repo_tmp):
     with pytest.raises(ValueError, match="cannot open"):
         ovw1.OVW1File(str(repo_tmp / "nope.ovw"))

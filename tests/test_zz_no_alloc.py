@@ -77,5 +77,9 @@ def test_static_entry_point_rejects_sizes_beyond_its_array(cuda):
     C = torch.zeros((M, 64), device=cuda)
     st = lib.ovb_linear_static(M, w.handle, A.data_ptr(), K, C.data_ptr(), 64, 0, _stream())
     assert st == L.OVB_ERR_INVALID_ARG
-    assert b"static limit" in lib.ovb_last_error()
+    assert b"static" in lib.ovb_last_error()
+    # A row count so large that its byte count would wrap is refused too.
+    st = lib.ovb_linear_static(1 << 62, w.handle, A.data_ptr(), K, C.data_ptr(), 64, 0, _stream())
+    assert st == L.OVB_ERR_INVALID_ARG
+    assert b"static" in lib.ovb_last_error()
     w.close()
