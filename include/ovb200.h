@@ -76,6 +76,13 @@ extern "C" {
 #define OVB_AQ_U8 1      /* quantisers: write reference u8 (q+128) instead of int8 */
 #define OVB_AQ_F16 2     /* quantisers: write fp16(q * asc), [M, Kp] fp16 (2 bytes per
                             element, 16-byte aligned), the input of ovb_linear_h */
+#define OVB_AQ_F16_RAW 4 /* quantisers: write fp16 of the (normalised) fp32 values
+                            themselves, not quantised, [M, Kp] fp16 with a zero tail;
+                            asc is not written and may be NULL.  The input of
+                            ovb_linear_h with a weight from ovb_weight_create_f32: the
+                            reference's fp32 activations x fp32 weights (linear_f32,
+                            Mat::mul on an fp32 weight, mat.cpp:11-13).  Values beyond
+                            the fp16 range set ovb_device_status bit 16. */
 
 typedef struct ovb_weight ovb_weight;
 
@@ -140,6 +147,21 @@ typedef struct ovb_weight_src {
  * tensor by tensor on the host, mat.cpp:69-106). */
 int ovb_weight_create_batch(const ovb_weight_src* srcs, int n, int flags, void* stream,
                             ovb_weight** out);
+
+/* An fp32 linear weight -- the reference's fp32 encoding of a linear layer
+ * (OVW1 layout 1, [K, N], as tools/convert_weights.py:178-180 stores every
+ * fp32 matrix, e.g. the default fp32 audio heads, :326-327; or layout 0,
+ * [N, K]) consumed by Mat::mul -> linear_f32 (mat.cpp:11-13) -- held on the
+ * device as fp16 [N, Kp] with one power-of-two scale per output channel
+ * (2^(e-10), e the exponent of the channel's largest |w|: the scaling is
+ * exact and the one rounding is W/s to fp16, relative error <= 2^-11).  Only
+ * ovb_linear_h / ovb_linear_h_sliced accept it, with activations from a
+ * quantiser run with OVB_AQ_F16_RAW: fp16 x fp16 products summed in fp32,
+ * the precision of the reference CUDA runner's fp16 GEMMs (cuda_lm.cu:
+ * 1023-1030).  The int8 entry points reject it (it has no int8 image).
+ * W is a host pointer; synchronous; non-finite weights are rejected. */
+int ovb_weight_create_f32(const float* W, int layout, int64_t N, int64_t K, void* stream,
+                          ovb_weight** out);
 
 /* Concatenate weights with the same K along N (q|k|v, gate|up).  Replaces
  * combine_packed (lm.cpp:57-94).  The parts stay valid.  The result has the
@@ -359,8 +381,11 @@ int ovb_ovw1_weights(const ovb_ovw1* f, const char* const* names, int n, int fla
  * The whole LM forward on the device, built from an OVW1 checkpoint: the
  * reference's LM (cpp/src/model/lm.h:52-140, lm.cpp) for the accelerator
  * hook LM::CudaForwardFn (lm.h:91-96) and the ragged
- * CFG forward.  Linear weights (q/k/v/o, gate/up/down, audio_heads) must be
- * int8 with per-output-channel scales, either orientation; embeddings int8
+ * CFG forward.  Linear weights (q/k/v/o, gate/up/down) must be int8 with
+ * per-output-channel scales, either orientation; the audio heads int8 the
+ * same way or fp32 (the reference converter's default, tools/
+ * convert_weights.py:326-327, run through ovb_weight_create_f32 and fp16
+ * activations of the final RMSNorm, OVB_AQ_F16_RAW); embeddings int8
  * with row scales or fp32; head_dim 128; LMConfig's rms_eps 1e-6 and
  * rope_theta 1e6.  flags: 0 runs the bit-exact int8 mainloop, OVB_WEIGHT_F16
  * the fp16 one.  One model per (thread, device); its forward buffers grow on
@@ -386,6 +411,23 @@ int ovb_lm_forward_cfg_device(ovb_lm* m, int cond_seq, int uncond_seq, const int
                               const uint8_t* audio_mask, const uint8_t* cond_attn,
                               const uint8_t* uncond_attn, const int64_t* pos, void* stream);
 const float* ovb_lm_logits(const ovb_lm* m);
+/* Several attention segments in one forward, on device inputs (stream-
+ * ordered, no synchronisation): segment i has seg_rows[i] >= 1 rows (a HOST
+ * array of n_segs <= 64 counts), packed one after another; ids [C, rows]
+ * codebook-major, audio_mask [rows], pos [rows] and masks (each segment's
+ * [seg_rows[i], seg_rows[i]] u8 attention mask, concatenated) are device
+ * arrays; the logits [rows, C*V] stay at ovb_lm_logits(m).  Rows attend only
+ * within their own segment, and every other step of the forward works row by
+ * row, so each segment's logits are those of a forward over that segment
+ * alone.  A CFG pair is two segments (LM::forward_cfg, lm.cpp:403-454, is
+ * this call with n_segs = 2) and a batch of B rows B segments (LM::forward,
+ * lm.cpp:343-401): the call packs several utterances' CFG pairs into one
+ * forward -- the reference's AttnSegment list (cpp/src/model/lm.h:46-51)
+ * with more than one utterance in it, which the reference never builds (it
+ * runs one utterance at a time, cpp/src/model/tts.cpp:260-269). */
+int ovb_lm_forward_segments_device(ovb_lm* m, int n_segs, const int32_t* seg_rows,
+                                   const int64_t* ids, const uint8_t* audio_mask,
+                                   const uint8_t* masks, const int64_t* pos, void* stream);
 /* LM::forward (lm.cpp:343-401) with CudaForwardFn's arguments on host
  * buffers: input_ids [B, C, S], audio_mask [B, S], attn_mask [B, S, S],
  * position [B, S]; logits [B, C, S, V].  batch <= 64.  Synchronous. */

@@ -14,6 +14,7 @@ from .gemm import (  # noqa: F401
     device_status,
     empty_quant,
     empty_quant_f16,
+    linear_f32,
     linear_h,
     linear_h_silu,
     linear_h_sliced,
@@ -23,11 +24,13 @@ from .gemm import (  # noqa: F401
     linear_s8_nk_packed_q,
     linear_s8_nk_packed_q_add,
     linear_s8_nk_packed_q_sliced,
+    rmsnorm_f16,
     rmsnorm_quantize_f32,
     s8_nk_quant_bytes,
     s8_nk_quant_scales,
     s8_nk_quantize,
     silu_mul_quantize_f32,
+    to_f16,
     workspace_bytes,
 )
 from .attention import attention  # noqa: F401

@@ -21,6 +21,7 @@ OVB_SRC_DEVICE = 1
 OVB_WEIGHT_F16 = 2
 OVB_AQ_U8 = 1
 OVB_AQ_F16 = 2
+OVB_AQ_F16_RAW = 4
 
 _i64 = C.c_int64
 _p = C.c_void_p
@@ -98,6 +99,8 @@ SIGNATURES = {
     "ovb_lm_logits": ([_p], _p),
     "ovb_lm_forward_cfg": ([_p, _int, _int, _p, _p, _p, _p, _p, _p, _p], _int),
     "ovb_lm_forward_cfg_device": ([_p, _int, _int, _p, _p, _p, _p, _p, _p], _int),
+    "ovb_lm_forward_segments_device": ([_p, _int, _p, _p, _p, _p, _p, _p], _int),
+    "ovb_weight_create_f32": ([_p, _int, _i64, _i64, _p, C.POINTER(_p)], _int),
     "ovb_lm_forward": ([_p, _int, _int, _p, _p, _p, _p, _p, _p], _int),
     "ovb_attention": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
                        C.POINTER(AttnSegment), _int, _p], _int),

@@ -9,7 +9,9 @@
 // message is kept per thread for ovb_last_error().
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -150,9 +152,14 @@ inline bool aligned(const void* p, uintptr_t a) {
 
 // Output form of a quantiser from its flags (0 int8, 1 u8, 2 fp16), or -1.
 int quant_mode(int flags) {
-  const int f = flags & (OVB_AQ_U8 | OVB_AQ_F16);
-  if (f == (OVB_AQ_U8 | OVB_AQ_F16)) return -1;
-  return f == OVB_AQ_F16 ? 2 : (f == OVB_AQ_U8 ? 1 : 0);
+  const int f = flags & (OVB_AQ_U8 | OVB_AQ_F16 | OVB_AQ_F16_RAW);
+  switch (f) {
+    case 0: return 0;
+    case OVB_AQ_U8: return 1;
+    case OVB_AQ_F16: return 2;
+    case OVB_AQ_F16_RAW: return 3;
+    default: return -1;  // the forms are exclusive
+  }
 }
 
 int invalid(const std::string& msg) {
@@ -212,6 +219,7 @@ void free_weight(ovb_weight* w) {
 // Common checks of a pre-quantised GEMM call.  Returns OVB_OK or a status.
 int check_q_args(int64_t M, const ovb_weight* w, const int8_t* aq, const float* asc) {
   if (!w) return invalid("weight handle is null");
+  if (!w->w) return invalid("weight has no int8 image (made by ovb_weight_create_f32): use ovb_linear_h");
   if (!aq || !asc) return invalid("aq/asc must be non-null");
   if (!aligned(aq, 16)) return invalid("aq must be 16-byte aligned (TMA source)");
   if (!aligned(asc, 4)) return invalid("asc must be 4-byte aligned");
@@ -342,7 +350,8 @@ int check_silu_out(const ovb_weight* w, void* out, float* out_asc, int flags, in
   if (w->glu_inter <= 0) return invalid("the fused SiLU*up GEMM needs a gate|up weight (ovb_weight_gate_up)");
   if (!out || !out_asc) return invalid("out/out_asc must be non-null");
   *mode = quant_mode(flags);
-  if (*mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
+  if (*mode < 0) return invalid("OVB_AQ_U8, OVB_AQ_F16 and OVB_AQ_F16_RAW are exclusive");
+  if (*mode == 3) return invalid("the fused SiLU*up GEMM writes quantised activations (no OVB_AQ_F16_RAW)");
   if (!aligned(out, 16) || !aligned(out_asc, 4)) return invalid("misaligned output buffer");
   return OVB_OK;
 }
@@ -439,6 +448,65 @@ int ovb_weight_create(const int8_t* W, int layout, int64_t N, int64_t K, const f
   if (!on_device && src_dev) cudaFree(src_dev);
   if (ok) ok = ensure_weight_tmap(w);
   if (ok && (flags & OVB_WEIGHT_F16)) ok = make_weight_f16(w, s);
+  if (!ok) {
+    free_weight(w);
+    return OVB_ERR_INTERNAL;
+  }
+  *out = w;
+  return OVB_OK;
+}
+
+int ovb_weight_create_f32(const float* W, int layout, int64_t N, int64_t K, void* stream,
+                          ovb_weight** out) {
+  if (!out) return invalid("out is null");
+  *out = nullptr;
+  if (N <= 0 || K <= 0) return invalid("weight shape must be positive");
+  if (!W) return invalid("W must be non-null");
+  if (layout != OVB_LAYOUT_NK && layout != OVB_LAYOUT_KN) return invalid("unknown layout");
+  if (N > (int64_t{1} << 31) - 1 || K > (int64_t{1} << 30))
+    return invalid("weight dimensions too large");
+  const int64_t Kb = kblocks(K), Kp = Kb * 32;
+  // Per output channel n: a power-of-two scale s[n] = 2^(e - 10), e the
+  // exponent of max_k |W[n, k]|, so that W / s is exact in fp32 and lies
+  // below 2048 in magnitude (well inside fp16), then one rounding to fp16.
+  // The GEMM's epilogue multiplies by s[n] again (exact).
+  std::vector<float> sc(static_cast<size_t>(N));
+  std::vector<__half> h(static_cast<size_t>(N * Kp), __float2half_rn(0.f));
+  auto at = [&](int64_t n, int64_t k) {
+    return layout == OVB_LAYOUT_NK ? W[n * K + k] : W[k * N + n];
+  };
+  for (int64_t n = 0; n < N; ++n) {
+    float amax = 0.f;
+    for (int64_t k = 0; k < K; ++k) {
+      const float v = at(n, k);
+      if (!std::isfinite(v)) return invalid("ovb_weight_create_f32: non-finite weight");
+      amax = std::fmax(amax, std::fabs(v));
+    }
+    const float s_n = amax > 0.f ? std::ldexp(1.f, std::ilogb(amax) - 10) : 1.f;
+    sc[static_cast<size_t>(n)] = s_n;
+    const float inv = 1.f / s_n;  // a power of two: exact
+    for (int64_t k = 0; k < K; ++k) h[static_cast<size_t>(n * Kp + k)] = __float2half_rn(at(n, k) * inv);
+  }
+  cudaStream_t s = as_stream(stream);
+  auto* w = new ovb_weight();
+  if (cuda_failed(cudaGetDevice(&w->device), "cudaGetDevice")) {
+    delete w;
+    return OVB_ERR_INTERNAL;
+  }
+  w->N = N;
+  w->K = K;
+  w->Kb = Kb;
+  w->Kp = Kp;
+  const size_t hbytes = h.size() * sizeof(__half), sbytes = sc.size() * sizeof(float);
+  bool ok = !cuda_failed(cudaMalloc(&w->w16, hbytes), "cudaMalloc(fp16 weight)") &&
+            !cuda_failed(cudaMalloc(&w->scale, sbytes), "cudaMalloc(scale)") &&
+            !cuda_failed(cudaMemcpyAsync(w->w16, h.data(), hbytes, cudaMemcpyHostToDevice, s),
+                         "copy fp16 weight") &&
+            !cuda_failed(cudaMemcpyAsync(w->scale, sc.data(), sbytes, cudaMemcpyHostToDevice, s),
+                         "copy scale") &&
+            !cuda_failed(cudaStreamSynchronize(s), "fp32 weight upload sync") &&
+            ensure_weight_tmap16(w);
+  if (ok) ovb::ensure_split_workspace(w->device);  // optional: split-K configs need it
   if (!ok) {
     free_weight(w);
     return OVB_ERR_INTERNAL;
@@ -558,6 +626,7 @@ int ovb_weight_concat(const ovb_weight* const* parts, int n_parts, void* stream,
   int64_t total = 0;
   for (int i = 0; i < n_parts; ++i) {
     if (!parts[i]) return invalid("null part");
+    if (!parts[i]->w) return invalid("concat: a part has no int8 image (ovb_weight_create_f32)");
     if (parts[i]->K != parts[0]->K) return invalid("concat: parts differ in K");
     if (parts[i]->device != parts[0]->device) return invalid("concat: parts on different devices");
     total += parts[i]->N;
@@ -599,6 +668,7 @@ int ovb_weight_gate_up(const ovb_weight* gate, const ovb_weight* up, void* strea
   if (!out) return invalid("out is null");
   *out = nullptr;
   if (!gate || !up) return invalid("gate/up handle is null");
+  if (!gate->w || !up->w) return invalid("gate_up: a part has no int8 image (ovb_weight_create_f32)");
   if (gate->N != up->N || gate->K != up->K) return invalid("gate_up: gate and up differ in shape");
   if (gate->N % 32 != 0) return invalid("gate_up: N must be a multiple of 32");
   if (gate->device != up->device) return invalid("gate_up: parts on different devices");
@@ -658,6 +728,7 @@ int ovb_weight_shape(const ovb_weight* w, int64_t* N, int64_t* K) {
 
 int ovb_weight_export(const ovb_weight* w, int8_t* W_nk, float* scale) {
   if (!w || !W_nk || !scale) return invalid("null argument");
+  if (!w->w) return invalid("weight has no int8 image (made by ovb_weight_create_f32)");
   if (cuda_failed(cudaMemcpy2D(W_nk, static_cast<size_t>(w->K), w->w, static_cast<size_t>(w->Kp),
                                static_cast<size_t>(w->K), static_cast<size_t>(w->N),
                                cudaMemcpyDeviceToHost),
@@ -673,11 +744,11 @@ int ovb_weight_export(const ovb_weight* w, int8_t* W_nk, float* scale) {
 int ovb_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq, float* asc,
                  int flags, void* stream) {
   if (M <= 0 || K <= 0) return OVB_OK;
-  if (!A || !aq || !asc) return invalid("A/aq/asc must be non-null");
-  if (lda < K) return invalid("lda < K");
   const int mode = quant_mode(flags);
-  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
-  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(A, 4))
+  if (mode < 0) return invalid("OVB_AQ_U8, OVB_AQ_F16 and OVB_AQ_F16_RAW are exclusive");
+  if (!A || !aq || (!asc && mode != 3)) return invalid("A/aq/asc must be non-null");
+  if (lda < K) return invalid("lda < K");
+  if (!aligned(aq, mode >= 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(A, 4))
     return invalid("misaligned buffer");
   if (cuda_failed(ovb::launch_quantize(M, K, A, lda, aq, asc, mode, as_stream(stream)),
                   "quantize launch"))
@@ -688,11 +759,11 @@ int ovb_quantize(int64_t M, int64_t K, const float* A, int64_t lda, void* aq, fl
 int ovb_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, const float* w, float eps,
                          void* aq, float* asc, int flags, void* stream) {
   if (rows <= 0 || cols <= 0) return OVB_OK;
-  if (!x || !w || !aq || !asc) return invalid("x/w/aq/asc must be non-null");
-  if (cols > 24 * 1024) return invalid("rmsnorm_quantize: cols > 24576 not supported");
   const int mode = quant_mode(flags);
-  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
-  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(x, 4) || !aligned(w, 4))
+  if (mode < 0) return invalid("OVB_AQ_U8, OVB_AQ_F16 and OVB_AQ_F16_RAW are exclusive");
+  if (!x || !w || !aq || (!asc && mode != 3)) return invalid("x/w/aq/asc must be non-null");
+  if (cols > 24 * 1024) return invalid("rmsnorm_quantize: cols > 24576 not supported");
+  if (!aligned(aq, mode >= 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(x, 4) || !aligned(w, 4))
     return invalid("misaligned buffer");
   if (cuda_failed(ovb::launch_rmsnorm_quantize(rows, cols, x, w, eps, aq, asc, mode,
                                                as_stream(stream)),
@@ -705,11 +776,11 @@ int ovb_silu_mul_quantize(int64_t M, int64_t K, const float* gate, int64_t ldg,
                           const float* up, int64_t ldu, void* aq, float* asc, int flags,
                           void* stream) {
   if (M <= 0 || K <= 0) return OVB_OK;
-  if (!gate || !up || !aq || !asc) return invalid("gate/up/aq/asc must be non-null");
-  if (ldg < K || ldu < K) return invalid("ldg/ldu < K");
   const int mode = quant_mode(flags);
-  if (mode < 0) return invalid("OVB_AQ_U8 and OVB_AQ_F16 are exclusive");
-  if (!aligned(aq, mode == 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(gate, 4) ||
+  if (mode < 0) return invalid("OVB_AQ_U8, OVB_AQ_F16 and OVB_AQ_F16_RAW are exclusive");
+  if (!gate || !up || !aq || (!asc && mode != 3)) return invalid("gate/up/aq/asc must be non-null");
+  if (ldg < K || ldu < K) return invalid("ldg/ldu < K");
+  if (!aligned(aq, mode >= 2 ? 16 : 8) || !aligned(asc, 4) || !aligned(gate, 4) ||
       !aligned(up, 4))
     return invalid("misaligned buffer");
   if (cuda_failed(ovb::launch_silu_mul_quantize(M, K, gate, ldg, up, ldu, aq, asc, mode,
@@ -817,6 +888,7 @@ int ovb_block_products(int64_t M, const ovb_weight* w, const int8_t* aq, int32_t
                        void* stream) {
   if (M <= 0) return OVB_OK;
   if (!w) return invalid("weight handle is null");
+  if (!w->w) return invalid("weight has no int8 image (made by ovb_weight_create_f32)");
   if (!aq || !P) return invalid("aq/P must be non-null");
   if (!aligned(aq, 16)) return invalid("aq must be 16-byte aligned (TMA source)");
   const ovb::SliceOut so{0, w->N, nullptr, w->N};

@@ -70,6 +70,7 @@ struct ovb_lm {
   };
   std::vector<Layer> layers;
   ovb_weight* heads = nullptr;
+  bool heads_f32 = false;  // the reference's default fp32 audio heads (ovb_weight_create_f32)
   const float* final_norm = nullptr;
   DevBuf norms, emb, offsets, inv_freq;
   ovb::EmbTable tok{}, aud{};
@@ -105,11 +106,18 @@ int emb_info(const ovb_ovw1* f, const char* name, int64_t cols, ovb_ovw1_tensor*
   return fail(std::string(name) + ": expected an fp32 or row-scaled int8 table");
 }
 
-int linear_nk(const ovb_ovw1* f, const std::string& name, int64_t* N, int64_t* K) {
+// Shape of a linear weight as make_linear reads it (mat.cpp:69-106): int8
+// with per-output-channel scales in either orientation, or -- when
+// `allow_f32` -- the fp32 encoding ([K, N], layout 1, or [N, K]).
+int linear_nk(const ovb_ovw1* f, const std::string& name, int64_t* N, int64_t* K,
+              bool allow_f32 = false, bool* is_f32 = nullptr) {
   ovb_ovw1_tensor t;
   if (ovb_ovw1_find(f, name.c_str(), &t) != OVB_OK) return OVB_ERR_INVALID_ARG;
-  if (t.ndim != 2 || t.dtype != 1 || t.quant != 1)
-    return fail(name + ": expected an int8 linear weight (the fp32 encodings are not on this path)");
+  const bool f32 = t.ndim == 2 && t.dtype == 0 && t.quant == 0;
+  if (is_f32) *is_f32 = f32;
+  if (!(t.ndim == 2 && t.dtype == 1 && t.quant == 1) && !(allow_f32 && f32))
+    return fail(name + (allow_f32 ? ": expected an int8 or fp32 linear weight"
+                                   : ": expected an int8 linear weight"));
   *N = t.layout == 1 ? t.dims[1] : t.dims[0];
   *K = t.layout == 1 ? t.dims[0] : t.dims[1];
   return OVB_OK;
@@ -155,7 +163,7 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
   m->vocab = tt.dims[0];
   if (ta.dims[0] % m->n_codebooks != 0) return fail("audio embedding rows mismatch");
   m->audio_vocab = static_cast<int>(ta.dims[0] / m->n_codebooks);
-  if ((rc = linear_nk(f, "audio_heads.weight", &N, &K)) != OVB_OK) return rc;
+  if ((rc = linear_nk(f, "audio_heads.weight", &N, &K, true, &m->heads_f32)) != OVB_OK) return rc;
   if (N != static_cast<int64_t>(m->n_codebooks) * m->audio_vocab || K != m->hidden)
     return fail("audio head shape mismatch");
   const int64_t H = m->hidden, QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
@@ -184,7 +192,7 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
       na.push_back(lname(i, p));
   for (int i = 0; i < L; ++i)
     for (const char* p : {"self_attn.o_proj.weight", "mlp.down_proj.weight"}) nb.push_back(lname(i, p));
-  nb.push_back("audio_heads.weight");
+  if (!m->heads_f32) nb.push_back("audio_heads.weight");
   auto cstrs = [](const std::vector<std::string>& v) {
     std::vector<const char*> c;
     for (const auto& x : v) c.push_back(x.c_str());
@@ -209,12 +217,26 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
     Ly.down = wb[static_cast<size_t>(i) * 2 + 1];
     wb[static_cast<size_t>(i) * 2] = wb[static_cast<size_t>(i) * 2 + 1] = nullptr;
   }
-  m->heads = wb.back();
-  wb.back() = nullptr;
+  if (!m->heads_f32) {
+    m->heads = wb.back();
+    wb.back() = nullptr;
+  }
   for (ovb_weight* w : wa) ovb_weight_destroy(w);
   for (ovb_weight* w : wb)
     if (w) ovb_weight_destroy(w);
   if (rc != OVB_OK) return rc;
+  if (m->heads_f32) {
+    // The reference's default checkpoint keeps the audio heads in fp32
+    // (tools/convert_weights.py:326-327), consumed by Mat::mul -> linear_f32
+    // (lm.cpp:449-451, mat.cpp:11-13): fp16 tensor-core GEMM on fp16
+    // activations (ovb_weight_create_f32, OVB_AQ_F16_RAW).
+    ovb_ovw1_tensor th;
+    if ((rc = ovb_ovw1_find(f, "audio_heads.weight", &th)) != OVB_OK) return rc;
+    rc = ovb_weight_create_f32(static_cast<const float*>(th.data), th.layout == 1 ? OVB_LAYOUT_KN
+                                                                                  : OVB_LAYOUT_NK,
+                               N, K, s, &m->heads);
+    if (rc != OVB_OK) return rc;
+  }
 
   // ---- norms (fp32), one device buffer: per layer in / post (H), q / k (D); final (H)
   const int64_t per = 2 * H + 2 * 128;
@@ -299,7 +321,8 @@ bool reserve(ovb_lm* m, int64_t rows, int64_t mask_elems) {
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
   const size_t ab = m->f16 ? 2 : 1;
   const size_t r = static_cast<size_t>(rows);
-  return m->x.grow(r * H * 4) && m->aq.grow(r * KM * ab) && m->asc.grow(r * (KM / 32) * 4) &&
+  return m->x.grow(r * H * 4) && m->aq.grow(r * std::max<int64_t>(KM * ab, H * 2)) &&
+         m->asc.grow(r * (KM / 32) * 4) &&
          m->q.grow(r * QD * 4) && m->k.grow(r * KVD * 4) && m->v.grow(r * KVD * 4) &&
          m->attn.grow(r * QD * 4) && m->qi.grow(r * m->inter * ab) &&
          m->asci.grow(r * (m->inter / 32) * 4) && m->logits.grow(r * CV * 4) &&
@@ -351,9 +374,17 @@ int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_se
   }
   // final RMSNorm + the audio heads (rmsnorm_f32 + audio_heads_.mul, lm.cpp:446-447:
   // byte-identical to rmsnorm_quantize_f32 + linear_s8_nk_packed_q)
-  OVB_LM_TRY(ovb_rmsnorm_quantize(rows, H, x, m->final_norm, m->eps, aq, asc, qf, s));
-  OVB_LM_TRY(m->f16 ? ovb_linear_h(rows, m->heads, aq, m->logits.as<float>(), CV, 0, s)
-                    : ovb_linear_q(rows, m->heads, aq, asc, m->logits.as<float>(), CV, 0, s));
+  if (m->heads_f32) {
+    // rmsnorm_f32 + linear_f32 on fp32 heads: fp16 of the normalised rows
+    // (not quantised) times the fp16 heads, fp32 accumulation.
+    OVB_LM_TRY(ovb_rmsnorm_quantize(rows, H, x, m->final_norm, m->eps, aq, nullptr,
+                                    OVB_AQ_F16_RAW, s));
+    OVB_LM_TRY(ovb_linear_h(rows, m->heads, aq, m->logits.as<float>(), CV, 0, s));
+  } else {
+    OVB_LM_TRY(ovb_rmsnorm_quantize(rows, H, x, m->final_norm, m->eps, aq, asc, qf, s));
+    OVB_LM_TRY(m->f16 ? ovb_linear_h(rows, m->heads, aq, m->logits.as<float>(), CV, 0, s)
+                      : ovb_linear_q(rows, m->heads, aq, asc, m->logits.as<float>(), CV, 0, s));
+  }
 #undef OVB_LM_TRY
   m->last_rows = rows;
   return OVB_OK;
@@ -458,6 +489,42 @@ int ovb_lm_forward_cfg_device(ovb_lm* m, int cond_seq, int uncond_seq, const int
       {m->bias.as<float>(), cond_seq, 0, 0},
       {m->bias.as<float>() + cm, uncond_seq, int64_t(cond_seq) * QD, int64_t(cond_seq) * KVD}};
   return run(m, rows, static_cast<int>(rows), segs, 2, s);
+}
+
+int ovb_lm_forward_segments_device(ovb_lm* m, int n_segs, const int32_t* seg_rows,
+                                   const int64_t* ids, const uint8_t* audio_mask,
+                                   const uint8_t* masks, const int64_t* pos, void* stream) {
+  if (!m) return fail("model is null");
+  if (n_segs <= 0) return OVB_OK;
+  if (n_segs > ovb::kAttMaxSegs) return fail("at most 64 segments per forward");
+  if (!seg_rows || !ids || !audio_mask || !masks || !pos) return fail("null input");
+  int64_t rows = 0, mask_elems = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    if (seg_rows[i] <= 0) return fail("every segment must have at least one row");
+    rows += seg_rows[i];
+    mask_elems += int64_t(seg_rows[i]) * seg_rows[i];
+  }
+  if (rows > (int64_t{1} << 30)) return fail("too many rows");
+  DeviceScope d(m->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!reserve(m, rows, mask_elems)) return internal("cudaMalloc(forward buffers) failed");
+  const auto dd = cudaMemcpyDeviceToDevice;
+  if (cudaMemcpyAsync(m->ids.p, ids, rows * m->n_codebooks * 8, dd, s) != cudaSuccess ||
+      cudaMemcpyAsync(m->amask.p, audio_mask, rows, dd, s) != cudaSuccess ||
+      cudaMemcpyAsync(m->pos.p, pos, rows * 8, dd, s) != cudaSuccess ||
+      cudaMemcpyAsync(m->masks.p, masks, mask_elems, dd, s) != cudaSuccess ||
+      ovb::launch_mask_bias(m->masks.as<uint8_t>(), mask_elems, m->bias.as<float>(), s) !=
+          cudaSuccess)
+    return internal("input copies failed");
+  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
+  ovb_attn_segment segs[ovb::kAttMaxSegs];
+  int64_t r0 = 0, b0 = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    segs[i] = {m->bias.as<float>() + b0, seg_rows[i], r0 * QD, r0 * KVD};
+    r0 += seg_rows[i];
+    b0 += int64_t(seg_rows[i]) * seg_rows[i];
+  }
+  return run(m, rows, static_cast<int>(rows), segs, n_segs, s);
 }
 
 int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* ids,

@@ -3,7 +3,9 @@
 // Three producers, each writing asc (fp32 block scales) and aq in one of three
 // forms (`mode`): int8 q (0), the reference's u8 q+128 (1, OVB_AQ_U8), or the
 // dequantised activation fp16(q * asc) for the fp16 tensor-core mainloop (2,
-// OVB_AQ_F16; aq is then [M, Kp] fp16).  q and asc are bit-identical to the
+// OVB_AQ_F16; aq is then [M, Kp] fp16).  A fourth form (3, OVB_AQ_F16_RAW)
+// skips the quantisation: fp16 of the fp32 value itself, no asc, the input
+// of fp32 linear weights (ovb_weight_create_f32).  q and asc are bit-identical to the
 // reference CPU path:
 //   quantize_kernel          quantize_a_u8          gemm.cpp:379-430
 //   rmsnorm_quantize_kernel  rmsnorm_quantize_avx2  gemm.cpp:638-707
@@ -31,6 +33,7 @@ namespace {
 
 constexpr int kModeU8 = 1;
 constexpr int kModeF16 = 2;
+constexpr int kModeF16Raw = 3;  // fp16(a) itself, not quantised (asc not written)
 constexpr int kErrF16Range = 16;
 constexpr int kErrSelftest = 64;  // the wait self-test's deliberate timeout
 
@@ -67,7 +70,16 @@ __device__ __forceinline__ uint4 dequant8_f16(const float (&v)[8], int nv, float
 template <int kMode>
 __device__ __forceinline__ void store4(uint8_t* aq, int64_t idx, const float (&v)[4], int nv,
                                        float inv, float scale) {
-  if constexpr (kMode == kModeF16) {
+  if constexpr (kMode == kModeF16Raw) {
+    const __half2 h0 = __floats2half2_rn(nv > 0 ? v[0] : 0.f, nv > 1 ? v[1] : 0.f);
+    const __half2 h1 = __floats2half2_rn(nv > 2 ? v[2] : 0.f, nv > 3 ? v[3] : 0.f);
+    bool range_ok = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) range_ok = range_ok && !(i < nv && !(fabsf(v[i]) <= 65504.f));
+    if (!range_ok) atomicOr(&g_status_q, kErrF16Range);
+    *reinterpret_cast<uint2*>(aq + 2 * idx) = make_uint2(*reinterpret_cast<const uint32_t*>(&h0),
+                                                         *reinterpret_cast<const uint32_t*>(&h1));
+  } else if constexpr (kMode == kModeF16) {
     uint32_t w[2];
     bool range_ok = true;
 #pragma unroll
@@ -102,7 +114,12 @@ __device__ __forceinline__ void store4(uint8_t* aq, int64_t idx, const float (&v
 template <int kMode>
 __device__ __forceinline__ void store8(uint8_t* aq, int64_t idx, const float (&v)[8], int nv,
                                        float inv, float scale) {
-  if constexpr (kMode == kModeF16)
+  if constexpr (kMode == kModeF16Raw) {
+    const float lo[4] = {v[0], v[1], v[2], v[3]};
+    const float hi[4] = {v[4], v[5], v[6], v[7]};
+    store4<kModeF16Raw>(aq, idx, lo, nv < 4 ? nv : 4, inv, scale);
+    store4<kModeF16Raw>(aq, idx + 4, hi, nv > 4 ? nv - 4 : 0, inv, scale);
+  } else if constexpr (kMode == kModeF16)
     *reinterpret_cast<uint4*>(aq + 2 * idx) = dequant8_f16(v, nv, inv, scale);
   else
     *reinterpret_cast<uint2*>(aq + idx) = quant8(v, nv, inv, kMode == kModeU8);
@@ -154,7 +171,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(int64_t M, int64_t K, con
     block_scales(amax, &scale, &inv);
     if (valid) {
       store8<kMode>(aq, row * Kp + k, v, nv, inv, scale);
-      if (sub == 0) asc[row * Kb + b] = scale;
+      if (kMode != kModeF16Raw && sub == 0) asc[row * Kb + b] = scale;
     }
   }
 }
@@ -275,7 +292,7 @@ __global__ void __launch_bounds__(256) rmsnorm_quantize_kernel(int64_t rows, int
       float bs, inv;
       block_scales(amax, &bs, &inv);
       if (b < Kb) {
-        if (sub == 0) asc[r * Kb + b] = bs;
+        if (kMode != kModeF16Raw && sub == 0) asc[r * Kb + b] = bs;
         store4<kMode>(aq, r * Kp + k, v, nv, inv, bs);
       }
     }
@@ -364,7 +381,7 @@ __global__ void __launch_bounds__(kSmallThreads) rmsnorm_quantize_small_kernel(
       float bs, inv;
       block_scales(amax, &bs, &inv);
       if (b < Kb) {
-        if ((lane & 7) == 0) asc[r * Kb + b] = bs;
+        if (kMode != kModeF16Raw && (lane & 7) == 0) asc[r * Kb + b] = bs;
         store4<kMode>(aq, r * Kp + k, v, nv, inv, bs);
       }
     }
@@ -413,7 +430,7 @@ __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64
     block_scales(amax, &scale, &inv);
     if (valid) {
       store8<kMode>(aq, row * Kp + k, v, nv, inv, scale);
-      if (sub == 0) asc[row * Kb + b] = scale;
+      if (kMode != kModeF16Raw && sub == 0) asc[row * Kb + b] = scale;
     }
   }
 }
@@ -436,6 +453,7 @@ cudaError_t launch_quantize(int64_t M, int64_t K, const float* A, int64_t lda, v
   switch (mode) {
     case 0: return launch_plain(quantize_kernel<0>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
     case 1: return launch_plain(quantize_kernel<1>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
+    case 3: return launch_plain(quantize_kernel<3>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
     default: return launch_plain(quantize_kernel<2>, grid, dim3(256), 0, s, M, K, A, lda, q8, asc);
   }
 }
@@ -455,7 +473,7 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
     for (auto* k : {rmsnorm_quantize_kernel<0>, rmsnorm_quantize_kernel<1>,
-                    rmsnorm_quantize_kernel<2>}) {
+                    rmsnorm_quantize_kernel<2>, rmsnorm_quantize_kernel<3>}) {
       cudaError_t e =
           cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       if (e != cudaSuccess) return e;
@@ -475,6 +493,8 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
                                 0, s, rows, cols, x, w, eps, q8s, asc);
       case 1: return launch_plain(rmsnorm_quantize_small_kernel<1>, dim3(sgrid), dim3(kSmallThreads),
                                 0, s, rows, cols, x, w, eps, q8s, asc);
+      case 3: return launch_plain(rmsnorm_quantize_small_kernel<3>, dim3(sgrid), dim3(kSmallThreads),
+                                0, s, rows, cols, x, w, eps, q8s, asc);
       default: return launch_plain(rmsnorm_quantize_small_kernel<2>, dim3(sgrid),
                                  dim3(kSmallThreads), 0, s, rows, cols, x, w, eps, q8s, asc);
     }
@@ -484,6 +504,8 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
     case 0: return launch_plain(rmsnorm_quantize_kernel<0>, dim3(grid), dim3(warps * 32), smem, s,
                               rows, cols, x, w, eps, q8, asc);
     case 1: return launch_plain(rmsnorm_quantize_kernel<1>, dim3(grid), dim3(warps * 32), smem, s,
+                              rows, cols, x, w, eps, q8, asc);
+    case 3: return launch_plain(rmsnorm_quantize_kernel<3>, dim3(grid), dim3(warps * 32), smem, s,
                               rows, cols, x, w, eps, q8, asc);
     default: return launch_plain(rmsnorm_quantize_kernel<2>, dim3(grid), dim3(warps * 32), smem, s,
                                rows, cols, x, w, eps, q8, asc);
@@ -500,6 +522,8 @@ cudaError_t launch_silu_mul_quantize(int64_t M, int64_t K, const float* gate, in
     case 0: return launch_plain(silu_mul_quantize_kernel<0>, grid, dim3(256), 0, s, M, K, gate, ldg,
                               up, ldu, q8, asc);
     case 1: return launch_plain(silu_mul_quantize_kernel<1>, grid, dim3(256), 0, s, M, K, gate, ldg,
+                              up, ldu, q8, asc);
+    case 3: return launch_plain(silu_mul_quantize_kernel<3>, grid, dim3(256), 0, s, M, K, gate, ldg,
                               up, ldu, q8, asc);
     default: return launch_plain(silu_mul_quantize_kernel<2>, grid, dim3(256), 0, s, M, K, gate, ldg,
                                up, ldu, q8, asc);

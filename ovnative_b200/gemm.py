@@ -118,6 +118,24 @@ class Weight:
         return cls._create(W, scale, L.OVB_LAYOUT_KN, N, K, f16)
 
     @classmethod
+    def from_f32(cls, W, layout: int = 1) -> "Weight":
+        """An fp32 linear weight (ovb_weight_create_f32): the reference's fp32
+        encoding, layout 1 [K, N] (tools/convert_weights.py:178-180) or
+        layout 0 [N, K], held as fp16 with power-of-two channel scales.  Only
+        the fp16 mainloop (linear_h / linear_f32) takes it."""
+        Wn = np.ascontiguousarray(W.cpu().numpy() if isinstance(W, torch.Tensor) else W,
+                                  dtype=np.float32)
+        if Wn.ndim != 2:
+            raise ValueError("expected a 2-D weight")
+        N, K = (Wn.shape[1], Wn.shape[0]) if layout == L.OVB_LAYOUT_KN else Wn.shape
+        out = C.c_void_p()
+        L.check(L.lib().ovb_weight_create_f32(Wn.ctypes.data, layout, N, K, _stream(),
+                                              C.byref(out)))
+        w = cls(out.value, N, K, True)
+        w.fp32 = True
+        return w
+
+    @classmethod
     def concat(cls, parts: list["Weight"]) -> "Weight":
         """combine_packed (lm.cpp:57-94): q|k|v or gate|up along N."""
         arr = (C.c_void_p * len(parts))(*[p.handle for p in parts])
@@ -160,6 +178,31 @@ def _flags(u8: bool, f16: bool = False) -> int:
     if u8 and f16:
         raise ValueError("u8 and f16 outputs are exclusive")
     return (L.OVB_AQ_U8 if u8 else 0) | (L.OVB_AQ_F16 if f16 else 0)
+
+
+def to_f16(A: torch.Tensor, out=None) -> torch.Tensor:
+    """fp16 of A itself, [M, Kp] with a zero tail (OVB_AQ_F16_RAW): the
+    activations of an fp32 weight."""
+    _rows_ok(A, "A")
+    M, K = A.shape
+    a16 = out if out is not None else torch.empty((M, kblocks(K) * 32), dtype=torch.float16,
+                                                  device=A.device)
+    L.check(L.lib().ovb_quantize(M, K, _dev_ptr(A), A.stride(0), _dev_ptr(a16), None,
+                                 L.OVB_AQ_F16_RAW, _stream()))
+    return a16
+
+
+def rmsnorm_f16(x: torch.Tensor, w: torch.Tensor, eps: float, out=None) -> torch.Tensor:
+    """fp16 of rmsnorm_into_f32's output (ops_cpu.cpp:812-825; the same
+    values rmsnorm_quantize_f32 quantises), [M, Kp] with a zero tail."""
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    M, K = x.shape
+    a16 = out if out is not None else torch.empty((M, kblocks(K) * 32), dtype=torch.float16,
+                                                  device=x.device)
+    L.check(L.lib().ovb_rmsnorm_quantize(M, K, _dev_ptr(x), _dev_ptr(w.contiguous()), eps,
+                                         _dev_ptr(a16), None, L.OVB_AQ_F16_RAW, _stream()))
+    return a16
 
 
 def empty_quant_f16(M: int, K: int, device=None):
@@ -273,6 +316,14 @@ def linear_h_sliced(a16: torch.Tensor, w: Weight, Cs: list[torch.Tensor]):
     L.check(L.lib().ovb_linear_h_sliced(a16.shape[0], w.handle, _dev_ptr(a16), arr, len(Cs),
                                         _stream()))
     return Cs
+
+
+def linear_f32(A: torch.Tensor, w: Weight, C=None, accumulate: bool = False):
+    """ov::linear_f32 / linear_f32_ld with accumulate (Mat::mul / mul_add on
+    an fp32 weight, mat.cpp:11-13, :39-43) on the fp16 tensor cores: A to
+    fp16, then linear_h with a weight from Weight.from_f32."""
+    a16 = to_f16(A)
+    return linear_h(a16, w, C, accumulate)
 
 
 def _silu_out(M, w: Weight, device, u8, f16, out):

@@ -86,6 +86,21 @@ class LM:
         return _device_view(L.lib().ovb_lm_logits(self._h), cs + us, self.C * self.V)
 
 
+    def forward_segments_device(self, seg_rows, ids, amask, masks, pos) -> torch.Tensor:
+        """Several attention segments (e.g. the CFG pairs of several
+        utterances) in one forward on CUDA tensors, stream-ordered:
+        seg_rows a list of row counts, ids [C, rows] int64, amask [rows] u8,
+        masks the segments' [r, r] u8 masks concatenated (1-D), pos [rows]
+        int64.  Returns a view of the device logits [rows, C*V] (valid until
+        the next forward)."""
+        n = len(seg_rows)
+        arr = (C.c_int32 * max(n, 1))(*[int(r) for r in seg_rows])
+        L.check(L.lib().ovb_lm_forward_segments_device(
+            self._h, n, C.cast(arr, C.c_void_p), ids.data_ptr(), amask.data_ptr(),
+            masks.data_ptr(), pos.data_ptr(), torch.cuda.current_stream().cuda_stream))
+        return _device_view(L.lib().ovb_lm_logits(self._h), int(sum(seg_rows)), self.C * self.V)
+
+
 def _device_view(ptr: int, rows: int, cols: int) -> torch.Tensor:
     """A torch view of `rows x cols` fp32 device memory at `ptr` (no copy)."""
     class _Mem:

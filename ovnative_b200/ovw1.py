@@ -177,12 +177,15 @@ class OVW1File:
 
 def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden: int = 1024,
               n_heads: int = 16, n_kv: int = 8, inter: int = 3072, audio_vocab: int = 1025,
-              codebooks: int = 8) -> None:
+              codebooks: int = 8, heads_f32: bool = False) -> None:
     """A random-weight checkpoint of the reference LM's shape and tensor names
     (cpp/src/model/lm.cpp:96-141): int8 [N, K] linear weights with
     per-output-channel scales |N(0, 0.02)| / 127 (the --int8-layout nk
     encoding, audio heads int8 as well), int8 embedding tables with row
-    scales, RMSNorm gains 1 + N(0, 0.05), codebook offsets c * audio_vocab."""
+    scales, RMSNorm gains 1 + N(0, 0.05), codebook offsets c * audio_vocab.
+    ``heads_f32`` stores the audio heads as the reference's converter does
+    by default (tools/convert_weights.py:326-327: kept fp32, written
+    transposed [K, N] with layout 1, :178-180), values N(0, 0.02)."""
     rng = np.random.default_rng(seed)
     D = 128
 
@@ -199,7 +202,11 @@ def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden
     W, s = lin(codebooks * audio_vocab, hidden)
     ts.append(("audio_embeddings.weight", W, 0, (s * 40).astype(np.float32)))
     W, s = lin(codebooks * audio_vocab, hidden)
-    ts.append(("audio_heads.weight", W, 0, s))
+    if heads_f32:
+        Wf = (rng.standard_normal((codebooks * audio_vocab, hidden)) * 0.02).astype(np.float32)
+        ts.append(("audio_heads.weight", np.ascontiguousarray(Wf.T), 1, None))
+    else:
+        ts.append(("audio_heads.weight", W, 0, s))
     ts.append(("llm.norm.weight", gain(hidden), 0, None))
     ts.append(("codebook_layer_offsets",
                (np.arange(codebooks, dtype=np.int64) * audio_vocab), 0, None))

@@ -350,3 +350,56 @@ def test_linear_h_pair_sliced(cuda, golden, monkeypatch):
         for j, c in enumerate(Cs):
             check_tolerance(host(c), golden[f"sliced{i}_C{j}"])
     assert ovb.device_status() == 0
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("M,N,K", [(1, 64, 32), (77, 8200, 1024), (300, 1024, 1000)])
+def test_fp32_weight_linear_matches_fp64(cuda, layout, M, N, K):
+    """ovb_weight_create_f32 + OVB_AQ_F16_RAW + ovb_linear_h against the
+    reference's fp32 linear_f32 (C = A W, mat.cpp:11-13), computed here in
+    float64: fp16 operands and fp32 accumulation hold rel-L2 <= 1e-3 and
+    max-abs <= 1e-2 * rms (the path's tolerance)."""
+    rng = np.random.default_rng(M + N + K + layout)
+    Wnk = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    Wnk[N // 3] *= 1e-3  # a quiet channel keeps its precision (own scale)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    w = ovb.Weight.from_f32(Wnk if layout == 0 else np.ascontiguousarray(Wnk.T), layout=layout)
+    assert (w.N, w.K) == (N, K)
+    got = ovb.linear_f32(torch.from_numpy(A).to(cuda), w).cpu().numpy()
+    want = A.astype(np.float64) @ Wnk.astype(np.float64).T
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    rms = np.sqrt((want ** 2).mean())
+    assert err <= 1e-3, err
+    assert np.abs(got - want).max() <= 1e-2 * rms
+    q = want[:, N // 3]
+    assert np.linalg.norm(got[:, N // 3] - q) <= 1e-3 * np.linalg.norm(q)
+    # accumulate (linear_f32_ld with accumulate, Mat::mul_add, mat.cpp:39-43)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    Ct = torch.from_numpy(C0).to(cuda)
+    ovb.linear_f32(torch.from_numpy(A).to(cuda), w, Ct, accumulate=True)
+    got2 = Ct.cpu().numpy()
+    assert np.linalg.norm(got2 - (C0 + want)) <= 1e-3 * np.linalg.norm(C0 + want)
+    assert ovb.device_status() == 0
+    w.close()
+
+
+def test_raw_f16_forms(cuda):
+    """OVB_AQ_F16_RAW writes fp16 of the values themselves (zero K tail) from
+    ovb_quantize and of rmsnorm_into_f32's values from ovb_rmsnorm_quantize,
+    and the int8 entry points refuse an fp32-created weight."""
+    rng = np.random.default_rng(3)
+    A = (rng.standard_normal((37, 70)) * 3).astype(np.float32)
+    a16 = ovb.to_f16(torch.from_numpy(A).to(cuda)).cpu().numpy()
+    assert a16.shape == (37, 96)
+    np.testing.assert_array_equal(a16[:, :70], A.astype(np.float16))
+    assert not a16[:, 70:].any()
+    x = rng.standard_normal((20, 1024)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    h = ovb.rmsnorm_f16(torch.from_numpy(x).to(cuda), torch.from_numpy(g).to(cuda), 1e-6)
+    want = O.rmsnorm_into(x, g, 1e-6).astype(np.float16)
+    np.testing.assert_array_equal(h.cpu().numpy(), want)
+    w = ovb.Weight.from_f32(np.ones((64, 32), np.float32), layout=0)
+    aq, asc = ovb.s8_nk_quantize(torch.from_numpy(A[:, :32].copy()).to(cuda))
+    with pytest.raises(ValueError, match="no int8 image"):
+        ovb.linear_s8_nk_packed_q(aq, asc, w)
+    w.close()

@@ -65,8 +65,9 @@ def _create(path):
 
 def test_lm_create_rejects_bad_checkpoints(repo_tmp):
     """ovb_lm_create's checks run before any device call (so on the CPU):
-    a missing file, a file without layers, and fp32 audio heads (not on the
-    int8 path) are invalid arguments with a message."""
+    a missing file, a file without layers, and fp16 audio heads (neither the
+    int8 nor the fp32 encoding of a linear weight) are invalid arguments with
+    a message."""
     from ovnative_b200 import _lib as L
     rc, msg = _create(str(repo_tmp / "absent.ovw"))
     assert rc == L.OVB_ERR_INVALID_ARG and "cannot open" in msg
@@ -74,8 +75,7 @@ def test_lm_create_rejects_bad_checkpoints(repo_tmp):
     ovw1.write(p, [("llm.norm.weight", np.ones(1024, np.float32), 0, None)])
     rc, msg = _create(p)
     assert rc == L.OVB_ERR_INVALID_ARG and "llm.layers.0" in msg
-    # a one-layer checkpoint whose audio heads are fp32 [K, N] (the reference's
-    # default conversion)
+    # a one-layer checkpoint whose audio heads are fp16 [K, N]
     full = str(repo_tmp / "lm1.ovw")
     ovw1.random_lm(full, n_layers=1, vocab=64, seed=5)
     with ovw1.OVW1File(full) as f:
@@ -84,13 +84,31 @@ def test_lm_create_rejects_bad_checkpoints(repo_tmp):
             a = np.array(f.array(name))
             sc = f.scales(name)
             if name == "audio_heads.weight":
-                ts.append((name, np.zeros((1024, 8200), np.float32), 1, None))
+                ts.append((name, np.zeros((1024, 8200), np.float16), 1, None))
             else:
                 ts.append((name, a, f.info(name).layout, None if sc is None else np.array(sc)))
-    p = str(repo_tmp / "fp32_heads.ovw")
+    p = str(repo_tmp / "fp16_heads.ovw")
     ovw1.write(p, ts)
     rc, msg = _create(p)
     assert rc == L.OVB_ERR_INVALID_ARG and "audio_heads.weight" in msg
+    assert "int8 or fp32" in msg
+
+
+def test_reference_lm_runs_fp32_heads(repo_tmp):
+    """The reference's default conversion keeps the audio heads fp32 [K, N]
+    (tools/convert_weights.py:326-327); its LM loads such a file written by
+    random_lm(heads_f32=True) and runs them through linear_f32."""
+    p = str(repo_tmp / "lm1f.ovw")
+    ovw1.random_lm(p, n_layers=1, vocab=256, seed=4, heads_f32=True)
+    with ovw1.OVW1File(p) as f:
+        t = f.info("audio_heads.weight")
+        assert t.dtype == 0 and t.layout == 1 and t.dims[0] == 1024 and t.dims[1] == C * V
+    ref = O.RefLM(p, 1)
+    rng = np.random.default_rng(6)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 20, 12, 256)
+    logits = ref.forward_cfg(ids, amask, cond, unc, pos)
+    assert logits.shape == (32, C * V) and np.isfinite(logits).all() and logits.std() > 0.01
+    ref.close()
 
 
 def test_lm_entry_points_reject_null_model():
@@ -101,5 +119,7 @@ def test_lm_entry_points_reject_null_model():
     assert lib.ovb_lm_forward(None, 1, 4, None, None, None, None, None, None) == \
         L.OVB_ERR_INVALID_ARG
     assert lib.ovb_lm_reserve(None, 4, 16) == L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_lm_forward_segments_device(None, 1, None, None, None, None, None, None) == \
+        L.OVB_ERR_INVALID_ARG
     assert lib.ovb_lm_destroy(None) == L.OVB_OK
     assert lib.ovb_lm_logits(None) is None
