@@ -1,27 +1,31 @@
-"""Benchmark of the B200 int8 LM GEMM path.
+"""Benchmark of the B200-native int8 LM path of OVNative.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one pass of one Qwen3-0.6B-shaped decoder layer's int8 linear set
-(q/k/v, o, gate/up, down with their RMSNorm/SiLU quantisers) over one batch
-of M = 2 x 200 tokens (a CFG pair), the int8 branch of LM::run_layer
-(cpp/src/model/lm.cpp:217-322) without attention.  Consecutive steps walk
-through 28 distinct random-init layers (440 MB of int8 weights, > L2), as a
-forward pass does, so every step's weights come from HBM.
+Headline (every N): BASELINE config 4.  64 CFG-paired utterances, lengths
+uniform in [150, 800] tokens (seed 0), each a CFG pair of 2 x len rows (the
+B = 2 batch the reference's CUDA path builds, cpp/src/model/tts.cpp:172-204),
+are sharded over the N GPUs by longest-processing-time first (whole pairs per
+GPU, no collective on the data path).  A step is one TTS diffusion step of
+every utterance: the 28-layer Qwen3-0.6B-shaped LM forward of its CFG pair
+(random-init int8 weights, 151,676-token vocabulary, int8 audio heads) and
+the guided sampler on its logits.  Each GPU packs its pairs into forwards of
+at most 16,384 rows.  value = tokens (rows) of all utterances x K / the
+slowest rank's device time, in tokens/s; `scaling` is strong (the 64
+utterances are the whole job at every N).
 
-Metric: int8 tera-ops/s, ops = 2 * M * sum(N*K) = 12.58 G per step.  Under
-torchrun each rank runs the same per-GPU workload (utterance-parallel data
-parallelism: no data-path collective) and `value` is the whole-job total.
+With N = 1 the line also carries config 1 (one layer's linear set at
+M = 400, `layer_step`), configs 2 and 3 (`lm_forward`), the sampler, the
+attention and the weight loader, each with its own device timing, bound and
+the reference's CPU implementation timed beside it.
 
-Numerics (--numerics): `fp16` (default) runs the fp16 tensor-core mainloop
-(weights with OVB_WEIGHT_F16, quantisers writing fp16(q*asc), ovb_linear_h),
-whose outputs meet the contract's rel-L2 <= 1e-3 / max-abs <= 1e-2*rms;
-`exact` runs the int8 mainloop that reproduces the reference bit for bit.
-The line always carries the other path's number as well (key `exact` or
-`fp16`), measured over the same steps right after the timed region.
+Numerics (--numerics): `fp16` (default) runs the fp16 tensor-core mainloops
+(outputs within rel-L2 <= 1e-3 / max-abs <= 1e-2*rms of the reference);
+`exact` the int8 mainloop that reproduces the reference bit for bit.
 
-`--impl reference` times the reference's own CPU implementation of the same
-layer step (oracle/_ref, built from the reference's sources) on the host cores.
+`--impl reference` times the reference's own CPU implementation of the
+headline workload on the host cores (its LM forward, oracle/_ref, built from
+the reference's sources).
 """
 from __future__ import annotations
 
@@ -40,8 +44,21 @@ sys.path.insert(0, ROOT)
 
 M_TOKENS = 400
 N_LAYERS = 28
-METRIC = "int8 LM GEMM TOPS (one decoder layer's linear set, M=2x200)"
+LAYER_METRIC = "int8 LM GEMM TOPS (one decoder layer's linear set, M=2x200)"
 WORKLOAD = "config1: Qwen3-0.6B-shaped decoder layer linear set, int8, M=400"
+
+# BASELINE config 4, the headline at every N: 64 CFG-paired utterances,
+# lengths uniform in [150, 800] (seed 0), each a CFG pair of 2 x len rows,
+# sharded over the GPUs by LPT; a step is one TTS diffusion step of every
+# utterance (its LM forward + the guided sampler).
+UTT_N, UTT_LO, UTT_HI, UTT_SEED = 64, 150, 800, 0
+LM_LAYERS, LM_VOCAB = 28, 151676
+MAX_ROWS = 16384
+METRIC = ("LM forward tokens/s (config 4: 64 CFG-paired utterances, len U[150,800], "
+          "utterance-parallel)")
+UTT_WORKLOAD = ("config4: 64 CFG-paired utterances (2 x len rows each, len ~ U[150,800], seed "
+                "0), one TTS step = 28-layer Qwen3-0.6B-shaped LM forward + guided sampler per "
+                "utterance")
 
 
 def env_int(k, d):
@@ -59,7 +76,9 @@ def config(world: int) -> dict:
         "weights": "random int8 uniform[-127,127], scale |N(0,0.02)|/127, RMSNorm gains 1",
         "l2": "inputs larger than L2: each step reads a different layer's 15.7 MB of weights, "
               "28 layers = 440 MB",
-        "parallelism": f"dp{world} (utterance sharding, no collectives)",
+        "parallelism": ("dp1" if world == 1 else
+                        f"replicas x{world}: every GPU runs the same layer step (weak scaling of "
+                        "the layer microbenchmark, no collectives)"),
         "attention": "out of scope; o_proj consumes the q projection (identity stand-in)",
     }
 
@@ -252,33 +271,18 @@ class LayerPath:
             lw.close()
 
 
-def run_ours(args, rank: int, world: int, local_rank: int):
+def time_layer_step(args, dev, stream, world: int, barrier, max_over_ranks) -> dict:
+    """one decoder layer's linear set at M = 400 (a CFG
+    pair of 2 x 200 tokens), stepping through 28 layers' weights (L2-cold),
+    replayed from CUDA graphs.  Returns the entry with its live per-GEMM
+    roofline, the end-to-end pipelined step (host buffers in and out) and
+    the other numerics path over the same steps."""
     import torch
-    import torch.distributed as dist
 
     import ovnative_b200 as ovb
     from ovnative_b200 import layer as LY
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(ms: float) -> float:
-        if world == 1:
-            return ms
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     f16 = args.numerics == "fp16"
-    stream = torch.cuda.Stream(device=dev)
     path = LayerPath(f16, dev, stream)
     layers, buf, x0, x = path.layers, path.buf, path.x0, path.x
     graphs = path.graphs
@@ -288,17 +292,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         path.run_steps(args.warmup)
     torch.cuda.synchronize()
 
-    # ---- timed region: exactly K steps
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            path.run_steps(args.steps)
-            ev1.record(stream)
-        torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        path.run_steps(args.steps)
+        ev1.record(stream)
+    torch.cuda.synchronize()
     barrier()
     ms_max = max_over_ranks(ev0.elapsed_time(ev1))
     value = world * args.steps * ops_step / (ms_max * 1e-3) / 1e12
@@ -335,19 +337,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         ovb.rmsnorm_quantize_f32(x0, layers[0].post_ln, LY.RMS_EPS, out=buf.qh, f16=f16)
         ovb.s8_nk_quantize(buf.q, out=buf.qo, f16=f16)
         for name, (fn, N_g, K_g, res, ob) in gemms.items():
-            kg = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(kg, stream=stream):
-                for i in range(n_launch):
-                    fn(i % N_LAYERS)
-            kg.replay()  # warm
-            k0 = torch.cuda.Event(enable_timing=True)
-            k1 = torch.cuda.Event(enable_timing=True)
-            k0.record(stream)
-            kg.replay()
-            k1.record(stream)
-            k1.synchronize()
-            gemm_us = k0.elapsed_time(k1) * 1e3 / n_launch
-            kg.reset()
+            gemm_us = _graph_time_us(stream, lambda i, fn=fn: fn(i % N_LAYERS), n_launch)
             per_gemm.append(gemm_roofline(name, kern, M_TOKENS, N_g, K_g, res, ob, gemm_us, f16))
     torch.cuda.synchronize()
     roofline = dict(max(per_gemm, key=lambda r: r["us_per_launch"]))
@@ -395,12 +385,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(e0.elapsed_time(e1))
 
     e2e_serial_ms = timed_e2e(False)
     e2e_ms = timed_e2e(True)
@@ -412,18 +397,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "host-to-device copy and the previous step's device-to-host copy (two copy "
                    "streams, three buffers in rotation)",
            "serial_ms_per_step": e2e_serial_ms / args.steps}
-
     status = ovb.device_status()
     pipe.release()
     path.release()
-    sampler = time_sampler(dev, stream) if world == 1 else None
-    attention = time_attention(dev, stream) if world == 1 else None
-    weight_load = time_weight_load(dev) if world == 1 and not args.no_cpu_baseline else None
-    lm_forward = (time_lm_forward(dev, stream, f16) if world == 1 and not args.no_cpu_baseline
-                  else None)
-    status |= ovb.device_status()
 
-    # ---- the other numerics path over the same K steps (reported, not headline)
+    # ---- the other numerics path over the same K steps
     other_line = None
     if not args.skip_other:
         other = LayerPath(not f16, dev, stream)
@@ -445,50 +423,45 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         other_line = {"value": world * args.steps * ops_step / (o_ms * 1e-3) / 1e12,
                       "unit": "TOPS", "ms_per_step": o_ms / args.steps,
                       "numerics": NUMERICS["exact" if f16 else "fp16"]}
-
-    if world > 1:
-        dist.destroy_process_group()
     if status != 0:
         raise RuntimeError(f"bounded device wait timed out (status {status})")
-
-    if rank != 0:
-        return None
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        import oracle.cpu_baseline as CB
-        r = CB.run(M=M_TOKENS, layers=4, budget_s=args.cpu_seconds)
-        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        if sampler is not None:
-            sampler["cpu_baseline"] = sampler_cpu_baseline()
-        if attention is not None:
-            attention["cpu_baseline"] = attention_cpu_baseline()
     return {
-        "metric": METRIC,
+        "metric": LAYER_METRIC,
         "value": value,
         "unit": "TOPS",
-        "n_gpus": world,
         "steps": args.steps,
-        "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
         "dtype": DTYPE[args.numerics],
         "numerics": NUMERICS[args.numerics],
-        "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
         "config": config(world),
-        "impl": "ours",
         ("exact" if f16 else "fp16"): other_line,
         "e2e": e2e,
         "gpu_launches": args.steps * LY.KERNELS_PER_LAYER,
         "roofline": roofline,
-        "cpu_baseline": cpu,
-        "sampler": sampler,
-        "attention": attention,
-        "weight_load": weight_load,
-        "lm_forward": lm_forward,
-        "clocks": clk.summary(),
     }
+
+
+def _graph_time_us(stream, fn, launches: int, warm: int = 3) -> float:
+    """Device microseconds per call of fn(i): `warm` eager calls, then
+    `launches` calls captured in one CUDA graph, replayed once untimed and
+    once between CUDA events on `stream`."""
+    import torch
+    with torch.cuda.stream(stream):
+        for i in range(warm):
+            fn(i)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(launches):
+                fn(i)
+        g.replay()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    g.reset()
+    return e0.elapsed_time(e1) * 1e3 / launches
 
 
 # ------------------------------------------------------ guided sampler
@@ -780,7 +753,7 @@ def _lm_inputs(rng, S, vocab, n_text=40):
 
 
 def time_lm_forward(dev, stream, f16: bool, layers: int = 28, vocab: int = 151676,
-                    reps: int = 8) -> dict:
+                    reps: int = 8, path: str | None = None, cpu: bool = True) -> dict:
     """LM forward tokens/s (cond + uncond rows per forward / time) at configs
     2 and 3 through ovb_lm: device-resident inputs, the forward captured in
     one CUDA graph, CUDA events around `reps` replays; e2e through
@@ -797,15 +770,16 @@ def time_lm_forward(dev, stream, f16: bool, layers: int = 28, vocab: int = 15167
     import ovnative_b200 as ovb
     from ovnative_b200 import lm as LM
     from ovnative_b200 import ovw1
-    d = tempfile.mkdtemp(prefix="ovb_lm_")
+    d = None if path else tempfile.mkdtemp(prefix="ovb_lm_")
     out = {"layers": layers, "numerics": "fp16" if f16 else "exact", "vocab": vocab,
            "data": "synthetic (random-init int8 weights and embeddings, random ids)"}
     try:
-        path = os.path.join(d, "lm.ovw")
-        ovw1.random_lm(path, n_layers=layers, vocab=vocab, seed=21)
+        if path is None:
+            path = os.path.join(d, "lm.ovw")
+            ovw1.random_lm(path, n_layers=layers, vocab=vocab, seed=21)
         m = LM.LM(path, f16=f16)
         rng = np.random.default_rng(22)
-        ref = O.RefLM(path, layers) if O.ref_available() else None
+        ref = O.RefLM(path, layers) if (cpu and O.ref_available()) else None
         for name, S in LM_CONFIGS.items():
             ids, amask, cond, unc, pos = _lm_inputs(rng, S, vocab)
             rows = 2 * S
@@ -853,7 +827,8 @@ def time_lm_forward(dev, stream, f16: bool, layers: int = 28, vocab: int = 15167
         if ref is not None:
             ref.close()
     finally:
-        shutil.rmtree(d, ignore_errors=True)
+        if d:
+            shutil.rmtree(d, ignore_errors=True)
     return out
 
 
@@ -979,32 +954,463 @@ def attention_cpu_baseline(budget_s: float = 1.0) -> dict:
             "sample": f"{n} (segment, head) units of {S} rows in {sec:.2f} s, scaled to {units}"}
 
 
-# ---------------------------------------------------------- reference arm
-def run_reference(args, rank: int, world: int):
+# ------------------------------------------------- config 4: utterances
+def utterance_lengths() -> dict:
+    """uid -> length of the 64 config-4 utterances (seed 0)."""
+    from ovnative_b200 import shard
+    return dict(enumerate(int(x) for x in shard.synthetic_utterances(UTT_N, UTT_LO, UTT_HI,
+                                                                      UTT_SEED)))
+
+
+def config_utt(world: int, lengths: dict) -> dict:
+    rows = sum(2 * v for v in lengths.values())
+    return {
+        "workload": UTT_WORKLOAD,
+        "utterances": len(lengths),
+        "rows_per_step": rows,
+        "lengths": f"U[{UTT_LO},{UTT_HI}] seed {UTT_SEED}, sum {sum(lengths.values())}",
+        "tts_step": "per utterance: LM forward of its B=2 CFG pair (cond = 40 text ids + "
+                    "len-40 masked frames, uncond = the target slice; cpp/src/model/tts.cpp:"
+                    "172-204) + guided sampler (guidance 2.0, layer_penalty 5.0)",
+        "layers": LM_LAYERS, "vocab": LM_VOCAB, "audio_heads": "int8",
+        "batching": f"each GPU packs its CFG pairs into forwards of <= {MAX_ROWS} rows "
+                    "(attention segments stay per pair)",
+        "parallelism": f"dp{world}: utterance-parallel, LPT shards of whole CFG pairs, no "
+                       "collective on the data path",
+        "l2": "inputs larger than L2: every forward streams 449 MB of int8 weights (plus their "
+              "fp16 copy on the fp16 path) and the batch's activations",
+        "weights": "random-init int8, scale |N(0,0.02)|/127, RMSNorm gains 1 + N(0,0.05)",
+    }
+
+
+def shared_checkpoint(rank: int, world: int, dist=None) -> tuple[str, str]:
+    """A 28-layer random-init checkpoint of the reference LM's shape (OVW1,
+    151,676-token vocabulary, int8 heads), written once by rank 0 into a
+    temporary directory whose path the other ranks receive.  Returns
+    (path, directory)."""
+    import tempfile
+
+    from ovnative_b200 import ovw1
+    obj = [None, None]
+    if rank == 0:
+        d = tempfile.mkdtemp(prefix="ovb_lm_")
+        path = os.path.join(d, "lm28.ovw")
+        ovw1.random_lm(path, n_layers=LM_LAYERS, vocab=LM_VOCAB, seed=21)
+        obj = [path, d]
+    if world > 1:
+        dist.broadcast_object_list(obj, src=0)
+    return obj[0], obj[1]
+
+
+def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
+                         n_layers: int = 8) -> dict:
+    """Device time per launch of each GEMM and of the attention of a forward
+    over M packed rows with the given attention segments: the GEMMs on
+    random int8 weights of the LM's shapes rotating over `n_layers` layers
+    (> L2), the attention on the segments with a 0 / -1e30 padding bias,
+    each in a CUDA graph of launches between CUDA events.  Returns every
+    kernel's roofline entry with its share of a 28-layer forward (time x
+    launches per forward) and the dominant one."""
+    import torch
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import layer as LY
+    rng = np.random.default_rng(41)
+    H, QD, KVD, INTER = LY.HIDDEN, LY.QD, LY.KVD, LY.INTER
+    layers = [LY.LayerWeights.from_host(LY.random_layer_host(rng), dev, f16=f16)
+              for _ in range(n_layers)]
+    CV = 8 * 1025
+    heads = [ovb.Weight.from_nk(rng.integers(-127, 128, size=(CV, H), dtype=np.int8),
+                                (np.abs(rng.standard_normal(CV)) * 0.02 / 127).astype(np.float32),
+                                f16=f16) for _ in range(3)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(42)
+    x = torch.randn((M, H), device=dev, generator=gen)
+    q = torch.randn((M, QD), device=dev, generator=gen)
+    k = torch.randn((M, KVD), device=dev, generator=gen)
+    v = torch.randn((M, KVD), device=dev, generator=gen)
+    out = torch.empty_like(q)
+    logits = torch.empty((M, CV), device=dev)
+    qh = ovb.rmsnorm_quantize_f32(x, layers[0].input_ln, LY.RMS_EPS, f16=f16)
+    qo = ovb.s8_nk_quantize(q, f16=f16)
+    qi = ovb.linear_h_silu(qh[0], layers[0].gate_up) if f16 else \
+        ovb.linear_q_silu(*qh, layers[0].gate_up)
+    kern = "gemm_h (fp16 mainloop)" if f16 else "gemm_s8_tc (int8 mainloop)"
+    L_ = lambda i: layers[i % n_layers]  # noqa: E731
+    gemms = {
+        "qkv": ((lambda i: ovb.linear_h_sliced(qh[0], L_(i).qkv, [q, k, v])) if f16 else
+                (lambda i: ovb.linear_s8_nk_packed_q_sliced(*qh, L_(i).qkv, [q, k, v])),
+                QD + 2 * KVD, H, False, 4 * M * (QD + 2 * KVD), LM_LAYERS),
+        "o": ((lambda i: ovb.linear_h(qo[0], L_(i).o, x, accumulate=True)) if f16 else
+              (lambda i: ovb.linear_s8_nk_packed_q_add(*qo, L_(i).o, x)),
+              H, QD, True, 4 * M * H, LM_LAYERS),
+        "gate_up+silu": ((lambda i: ovb.linear_h_silu(qh[0], L_(i).gate_up, out=qi)) if f16 else
+                         (lambda i: ovb.linear_q_silu(*qh, L_(i).gate_up, out=qi)),
+                         2 * INTER, H, False, M * INTER * (2 if f16 else 1) + 4 * M * INTER // 32,
+                         LM_LAYERS),
+        "down": ((lambda i: ovb.linear_h(qi[0], L_(i).down, x, accumulate=True)) if f16 else
+                 (lambda i: ovb.linear_s8_nk_packed_q_add(*qi, L_(i).down, x)),
+                 H, INTER, True, 4 * M * H, LM_LAYERS),
+        "heads": ((lambda i: ovb.linear_h(qh[0], heads[i % 3], logits)) if f16 else
+                  (lambda i: ovb.linear_s8_nk_packed_q(*qh, heads[i % 3], logits)),
+                  CV, H, False, 4 * M * CV, 1),
+    }
+    entries = []
+    launches = 2 * n_layers
+    for name, (fn, N_g, K_g, res, ob, per_fwd) in gemms.items():
+        us = _graph_time_us(stream, fn, launches)
+        r = gemm_roofline(name, kern, M, N_g, K_g, res, ob, us, f16)
+        r["launches_per_forward"] = per_fwd
+        r["us_per_forward"] = round(us * per_fwd, 1)
+        r["traffic"] = None
+        entries.append(r)
+    # attention over the batch's segments (bias: the first 8 keys padded)
+    segs, r0 = [], 0
+    for rows in seg_rows:
+        bias = torch.zeros((rows, rows), device=dev)
+        bias[:, :min(8, rows - 1)] = -1e30
+        segs.append((bias, rows, r0 * QD, r0 * KVD))
+        r0 += rows
+    scale = 1.0 / float(np.sqrt(128))
+    us = _graph_time_us(stream, lambda i: ovb.attention(q, k, v, segs, 16, 8, scale, out=out),
+                        launches)
+    flops = sum(4 * r * r * 128 * 16 for r in seg_rows)
+    peaks = load_peaks()
+    ach = flops / (us * 1e-6) / 1e12
+    entries.append({"kernel": f"attention_kernel ({len(seg_rows)} segments, {M} rows)",
+                    "bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                    "peak_source": peaks["source"] + " bf16 burst",
+                    "algorithmic_flops": flops, "us_per_launch": round(us, 3),
+                    "roofline_us": round(flops / (peaks["bf16_tflops"] * 1e12) * 1e6, 3),
+                    "launches_per_forward": LM_LAYERS,
+                    "us_per_forward": round(us * LM_LAYERS, 1), "traffic": None})
+    for lw in layers:
+        lw.close()
+    for w in heads:
+        w.close()
+    if ovb.device_status() != 0:
+        raise RuntimeError("bounded device wait timed out in the kernel timings")
+    total = sum(e["us_per_forward"] for e in entries)
+    for e in entries:
+        e["share_of_timed_kernels"] = round(e["us_per_forward"] / total, 4)
+    dom = dict(max(entries, key=lambda e: e["us_per_forward"]))
+    dom["all_kernels"] = [{k: e[k] for k in ("kernel", "us_per_launch", "launches_per_forward",
+                                             "share_of_timed_kernels", "bound", "achieved",
+                                             "unit", "frac")} for e in entries]
+    return dom
+
+
+def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier,
+                    max_over_ranks, sum_over_ranks, gather) -> dict:
+    """The config-4 headline: this rank's LPT shard of the 64 utterances,
+    packed into forwards, K TTS steps timed on the device (CUDA events on the
+    launching stream, max over ranks), then the same K steps end to end (ids
+    in from pinned host memory, predictions and scores back every step)."""
+    import torch
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import lm as LM
+    from ovnative_b200 import shard
+    from ovnative_b200 import tts_batch as TB
+    f16 = args.numerics == "fp16"
+    lengths = utterance_lengths()
+    plan = shard.lpt_assign([lengths[i] for i in range(len(lengths))], world)
+    m = LM.LM(path, f16=f16)
+    sp = TB.Stepper(m, lengths, plan[rank], dev, stream, max_rows=MAX_ROWS, seed=rank)
+    sp.warm_and_capture()
+    for _ in range(args.warmup):
+        sp.step()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            sp.step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    my_ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(my_ms)
+    rank_ms = gather(my_ms)
+    rank_rows = gather(float(sp.rows_per_step))
+    total_rows = sum(2 * v for v in lengths.values())
+    value = args.steps * total_rows / (ms_max * 1e-3)
+
+    # end to end: the same steps with host ids in and host predictions out
+    for _ in range(2):
+        sp.step_e2e()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        sp.step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    h2d = int(sum_over_ranks(float(sp.h2d_bytes_per_step())))
+    d2h = int(sum_over_ranks(float(sp.d2h_bytes_per_step())))
+    launches = int(sum_over_ranks(float(sum(256 + len(b.pairs) for b in sp.batches))))
+    status = ovb.device_status()
+    biggest = max(sp.batches, key=lambda b: b.rows) if sp.batches else None
+    batches = [{"rows": b.rows, "pairs": len(b.pairs)} for b in sp.batches]
+    sp.release()
+    m.close()
+    if status != 0:
+        raise RuntimeError(f"bounded device wait timed out (status {status})")
+    roofline = None
+    if rank == 0 and biggest is not None and not args.no_roofline:
+        roofline = time_forward_kernels(dev, stream, f16, biggest.rows, biggest.seg_rows)
+    mean_ms = sum(rank_ms) / len(rank_ms)
+    return {
+        "value": value,
+        "ms_per_step": ms_max / args.steps,
+        "e2e": {"value": args.steps * total_rows / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms / args.steps,
+                "mode": "every step, per batch: ids [C, rows] int64 copied in from pinned host "
+                        "memory, the batch's CUDA graph (forward + samplers), predictions and "
+                        "scores copied back to pinned host memory; a host synchronisation "
+                        "ends the step"},
+        "gpu_launches": launches * args.steps,
+        "roofline": roofline,
+        "ranks": {"device_ms": [round(x, 3) for x in rank_ms],
+                  "rows_per_step": [int(x) for x in rank_rows],
+                  "load_imbalance": round(max(rank_ms) / mean_ms, 4) if mean_ms > 0 else None,
+                  "rank0_batches": batches},
+        "clocks": clk.summary(),
+        "config": config_utt(world, lengths),
+    }
+
+
+def utterance_cpu_baseline(path: str, budget_s: float, max_forwards: int = 1 << 30,
+                           warmup: int = 1) -> dict:
+    """The reference's own LM forward (LM::forward, B = 2 -- the CUDA path's
+    CFG batch, cpp/src/model/tts.cpp:260-266 -- AVX-VNNI int8, OpenMP on all
+    host cores, oracle/_ref) on a bounded sample of the config-4 utterances:
+    one forward per utterance in id order after `warmup` untimed ones, until
+    `budget_s` or `max_forwards`.  tokens/s = rows (2 x len) / time.  The
+    sampler pass is not timed here (the reference's loop for it lives inside
+    a Pipeline method; ~1 % of a CPU step)."""
+    import oracle as O
+    import oracle.cpu_baseline as CB
+    from ovnative_b200 import tts_batch as TB
+    if not O.ref_available():
+        return {"unavailable": "oracle/_ref is not built"}
+    lengths = utterance_lengths()
+    rng = np.random.default_rng(3)
+    ref = O.RefLM(path, LM_LAYERS)
+    C = 8
+
+    def b2(S):
+        ids, amask, cond, unc, pos = TB.cfg_pair_inputs(rng, S, C)
+        return (np.ascontiguousarray(ids.reshape(C, 2, S).transpose(1, 0, 2)),
+                amask.reshape(2, S), np.stack([cond, unc]), pos.reshape(2, S))
+
+    for u in range(warmup):
+        ref.forward(*b2(lengths[u]))
+    n, rows, t0 = 0, 0, time.perf_counter()
+    u = warmup
+    while n < max_forwards and (n == 0 or time.perf_counter() - t0 < budget_s):
+        S = lengths[u % len(lengths)]
+        ref.forward(*b2(S))
+        rows += 2 * S
+        n += 1
+        u += 1
+    sec = time.perf_counter() - t0
+    ref.close()
+    mode, kind = CB.pick_mode()
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": rows / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{n} utterance forwards ({rows} rows, config-4 lengths in id order) in "
+                      f"{sec:.1f} s: LM::forward B=2 (reference {mode} int8 path, OpenMP), "
+                      "guided sampler not timed",
+            "forwards": n, "seconds": sec, "host": CB.host_cpu()}
+
+
+# --------------------------------------------------------------- our arm
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import shutil
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def reduce(x: float, op) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max_over_ranks(ms: float) -> float:
+        return reduce(ms, dist.ReduceOp.MAX if world > 1 else None)
+
+    def sum_over_ranks(x: float) -> float:
+        return reduce(x, dist.ReduceOp.SUM if world > 1 else None)
+
+    def gather(x: float) -> list:
+        if world == 1:
+            return [x]
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = x
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return [float(v) for v in t.tolist()]
+
+    stream = torch.cuda.Stream(device=dev)
+    f16 = args.numerics == "fp16"
+    if args.workload == "layer":
+        with ClockSampler(local_rank) as clk:
+            out = time_layer_step(args, dev, stream, world, barrier, max_over_ranks)
+        if world > 1:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            import oracle.cpu_baseline as CB
+            r = CB.run(M=M_TOKENS, layers=4, budget_s=args.cpu_seconds)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "host")}
+        out.update({"n_gpus": world, "warmup": args.warmup, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "impl": "ours",
+                    "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
+                    "cpu_baseline": cpu, "clocks": clk.summary()})
+        return out
+
+    path, tmpdir = shared_checkpoint(rank, world, dist if world > 1 else None)
+    try:
+        head = time_utterances(args, rank, world, dev, stream, path, barrier, max_over_ranks,
+                               sum_over_ranks, gather)
+        extras = {}
+        if world == 1 and not args.headline_only:
+            import ovnative_b200 as ovb
+            # config 1's layer step is ~55 us: time 2800 of them (100 passes over
+            # the 28 layers' weights) after 280 warm-up steps
+            largs = argparse.Namespace(**{**vars(args), "steps": 2800, "warmup": 280})
+            extras["layer_step"] = time_layer_step(largs, dev, stream, world, barrier,
+                                                   max_over_ranks)
+            extras["sampler"] = time_sampler(dev, stream)
+            extras["attention"] = time_attention(dev, stream)
+            if not args.no_cpu_baseline:
+                extras["weight_load"] = time_weight_load(dev)
+            extras["lm_forward"] = time_lm_forward(dev, stream, f16, path=path,
+                                                   cpu=not args.no_cpu_baseline)
+            if ovb.device_status() != 0:
+                raise RuntimeError("bounded device wait timed out in the extra entries")
+        barrier()
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            cpu = utterance_cpu_baseline(path, args.cpu_seconds)
+            if "layer_step" in extras:
+                import oracle.cpu_baseline as CB
+                r = CB.run(M=M_TOKENS, layers=4, budget_s=min(args.cpu_seconds, 5.0))
+                extras["layer_step"]["cpu_baseline"] = {
+                    k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "host")}
+            if "sampler" in extras:
+                extras["sampler"]["cpu_baseline"] = sampler_cpu_baseline()
+            if "attention" in extras:
+                extras["attention"]["cpu_baseline"] = attention_cpu_baseline()
+    finally:
+        if rank == 0 and tmpdir:
+            shutil.rmtree(tmpdir, ignore_errors=True)
+    if world > 1:
+        dist.destroy_process_group()
     if rank != 0:
         return None
-    import oracle.cpu_baseline as CB
-    # Bounded sample: at most K steps, at most ~budget seconds of CPU time.
-    r = CB.run(M=M_TOKENS, layers=4, max_steps=args.steps, budget_s=args.ref_seconds,
-               warmup=min(args.warmup, 3))
+    line = {
+        "metric": METRIC,
+        "value": head["value"],
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": DTYPE[args.numerics],
+        "numerics": NUMERICS[args.numerics],
+        "data": "synthetic (seeded random-init int8 weights and embeddings, random text ids, "
+                "masked target frames)",
+        "config": head["config"],
+        "impl": "ours",
+        "e2e": head["e2e"],
+        "gpu_launches": head["gpu_launches"],
+        "roofline": head["roofline"],
+        "cpu_baseline": cpu,
+        "ranks": head["ranks"],
+        "clocks": head["clocks"],
+    }
+    line.update(extras)
+    return line
+
+
+# ---------------------------------------------------------- reference arm
+def run_reference(args, rank: int, world: int):
+    """The reference's own CPU implementation of the headline workload on
+    the host cores (oracle/_ref: its LM forward), rank 0 only: after one
+    untimed forward, one utterance forward per step, at most --steps of them
+    and at most --ref-seconds, on the config-4 checkpoint and lengths."""
+    if rank != 0:
+        return None
+    import shutil
+    if args.workload == "layer":
+        import oracle.cpu_baseline as CB
+        r = CB.run(M=M_TOKENS, layers=4, max_steps=args.steps, budget_s=args.ref_seconds,
+                   warmup=min(args.warmup, 3))
+        return {
+            "metric": LAYER_METRIC, "value": r["value"], "unit": "TOPS", "n_gpus": world,
+            "steps": r["steps"], "warmup": min(args.warmup, 3),
+            "ms_per_step": r["seconds"] * 1e3 / max(r["steps"], 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (u8 x s8 VNNI per 32-k block, fp32 epilogue)",
+            "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
+            "config": config(world), "impl": "reference",
+            "cpu_baseline": {"value": r["value"], "unit": "TOPS", "cores": r["cores"],
+                             "kind": r["kind"], "sample": r["sample"], "host": r["host"]},
+            "e2e": {"value": r["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+    path, tmpdir = shared_checkpoint(0, 1)
+    try:
+        r = utterance_cpu_baseline(path, args.ref_seconds, max_forwards=args.steps, warmup=1)
+    finally:
+        shutil.rmtree(tmpdir, ignore_errors=True)
+    if "unavailable" in r:
+        return {"impl": "reference", "unavailable": r["unavailable"]}
     return {
         "metric": METRIC,
         "value": r["value"],
-        "unit": "TOPS",
+        "unit": "tokens/s",
         "n_gpus": world,
-        "steps": r["steps"],
-        "warmup": min(args.warmup, 3),
-        "ms_per_step": r["seconds"] * 1e3 / max(r["steps"], 1),
+        "steps": r["forwards"],
+        "warmup": 1,
+        "ms_per_step": r["seconds"] * 1e3 / max(r["forwards"], 1),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8 (u8 x s8 VNNI per 32-k block, fp32 epilogue)",
-        "data": "synthetic (seeded random-init int8 weights and N(0,1) activations)",
-        "config": config(world),
+        "data": "synthetic (seeded random-init int8 weights and embeddings, random text ids, "
+                "masked target frames)",
+        "config": config_utt(world, utterance_lengths()),
         "impl": "reference",
-        "cpu_baseline": {"value": r["value"], "unit": "TOPS", "cores": r["cores"],
-                         "kind": r["kind"], "sample": r["sample"]},
-        "e2e": {"value": r["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "host")},
+        "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
@@ -1012,15 +1418,23 @@ def run_reference(args, rank: int, world: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=28000)
-    ap.add_argument("--warmup", type=int, default=280)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["utterances", "layer"], default="utterances",
+                    help="utterances: BASELINE config 4 (the headline); layer: config 1's "
+                         "layer step as the headline (profiling)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="skip the N=1 extra entries (layer step, sampler, attention, loader, "
+                         "configs 2/3)")
+    ap.add_argument("--no-roofline", action="store_true",
+                    help="skip the per-kernel timings behind `roofline` (profiling runs)")
     ap.add_argument("--numerics", choices=["fp16", "exact"], default="fp16")
     ap.add_argument("--skip-other", action="store_true",
-                    help="do not time the other numerics path (for profiling runs)")
+                    help="do not time the other numerics path of the layer step")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="only time the isolated GEMM M-sweep of config 4 (both mainloops)")
     ap.add_argument("--lm-only", action="store_true",
@@ -1054,7 +1468,8 @@ def main():
         import torch
         dev = torch.device("cuda", 0)
         print(json.dumps(time_lm_forward(dev, torch.cuda.Stream(device=dev),
-                                         args.numerics == "fp16")), flush=True)
+                                         args.numerics == "fp16",
+                                         cpu=not args.no_cpu_baseline)), flush=True)
         return
     if args.load_only:
         import torch
