@@ -232,9 +232,10 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
     // activations (ovb_weight_create_f32, OVB_AQ_F16_RAW).
     ovb_ovw1_tensor th;
     if ((rc = ovb_ovw1_find(f, "audio_heads.weight", &th)) != OVB_OK) return rc;
-    rc = ovb_weight_create_f32(static_cast<const float*>(th.data), th.layout == 1 ? OVB_LAYOUT_KN
-                                                                                  : OVB_LAYOUT_NK,
-                               N, K, s, &m->heads);
+    const bool kn = th.layout == 1;
+    rc = ovb_weight_create_f32(static_cast<const float*>(th.data),
+                               kn ? OVB_LAYOUT_KN : OVB_LAYOUT_NK, kn ? th.dims[1] : th.dims[0],
+                               kn ? th.dims[0] : th.dims[1], s, &m->heads);
     if (rc != OVB_OK) return rc;
   }
 

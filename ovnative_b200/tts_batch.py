@@ -45,7 +45,7 @@ def target_len(S: int) -> int:
     return max(1, int(S) - N_TEXT)
 
 
-def cfg_pair_inputs(rng: np.random.Generator, S: int, C: int = 8):
+def cfg_pair_inputs(rng: np.random.Generator, S: int, C: int = 8, text_vocab: int = TEXT_VOCAB):
     """The B = 2 CFG inputs of one utterance as run_sampling builds them for
     the CUDA path (tts.cpp:172-204), as two packed segments of S rows:
     ids [C, 2S] (codebook-major), audio_mask [2S], the two [S, S] masks and
@@ -53,7 +53,7 @@ def cfg_pair_inputs(rng: np.random.Generator, S: int, C: int = 8):
     ids in every codebook row, then T = S - N_TEXT masked audio frames."""
     T = target_len(S)
     prompt = np.full((C, S), MASK_ID, np.int64)
-    prompt[:, :S - T] = rng.integers(0, TEXT_VOCAB, size=S - T)
+    prompt[:, :S - T] = rng.integers(0, min(text_vocab, TEXT_VOCAB), size=S - T)
     amask_p = np.zeros(S, np.uint8)
     amask_p[S - T:] = 1
     ids = np.full((C, 2 * S), MASK_ID, np.int64)
@@ -112,6 +112,7 @@ class Batch:
 
     def __init__(self, lm: LM, lengths: dict, uids: list, rng: np.random.Generator,
                  dev: torch.device):
+        text_vocab = lm.config["vocab"]
         C = lm.C
         self.lm = lm
         self.pairs, parts, r0, o0 = [], [], 0, 0
@@ -119,7 +120,7 @@ class Batch:
             S = int(lengths[u])
             T = target_len(S)
             self.pairs.append(_Pair(u, S, T, r0, o0))
-            parts.append(cfg_pair_inputs(rng, S, C))
+            parts.append(cfg_pair_inputs(rng, S, C, text_vocab))
             r0 += 2 * S
             o0 += C * T
         self.rows, self.n_out = r0, o0

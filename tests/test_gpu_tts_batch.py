@@ -25,7 +25,7 @@ from tests.test_gpu_sampler import second_gap
 
 pytestmark = pytest.mark.gpu
 
-LAYERS, VOCAB = 2, 512
+LAYERS, VOCAB = 2, 2048  # > the mask id 1024, which the uncond tail rows embed as a token
 LENGTHS = {0: 50, 1: 75, 2: 41, 3: 120, 4: 64}
 
 
