@@ -400,7 +400,8 @@ int ovb_lm_reserve(ovb_lm* m, int64_t rows, int64_t mask_elems);
 /* LM::forward_cfg (lm.cpp:403-454) on host buffers: input_ids [C, rows]
  * (rows = cond_seq + uncond_seq, codebook-major), audio_mask [rows],
  * cond_attn [cond_seq, cond_seq], uncond_attn [uncond_seq, uncond_seq],
- * position [rows]; logits [rows, C*V] token-major.  Synchronous. */
+ * position [rows]; logits [rows, C*V] token-major, or NULL to leave them on
+ * the device only (ovb_lm_logits).  Synchronous. */
 int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* ids,
                        const uint8_t* audio_mask, const uint8_t* cond_attn,
                        const uint8_t* uncond_attn, const int64_t* pos, float* logits,
@@ -430,9 +431,21 @@ int ovb_lm_forward_segments_device(ovb_lm* m, int n_segs, const int32_t* seg_row
                                    const uint8_t* masks, const int64_t* pos, void* stream);
 /* LM::forward (lm.cpp:343-401) with CudaForwardFn's arguments on host
  * buffers: input_ids [B, C, S], audio_mask [B, S], attn_mask [B, S, S],
- * position [B, S]; logits [B, C, S, V].  batch <= 64.  Synchronous. */
+ * position [B, S]; logits [B, C, S, V], or NULL to leave them on the device
+ * only, token-major [B * S, C * V] at ovb_lm_logits -- the reference runner's
+ * device-sampling mode (LmRunnerSetDeviceSampling, cuda_lm.h:48-50), whose
+ * CFG planes LM::sample_guided then reads (tts.cpp:270-282).  batch <= 64.
+ * Synchronous. */
 int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint8_t* audio_mask,
                    const uint8_t* attn_mask, const int64_t* pos, float* logits, void* stream);
+/* LM::CudaSampleFn (lm.h:101-108) on the model's device: ovb_guided_sample on
+ * the device planes cond / uncond (e.g. ovb_lm_logits and the plane after
+ * it), then pred and scores ([C, target_len], HOST arrays) copied back,
+ * synchronously; the device outputs are the model's own buffers.  The
+ * contract of the reference's LmRunnerSampleThunk (cuda_lm.cu:1227-1262). */
+int ovb_lm_sample(ovb_lm* m, const float* cond, int cond_seq, const float* uncond,
+                  int uncond_seq, int target_len, float guidance, float layer_penalty,
+                  int mask_id, int32_t* pred, float* scores, void* stream);
 
 #ifdef __cplusplus
 }

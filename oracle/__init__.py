@@ -9,6 +9,9 @@ Two checkers live here, both driven through ctypes with numpy arrays:
   compiled from source by oracle/Makefile.  Its int8 quantised path needs an
   AVX-VNNI host (cpu_vnni_available(), gemm.cpp:556-572); ``ref_vnni()`` says
   whether it can run here.
+* ``ref_cuda`` -- _ref/libovref_cuda.so, the reference's CUDA LM runner source
+  built for sm_100a, for its guided_sample_kernel (the GPU-side checker of
+  the device sampler; device pointers, needs a GPU).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
 this package.  The product (ovnative_b200) never does.
@@ -26,6 +29,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _PORT_PATH = os.path.join(_HERE, "liboracle.so")
 _REF_PATH = os.path.join(_HERE, "_ref", "libovref.so")
+_REF_CUDA_PATH = os.path.join(_HERE, "_ref", "libovref_cuda.so")
 
 _i64 = C.c_int64
 _p = C.c_void_p
@@ -482,3 +486,40 @@ def attention_layer(q: np.ndarray, k: np.ndarray, v: np.ndarray, segs, n_heads: 
                                        _ptr(rows), _ptr(qo), _ptr(ko), n),
          "attention loop of LM::run_layer")
     return out
+
+
+# ----------------------------------------------- reference CUDA sampler
+_ref_cuda = None
+
+
+def ref_cuda_available() -> bool:
+    return os.path.exists(_REF_CUDA_PATH)
+
+
+def ref_cuda_guided_sample(cond, uncond, T: int, C_books: int, guidance: float, penalty: float,
+                           mask_id: int = 1024):
+    """The reference's own CUDA guided_sample_kernel (cpp/src/backend/cuda/
+    cuda_lm.cu:679-758, launched as LmRunnerSampleThunk launches it) on
+    token-major torch CUDA planes cond [cond_seq, C*V] / uncond
+    [uncond_seq, C*V].  Returns (pred int32 [C, T], scores fp32 [C, T]) as
+    torch CUDA tensors, ordered on torch's current stream."""
+    import torch
+    global _ref_cuda
+    if _ref_cuda is None:
+        if not ref_cuda_available():
+            raise RuntimeError(f"reference CUDA library not built: {_REF_CUDA_PATH}")
+        lib = C.CDLL(_REF_CUDA_PATH)
+        lib.ref_cuda_guided_sample.argtypes = [_p, C.c_int, _p, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_float, C.c_float, C.c_int, _p, _p,
+                                               _p]
+        lib.ref_cuda_guided_sample.restype = C.c_int
+        _ref_cuda = lib
+    V = cond.shape[1] // C_books
+    pred = torch.empty((C_books, T), dtype=torch.int32, device=cond.device)
+    scores = torch.empty((C_books, T), dtype=torch.float32, device=cond.device)
+    rc = _ref_cuda.ref_cuda_guided_sample(cond.data_ptr(), cond.shape[0], uncond.data_ptr(),
+                                          uncond.shape[0], C_books, V, T, guidance, penalty,
+                                          mask_id, pred.data_ptr(), scores.data_ptr(),
+                                          torch.cuda.current_stream().cuda_stream)
+    _chk(rc, "guided_sample_kernel launch")
+    return pred, scores

@@ -102,6 +102,8 @@ SIGNATURES = {
     "ovb_lm_forward_segments_device": ([_p, _int, _p, _p, _p, _p, _p, _p], _int),
     "ovb_weight_create_f32": ([_p, _int, _i64, _i64, _p, C.POINTER(_p)], _int),
     "ovb_lm_forward": ([_p, _int, _int, _p, _p, _p, _p, _p, _p], _int),
+    "ovb_lm_sample": ([_p, _p, _int, _p, _int, _int, C.c_float, C.c_float, _int, _p, _p, _p],
+                      _int),
     "ovb_attention": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
                        C.POINTER(AttnSegment), _int, _p], _int),
 }

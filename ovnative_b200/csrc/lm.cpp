@@ -76,6 +76,7 @@ struct ovb_lm {
   ovb::EmbTable tok{}, aud{};
   // forward buffers (grown on demand)
   DevBuf x, aq, asc, q, k, v, attn, qi, asci, logits, logits_perm, ids, amask, pos, masks, bias;
+  DevBuf pred, scores;  // ovb_lm_sample's device outputs
   int64_t last_rows = 0;
 
   ~ovb_lm() {
@@ -534,7 +535,7 @@ int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* i
                        void* stream) {
   if (!m) return fail("model is null");
   if (cond_seq <= 0 || uncond_seq <= 0) return fail("forward_cfg: both segments must be non-empty");
-  if (!ids || !audio_mask || !cond_attn || !uncond_attn || !pos || !logits) return fail("null input");
+  if (!ids || !audio_mask || !cond_attn || !uncond_attn || !pos) return fail("null input");
   DeviceScope d(m->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows = int64_t(cond_seq) + uncond_seq;
@@ -555,7 +556,8 @@ int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* i
   int rc = run(m, rows, static_cast<int>(rows), segs, 2, s);
   if (rc != OVB_OK) return rc;
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
-  if (cudaMemcpyAsync(logits, m->logits.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+  if (logits &&
+      cudaMemcpyAsync(logits, m->logits.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
     return internal("logits copy failed");
   return finish(m, s);
 }
@@ -565,7 +567,7 @@ int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint
   if (!m) return fail("model is null");
   if (batch <= 0 || seq <= 0) return OVB_OK;
   if (batch > 64) return fail("batch must be <= 64");
-  if (!ids || !audio_mask || !attn_mask || !pos || !logits) return fail("null input");
+  if (!ids || !audio_mask || !attn_mask || !pos) return fail("null input");
   DeviceScope d(m->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows = int64_t(batch) * seq, mm = rows * seq;
@@ -586,11 +588,33 @@ int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint
                                     int64_t(b) * seq * QD, int64_t(b) * seq * KVD};
   int rc = run(m, rows, seq, segs.data(), batch, s);
   if (rc != OVB_OK) return rc;
-  if (ovb::launch_permute_logits(m->logits.as<float>(), m->logits_perm.as<float>(), batch, seq,
-                                 m->n_codebooks, m->audio_vocab, s) != cudaSuccess ||
-      cudaMemcpyAsync(logits, m->logits_perm.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) !=
-          cudaSuccess)
+  if (logits &&
+      (ovb::launch_permute_logits(m->logits.as<float>(), m->logits_perm.as<float>(), batch, seq,
+                                  m->n_codebooks, m->audio_vocab, s) != cudaSuccess ||
+       cudaMemcpyAsync(logits, m->logits_perm.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) !=
+           cudaSuccess))
     return internal("logits copy failed");
+  return finish(m, s);
+}
+
+int ovb_lm_sample(ovb_lm* m, const float* cond, int cond_seq, const float* uncond,
+                  int uncond_seq, int target_len, float guidance, float layer_penalty,
+                  int mask_id, int32_t* pred, float* scores, void* stream) {
+  if (!m) return fail("model is null");
+  if (target_len <= 0) return OVB_OK;
+  if (!pred || !scores) return fail("pred/scores must be non-null");
+  DeviceScope d(m->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t n = static_cast<size_t>(m->n_codebooks) * static_cast<size_t>(target_len);
+  if (!m->pred.grow(n * 4) || !m->scores.grow(n * 4))
+    return internal("cudaMalloc(sampler outputs) failed");
+  int rc = ovb_guided_sample(cond, cond_seq, uncond, uncond_seq, m->n_codebooks, m->audio_vocab,
+                             target_len, guidance, layer_penalty, mask_id, m->pred.as<int32_t>(),
+                             m->scores.as<float>(), stream);
+  if (rc != OVB_OK) return rc;
+  if (cudaMemcpyAsync(pred, m->pred.p, n * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyAsync(scores, m->scores.p, n * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return internal("sampler output copy failed");
   return finish(m, s);
 }
 
