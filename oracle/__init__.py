@@ -496,14 +496,7 @@ def ref_cuda_available() -> bool:
     return os.path.exists(_REF_CUDA_PATH)
 
 
-def ref_cuda_guided_sample(cond, uncond, T: int, C_books: int, guidance: float, penalty: float,
-                           mask_id: int = 1024):
-    """The reference's own CUDA guided_sample_kernel (cpp/src/backend/cuda/
-    cuda_lm.cu:679-758, launched as LmRunnerSampleThunk launches it) on
-    token-major torch CUDA planes cond [cond_seq, C*V] / uncond
-    [uncond_seq, C*V].  Returns (pred int32 [C, T], scores fp32 [C, T]) as
-    torch CUDA tensors, ordered on torch's current stream."""
-    import torch
+def _ref_cuda_lib():
     global _ref_cuda
     if _ref_cuda is None:
         if not ref_cuda_available():
@@ -513,11 +506,64 @@ def ref_cuda_guided_sample(cond, uncond, T: int, C_books: int, guidance: float, 
                                                C.c_int, C.c_float, C.c_float, C.c_int, _p, _p,
                                                _p]
         lib.ref_cuda_guided_sample.restype = C.c_int
+        lib.ref_cuda_lm_create.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_int]
+        lib.ref_cuda_lm_create.restype = _p
+        lib.ref_cuda_lm_destroy.argtypes = [_p]
+        lib.ref_cuda_lm_destroy.restype = None
+        lib.ref_cuda_lm_forward.argtypes = [_p, C.c_int, C.c_int, _p, _p, _p, _p, _p]
+        lib.ref_cuda_lm_forward.restype = C.c_int
         _ref_cuda = lib
+    return _ref_cuda
+
+
+class RefCudaLM:
+    """The reference's own CUDA LM runner (cpp/src/backend/cuda/cuda_lm.cu:
+    790-1221, built from its source into oracle/_ref) on an OVW1 file in the
+    [K, N] int8 encoding: LM::forward's arguments on host buffers."""
+
+    def __init__(self, path: str, n_layers: int):
+        self._h = None
+        err = C.create_string_buffer(512)
+        h = _ref_cuda_lib().ref_cuda_lm_create(path.encode(), n_layers, err, 512)
+        if not h:
+            raise RuntimeError(f"reference CUDA LM: {err.value.decode()}")
+        self._h = h
+        self.C, self.V = 8, 1025
+
+    def close(self):
+        if self._h:
+            _ref_cuda_lib().ref_cuda_lm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, ids, amask, attn, pos) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int64)
+        B, _, S = ids.shape
+        out = np.zeros((B, self.C, S, self.V), np.float32)
+        a = np.ascontiguousarray(amask, np.uint8)
+        m = np.ascontiguousarray(attn, np.uint8)
+        pos = np.ascontiguousarray(pos, np.int64)
+        rc = _ref_cuda_lib().ref_cuda_lm_forward(self._h, B, S, _ptr(ids), _ptr(a), _ptr(m),
+                                                 _ptr(pos), _ptr(out))
+        _chk(rc, "LmRunner::forward")
+        return out
+
+
+def ref_cuda_guided_sample(cond, uncond, T: int, C_books: int, guidance: float, penalty: float,
+                           mask_id: int = 1024):
+    """The reference's own CUDA guided_sample_kernel (cpp/src/backend/cuda/
+    cuda_lm.cu:679-758, launched as LmRunnerSampleThunk launches it) on
+    token-major torch CUDA planes cond [cond_seq, C*V] / uncond
+    [uncond_seq, C*V].  Returns (pred int32 [C, T], scores fp32 [C, T]) as
+    torch CUDA tensors, ordered on torch's current stream."""
+    import torch
+    lib = _ref_cuda_lib()
     V = cond.shape[1] // C_books
     pred = torch.empty((C_books, T), dtype=torch.int32, device=cond.device)
     scores = torch.empty((C_books, T), dtype=torch.float32, device=cond.device)
-    rc = _ref_cuda.ref_cuda_guided_sample(cond.data_ptr(), cond.shape[0], uncond.data_ptr(),
+    rc = lib.ref_cuda_guided_sample(cond.data_ptr(), cond.shape[0], uncond.data_ptr(),
                                           uncond.shape[0], C_books, V, T, guidance, penalty,
                                           mask_id, pred.data_ptr(), scores.data_ptr(),
                                           torch.cuda.current_stream().cuda_stream)

@@ -32,3 +32,55 @@ extern "C" int ref_cuda_guided_sample(const float* cond, int cond_seq, const flo
       mask_id, pred, scores);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
+
+// The reference's own CUDA LM forward (LmRunner, cuda_lm.cu:790-1221: fp16
+// cublasGemmEx on weights dequantised at load, TF32 attention from 160
+// tokens) for the end-to-end parity tests: how far the reference's GPU path
+// itself sits from its CPU path on the same checkpoint.  The file must use the
+// [K, N] int8 encoding (lm.h:60-63).
+namespace {
+struct RefCudaLm {
+  ov::WeightFile wf;
+  ov::cuda::LmRunnerPtr runner{nullptr, &ov::cuda::LmRunnerDelete};
+};
+
+void put_err(const char* msg, char* err, int err_len) {
+  if (err && err_len > 0) {
+    std::strncpy(err, msg, static_cast<size_t>(err_len) - 1);
+    err[err_len - 1] = 0;
+  }
+}
+}  // namespace
+
+extern "C" void* ref_cuda_lm_create(const char* path, int n_layers, char* err, int err_len) {
+  try {
+    auto r = std::make_unique<RefCudaLm>();
+    r->wf = ov::WeightFile::Open(path);
+    ov::LMConfig cfg;
+    cfg.n_layers = n_layers;
+    r->runner = ov::cuda::LmRunnerCreate(r->wf, cfg);
+    if (!r->runner) {
+      put_err("LmRunnerCreate failed", err, err_len);
+      return nullptr;
+    }
+    return r.release();
+  } catch (const std::exception& e) {
+    put_err(e.what(), err, err_len);
+    return nullptr;
+  }
+}
+
+extern "C" void ref_cuda_lm_destroy(void* h) { delete static_cast<RefCudaLm*>(h); }
+
+// LmRunner::forward with LM::forward's arguments (host buffers, synchronous).
+extern "C" int ref_cuda_lm_forward(void* h, int batch, int seq, const int64_t* ids,
+                                   const uint8_t* amask, const uint8_t* attn, const int64_t* pos,
+                                   float* logits) {
+  try {
+    ov::cuda::LmRunnerForward(*static_cast<RefCudaLm*>(h)->runner, batch, seq, ids, amask, attn,
+                              pos, logits);
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : 3;
+  } catch (const std::exception&) {
+    return 1;
+  }
+}

@@ -177,7 +177,7 @@ class OVW1File:
 
 def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden: int = 1024,
               n_heads: int = 16, n_kv: int = 8, inter: int = 3072, audio_vocab: int = 1025,
-              codebooks: int = 8, heads_f32: bool = False) -> None:
+              codebooks: int = 8, heads_f32: bool = False, layout: str = "nk") -> None:
     """A random-weight checkpoint of the reference LM's shape and tensor names
     (cpp/src/model/lm.cpp:96-141): int8 [N, K] linear weights with
     per-output-channel scales |N(0, 0.02)| / 127 (the --int8-layout nk
@@ -185,7 +185,12 @@ def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden
     scales, RMSNorm gains 1 + N(0, 0.05), codebook offsets c * audio_vocab.
     ``heads_f32`` stores the audio heads as the reference's converter does
     by default (tools/convert_weights.py:326-327: kept fp32, written
-    transposed [K, N] with layout 1, :178-180), values N(0, 0.02)."""
+    transposed [K, N] with layout 1, :178-180), values N(0, 0.02).
+    ``layout="kn"`` writes the same integer weights in the converter's
+    default int8 encoding instead ([K, N], one scale per column, layout 1,
+    :170-176) -- the only one the reference's CUDA runner reads."""
+    if layout not in ("nk", "kn"):
+        raise ValueError("layout must be 'nk' or 'kn'")
     rng = np.random.default_rng(seed)
     D = 128
 
@@ -205,6 +210,8 @@ def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden
     if heads_f32:
         Wf = (rng.standard_normal((codebooks * audio_vocab, hidden)) * 0.02).astype(np.float32)
         ts.append(("audio_heads.weight", np.ascontiguousarray(Wf.T), 1, None))
+    elif layout == "kn":
+        ts.append(("audio_heads.weight", np.ascontiguousarray(W.T), 1, s))
     else:
         ts.append(("audio_heads.weight", W, 0, s))
     ts.append(("llm.norm.weight", gain(hidden), 0, None))
@@ -222,5 +229,8 @@ def random_lm(path: str, n_layers: int, vocab: int = 4096, seed: int = 0, hidden
                            ("mlp.gate_proj", inter, hidden), ("mlp.up_proj", inter, hidden),
                            ("mlp.down_proj", hidden, inter)):
             W, s = lin(N, K)
-            ts.append((p + name + ".weight", W, 0, s))
+            if layout == "kn":
+                ts.append((p + name + ".weight", np.ascontiguousarray(W.T), 1, s))
+            else:
+                ts.append((p + name + ".weight", W, 0, s))
     write(path, ts)

@@ -123,3 +123,23 @@ def test_lm_entry_points_reject_null_model():
         L.OVB_ERR_INVALID_ARG
     assert lib.ovb_lm_destroy(None) == L.OVB_OK
     assert lib.ovb_lm_logits(None) is None
+
+
+def test_kn_encoding_of_the_same_weights(repo_tmp):
+    """random_lm(layout="kn") writes the same integer weights in the
+    converter's default [K, N] encoding (layout 1, column scales), which the
+    reference's LM reads too (Mat::mul -> linear_s8, mat.cpp:11-24)."""
+    a, b = str(repo_tmp / "nk.ovw"), str(repo_tmp / "kn.ovw")
+    ovw1.random_lm(a, n_layers=1, vocab=1100, seed=8)
+    ovw1.random_lm(b, n_layers=1, vocab=1100, seed=8, layout="kn")
+    name = "llm.layers.0.self_attn.q_proj.weight"
+    with ovw1.OVW1File(a) as fa, ovw1.OVW1File(b) as fb:
+        assert fa.info(name).layout == 0 and fb.info(name).layout == 1
+        np.testing.assert_array_equal(fa.array(name), fb.array(name).T)
+        np.testing.assert_array_equal(fa.scales(name), fb.scales(name))
+    ref = O.RefLM(b, 1)
+    rng = np.random.default_rng(9)
+    ids, amask, cond, unc, pos = cfg_inputs(rng, 20, 12, 1100)
+    out = ref.forward_cfg(ids, amask, cond, unc, pos)
+    assert np.isfinite(out).all() and out.std() > 0.01
+    ref.close()
