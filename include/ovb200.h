@@ -320,6 +320,34 @@ int ovb_attention(const float* q, const float* k, const float* v, float* out, in
                   int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
                   const ovb_attn_segment* segs, int n_segs, void* stream);
 
+/* The same attention on fp16 q / k / v ([rows, q_stride] and [rows,
+ * kv_stride] fp16, strides and offsets multiples of 8 elements), the form
+ * the LM forward writes after its q/k norm + RoPE: two query heads of a kv
+ * head per CTA sharing each K / V tile, the tensor core and the softmax
+ * overlapped (S, P and O in tensor memory), V read in place as an MN-major
+ * operand.  `tiles` is a table from ovb_attention_tiles for the same
+ * segment list (the segments' masks; their bias fields are then ignored) or
+ * NULL (each segment's fp32 bias, or none, read per element).  Output fp32
+ * like ovb_attention; the same agreement with the fp32 reference (fp16
+ * operands, fp32 accumulation and softmax).  Segment rows <= 32768.  No
+ * counterpart in the reference beyond ovb_attention's. */
+int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
+                    int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                    const ovb_attn_segment* segs, int n_segs, const void* tiles, void* stream);
+/* Bytes of the tile table of a segment list (seg_rows: host array of the
+ * segments' row counts): per (segment, 128-query block, 128-key tile) a
+ * class byte and 2 KB of mask bits. */
+size_t ovb_attention_tiles_bytes(const int32_t* seg_rows, int n_segs);
+/* Build that table on the device from the segments' u8 attention masks
+ * (1 = attend; [rows_i, rows_i] each, concatenated in segment order, the
+ * reference's attn masks, lm.cpp:365): class 0 when every key of a tile is
+ * attended (no mask is read), 1 when mixed (its bits are read), 3 when none
+ * is (the tile is skipped) -- the same softmax as the additive bias
+ * 0 / -1e30 the reference builds from the masks.  `tiles` 256-byte aligned,
+ * tiles_bytes >= ovb_attention_tiles_bytes. */
+int ovb_attention_tiles(const int32_t* seg_rows, int n_segs, const uint8_t* masks, void* tiles,
+                        size_t tiles_bytes, void* stream);
+
 /* ------------------------------------------------------------------ OVW1
  * The reference's weight file (docs/weight-format.en.md), read the way its
  * loader reads it (ov::WeightFile::Open, cpp/src/core/weight_file.cpp:124-206:

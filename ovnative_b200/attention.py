@@ -62,3 +62,60 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, segs, n_heads: 
                                   C.cast(arr, C.POINTER(L.AttnSegment)), len(segs),
                                   torch.cuda.current_stream().cuda_stream))
     return out
+
+
+def attention_tiles(seg_rows, masks: torch.Tensor) -> torch.Tensor:
+    """The tile table (ovb_attention_tiles) of a segment list from its u8
+    masks (1 = attend), the segments' [r, r] masks concatenated into one
+    contiguous uint8 CUDA tensor.  Returns the device table (uint8)."""
+    seg_rows = [int(r) for r in seg_rows]
+    if not masks.is_cuda or masks.dtype != torch.uint8 or not masks.is_contiguous():
+        raise ValueError("masks must be a contiguous uint8 CUDA tensor")
+    if masks.numel() < sum(r * r for r in seg_rows):
+        raise ValueError("masks holds fewer than sum(rows^2) entries")
+    rows = (C.c_int32 * max(1, len(seg_rows)))(*seg_rows)
+    nbytes = int(L.lib().ovb_attention_tiles_bytes(C.cast(rows, C.c_void_p), len(seg_rows)))
+    tiles = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=masks.device)
+    L.check(L.lib().ovb_attention_tiles(C.cast(rows, C.c_void_p), len(seg_rows), masks.data_ptr(),
+                                        tiles.data_ptr(), tiles.numel(),
+                                        torch.cuda.current_stream().cuda_stream))
+    return tiles
+
+
+def attention_h(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, segs, n_heads: int,
+                n_kv: int, scale: float, out: torch.Tensor | None = None,
+                tiles: torch.Tensor | None = None) -> torch.Tensor:
+    """ovb_attention_h: the same attention on fp16 q [T, n_heads * 128] and
+    k / v [T', n_kv * 128] (contiguous CUDA tensors).  segs as for
+    `attention` (biases ignored when `tiles`, from attention_tiles over the
+    same segments, is given).  Returns fp32 out shaped like q."""
+    for name, t in (("q", q16), ("k", k16), ("v", v16)):
+        if not t.is_cuda or t.dtype != torch.float16 or t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 2-D float16 CUDA tensor")
+    if k16.shape != v16.shape:
+        raise ValueError("k and v must have the same shape")
+    if q16.shape[1] != n_heads * HEAD_DIM or k16.shape[1] != n_kv * HEAD_DIM:
+        raise ValueError("q / k widths must be n_heads * 128 / n_kv * 128")
+    if out is None:
+        out = torch.zeros(q16.shape, dtype=torch.float32, device=q16.device)
+    segs = list(segs)
+    arr = (L.AttnSegment * max(1, len(segs)))()
+    keep = []
+    for i, (bias, rows, q_off, kv_off) in enumerate(segs):
+        if q_off + rows * q16.shape[1] > q16.numel() or kv_off + rows * k16.shape[1] > k16.numel():
+            raise ValueError("segment runs past the end of q / k")
+        bp = None
+        if bias is not None and tiles is None:
+            if (not bias.is_cuda or bias.dtype != torch.float32 or not bias.is_contiguous()
+                    or bias.numel() != rows * rows):
+                raise ValueError("bias must be a contiguous float32 CUDA tensor of rows * rows")
+            keep.append(bias)
+            bp = bias.data_ptr()
+        arr[i] = L.AttnSegment(bp, int(rows), int(q_off), int(kv_off))
+    L.check(L.lib().ovb_attention_h(q16.data_ptr(), k16.data_ptr(), v16.data_ptr(),
+                                    out.data_ptr(), q16.shape[1], k16.shape[1], n_heads, n_kv,
+                                    HEAD_DIM, float(scale),
+                                    C.cast(arr, C.POINTER(L.AttnSegment)), len(segs),
+                                    None if tiles is None else tiles.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream))
+    return out

@@ -445,6 +445,428 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   }
 }
 
+// ============================================================ fp16 operands
+// attention_h_kernel: the same attention on fp16 q / k / v (written once per
+// layer by the q/k-norm + RoPE kernel), warp-specialised so that the tensor
+// core, the softmax and the loads overlap.
+//
+// One CTA per (segment, block of 128 query rows, kv head, pair of the query
+// heads that share it): the two heads' Q tiles stay in shared memory and every
+// K / V tile is loaded once for both.  320 threads:
+//   warps 0-3  softmax of head A (thread = query row = TMEM lane),
+//   warps 4-7  softmax of head B,
+//   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles into a
+//              two-stage ring (fp16, 128-byte swizzle, two 64-column boxes
+//              per tile),
+//   warp 9     TMEM allocator and MMA issuer (one thread).
+// TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512) fp32
+// columns; P (fp16 pairs) overwrites the first 64 columns of its head's S.
+// The MMA issue order ping-pongs the heads,
+//     S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) ...
+// so the tensor core computes one head's next scores while the other head's
+// softmax runs.  MMAs of the CTA complete in issue order, so a head's S(i)
+// being complete (its commit) means its P V(i - 1) is complete too: the
+// softmax then owns O for a rescale, and P(i - 1) has been read before S(i)
+// overwrote it.  V is the B operand of P V in MN-major form (the keys are
+// its K dimension), read straight from the TMA layout.
+//
+// Masks: an optional tile table (ovb_attention_tiles) classes every
+// (segment, query block, key tile): 0 every key attended, 1 mixed (128 x 128
+// bits, one 16-byte load per row), 3 nothing attended (the tile is skipped by
+// every role).  Without a table, tiles read the segment's fp32 bias (or none).
+// Scores are kept in base-2 units (x = s * scale * log2 e), the softmax
+// reference point m moves only when a tile's maximum exceeds it by more than
+// 8 (P <= 256), and a row whose scores are all below -1e29 (the reference's
+// fully masked rows) gives zeros, as ov::attention_head_f32 does.
+namespace {
+
+constexpr int kHThreads = 320;
+constexpr int kHMaxTiles = 256;  // key tiles per segment (32768 rows)
+constexpr uint32_t kHBox = 128 * 128;         // bytes of one 64-column fp16 box (128 rows)
+constexpr uint32_t kHTile = 2 * kHBox;        // one 128 x 128 fp16 tile
+constexpr uint32_t kHOffQ = 0;                // Q_A, Q_B
+constexpr uint32_t kHOffKV = 2 * kHTile;      // stage s: K at +2s tiles, V at +2s+1
+constexpr uint32_t kHOffCtl = kHOffKV + 4 * kHTile;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kHRescale = 8.f;              // base-2 units
+
+struct AttnHCtl {
+  uint64_t q_full;
+  uint64_t kv_full[2];
+  uint64_t kv_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_final[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int n_act;
+  int16_t act[kHMaxTiles];  // key tiles with something to attend, in order
+};
+constexpr size_t kAttHSmem = 1024 + kHOffCtl + sizeof(AttnHCtl);
+static_assert(kAttHSmem <= 227 * 1024, "attention_h shared memory");
+
+// Shared-memory descriptor of an MN-major operand written by TMA with the
+// 128-byte swizzle: 64-element (128-byte) rows along MN, one row per K index,
+// 8-row groups SBO bytes apart, the next 64 MN elements LBO bytes further.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(lbo >> 4) << 16;
+  d |= static_cast<uint64_t>(sbo >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kHThreads, 1)
+    attention_h_kernel(const __grid_constant__ AttnHArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  AttnHCtl* ctl = reinterpret_cast<AttnHCtl*>(smem + kHOffCtl);
+  const uint32_t sbase = smem_u32(smem);
+  volatile int* abort = &ctl->abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- this CTA's (segment, query block, kv head, head pair)
+  int si = 0;
+  for (int i = 1; i < args.n_segs; ++i)
+    if (static_cast<int>(blockIdx.x) >= args.segs[i].cta0) si = i;
+  const AttnHSeg& sg = args.segs[si];
+  int rem = static_cast<int>(blockIdx.x) - sg.cta0;
+  const int pair = rem % args.pairs;
+  rem /= args.pairs;
+  const int kv = rem % args.n_kv;
+  const int qb = rem / args.n_kv;
+  const int S = sg.rows;
+  const int row0 = qb * 128;
+  const int head0 = kv * args.group + 2 * pair;
+  const int nh = min(2, args.group - 2 * pair);  // heads in this CTA (1 or 2)
+  const int nkt = (S + 127) / 128;
+  const int kx = sg.kv_x + kv * 128;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&ctl->q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&ctl->kv_full[i]), 1);
+      mbar_init(smem_u32(&ctl->kv_empty[i]), 1);
+      mbar_init(smem_u32(&ctl->s_full[i]), 1);
+      mbar_init(smem_u32(&ctl->p_full[i]), 128);
+      mbar_init(smem_u32(&ctl->o_final[i]), 1);
+    }
+    mbar_init(smem_u32(&ctl->mma_done), 1);
+    ctl->abort = 0;
+    int n = 0;
+    for (int j = 0; j < nkt; ++j) {
+      const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : 0;
+      if (cls != 3) ctl->act[n++] = static_cast<int16_t>(j);
+    }
+    ctl->n_act = n;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int n_act = ctl->n_act;
+  bool ok = true;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (!ovb_wait(smem_u32(bar), parity, abort)) {
+      ok = false;
+      *abort = 1;
+    }
+    return ok;
+  };
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t qbytes = static_cast<uint32_t>(nh) * kHTile;
+      mbar_arrive_expect_tx(smem_u32(&ctl->q_full), qbytes);
+      for (int h = 0; h < nh; ++h)
+        for (int b = 0; b < 2; ++b)
+          tma_load_2d(sbase + kHOffQ + h * kHTile + b * kHBox, &args.tm_q,
+                      sg.q_x + (head0 + h) * 128 + b * 64, sg.q_y + row0,
+                      smem_u32(&ctl->q_full));
+      int issued = 0;
+      for (int i = 0; i < n_act && ok; ++i) {
+        const int st = i & 1;
+        if (i >= 2 && !wait(&ctl->kv_empty[st], static_cast<uint32_t>((i >> 1) - 1) & 1u)) break;
+        issued = i + 1;
+        const int ky = sg.kv_y + ctl->act[i] * 128;
+        const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile, vb = kb + kHTile;
+        mbar_arrive_expect_tx(smem_u32(&ctl->kv_full[st]), 2 * kHTile);
+        for (int b = 0; b < 2; ++b) {
+          tma_load_2d(kb + b * kHBox, &args.tm_k, kx + b * 64, ky, smem_u32(&ctl->kv_full[st]));
+          tma_load_2d(vb + b * kHBox, &args.tm_v, kx + b * 64, ky, smem_u32(&ctl->kv_full[st]));
+        }
+      }
+      // every load this thread issued has landed before the CTA can exit
+      volatile int no_abort = 0;
+      ovb_wait(smem_u32(&ctl->q_full), 0u, &no_abort);
+      for (int st = 0; st < 2 && st < issued; ++st) {
+        const int last = ((issued - 1 - st) / 2) * 2 + st;  // last tile loaded into stage st
+        ovb_wait(smem_u32(&ctl->kv_full[st]), static_cast<uint32_t>(last >> 1) & 1u, &no_abort);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16(128, 128);
+      const uint32_t id_o = idesc_f16(128, 128) | (1u << 16);  // B (V) MN-major
+      auto issue_s = [&](int h, int st) {
+        const uint32_t qa = sbase + kHOffQ + h * kHTile;
+        const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = static_cast<uint32_t>((kk >> 2) * kHBox + (kk & 3) * 32);
+          mma_f16_ss(tmem + h * 128, sw128_kmajor_desc(qa, off), sw128_kmajor_desc(kb, off), id_s,
+                     kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&ctl->s_full[h]));
+      };
+      auto issue_pv = [&](int h, int st, bool first) {
+        const uint32_t vb = sbase + kHOffKV + (2 * st + 1) * kHTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8,
+                     sw128_mnmajor_desc(vb + kk * 2048, kHBox, 1024), id_o,
+                     (!first || kk > 0) ? 1u : 0u);
+      };
+      if (wait(&ctl->q_full, 0u) && n_act > 0 && wait(&ctl->kv_full[0], 0u)) {
+        tc_fence_after();
+        for (int h = 0; h < nh; ++h) issue_s(h, 0);
+        for (int i = 0; i < n_act && ok; ++i) {
+          const int st = i & 1;
+          const bool more = i + 1 < n_act;
+          if (!wait(&ctl->p_full[0], static_cast<uint32_t>(i) & 1u)) break;
+          tc_fence_after();
+          issue_pv(0, st, i == 0);
+          if (!more) tc_commit(smem_u32(&ctl->o_final[0]));
+          if (more) {
+            if (!wait(&ctl->kv_full[st ^ 1], static_cast<uint32_t>((i + 1) >> 1) & 1u)) break;
+            tc_fence_after();
+            issue_s(0, st ^ 1);
+          }
+          if (nh == 2) {
+            if (!wait(&ctl->p_full[1], static_cast<uint32_t>(i) & 1u)) break;
+            tc_fence_after();
+            issue_pv(1, st, i == 0);
+            if (!more) tc_commit(smem_u32(&ctl->o_final[1]));
+          }
+          tc_commit(smem_u32(&ctl->kv_empty[st]));
+          if (nh == 2 && more) issue_s(1, st ^ 1);
+        }
+      }
+      // every MMA issued has completed before TMEM is freed
+      tc_commit(smem_u32(&ctl->mma_done));
+      volatile int no_abort = 0;
+      ovb_wait(smem_u32(&ctl->mma_done), 0u, &no_abort);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int h = warp >> 2;          // head of this warpgroup
+    const int r = (warp & 3) * 32 + lane;
+    const int row = row0 + r;
+    const bool row_ok = row < S;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + static_cast<uint32_t>(h * 128);
+    const uint32_t o_col = tmem + lane_off + static_cast<uint32_t>(256 + h * 128);
+    const float sl2 = args.scale * kLog2e;
+    float m = -INFINITY, mt = -INFINITY, l = 0.f;
+    if (h < nh) {
+      for (int i = 0; i < n_act; ++i) {
+        // the warp leaves together: its TMEM accesses are warp-collective
+        if (!__all_sync(0xffffffffu, wait(&ctl->s_full[h], static_cast<uint32_t>(i) & 1u))) {
+          ok = false;
+          *abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const int j = ctl->act[i];
+        const int key0 = j * 128;
+        const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j]
+                                        : (sg.bias ? 2 : 0);
+        uint4 bits = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+        if (cls == 1)
+          bits = __ldg(reinterpret_cast<const uint4*>(args.tile_bits) +
+                       (static_cast<int64_t>(sg.tile0 + qb * nkt + j) * 128 + r));
+        uint32_t u[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u[c]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc_wait_ld32(u[c]);
+        const uint32_t bw[4] = {bits.x, bits.y, bits.z, bits.w};
+        const float* brow = sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S;
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = key0 + c * 32 + e;
+            float x;
+            if (cls == 2) {
+              const float b = (row_ok && key < S) ? brow[key] : 0.f;
+              x = __fmul_rn(__fadd_rn(__fmul_rn(__uint_as_float(u[c][e]), args.scale), b), kLog2e);
+            } else {
+              x = __fmul_rn(__uint_as_float(u[c][e]), sl2);
+            }
+            const bool on = key < S && ((bw[c] >> e) & 1u);
+            x = on ? x : -INFINITY;
+            tmax = fmaxf(tmax, x);
+            u[c][e] = __float_as_uint(x);
+          }
+        }
+        mt = fmaxf(mt, tmax);
+        float factor = 1.f;
+        if (tmax > m + kHRescale) {  // also the first finite maximum (m = -inf)
+          factor = m == -INFINITY ? 0.f : ex2_approx(m - tmax);
+          l = __fmul_rn(l, factor);
+          m = tmax;
+        }
+        if (i > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+          // 16 columns at a time: the row's scores stay live in registers
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[16];
+            tmem_ld16(o_col + static_cast<uint32_t>(c * 16), o);
+            tc_wait_ld16(o);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__fmul_rn(__uint_as_float(o[e]), factor));
+            tmem_st16(o_col + static_cast<uint32_t>(c * 16), o);
+          }
+        }
+        const float mexp = m == -INFINITY ? 0.f : m;
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(__uint_as_float(u[c][2 * e]) - mexp);
+            const float p1 = ex2_approx(__uint_as_float(u[c][2 * e + 1]) - mexp);
+            sum += p0 + p1;
+            pk[e] = pack2(p0, p1);
+          }
+          tmem_st16(s_col + static_cast<uint32_t>(c * 16), pk);
+        }
+        l += sum;
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->p_full[h]));
+      }
+      // ---- O / l to the output row
+      const bool have_o =
+          __all_sync(0xffffffffu, n_act > 0 && ok && wait(&ctl->o_final[h], 0u));
+      if (have_o) tc_fence_after();
+      const bool masked = !(mt >= -1e29f * kLog2e);
+      const float inv_l = masked || !(l > 0.f) ? 0.f : __frcp_rn(l);
+      float* orow = args.out + sg.q_off + static_cast<int64_t>(head0 + h) * 128 +
+                    static_cast<int64_t>(row_ok ? row : 0) * args.q_stride;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (have_o) {
+          tmem_ld32(o_col + static_cast<uint32_t>(c * 32), o);
+          tc_wait_ld32(o);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(orow + c * 32 + e) =
+                make_float4(__fmul_rn(__uint_as_float(o[e]), inv_l),
+                            __fmul_rn(__uint_as_float(o[e + 1]), inv_l),
+                            __fmul_rn(__uint_as_float(o[e + 2]), inv_l),
+                            __fmul_rn(__uint_as_float(o[e + 3]), inv_l));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort) atomicOr(&g_status_att, kErrAttWait);
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Tile table of a segment list from its u8 masks (ovb_attention_tiles): one
+// CTA of 128 threads per (segment, query block, key tile); thread r packs the
+// 128 mask bits of query row r (keys past the segment count as attended, rows
+// past it are not looked at) and the CTA classes the tile.
+__global__ void __launch_bounds__(128) attn_tiles_kernel(const __grid_constant__ AttnTilesArgs a,
+                                                         uint8_t* cls, uint32_t* bits) {
+  const int t = blockIdx.x;
+  int si = 0;
+  for (int i = 1; i < a.n_segs; ++i)
+    if (t >= a.tile0[i]) si = i;
+  const int S = a.rows[si];
+  const int nkt = (S + 127) / 128;
+  const int qb = (t - a.tile0[si]) / nkt, kt = (t - a.tile0[si]) % nkt;
+  const int r = threadIdx.x;
+  const int row = qb * 128 + r;
+  const uint8_t* mrow = a.masks + a.mask_off[si] + static_cast<int64_t>(row) * S;
+  uint32_t w[4];
+  bool any0 = false, any1 = false;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v = 0;
+    for (int e = 0; e < 32; ++e) {
+      const int key = kt * 128 + c * 32 + e;
+      bool on = true;
+      if (row < S && key < S) {
+        on = mrow[key] != 0;
+        any0 |= !on;
+        any1 |= on;
+      }
+      v |= static_cast<uint32_t>(on) << e;
+    }
+    w[c] = v;
+  }
+  reinterpret_cast<uint4*>(bits)[static_cast<int64_t>(t) * 128 + r] = make_uint4(w[0], w[1], w[2], w[3]);
+  const int n0 = __syncthreads_or(any0), n1 = __syncthreads_or(any1);
+  if (r == 0) cls[t] = static_cast<uint8_t>(!n0 ? 0 : (!n1 ? 3 : 1));
+}
+
+cudaError_t launch_attention_h(const AttnHArgs& args, int ctas, cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static thread_local int configured_dev = -1;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(attention_h_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kAttHSmem));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  return launch_plain(attention_h_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kHThreads),
+                      kAttHSmem, s, args);
+}
+
+cudaError_t launch_attn_tiles(const AttnTilesArgs& a, int tiles, uint8_t* cls, uint32_t* bits,
+                              cudaStream_t s) {
+  return launch_plain(attn_tiles_kernel, dim3(static_cast<unsigned>(tiles)), dim3(128), 0, s, a,
+                      cls, bits);
+}
+
 cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);

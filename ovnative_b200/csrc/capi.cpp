@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -986,6 +987,146 @@ int ovb_attention(const float* q, const float* k, const float* v, float* out, in
     return OVB_ERR_INTERNAL;
   if (cuda_failed(ovb::launch_attention(a, static_cast<int>(blocks), as_stream(stream)),
                   "attention launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+// ------------------------------------------------- fp16-operand attention
+namespace {
+// Tile count of a segment list: per segment ceil(rows/128) query blocks x as
+// many key tiles.
+int64_t attn_tile_count(const int32_t* seg_rows, int n_segs) {
+  int64_t t = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    const int64_t b = (int64_t{seg_rows[i]} + 127) / 128;
+    t += b * b;
+  }
+  return t;
+}
+size_t attn_class_bytes(int64_t tiles) { return static_cast<size_t>((tiles + 255) / 256 * 256); }
+}  // namespace
+
+size_t ovb_attention_tiles_bytes(const int32_t* seg_rows, int n_segs) {
+  if (!seg_rows || n_segs <= 0) return 0;
+  for (int i = 0; i < n_segs; ++i)
+    if (seg_rows[i] < 0) return 0;
+  const int64_t t = attn_tile_count(seg_rows, n_segs);
+  return attn_class_bytes(t) + static_cast<size_t>(t) * 2048;
+}
+
+int ovb_attention_tiles(const int32_t* seg_rows, int n_segs, const uint8_t* masks, void* tiles,
+                        size_t tiles_bytes, void* stream) {
+  if (n_segs == 0) return OVB_OK;
+  if (n_segs < 0 || n_segs > ovb::kAttMaxSegs) return invalid("n_segs must be in [0, 64]");
+  if (!seg_rows || !masks || !tiles) return invalid("seg_rows/masks/tiles must be non-null");
+  if (!aligned(tiles, 256)) return invalid("tiles must be 256-byte aligned");
+  ovb::AttnTilesArgs a = {};
+  a.masks = masks;
+  a.n_segs = n_segs;
+  int64_t t = 0, off = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    if (seg_rows[i] < 0 || seg_rows[i] > 128 * 256) return invalid("segment rows must be in [0, 32768]");
+    const int64_t b = (int64_t{seg_rows[i]} + 127) / 128;
+    a.rows[i] = seg_rows[i];
+    a.tile0[i] = static_cast<int>(t);
+    a.mask_off[i] = off;
+    t += b * b;
+    off += int64_t{seg_rows[i]} * seg_rows[i];
+  }
+  if (tiles_bytes < ovb_attention_tiles_bytes(seg_rows, n_segs)) return invalid("tiles buffer too small");
+  if (t == 0) return OVB_OK;
+  if (t > (int64_t{1} << 30)) return invalid("too many tiles");
+  auto* cls = static_cast<uint8_t*>(tiles);
+  auto* bits = reinterpret_cast<uint32_t*>(cls + attn_class_bytes(t));
+  if (cuda_failed(ovb::launch_attn_tiles(a, static_cast<int>(t), cls, bits, as_stream(stream)),
+                  "attention tile table launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
+                    int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                    const ovb_attn_segment* segs, int n_segs, const void* tiles, void* stream) {
+  if (n_segs == 0) return OVB_OK;
+  if (n_segs < 0 || n_segs > ovb::kAttMaxSegs) return invalid("n_segs must be in [0, 64]");
+  if (!segs || !q || !k || !v || !out) return invalid("q/k/v/out/segs must be non-null");
+  if (head_dim != 128) return invalid("head_dim must be 128");
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0)
+    return invalid("n_heads must be a positive multiple of n_kv");
+  if (q_stride < int64_t{n_heads} * head_dim || kv_stride < int64_t{n_kv} * head_dim)
+    return invalid("row strides must cover every head");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) ||
+      q_stride % 8 != 0 || kv_stride % 8 != 0)
+    return invalid("q/k/v/out must be 16-byte aligned with strides a multiple of 8");
+  if (tiles && !aligned(tiles, 256)) return invalid("tiles must be 256-byte aligned");
+  if (q_stride > (int64_t{1} << 30) || kv_stride > (int64_t{1} << 30))
+    return invalid("row strides too large");
+  ovb::AttnHArgs a = {};
+  a.out = out;
+  a.q_stride = q_stride;
+  a.n_heads = n_heads;
+  a.n_kv = n_kv;
+  a.group = n_heads / n_kv;
+  a.pairs = (a.group + 1) / 2;
+  a.scale = scale;
+  std::vector<int32_t> rows(static_cast<size_t>(n_segs));
+  for (int i = 0; i < n_segs; ++i) rows[static_cast<size_t>(i)] = segs[i].rows;
+  // Longer segments' CTAs first (they run longest), the table in segment order.
+  std::vector<int> order(static_cast<size_t>(n_segs));
+  for (int i = 0; i < n_segs; ++i) order[static_cast<size_t>(i)] = i;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int x, int y) { return segs[x].rows > segs[y].rows; });
+  std::vector<int64_t> tile0(static_cast<size_t>(n_segs));
+  int64_t t = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    if (segs[i].rows < 0 || segs[i].rows > 128 * 256) return invalid("segment rows must be in [0, 32768]");
+    tile0[static_cast<size_t>(i)] = t;
+    const int64_t b = (int64_t{segs[i].rows} + 127) / 128;
+    t += b * b;
+  }
+  int64_t ctas = 0, q_rows = 1, kv_rows = 1;
+  for (int oi = 0; oi < n_segs; ++oi) {
+    const ovb_attn_segment& g = segs[order[static_cast<size_t>(oi)]];
+    if (g.q_off < 0 || g.kv_off < 0) return invalid("negative segment field");
+    if (g.q_off % 8 != 0 || g.kv_off % 8 != 0)
+      return invalid("segment offsets must be multiples of 8");
+    if (g.rows == 0) continue;
+    const int64_t qx = g.q_off % q_stride, qy = g.q_off / q_stride;
+    const int64_t kx = g.kv_off % kv_stride, ky = g.kv_off / kv_stride;
+    if (qx + int64_t{n_heads} * head_dim > q_stride || kx + int64_t{n_kv} * head_dim > kv_stride)
+      return invalid("segment offset leaves no room for every head within a row");
+    if (qy + g.rows > (int64_t{1} << 31) - 1 - 128 || ky + g.rows > (int64_t{1} << 31) - 1 - 128)
+      return invalid("segment rows too large");
+    ovb::AttnHSeg& d = a.segs[a.n_segs++];
+    d.bias = tiles ? nullptr : g.bias;
+    d.q_off = g.q_off;
+    d.rows = g.rows;
+    d.cta0 = static_cast<int>(ctas);
+    d.q_x = static_cast<int>(qx);
+    d.q_y = static_cast<int>(qy);
+    d.kv_x = static_cast<int>(kx);
+    d.kv_y = static_cast<int>(ky);
+    d.tile0 = static_cast<int>(tile0[static_cast<size_t>(order[static_cast<size_t>(oi)])]);
+    q_rows = std::max(q_rows, qy + g.rows);
+    kv_rows = std::max(kv_rows, ky + g.rows);
+    ctas += (g.rows + 127) / 128 * n_kv * a.pairs;
+    if (ctas > (int64_t{1} << 31) - 1) return invalid("too many query blocks");
+  }
+  if (ctas == 0) return OVB_OK;
+  if (tiles) {
+    a.tile_class = static_cast<const uint8_t*>(tiles);
+    a.tile_bits = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(tiles) +
+                                                    attn_class_bytes(t));
+  }
+  if (!ovb::encode_tmap_2d(&a.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q_stride, q_rows,
+                           q_stride * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !ovb::encode_tmap_2d(&a.tm_k, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kv_stride, kv_rows,
+                           kv_stride * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !ovb::encode_tmap_2d(&a.tm_v, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kv_stride, kv_rows,
+                           kv_stride * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return OVB_ERR_INTERNAL;
+  if (cuda_failed(ovb::launch_attention_h(a, static_cast<int>(ctas), as_stream(stream)),
+                  "attention_h launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
 }

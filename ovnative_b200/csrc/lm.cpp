@@ -4,7 +4,9 @@
 // (lm.h:91-96) and the ragged CFG forward (LM::forward_cfg, lm.cpp:403-454).
 //
 // Per layer (LM::run_layer, lm.cpp:217-322): RMSNorm + quantise -> q|k|v
-// GEMM -> per-head RMSNorm + RoPE -> attention over the segments -> quantise
+// GEMM -> per-head RMSNorm + RoPE (written as fp16 q / k, with v as fp16) ->
+// attention over the segments (ovb_attention_h; the masks as a tile table
+// built once per forward) -> quantise
 // -> o GEMM += x -> RMSNorm + quantise -> gate|up GEMM fused with SiLU*up +
 // quantise -> down GEMM += x.  Then the final RMSNorm + quantise and the
 // audio-heads GEMM.  The linear weights are int8 (either OVW1 orientation)
@@ -75,7 +77,9 @@ struct ovb_lm {
   DevBuf norms, emb, offsets, inv_freq;
   ovb::EmbTable tok{}, aud{};
   // forward buffers (grown on demand)
-  DevBuf x, aq, asc, q, k, v, attn, qi, asci, logits, logits_perm, ids, amask, pos, masks, bias;
+  DevBuf x, aq, asc, q, k, v, attn, qi, asci, logits, logits_perm, ids, amask, pos, masks;
+  DevBuf q16, k16, v16;  // fp16 q / k (normalised, rotated) and v: the attention's operands
+  DevBuf tiles;          // the attention's mask tile table (ovb_attention_tiles)
   DevBuf pred, scores;  // ovb_lm_sample's device outputs
   int64_t last_rows = 0;
 
@@ -315,6 +319,14 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
   return OVB_OK;
 }
 
+// Bytes of the mask tile table for any segment list of `rows` rows in total
+// whose masks hold `mask_elems` entries (sum of rows_i^2): sum of
+// ceil(r_i / 128)^2 <= mask_elems / 16384 + rows / 64 + n_segs (n_segs <= 64).
+size_t tiles_bound(int64_t rows, int64_t mask_elems) {
+  const int64_t t = mask_elems / 16384 + rows / 64 + 128;
+  return static_cast<size_t>((t + 255) / 256 * 256 + t * 2048);
+}
+
 // Size every forward buffer for `rows` packed rows and `mask_elems` attention
 // mask entries.
 bool reserve(ovb_lm* m, int64_t rows, int64_t mask_elems) {
@@ -329,14 +341,15 @@ bool reserve(ovb_lm* m, int64_t rows, int64_t mask_elems) {
          m->attn.grow(r * QD * 4) && m->qi.grow(r * m->inter * ab) &&
          m->asci.grow(r * (m->inter / 32) * 4) && m->logits.grow(r * CV * 4) &&
          m->ids.grow(r * m->n_codebooks * 8) && m->amask.grow(r) && m->pos.grow(r * 8) &&
-         m->masks.grow(static_cast<size_t>(mask_elems)) &&
-         m->bias.grow(static_cast<size_t>(mask_elems) * 4);
+         m->masks.grow(static_cast<size_t>(mask_elems)) && m->q16.grow(r * QD * 2) &&
+         m->k16.grow(r * KVD * 2) && m->v16.grow(r * KVD * 2) &&
+         m->tiles.grow(tiles_bound(rows, mask_elems));
 }
 
 // The layers and heads on device buffers already holding ids / amask / pos
-// and the biases: x <- embed; per layer; logits <- heads.
+// and the attention's tile table: x <- embed; per layer; logits <- heads.
 int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_segs,
-        cudaStream_t s) {
+        const void* tiles, cudaStream_t s) {
   const int64_t H = m->hidden, QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
   const int qf = m->f16 ? OVB_AQ_F16 : 0;
@@ -356,13 +369,13 @@ int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_se
                              {KVD, m->v.as<float>(), KVD}};
     OVB_LM_TRY(m->f16 ? ovb_linear_h_sliced(rows, L.qkv, aq, sl, 3, s)
                       : ovb_linear_q_sliced(rows, L.qkv, aq, asc, sl, 3, s));
-    if (ovb::launch_qk_norm_rope(m->q.as<float>(), m->k.as<float>(), L.q_norm, L.k_norm,
-                                 m->pos.as<int64_t>(), m->inv_freq.as<float>(), rows, m->n_heads,
-                                 m->n_kv, m->eps, s) != cudaSuccess)
+    if (ovb::launch_qk_norm_rope_f16(m->q.as<float>(), m->k.as<float>(), m->v.as<float>(),
+                                     m->q16.p, m->k16.p, m->v16.p, L.q_norm, L.k_norm,
+                                     m->pos.as<int64_t>(), m->inv_freq.as<float>(), rows,
+                                     m->n_heads, m->n_kv, m->eps, s) != cudaSuccess)
       return internal("qk norm / rope launch failed");
-    OVB_LM_TRY(ovb_attention(m->q.as<float>(), m->k.as<float>(), m->v.as<float>(),
-                             m->attn.as<float>(), QD, KVD, m->n_heads, m->n_kv, 128, scale, segs,
-                             n_segs, s));
+    OVB_LM_TRY(ovb_attention_h(m->q16.p, m->k16.p, m->v16.p, m->attn.as<float>(), QD, KVD,
+                               m->n_heads, m->n_kv, 128, scale, segs, n_segs, tiles, s));
     OVB_LM_TRY(ovb_quantize(rows, QD, m->attn.as<float>(), QD, aq, asc, qf, s));
     OVB_LM_TRY(m->f16 ? ovb_linear_h(rows, L.o, aq, x, H, 1, s)
                       : ovb_linear_q(rows, L.o, aq, asc, x, H, 1, s));
@@ -390,6 +403,22 @@ int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_se
 #undef OVB_LM_TRY
   m->last_rows = rows;
   return OVB_OK;
+}
+
+// The forward over packed segments whose u8 masks are in m->masks (in
+// segment order): the attention's tile table from the masks, then run().
+int run_segments(ovb_lm* m, const int32_t* seg_rows, int n_segs, int64_t rows, int seq,
+                 cudaStream_t s) {
+  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
+  int rc = ovb_attention_tiles(seg_rows, n_segs, m->masks.as<uint8_t>(), m->tiles.p, m->tiles.n, s);
+  if (rc != OVB_OK) return rc;
+  ovb_attn_segment segs[ovb::kAttMaxSegs];
+  int64_t r0 = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    segs[i] = {nullptr, seg_rows[i], r0 * QD, r0 * KVD};
+    r0 += seg_rows[i];
+  }
+  return run(m, rows, seq, segs, n_segs, m->tiles.p, s);
 }
 
 }  // namespace
@@ -483,14 +512,10 @@ int ovb_lm_forward_cfg_device(ovb_lm* m, int cond_seq, int uncond_seq, const int
       cudaMemcpyAsync(m->amask.p, audio_mask, rows, dd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->pos.p, pos, rows * 8, dd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->masks.p, cond_attn, cm, dd, s) != cudaSuccess ||
-      cudaMemcpyAsync(m->masks.as<uint8_t>() + cm, uncond_attn, um, dd, s) != cudaSuccess ||
-      ovb::launch_mask_bias(m->masks.as<uint8_t>(), cm + um, m->bias.as<float>(), s) != cudaSuccess)
+      cudaMemcpyAsync(m->masks.as<uint8_t>() + cm, uncond_attn, um, dd, s) != cudaSuccess)
     return internal("input copies failed");
-  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
-  const ovb_attn_segment segs[2] = {
-      {m->bias.as<float>(), cond_seq, 0, 0},
-      {m->bias.as<float>() + cm, uncond_seq, int64_t(cond_seq) * QD, int64_t(cond_seq) * KVD}};
-  return run(m, rows, static_cast<int>(rows), segs, 2, s);
+  const int32_t seg_rows[2] = {cond_seq, uncond_seq};
+  return run_segments(m, seg_rows, 2, rows, static_cast<int>(rows), s);
 }
 
 int ovb_lm_forward_segments_device(ovb_lm* m, int n_segs, const int32_t* seg_rows,
@@ -514,19 +539,9 @@ int ovb_lm_forward_segments_device(ovb_lm* m, int n_segs, const int32_t* seg_row
   if (cudaMemcpyAsync(m->ids.p, ids, rows * m->n_codebooks * 8, dd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->amask.p, audio_mask, rows, dd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->pos.p, pos, rows * 8, dd, s) != cudaSuccess ||
-      cudaMemcpyAsync(m->masks.p, masks, mask_elems, dd, s) != cudaSuccess ||
-      ovb::launch_mask_bias(m->masks.as<uint8_t>(), mask_elems, m->bias.as<float>(), s) !=
-          cudaSuccess)
+      cudaMemcpyAsync(m->masks.p, masks, mask_elems, dd, s) != cudaSuccess)
     return internal("input copies failed");
-  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
-  ovb_attn_segment segs[ovb::kAttMaxSegs];
-  int64_t r0 = 0, b0 = 0;
-  for (int i = 0; i < n_segs; ++i) {
-    segs[i] = {m->bias.as<float>() + b0, seg_rows[i], r0 * QD, r0 * KVD};
-    r0 += seg_rows[i];
-    b0 += int64_t(seg_rows[i]) * seg_rows[i];
-  }
-  return run(m, rows, static_cast<int>(rows), segs, n_segs, s);
+  return run_segments(m, seg_rows, n_segs, rows, static_cast<int>(rows), s);
 }
 
 int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* ids,
@@ -546,14 +561,10 @@ int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* i
       cudaMemcpyAsync(m->amask.p, audio_mask, rows, hd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->pos.p, pos, rows * 8, hd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->masks.p, cond_attn, cm, hd, s) != cudaSuccess ||
-      cudaMemcpyAsync(m->masks.as<uint8_t>() + cm, uncond_attn, um, hd, s) != cudaSuccess ||
-      ovb::launch_mask_bias(m->masks.as<uint8_t>(), cm + um, m->bias.as<float>(), s) != cudaSuccess)
+      cudaMemcpyAsync(m->masks.as<uint8_t>() + cm, uncond_attn, um, hd, s) != cudaSuccess)
     return internal("input copies failed");
-  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
-  const ovb_attn_segment segs[2] = {
-      {m->bias.as<float>(), cond_seq, 0, 0},
-      {m->bias.as<float>() + cm, uncond_seq, int64_t(cond_seq) * QD, int64_t(cond_seq) * KVD}};
-  int rc = run(m, rows, static_cast<int>(rows), segs, 2, s);
+  const int32_t seg_rows[2] = {cond_seq, uncond_seq};
+  int rc = run_segments(m, seg_rows, 2, rows, static_cast<int>(rows), s);
   if (rc != OVB_OK) return rc;
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
   if (logits &&
@@ -578,15 +589,10 @@ int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint
   if (cudaMemcpyAsync(m->ids.p, ids, rows * m->n_codebooks * 8, hd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->amask.p, audio_mask, rows, hd, s) != cudaSuccess ||
       cudaMemcpyAsync(m->pos.p, pos, rows * 8, hd, s) != cudaSuccess ||
-      cudaMemcpyAsync(m->masks.p, attn_mask, mm, hd, s) != cudaSuccess ||
-      ovb::launch_mask_bias(m->masks.as<uint8_t>(), mm, m->bias.as<float>(), s) != cudaSuccess)
+      cudaMemcpyAsync(m->masks.p, attn_mask, mm, hd, s) != cudaSuccess)
     return internal("input copies failed");
-  const int64_t QD = int64_t(m->n_heads) * 128, KVD = int64_t(m->n_kv) * 128;
-  std::vector<ovb_attn_segment> segs(static_cast<size_t>(batch));
-  for (int b = 0; b < batch; ++b)
-    segs[static_cast<size_t>(b)] = {m->bias.as<float>() + int64_t(b) * seq * seq, seq,
-                                    int64_t(b) * seq * QD, int64_t(b) * seq * KVD};
-  int rc = run(m, rows, seq, segs.data(), batch, s);
+  std::vector<int32_t> seg_rows(static_cast<size_t>(batch), seq);
+  int rc = run_segments(m, seg_rows.data(), batch, rows, seq, s);
   if (rc != OVB_OK) return rc;
   if (logits &&
       (ovb::launch_permute_logits(m->logits.as<float>(), m->logits_perm.as<float>(), batch, seq,

@@ -4,6 +4,7 @@
 // They are what LM::forward / LM::forward_cfg (cpp/src/model/lm.cpp:343-454)
 // run between the hot-path kernels, so that a whole forward stays on the
 // device (ovb_lm_*, lm.cpp in this directory).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -18,6 +19,7 @@ __device__ int g_status_lm;
 namespace {
 
 constexpr int kErrLmIndex = 128;  // a token / codebook id outside its table (row left zero)
+constexpr int kErrLmF16Range = 16;  // a q / k / v value beyond the fp16 range
 
 // One row of an embedding table as Emb::gather reads it (mat.cpp:52-66):
 // int8 entries times the row's scale, or fp32 entries.
@@ -119,6 +121,69 @@ __global__ void qk_norm_rope_kernel(float* q, float* k, const float* qw, const f
   }
 }
 
+// The same q / k normalisation and rotation, written as fp16 into q16 / k16
+// (the attention's operands), and v converted to fp16 into v16, in one pass
+// over the row; q, k, v (fp32, from the q|k|v GEMM) are only read.  A value
+// beyond the fp16 range sets status bit 16.
+__global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const float* v,
+                                        __half* q16, __half* k16, __half* v16, const float* qw,
+                                        const float* kw, const int64_t* pos,
+                                        const float* inv_freq, int64_t rows, int n_heads,
+                                        int n_kv, float eps) {
+  constexpr int D = 128, half = 64;
+  __shared__ float cs_s[half], sn_s[half];
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  if (threadIdx.x < half) {
+    const float angle = __fmul_rn(static_cast<float>(pos[r]), inv_freq[threadIdx.x]);
+    cs_s[threadIdx.x] = cosf(angle);
+    sn_s[threadIdx.x] = sinf(angle);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = static_cast<int>(blockDim.x >> 5);
+  bool range_ok = true;
+  for (int h = warp; h < n_heads + 2 * n_kv; h += nw) {
+    if (h >= n_heads + n_kv) {  // v: convert only
+      const int64_t base = (r * n_kv + (h - n_heads - n_kv)) * D;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = v[base + lane + 32 * j];
+        range_ok = range_ok && fabsf(x) <= 65504.f;
+        v16[base + lane + 32 * j] = __float2half_rn(x);
+      }
+      continue;
+    }
+    const bool is_q = h < n_heads;
+    const int64_t base = is_q ? (r * n_heads + h) * D : (r * n_kv + (h - n_heads)) * D;
+    const float* src = is_q ? q + base : k + base;
+    __half* dst = is_q ? q16 + base : k16 + base;
+    const float* w = is_q ? qw : kw;
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = src[lane + 32 * j];
+    float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
+                          __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float scale =
+        __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(D)), eps)));
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = lane + 32 * j;  // 0 .. 63
+      const float cs = cs_s[i], sn = sn_s[i];
+      const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
+      const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
+      const float lo = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+      const float hi = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+      range_ok = range_ok && fabsf(lo) <= 65504.f && fabsf(hi) <= 65504.f;
+      dst[i] = __float2half_rn(lo);
+      dst[i + half] = __float2half_rn(hi);
+    }
+  }
+  if (!range_ok) atomicOr(&g_status_lm, kErrLmF16Range);
+}
+
 // [B*S, C*V] -> [B, C, S, V] (lm.cpp:387-398).  One block per (b, s) row.
 __global__ void permute_logits_kernel(const float* src, float* dst, int S, int C, int V) {
   const int64_t r = blockIdx.x;
@@ -148,6 +213,15 @@ cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float
                                 int n_heads, int n_kv, float eps, cudaStream_t s) {
   return launch_plain(qk_norm_rope_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s, q,
                       k, qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
+}
+
+cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float* v, void* q16,
+                                    void* k16, void* v16, const float* qw, const float* kw,
+                                    const int64_t* pos, const float* inv_freq, int64_t rows,
+                                    int n_heads, int n_kv, float eps, cudaStream_t s) {
+  return launch_plain(qk_norm_rope_f16_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s,
+                      q, k, v, static_cast<__half*>(q16), static_cast<__half*>(k16),
+                      static_cast<__half*>(v16), qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
 }
 
 cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,

@@ -216,6 +216,44 @@ struct AttnArgs {
   AttnSeg segs[kAttMaxSegs];
 };
 cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s);
+// The fp16-operand attention (attention_h_kernel): one CTA per (segment, 128
+// query rows, kv head, pair of query heads), numbered from the segment's cta0.
+struct AttnHSeg {
+  const float* bias;  // [rows, rows] additive (no tile table), or null
+  int64_t q_off;      // element offset of the segment's first query row (out)
+  int rows;
+  int cta0;
+  int q_x, q_y;       // q_off = q_y * q_stride + q_x
+  int kv_x, kv_y;
+  int tile0;          // the segment's first entry in the tile table
+};
+struct AttnHArgs {
+  // fp16 2-D maps {row stride, rows}, box 64 x 128, 128-byte swizzle
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  float* out;
+  int64_t q_stride;
+  int n_heads;
+  int n_kv;
+  int group;
+  int pairs;          // CTAs per (query block, kv head): ceil(group / 2)
+  int n_segs;
+  float scale;
+  const uint8_t* tile_class;  // [tiles] 0 / 1 / 3, or null (then the biases)
+  const uint32_t* tile_bits;  // [tiles][128 rows][4 words]
+  AttnHSeg segs[kAttMaxSegs];
+};
+cudaError_t launch_attention_h(const AttnHArgs& args, int ctas, cudaStream_t s);
+struct AttnTilesArgs {
+  const uint8_t* masks;         // the segments' [rows, rows] u8 masks, concatenated
+  int n_segs;
+  int rows[kAttMaxSegs];
+  int tile0[kAttMaxSegs];
+  int64_t mask_off[kAttMaxSegs];
+};
+cudaError_t launch_attn_tiles(const AttnTilesArgs& a, int tiles, uint8_t* cls, uint32_t* bits,
+                              cudaStream_t s);
 // LM forward steps (lm_ops.cu).  An embedding table on the device: int8
 // rows with one fp32 scale per row, or fp32 rows.
 struct EmbTable {
@@ -234,6 +272,12 @@ cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float
                                 int n_heads, int n_kv, float eps, cudaStream_t s);
 cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,
                                   cudaStream_t s);
+// q / k RMSNorm + RoPE written as fp16 (q16, k16) and v converted to fp16
+// (v16): the operands of ovb_attention_h.
+cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float* v, void* q16,
+                                    void* k16, void* v16, const float* qw, const float* kw,
+                                    const int64_t* pos, const float* inv_freq, int64_t rows,
+                                    int n_heads, int n_kv, float eps, cudaStream_t s);
 cudaError_t read_and_clear_status_lm(int* out, cudaStream_t s);
 cudaError_t read_and_clear_status_att(int* out, cudaStream_t s);
 // Index into kTileNF of the tile width used by the fp16 mainloop.
