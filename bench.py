@@ -865,8 +865,10 @@ def attention_flops() -> int:
 
 
 def time_attention(dev, stream, launches: int = 32, sets: int = 4) -> dict:
-    """Device time per ovb_attention launch, CUDA events around a graph of
-    `launches` launches rotating over `sets` q/k/v sets (4 x 34 MB > L2)."""
+    """Device time per launch of the fp16-operand attention the LM runs
+    (ovb_attention_h, the padding masks as a tile table) and of the
+    fp32-operand ovb_attention, CUDA events around a graph of `launches`
+    launches rotating over `sets` q/k/v sets (4 x 34 MB > L2)."""
     import torch
     import ovnative_b200 as ovb
     at = ATTENTION
@@ -874,37 +876,34 @@ def time_attention(dev, stream, launches: int = 32, sets: int = 4) -> dict:
     gen.manual_seed(17)
     qs, ks, vs, segs = _attention_inputs(dev, gen, sets)
     outs = [torch.empty_like(q) for q in qs]
+    q16s, k16s, v16s = ([t.half() for t in ts] for ts in (qs, ks, vs))
+    masks = torch.cat([(b > -1e29).to(torch.uint8).reshape(-1) for b, _, _, _ in segs])
+    tiles = ovb.attention_tiles([r for _, r, _, _ in segs], masks)
+    segs_t = [(None, r, qo, ko) for _, r, qo, ko in segs]
     scale = 1.0 / float(np.sqrt(at["head_dim"]))
 
-    def one(i):
+    def one_h(i):
+        j = i % sets
+        ovb.attention_h(q16s[j], k16s[j], v16s[j], segs_t, at["n_heads"], at["n_kv"], scale,
+                        out=outs[j], tiles=tiles)
+
+    def one_f32(i):
         j = i % sets
         ovb.attention(qs[j], ks[j], vs[j], segs, at["n_heads"], at["n_kv"], scale, out=outs[j])
 
-    with torch.cuda.stream(stream):
-        for i in range(3):
-            one(i)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(launches):
-                one(i)
-        g.replay()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        g.replay()
-        e1.record(stream)
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / launches
-    del g
+    us = _graph_time_us(stream, one_h, launches)
+    us32 = _graph_time_us(stream, one_f32, launches)
     flops = attention_flops()
     peaks = load_peaks()
     achieved = flops / (us * 1e-6) / 1e12
-    return {"kernel": "attention_kernel (one CTA per segment x head x 128 query rows; "
-                      "tcgen05 kind::f16, S and P v in TMEM)",
+    return {"kernel": "attention_h_kernel (one CTA per segment x 128 query rows x kv head x "
+                      "pair of query heads; fp16 q/k/v, tcgen05 kind::f16, S/P/O in TMEM)",
             "config": dict(at), "us_per_launch": us, "bound": "tensor",
             "algorithmic_flops": flops, "achieved": achieved, "peak": peaks["bf16_tflops"],
             "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-            "peak_source": peaks["source"], "l2": "4 q/k/v sets rotated, 137 MB > L2"}
+            "peak_source": peaks["source"], "l2": "4 q/k/v sets rotated, 137 MB > L2",
+            "fp32_operands": {"kernel": "attention_kernel (ovb_attention)", "us_per_launch": us32,
+                              "frac": flops / (us32 * 1e-6) / 1e12 / peaks["bf16_tflops"]}}
 
 
 def attention_cpu_baseline(budget_s: float = 1.0) -> dict:
@@ -1064,20 +1063,29 @@ def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
         r["us_per_forward"] = round(us * per_fwd, 1)
         r["traffic"] = None
         entries.append(r)
-    # attention over the batch's segments (bias: the first 8 keys padded)
-    segs, r0 = [], 0
-    for rows in seg_rows:
-        bias = torch.zeros((rows, rows), device=dev)
-        bias[:, :min(8, rows - 1)] = -1e30
-        segs.append((bias, rows, r0 * QD, r0 * KVD))
+    # attention over the batch's segments with the LM's operands: fp16 q / k /
+    # v and the tile table of the CFG masks (cond: all attended; uncond: the
+    # target slice, then the tail rows seeing themselves, tts.cpp:186-198)
+    segs, r0, masks = [], 0, []
+    for si, rows in enumerate(seg_rows):
+        mk = np.ones((rows, rows), np.uint8)
+        if si % 2 == 1:
+            T = max(1, rows - 40)
+            mk[:] = 0
+            mk[:T, :T] = 1
+            mk[np.arange(T, rows), np.arange(T, rows)] = 1
+        masks.append(mk.reshape(-1))
+        segs.append((None, rows, r0 * QD, r0 * KVD))
         r0 += rows
+    tiles = ovb.attention_tiles(seg_rows, torch.from_numpy(np.concatenate(masks)).to(dev))
+    q16, k16, v16 = q.half(), k.half(), v.half()
     scale = 1.0 / float(np.sqrt(128))
-    us = _graph_time_us(stream, lambda i: ovb.attention(q, k, v, segs, 16, 8, scale, out=out),
-                        launches)
+    us = _graph_time_us(stream, lambda i: ovb.attention_h(q16, k16, v16, segs, 16, 8, scale,
+                                                          out=out, tiles=tiles), launches)
     flops = sum(4 * r * r * 128 * 16 for r in seg_rows)
     peaks = load_peaks()
     ach = flops / (us * 1e-6) / 1e12
-    entries.append({"kernel": f"attention_kernel ({len(seg_rows)} segments, {M} rows)",
+    entries.append({"kernel": f"attention_h_kernel ({len(seg_rows)} segments, {M} rows)",
                     "bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
                     "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
                     "peak_source": peaks["source"] + " bf16 burst",
