@@ -502,6 +502,10 @@ struct AttnHCtl {
   int abort;
   int n_act;
   int16_t act[kHMaxTiles];  // key tiles with something to attend, in order
+  // how each active tile's scores are formed: 0 plain (every key attended and
+  // inside the segment), 1 masked (class-1 bits and / or the segment's end),
+  // 2 biased (the segment's fp32 bias, no table)
+  int8_t kind[kHMaxTiles];
 };
 constexpr size_t kAttHSmem = 1024 + kHOffCtl + sizeof(AttnHCtl);
 static_assert(kAttHSmem <= 227 * 1024, "attention_h shared memory");
@@ -567,8 +571,11 @@ __global__ void __launch_bounds__(kHThreads, 1)
     ctl->abort = 0;
     int n = 0;
     for (int j = 0; j < nkt; ++j) {
-      const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : 0;
-      if (cls != 3) ctl->act[n++] = static_cast<int16_t>(j);
+      const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : (sg.bias ? 2 : 0);
+      if (cls == 3) continue;
+      ctl->act[n] = static_cast<int16_t>(j);
+      ctl->kind[n] = static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > S ? 1 : 0));
+      ++n;
     }
     ctl->n_act = n;
     fence_mbar_init();
@@ -698,37 +705,66 @@ __global__ void __launch_bounds__(kHThreads, 1)
         tc_fence_after();
         const int j = ctl->act[i];
         const int key0 = j * 128;
-        const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j]
-                                        : (sg.bias ? 2 : 0);
-        uint4 bits = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
-        if (cls == 1)
-          bits = __ldg(reinterpret_cast<const uint4*>(args.tile_bits) +
-                       (static_cast<int64_t>(sg.tile0 + qb * nkt + j) * 128 + r));
+        const int kind = ctl->kind[i];  // warp-uniform
         uint32_t u[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u[c]);
 #pragma unroll
         for (int c = 0; c < 4; ++c) tc_wait_ld32(u[c]);
-        const uint32_t bw[4] = {bits.x, bits.y, bits.z, bits.w};
-        const float* brow = sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S;
-        float tmax = -INFINITY;
+        // Pass 1: the tile maximum in base-2 units.  A plain tile needs only the
+        // maximum of the raw scores (scale > 0); the others form every score
+        // x (masked keys -inf) in place.
+        float tmax, mul;
+        if (kind == 0) {
+          float mr = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = key0 + c * 32 + e;
-            float x;
-            if (cls == 2) {
-              const float b = (row_ok && key < S) ? brow[key] : 0.f;
-              x = __fmul_rn(__fadd_rn(__fmul_rn(__uint_as_float(u[c][e]), args.scale), b), kLog2e);
-            } else {
-              x = __fmul_rn(__uint_as_float(u[c][e]), sl2);
-            }
-            const bool on = key < S && ((bw[c] >> e) & 1u);
-            x = on ? x : -INFINITY;
-            tmax = fmaxf(tmax, x);
-            u[c][e] = __float_as_uint(x);
+            for (int e = 0; e < 32; ++e) mr = fmaxf(mr, __uint_as_float(u[c][e]));
+          tmax = __fmul_rn(mr, sl2);
+          mul = sl2;
+        } else {
+          uint32_t bw[4];
+          if (args.tile_class && args.tile_class[sg.tile0 + qb * nkt + j] == 1) {
+            const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(args.tile_bits) +
+                                   (static_cast<int64_t>(sg.tile0 + qb * nkt + j) * 128 + r));
+            bw[0] = b4.x; bw[1] = b4.y; bw[2] = b4.z; bw[3] = b4.w;
+          } else {
+            bw[0] = bw[1] = bw[2] = bw[3] = 0xffffffffu;
           }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {  // keys past the segment's end
+            const int vc = S - key0 - 32 * c;
+            bw[c] &= vc >= 32 ? 0xffffffffu : (vc <= 0 ? 0u : (1u << vc) - 1u);
+          }
+          tmax = -INFINITY;
+          if (kind == 1) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const float x = ((bw[c] >> e) & 1u) ? __fmul_rn(__uint_as_float(u[c][e]), sl2)
+                                                    : -INFINITY;
+                tmax = fmaxf(tmax, x);
+                u[c][e] = __float_as_uint(x);
+              }
+          } else {
+            const float* brow = sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S + key0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const bool on = row_ok && ((bw[c] >> e) & 1u);
+                const float b = on ? brow[c * 32 + e] : 0.f;
+                const float x =
+                    on ? __fmul_rn(__fadd_rn(__fmul_rn(__uint_as_float(u[c][e]), args.scale), b),
+                                   kLog2e)
+                       : -INFINITY;
+                tmax = fmaxf(tmax, x);
+                u[c][e] = __float_as_uint(x);
+              }
+          }
+          mul = 1.f;
         }
         mt = fmaxf(mt, tmax);
         float factor = 1.f;
@@ -749,16 +785,18 @@ __global__ void __launch_bounds__(kHThreads, 1)
             tmem_st16(o_col + static_cast<uint32_t>(c * 16), o);
           }
         }
-        const float mexp = m == -INFINITY ? 0.f : m;
+        // Pass 2: P = 2^(x - m), x = u * mul (the raw score times scale log2 e
+        // on a plain tile, x itself otherwise), one FFMA and one ex2 each.
+        const float nm = m == -INFINITY ? 0.f : -m;
         float sum = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(__uint_as_float(u[c][2 * e]) - mexp);
-            const float p1 = ex2_approx(__uint_as_float(u[c][2 * e + 1]) - mexp);
-            sum += p0 + p1;
+            const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(u[c][2 * e]), mul, nm));
+            const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(u[c][2 * e + 1]), mul, nm));
+            sum = __fadd_rn(sum, __fadd_rn(p0, p1));
             pk[e] = pack2(p0, p1);
           }
           tmem_st16(s_col + static_cast<uint32_t>(c * 16), pk);
