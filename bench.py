@@ -1451,10 +1451,40 @@ def main():
                     help="only time loading a synthetic OVW1 checkpoint's int8 weights")
     ap.add_argument("--attention-only", action="store_true",
                     help="only time the attention (one q/k/v set, 8 launches; for ncu)")
+    ap.add_argument("--profile-forward", action="store_true",
+                    help="build the 28-layer LM and the largest config-4 batch of one GPU and run "
+                         "two eager forwards + samplers (for an ncu launch list)")
     ap.add_argument("--sampler-only", action="store_true",
                     help="only time the guided sampler (one plane set, 8 launches; for "
                          "profiling runs) and print its entry")
     args = ap.parse_args()
+    if args.profile_forward:
+        import shutil
+
+        import torch
+
+        from ovnative_b200 import lm as LM
+        from ovnative_b200 import shard
+        from ovnative_b200 import tts_batch as TB
+        dev = torch.device("cuda", 0)
+        path, tmpdir = shared_checkpoint(0, 1)
+        try:
+            lengths = utterance_lengths()
+            uids = shard.lpt_assign([lengths[i] for i in range(len(lengths))], 1)[0]
+            m = LM.LM(path, f16=args.numerics == "fp16")
+            st = torch.cuda.Stream(device=dev)
+            sp = TB.Stepper(m, lengths, uids, dev, st, max_rows=MAX_ROWS)
+            b = max(sp.batches, key=lambda x: x.rows)
+            with torch.cuda.stream(st):
+                for _ in range(2):
+                    b.run()
+            torch.cuda.synchronize()
+            print(json.dumps({"rows": b.rows, "pairs": len(b.pairs), "segments": len(b.seg_rows)}),
+                  flush=True)
+            m.close()
+        finally:
+            shutil.rmtree(tmpdir, ignore_errors=True)
+        return
     if args.sampler_only:
         import torch
         dev = torch.device("cuda", 0)

@@ -334,6 +334,19 @@ int ovb_attention(const float* q, const float* k, const float* v, float* out, in
 int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
                     int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
                     const ovb_attn_segment* segs, int n_segs, const void* tiles, void* stream);
+/* ovb_attention_h followed by ovb_quantize of its output (the o
+ * projection's input, LM::run_layer lm.cpp:281 quantising inside
+ * linear_s8_nk_packed_add), in one kernel: every query row's head output is
+ * four whole 32-k blocks, quantised as the output is formed and written in
+ * the form `flags` selects (0 int8 q / OVB_AQ_U8 / OVB_AQ_F16) into aq
+ * [rows, n_heads * head_dim] and its scales into asc [rows, n_heads *
+ * head_dim / 32] -- bit-identical to the two calls, without the fp32
+ * output.  Needs q_stride == n_heads * head_dim and segment offsets at whole
+ * rows; rows are those of the q view.  No counterpart in the reference. */
+int ovb_attention_h_q(const void* q, const void* k, const void* v, int64_t q_stride,
+                      int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                      const ovb_attn_segment* segs, int n_segs, const void* tiles, void* aq,
+                      float* asc, int flags, void* stream);
 /* Bytes of the tile table of a segment list (seg_rows: host array of the
  * segments' row counts): per (segment, 128-query block, 128-key tile) a
  * class byte and 2 KB of mask bits. */

@@ -33,5 +33,5 @@ from .gemm import (  # noqa: F401
     to_f16,
     workspace_bytes,
 )
-from .attention import attention, attention_h, attention_tiles  # noqa: F401
+from .attention import attention, attention_h, attention_h_q, attention_tiles  # noqa: F401
 from .sampler import guided_sample  # noqa: F401

@@ -108,6 +108,8 @@ SIGNATURES = {
                        C.POINTER(AttnSegment), _int, _p], _int),
     "ovb_attention_h": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
                          C.POINTER(AttnSegment), _int, _p, _p], _int),
+    "ovb_attention_h_q": ([_p, _p, _p, _i64, _i64, _int, _int, _int, C.c_float,
+                           C.POINTER(AttnSegment), _int, _p, _p, _p, _int, _p], _int),
     "ovb_attention_tiles_bytes": ([_p, _int], C.c_size_t),
     "ovb_attention_tiles": ([_p, _int, _p, _p, C.c_size_t, _p], _int),
 }

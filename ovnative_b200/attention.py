@@ -119,3 +119,36 @@ def attention_h(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, segs, n
                                     None if tiles is None else tiles.data_ptr(),
                                     torch.cuda.current_stream().cuda_stream))
     return out
+
+
+def attention_h_q(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, segs, n_heads: int,
+                  n_kv: int, scale: float, tiles: torch.Tensor | None = None, u8: bool = False,
+                  f16: bool = False):
+    """ovb_attention_h_q: attention_h with ovb_quantize of its output fused
+    into the epilogue.  Returns (aq, asc) in the form the flags select (int8
+    q, u8 q+128 or fp16 q*asc) for the q rows [T, n_heads * 128]."""
+    from .gemm import empty_quant, empty_quant_f16
+    T, QD = q16.shape
+    if f16:
+        aq, asc = empty_quant_f16(T, QD, q16.device)
+    else:
+        aq, asc = empty_quant(T, QD, q16.device)
+        if u8:
+            aq = aq.view(torch.uint8)
+    segs = list(segs)
+    arr = (L.AttnSegment * max(1, len(segs)))()
+    keep = []
+    for i, (bias, rows, q_off, kv_off) in enumerate(segs):
+        bp = None
+        if bias is not None and tiles is None:
+            keep.append(bias)
+            bp = bias.data_ptr()
+        arr[i] = L.AttnSegment(bp, int(rows), int(q_off), int(kv_off))
+    flags = (L.OVB_AQ_U8 if u8 else 0) | (L.OVB_AQ_F16 if f16 else 0)
+    L.check(L.lib().ovb_attention_h_q(q16.data_ptr(), k16.data_ptr(), v16.data_ptr(), QD,
+                                      k16.shape[1], n_heads, n_kv, HEAD_DIM, float(scale),
+                                      C.cast(arr, C.POINTER(L.AttnSegment)), len(segs),
+                                      None if tiles is None else tiles.data_ptr(), aq.data_ptr(),
+                                      asc.data_ptr(), flags,
+                                      torch.cuda.current_stream().cuda_stream))
+    return aq, asc

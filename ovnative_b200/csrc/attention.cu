@@ -43,6 +43,7 @@
 
 #include "ovb_internal.h"
 #include "ovb_ptx.cuh"
+#include "ovb_quant.cuh"
 
 namespace ovb {
 
@@ -812,8 +813,14 @@ __global__ void __launch_bounds__(kHThreads, 1)
       if (have_o) tc_fence_after();
       const bool masked = !(mt >= -1e29f * kLog2e);
       const float inv_l = masked || !(l > 0.f) ? 0.f : __frcp_rn(l);
-      float* orow = args.out + sg.q_off + static_cast<int64_t>(head0 + h) * 128 +
-                    static_cast<int64_t>(row_ok ? row : 0) * args.q_stride;
+      float* orow = args.out ? args.out + sg.q_off + static_cast<int64_t>(head0 + h) * 128 +
+                                   static_cast<int64_t>(row_ok ? row : 0) * args.q_stride
+                             : nullptr;
+      // quantised output: the head's 128 values are four whole 32-k blocks of
+      // the o projection's input row (q_x is 0: rows of the 2-D view)
+      const int64_t qrow = static_cast<int64_t>(sg.q_y) + (row_ok ? row : 0);
+      const int es = args.q_mode == 2 ? 2 : 1;
+      bool range_bad = false;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -824,7 +831,16 @@ __global__ void __launch_bounds__(kHThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
-        if (row_ok) {
+        if (!row_ok) continue;
+        if (args.q_out) {
+          float vq[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) vq[e] = __fmul_rn(__uint_as_float(o[e]), inv_l);
+          const int64_t blk = static_cast<int64_t>(head0 + h) * 4 + c;
+          const float bs = quant_block32(
+              vq, args.q_out + (qrow * args.q_kb * 32 + blk * 32) * es, args.q_mode, &range_bad);
+          args.q_asc[qrow * args.q_kb + blk] = bs;
+        } else {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
             *reinterpret_cast<float4*>(orow + c * 32 + e) =
@@ -834,6 +850,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
                             __fmul_rn(__uint_as_float(o[e + 3]), inv_l));
         }
       }
+      if (range_bad) atomicOr(&g_status_att, kErrAttRange);
     }
   }
   tc_fence_before();

@@ -1044,12 +1044,18 @@ int ovb_attention_tiles(const int32_t* seg_rows, int n_segs, const uint8_t* mask
   return OVB_OK;
 }
 
-int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
-                    int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
-                    const ovb_attn_segment* segs, int n_segs, const void* tiles, void* stream) {
+}  // extern "C"
+
+namespace {
+// ovb_attention_h and ovb_attention_h_q: `out` (fp32) or the quantised
+// output (q_out / q_asc in form q_mode) is written.
+int attention_h_impl(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
+                     int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                     const ovb_attn_segment* segs, int n_segs, const void* tiles, void* q_out,
+                     float* q_asc, int q_mode, void* stream) {
   if (n_segs == 0) return OVB_OK;
   if (n_segs < 0 || n_segs > ovb::kAttMaxSegs) return invalid("n_segs must be in [0, 64]");
-  if (!segs || !q || !k || !v || !out) return invalid("q/k/v/out/segs must be non-null");
+  if (!segs || !q || !k || !v || (!out && !q_out)) return invalid("q/k/v/out/segs must be non-null");
   if (head_dim != 128) return invalid("head_dim must be 128");
   if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0)
     return invalid("n_heads must be a positive multiple of n_kv");
@@ -1059,6 +1065,11 @@ int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int
       q_stride % 8 != 0 || kv_stride % 8 != 0)
     return invalid("q/k/v/out must be 16-byte aligned with strides a multiple of 8");
   if (tiles && !aligned(tiles, 256)) return invalid("tiles must be 256-byte aligned");
+  if (q_out) {
+    if (!q_asc || !aligned(q_out, 16) || !aligned(q_asc, 4)) return invalid("misaligned aq/asc");
+    if (q_stride != int64_t{n_heads} * head_dim)
+      return invalid("the quantised output needs q_stride == n_heads * head_dim");
+  }
   if (q_stride > (int64_t{1} << 30) || kv_stride > (int64_t{1} << 30))
     return invalid("row strides too large");
   ovb::AttnHArgs a = {};
@@ -1097,6 +1108,7 @@ int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int
       return invalid("segment offset leaves no room for every head within a row");
     if (qy + g.rows > (int64_t{1} << 31) - 1 - 128 || ky + g.rows > (int64_t{1} << 31) - 1 - 128)
       return invalid("segment rows too large");
+    if (q_out && qx != 0) return invalid("the quantised output needs row-aligned segment offsets");
     ovb::AttnHSeg& d = a.segs[a.n_segs++];
     d.bias = tiles ? nullptr : g.bias;
     d.q_off = g.q_off;
@@ -1125,10 +1137,39 @@ int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int
       !ovb::encode_tmap_2d(&a.tm_v, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kv_stride, kv_rows,
                            kv_stride * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return OVB_ERR_INTERNAL;
+  if (q_out) {
+    a.q_out = static_cast<uint8_t*>(q_out);
+    a.q_asc = q_asc;
+    a.q_mode = q_mode;
+    a.q_kb = n_heads * head_dim / 32;
+    a.out = nullptr;
+  }
   if (cuda_failed(ovb::launch_attention_h(a, static_cast<int>(ctas), as_stream(stream)),
                   "attention_h launch"))
     return OVB_ERR_INTERNAL;
   return OVB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ovb_attention_h(const void* q, const void* k, const void* v, float* out, int64_t q_stride,
+                    int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                    const ovb_attn_segment* segs, int n_segs, const void* tiles, void* stream) {
+  if (n_segs > 0 && !out) return invalid("out must be non-null");
+  return attention_h_impl(q, k, v, out, q_stride, kv_stride, n_heads, n_kv, head_dim, scale,
+                          segs, n_segs, tiles, nullptr, nullptr, 0, stream);
+}
+
+int ovb_attention_h_q(const void* q, const void* k, const void* v, int64_t q_stride,
+                      int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
+                      const ovb_attn_segment* segs, int n_segs, const void* tiles, void* aq,
+                      float* asc, int flags, void* stream) {
+  const int mode = quant_mode(flags);
+  if (mode < 0 || mode == 3) return invalid("flags: 0, OVB_AQ_U8 or OVB_AQ_F16");
+  if (n_segs > 0 && (!aq || !asc)) return invalid("aq/asc must be non-null");
+  return attention_h_impl(q, k, v, nullptr, q_stride, kv_stride, n_heads, n_kv, head_dim, scale,
+                          segs, n_segs, tiles, aq, asc, mode, stream);
 }
 
 }  // extern "C"

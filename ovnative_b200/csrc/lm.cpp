@@ -5,8 +5,9 @@
 //
 // Per layer (LM::run_layer, lm.cpp:217-322): RMSNorm + quantise -> q|k|v
 // GEMM -> per-head RMSNorm + RoPE (written as fp16 q / k, with v as fp16) ->
-// attention over the segments (ovb_attention_h; the masks as a tile table
-// built once per forward) -> quantise
+// attention over the segments with the o projection's quantiser in its
+// epilogue (ovb_attention_h_q; the masks as a tile table built once per
+// forward)
 // -> o GEMM += x -> RMSNorm + quantise -> gate|up GEMM fused with SiLU*up +
 // quantise -> down GEMM += x.  Then the final RMSNorm + quantise and the
 // audio-heads GEMM.  The linear weights are int8 (either OVW1 orientation)
@@ -77,7 +78,7 @@ struct ovb_lm {
   DevBuf norms, emb, offsets, inv_freq;
   ovb::EmbTable tok{}, aud{};
   // forward buffers (grown on demand)
-  DevBuf x, aq, asc, q, k, v, attn, qi, asci, logits, logits_perm, ids, amask, pos, masks;
+  DevBuf x, aq, asc, q, k, v, qi, asci, logits, logits_perm, ids, amask, pos, masks;
   DevBuf q16, k16, v16;  // fp16 q / k (normalised, rotated) and v: the attention's operands
   DevBuf tiles;          // the attention's mask tile table (ovb_attention_tiles)
   DevBuf pred, scores;  // ovb_lm_sample's device outputs
@@ -338,7 +339,7 @@ bool reserve(ovb_lm* m, int64_t rows, int64_t mask_elems) {
   return m->x.grow(r * H * 4) && m->aq.grow(r * std::max<int64_t>(KM * ab, H * 2)) &&
          m->asc.grow(r * (KM / 32) * 4) &&
          m->q.grow(r * QD * 4) && m->k.grow(r * KVD * 4) && m->v.grow(r * KVD * 4) &&
-         m->attn.grow(r * QD * 4) && m->qi.grow(r * m->inter * ab) &&
+         m->qi.grow(r * m->inter * ab) &&
          m->asci.grow(r * (m->inter / 32) * 4) && m->logits.grow(r * CV * 4) &&
          m->ids.grow(r * m->n_codebooks * 8) && m->amask.grow(r) && m->pos.grow(r * 8) &&
          m->masks.grow(static_cast<size_t>(mask_elems)) && m->q16.grow(r * QD * 2) &&
@@ -374,9 +375,9 @@ int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_se
                                      m->pos.as<int64_t>(), m->inv_freq.as<float>(), rows,
                                      m->n_heads, m->n_kv, m->eps, s) != cudaSuccess)
       return internal("qk norm / rope launch failed");
-    OVB_LM_TRY(ovb_attention_h(m->q16.p, m->k16.p, m->v16.p, m->attn.as<float>(), QD, KVD,
-                               m->n_heads, m->n_kv, 128, scale, segs, n_segs, tiles, s));
-    OVB_LM_TRY(ovb_quantize(rows, QD, m->attn.as<float>(), QD, aq, asc, qf, s));
+    // attention with the o projection's quantiser in its epilogue
+    OVB_LM_TRY(ovb_attention_h_q(m->q16.p, m->k16.p, m->v16.p, QD, KVD, m->n_heads, m->n_kv, 128,
+                                 scale, segs, n_segs, tiles, aq, asc, qf, s));
     OVB_LM_TRY(m->f16 ? ovb_linear_h(rows, L.o, aq, x, H, 1, s)
                       : ovb_linear_q(rows, L.o, aq, asc, x, H, 1, s));
     OVB_LM_TRY(ovb_rmsnorm_quantize(rows, H, x, L.post_ln, m->eps, aq, asc, qf, s));

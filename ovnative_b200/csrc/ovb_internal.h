@@ -242,6 +242,13 @@ struct AttnHArgs {
   float scale;
   const uint8_t* tile_class;  // [tiles] 0 / 1 / 3, or null (then the biases)
   const uint32_t* tile_bits;  // [tiles][128 rows][4 words]
+  // When q_out is set, the output is written quantised instead of to `out`:
+  // ovb_quantize's form q_mode (0 int8 q, 1 u8, 2 fp16 q*asc) into q_out
+  // [rows, q_kb * 32] and the block scales into q_asc [rows, q_kb].
+  uint8_t* q_out;
+  float* q_asc;
+  int q_mode;
+  int q_kb;
   AttnHSeg segs[kAttMaxSegs];
 };
 cudaError_t launch_attention_h(const AttnHArgs& args, int ctas, cudaStream_t s);

@@ -187,3 +187,29 @@ def test_matches_fp32_entry_point(cuda):
     a = ovb.attention(tq, tk, tv, tsegs, 16, 8, scale).cpu().numpy()
     b = run_h(q, k, v, segs, 16, 8, scale, cuda, "table")
     assert np.linalg.norm(a - b) <= 1e-3 * np.linalg.norm(a)
+
+
+@pytest.mark.parametrize("form", ["int8", "u8", "fp16"])
+@pytest.mark.parametrize("mode", MODES)
+def test_fused_quantised_output_equals_quantise_of_output(form, mode, cuda):
+    """ovb_attention_h_q writes exactly ovb_quantize(ovb_attention_h(...)):
+    the same fp32 values, quantised per 32-k block in the epilogue."""
+    rng = np.random.default_rng(41)
+    q, k, v, segs = make_case(rng, (300, 97, 150), 16, 8, masked_rows=(2,), pad_keys=4)
+    scale = 1.0 / np.sqrt(D)
+    tq, tk, tv = (torch.from_numpy(x.astype(np.float16)).to(cuda) for x in (q, k, v))
+    if mode == "bias":
+        tsegs = [(torch.from_numpy(b).to(cuda), r, qo, ko) for b, r, qo, ko in segs]
+        tiles = None
+    else:
+        tsegs = [(None, r, qo, ko) for _, r, qo, ko in segs]
+        masks = np.concatenate([(b > -1e29).astype(np.uint8).reshape(-1) for b, _, _, _ in segs])
+        tiles = ovb.attention_tiles([r for _, r, _, _ in segs], torch.from_numpy(masks).to(cuda))
+    kw = {"u8": form == "u8", "f16": form == "fp16"}
+    out = ovb.attention_h(tq, tk, tv, tsegs, 16, 8, scale, tiles=tiles)
+    want_q, want_s = ovb.s8_nk_quantize(out, **kw)
+    got_q, got_s = ovb.attention_h_q(tq, tk, tv, tsegs, 16, 8, scale, tiles=tiles, **kw)
+    torch.cuda.synchronize()
+    assert ovb.device_status() == 0
+    assert torch.equal(got_q.view(torch.uint8), want_q.view(torch.uint8))
+    assert torch.equal(got_s, want_s)
