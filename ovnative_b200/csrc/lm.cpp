@@ -82,9 +82,15 @@ struct ovb_lm {
   DevBuf q16, k16, v16;  // fp16 q / k (normalised, rotated) and v: the attention's operands
   DevBuf tiles;          // the attention's mask tile table (ovb_attention_tiles)
   DevBuf pred, scores;  // ovb_lm_sample's device outputs
+  // pinned host staging of the logits for the host-buffer forwards: one
+  // device-to-host copy at full link speed, then a host copy into the
+  // caller's (pageable) array
+  void* stage = nullptr;
+  size_t stage_n = 0;
   int64_t last_rows = 0;
 
   ~ovb_lm() {
+    if (stage) cudaFreeHost(stage);
     for (Layer& L : layers)
       for (ovb_weight* w : {L.qkv, L.o, L.gate_up, L.down})
         if (w) ovb_weight_destroy(w);
@@ -440,6 +446,24 @@ struct DeviceScope {
   }
 };
 
+// Device logits -> the caller's host array through the pinned staging
+// buffer (grown on demand), synchronising the stream.
+int copy_logits_out(ovb_lm* m, const float* dev, size_t bytes, float* host, cudaStream_t s) {
+  if (bytes > m->stage_n) {
+    if (m->stage) cudaFreeHost(m->stage);
+    m->stage = nullptr;
+    m->stage_n = 0;
+    if (cudaHostAlloc(&m->stage, bytes, cudaHostAllocDefault) != cudaSuccess)
+      return internal("cudaHostAlloc(logits staging) failed");
+    m->stage_n = bytes;
+  }
+  if (cudaMemcpyAsync(m->stage, dev, bytes, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return internal("logits copy failed");
+  std::memcpy(host, m->stage, bytes);
+  return OVB_OK;
+}
+
 int finish(ovb_lm* m, cudaStream_t s) {
   (void)m;
   if (cudaStreamSynchronize(s) != cudaSuccess) return internal("forward failed on the device");
@@ -568,9 +592,10 @@ int ovb_lm_forward_cfg(ovb_lm* m, int cond_seq, int uncond_seq, const int64_t* i
   int rc = run_segments(m, seg_rows, 2, rows, static_cast<int>(rows), s);
   if (rc != OVB_OK) return rc;
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
-  if (logits &&
-      cudaMemcpyAsync(logits, m->logits.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
-    return internal("logits copy failed");
+  if (logits) {
+    rc = copy_logits_out(m, m->logits.as<float>(), static_cast<size_t>(rows * CV * 4), logits, s);
+    if (rc != OVB_OK) return rc;
+  }
   return finish(m, s);
 }
 
@@ -595,12 +620,14 @@ int ovb_lm_forward(ovb_lm* m, int batch, int seq, const int64_t* ids, const uint
   std::vector<int32_t> seg_rows(static_cast<size_t>(batch), seq);
   int rc = run_segments(m, seg_rows.data(), batch, rows, seq, s);
   if (rc != OVB_OK) return rc;
-  if (logits &&
-      (ovb::launch_permute_logits(m->logits.as<float>(), m->logits_perm.as<float>(), batch, seq,
-                                  m->n_codebooks, m->audio_vocab, s) != cudaSuccess ||
-       cudaMemcpyAsync(logits, m->logits_perm.p, rows * CV * 4, cudaMemcpyDeviceToHost, s) !=
-           cudaSuccess))
-    return internal("logits copy failed");
+  if (logits) {
+    if (ovb::launch_permute_logits(m->logits.as<float>(), m->logits_perm.as<float>(), batch, seq,
+                                   m->n_codebooks, m->audio_vocab, s) != cudaSuccess)
+      return internal("logits permute failed");
+    rc = copy_logits_out(m, m->logits_perm.as<float>(), static_cast<size_t>(rows * CV * 4),
+                         logits, s);
+    if (rc != OVB_OK) return rc;
+  }
   return finish(m, s);
 }
 

@@ -60,6 +60,31 @@ class LM:
                                            torch.cuda.current_stream().cuda_stream))
         return out
 
+    def forward_cfg_sample(self, ids, amask, cond_attn, uncond_attn, pos, target_len: int,
+                           guidance: float = 2.0, layer_penalty: float = 5.0,
+                           mask_id: int = 1024):
+        """One TTS step the way the reference's CUDA path runs it (device
+        sampling, tts.cpp:270-282): LM::forward_cfg on host inputs with the
+        logits kept on the device, then the guided sampler on its two CFG
+        planes (cond at its last target_len rows, uncond at its first),
+        returning host (pred int32 [C, T], scores fp32 [C, T])."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        a = np.ascontiguousarray(amask, np.uint8)
+        cm = np.ascontiguousarray(cond_attn, np.uint8)
+        um = np.ascontiguousarray(uncond_attn, np.uint8)
+        pos = np.ascontiguousarray(pos, np.int64)
+        cs, us = cm.shape[0], um.shape[0]
+        stream = torch.cuda.current_stream().cuda_stream
+        L.check(L.lib().ovb_lm_forward_cfg(self._h, cs, us, _p(ids), _p(a), _p(cm), _p(um), _p(pos),
+                                           None, stream))
+        base = L.lib().ovb_lm_logits(self._h)
+        pred = np.empty((self.C, target_len), np.int32)
+        scores = np.empty((self.C, target_len), np.float32)
+        L.check(L.lib().ovb_lm_sample(self._h, base, cs, base + cs * self.C * self.V * 4, us,
+                                      target_len, guidance, layer_penalty, mask_id, _p(pred),
+                                      _p(scores), stream))
+        return pred, scores
+
     def forward(self, ids, amask, attn, pos) -> np.ndarray:
         """ids [B, C, S], amask [B, S], attn [B, S, S], pos [B, S] -> logits
         [B, C, S, V]."""
