@@ -143,12 +143,30 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = static_cast<int>(blockDim.x >> 5);
   bool range_ok = true;
-  for (int h = warp; h < n_heads + 2 * n_kv; h += nw) {
+  // Each warp's head vectors (q, then k, then v heads), loaded in groups of
+  // four before any of them is reduced, so that their loads are in flight
+  // together.
+  const int nvec = n_heads + 2 * n_kv;
+  for (int h0 = warp; h0 < nvec; h0 += 4 * nw) {
+    float xs[4][4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int h = h0 + g * nw;
+      const float* src = h < n_heads ? q + (r * n_heads + h) * D
+                         : h < n_heads + n_kv ? k + (r * n_kv + (h - n_heads)) * D
+                                              : v + (r * n_kv + (h - n_heads - n_kv)) * D;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xs[g][j] = h < nvec ? src[lane + 32 * j] : 0.f;
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+    const int h = h0 + g * nw;
+    if (h >= nvec) break;
     if (h >= n_heads + n_kv) {  // v: convert only
       const int64_t base = (r * n_kv + (h - n_heads - n_kv)) * D;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float x = v[base + lane + 32 * j];
+        const float x = xs[g][j];
         range_ok = range_ok && fabsf(x) <= 65504.f;
         v16[base + lane + 32 * j] = __float2half_rn(x);
       }
@@ -156,12 +174,11 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
     }
     const bool is_q = h < n_heads;
     const int64_t base = is_q ? (r * n_heads + h) * D : (r * n_kv + (h - n_heads)) * D;
-    const float* src = is_q ? q + base : k + base;
     __half* dst = is_q ? q16 + base : k16 + base;
     const float* w = is_q ? qw : kw;
     float x[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = src[lane + 32 * j];
+    for (int j = 0; j < 4; ++j) x[j] = xs[g][j];
     float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
                           __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
 #pragma unroll
@@ -179,6 +196,7 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
       range_ok = range_ok && fabsf(lo) <= 65504.f && fabsf(hi) <= 65504.f;
       dst[i] = __float2half_rn(lo);
       dst[i + half] = __float2half_rn(hi);
+    }
     }
   }
   if (!range_ok) atomicOr(&g_status_lm, kErrLmF16Range);

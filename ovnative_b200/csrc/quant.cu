@@ -482,9 +482,14 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
   }
   const int64_t blocks = (rows + warps - 1) / warps;
   const int grid = static_cast<int>(imin64(blocks, static_cast<int64_t>(num_sms(dev)) * 16));
+  // The block-per-row kernel spreads one row over four warps, which suits a
+  // few hundred rows; with many rows the warp-per-row kernel keeps four times
+  // as many rows (and their loads) in flight per SM.  Both follow the
+  // reference's order and write the same bytes.
   const bool small = cols <= kSmallCols && (cols & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+                     (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                     rows <= static_cast<int64_t>(num_sms(dev)) * 8;
   if (small) {
     const int sgrid = static_cast<int>(imin64(rows, static_cast<int64_t>(num_sms(dev)) * 16));
     auto* q8s = static_cast<uint8_t*>(aq);

@@ -84,6 +84,26 @@ def test_quantizers_lm_shapes_vs_port(cuda, M, K):
         assert_same(host(got[1]), want[1])
 
 
+@pytest.mark.parametrize("M", [1185, 15408])
+def test_rmsnorm_quantize_many_rows(cuda, M):
+    """Beyond 8 rows per SM the warp-per-row kernel runs: the same bytes as
+    the reference restatement, in the int8 / u8 forms and the fp16 form
+    fp16(q * asc)."""
+    rng = np.random.default_rng(M)
+    K = 1024
+    A = (rng.standard_normal((M, K)) * 4).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    want_q, want_s = O.rmsnorm_quantize(A, w, 1e-6)
+    got = ovb.rmsnorm_quantize_f32(dev(A, cuda), dev(w, cuda), 1e-6, u8=True)
+    assert_same(host(got[0]), want_q)
+    assert_same(host(got[1]), want_s)
+    a16, s16 = ovb.rmsnorm_quantize_f32(dev(A, cuda), dev(w, cuda), 1e-6, f16=True)
+    q = want_q.astype(np.int32) - 128
+    deq = (q.reshape(M, -1, 32).astype(np.float32) * want_s[:, :, None]).reshape(M, -1)
+    assert_same(host(a16), deq.astype(np.float16))
+    assert_same(host(s16), want_s)
+
+
 def test_strided_and_misaligned_inputs(cuda):
     rng = np.random.default_rng(5)
     M, K = 33, 200
