@@ -389,6 +389,178 @@ __global__ void __launch_bounds__(kSmallThreads) rmsnorm_quantize_small_kernel(
   }
 }
 
+// ------------------------------------ rmsnorm + quantize, rows in batches
+// For many rows of at most 1024 columns (cols % 32 == 0, 16-byte aligned x
+// and w): each warp takes four rows at a time.  The rows are staged in shared
+// memory (16-byte chunks XOR-swizzled by their 8-chunk group, and each row
+// slot padded by one chunk, so that both access patterns below are free of
+// bank conflicts); lanes 8g .. 8g + 7 run row g's eight reference-ordered
+// FMA chains (gemm.cpp:655-663) and every lane of the group forms the row's
+// scale; then, row by row, lane b quantises 32-k block b on its own: the
+// block scale's two IEEE divisions run once per block instead of once per
+// eight lanes, and the rounding uses the exact identity
+//   rne(y) = fl(y + 1.5 * 2^23) - 1.5 * 2^23   for |y| < 2^22
+// (|v * inv| <= 127 (1 + 2^-23) inside a finite block), so the bytes equal
+// quantize_a_u8's; a block holding a NaN or an infinity takes the
+// x86-conversion path of the other kernels.
+constexpr int kRows4 = 4;      // rows per warp
+constexpr int kRows4Warps = 4;  // warps per block
+
+__device__ __forceinline__ int swz4(int c) { return c ^ ((c >> 3) & 7); }
+
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kRows4Warps * 32) rmsnorm_quantize_rows4_kernel(
+    int64_t rows, int cols, const float* x, const float* w, float eps, uint8_t* aq, float* asc) {
+  pdl_wait();  // the producer of this kernel's input is complete
+  pdl_launch_dependents();
+  extern __shared__ float4 sm4[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = cols / 4, rstride = nch + 1, Kb = cols / 32;
+  float4* sw = sm4;
+  float4* srows = sm4 + nch + warp * kRows4 * rstride;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (int c = threadIdx.x; c < nch; c += blockDim.x) sw[swz4(c)] = __ldg(w4 + c);
+  __syncthreads();
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kRows4Warps * kRows4;
+  for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * kRows4Warps + warp) * kRows4; r0 < rows;
+       r0 += step) {
+    const int nr = static_cast<int>(imin64(kRows4, rows - r0));
+    // ---- stage the rows (coalesced 16-byte loads, all issued before the stores)
+#pragma unroll
+    for (int g = 0; g < kRows4; ++g) {
+      if (g < nr) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (r0 + g) * cols);
+        float4 t[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int c = lane + 32 * k;
+          t[k] = c < nch ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int c = lane + 32 * k;
+          if (c < nch) srows[g * rstride + swz4(c)] = t[k];
+        }
+      }
+    }
+    __syncwarp();
+    // ---- sum of squares in the reference's order: lane 8g + q, chain q of row g
+    const int g = lane >> 3, q = lane & 7;
+    float acc = 0.f;
+    if (g < nr) {
+      const float* rowf = reinterpret_cast<const float*>(srows + g * rstride);
+#pragma unroll 8
+      for (int i = 0; i < cols / 8; ++i) {
+        const int f = 8 * i + q;
+        const float v = rowf[swz4(f >> 2) * 4 + (f & 3)];
+        acc = __fmaf_rn(v, v, acc);
+      }
+    }
+    float sum = __shfl_sync(0xffffffffu, acc, 8 * g);
+#pragma unroll
+    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, acc, 8 * g + l));
+    const float rscale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+    // ---- quantise: lane b takes 32-k block b of each row in turn
+    for (int gg = 0; gg < nr; ++gg) {
+      const float s = __shfl_sync(0xffffffffu, rscale, 8 * gg);
+      if (lane < Kb) {
+        const int64_t row = r0 + gg;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          // chunk j of block `lane`: the swizzle puts lanes 0-7 (one
+          // quarter-warp phase) in distinct bank groups
+          const int c = lane * 8 + j;
+          const float4 a = srows[gg * rstride + swz4(c)];
+          const float4 b = sw[swz4(c)];
+          const int o = j * 4;
+          v[o] = __fmul_rn(__fmul_rn(a.x, s), b.x);
+          v[o + 1] = __fmul_rn(__fmul_rn(a.y, s), b.y);
+          v[o + 2] = __fmul_rn(__fmul_rn(a.z, s), b.z);
+          v[o + 3] = __fmul_rn(__fmul_rn(a.w, s), b.w);
+        }
+        uint8_t* out = aq + (row * Kb + lane) * 32 * (kMode >= kModeF16 ? 2 : 1);
+        if constexpr (kMode == kModeF16Raw) {
+          bool range_ok = true;
+          uint32_t hw[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            range_ok = range_ok && fabsf(v[2 * i]) <= 65504.f && fabsf(v[2 * i + 1]) <= 65504.f;
+            const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            hw[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          if (!range_ok) atomicOr(&g_status_q, kErrF16Range);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(out)[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2],
+                                                          hw[4 * i + 3]);
+        } else {
+          float amax = 0.f, anan = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            amax = fmaxf(amax, fabsf(v[i]));
+            anan = fmax_nan(anan, fabsf(v[i]));
+          }
+          float bs, inv;
+          block_scales(amax, &bs, &inv);
+          asc[row * Kb + lane] = bs;
+          if (!(anan <= 3.402823466e38f)) {  // a NaN or an infinity: the x86 conversion path
+            bool bad = false;
+            quant_block32(v, out, kMode, &bad);
+            if (bad) atomicOr(&g_status_q, kErrF16Range);
+          } else if constexpr (kMode == kModeF16) {
+            constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+            uint32_t hw[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float d[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float zf = __fsub_rn(__fadd_rn(__fmul_rn(v[2 * i + e], inv), kMagic), kMagic);
+                d[e] = __fmul_rn(zf, bs);
+              }
+              const __half2 h = __floats2half2_rn(d[0], d[1]);
+              hw[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            // the largest |q * asc| is 127 * asc (the block's maximum maps to 127)
+            if (amax > 0.f && __fmul_rn(127.f, bs) > 65504.f) atomicOr(&g_status_q, kErrF16Range);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<uint4*>(out)[i] = make_uint4(hw[4 * i], hw[4 * i + 1],
+                                                            hw[4 * i + 2], hw[4 * i + 3]);
+          } else {
+            constexpr float kMagic = 12582912.0f;
+            uint32_t wq[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              uint32_t word = 0;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int z = __float_as_int(__fadd_rn(__fmul_rn(v[4 * i + e], inv), kMagic)) -
+                              0x4B400000;
+                const uint32_t byte =
+                    kMode == kModeU8 ? static_cast<uint32_t>(z + 128) : static_cast<uint32_t>(z & 0xFF);
+                word |= byte << (8 * e);
+              }
+              wq[i] = word;
+            }
+            reinterpret_cast<uint4*>(out)[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+            reinterpret_cast<uint4*>(out)[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+          }
+        }
+      }
+    }
+    __syncwarp();  // the row slots are reused by the next rows
+  }
+}
+
 // ------------------------------------------------- silu(gate)*up + quantize
 template <int kMode>
 __global__ void __launch_bounds__(256) silu_mul_quantize_kernel(int64_t M, int64_t K,
@@ -490,6 +662,38 @@ cudaError_t launch_rmsnorm_quantize(int64_t rows, int64_t cols, const float* x, 
                      (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
                      rows <= static_cast<int64_t>(num_sms(dev)) * 8;
+  const bool batched = cols <= kSmallCols && (cols & 31) == 0 &&
+                       (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                       rows > static_cast<int64_t>(num_sms(dev)) * 8;
+  if (batched) {
+    static thread_local int configured_dev4 = -1;
+    const size_t smem4 = static_cast<size_t>(cols / 4 + kRows4Warps * kRows4 * (cols / 4 + 1)) * 16;
+    if (configured_dev4 != dev) {
+      for (auto* k : {rmsnorm_quantize_rows4_kernel<0>, rmsnorm_quantize_rows4_kernel<1>,
+                      rmsnorm_quantize_rows4_kernel<2>, rmsnorm_quantize_rows4_kernel<3>}) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem4));
+        if (e != cudaSuccess) return e;
+      }
+      configured_dev4 = dev;
+    }
+    const int64_t per_block = kRows4Warps * kRows4;
+    const int g4 = static_cast<int>(imin64((rows + per_block - 1) / per_block,
+                                           static_cast<int64_t>(num_sms(dev)) * 3));
+    auto* q8b = static_cast<uint8_t*>(aq);
+    const int c = static_cast<int>(cols);
+    switch (mode) {
+      case 0: return launch_plain(rmsnorm_quantize_rows4_kernel<0>, dim3(g4), dim3(kRows4Warps * 32),
+                                smem4, s, rows, c, x, w, eps, q8b, asc);
+      case 1: return launch_plain(rmsnorm_quantize_rows4_kernel<1>, dim3(g4), dim3(kRows4Warps * 32),
+                                smem4, s, rows, c, x, w, eps, q8b, asc);
+      case 3: return launch_plain(rmsnorm_quantize_rows4_kernel<3>, dim3(g4), dim3(kRows4Warps * 32),
+                                smem4, s, rows, c, x, w, eps, q8b, asc);
+      default: return launch_plain(rmsnorm_quantize_rows4_kernel<2>, dim3(g4),
+                                 dim3(kRows4Warps * 32), smem4, s, rows, c, x, w, eps, q8b, asc);
+    }
+  }
   if (small) {
     const int sgrid = static_cast<int>(imin64(rows, static_cast<int64_t>(num_sms(dev)) * 16));
     auto* q8s = static_cast<uint8_t*>(aq);

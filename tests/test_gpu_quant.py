@@ -104,6 +104,31 @@ def test_rmsnorm_quantize_many_rows(cuda, M):
     assert_same(host(s16), want_s)
 
 
+def test_rmsnorm_quantize_many_rows_all_forms_and_special_values(cuda):
+    """The row-batched kernel (beyond 8 rows per SM) in every output form:
+    int8 q, the fp16 form and fp16 of the normalised values themselves
+    (OVB_AQ_F16_RAW), with blocks holding zeros, denormals, huge values, an
+    infinity and a NaN (the x86-conversion path) among ordinary rows."""
+    rng = np.random.default_rng(9)
+    M, K = 2000, 1024
+    A = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    A[3, :32] = 0.0
+    A[5, 100:140] = 1e-40
+    A[7, 64:96] = 3e37
+    A[11, 200] = np.inf
+    A[13, 300] = np.nan
+    A[17] = 0.0
+    w = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    want_q, want_s = O.rmsnorm_quantize(A, w, 1e-6)
+    q8, s8 = ovb.rmsnorm_quantize_f32(dev(A, cuda), dev(w, cuda), 1e-6)
+    assert_same(host(q8).view(np.uint8), (want_q.astype(np.int32) - 128).astype(np.int8).view(np.uint8))
+    assert_same(host(s8), want_s)
+    raw = ovb.rmsnorm_f16(dev(A, cuda), dev(w, cuda), 1e-6)
+    want_raw = O.rmsnorm_into(A, w, 1e-6).astype(np.float16)
+    np.testing.assert_array_equal(host(raw), want_raw)  # NaN payloads aside, the same values
+    assert ovb.device_status() in (0, 16)  # the huge row leaves the fp16 range
+
+
 def test_strided_and_misaligned_inputs(cuda):
     rng = np.random.default_rng(5)
     M, K = 33, 200
