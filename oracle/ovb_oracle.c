@@ -48,12 +48,24 @@ static int32_t cvt_rne_x86(float v) {
  * (<= 32) activations of the block; writes 32 bytes of q (u8 = q+128, tail
  * bytes 0) and returns the block scale. */
 static float quant_block_u8(const float* v, int64_t kn, uint8_t* q) {
-  /* amax: |v| via sign-bit clear (andnot), max over the block; the order of a
-   * max is irrelevant, so one scalar loop reproduces the 8-lane version. */
+  /* amax exactly as the reference forms it (gemm.cpp:396-406), NaN included:
+   * eight lanes, each folding the block's whole 8-vectors with MAXPS
+   * (_mm256_max_ps(m, x) = (m > x) ? m : x -- a NaN on either side yields x),
+   * then the lanes and the tail folded with std::max(amax, x) = (amax < x) ?
+   * x : amax, which never lets a NaN through.  For finite values this is the
+   * plain maximum of |v|. */
+  float lane[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int64_t k = 0;
+  for (; k + 8 <= kn; k += 8)
+    for (int j = 0; j < 8; ++j) {
+      const float a = fabsf(v[k + j]);
+      lane[j] = (lane[j] > a) ? lane[j] : a;
+    }
   float amax = 0.f;
-  for (int64_t k = 0; k < kn; ++k) {
-    float a = fabsf(v[k]);
-    amax = (amax > a) ? amax : a; /* std::max(amax, a) / _mm256_max_ps(vmax, a) */
+  for (int j = 0; j < 8; ++j) amax = (amax < lane[j]) ? lane[j] : amax;
+  for (; k < kn; ++k) {
+    const float a = fabsf(v[k]);
+    amax = (amax < a) ? a : amax;
   }
   const float scale = amax / 127.0f;                 /* gemm.cpp:407 */
   const float inv = amax > 0.f ? 127.0f / amax : 0.f; /* gemm.cpp:408 */

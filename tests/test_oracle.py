@@ -130,6 +130,34 @@ def test_port_special_values_match_reference_semantics():
         assert same(aq, r[0]) and same(asc, r[1])
 
 
+@pytest.mark.skipif(not O.ref_vnni(), reason="reference library not built or no AVX-VNNI")
+def test_port_nan_blocks_match_reference():
+    """Blocks holding NaNs: the reference folds each of its eight lanes with
+    MAXPS (a NaN yields the other operand) and the lanes with std::max (which
+    drops a NaN), so a NaN after a lane's maximum erases it.  The restatement
+    reproduces that in every position: mid-lane, last vector, tail, all-NaN,
+    for the three quantisers."""
+    rng = np.random.default_rng(23)
+    K = 70  # two whole blocks and a 6-element tail block
+    A = (rng.standard_normal((8, K)) * 3).astype(np.float32)
+    A[0, 1] = 50.0
+    A[0, 9] = np.nan            # lane 1: 50 then NaN -> 50 lost
+    A[1, 24 + 3] = np.nan       # lane 3, last vector of block 0
+    A[2, 33] = np.nan           # block 1, first vector
+    A[3, 66] = np.nan           # the tail block
+    A[4, :32] = np.nan          # an all-NaN block
+    A[5, 5] = np.nan
+    A[5, 13] = 80.0             # lane 5: NaN then 80 -> 80 kept
+    a1, a2 = O.quantize(A), O.ref_quantize(A)
+    assert same(a1[0], a2[0]) and same(a1[1], a2[1])
+    w = rng.uniform(0.5, 1.5, K).astype(np.float32)
+    b1, b2 = O.rmsnorm_quantize(A, w, 1e-6), O.ref_rmsnorm_quantize(A, w, 1e-6)
+    assert same(b1[0], b2[0]) and same(b1[1], b2[1])
+    g = (rng.standard_normal((8, K)) * 3).astype(np.float32)
+    c1, c2 = O.silu_mul_quantize(g, A), O.ref_silu_mul_quantize(g, A)
+    assert same(c1[0], c2[0]) and same(c1[1], c2[1])
+
+
 def test_port_cfg0_digests(cfg0_digests):
     """BASELINE config 0 at full size: the port reproduces the reference's
     outputs byte for byte (digests recorded by make_golden.py)."""
