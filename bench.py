@@ -1176,7 +1176,12 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     h2d = int(sum_over_ranks(float(sp.h2d_bytes_per_step())))
     d2h = int(sum_over_ranks(float(sp.d2h_bytes_per_step())))
-    launches = int(sum_over_ranks(float(sum(256 + len(b.pairs) for b in sp.batches))))
+    # per forward: embedding gather, mask tile table, 8 per layer (RMSNorm +
+    # quantise, q|k|v, q/k norm + RoPE, attention + o quantiser, o, RMSNorm +
+    # quantise, gate|up + SiLU, down), final RMSNorm + quantise, heads; then
+    # one sampler per CFG pair
+    per_fwd = 2 + 8 * LM_LAYERS + 2
+    launches = int(sum_over_ranks(float(sum(per_fwd + len(b.pairs) for b in sp.batches))))
     status = ovb.device_status()
     biggest = max(sp.batches, key=lambda b: b.rows) if sp.batches else None
     batches = [{"rows": b.rows, "pairs": len(b.pairs)} for b in sp.batches]
