@@ -1393,6 +1393,11 @@ def run_reference(args, rank: int, world: int):
     and at most --ref-seconds, on the config-4 checkpoint and lengths."""
     if rank != 0:
         return None
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; rank 0 alone runs the
+    # reference here, on all the host cores it may use.  OpenMP reads the
+    # variable when its runtime loads, which has not happened yet (nothing
+    # above imports torch or the reference library).
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
     import shutil
     if args.workload == "layer":
         import oracle.cpu_baseline as CB
