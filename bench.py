@@ -1048,10 +1048,18 @@ def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
         ovb.linear_q_silu(*qh, layers[0].gate_up)
     kern = "gemm_h (fp16 mainloop)" if f16 else "gemm_s8_tc (int8 mainloop)"
     L_ = lambda i: layers[i % n_layers]  # noqa: E731
+    # the fp16 forward's q|k|v GEMM carries the q/k norm + RoPE in its
+    # epilogue and writes fp16 q / k / v (the LM's path, ovb_linear_h_qk_rope)
+    tab = ovb.rope_table(torch.arange(M, device=dev, dtype=torch.int64))
+    nrm = torch.ones(128, device=dev)
+    qkv16 = (torch.empty((M, QD), dtype=torch.float16, device=dev),
+             torch.empty((M, KVD), dtype=torch.float16, device=dev),
+             torch.empty((M, KVD), dtype=torch.float16, device=dev))
     gemms = {
-        "qkv": ((lambda i: ovb.linear_h_sliced(qh[0], L_(i).qkv, [q, k, v])) if f16 else
+        "qkv": ((lambda i: ovb.linear_h_qk_rope(qh[0], L_(i).qkv, QD // 128, KVD // 128, nrm, nrm,
+                                                LY.RMS_EPS, tab, out=qkv16)) if f16 else
                 (lambda i: ovb.linear_s8_nk_packed_q_sliced(*qh, L_(i).qkv, [q, k, v])),
-                QD + 2 * KVD, H, False, 4 * M * (QD + 2 * KVD), LM_LAYERS),
+                QD + 2 * KVD, H, False, (2 if f16 else 4) * M * (QD + 2 * KVD), LM_LAYERS),
         "o": ((lambda i: ovb.linear_h(qo[0], L_(i).o, x, accumulate=True)) if f16 else
               (lambda i: ovb.linear_s8_nk_packed_q_add(*qo, L_(i).o, x)),
               H, QD, True, 4 * M * H, LM_LAYERS),
@@ -1176,11 +1184,12 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     h2d = int(sum_over_ranks(float(sp.h2d_bytes_per_step())))
     d2h = int(sum_over_ranks(float(sp.d2h_bytes_per_step())))
-    # per forward: embedding gather, mask tile table, 8 per layer (RMSNorm +
-    # quantise, q|k|v, q/k norm + RoPE, attention + o quantiser, o, RMSNorm +
-    # quantise, gate|up + SiLU, down), final RMSNorm + quantise, heads; then
-    # one sampler per CFG pair
-    per_fwd = 2 + 8 * LM_LAYERS + 2
+    # per forward: embedding gather, mask tile table, RoPE table; per layer
+    # RMSNorm + quantise, q|k|v (+ q/k norm + RoPE in its epilogue on the fp16
+    # path, a launch of its own on the int8 path), attention + o quantiser, o,
+    # RMSNorm + quantise, gate|up + SiLU, down; final RMSNorm + quantise,
+    # heads; then one sampler per CFG pair
+    per_fwd = 3 + (7 if f16 else 8) * LM_LAYERS + 2
     launches = int(sum_over_ranks(float(sum(per_fwd + len(b.pairs) for b in sp.batches))))
     status = ovb.device_status()
     biggest = max(sp.batches, key=lambda b: b.rows) if sp.batches else None

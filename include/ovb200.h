@@ -232,6 +232,38 @@ int ovb_linear_h(int64_t M, const ovb_weight* w, const void* a16, float* C, int6
                  int accumulate, void* stream);
 int ovb_linear_h_sliced(int64_t M, const ovb_weight* w, const void* a16, const ovb_slice* slices,
                         int n_slices, void* stream);
+
+/* The RoPE table of `rows` positions (device int64 pos): table [rows, 64] of
+ * fp32 (cos, sin) pairs, cos / sin of fl(fl(pos[r]) * inv_freq[i]),
+ * inv_freq[i] = (float) theta^(-2i/128) computed on the host as the
+ * reference does.  The reference tabulates the same per row and keeps it
+ * across layers (qk_norm_rope_f32, ops_cpu.cpp:945-986); the device LM
+ * builds it once per forward.  head_dim must be 128; table 16-byte aligned. */
+int ovb_rope_table(const int64_t* pos, int64_t rows, int head_dim, float theta, float* table,
+                   void* stream);
+
+/* The per-head q / k RMSNorm + RoPE of one layer (qk_norm_rope_f32,
+ * ops_cpu.cpp:945-1013; the reference CUDA runner's norm_rope_heads_kernel,
+ * cuda_lm.cu:117-147) written as fp16: q [rows, n_heads*128] and k [rows,
+ * n_kv*128] (fp32, as the q|k|v GEMM writes them, read only) normalised with
+ * q_norm / k_norm [128], rotated by `table` (ovb_rope_table) and stored into
+ * q16 / k16; v [rows, n_kv*128] converted into v16 -- the operands of
+ * ovb_attention_h.  A value beyond the fp16 range sets status bit 16. */
+int ovb_qk_norm_rope_f16(int64_t rows, const float* q, const float* k, const float* v,
+                         int n_heads, int n_kv, int head_dim, const float* q_norm,
+                         const float* k_norm, float eps, const float* table, void* q16, void* k16,
+                         void* v16, void* stream);
+
+/* The q|k|v GEMM on the fp16 mainloop with ovb_qk_norm_rope_f16 fused into
+ * its epilogue: w is the concatenation q|k|v (OVB_WEIGHT_F16, N = (n_heads +
+ * 2 n_kv) * 128), a16 as for ovb_linear_h.  Writes the same bytes into q16 /
+ * k16 / v16 as ovb_linear_h_sliced into fp32 q / k / v followed by
+ * ovb_qk_norm_rope_f16, without the fp32 q / k / v.  No counterpart in the
+ * reference (its q|k|v GEMM and norm + RoPE are separate calls, lm.cpp:
+ * 228-253). */
+int ovb_linear_h_qk_rope(int64_t M, const ovb_weight* w, const void* a16, int n_heads, int n_kv,
+                         int head_dim, const float* q_norm, const float* k_norm, float eps,
+                         const float* table, void* q16, void* k16, void* v16, void* stream);
 /* fp32 activations in, quantised inside (two launches).  accumulate = 0
  * replaces ov::linear_s8_nk_packed (ov_gemm.h:67-69); accumulate = 1
  * replaces ov::linear_s8_nk_packed_add (ov_gemm.h:73-75).  `work` is a device

@@ -16,6 +16,7 @@ from .gemm import (  # noqa: F401
     empty_quant_f16,
     linear_f32,
     linear_h,
+    linear_h_qk_rope,
     linear_h_silu,
     linear_h_sliced,
     linear_q_silu,
@@ -33,5 +34,12 @@ from .gemm import (  # noqa: F401
     to_f16,
     workspace_bytes,
 )
-from .attention import attention, attention_h, attention_h_q, attention_tiles  # noqa: F401
+from .attention import (  # noqa: F401
+    attention,
+    attention_h,
+    attention_h_q,
+    attention_tiles,
+    qk_norm_rope_f16,
+    rope_table,
+)
 from .sampler import guided_sample  # noqa: F401

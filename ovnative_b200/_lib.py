@@ -75,6 +75,11 @@ SIGNATURES = {
     "ovb_linear_h_silu": ([_i64, _p, _p, _p, _p, _int, _p], _int),
     "ovb_weight_gate_up": ([_p, _p, _p, C.POINTER(_p)], _int),
     "ovb_linear_h_sliced": ([_i64, _p, _p, C.POINTER(Slice), _int, _p], _int),
+    "ovb_rope_table": ([_p, _i64, _int, C.c_float, _p, _p], _int),
+    "ovb_qk_norm_rope_f16": ([_i64, _p, _p, _p, _int, _int, _int, _p, _p, C.c_float, _p, _p, _p,
+                              _p, _p], _int),
+    "ovb_linear_h_qk_rope": ([_i64, _p, _p, _int, _int, _int, _p, _p, C.c_float, _p, _p, _p, _p,
+                              _p], _int),
     "ovb_linear_workspace_bytes": ([_i64, _i64], C.c_size_t),
     "ovb_linear": ([_i64, _p, _p, _i64, _p, _i64, _int, _p, C.c_size_t, _p], _int),
     "ovb_linear_static": ([_i64, _p, _p, _i64, _p, _i64, _int, _p], _int),

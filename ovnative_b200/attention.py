@@ -152,3 +152,38 @@ def attention_h_q(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, segs,
                                       asc.data_ptr(), flags,
                                       torch.cuda.current_stream().cuda_stream))
     return aq, asc
+
+
+def rope_table(pos: torch.Tensor, theta: float = 1e6) -> torch.Tensor:
+    """The RoPE table of int64 positions ``pos`` [rows] (ovb_rope_table):
+    [rows, 64, 2] fp32 (cos, sin) of pos * inv_freq[i], inv_freq[i] =
+    theta^(-2i/128) rounded to fp32 (qk_norm_rope_f32's table,
+    ops_cpu.cpp:945-986)."""
+    if not pos.is_cuda or pos.dtype != torch.int64 or not pos.is_contiguous():
+        raise ValueError("pos must be a contiguous int64 CUDA tensor")
+    tab = torch.empty((pos.numel(), 64, 2), dtype=torch.float32, device=pos.device)
+    L.check(L.lib().ovb_rope_table(pos.data_ptr(), pos.numel(), HEAD_DIM, float(theta),
+                                   tab.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    return tab
+
+
+def qk_norm_rope_f16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm: torch.Tensor,
+                     k_norm: torch.Tensor, eps: float, table: torch.Tensor):
+    """Per-head q / k RMSNorm + RoPE into fp16, v converted to fp16
+    (ovb_qk_norm_rope_f16): q [rows, n_heads*128], k / v [rows, n_kv*128]
+    contiguous fp32; returns (q16, k16, v16), the operands of attention_h."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("q_norm", q_norm), ("k_norm", k_norm),
+                    ("table", table)):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous float32 CUDA tensor")
+    rows = q.shape[0]
+    n_heads, n_kv = q.shape[1] // HEAD_DIM, k.shape[1] // HEAD_DIM
+    q16 = torch.empty(q.shape, dtype=torch.float16, device=q.device)
+    k16 = torch.empty(k.shape, dtype=torch.float16, device=q.device)
+    v16 = torch.empty(v.shape, dtype=torch.float16, device=q.device)
+    L.check(L.lib().ovb_qk_norm_rope_f16(rows, q.data_ptr(), k.data_ptr(), v.data_ptr(), n_heads,
+                                         n_kv, HEAD_DIM, q_norm.data_ptr(), k_norm.data_ptr(),
+                                         float(eps), table.data_ptr(), q16.data_ptr(),
+                                         k16.data_ptr(), v16.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream))
+    return q16, k16, v16

@@ -288,9 +288,18 @@ int run_gemm(int64_t M, const ovb_weight* wc, const int8_t* aq, const float* asc
   return OVB_OK;
 }
 
+// Outputs of the fused q/k RMSNorm + RoPE epilogue (null: none).
+struct RopeOut {
+  void *q16, *k16, *v16;
+  const float *qw, *kw, *tab;
+  int64_t qd, kvd;
+  float eps;
+};
+
 // The plain fp16 mainloop on dequantised activations a16 [M, Kp] fp16.
 int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::SliceOut* slices,
-               int n_slices, int accumulate, cudaStream_t s, const SiluOut* silu = nullptr) {
+               int n_slices, int accumulate, cudaStream_t s, const SiluOut* silu = nullptr,
+               const RopeOut* rope = nullptr) {
   ovb_weight* w = const_cast<ovb_weight*>(wc);
   if (!ensure_weight_tmap16(w)) return OVB_ERR_INTERNAL;
   CUtensorMap tmap_a;
@@ -315,11 +324,25 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
     args.silu_mode = silu->mode;
     args.silu_kp = w->glu_inter;
   }
+  if (rope) {
+    args.rope_q16 = rope->q16;
+    args.rope_k16 = rope->k16;
+    args.rope_v16 = rope->v16;
+    args.rope_qw = rope->qw;
+    args.rope_kw = rope->kw;
+    args.rope_tab = rope->tab;
+    args.rope_qd = rope->qd;
+    args.rope_kvd = rope->kvd;
+    args.rope_eps = rope->eps;
+  }
   args.split_ws = ovb::split_workspace(w->device);
   // split-K configurations need the workspace; the fused SiLU*up epilogue
-  // takes BN >= 64 without split-K
-  const int config = ovb::pick_tile_h(
-      M, w->N, w->Kb, w->device, silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit));
+  // takes BN >= 64 without split-K; the fused q/k norm + RoPE epilogue
+  // single-CTA 256-column tiles (configuration 0: two whole heads per tile)
+  const int config =
+      rope ? 0
+           : ovb::pick_tile_h(M, w->N, w->Kb, w->device,
+                              silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit));
   const int width = ovb::kHConfigs[config].width;
   if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
@@ -367,6 +390,18 @@ int check_h_args(int64_t M, const ovb_weight* w, const void* a16) {
   int dev = 0;
   if (cuda_failed(cudaGetDevice(&dev), "cudaGetDevice")) return OVB_ERR_INTERNAL;
   if (dev != w->device) return invalid("weight lives on another device than the current one");
+  return OVB_OK;
+}
+
+int check_rope(int n_heads, int n_kv, int head_dim, const float* q_norm, const float* k_norm,
+               const float* table, const void* q16, const void* k16, const void* v16) {
+  if (head_dim != 128) return invalid("head_dim must be 128");
+  if (n_heads <= 0 || n_kv <= 0) return invalid("n_heads and n_kv must be positive");
+  if (!q_norm || !k_norm || !table || !q16 || !k16 || !v16)
+    return invalid("q_norm/k_norm/table/q16/k16/v16 must be non-null");
+  if (!aligned(table, 16)) return invalid("table must be 16-byte aligned");
+  if (!aligned(q16, 16) || !aligned(k16, 16) || !aligned(v16, 16))
+    return invalid("q16/k16/v16 must be 16-byte aligned");
   return OVB_OK;
 }
 
@@ -860,6 +895,55 @@ int ovb_linear_h_sliced(int64_t M, const ovb_weight* w, const void* a16, const o
   st = build_slices(w, slices, n_slices, so);
   if (st != OVB_OK) return st;
   return run_gemm_h(M, w, a16, so, n_slices, 0, as_stream(stream));
+}
+
+int ovb_rope_table(const int64_t* pos, int64_t rows, int head_dim, float theta, float* table,
+                   void* stream) {
+  if (rows <= 0) return OVB_OK;
+  if (head_dim != 128) return invalid("head_dim must be 128");
+  if (!pos || !table) return invalid("pos/table must be non-null");
+  if (!aligned(table, 16)) return invalid("table must be 16-byte aligned");
+  if (!aligned(pos, 8)) return invalid("pos must be 8-byte aligned");
+  if (rows > (int64_t{1} << 31) - 1) return invalid("rows exceeds 2^31-1");
+  // inv_freq as qk_norm_rope_f32 computes it (ops_cpu.cpp:953-962)
+  ovb::RopeFreq f;
+  for (int i = 0; i < 64; ++i)
+    f.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(theta), -2.0 * i / 128.0));
+  if (cuda_failed(ovb::launch_rope_table(pos, f, rows, table, as_stream(stream)), "rope table launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_qk_norm_rope_f16(int64_t rows, const float* q, const float* k, const float* v,
+                         int n_heads, int n_kv, int head_dim, const float* q_norm,
+                         const float* k_norm, float eps, const float* table, void* q16, void* k16,
+                         void* v16, void* stream) {
+  if (rows <= 0) return OVB_OK;
+  int st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, table, q16, k16, v16);
+  if (st != OVB_OK) return st;
+  if (!q || !k || !v) return invalid("q/k/v must be non-null");
+  if (rows > (int64_t{1} << 31) - 1) return invalid("rows exceeds 2^31-1");
+  if (cuda_failed(ovb::launch_qk_norm_rope_f16(q, k, v, q16, k16, v16, q_norm, k_norm, table, rows,
+                                               n_heads, n_kv, eps, as_stream(stream)),
+                  "qk norm / rope launch"))
+    return OVB_ERR_INTERNAL;
+  return OVB_OK;
+}
+
+int ovb_linear_h_qk_rope(int64_t M, const ovb_weight* w, const void* a16, int n_heads, int n_kv,
+                         int head_dim, const float* q_norm, const float* k_norm, float eps,
+                         const float* table, void* q16, void* k16, void* v16, void* stream) {
+  if (M <= 0) return OVB_OK;
+  int st = check_h_args(M, w, a16);
+  if (st != OVB_OK) return st;
+  st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, table, q16, k16, v16);
+  if (st != OVB_OK) return st;
+  const int64_t qd = int64_t{n_heads} * 128, kvd = int64_t{n_kv} * 128;
+  if (w->N != qd + 2 * kvd)
+    return invalid("the weight's N must be (n_heads + 2 n_kv) * head_dim (a q|k|v weight)");
+  const ovb::SliceOut so{0, w->N, nullptr, w->N};
+  const RopeOut r{q16, k16, v16, q_norm, k_norm, table, qd, kvd, eps};
+  return run_gemm_h(M, w, a16, &so, 1, 0, as_stream(stream), nullptr, &r);
 }
 
 size_t ovb_linear_workspace_bytes(int64_t M, int64_t K) {

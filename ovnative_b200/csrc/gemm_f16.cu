@@ -381,6 +381,188 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   }
 }
 
+// The epilogue loop of the fused q|k|v mode (args.rope_q16 non-null; BN =
+// 256, two 128-column heads per tile).  Warp (quarter, eh) takes head eh of
+// the tile for TMEM lanes 32*quarter..: each thread holds one row of the
+// head.  x = D * wscale per column is the plain epilogue's output value; q
+// and k heads are then RMS-normalised and rotated exactly as
+// qk_norm_rope_f16_kernel (lm_ops.cu) does -- the same sum of squares
+// (s_l = (x_l^2 + x_{l+32}^2) + (x_{l+64}^2 + x_{l+96}^2), then pairwise sums
+// at distances 16, 8, .., 1, the order of its warp tree), the same scale and
+// rotation -- so the fp16 outputs equal the unfused sequence bit for bit; v
+// heads are converted.  Two passes over TMEM: the sum of squares, then the
+// rotation set by set (columns 32s.. with 64+32s.., s = 0, 1), each set's 64
+// fp16 outputs staged in shared memory (32 rows x 128 bytes, 16-byte chunks
+// XOR-swizzled by row: conflict-free both ways) and written as 64-byte row
+// segments, 8 lanes per row.
+template <int BN, int kAcc>
+__device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_t* tfull,
+                                                   volatile int* abort, uint32_t tmem_base,
+                                                   float* stg, int quarter, int eh, int dfree_bar,
+                                                   int64_t tiles, int64_t m_tiles,
+                                                   int64_t my_tiles, int64_t tile_first,
+                                                   int64_t tile_step) {
+  static_assert(BN == 256, "two heads per tile, one per epilogue warp of a lane quarter");
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N;
+  const int64_t qd = args.rope_qd, kvd = args.rope_kvd;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  uint8_t* st8 = reinterpret_cast<uint8_t*>(stg);
+  bool range_ok = true;
+  int64_t t = 0;
+  for (int64_t tile = tile_first; tile < tiles; tile += tile_step, ++t) {
+    const int d = static_cast<int>(t % kAcc);
+    const uint32_t ph = static_cast<uint32_t>((t / kAcc) & 1);
+    int64_t m0, n0;
+    tile_origin(tile, m_tiles, BN, &m0, &n0);
+    const int64_t hc = n0 + 128 * eh;  // this warp's head: columns hc .. hc + 127
+    const bool has = hc < N;           // uniform per warp
+    const int kind = hc < qd ? 0 : (hc < qd + kvd ? 1 : 2);  // q, k or v head
+    // Lane l: the wscale of columns hc + 32 j + l and the norm weight of head
+    // element 32 j + l, fetched before the accumulator is ready.
+    const float* nw = kind == 0 ? args.rope_qw : args.rope_kw;
+    float wsl[4], nwl[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      wsl[j] = has ? __ldg(args.wscale + hc + 32 * j + lane) : 0.f;
+      nwl[j] = (has && kind < 2) ? __ldg(nw + 32 * j + lane) : 0.f;
+    }
+    const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0) {
+        atomicOr(&g_status_f16, kErrEpilogue);
+        *abort = 1;
+      }
+    } else {
+      tc_fence_after();
+      const int64_t r0 = m0 + quarter * 32;
+      const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
+      if (has && rows > 0) {  // uniform per warp
+        const uint32_t dcol =
+            tmem_base + lane_off + static_cast<uint32_t>(d * BN + 128 * eh);
+        const bool row_ok = lane < rows;
+        float scale = 0.f;
+        if (kind < 2) {
+          // pass 1: the sum of squares of the row's head
+          float s01[32], s23[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld32(dcol + static_cast<uint32_t>(32 * c), v);
+            tc_wait_ld32(v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float x =
+                  __fmul_rn(__uint_as_float(v[i]), __shfl_sync(0xffffffffu, wsl[c], i));
+              const float x2 = __fmul_rn(x, x);
+              if (c == 0) s01[i] = x2;
+              if (c == 1) s01[i] = __fadd_rn(s01[i], x2);
+              if (c == 2) s23[i] = x2;
+              if (c == 3) s23[i] = __fadd_rn(s23[i], x2);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s01[i] = __fadd_rn(s01[i], s23[i]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < o; ++i) s01[i] = __fadd_rn(s01[i], s01[i + o]);
+          }
+          scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s01[0], 128.f), args.rope_eps)));
+        }
+        // The output rows of this head.
+        __half* out;
+        int64_t ld, col0;
+        if (kind == 0) {
+          out = static_cast<__half*>(args.rope_q16);
+          ld = qd;
+          col0 = hc;
+        } else if (kind == 1) {
+          out = static_cast<__half*>(args.rope_k16);
+          ld = kvd;
+          col0 = hc - qd;
+        } else {
+          out = static_cast<__half*>(args.rope_v16);
+          ld = kvd;
+          col0 = hc - qd - kvd;
+        }
+        // This row's (cos, sin) pairs: 64 per row, 128 floats.
+        const float4* tab_row = reinterpret_cast<const float4*>(
+            args.rope_tab + (row_ok ? r0 + lane : 0) * 128);
+        // pass 2: set s = head elements 32s + i (lo) and 64 + 32s + i (hi)
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(dcol + static_cast<uint32_t>(32 * s), va);
+          tmem_ld32(dcol + static_cast<uint32_t>(64 + 32 * s), vb);
+          tc_wait_ld32(va);
+          tc_wait_ld32(vb);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {  // elements 8g .. 8g + 7: float4s 16s + 4g .. + 3
+            float4 cs4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              cs4[u] = (kind < 2 && row_ok) ? __ldg(tab_row + 16 * s + 4 * g + u)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint32_t lo_w[4], hi_w[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              float lo[2], hi[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int i = 8 * g + e + h;
+                const float x =
+                    __fmul_rn(__uint_as_float(va[i]), __shfl_sync(0xffffffffu, wsl[s], i));
+                const float y =
+                    __fmul_rn(__uint_as_float(vb[i]), __shfl_sync(0xffffffffu, wsl[s + 2], i));
+                const float wa = __shfl_sync(0xffffffffu, nwl[s], i);
+                const float wb = __shfl_sync(0xffffffffu, nwl[s + 2], i);
+                if (kind < 2) {
+                  const float4 c2 = cs4[(e + h) >> 1];
+                  const float cs = ((e + h) & 1) ? c2.z : c2.x;
+                  const float sn = ((e + h) & 1) ? c2.w : c2.y;
+                  const float a = __fmul_rn(__fmul_rn(x, scale), wa);
+                  const float b = __fmul_rn(__fmul_rn(y, scale), wb);
+                  lo[h] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+                  hi[h] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+                } else {
+                  lo[h] = x;
+                  hi[h] = y;
+                }
+                if (row_ok && !(fabsf(lo[h]) <= 65504.f && fabsf(hi[h]) <= 65504.f))
+                  range_ok = false;
+              }
+              const __half2 l2 = __floats2half2_rn(lo[0], lo[1]);
+              const __half2 h2 = __floats2half2_rn(hi[0], hi[1]);
+              lo_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
+              hi_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * (g ^ (lane & 7))) =
+                make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+            *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * ((4 + g) ^ (lane & 7))) =
+                make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+          }
+          __syncwarp();
+          // chunk k of row r: columns 32s + 8k (k < 4) or 64 + 32s + 8(k - 4)
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3);
+            const int k = lane & 7;
+            const int64_t col = col0 + (k < 4 ? 32 * s + 8 * k : 64 + 32 * s + 8 * (k - 4));
+            if (r < rows)
+              *reinterpret_cast<uint4*>(out + (r0 + r) * ld + col) =
+                  *reinterpret_cast<const uint4*>(st8 + r * 128 + 16 * (k ^ (r & 7)));
+          }
+          __syncwarp();
+        }
+      }
+    }
+    tc_fence_before();
+    if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiWarpsF + 1));
+  }
+  if (!range_ok) atomicOr(&g_status_f16, kErrF16Range);
+}
+
 // silu(g) * u for the fp16 mainloop's fused epilogue, which owes the
 // contract's tolerance rather than the reference's bits: the hardware's
 // approximate exponential and division (CUDA's __expf / __fdividef, relative
@@ -1006,7 +1188,7 @@ __device__ __forceinline__ void split_finish(const GemmArgs& args, CtlH* ctl,
   }
 }
 
-template <int BN, bool kSilu, int kSplit>
+template <int BN, bool kSilu, int kSplit, bool kRope>
 __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_w,
@@ -1156,6 +1338,11 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
         split_send<BN, kSplit>(args, ctl, abort, tmem_base,
                                stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
                                (warp - kFirstEpiH) >> 2, rank);
+    } else if constexpr (kRope) {
+      epilogue_rope_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                                      stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                                      (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles,
+                                      my_tiles, blockIdx.x, gridDim.x);
     } else if constexpr (kSilu) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
       silu_epilogue<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
@@ -1187,11 +1374,11 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
   }
 }
 
-template <int BN, bool kSilu, int kSplit = 1>
+template <int BN, bool kSilu, int kSplit = 1, bool kRope = false>
 cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
   using T = TileH<BN, kSilu, kSplit>;
-  auto* kernel = gemm_h_kernel<BN, kSilu, kSplit>;
+  auto* kernel = gemm_h_kernel<BN, kSilu, kSplit, kRope>;
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
@@ -1550,6 +1737,9 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) 
 
 cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
+  if (args.rope_q16)  // the fused q/k norm + RoPE epilogue: two whole heads per tile
+    return config == 0 ? launch_h_impl<256, false, 1, true>(tmap_a, tmap_w, args, s)
+                       : cudaErrorInvalidValue;
   if (args.silu_out) {
     switch (config) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
       case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);

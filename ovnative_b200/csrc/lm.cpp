@@ -4,10 +4,11 @@
 // (lm.h:91-96) and the ragged CFG forward (LM::forward_cfg, lm.cpp:403-454).
 //
 // Per layer (LM::run_layer, lm.cpp:217-322): RMSNorm + quantise -> q|k|v
-// GEMM -> per-head RMSNorm + RoPE (written as fp16 q / k, with v as fp16) ->
-// attention over the segments with the o projection's quantiser in its
-// epilogue (ovb_attention_h_q; the masks as a tile table built once per
-// forward)
+// GEMM -> per-head RMSNorm + RoPE (written as fp16 q / k, with v as fp16; on
+// the fp16 path fused into the q|k|v GEMM's epilogue, ovb_linear_h_qk_rope)
+// -> attention over the segments with the o projection's quantiser in its
+// epilogue (ovb_attention_h_q; the masks as a tile table and the RoPE
+// angles as a table, both built once per forward)
 // -> o GEMM += x -> RMSNorm + quantise -> gate|up GEMM fused with SiLU*up +
 // quantise -> down GEMM += x.  Then the final RMSNorm + quantise and the
 // audio-heads GEMM.  The linear weights are int8 (either OVW1 orientation)
@@ -75,11 +76,12 @@ struct ovb_lm {
   ovb_weight* heads = nullptr;
   bool heads_f32 = false;  // the reference's default fp32 audio heads (ovb_weight_create_f32)
   const float* final_norm = nullptr;
-  DevBuf norms, emb, offsets, inv_freq;
+  DevBuf norms, emb, offsets;
   ovb::EmbTable tok{}, aud{};
   // forward buffers (grown on demand)
   DevBuf x, aq, asc, q, k, v, qi, asci, logits, logits_perm, ids, amask, pos, masks;
   DevBuf q16, k16, v16;  // fp16 q / k (normalised, rotated) and v: the attention's operands
+  DevBuf rope;           // the RoPE table of the forward's positions (ovb_rope_table)
   DevBuf tiles;          // the attention's mask tile table (ovb_attention_tiles)
   DevBuf pred, scores;  // ovb_lm_sample's device outputs
   // pinned host staging of the logits for the host-buffer forwards: one
@@ -316,13 +318,6 @@ int load(ovb_lm* m, const ovb_ovw1* f, cudaStream_t s) {
       cudaMemcpy(m->offsets.p, offs, static_cast<size_t>(m->n_codebooks) * 8,
                  cudaMemcpyHostToDevice) != cudaSuccess)
     return internal("offset upload failed");
-  // inv_freq as qk_norm_rope_f32 computes it (ops_cpu.cpp:953-962)
-  float invf[64];
-  for (int i = 0; i < 64; ++i)
-    invf[i] = static_cast<float>(std::pow(static_cast<double>(m->theta), -2.0 * i / 128.0));
-  if (!m->inv_freq.grow(sizeof invf) ||
-      cudaMemcpy(m->inv_freq.p, invf, sizeof invf, cudaMemcpyHostToDevice) != cudaSuccess)
-    return internal("inv_freq upload failed");
   return OVB_OK;
 }
 
@@ -342,9 +337,13 @@ bool reserve(ovb_lm* m, int64_t rows, int64_t mask_elems) {
   const int64_t CV = int64_t(m->n_codebooks) * m->audio_vocab;
   const size_t ab = m->f16 ? 2 : 1;
   const size_t r = static_cast<size_t>(rows);
+  // fp32 q / k / v only on the int8 path (the fp16 path's q|k|v GEMM writes
+  // the fp16 operands directly)
+  const bool qkv32 = !m->f16;
   return m->x.grow(r * H * 4) && m->aq.grow(r * std::max<int64_t>(KM * ab, H * 2)) &&
          m->asc.grow(r * (KM / 32) * 4) &&
-         m->q.grow(r * QD * 4) && m->k.grow(r * KVD * 4) && m->v.grow(r * KVD * 4) &&
+         (!qkv32 || (m->q.grow(r * QD * 4) && m->k.grow(r * KVD * 4) && m->v.grow(r * KVD * 4))) &&
+         m->rope.grow(r * 128 * 4) &&
          m->qi.grow(r * m->inter * ab) &&
          m->asci.grow(r * (m->inter / 32) * 4) && m->logits.grow(r * CV * 4) &&
          m->ids.grow(r * m->n_codebooks * 8) && m->amask.grow(r) && m->pos.grow(r * 8) &&
@@ -367,20 +366,24 @@ int run(ovb_lm* m, int64_t rows, int seq, const ovb_attn_segment* segs, int n_se
                         m->n_codebooks, rows, seq, m->tok, m->aud, x, m->hidden, s) != cudaSuccess)
     return internal("embed launch failed");
   const float scale = 1.f / std::sqrt(static_cast<float>(m->head_dim));
+  const float* rope = m->rope.as<float>();
   int rc = OVB_OK;
 #define OVB_LM_TRY(call) \
   if ((rc = (call)) != OVB_OK) return rc
+  OVB_LM_TRY(ovb_rope_table(m->pos.as<int64_t>(), rows, 128, m->theta, m->rope.as<float>(), s));
   for (const ovb_lm::Layer& L : m->layers) {
     OVB_LM_TRY(ovb_rmsnorm_quantize(rows, H, x, L.in_ln, m->eps, aq, asc, qf, s));
-    const ovb_slice sl[3] = {{QD, m->q.as<float>(), QD}, {KVD, m->k.as<float>(), KVD},
-                             {KVD, m->v.as<float>(), KVD}};
-    OVB_LM_TRY(m->f16 ? ovb_linear_h_sliced(rows, L.qkv, aq, sl, 3, s)
-                      : ovb_linear_q_sliced(rows, L.qkv, aq, asc, sl, 3, s));
-    if (ovb::launch_qk_norm_rope_f16(m->q.as<float>(), m->k.as<float>(), m->v.as<float>(),
-                                     m->q16.p, m->k16.p, m->v16.p, L.q_norm, L.k_norm,
-                                     m->pos.as<int64_t>(), m->inv_freq.as<float>(), rows,
-                                     m->n_heads, m->n_kv, m->eps, s) != cudaSuccess)
-      return internal("qk norm / rope launch failed");
+    if (m->f16) {
+      OVB_LM_TRY(ovb_linear_h_qk_rope(rows, L.qkv, aq, m->n_heads, m->n_kv, 128, L.q_norm,
+                                      L.k_norm, m->eps, rope, m->q16.p, m->k16.p, m->v16.p, s));
+    } else {
+      const ovb_slice sl[3] = {{QD, m->q.as<float>(), QD}, {KVD, m->k.as<float>(), KVD},
+                               {KVD, m->v.as<float>(), KVD}};
+      OVB_LM_TRY(ovb_linear_q_sliced(rows, L.qkv, aq, asc, sl, 3, s));
+      OVB_LM_TRY(ovb_qk_norm_rope_f16(rows, m->q.as<float>(), m->k.as<float>(), m->v.as<float>(),
+                                      m->n_heads, m->n_kv, 128, L.q_norm, L.k_norm, m->eps, rope,
+                                      m->q16.p, m->k16.p, m->v16.p, s));
+    }
     // attention with the o projection's quantiser in its epilogue
     OVB_LM_TRY(ovb_attention_h_q(m->q16.p, m->k16.p, m->v16.p, QD, KVD, m->n_heads, m->n_kv, 128,
                                  scale, segs, n_segs, tiles, aq, asc, qf, s));

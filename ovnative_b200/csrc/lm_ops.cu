@@ -1,6 +1,7 @@
 // lm_ops.cu -- the steps of the LM forward that are not GEMMs, quantisers or
-// attention: the embedding gather, the attention-mask bias, the per-head
-// RMSNorm + RoPE of q and k, and the logits permute of the batched forward.
+// attention: the embedding gather, the RoPE table, the per-head RMSNorm + RoPE
+// of q and k (the int8 path; the fp16 path fuses it into the q|k|v GEMM), and
+// the logits permute of the batched forward.
 // They are what LM::forward / LM::forward_cfg (cpp/src/model/lm.cpp:343-454)
 // run between the hot-path kernels, so that a whole forward stays on the
 // device (ovb_lm_*, lm.cpp in this directory).
@@ -64,84 +65,43 @@ __global__ void embed_kernel(const int64_t* ids, const uint8_t* mask, const int6
   if (!ok && threadIdx.x == 0) atomicOr(&g_status_lm, kErrLmIndex);
 }
 
-// bias = attn ? 0 : -1e30 (lm.cpp:365, :431-434).
-__global__ void mask_bias_kernel(const uint8_t* attn, int64_t n, float* bias) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    bias[i] = attn[i] ? 0.f : -1e30f;
+// The RoPE table of a forward: tab[r, i] = (cos(angle), sin(angle)) with
+// angle = fl(fl(pos[r]) * inv_freq[i]) for i < 64, inv_freq[i] = (float)
+// theta^(-2i/D) computed on the host as the reference does.  The reference
+// tabulates the same per row and keeps the table across layers while the
+// positions do not change (qk_norm_rope_f32, ops_cpu.cpp:945-986); here it is
+// built once per forward.  cos / sin are CUDA's (not glibc's): they agree to a
+// few ulps.  One thread per (row, i).
+__global__ void rope_table_kernel(const int64_t* pos, RopeFreq f, int64_t rows, float2* tab) {
+  const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (t >= rows * 64) return;
+  const int64_t r = t >> 6;
+  const int i = static_cast<int>(t & 63);
+  const float angle = __fmul_rn(static_cast<float>(pos[r]), f.inv_freq[i]);
+  tab[t] = make_float2(cosf(angle), sinf(angle));
 }
 
-// qk_norm_rope_f32 (ops_cpu.cpp:945-1013) for head_dim 128: each head vector
-// v of q (n_heads per row) and k (n_kv per row) is RMS-normalised with its
-// weight, then rotated by the position's angles:
-//   scale = 1 / sqrt(sum(v^2) / D + eps);  a = (v[i] scale) w[i],
-//   b = (v[i+64] scale) w[i+64];  v[i] = a cos - b sin;  v[i+64] = b cos + a sin,
-// angle = pos * inv_freq[i], inv_freq[i] = (float) theta^(-2i/D) computed on
-// the host as the reference does.  One block per row: its 64 cos / sin pairs
-// are computed once into shared memory (as the reference tabulates them per
-// row), then each warp normalises and rotates head vectors of the row; lane l
-// holds elements l, l+32, l+64, l+96.  The sum of squares runs in a warp tree
-// and cos / sin are CUDA's (not glibc's): results agree to a few ulps.
-__global__ void qk_norm_rope_kernel(float* q, float* k, const float* qw, const float* kw,
-                                    const int64_t* pos, const float* inv_freq, int64_t rows,
-                                    int n_heads, int n_kv, float eps) {
-  constexpr int D = 128, half = 64;
-  __shared__ float cs_s[half], sn_s[half];
-  const int64_t r = blockIdx.x;
-  if (r >= rows) return;
-  if (threadIdx.x < half) {
-    const float angle = __fmul_rn(static_cast<float>(pos[r]), inv_freq[threadIdx.x]);
-    cs_s[threadIdx.x] = cosf(angle);
-    sn_s[threadIdx.x] = sinf(angle);
-  }
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nw = static_cast<int>(blockDim.x >> 5);
-  for (int h = warp; h < n_heads + n_kv; h += nw) {
-    float* v = h < n_heads ? q + (r * n_heads + h) * D : k + (r * n_kv + (h - n_heads)) * D;
-    const float* w = h < n_heads ? qw : kw;
-    float x[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = v[lane + 32 * j];
-    float sum = __fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])),
-                          __fadd_rn(__fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-    const float scale =
-        __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(D)), eps)));
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int i = lane + 32 * j;  // 0 .. 63
-      const float cs = cs_s[i], sn = sn_s[i];
-      const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
-      const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
-      v[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-      v[i + half] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
-    }
-  }
-}
-
-// The same q / k normalisation and rotation, written as fp16 into q16 / k16
-// (the attention's operands), and v converted to fp16 into v16, in one pass
-// over the row; q, k, v (fp32, from the q|k|v GEMM) are only read.  A value
-// beyond the fp16 range sets status bit 16.
+// qk_norm_rope_f32 (ops_cpu.cpp:945-1013) for head_dim 128, written as fp16
+// into q16 / k16 (the attention's operands), and v converted to fp16 into
+// v16, in one pass over the row; q, k, v (fp32, from the q|k|v GEMM) are only
+// read.  Each head vector x of q (n_heads per row) and k (n_kv per row) is
+// RMS-normalised with its weight, then rotated by the row's angles:
+//   scale = 1 / sqrt(sum(x^2) / D + eps);  a = (x[i] scale) w[i],
+//   b = (x[i+64] scale) w[i+64];  x[i] = a cos - b sin;  x[i+64] = b cos + a sin.
+// One block per row, one warp per head vector; lane l holds elements l,
+// l+32, l+64, l+96 and the sum of squares runs in a warp tree (the fused q|k|v
+// GEMM epilogue, gemm_f16.cu, reproduces this order).  A value beyond the
+// fp16 range sets status bit 16.
 __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const float* v,
                                         __half* q16, __half* k16, __half* v16, const float* qw,
-                                        const float* kw, const int64_t* pos,
-                                        const float* inv_freq, int64_t rows, int n_heads,
-                                        int n_kv, float eps) {
+                                        const float* kw, const float2* tab, int64_t rows,
+                                        int n_heads, int n_kv, float eps) {
   constexpr int D = 128, half = 64;
-  __shared__ float cs_s[half], sn_s[half];
   const int64_t r = blockIdx.x;
   if (r >= rows) return;
-  if (threadIdx.x < half) {
-    const float angle = __fmul_rn(static_cast<float>(pos[r]), inv_freq[threadIdx.x]);
-    cs_s[threadIdx.x] = cosf(angle);
-    sn_s[threadIdx.x] = sinf(angle);
-  }
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = static_cast<int>(blockDim.x >> 5);
+  const float2 cs0 = tab[r * half + lane], cs1 = tab[r * half + lane + 32];
   bool range_ok = true;
   // Each warp's head vectors (q, then k, then v heads), loaded in groups of
   // four before any of them is reduced, so that their loads are in flight
@@ -188,7 +148,7 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int i = lane + 32 * j;  // 0 .. 63
-      const float cs = cs_s[i], sn = sn_s[i];
+      const float cs = j ? cs1.x : cs0.x, sn = j ? cs1.y : cs0.y;
       const float a = __fmul_rn(__fmul_rn(x[j], scale), w[i]);
       const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
       const float lo = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
@@ -220,26 +180,21 @@ cudaError_t launch_embed(const int64_t* ids, const uint8_t* mask, const int64_t*
                       mask, offsets, C, seq, tok, aud, out, H);
 }
 
-cudaError_t launch_mask_bias(const uint8_t* attn, int64_t n, float* bias, cudaStream_t s) {
-  const int64_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
-  return launch_plain(mask_bias_kernel, dim3(static_cast<unsigned>(blocks > 0 ? blocks : 1)),
-                      dim3(256), 0, s, attn, n, bias);
-}
-
-cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float* kw,
-                                const int64_t* pos, const float* inv_freq, int64_t rows,
-                                int n_heads, int n_kv, float eps, cudaStream_t s) {
-  return launch_plain(qk_norm_rope_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s, q,
-                      k, qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
+cudaError_t launch_rope_table(const int64_t* pos, const RopeFreq& f, int64_t rows, float* tab,
+                              cudaStream_t s) {
+  const int64_t n = rows * 64;
+  return launch_plain(rope_table_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256),
+                      0, s, pos, f, rows, reinterpret_cast<float2*>(tab));
 }
 
 cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float* v, void* q16,
                                     void* k16, void* v16, const float* qw, const float* kw,
-                                    const int64_t* pos, const float* inv_freq, int64_t rows,
-                                    int n_heads, int n_kv, float eps, cudaStream_t s) {
+                                    const float* tab, int64_t rows, int n_heads, int n_kv,
+                                    float eps, cudaStream_t s) {
   return launch_plain(qk_norm_rope_f16_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s,
                       q, k, v, static_cast<__half*>(q16), static_cast<__half*>(k16),
-                      static_cast<__half*>(v16), qw, kw, pos, inv_freq, rows, n_heads, n_kv, eps);
+                      static_cast<__half*>(v16), qw, kw, reinterpret_cast<const float2*>(tab),
+                      rows, n_heads, n_kv, eps);
 }
 
 cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,

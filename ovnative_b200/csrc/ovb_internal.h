@@ -135,6 +135,20 @@ struct GemmArgs {
   // kSplitSlots slots of kSplitSlotBytes, slot i used only by the CTA
   // running on the SM with %smid == i.
   float* split_ws;
+  // Fused q/k RMSNorm + RoPE epilogue (a q|k|v weight, plain fp16 mainloop):
+  // when rope_q16 is non-null the kernel writes the q heads (columns
+  // [0, rope_qd)) normalised with rope_qw and rotated, the k heads (the next
+  // rope_kvd columns) likewise with rope_kw, and the v heads converted, all as
+  // fp16 into rope_q16 [M, rope_qd], rope_k16 / rope_v16 [M, rope_kvd];
+  // rope_tab is the RoPE table [M, 64] of (cos, sin).  Head dim 128.
+  void* rope_q16;
+  void* rope_k16;
+  void* rope_v16;
+  const float* rope_qw;
+  const float* rope_kw;
+  const float* rope_tab;
+  int64_t rope_qd, rope_kvd;
+  float rope_eps;
 };
 
 // The split-K workspace: one slot per SM id (%smid < kSplitSlots), each large
@@ -273,18 +287,21 @@ struct EmbTable {
 cudaError_t launch_embed(const int64_t* ids, const uint8_t* mask, const int64_t* offsets, int C,
                          int64_t rows, int seq, const EmbTable& tok, const EmbTable& aud,
                          float* out, int H, cudaStream_t s);
-cudaError_t launch_mask_bias(const uint8_t* attn, int64_t n, float* bias, cudaStream_t s);
-cudaError_t launch_qk_norm_rope(float* q, float* k, const float* qw, const float* kw,
-                                const int64_t* pos, const float* inv_freq, int64_t rows,
-                                int n_heads, int n_kv, float eps, cudaStream_t s);
 cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, int C, int V,
                                   cudaStream_t s);
+// RoPE frequencies of head_dim 128: inv_freq[i] = (float) theta^(-2i/128).
+struct RopeFreq {
+  float inv_freq[64];
+};
+// The RoPE table of `rows` positions: tab [rows, 64] of (cos, sin) fp32 pairs.
+cudaError_t launch_rope_table(const int64_t* pos, const RopeFreq& f, int64_t rows, float* tab,
+                              cudaStream_t s);
 // q / k RMSNorm + RoPE written as fp16 (q16, k16) and v converted to fp16
-// (v16): the operands of ovb_attention_h.
+// (v16): the operands of ovb_attention_h.  tab from launch_rope_table.
 cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float* v, void* q16,
                                     void* k16, void* v16, const float* qw, const float* kw,
-                                    const int64_t* pos, const float* inv_freq, int64_t rows,
-                                    int n_heads, int n_kv, float eps, cudaStream_t s);
+                                    const float* tab, int64_t rows, int n_heads, int n_kv,
+                                    float eps, cudaStream_t s);
 cudaError_t read_and_clear_status_lm(int* out, cudaStream_t s);
 cudaError_t read_and_clear_status_att(int* out, cudaStream_t s);
 // Index into kTileNF of the tile width used by the fp16 mainloop.

@@ -318,6 +318,29 @@ def linear_h_sliced(a16: torch.Tensor, w: Weight, Cs: list[torch.Tensor]):
     return Cs
 
 
+def linear_h_qk_rope(a16: torch.Tensor, w: Weight, n_heads: int, n_kv: int, q_norm: torch.Tensor,
+                     k_norm: torch.Tensor, eps: float, table: torch.Tensor, out=None):
+    """The q|k|v GEMM with the per-head q/k RMSNorm + RoPE fused into its
+    epilogue (ovb_linear_h_qk_rope): returns fp16 (q16 [M, n_heads*128], k16,
+    v16 [M, n_kv*128]), the same bytes as linear_h_sliced into fp32 q / k / v
+    followed by attention.qk_norm_rope_f16.  ``table`` from
+    attention.rope_table."""
+    M = a16.shape[0]
+    if out is None:
+        out = (torch.empty((M, n_heads * 128), dtype=torch.float16, device=a16.device),
+               torch.empty((M, n_kv * 128), dtype=torch.float16, device=a16.device),
+               torch.empty((M, n_kv * 128), dtype=torch.float16, device=a16.device))
+    for t in (q_norm, k_norm, table, *out):
+        if not t.is_contiguous():
+            raise ValueError("q_norm, k_norm, table and the outputs must be contiguous")
+    q16, k16, v16 = out
+    L.check(L.lib().ovb_linear_h_qk_rope(M, w.handle, _dev_ptr(a16), n_heads, n_kv, 128,
+                                         _dev_ptr(q_norm), _dev_ptr(k_norm), float(eps),
+                                         _dev_ptr(table), _dev_ptr(q16), _dev_ptr(k16),
+                                         _dev_ptr(v16), _stream()))
+    return out
+
+
 def linear_f32(A: torch.Tensor, w: Weight, C=None, accumulate: bool = False):
     """ov::linear_f32 / linear_f32_ld with accumulate (Mat::mul / mul_add on
     an fp32 weight, mat.cpp:11-13, :39-43) on the fp16 tensor cores: A to

@@ -70,3 +70,26 @@ def test_static_linear_checks_arguments_before_the_device():
     assert lib.ovb_linear_static(4, C.addressof(fake), None, 0, None, 0, 0, None) == \
         L.OVB_ERR_INVALID_ARG
     assert b"A/C" in lib.ovb_last_error()
+
+
+def test_rope_entry_points_check_arguments_before_the_device():
+    """The RoPE table, the unfused q/k norm + RoPE and the fused q|k|v GEMM
+    reject bad shapes and null pointers without touching a device; zero rows
+    are a no-op."""
+    lib = L.lib()
+    assert lib.ovb_rope_table(None, 0, 128, 1e6, None, None) == L.OVB_OK
+    assert lib.ovb_rope_table(None, 4, 64, 1e6, None, None) == L.OVB_ERR_INVALID_ARG
+    assert b"head_dim" in lib.ovb_last_error()
+    assert lib.ovb_rope_table(None, 4, 128, 1e6, None, None) == L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_qk_norm_rope_f16(0, None, None, None, 16, 8, 128, None, None, 1e-6, None,
+                                    None, None, None, None) == L.OVB_OK
+    assert lib.ovb_qk_norm_rope_f16(4, None, None, None, 16, 8, 128, None, None, 1e-6, None,
+                                    None, None, None, None) == L.OVB_ERR_INVALID_ARG
+    assert lib.ovb_qk_norm_rope_f16(4, None, None, None, 16, 8, 96, None, None, 1e-6, None,
+                                    None, None, None, None) == L.OVB_ERR_INVALID_ARG
+    assert b"head_dim" in lib.ovb_last_error()
+    assert lib.ovb_linear_h_qk_rope(0, None, None, 16, 8, 128, None, None, 1e-6, None, None,
+                                    None, None, None) == L.OVB_OK
+    assert lib.ovb_linear_h_qk_rope(4, None, None, 16, 8, 128, None, None, 1e-6, None, None,
+                                    None, None, None) == L.OVB_ERR_INVALID_ARG
+    assert b"null" in lib.ovb_last_error()

@@ -1,0 +1,134 @@
+"""The q / k RMSNorm + RoPE of the LM forward on the GPU: the RoPE table
+(ovb_rope_table), the unfused fp16 kernel (ovb_qk_norm_rope_f16) and the
+q|k|v GEMM with it fused into its epilogue (ovb_linear_h_qk_rope).
+
+* The table against cos / sin in float64 of the same fp32 angles
+  (qk_norm_rope_f32's table, cpp/src/backend/cpu/ops_cpu.cpp:945-986).
+* The unfused kernel against a float64 restatement of qk_norm_rope_f32
+  (ops_cpu.cpp:945-1013) on the same table, to the fp16 rounding of the
+  outputs.
+* The fused GEMM against the unfused sequence (ovb_linear_h_sliced into fp32
+  q / k / v, then ovb_qk_norm_rope_f16): bit for bit, for the LM's shape and
+  for head layouts whose tiles mix q, k and v heads or end on a single head,
+  over ragged row counts.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import ovnative_b200 as ovb
+
+pytestmark = pytest.mark.gpu
+
+EPS = 1e-6
+THETA = 1e6
+
+
+def inv_freq(theta=THETA):
+    return np.array([np.float32(theta ** (-2.0 * i / 128.0)) for i in range(64)], np.float32)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def test_rope_table_matches_cos_sin_of_the_fp32_angles(cuda):
+    rng = np.random.default_rng(1)
+    pos = rng.integers(0, 4096, size=777).astype(np.int64)
+    tab = host(ovb.rope_table(torch.from_numpy(pos).to(cuda), THETA))
+    ang = (pos.astype(np.float32)[:, None] * inv_freq()[None, :]).astype(np.float32)
+    np.testing.assert_allclose(tab[..., 0], np.cos(ang.astype(np.float64)), rtol=0, atol=2e-6)
+    np.testing.assert_allclose(tab[..., 1], np.sin(ang.astype(np.float64)), rtol=0, atol=2e-6)
+
+
+def norm_rope_ref(x, w, tab):
+    """qk_norm_rope_f32 on [rows, heads, 128] in float64 with the table's
+    cos / sin."""
+    x = x.astype(np.float64)
+    s = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True) / 128.0 + EPS)
+    a = x[..., :64] * s * w[:64]
+    b = x[..., 64:] * s * w[64:]
+    c = tab[:, None, :, 0].astype(np.float64)
+    sn = tab[:, None, :, 1].astype(np.float64)
+    return np.concatenate([a * c - b * sn, b * c + a * sn], -1)
+
+
+def test_unfused_kernel_against_the_reference_formula(cuda):
+    rng = np.random.default_rng(2)
+    rows, H, KV = 301, 16, 8
+    q = rng.standard_normal((rows, H * 128)).astype(np.float32) * 3
+    k = rng.standard_normal((rows, KV * 128)).astype(np.float32)
+    v = rng.standard_normal((rows, KV * 128)).astype(np.float32)
+    qw = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kw = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    pos = np.arange(rows, dtype=np.int64)
+    d = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    tab = ovb.rope_table(d(pos), THETA)
+    q16, k16, v16 = ovb.qk_norm_rope_f16(d(q), d(k), d(v), d(qw), d(kw), EPS, tab)
+    tabh = host(tab)
+    for got, x, w, n in ((q16, q, qw, H), (k16, k, kw, KV)):
+        want = norm_rope_ref(x.reshape(rows, n, 128), w, tabh).reshape(rows, n * 128)
+        g = host(got).astype(np.float64)
+        np.testing.assert_allclose(g, want, rtol=1e-3, atol=1e-3 * np.abs(want).max())
+    np.testing.assert_array_equal(host(v16), v.astype(np.float16))
+    assert ovb.device_status() == 0
+
+
+def qkv_weight(rng, H, KV, K):
+    parts = []
+    for n in (H * 128, KV * 128, KV * 128):
+        W = rng.integers(-127, 128, size=(n, K), dtype=np.int8)
+        sc = (np.abs(rng.standard_normal(n)) * 0.02 / 127).astype(np.float32)
+        parts.append(ovb.Weight.from_nk(W, sc, f16=True))
+    w = ovb.Weight.concat(parts)
+    for p in parts:
+        p.close()
+    return w
+
+
+@pytest.mark.parametrize("H,KV,K", [(16, 8, 1024), (2, 1, 256), (3, 1, 320), (4, 2, 64)])
+@pytest.mark.parametrize("M", [1, 77, 128, 300, 1000])
+def test_fused_qkv_gemm_equals_the_unfused_sequence(cuda, H, KV, K, M):
+    rng = np.random.default_rng(M * 100 + H)
+    w = qkv_weight(rng, H, KV, K)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    x = d(rng.standard_normal((M, K)).astype(np.float32))
+    gain = d(np.ones(K, np.float32))
+    a16, _ = ovb.rmsnorm_quantize_f32(x, gain, EPS, f16=True)
+    qw = d(rng.uniform(0.5, 1.5, 128).astype(np.float32))
+    kw = d(rng.uniform(0.5, 1.5, 128).astype(np.float32))
+    pos = d(rng.permutation(max(M, 2048))[:M].astype(np.int64))
+    tab = ovb.rope_table(pos, THETA)
+    q = torch.empty((M, H * 128), device=cuda)
+    k = torch.empty((M, KV * 128), device=cuda)
+    v = torch.empty((M, KV * 128), device=cuda)
+    ovb.linear_h_sliced(a16, w, [q, k, v])
+    want = ovb.qk_norm_rope_f16(q, k, v, qw, kw, EPS, tab)
+    got = ovb.linear_h_qk_rope(a16, w, H, KV, qw, kw, EPS, tab)
+    for g, e in zip(got, want):
+        np.testing.assert_array_equal(host(g).view(np.uint16), host(e).view(np.uint16))
+    assert ovb.device_status() == 0
+    w.close()
+
+
+def test_fused_qkv_gemm_flags_fp16_overflow(cuda):
+    """A v value beyond the fp16 range sets status bit 16 (q and k are
+    normalised, so only v can leave the range)."""
+    rng = np.random.default_rng(7)
+    H, KV, K, M = 2, 1, 64, 40
+    parts = []
+    for n in (H * 128, KV * 128, KV * 128):
+        W = rng.integers(-127, 128, size=(n, K), dtype=np.int8)
+        parts.append(ovb.Weight.from_nk(W, np.full(n, 100.0, np.float32), f16=True))
+    w = ovb.Weight.concat(parts)
+    a16, _ = ovb.rmsnorm_quantize_f32(torch.full((M, K), 8.0, device=cuda),
+                                      torch.full((K,), 100.0, device=cuda), EPS, f16=True)
+    one = torch.ones(128, device=cuda)
+    tab = ovb.rope_table(torch.arange(M, device=cuda, dtype=torch.int64), THETA)
+    ovb.linear_h_qk_rope(a16, w, H, KV, one, one, EPS, tab)
+    assert ovb.device_status() & 16
+    for p in (*parts, w):
+        p.close()
