@@ -453,13 +453,16 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 //
 // One CTA per (segment, block of 128 query rows, kv head, pair of the query
 // heads that share it): the two heads' Q tiles stay in shared memory and every
-// K / V tile is loaded once for both.  320 threads:
+// K / V tile is loaded once for both.  352 threads:
 //   warps 0-3  softmax of head A (thread = query row = TMEM lane),
 //   warps 4-7  softmax of head B,
 //   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles into a
 //              two-stage ring (fp16, 128-byte swizzle, two 64-column boxes
 //              per tile),
-//   warp 9     TMEM allocator and MMA issuer (one thread).
+//   warp 9     TMEM allocator and MMA issuer (one thread),
+//   warp 10    watcher: waits on the mbarriers the MMA issuer needs and meets
+//              it on a named barrier, so that the issuer never waits on an
+//              mbarrier while its MMAs are in flight.
 // TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512) fp32
 // columns; P (fp16 pairs) overwrites the first 64 columns of its head's S.
 // The MMA issue order ping-pongs the heads,
@@ -481,7 +484,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 // fully masked rows) gives zeros, as ov::attention_head_f32 does.
 namespace {
 
-constexpr int kHThreads = 320;
+constexpr int kHThreads = 352;
+constexpr int kHBarW = 1;  // named barrier of the MMA warp and the watcher warp
 constexpr int kHMaxTiles = 256;  // key tiles per segment (32768 rows)
 constexpr uint32_t kHBox = 128 * 128;         // bytes of one 64-column fp16 box (128 rows)
 constexpr uint32_t kHTile = 2 * kHBox;        // one 128 x 128 fp16 tile
@@ -501,6 +505,7 @@ struct AttnHCtl {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  int wabort;  // set by the watcher warp only (see its loop)
   int n_act;
   int16_t act[kHMaxTiles];  // key tiles with something to attend, in order
   // how each active tile's scores are formed: 0 plain (every key attended and
@@ -522,6 +527,10 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t addr, uint32_t l
   d |= static_cast<uint64_t>(1) << 46;
   d |= static_cast<uint64_t>(2) << 61;
   return d;
+}
+
+__device__ __forceinline__ void bar_sync_n(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -559,7 +568,11 @@ __global__ void __launch_bounds__(kHThreads, 1)
   const int nkt = (S + 127) / 128;
   const int kx = sg.kv_x + kv * 128;
 
-  if (tid == 0) {
+  // Set-up, three warps at once: warp 8's thread initialises the barriers
+  // and starts the Q loads (they need nothing else), warp 0 lists the key
+  // tiles with something to attend (one load of 32 tile classes per lane
+  // round, compacted by ballot), warp 9 allocates TMEM.
+  if (warp == 8 && lane == 0) {
     mbar_init(smem_u32(&ctl->q_full), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&ctl->kv_full[i]), 1);
@@ -570,16 +583,33 @@ __global__ void __launch_bounds__(kHThreads, 1)
     }
     mbar_init(smem_u32(&ctl->mma_done), 1);
     ctl->abort = 0;
-    int n = 0;
-    for (int j = 0; j < nkt; ++j) {
-      const int cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : (sg.bias ? 2 : 0);
-      if (cls == 3) continue;
-      ctl->act[n] = static_cast<int16_t>(j);
-      ctl->kind[n] = static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > S ? 1 : 0));
-      ++n;
-    }
-    ctl->n_act = n;
+    ctl->wabort = 0;
     fence_mbar_init();
+    const uint32_t qbytes = static_cast<uint32_t>(nh) * kHTile;
+    mbar_arrive_expect_tx(smem_u32(&ctl->q_full), qbytes);
+    for (int h = 0; h < nh; ++h)
+      for (int b = 0; b < 2; ++b)
+        tma_load_2d(sbase + kHOffQ + h * kHTile + b * kHBox, &args.tm_q,
+                    sg.q_x + (head0 + h) * 128 + b * 64, sg.q_y + row0, smem_u32(&ctl->q_full));
+  }
+  if (warp == 0) {
+    int n = 0;
+    for (int j0 = 0; j0 < nkt; j0 += 32) {
+      const int j = j0 + lane;
+      int cls = 3;
+      if (j < nkt)
+        cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : (sg.bias ? 2 : 0);
+      const bool on = cls != 3;
+      const unsigned m = __ballot_sync(0xffffffffu, on);
+      if (on) {
+        const int at = n + __popc(m & ((1u << lane) - 1u));
+        ctl->act[at] = static_cast<int16_t>(j);
+        ctl->kind[at] =
+            static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > S ? 1 : 0));
+      }
+      n += __popc(m);
+    }
+    if (lane == 0) ctl->n_act = n;
   }
   if (warp == 9) {
     tmem_alloc(smem_u32(&ctl->tmem_base), 512);
@@ -601,14 +631,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint32_t qbytes = static_cast<uint32_t>(nh) * kHTile;
-      mbar_arrive_expect_tx(smem_u32(&ctl->q_full), qbytes);
-      for (int h = 0; h < nh; ++h)
-        for (int b = 0; b < 2; ++b)
-          tma_load_2d(sbase + kHOffQ + h * kHTile + b * kHBox, &args.tm_q,
-                      sg.q_x + (head0 + h) * 128 + b * 64, sg.q_y + row0,
-                      smem_u32(&ctl->q_full));
+    if (lane == 0) {  // the Q loads were issued during the set-up
       int issued = 0;
       for (int i = 0; i < n_act && ok; ++i) {
         const int st = i & 1;
@@ -632,59 +655,100 @@ __global__ void __launch_bounds__(kHThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t id_s = idesc_f16(128, 128);
-      const uint32_t id_o = idesc_f16(128, 128) | (1u << 16);  // B (V) MN-major
-      auto issue_s = [&](int h, int st) {
-        const uint32_t qa = sbase + kHOffQ + h * kHTile;
-        const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile;
+    // The whole warp meets the watcher (warp 10) on named barrier kHBarW
+    // before each step; lane 0 issues.  A thread with MMAs in flight would
+    // pay ~400 clocks for each mbarrier wait of its own, so the MMA warp
+    // never waits on an mbarrier until its last commit.
+    const uint32_t id_s = idesc_f16(128, 128);
+    const uint32_t id_o = idesc_f16(128, 128) | (1u << 16);  // B (V) MN-major
+    auto issue_s = [&](int h, int st) {
+      if (lane != 0) return;
+      const uint32_t qa = sbase + kHOffQ + h * kHTile;
+      const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = static_cast<uint32_t>((kk >> 2) * kHBox + (kk & 3) * 32);
-          mma_f16_ss(tmem + h * 128, sw128_kmajor_desc(qa, off), sw128_kmajor_desc(kb, off), id_s,
-                     kk > 0 ? 1u : 0u);
-        }
-        tc_commit(smem_u32(&ctl->s_full[h]));
-      };
-      auto issue_pv = [&](int h, int st, bool first) {
-        const uint32_t vb = sbase + kHOffKV + (2 * st + 1) * kHTile;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8,
-                     sw128_mnmajor_desc(vb + kk * 2048, kHBox, 1024), id_o,
-                     (!first || kk > 0) ? 1u : 0u);
-      };
-      if (wait(&ctl->q_full, 0u) && n_act > 0 && wait(&ctl->kv_full[0], 0u)) {
-        tc_fence_after();
-        for (int h = 0; h < nh; ++h) issue_s(h, 0);
-        for (int i = 0; i < n_act && ok; ++i) {
-          const int st = i & 1;
-          const bool more = i + 1 < n_act;
-          if (!wait(&ctl->p_full[0], static_cast<uint32_t>(i) & 1u)) break;
-          tc_fence_after();
-          issue_pv(0, st, i == 0);
-          if (!more) tc_commit(smem_u32(&ctl->o_final[0]));
-          if (more) {
-            if (!wait(&ctl->kv_full[st ^ 1], static_cast<uint32_t>((i + 1) >> 1) & 1u)) break;
-            tc_fence_after();
-            issue_s(0, st ^ 1);
-          }
-          if (nh == 2) {
-            if (!wait(&ctl->p_full[1], static_cast<uint32_t>(i) & 1u)) break;
-            tc_fence_after();
-            issue_pv(1, st, i == 0);
-            if (!more) tc_commit(smem_u32(&ctl->o_final[1]));
-          }
-          tc_commit(smem_u32(&ctl->kv_empty[st]));
-          if (nh == 2 && more) issue_s(1, st ^ 1);
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = static_cast<uint32_t>((kk >> 2) * kHBox + (kk & 3) * 32);
+        mma_f16_ss(tmem + h * 128, sw128_kmajor_desc(qa, off), sw128_kmajor_desc(kb, off), id_s,
+                   kk > 0 ? 1u : 0u);
       }
-      // every MMA issued has completed before TMEM is freed
+      tc_commit(smem_u32(&ctl->s_full[h]));
+    };
+    auto issue_pv = [&](int h, int st, bool first) {
+      if (lane != 0) return;
+      const uint32_t vb = sbase + kHOffKV + (2 * st + 1) * kHTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8,
+                   sw128_mnmajor_desc(vb + kk * 2048, kHBox, 1024), id_o,
+                   (!first || kk > 0) ? 1u : 0u);
+    };
+    auto commit = [&](uint64_t* bar) {
+      if (lane == 0) tc_commit(smem_u32(bar));
+    };
+    // one step: the watcher has seen what the next MMAs need (or gave up)
+    auto step = [&]() {
+      bar_sync_n(kHBarW, 64);
+      tc_fence_after();
+      return ctl->wabort == 0;
+    };
+    if (n_act > 0 && step()) {  // Q and the first K / V tile
+      for (int h = 0; h < nh; ++h) issue_s(h, 0);
+      for (int i = 0; i < n_act; ++i) {
+        const int st = i & 1;
+        const bool more = i + 1 < n_act;
+        if (!step()) break;  // P_A(i)
+        issue_pv(0, st, i == 0);
+        if (!more) commit(&ctl->o_final[0]);
+        if (more) {
+          if (!step()) break;  // K / V(i + 1)
+          issue_s(0, st ^ 1);
+        }
+        if (nh == 2) {
+          if (!step()) break;  // P_B(i)
+          issue_pv(1, st, i == 0);
+          if (!more) commit(&ctl->o_final[1]);
+        }
+        commit(&ctl->kv_empty[st]);
+        if (nh == 2 && more) issue_s(1, st ^ 1);
+      }
+    }
+    __syncwarp();
+    // every MMA issued has completed before TMEM is freed
+    if (lane == 0) {
       tc_commit(smem_u32(&ctl->mma_done));
       volatile int no_abort = 0;
       ovb_wait(smem_u32(&ctl->mma_done), 0u, &no_abort);
     }
+    __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ watcher
+    // The MMA warp's waits, in the MMA warp's order; each step ends in
+    // exactly one bar.sync on kHBarW, also after a failed wait (then wabort,
+    // which only this warp writes, stops the MMA warp at the same step).
+    auto seen = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, ovb_wait(smem_u32(bar), parity, abort));
+    };
+    auto release = [&](bool got) {
+      if (!got && lane == 0) {
+        ctl->wabort = 1;
+        *abort = 1;
+      }
+      bar_sync_n(kHBarW, 64);
+      return got;
+    };
+    if (n_act > 0 && release(seen(&ctl->q_full, 0u) && seen(&ctl->kv_full[0], 0u))) {
+      for (int i = 0; i < n_act; ++i) {
+        const int st = i & 1;
+        const bool more = i + 1 < n_act;
+        if (!release(seen(&ctl->p_full[0], static_cast<uint32_t>(i) & 1u))) break;
+        if (more &&
+            !release(seen(&ctl->kv_full[st ^ 1], static_cast<uint32_t>((i + 1) >> 1) & 1u)))
+          break;
+        if (nh == 2 && !release(seen(&ctl->p_full[1], static_cast<uint32_t>(i) & 1u))) break;
+      }
+    }
   } else {
+    // ------------------------------------------------------------ softmax  } else {
     // ------------------------------------------------------------ softmax
     const int h = warp >> 2;          // head of this warpgroup
     const int r = (warp & 3) * 32 + lane;

@@ -441,12 +441,23 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         const uint32_t dcol =
             tmem_base + lane_off + static_cast<uint32_t>(d * BN + 128 * eh);
         const bool row_ok = lane < rows;
+        // This row's (cos, sin) pairs: 64 per row, 128 floats; set s uses
+        // float4s 16s .. 16s + 15.  Set 0's are loaded here, so that their
+        // latency passes during pass 1; set 1's while set 0 is stored.
+        const float4* tab_row = reinterpret_cast<const float4*>(
+            args.rope_tab + (row_ok ? r0 + lane : 0) * 128);
+        float4 cs[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          cs[u] = (kind < 2 && row_ok) ? __ldg(tab_row + u) : make_float4(0.f, 0.f, 0.f, 0.f);
         float scale = 0.f;
         if (kind < 2) {
-          // pass 1: the sum of squares of the row's head
-          float s01[32], s23[32];
+          // pass 1: the sum of squares of the row's head, s01 = x0^2 + x1^2
+          // from chunks 0 and 1, then + (x2^2 + x3^2) sixteen columns at a
+          // time (few registers live beside the table)
+          float s01[32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t v[32];
             tmem_ld32(dcol + static_cast<uint32_t>(32 * c), v);
             tc_wait_ld32(v);
@@ -454,15 +465,26 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
             for (int i = 0; i < 32; ++i) {
               const float x =
                   __fmul_rn(__uint_as_float(v[i]), __shfl_sync(0xffffffffu, wsl[c], i));
-              const float x2 = __fmul_rn(x, x);
-              if (c == 0) s01[i] = x2;
-              if (c == 1) s01[i] = __fadd_rn(s01[i], x2);
-              if (c == 2) s23[i] = x2;
-              if (c == 3) s23[i] = __fadd_rn(s23[i], x2);
+              s01[i] = c == 0 ? __fmul_rn(x, x) : __fadd_rn(s01[i], __fmul_rn(x, x));
             }
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s01[i] = __fadd_rn(s01[i], s23[i]);
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t v2[16], v3[16];
+            tmem_ld16(dcol + static_cast<uint32_t>(64 + 16 * hf), v2);
+            tmem_ld16(dcol + static_cast<uint32_t>(96 + 16 * hf), v3);
+            tc_wait_ld16(v2);
+            tc_wait_ld16(v3);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int i = 16 * hf + e;
+              const float x2 =
+                  __fmul_rn(__uint_as_float(v2[e]), __shfl_sync(0xffffffffu, wsl[2], i));
+              const float x3 =
+                  __fmul_rn(__uint_as_float(v3[e]), __shfl_sync(0xffffffffu, wsl[3], i));
+              s01[i] = __fadd_rn(s01[i], __fadd_rn(__fmul_rn(x2, x2), __fmul_rn(x3, x3)));
+            }
+          }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
@@ -486,45 +508,42 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
           ld = kvd;
           col0 = hc - qd - kvd;
         }
-        // This row's (cos, sin) pairs: 64 per row, 128 floats.
-        const float4* tab_row = reinterpret_cast<const float4*>(
-            args.rope_tab + (row_ok ? r0 + lane : 0) * 128);
-        // pass 2: set s = head elements 32s + i (lo) and 64 + 32s + i (hi)
+        // pass 2: set s = head elements 32s + i (lo) and 64 + 32s + i (hi),
+        // sixteen elements (two 16-byte chunks of lo and of hi) at a time
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-          uint32_t va[32], vb[32];
-          tmem_ld32(dcol + static_cast<uint32_t>(32 * s), va);
-          tmem_ld32(dcol + static_cast<uint32_t>(64 + 32 * s), vb);
-          tc_wait_ld32(va);
-          tc_wait_ld32(vb);
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {  // elements 8g .. 8g + 7: float4s 16s + 4g .. + 3
-            float4 cs4[4];
+          for (int hf = 0; hf < 2; ++hf) {
+          uint32_t va[16], vb[16];
+          tmem_ld16(dcol + static_cast<uint32_t>(32 * s + 16 * hf), va);
+          tmem_ld16(dcol + static_cast<uint32_t>(64 + 32 * s + 16 * hf), vb);
+          tc_wait_ld16(va);
+          tc_wait_ld16(vb);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              cs4[u] = (kind < 2 && row_ok) ? __ldg(tab_row + 16 * s + 4 * g + u)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int gg = 0; gg < 2; ++gg) {  // elements 8g .. 8g + 7 of the set: cs[4g .. 4g + 3]
+            const int g = 2 * hf + gg;
             uint32_t lo_w[4], hi_w[4];
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
               float lo[2], hi[2];
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
-                const int i = 8 * g + e + h;
+                const int i = 8 * g + e + h;  // element of the set
+                const int iv = 8 * gg + e + h;  // element of va / vb
                 const float x =
-                    __fmul_rn(__uint_as_float(va[i]), __shfl_sync(0xffffffffu, wsl[s], i));
+                    __fmul_rn(__uint_as_float(va[iv]), __shfl_sync(0xffffffffu, wsl[s], i));
                 const float y =
-                    __fmul_rn(__uint_as_float(vb[i]), __shfl_sync(0xffffffffu, wsl[s + 2], i));
+                    __fmul_rn(__uint_as_float(vb[iv]), __shfl_sync(0xffffffffu, wsl[s + 2], i));
                 const float wa = __shfl_sync(0xffffffffu, nwl[s], i);
                 const float wb = __shfl_sync(0xffffffffu, nwl[s + 2], i);
                 if (kind < 2) {
-                  const float4 c2 = cs4[(e + h) >> 1];
-                  const float cs = ((e + h) & 1) ? c2.z : c2.x;
+                  const float4 c2 = cs[4 * g + ((e + h) >> 1)];
+                  const float cs_ = ((e + h) & 1) ? c2.z : c2.x;
                   const float sn = ((e + h) & 1) ? c2.w : c2.y;
                   const float a = __fmul_rn(__fmul_rn(x, scale), wa);
                   const float b = __fmul_rn(__fmul_rn(y, scale), wb);
-                  lo[h] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-                  hi[h] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+                  lo[h] = __fsub_rn(__fmul_rn(a, cs_), __fmul_rn(b, sn));
+                  hi[h] = __fadd_rn(__fmul_rn(b, cs_), __fmul_rn(a, sn));
                 } else {
                   lo[h] = x;
                   hi[h] = y;
@@ -541,6 +560,13 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                 make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
             *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * ((4 + g) ^ (lane & 7))) =
                 make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+          }
+          }
+          if (s == 0) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              cs[u] = (kind < 2 && row_ok) ? __ldg(tab_row + 16 + u)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
           }
           __syncwarp();
           // chunk k of row r: columns 32s + 8k (k < 4) or 64 + 32s + 8(k - 4)
