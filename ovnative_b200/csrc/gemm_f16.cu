@@ -86,6 +86,9 @@ constexpr uint32_t kABytesF = kBlockM * kStageKF;
 // row-per-lane float4 writes and the 4-rows-per-instruction float4 reads of
 // a 32x32 chunk are free of bank conflicts.
 constexpr int kStgStrideF = 36;
+// Per epilogue warp of the fused q|k|v mode: one head's wscale and norm
+// weights, staged for broadcast reads.
+constexpr int kRopeColFloats = 256;
 // named barriers (0 is __syncthreads)
 constexpr int kBarStage = 1;                    // + s: converters -> MMA warp
 constexpr int kBarDfree = kBarStage + kStagesF;  // + d: epilogue -> MMA warp
@@ -381,6 +384,12 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   }
 }
 
+// Element e (0 .. 7) of two float4.
+__device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
+  const float4 q = v[e >> 2];
+  return (e & 3) == 0 ? q.x : (e & 3) == 1 ? q.y : (e & 3) == 2 ? q.z : q.w;
+}
+
 // The epilogue loop of the fused q|k|v mode (args.rope_q16 non-null; BN =
 // 256, two 128-column heads per tile).  Warp (quarter, eh) takes head eh of
 // the tile for TMEM lanes 32*quarter..: each thread holds one row of the
@@ -390,16 +399,19 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
 // (s_l = (x_l^2 + x_{l+32}^2) + (x_{l+64}^2 + x_{l+96}^2), then pairwise sums
 // at distances 16, 8, .., 1, the order of its warp tree), the same scale and
 // rotation -- so the fp16 outputs equal the unfused sequence bit for bit; v
-// heads are converted.  Two passes over TMEM: the sum of squares, then the
-// rotation set by set (columns 32s.. with 64+32s.., s = 0, 1), each set's 64
-// fp16 outputs staged in shared memory (32 rows x 128 bytes, 16-byte chunks
+// heads are converted.  The per-column values (wscale, norm weight) are the
+// same for every lane: they are read as float4 broadcasts.  Two passes over
+// TMEM, sixteen columns at a time: the sum of squares, then the rotation of
+// set s (head elements 32s + i with 64 + 32s + i, s = 0, 1), whose 64 fp16
+// outputs are staged in shared memory (32 rows x 128 bytes, 16-byte chunks
 // XOR-swizzled by row: conflict-free both ways) and written as 64-byte row
-// segments, 8 lanes per row.
+// segments, 8 lanes per row.  The row's RoPE table (512 bytes) is loaded
+// sixteen elements at a time, one step ahead.
 template <int BN, int kAcc>
 __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_t* tfull,
                                                    volatile int* abort, uint32_t tmem_base,
-                                                   float* stg, int quarter, int eh, int dfree_bar,
-                                                   int64_t tiles, int64_t m_tiles,
+                                                   float* stg, float* colv, int quarter, int eh,
+                                                   int dfree_bar, int64_t tiles, int64_t m_tiles,
                                                    int64_t my_tiles, int64_t tile_first,
                                                    int64_t tile_step) {
   static_assert(BN == 256, "two heads per tile, one per epilogue warp of a lane quarter");
@@ -418,15 +430,24 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
     const int64_t hc = n0 + 128 * eh;  // this warp's head: columns hc .. hc + 127
     const bool has = hc < N;           // uniform per warp
     const int kind = hc < qd ? 0 : (hc < qd + kvd ? 1 : 2);  // q, k or v head
-    // Lane l: the wscale of columns hc + 32 j + l and the norm weight of head
-    // element 32 j + l, fetched before the accumulator is ready.
-    const float* nw = kind == 0 ? args.rope_qw : args.rope_kw;
-    float wsl[4], nwl[4];
+    // The head's wscale (colv[0, 128)) and norm weights (colv[128, 256))
+    // into this warp's shared area before the accumulator is ready; read
+    // back as float4 broadcasts (every lane the same columns).
+    if (has) {
+      const float* nw = kind == 0 ? args.rope_qw : args.rope_kw;
+      float wv[4], nv[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      wsl[j] = has ? __ldg(args.wscale + hc + 32 * j + lane) : 0.f;
-      nwl[j] = (has && kind < 2) ? __ldg(nw + 32 * j + lane) : 0.f;
+      for (int j = 0; j < 4; ++j) {
+        wv[j] = __ldg(args.wscale + hc + 32 * j + lane);
+        nv[j] = kind < 2 ? __ldg(nw + 32 * j + lane) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        colv[32 * j + lane] = wv[j];
+        colv[128 + 32 * j + lane] = nv[j];
+      }
     }
+    __syncwarp();
     const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
     if (!__all_sync(0xffffffffu, got)) {
       if (lane == 0) {
@@ -441,48 +462,48 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         const uint32_t dcol =
             tmem_base + lane_off + static_cast<uint32_t>(d * BN + 128 * eh);
         const bool row_ok = lane < rows;
+        bool bad = false;  // an fp16 output of this row overflowed (or is NaN)
+        const float4* ws4 = reinterpret_cast<const float4*>(colv);
+        const float4* nw4 = reinterpret_cast<const float4*>(colv + 128);
         // This row's (cos, sin) pairs: 64 per row, 128 floats; set s uses
-        // float4s 16s .. 16s + 15.  Set 0's are loaded here, so that their
-        // latency passes during pass 1; set 1's while set 0 is stored.
+        // float4s 16s .. 16s + 15.
         const float4* tab_row = reinterpret_cast<const float4*>(
             args.rope_tab + (row_ok ? r0 + lane : 0) * 128);
-        float4 cs[16];
+        // the table of pass 2's first sixteen elements, early
+        float4 cs[8];
 #pragma unroll
-        for (int u = 0; u < 16; ++u)
+        for (int u = 0; u < 8; ++u)
           cs[u] = (kind < 2 && row_ok) ? __ldg(tab_row + u) : make_float4(0.f, 0.f, 0.f, 0.f);
         float scale = 0.f;
         if (kind < 2) {
-          // pass 1: the sum of squares of the row's head, s01 = x0^2 + x1^2
-          // from chunks 0 and 1, then + (x2^2 + x3^2) sixteen columns at a
-          // time (few registers live beside the table)
+          // pass 1: s01 = x0^2 + x1^2 (chunks 0 and 1), then + (x2^2 + x3^2)
           float s01[32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t v[32];
-            tmem_ld32(dcol + static_cast<uint32_t>(32 * c), v);
-            tc_wait_ld32(v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float x =
-                  __fmul_rn(__uint_as_float(v[i]), __shfl_sync(0xffffffffu, wsl[c], i));
-              s01[i] = c == 0 ? __fmul_rn(x, x) : __fadd_rn(s01[i], __fmul_rn(x, x));
-            }
-          }
-#pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
-            uint32_t v2[16], v3[16];
-            tmem_ld16(dcol + static_cast<uint32_t>(64 + 16 * hf), v2);
-            tmem_ld16(dcol + static_cast<uint32_t>(96 + 16 * hf), v3);
-            tc_wait_ld16(v2);
-            tc_wait_ld16(v3);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int i = 16 * hf + e;
-              const float x2 =
-                  __fmul_rn(__uint_as_float(v2[e]), __shfl_sync(0xffffffffu, wsl[2], i));
-              const float x3 =
-                  __fmul_rn(__uint_as_float(v3[e]), __shfl_sync(0xffffffffu, wsl[3], i));
-              s01[i] = __fadd_rn(s01[i], __fadd_rn(__fmul_rn(x2, x2), __fmul_rn(x3, x3)));
+            for (int pr = 0; pr < 2; ++pr) {  // chunks 2 pr and 2 pr + 1
+              uint32_t va[16], vb[16];
+              tmem_ld16(dcol + static_cast<uint32_t>(64 * pr + 16 * hf), va);
+              tmem_ld16(dcol + static_cast<uint32_t>(64 * pr + 32 + 16 * hf), vb);
+              tc_wait_ld16(va);
+              tc_wait_ld16(vb);
+#pragma unroll
+              for (int gg = 0; gg < 2; ++gg) {
+                float4 wa[2], wb[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  wa[u] = *(ws4 + 16 * pr + 4 * hf + 2 * gg + u);
+                  wb[u] = *(ws4 + 16 * pr + 8 + 4 * hf + 2 * gg + u);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const int iv = 8 * gg + e;
+                  const float x = __fmul_rn(__uint_as_float(va[iv]), f4_at2(wa, e));
+                  const float y = __fmul_rn(__uint_as_float(vb[iv]), f4_at2(wb, e));
+                  const float q2 = __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y));
+                  s01[16 * hf + iv] = pr == 0 ? q2 : __fadd_rn(s01[16 * hf + iv], q2);
+                }
+              }
             }
           }
 #pragma unroll
@@ -508,65 +529,75 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
           ld = kvd;
           col0 = hc - qd - kvd;
         }
-        // pass 2: set s = head elements 32s + i (lo) and 64 + 32s + i (hi),
-        // sixteen elements (two 16-byte chunks of lo and of hi) at a time
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
-          uint32_t va[16], vb[16];
-          tmem_ld16(dcol + static_cast<uint32_t>(32 * s + 16 * hf), va);
-          tmem_ld16(dcol + static_cast<uint32_t>(64 + 32 * s + 16 * hf), vb);
-          tc_wait_ld16(va);
-          tc_wait_ld16(vb);
+            // set s, elements 16 hf .. 16 hf + 15: lo columns 32s + 16hf ..,
+            // hi columns 64 + 32s + 16hf ..; cs holds their table, the next
+            // step's is loaded now
+            float4 cn[8];
+            const int nxt = 2 * s + hf + 1;
 #pragma unroll
-          for (int gg = 0; gg < 2; ++gg) {  // elements 8g .. 8g + 7 of the set: cs[4g .. 4g + 3]
-            const int g = 2 * hf + gg;
-            uint32_t lo_w[4], hi_w[4];
+            for (int u = 0; u < 8; ++u)
+              cn[u] = (nxt < 4 && kind < 2 && row_ok) ? __ldg(tab_row + 8 * nxt + u)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint32_t va[16], vb[16];
+            tmem_ld16(dcol + static_cast<uint32_t>(32 * s + 16 * hf), va);
+            tmem_ld16(dcol + static_cast<uint32_t>(64 + 32 * s + 16 * hf), vb);
+            tc_wait_ld16(va);
+            tc_wait_ld16(vb);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              float lo[2], hi[2];
+            for (int gg = 0; gg < 2; ++gg) {
+              const int g = 2 * hf + gg;  // 16-byte chunk g (lo) and 4 + g (hi)
+              // the eight elements' wscale and norm weights (broadcast reads)
+              float4 wa[2], wb[2], na[2], nb[2];
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int i = 8 * g + e + h;  // element of the set
-                const int iv = 8 * gg + e + h;  // element of va / vb
-                const float x =
-                    __fmul_rn(__uint_as_float(va[iv]), __shfl_sync(0xffffffffu, wsl[s], i));
-                const float y =
-                    __fmul_rn(__uint_as_float(vb[iv]), __shfl_sync(0xffffffffu, wsl[s + 2], i));
-                const float wa = __shfl_sync(0xffffffffu, nwl[s], i);
-                const float wb = __shfl_sync(0xffffffffu, nwl[s + 2], i);
-                if (kind < 2) {
-                  const float4 c2 = cs[4 * g + ((e + h) >> 1)];
-                  const float cs_ = ((e + h) & 1) ? c2.z : c2.x;
-                  const float sn = ((e + h) & 1) ? c2.w : c2.y;
-                  const float a = __fmul_rn(__fmul_rn(x, scale), wa);
-                  const float b = __fmul_rn(__fmul_rn(y, scale), wb);
-                  lo[h] = __fsub_rn(__fmul_rn(a, cs_), __fmul_rn(b, sn));
-                  hi[h] = __fadd_rn(__fmul_rn(b, cs_), __fmul_rn(a, sn));
-                } else {
-                  lo[h] = x;
-                  hi[h] = y;
-                }
-                if (row_ok && !(fabsf(lo[h]) <= 65504.f && fabsf(hi[h]) <= 65504.f))
-                  range_ok = false;
+              for (int u = 0; u < 2; ++u) {
+                wa[u] = *(ws4 + 8 * s + 2 * g + u);
+                wb[u] = *(ws4 + 16 + 8 * s + 2 * g + u);
+                na[u] = kind < 2 ? *(nw4 + 8 * s + 2 * g + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                nb[u] = kind < 2 ? *(nw4 + 16 + 8 * s + 2 * g + u)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
               }
-              const __half2 l2 = __floats2half2_rn(lo[0], lo[1]);
-              const __half2 h2 = __floats2half2_rn(hi[0], hi[1]);
-              lo_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
-              hi_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
-            *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * (g ^ (lane & 7))) =
-                make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
-            *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * ((4 + g) ^ (lane & 7))) =
-                make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
-          }
-          }
-          if (s == 0) {
+              uint32_t lo_w[4], hi_w[4];
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
-              cs[u] = (kind < 2 && row_ok) ? __ldg(tab_row + 16 + u)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int e = 0; e < 8; e += 2) {
+                float lo[2], hi[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int iv = 8 * gg + e + h;  // element of va / vb
+                  const int iw = e + h;           // element of wa / wb / na / nb
+                  const float x = __fmul_rn(__uint_as_float(va[iv]), f4_at2(wa, iw));
+                  const float y = __fmul_rn(__uint_as_float(vb[iv]), f4_at2(wb, iw));
+                  if (kind < 2) {
+                    const float4 c2 = cs[4 * gg + ((e + h) >> 1)];
+                    const float cs_ = ((e + h) & 1) ? c2.z : c2.x;
+                    const float sn = ((e + h) & 1) ? c2.w : c2.y;
+                    const float a = __fmul_rn(__fmul_rn(x, scale), f4_at2(na, iw));
+                    const float b = __fmul_rn(__fmul_rn(y, scale), f4_at2(nb, iw));
+                    lo[h] = __fsub_rn(__fmul_rn(a, cs_), __fmul_rn(b, sn));
+                    hi[h] = __fadd_rn(__fmul_rn(b, cs_), __fmul_rn(a, sn));
+                  } else {
+                    lo[h] = x;
+                    hi[h] = y;
+                  }
+                }
+                const __half2 l2 = __floats2half2_rn(lo[0], lo[1]);
+                const __half2 h2 = __floats2half2_rn(hi[0], hi[1]);
+                lo_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
+                hi_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+                // an fp16 output that is infinite or NaN: exponent bits all set
+                bad = bad || __vcmpeq2(lo_w[e >> 1] & 0x7c007c00u, 0x7c007c00u) != 0u ||
+                      __vcmpeq2(hi_w[e >> 1] & 0x7c007c00u, 0x7c007c00u) != 0u;
+              }
+              *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * (g ^ (lane & 7))) =
+                  make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+              *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * ((4 + g) ^ (lane & 7))) =
+                  make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) cs[u] = cn[u];
           }
           __syncwarp();
           // chunk k of row r: columns 32s + 8k (k < 4) or 64 + 32s + 8(k - 4)
@@ -581,6 +612,7 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
           }
           __syncwarp();
         }
+        if (row_ok && bad) range_ok = false;  // rows past M hold no outputs
       }
     }
     tc_fence_before();
@@ -1020,7 +1052,7 @@ struct CtlH {
 // [kSplit - 1 senders][128 rows][kOwn floats].  A split-K CTA needs more
 // than half of the SM's shared memory, so no two of them share an SM (or a
 // workspace slot).
-template <int BN, bool kSilu, int kSplit = 1>
+template <int BN, bool kSilu, int kSplit = 1, bool kRope = false>
 struct TileH {
   static_assert(kSplit == 1 || (!kSilu && (BN / kSplit) % 32 == 0), "split-K layout");
   static constexpr uint32_t kWBytes = BN * 128;
@@ -1030,7 +1062,8 @@ struct TileH {
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
   // epilogue staging: 32 x 32 fp32 chunks, or 32 rows x 64 bytes of the
   // fused SiLU*up epilogue's quantised output
-  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4);
+  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4) +
+                                    (kRope ? static_cast<size_t>(kEpiW) * kRopeColFloats * 4 : 0);
   static constexpr int kOwn = BN / kSplit;  // columns owned per rank
   static constexpr size_t kPartialFloats = static_cast<size_t>(kBlockM) * kOwn;  // per sender
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
@@ -1219,7 +1252,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ GemmArgs args) {
-  using T = TileH<BN, kSilu, kSplit>;
+  using T = TileH<BN, kSilu, kSplit, kRope>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1366,9 +1399,11 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
                                (warp - kFirstEpiH) >> 2, rank);
     } else if constexpr (kRope) {
       epilogue_rope_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                                      stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                                      (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles,
-                                      my_tiles, blockIdx.x, gridDim.x);
+                                      stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF),
+                                      stg_all + T::kEpiW * (32 * kStgStrideF) +
+                                          (warp - kFirstEpiH) * kRopeColFloats,
+                                      warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
+                                      m_tiles, my_tiles, blockIdx.x, gridDim.x);
     } else if constexpr (kSilu) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
       silu_epilogue<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
@@ -1403,7 +1438,7 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
 template <int BN, bool kSilu, int kSplit = 1, bool kRope = false>
 cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  using T = TileH<BN, kSilu, kSplit>;
+  using T = TileH<BN, kSilu, kSplit, kRope>;
   auto* kernel = gemm_h_kernel<BN, kSilu, kSplit, kRope>;
   int dev = 0;
   cudaGetDevice(&dev);

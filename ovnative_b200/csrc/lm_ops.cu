@@ -90,8 +90,8 @@ __global__ void rope_table_kernel(const int64_t* pos, RopeFreq f, int64_t rows, 
 //   b = (x[i+64] scale) w[i+64];  x[i] = a cos - b sin;  x[i+64] = b cos + a sin.
 // One block per row, one warp per head vector; lane l holds elements l,
 // l+32, l+64, l+96 and the sum of squares runs in a warp tree (the fused q|k|v
-// GEMM epilogue, gemm_f16.cu, reproduces this order).  A value beyond the
-// fp16 range sets status bit 16.
+// GEMM epilogue, gemm_f16.cu, reproduces this order).  An output that
+// rounds to an fp16 infinity (|x| >= 65520) or is NaN sets status bit 16.
 __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const float* v,
                                         __half* q16, __half* k16, __half* v16, const float* qw,
                                         const float* kw, const float2* tab, int64_t rows,
@@ -127,7 +127,7 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float x = xs[g][j];
-        range_ok = range_ok && fabsf(x) <= 65504.f;
+        range_ok = range_ok && fabsf(x) < 65520.f;
         v16[base + lane + 32 * j] = __float2half_rn(x);
       }
       continue;
@@ -153,7 +153,7 @@ __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const fl
       const float b = __fmul_rn(__fmul_rn(x[j + 2], scale), w[i + half]);
       const float lo = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
       const float hi = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
-      range_ok = range_ok && fabsf(lo) <= 65504.f && fabsf(hi) <= 65504.f;
+      range_ok = range_ok && fabsf(lo) < 65520.f && fabsf(hi) < 65520.f;
       dst[i] = __float2half_rn(lo);
       dst[i + half] = __float2half_rn(hi);
     }
