@@ -38,6 +38,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -497,21 +498,33 @@ constexpr float kHRescale = 8.f;              // base-2 units
 
 struct AttnHCtl {
   uint64_t q_full;
+  uint64_t q_empty;      // the item's last S has read Q (MMA commit)
   uint64_t kv_full[2];
   uint64_t kv_empty[2];
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_final[2];
+  uint64_t o_free[2];    // the epilogue of head h has read O_h (128 arrivals)
+  uint64_t list_full[2];   // the key-tile list of list slot b is written
+  uint64_t list_empty[2];  // ... and read by the watcher and the 8 softmax warps
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
   int wabort;  // set by the watcher warp only (see its loop)
-  int n_act;
-  int16_t act[kHMaxTiles];  // key tiles with something to attend, in order
+  int n_act[2];
+  int16_t act[2][kHMaxTiles];  // key tiles with something to attend, in order
   // how each active tile's scores are formed: 0 plain (every key attended and
   // inside the segment), 1 masked (class-1 bits and / or the segment's end),
   // 2 biased (the segment's fp32 bias, no table)
-  int8_t kind[kHMaxTiles];
+  int8_t kind[2][kHMaxTiles];
+};
+// Arrivals that release a list slot: the watcher warp and the 8 softmax warps.
+constexpr int kHListUsers = 9;
+
+// One work item: (segment, block of 128 query rows, kv head, pair of the
+// query heads sharing it), numbered from its segment's cta0.
+struct HItem {
+  int si, qb, kv, nh, head0, S, row0, nkt, kx;
 };
 constexpr size_t kAttHSmem = 1024 + kHOffCtl + sizeof(AttnHCtl);
 static_assert(kAttHSmem <= 227 * 1024, "attention_h shared memory");
@@ -529,6 +542,29 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t addr, uint32_t l
   return d;
 }
 
+// max(a, b, c) in one instruction (the 3-input form of max.f32).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (y0, y1) = (x0, x1) * m + n, one packed f32x2 FFMA (each lane an fma.rn).
+__device__ __forceinline__ void fma2(float x0, float x1, float m, float n, float& y0, float& y1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
+      "mov.b64 c, {%5, %5};\n\tfma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "f"(x0), "f"(x1), "f"(m), "f"(n));
+}
+
+// (s0, s1) += (a, b), one packed f32x2 FADD.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a, float b) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a), "f"(b));
+}
+
 __device__ __forceinline__ void bar_sync_n(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -537,6 +573,27 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ HItem decode_item(const AttnHArgs& args, int it) {
+  int si = 0;
+  for (int i = 1; i < args.n_segs; ++i)
+    if (it >= args.segs[i].cta0) si = i;
+  const AttnHSeg& sg = args.segs[si];
+  int rem = it - sg.cta0;
+  const int pair = rem % args.pairs;
+  rem /= args.pairs;
+  HItem w;
+  w.si = si;
+  w.kv = rem % args.n_kv;
+  w.qb = rem / args.n_kv;
+  w.S = sg.rows;
+  w.row0 = w.qb * 128;
+  w.head0 = w.kv * args.group + 2 * pair;
+  w.nh = min(2, args.group - 2 * pair);
+  w.nkt = (w.S + 127) / 128;
+  w.kx = sg.kv_x + w.kv * 128;
+  return w;
 }
 
 }  // namespace
@@ -550,66 +607,26 @@ __global__ void __launch_bounds__(kHThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   volatile int* abort = &ctl->abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int it0 = static_cast<int>(blockIdx.x), it_step = static_cast<int>(gridDim.x);
+  const int n_items = args.n_items;
 
-  // ---- this CTA's (segment, query block, kv head, head pair)
-  int si = 0;
-  for (int i = 1; i < args.n_segs; ++i)
-    if (static_cast<int>(blockIdx.x) >= args.segs[i].cta0) si = i;
-  const AttnHSeg& sg = args.segs[si];
-  int rem = static_cast<int>(blockIdx.x) - sg.cta0;
-  const int pair = rem % args.pairs;
-  rem /= args.pairs;
-  const int kv = rem % args.n_kv;
-  const int qb = rem / args.n_kv;
-  const int S = sg.rows;
-  const int row0 = qb * 128;
-  const int head0 = kv * args.group + 2 * pair;
-  const int nh = min(2, args.group - 2 * pair);  // heads in this CTA (1 or 2)
-  const int nkt = (S + 127) / 128;
-  const int kx = sg.kv_x + kv * 128;
-
-  // Set-up, three warps at once: warp 8's thread initialises the barriers
-  // and starts the Q loads (they need nothing else), warp 0 lists the key
-  // tiles with something to attend (one load of 32 tile classes per lane
-  // round, compacted by ballot), warp 9 allocates TMEM.
-  if (warp == 8 && lane == 0) {
+  if (tid == 0) {
     mbar_init(smem_u32(&ctl->q_full), 1);
+    mbar_init(smem_u32(&ctl->q_empty), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&ctl->kv_full[i]), 1);
       mbar_init(smem_u32(&ctl->kv_empty[i]), 1);
       mbar_init(smem_u32(&ctl->s_full[i]), 1);
       mbar_init(smem_u32(&ctl->p_full[i]), 128);
       mbar_init(smem_u32(&ctl->o_final[i]), 1);
+      mbar_init(smem_u32(&ctl->o_free[i]), 128);
+      mbar_init(smem_u32(&ctl->list_full[i]), 1);
+      mbar_init(smem_u32(&ctl->list_empty[i]), kHListUsers);
     }
     mbar_init(smem_u32(&ctl->mma_done), 1);
     ctl->abort = 0;
     ctl->wabort = 0;
     fence_mbar_init();
-    const uint32_t qbytes = static_cast<uint32_t>(nh) * kHTile;
-    mbar_arrive_expect_tx(smem_u32(&ctl->q_full), qbytes);
-    for (int h = 0; h < nh; ++h)
-      for (int b = 0; b < 2; ++b)
-        tma_load_2d(sbase + kHOffQ + h * kHTile + b * kHBox, &args.tm_q,
-                    sg.q_x + (head0 + h) * 128 + b * 64, sg.q_y + row0, smem_u32(&ctl->q_full));
-  }
-  if (warp == 0) {
-    int n = 0;
-    for (int j0 = 0; j0 < nkt; j0 += 32) {
-      const int j = j0 + lane;
-      int cls = 3;
-      if (j < nkt)
-        cls = args.tile_class ? args.tile_class[sg.tile0 + qb * nkt + j] : (sg.bias ? 2 : 0);
-      const bool on = cls != 3;
-      const unsigned m = __ballot_sync(0xffffffffu, on);
-      if (on) {
-        const int at = n + __popc(m & ((1u << lane) - 1u));
-        ctl->act[at] = static_cast<int16_t>(j);
-        ctl->kind[at] =
-            static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > S ? 1 : 0));
-      }
-      n += __popc(m);
-    }
-    if (lane == 0) ctl->n_act = n;
   }
   if (warp == 9) {
     tmem_alloc(smem_u32(&ctl->tmem_base), 512);
@@ -619,40 +636,91 @@ __global__ void __launch_bounds__(kHThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const int n_act = ctl->n_act;
-  bool ok = true;
-  auto wait = [&](uint64_t* bar, uint32_t parity) {
-    if (!ovb_wait(smem_u32(bar), parity, abort)) {
-      ok = false;
-      *abort = 1;
-    }
-    return ok;
-  };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {  // the Q loads were issued during the set-up
-      int issued = 0;
-      for (int i = 0; i < n_act && ok; ++i) {
-        const int st = i & 1;
-        if (i >= 2 && !wait(&ctl->kv_empty[st], static_cast<uint32_t>((i >> 1) - 1) & 1u)) break;
-        issued = i + 1;
-        const int ky = sg.kv_y + ctl->act[i] * 128;
-        const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile, vb = kb + kHTile;
-        mbar_arrive_expect_tx(smem_u32(&ctl->kv_full[st]), 2 * kHTile);
-        for (int b = 0; b < 2; ++b) {
-          tma_load_2d(kb + b * kHBox, &args.tm_k, kx + b * 64, ky, smem_u32(&ctl->kv_full[st]));
-          tma_load_2d(vb + b * kHBox, &args.tm_v, kx + b * 64, ky, smem_u32(&ctl->kv_full[st]));
+    // Per item: the whole warp writes the item's key-tile list into list
+    // slot c & 1 (once the item two back has released it); lane 0 then
+    // loads Q (once the previous item's last S has read its Q) and the key
+    // tiles into the two-stage ring.
+    bool ok = true;
+    int c = 0, q_loads = 0;
+    int64_t g = 0;  // key tiles loaded by this CTA
+    for (int it = it0; it < n_items && ok; it += it_step, ++c) {
+      const HItem w = decode_item(args, it);
+      const AttnHSeg& sg = args.segs[w.si];
+      const int b = c & 1;
+      if (c >= 2 &&
+          !__all_sync(0xffffffffu, ovb_wait(smem_u32(&ctl->list_empty[b]),
+                                            static_cast<uint32_t>((c >> 1) - 1) & 1u, abort))) {
+        if (lane == 0) *abort = 1;
+        ok = false;
+        break;
+      }
+      int n = 0;
+      for (int j0 = 0; j0 < w.nkt; j0 += 32) {
+        const int j = j0 + lane;
+        int cls = 3;
+        if (j < w.nkt)
+          cls = args.tile_class ? args.tile_class[sg.tile0 + w.qb * w.nkt + j] : (sg.bias ? 2 : 0);
+        const bool on = cls != 3;
+        const unsigned m = __ballot_sync(0xffffffffu, on);
+        if (on) {
+          const int at = n + __popc(m & ((1u << lane) - 1u));
+          ctl->act[b][at] = static_cast<int16_t>(j);
+          ctl->kind[b][at] =
+              static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > w.S ? 1 : 0));
+        }
+        n += __popc(m);
+      }
+      if (lane == 0) ctl->n_act[b] = n;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&ctl->list_full[b]));
+        if (c >= 1 &&
+            !ovb_wait(smem_u32(&ctl->q_empty), static_cast<uint32_t>(c - 1) & 1u, abort)) {
+          *abort = 1;
+          ok = false;
+        }
+        if (ok) {
+          mbar_arrive_expect_tx(smem_u32(&ctl->q_full), static_cast<uint32_t>(w.nh) * kHTile);
+          for (int h = 0; h < w.nh; ++h)
+            for (int bx = 0; bx < 2; ++bx)
+              tma_load_2d(sbase + kHOffQ + h * kHTile + bx * kHBox, &args.tm_q,
+                          sg.q_x + (w.head0 + h) * 128 + bx * 64, sg.q_y + w.row0,
+                          smem_u32(&ctl->q_full));
+          ++q_loads;
+        }
+        for (int i = 0; i < n && ok; ++i, ++g) {
+          const int st = static_cast<int>(g & 1);
+          if (g >= 2 && !ovb_wait(smem_u32(&ctl->kv_empty[st]),
+                                  static_cast<uint32_t>((g >> 1) - 1) & 1u, abort)) {
+            *abort = 1;
+            ok = false;
+            break;
+          }
+          const int ky = sg.kv_y + ctl->act[b][i] * 128;
+          const uint32_t kb = sbase + kHOffKV + (2 * st) * kHTile, vb = kb + kHTile;
+          mbar_arrive_expect_tx(smem_u32(&ctl->kv_full[st]), 2 * kHTile);
+          for (int bx = 0; bx < 2; ++bx) {
+            tma_load_2d(kb + bx * kHBox, &args.tm_k, w.kx + bx * 64, ky, smem_u32(&ctl->kv_full[st]));
+            tma_load_2d(vb + bx * kHBox, &args.tm_v, w.kx + bx * 64, ky, smem_u32(&ctl->kv_full[st]));
+          }
         }
       }
-      // every load this thread issued has landed before the CTA can exit
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    // every load lane 0 issued has landed before the CTA can exit
+    if (lane == 0) {
       volatile int no_abort = 0;
-      ovb_wait(smem_u32(&ctl->q_full), 0u, &no_abort);
-      for (int st = 0; st < 2 && st < issued; ++st) {
-        const int last = ((issued - 1 - st) / 2) * 2 + st;  // last tile loaded into stage st
+      if (q_loads > 0)
+        ovb_wait(smem_u32(&ctl->q_full), static_cast<uint32_t>(q_loads - 1) & 1u, &no_abort);
+      for (int st = 0; st < 2 && st < g; ++st) {
+        const int64_t last = ((g - 1 - st) / 2) * 2 + st;  // last tile loaded into stage st
         ovb_wait(smem_u32(&ctl->kv_full[st]), static_cast<uint32_t>(last >> 1) & 1u, &no_abort);
       }
     }
+    __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     // The whole warp meets the watcher (warp 10) on named barrier kHBarW
@@ -691,25 +759,49 @@ __global__ void __launch_bounds__(kHThreads, 1)
       tc_fence_after();
       return ctl->wabort == 0;
     };
-    if (n_act > 0 && step()) {  // Q and the first K / V tile
-      for (int h = 0; h < nh; ++h) issue_s(h, 0);
-      for (int i = 0; i < n_act; ++i) {
-        const int st = i & 1;
-        const bool more = i + 1 < n_act;
-        if (!step()) break;  // P_A(i)
+    int c = 0;
+    int64_t g = 0;
+    bool go = true;
+    for (int it = it0; it < n_items && go; it += it_step, ++c) {
+      const int nh = decode_item(args, it).nh;
+      if (!step()) break;  // the item's list, its Q and (if any) its first key tile
+      const int n = ctl->n_act[c & 1];
+      if (n == 0) {
+        commit(&ctl->q_empty);
+        continue;
+      }
+      for (int h = 0; h < nh; ++h) issue_s(h, static_cast<int>(g & 1));
+      if (n == 1) commit(&ctl->q_empty);  // the item's last S has been issued
+      for (int i = 0; i < n; ++i, ++g) {
+        const int st = static_cast<int>(g & 1);
+        const bool more = i + 1 < n;
+        if (!step()) {  // P_A(i) (and, at i = 0, O_A read by the last epilogue)
+          go = false;
+          break;
+        }
         issue_pv(0, st, i == 0);
         if (!more) commit(&ctl->o_final[0]);
         if (more) {
-          if (!step()) break;  // K / V(i + 1)
+          if (!step()) {  // K / V(i + 1)
+            go = false;
+            break;
+          }
           issue_s(0, st ^ 1);
+          if (nh == 1 && i + 2 == n) commit(&ctl->q_empty);
         }
         if (nh == 2) {
-          if (!step()) break;  // P_B(i)
+          if (!step()) {  // P_B(i)
+            go = false;
+            break;
+          }
           issue_pv(1, st, i == 0);
           if (!more) commit(&ctl->o_final[1]);
         }
         commit(&ctl->kv_empty[st]);
-        if (nh == 2 && more) issue_s(1, st ^ 1);
+        if (nh == 2 && more) {
+          issue_s(1, st ^ 1);
+          if (i + 2 == n) commit(&ctl->q_empty);
+        }
       }
     }
     __syncwarp();
@@ -736,41 +828,88 @@ __global__ void __launch_bounds__(kHThreads, 1)
       bar_sync_n(kHBarW, 64);
       return got;
     };
-    if (n_act > 0 && release(seen(&ctl->q_full, 0u) && seen(&ctl->kv_full[0], 0u))) {
-      for (int i = 0; i < n_act; ++i) {
-        const int st = i & 1;
-        const bool more = i + 1 < n_act;
-        if (!release(seen(&ctl->p_full[0], static_cast<uint32_t>(i) & 1u))) break;
-        if (more &&
-            !release(seen(&ctl->kv_full[st ^ 1], static_cast<uint32_t>((i + 1) >> 1) & 1u)))
+    int c = 0;
+    int64_t g = 0;
+    int tiles[2] = {0, 0}, items[2] = {0, 0};  // per head: P tiles and finished outputs
+    bool go = true;
+    for (int it = it0; it < n_items && go; it += it_step, ++c) {
+      const int nh = decode_item(args, it).nh;
+      const int b = c & 1;
+      bool got = seen(&ctl->list_full[b], static_cast<uint32_t>(c >> 1) & 1u) &&
+                 seen(&ctl->q_full, static_cast<uint32_t>(c) & 1u);
+      const int n = got ? ctl->n_act[b] : 0;
+      if (got && n > 0) got = seen(&ctl->kv_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u);
+      if (!release(got)) break;
+      for (int i = 0; i < n; ++i, ++g) {
+        const bool more = i + 1 < n;
+        // P_h(i); before an item's first P V_h, the last epilogue of head h
+        // has read O_h
+        auto p_ready = [&](int h) {
+          return seen(&ctl->p_full[h], static_cast<uint32_t>(tiles[h]) & 1u) &&
+                 (i > 0 || items[h] == 0 ||
+                  seen(&ctl->o_free[h], static_cast<uint32_t>(items[h] - 1) & 1u));
+        };
+        if (!release(p_ready(0))) {
+          go = false;
           break;
-        if (nh == 2 && !release(seen(&ctl->p_full[1], static_cast<uint32_t>(i) & 1u))) break;
+        }
+        ++tiles[0];
+        if (more && !release(seen(&ctl->kv_full[(g + 1) & 1],
+                                  static_cast<uint32_t>((g + 1) >> 1) & 1u))) {
+          go = false;
+          break;
+        }
+        if (nh == 2) {
+          if (!release(p_ready(1))) {
+            go = false;
+            break;
+          }
+          ++tiles[1];
+        }
       }
+      if (!go) break;
+      if (n > 0) {
+        ++items[0];
+        if (nh == 2) ++items[1];
+      }
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->list_empty[b]));
     }
   } else {
-    // ------------------------------------------------------------ softmax  } else {
     // ------------------------------------------------------------ softmax
     const int h = warp >> 2;          // head of this warpgroup
     const int r = (warp & 3) * 32 + lane;
-    const int row = row0 + r;
-    const bool row_ok = row < S;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_col = tmem + lane_off + static_cast<uint32_t>(h * 128);
     const uint32_t o_col = tmem + lane_off + static_cast<uint32_t>(256 + h * 128);
     const float sl2 = args.scale * kLog2e;
-    float m = -INFINITY, mt = -INFINITY, l = 0.f;
-    if (h < nh) {
-      for (int i = 0; i < n_act; ++i) {
+    bool ok = true;
+    int c = 0, tiles = 0, items = 0;  // this head's P tiles and finished outputs
+    for (int it = it0; it < n_items && ok; it += it_step, ++c) {
+      const HItem w = decode_item(args, it);
+      const AttnHSeg& sg = args.segs[w.si];
+      const int b = c & 1;
+      if (!__all_sync(0xffffffffu, ovb_wait(smem_u32(&ctl->list_full[b]),
+                                            static_cast<uint32_t>(c >> 1) & 1u, abort))) {
+        if (lane == 0) *abort = 1;
+        break;
+      }
+      const int n_act = ctl->n_act[b];
+      const int row = w.row0 + r;
+      const bool row_ok = row < w.S;
+      const bool mine = h < w.nh;
+      float m = -INFINITY, mt = -INFINITY, l = 0.f;
+      for (int i = 0; i < n_act && mine; ++i, ++tiles) {
         // the warp leaves together: its TMEM accesses are warp-collective
-        if (!__all_sync(0xffffffffu, wait(&ctl->s_full[h], static_cast<uint32_t>(i) & 1u))) {
+        if (!__all_sync(0xffffffffu, ovb_wait(smem_u32(&ctl->s_full[h]),
+                                              static_cast<uint32_t>(tiles) & 1u, abort))) {
           ok = false;
-          *abort = 1;
+          if (lane == 0) *abort = 1;
           break;
         }
         tc_fence_after();
-        const int j = ctl->act[i];
+        const int j = ctl->act[b][i];
         const int key0 = j * 128;
-        const int kind = ctl->kind[i];  // warp-uniform
+        const int kind = ctl->kind[b][i];  // warp-uniform
         uint32_t u[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u[c]);
@@ -781,40 +920,45 @@ __global__ void __launch_bounds__(kHThreads, 1)
         // x (masked keys -inf) in place.
         float tmax, mul;
         if (kind == 0) {
-          float mr = -INFINITY;
+          // four independent chains of 3-input maxima (short dependency chains)
+          float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mr = fmaxf(mr, __uint_as_float(u[c][e]));
-          tmax = __fmul_rn(mr, sl2);
+            for (int e = 0; e < 32; e += 2)
+              mr[(e >> 1) & 3] =
+                  max3f(mr[(e >> 1) & 3], __uint_as_float(u[c][e]), __uint_as_float(u[c][e + 1]));
+          tmax = __fmul_rn(max3f(mr[0], mr[1], fmaxf(mr[2], mr[3])), sl2);
           mul = sl2;
         } else {
           uint32_t bw[4];
-          if (args.tile_class && args.tile_class[sg.tile0 + qb * nkt + j] == 1) {
+          if (args.tile_class && args.tile_class[sg.tile0 + w.qb * w.nkt + j] == 1) {
             const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(args.tile_bits) +
-                                   (static_cast<int64_t>(sg.tile0 + qb * nkt + j) * 128 + r));
+                                   (static_cast<int64_t>(sg.tile0 + w.qb * w.nkt + j) * 128 + r));
             bw[0] = b4.x; bw[1] = b4.y; bw[2] = b4.z; bw[3] = b4.w;
           } else {
             bw[0] = bw[1] = bw[2] = bw[3] = 0xffffffffu;
           }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {  // keys past the segment's end
-            const int vc = S - key0 - 32 * c;
+            const int vc = w.S - key0 - 32 * c;
             bw[c] &= vc >= 32 ? 0xffffffffu : (vc <= 0 ? 0u : (1u << vc) - 1u);
           }
           tmax = -INFINITY;
           if (kind == 1) {
+            float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
               for (int e = 0; e < 32; ++e) {
                 const float x = ((bw[c] >> e) & 1u) ? __fmul_rn(__uint_as_float(u[c][e]), sl2)
                                                     : -INFINITY;
-                tmax = fmaxf(tmax, x);
+                mr[e & 3] = fmaxf(mr[e & 3], x);
                 u[c][e] = __float_as_uint(x);
               }
+            tmax = max3f(mr[0], mr[1], fmaxf(mr[2], mr[3]));
           } else {
-            const float* brow = sg.bias + static_cast<int64_t>(row_ok ? row : 0) * S + key0;
+            const float* brow = sg.bias + static_cast<int64_t>(row_ok ? row : 0) * w.S + key0;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -852,32 +996,46 @@ __global__ void __launch_bounds__(kHThreads, 1)
         }
         // Pass 2: P = 2^(x - m), x = u * mul (the raw score times scale log2 e
         // on a plain tile, x itself otherwise), one FFMA and one ex2 each.
+        // Pairs of elements go through the packed f32x2 FFMA and FADD; the row
+        // sum is kept in four partial sums (two f32x2 accumulators).
         const float nm = m == -INFINITY ? 0.f : -m;
-        float sum = 0.f;
+        float sa[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(u[c][2 * e]), mul, nm));
-            const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(u[c][2 * e + 1]), mul, nm));
-            sum = __fadd_rn(sum, __fadd_rn(p0, p1));
+            float x0, x1;
+            fma2(__uint_as_float(u[c][2 * e]), __uint_as_float(u[c][2 * e + 1]), mul, nm, x0, x1);
+            const float p0 = ex2_approx(x0);
+            const float p1 = ex2_approx(x1);
+            add2(sa[e & 1][0], sa[e & 1][1], p0, p1);
             pk[e] = pack2(p0, p1);
           }
           tmem_st16(s_col + static_cast<uint32_t>(c * 16), pk);
         }
+        const float sum = __fadd_rn(__fadd_rn(sa[0][0], sa[0][1]), __fadd_rn(sa[1][0], sa[1][1]));
         l += sum;
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&ctl->p_full[h]));
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl->list_empty[b]));  // done with the list
+      if (!ok || !mine) continue;
       // ---- O / l to the output row
       const bool have_o =
-          __all_sync(0xffffffffu, n_act > 0 && ok && wait(&ctl->o_final[h], 0u));
+          n_act > 0 && __all_sync(0xffffffffu, ovb_wait(smem_u32(&ctl->o_final[h]),
+                                                        static_cast<uint32_t>(items) & 1u, abort));
+      if (n_act > 0 && !have_o) {
+        ok = false;
+        if (lane == 0) *abort = 1;
+        break;
+      }
       if (have_o) tc_fence_after();
       const bool masked = !(mt >= -1e29f * kLog2e);
       const float inv_l = masked || !(l > 0.f) ? 0.f : __frcp_rn(l);
-      float* orow = args.out ? args.out + sg.q_off + static_cast<int64_t>(head0 + h) * 128 +
+      float* orow = args.out ? args.out + sg.q_off + static_cast<int64_t>(w.head0 + h) * 128 +
                                    static_cast<int64_t>(row_ok ? row : 0) * args.q_stride
                              : nullptr;
       // quantised output: the head's 128 values are four whole 32-k blocks of
@@ -900,8 +1058,8 @@ __global__ void __launch_bounds__(kHThreads, 1)
           float vq[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) vq[e] = __fmul_rn(__uint_as_float(o[e]), inv_l);
-          const int64_t blk = static_cast<int64_t>(head0 + h) * 4 + c;
-          const float bs = quant_block32(
+          const int64_t blk = static_cast<int64_t>(w.head0 + h) * 4 + c;
+          const float bs = quant_block32_fast(
               vq, args.q_out + (qrow * args.q_kb * 32 + blk * 32) * es, args.q_mode, &range_bad);
           args.q_asc[qrow * args.q_kb + blk] = bs;
         } else {
@@ -915,6 +1073,11 @@ __global__ void __launch_bounds__(kHThreads, 1)
         }
       }
       if (range_bad) atomicOr(&g_status_att, kErrAttRange);
+      if (have_o) {  // O_h read: the next item's first P V_h may overwrite it
+        tc_fence_before();
+        mbar_arrive(smem_u32(&ctl->o_free[h]));
+        ++items;
+      }
     }
   }
   tc_fence_before();
@@ -976,8 +1139,13 @@ cudaError_t launch_attention_h(const AttnHArgs& args, int ctas, cudaStream_t s) 
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  return launch_plain(attention_h_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kHThreads),
-                      kAttHSmem, s, args);
+  // persistent: at most one CTA per SM (the shared memory allows no more),
+  // each walking the work items it, it + grid, ...
+  AttnHArgs a = args;
+  a.n_items = ctas;
+  const int grid = std::min(ctas, num_sms(dev));
+  return launch_plain(attention_h_kernel, dim3(static_cast<unsigned>(grid)), dim3(kHThreads),
+                      kAttHSmem, s, a);
 }
 
 cudaError_t launch_attn_tiles(const AttnTilesArgs& a, int tiles, uint8_t* cls, uint32_t* bits,

@@ -230,8 +230,9 @@ struct AttnArgs {
   AttnSeg segs[kAttMaxSegs];
 };
 cudaError_t launch_attention(const AttnArgs& args, int total_qblocks, cudaStream_t s);
-// The fp16-operand attention (attention_h_kernel): one CTA per (segment, 128
-// query rows, kv head, pair of query heads), numbered from the segment's cta0.
+// The fp16-operand attention (attention_h_kernel): one work item per
+// (segment, 128 query rows, kv head, pair of query heads), numbered from the
+// segment's cta0.
 struct AttnHSeg {
   const float* bias;  // [rows, rows] additive (no tile table), or null
   int64_t q_off;      // element offset of the segment's first query row (out)
@@ -263,8 +264,10 @@ struct AttnHArgs {
   float* q_asc;
   int q_mode;
   int q_kb;
+  int n_items;        // work items (segment x query block x kv head x head pair)
   AttnHSeg segs[kAttMaxSegs];
 };
+// ctas = work items; the kernel runs persistent CTAs over them.
 cudaError_t launch_attention_h(const AttnHArgs& args, int ctas, cudaStream_t s);
 struct AttnTilesArgs {
   const uint8_t* masks;         // the segments' [rows, rows] u8 masks, concatenated

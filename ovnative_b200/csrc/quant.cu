@@ -408,6 +408,19 @@ constexpr int kRows4Warps = 4;  // warps per block
 
 __device__ __forceinline__ int swz4(int c) { return c ^ ((c >> 3) & 7); }
 
+// 16-byte asynchronous copy global -> shared (through L2 only), and the wait
+// for all of this thread's copies.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ float fmax_nan(float a, float b) {
   float r;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
@@ -431,24 +444,20 @@ __global__ void __launch_bounds__(kRows4Warps * 32) rmsnorm_quantize_rows4_kerne
   for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * kRows4Warps + warp) * kRows4; r0 < rows;
        r0 += step) {
     const int nr = static_cast<int>(imin64(kRows4, rows - r0));
-    // ---- stage the rows (coalesced 16-byte loads, all issued before the stores)
+    // ---- stage the rows: asynchronous 16-byte copies global -> shared
+    // (coalesced, all four rows' in flight at once, no registers)
 #pragma unroll
     for (int g = 0; g < kRows4; ++g) {
       if (g < nr) {
         const float4* xr = reinterpret_cast<const float4*>(x + (r0 + g) * cols);
-        float4 t[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int c = lane + 32 * k;
-          t[k] = c < nch ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int c = lane + 32 * k;
-          if (c < nch) srows[g * rstride + swz4(c)] = t[k];
+          if (c < nch) cp_async16(srows + g * rstride + swz4(c), xr + c);
         }
       }
     }
+    cp_async_wait_all();
     __syncwarp();
     // ---- sum of squares in the reference's order: lane 8g + q, chain q of row g
     const int g = lane >> 3, q = lane & 7;
