@@ -89,6 +89,8 @@ constexpr int kStgStrideF = 36;
 // Per epilogue warp of the fused q|k|v mode: one head's wscale and norm
 // weights, staged for broadcast reads.
 constexpr int kRopeColFloats = 256;
+// ... and two 2 KB buffers of the RoPE table (32 rows x 8 pairs each).
+constexpr int kRopeTabBufBytes = 2048;
 // named barriers (0 is __syncthreads)
 constexpr int kBarStage = 1;                    // + s: converters -> MMA warp
 constexpr int kBarDfree = kBarStage + kStagesF;  // + d: epilogue -> MMA warp
@@ -384,6 +386,22 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   }
 }
 
+// 16-byte asynchronous copy global -> shared (cp.async, L2 only), the group
+// commit, and the wait until at most N of this thread's groups are pending.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_n() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Element e (0 .. 7) of two float4.
 __device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
   const float4 q = v[e >> 2];
@@ -405,12 +423,14 @@ __device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
 // set s (head elements 32s + i with 64 + 32s + i, s = 0, 1), whose 64 fp16
 // outputs are staged in shared memory (32 rows x 128 bytes, 16-byte chunks
 // XOR-swizzled by row: conflict-free both ways) and written as 64-byte row
-// segments, 8 lanes per row.  The row's RoPE table (512 bytes) is loaded
-// sixteen elements at a time, one step ahead.
+// segments, 8 lanes per row.  The rows' RoPE table is staged in shared memory
+// by coalesced asynchronous copies (loads of 16 bytes from 32 different rows
+// per instruction cost the L1 far more than their bytes).
 template <int BN, int kAcc>
 __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_t* tfull,
                                                    volatile int* abort, uint32_t tmem_base,
-                                                   float* stg, float* colv, int quarter, int eh,
+                                                   float* stg, float* colv, uint8_t* tb,
+                                                   int quarter, int eh,
                                                    int dfree_bar, int64_t tiles, int64_t m_tiles,
                                                    int64_t my_tiles, int64_t tile_first,
                                                    int64_t tile_step) {
@@ -447,6 +467,27 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         colv[128 + 32 * j + lane] = nv[j];
       }
     }
+    // The RoPE table of this warp's 32 rows reaches shared memory eight
+    // elements (64 bytes per row) at a time, two steps ahead, by coalesced
+    // asynchronous copies: step k (pairs 8k .. 8k + 7) into buffer k & 1.
+    const int64_t r0 = m0 + quarter * 32;
+    const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
+    const bool use_tab = has && rows > 0 && kind < 2;  // uniform per warp
+    auto tab_copy = [&](int k) {
+      uint8_t* dst = tb + (k & 1) * kRopeTabBufBytes;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int q = lane + 32 * j, row = q >> 2, part = q & 3;
+        const int64_t src_row = r0 + row < M ? r0 + row : M - 1;
+        cp_async16(dst + row * 64 + 16 * (part ^ ((row >> 1) & 3)),
+                   args.rope_tab + src_row * 128 + 16 * k + 4 * part);
+      }
+      cp_async_commit();
+    };
+    if (use_tab) {
+      tab_copy(0);
+      tab_copy(1);
+    }
     __syncwarp();
     const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
     if (!__all_sync(0xffffffffu, got)) {
@@ -454,10 +495,9 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         atomicOr(&g_status_f16, kErrEpilogue);
         *abort = 1;
       }
+      if (use_tab) cp_async_wait_n<0>();  // no copy stays in flight
     } else {
       tc_fence_after();
-      const int64_t r0 = m0 + quarter * 32;
-      const int rows = static_cast<int>(M - r0 < 32 ? M - r0 : 32);
       if (has && rows > 0) {  // uniform per warp
         const uint32_t dcol =
             tmem_base + lane_off + static_cast<uint32_t>(d * BN + 128 * eh);
@@ -465,15 +505,6 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         bool bad = false;  // an fp16 output of this row overflowed (or is NaN)
         const float4* ws4 = reinterpret_cast<const float4*>(colv);
         const float4* nw4 = reinterpret_cast<const float4*>(colv + 128);
-        // This row's (cos, sin) pairs: 64 per row, 128 floats; set s uses
-        // float4s 16s .. 16s + 15.
-        const float4* tab_row = reinterpret_cast<const float4*>(
-            args.rope_tab + (row_ok ? r0 + lane : 0) * 128);
-        // the table of pass 2's first sixteen elements, early
-        float4 cs[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          cs[u] = (kind < 2 && row_ok) ? __ldg(tab_row + u) : make_float4(0.f, 0.f, 0.f, 0.f);
         float scale = 0.f;
         if (kind < 2) {
           // pass 1: s01 = x0^2 + x1^2 (chunks 0 and 1), then + (x2^2 + x3^2)
@@ -534,14 +565,7 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             // set s, elements 16 hf .. 16 hf + 15: lo columns 32s + 16hf ..,
-            // hi columns 64 + 32s + 16hf ..; cs holds their table, the next
-            // step's is loaded now
-            float4 cn[8];
-            const int nxt = 2 * s + hf + 1;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              cn[u] = (nxt < 4 && kind < 2 && row_ok) ? __ldg(tab_row + 8 * nxt + u)
-                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            // hi columns 64 + 32s + 16hf ..
             uint32_t va[16], vb[16];
             tmem_ld16(dcol + static_cast<uint32_t>(32 * s + 16 * hf), va);
             tmem_ld16(dcol + static_cast<uint32_t>(64 + 32 * s + 16 * hf), vb);
@@ -550,6 +574,18 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
 #pragma unroll
             for (int gg = 0; gg < 2; ++gg) {
               const int g = 2 * hf + gg;  // 16-byte chunk g (lo) and 4 + g (hi)
+              const int k = 4 * s + g;    // table step: pairs 8k .. 8k + 7
+              float4 cs[4];               // this row's pairs 8k + 2p, 8k + 2p + 1
+              if (use_tab) {
+                if (k + 1 < 8) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
+                __syncwarp();
+                const uint8_t* src = tb + (k & 1) * kRopeTabBufBytes + lane * 64;
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+                  cs[p] = *reinterpret_cast<const float4*>(src + 16 * (p ^ ((lane >> 1) & 3)));
+                __syncwarp();
+                if (k + 2 < 8) tab_copy(k + 2);
+              }
               // the eight elements' wscale and norm weights (broadcast reads)
               float4 wa[2], wb[2], na[2], nb[2];
 #pragma unroll
@@ -571,7 +607,7 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                   const float x = __fmul_rn(__uint_as_float(va[iv]), f4_at2(wa, iw));
                   const float y = __fmul_rn(__uint_as_float(vb[iv]), f4_at2(wb, iw));
                   if (kind < 2) {
-                    const float4 c2 = cs[4 * gg + ((e + h) >> 1)];
+                    const float4 c2 = cs[(e + h) >> 1];
                     const float cs_ = ((e + h) & 1) ? c2.z : c2.x;
                     const float sn = ((e + h) & 1) ? c2.w : c2.y;
                     const float a = __fmul_rn(__fmul_rn(x, scale), f4_at2(na, iw));
@@ -596,8 +632,6 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
               *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * ((4 + g) ^ (lane & 7))) =
                   make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
             }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) cs[u] = cn[u];
           }
           __syncwarp();
           // chunk k of row r: columns 32s + 8k (k < 4) or 64 + 32s + 8(k - 4)
@@ -1063,7 +1097,9 @@ struct TileH {
   // epilogue staging: 32 x 32 fp32 chunks, or 32 rows x 64 bytes of the
   // fused SiLU*up epilogue's quantised output
   static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4) +
-                                    (kRope ? static_cast<size_t>(kEpiW) * kRopeColFloats * 4 : 0);
+                                    (kRope ? static_cast<size_t>(kEpiW) *
+                                                 (kRopeColFloats * 4 + 2 * kRopeTabBufBytes)
+                                           : 0);
   static constexpr int kOwn = BN / kSplit;  // columns owned per rank
   static constexpr size_t kPartialFloats = static_cast<size_t>(kBlockM) * kOwn;  // per sender
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
@@ -1402,6 +1438,9 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
                                       stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF),
                                       stg_all + T::kEpiW * (32 * kStgStrideF) +
                                           (warp - kFirstEpiH) * kRopeColFloats,
+                                      reinterpret_cast<uint8_t*>(stg_all + T::kEpiW * (32 * kStgStrideF +
+                                                                                   kRopeColFloats)) +
+                                          (warp - kFirstEpiH) * (2 * kRopeTabBufBytes),
                                       warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
                                       m_tiles, my_tiles, blockIdx.x, gridDim.x);
     } else if constexpr (kSilu) {
