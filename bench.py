@@ -985,7 +985,8 @@ def config_utt(world: int, lengths: dict) -> dict:
                     "172-204) + guided sampler (guidance 2.0, layer_penalty 5.0)",
         "layers": LM_LAYERS, "vocab": LM_VOCAB, "audio_heads": "int8",
         "batching": f"each GPU packs its CFG pairs into forwards of <= {MAX_ROWS} rows "
-                    "(attention segments stay per pair)",
+                    "(attention segments stay per pair); with two or more batches, two LM "
+                    "instances run alternate batches on two streams",
         "parallelism": f"dp{world}: utterance-parallel, LPT shards of whole CFG pairs, no "
                        "collective on the data path",
         "l2": "inputs larger than L2: every forward streams 449 MB of int8 weights (plus their "
@@ -1145,7 +1146,12 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     lengths = utterance_lengths()
     plan = shard.lpt_assign([lengths[i] for i in range(len(lengths))], world)
     m = LM.LM(path, f16=f16)
-    sp = TB.Stepper(m, lengths, plan[rank], dev, stream, max_rows=MAX_ROWS, seed=rank)
+    # with two or more batches, a second LM instance (its own forward buffers)
+    # lets two batches' forwards run on two streams at once
+    n_batches = len(TB.pack_batches(lengths, plan[rank], MAX_ROWS)) if plan[rank] else 0
+    extra = [LM.LM(path, f16=f16)] if n_batches >= 2 else []
+    sp = TB.Stepper(m, lengths, plan[rank], dev, stream, max_rows=MAX_ROWS, seed=rank,
+                    extra_lms=extra)
     sp.warm_and_capture()
     for _ in range(args.warmup):
         sp.step()
@@ -1196,6 +1202,8 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     batches = [{"rows": b.rows, "pairs": len(b.pairs)} for b in sp.batches]
     sp.release()
     m.close()
+    for e in extra:
+        e.close()
     if status != 0:
         raise RuntimeError(f"bounded device wait timed out (status {status})")
     roofline = None

@@ -175,42 +175,70 @@ class Stepper:
     on the device (graph replays); `step_e2e()` is the same step as a serving
     loop drives it: every batch's ids copied in from pinned host memory, the
     graph, and the predictions and scores copied back, then a host
-    synchronisation (the next step's ids depend on them, tts.cpp:329-359)."""
+    synchronisation (the next step's ids depend on them, tts.cpp:329-359).
+
+    With `extra_lms` (further LM instances on the same checkpoint, each with
+    its own forward buffers) the batches are dealt round-robin to lanes, one
+    per LM, and each lane replays its graphs on a stream of its own: two
+    independent forwards then share the GPU, so that one's kernels fill the
+    SMs another's leave idle (the last tiles of a persistent GEMM, a kernel's
+    launch and ramp).  `stream` orders the step: the lanes start after the
+    work already queued on it, and it waits for all lanes at the end."""
 
     def __init__(self, lm: LM, lengths: dict, uids: list, dev: torch.device,
-                 stream: torch.cuda.Stream, max_rows: int = 16384, seed: int = 0):
+                 stream: torch.cuda.Stream, max_rows: int = 16384, seed: int = 0,
+                 extra_lms=()):
         rng = np.random.default_rng(seed)
         self.lm, self.stream = lm, stream
+        self.lms = [lm, *extra_lms]
+        self.streams = [stream] + [torch.cuda.Stream(device=dev) for _ in extra_lms]
         self.groups = pack_batches(lengths, uids, max_rows) if uids else []
-        self.batches = [Batch(lm, lengths, g, rng, dev) for g in self.groups]
-        if self.batches:
-            lm.reserve(max(b.rows for b in self.batches),
-                       max(b.mask_elems for b in self.batches))
+        self.lane = [i % len(self.lms) for i in range(len(self.groups))]
+        self.batches = [Batch(self.lms[k], lengths, g, rng, dev)
+                        for k, g in zip(self.lane, self.groups)]
+        for k, m in enumerate(self.lms):
+            mine = [b for b, lk in zip(self.batches, self.lane) if lk == k]
+            if mine:
+                m.reserve(max(b.rows for b in mine), max(b.mask_elems for b in mine))
         self.rows_per_step = sum(b.rows for b in self.batches)
         self.samplers = sum(len(b.pairs) for b in self.batches)
 
+    def _lanes(self):
+        return [(self.streams[k], b) for k, b in zip(self.lane, self.batches)]
+
     def warm_and_capture(self):
-        with torch.cuda.stream(self.stream):
-            for b in self.batches:  # eager first: kernel attributes are set outside capture
+        for s, b in self._lanes():  # eager first: kernel attributes are set outside capture
+            with torch.cuda.stream(s):
                 b.run()
         torch.cuda.synchronize()
-        for b in self.batches:
-            b.capture(self.stream)
+        for s, b in self._lanes():
+            b.capture(s)
+
+    def _fork(self):
+        for s in self.streams[1:]:
+            s.wait_stream(self.stream)
+
+    def _join(self):
+        for s in self.streams[1:]:
+            self.stream.wait_stream(s)
 
     def step(self):
-        with torch.cuda.stream(self.stream):
-            for b in self.batches:
+        self._fork()
+        for s, b in self._lanes():
+            with torch.cuda.stream(s):
                 b.graph.replay()
+        self._join()
 
     def step_e2e(self):
-        s = self.stream
-        with torch.cuda.stream(s):
-            for b in self.batches:
+        self._fork()
+        for s, b in self._lanes():
+            with torch.cuda.stream(s):
                 b.ids.copy_(b.h_ids, non_blocking=True)
                 b.graph.replay()
                 b.h_pred.copy_(b.pred, non_blocking=True)
                 b.h_scores.copy_(b.scores, non_blocking=True)
-        s.synchronize()
+        self._join()
+        self.stream.synchronize()
 
     def h2d_bytes_per_step(self) -> int:
         return sum(b.h2d_bytes() for b in self.batches)
