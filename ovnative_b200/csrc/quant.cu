@@ -427,6 +427,22 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return r;
 }
 
+// max(m, |a|, |b|) in one instruction, NaN if any input is NaN.
+__device__ __forceinline__ float fmax3_nan_abs(float m, float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return r;
+}
+
+// Packed f32x2 multiply (each lane an IEEE round-to-nearest product):
+// (r0, r1) = (a0 * b0, a1 * b1).
+__device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kRows4Warps * 32) rmsnorm_quantize_rows4_kernel(
     int64_t rows, int cols, const float* x, const float* w, float eps, uint8_t* aq, float* asc) {
@@ -490,10 +506,12 @@ __global__ void __launch_bounds__(kRows4Warps * 32) rmsnorm_quantize_rows4_kerne
           const float4 a = srows[gg * rstride + swz4(c)];
           const float4 b = sw[swz4(c)];
           const int o = j * 4;
-          v[o] = __fmul_rn(__fmul_rn(a.x, s), b.x);
-          v[o + 1] = __fmul_rn(__fmul_rn(a.y, s), b.y);
-          v[o + 2] = __fmul_rn(__fmul_rn(a.z, s), b.z);
-          v[o + 3] = __fmul_rn(__fmul_rn(a.w, s), b.w);
+          // (x * s) * w, two elements per packed multiply
+          float t0, t1, t2, t3;
+          mul2(a.x, a.y, s, s, t0, t1);
+          mul2(a.z, a.w, s, s, t2, t3);
+          mul2(t0, t1, b.x, b.y, v[o], v[o + 1]);
+          mul2(t2, t3, b.z, b.w, v[o + 2], v[o + 3]);
         }
         uint8_t* out = aq + (row * Kb + lane) * 32 * (kMode >= kModeF16 ? 2 : 1);
         if constexpr (kMode == kModeF16Raw) {
@@ -511,31 +529,41 @@ __global__ void __launch_bounds__(kRows4Warps * 32) rmsnorm_quantize_rows4_kerne
             reinterpret_cast<uint4*>(out)[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2],
                                                           hw[4 * i + 3]);
         } else {
-          float amax = 0.f, anan = 0.f;
+          // the block maximum, NaN if the block holds one (two chains of
+          // 3-input maxima); for a finite block it is the reference's amax
+          float an0 = 0.f, an1 = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            amax = fmaxf(amax, fabsf(v[i]));
-            anan = fmax_nan(anan, fabsf(v[i]));
+          for (int i = 0; i < 32; i += 4) {
+            an0 = fmax3_nan_abs(an0, v[i], v[i + 1]);
+            an1 = fmax3_nan_abs(an1, v[i + 2], v[i + 3]);
           }
+          const float anan = fmax_nan(an0, an1);
+          if (!(anan <= 3.402823466e38f)) {  // a NaN or an infinity: the x86 conversion path
+            bool bad = false;
+            asc[row * Kb + lane] = quant_block32(v, out, kMode, &bad);
+            if (bad) atomicOr(&g_status_q, kErrF16Range);
+            continue;
+          }
+          const float amax = anan;
           float bs, inv;
           block_scales(amax, &bs, &inv);
           asc[row * Kb + lane] = bs;
-          if (!(anan <= 3.402823466e38f)) {  // a NaN or an infinity: the x86 conversion path
-            bool bad = false;
-            quant_block32(v, out, kMode, &bad);
-            if (bad) atomicOr(&g_status_q, kErrF16Range);
-          } else if constexpr (kMode == kModeF16) {
+          if constexpr (kMode == kModeF16) {
             constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
             uint32_t hw[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              float d[2];
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const float zf = __fsub_rn(__fadd_rn(__fmul_rn(v[2 * i + e], inv), kMagic), kMagic);
-                d[e] = __fmul_rn(zf, bs);
-              }
-              const __half2 h = __floats2half2_rn(d[0], d[1]);
+              // rne(v * inv) * bs; the rounding steps stay scalar (a packed
+              // multiply followed by a packed add can be contracted into one
+              // fused multiply-add, which changes the rounding), the final
+              // products are packed
+              const float z0 =
+                  __fsub_rn(__fadd_rn(__fmul_rn(v[2 * i], inv), kMagic), kMagic);
+              const float z1 =
+                  __fsub_rn(__fadd_rn(__fmul_rn(v[2 * i + 1], inv), kMagic), kMagic);
+              float d0, d1;
+              mul2(z0, z1, bs, bs, d0, d1);
+              const __half2 h = __floats2half2_rn(d0, d1);
               hw[i] = *reinterpret_cast<const uint32_t*>(&h);
             }
             // the largest |q * asc| is 127 * asc (the block's maximum maps to 127)

@@ -139,3 +139,30 @@ def test_packed_step_equals_one_utterance_at_a_time(cuda, model_path):
         np.testing.assert_array_equal(b_s, a[u][1])
     assert ovb.device_status() == 0
     m.close()
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_two_lanes_equal_one(cuda, model_path, f16):
+    """Batches dealt to two LM instances on two streams give the same
+    predictions and scores as one lane, bit for bit (the forwards are
+    independent; only their timing overlaps)."""
+    st = torch.cuda.Stream()
+    out = []
+    for lanes in (1, 2):
+        ms = [LM.LM(model_path, f16=f16) for _ in range(lanes)]
+        sp = TB.Stepper(ms[0], LENGTHS, list(LENGTHS), cuda, st, max_rows=256, seed=7,
+                        extra_lms=ms[1:])
+        assert len(sp.batches) >= 3
+        sp.warm_and_capture()
+        for _ in range(2):
+            sp.step()
+        sp.step_e2e()
+        torch.cuda.synchronize()
+        out.append(sp.results())
+        sp.release()
+        for m in ms:
+            m.close()
+    for u in LENGTHS:
+        np.testing.assert_array_equal(out[0][u][0], out[1][u][0])
+        np.testing.assert_array_equal(out[0][u][1], out[1][u][1])
+    assert ovb.device_status() == 0
