@@ -338,11 +338,11 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
   args.split_ws = ovb::split_workspace(w->device);
   // split-K configurations need the workspace; the fused SiLU*up epilogue
   // takes BN >= 64 without split-K; the fused q/k norm + RoPE epilogue
-  // single-CTA 256-column tiles (configuration 0: two whole heads per tile)
-  const int config =
-      rope ? 0
-           : ovb::pick_tile_h(M, w->N, w->Kb, w->device,
-                              silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit));
+  // 256-column tiles per CTA (two whole heads): configurations 0 and 7
+  const int config = ovb::pick_tile_h(
+      M, w->N, w->Kb, w->device,
+      rope ? ovb::kHRope
+           : (silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit)));
   const int width = ovb::kHConfigs[config].width;
   if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;

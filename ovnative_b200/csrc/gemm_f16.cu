@@ -1073,6 +1073,7 @@ struct CtlH {
   uint64_t full[kMaxStagesH];
   uint64_t empty[kMaxStagesH];
   uint64_t tfull[2];
+  uint64_t pfree[2];  // CTA pair: the peer's epilogue released accumulator d
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -1516,47 +1517,65 @@ cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
 }
 
 // ---------------------------------------------------------------------------
-// CTA-pair fp16 mainloop (tcgen05 cta_group::2).  Two CTAs of a 2-CTA
-// cluster compute one 256 x BN output tile: rank r TMA-loads its 128 rows of
-// A' and rows [r * BN/2, (r + 1) * BN/2) of the W tile into its own shared
-// memory; the leader (rank 0) issues tcgen05.mma.cta_group::2 with M = 256,
-// which reads both CTAs' operands (each W half once, shared by both SMs'
-// tensor cores), and each CTA's TMEM receives its 128 rows x BN columns.
-// This halves the W bytes each SM loads per tile, the mainloop's bound at
-// M = 400 (L2-to-SM traffic).
-//   - Both CTAs' loads complete on the leader's `full[s]` barrier, which the
-//     leader alone arms with both CTAs' bytes (its producer); the peer's
-//     producer waits only on its own `empty[s]`.
-//   - The leader's commits arrive on `empty[s]` and `tfull` of both CTAs
-//     (multicast to cluster ranks 0 and 1).
+// CTA-pair fp16 mainloop (tcgen05 cta_group::2), persistent.  The two CTAs
+// of a 2-CTA cluster compute 256 x BN output tiles: rank r TMA-loads its 128
+// rows of A' and rows [r * BN/2, (r + 1) * BN/2) of the W tile into its own
+// shared memory; the leader (rank 0) issues tcgen05.mma.cta_group::2 with
+// M = 256, which reads both CTAs' operands, and each CTA's TMEM receives its
+// 128 rows x BN columns.  Each SM loads half of the W tile, so a stage
+// moves 32 KB into an SM's shared memory for 128 x 256 outputs instead of
+// 48 KB: the single-CTA mainloop's bound (shared-memory and L2-to-SM
+// traffic) drops by a third.
+//   - Cluster c takes the tile pairs c, c + clusters, ... (pair p covers
+//     rows [256 * (p % m_pairs), + 256) and columns [BN * (p / m_pairs),
+//     + BN)).  Seen from one CTA these are the 128-row tiles
+//     blockIdx.x + t * gridDim.x of a virtual tiling with 2 * m_pairs row
+//     tiles, which the single-CTA epilogues run on unchanged.
+//   - Both CTAs' loads complete on the leader's `full[s]` barrier, which
+//     the leader alone arms with both CTAs' bytes; each producer waits on
+//     its own `empty[s]`, which the leader's commits reach in both CTAs
+//     (multicast to cluster ranks 0 and 1), as they reach `tfull[d]`.
+//   - Two accumulators per CTA (2 x BN TMEM columns), so a tile's epilogue
+//     overlaps the next tile's mainloop.  Before the MMA warp reuses
+//     accumulator d it bar.syncs with its own CTA's epilogue (kBarDfreeH + d)
+//     and with the stage watcher (kBarPeerH), which has waited for the
+//     peer's release: the peer's warp 1 bar.syncs with the peer's epilogue
+//     and arrives on the leader's `pfree[d]` (release / acquire at cluster
+//     scope).  The MMA thread itself never waits on an mbarrier.
 //   - TMEM is allocated and freed collectively by warp 1 of both CTAs.
-// One tile per cluster; the epilogues are the single-CTA ones on the CTA's
-// 128-row tile (a virtual 128-row tiling of 2 * m_pairs row tiles).
-template <int BN, bool kSilu>
+// No load uses cluster multicast.
+constexpr int kBarPeerH = 4;
+
+template <int BN, bool kSilu, bool kRope = false>
 struct TileH2 {
   static_assert(BN == 256 || BN == 128, "pair tile widths");
+  static_assert(!kRope || (BN == 256 && !kSilu), "the norm + RoPE epilogue takes two heads");
   static constexpr uint32_t kWBytes = (BN / 2) * 128;  // this CTA's half of the W rows
   static constexpr uint32_t kStageBytes = kABytesH + kWBytes;
+  static constexpr int kAcc = 2;
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
-  static constexpr size_t kStgAll =
-      static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4);
+  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4) +
+                                    (kRope ? static_cast<size_t>(kEpiW) *
+                                                 (kRopeColFloats * 4 + 2 * kRopeTabBufBytes)
+                                           : 0);
   static constexpr int kStagesFit =
       static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
   static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
   static constexpr size_t kSmemBytes =
       1024 + static_cast<size_t>(kStages) * kStageBytes + kStgAll + sizeof(CtlH);
   static_assert(kStages >= 3, "too few pipeline stages");
+  static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(kStageBytes % 1024 == 0, "stage bases stay 1 KB aligned");
 };
 
-template <int BN, bool kSilu>
-__global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
+template <int BN, bool kSilu, bool kRope>
+__global__ void __launch_bounds__(TileH2<BN, kSilu, kRope>::kThreads, 1)
     gemm_h2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ GemmArgs args) {
-  using T = TileH2<BN, kSilu>;
+  using T = TileH2<BN, kSilu, kRope>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1570,13 +1589,10 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
   const int Kb = static_cast<int>(args.Kb);
   const int rank = static_cast<int>(cluster_ctarank());  // 0: leader, 1: peer
   const int64_t m_pairs = (M + 2 * kBlockM - 1) / (2 * kBlockM);
-  const uint32_t pair = blockIdx.x >> 1;
-  const uint32_t pm = pair % static_cast<uint32_t>(m_pairs);
-  const uint32_t pn = pair / static_cast<uint32_t>(m_pairs);
-  const int32_t a_row = static_cast<int32_t>((2 * pm + rank) * kBlockM);
-  const int32_t w_row = static_cast<int32_t>(pn * BN + rank * (BN / 2));
+  const int64_t pairs = m_pairs * ((N + BN - 1) / BN);
+  const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  const int64_t my_tiles = pairs > cluster ? (pairs - cluster + clusters - 1) / clusters : 0;
   const int64_t m_tiles_v = 2 * m_pairs;  // the epilogue's 128-row tiling
-  const int64_t vtile = static_cast<int64_t>(pn) * m_tiles_v + 2 * pm + rank;
   const int ksteps = (Kb + 1) / 2;
 
   if (threadIdx.x == 0) {
@@ -1584,7 +1600,10 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
       mbar_init(smem_u32(&ctl->full[s]), 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
     }
-    for (int d = 0; d < 2; ++d) mbar_init(smem_u32(&ctl->tfull[d]), 1);
+    for (int d = 0; d < 2; ++d) {
+      mbar_init(smem_u32(&ctl->tfull[d]), 1);
+      mbar_init(smem_u32(&ctl->pfree[d]), 1);
+    }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -1607,26 +1626,31 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
     // --------------------------------------------------- producer (both CTAs)
     if (lane == 0) {
       bool ok = true;
-      int st = 0;
-      for (; st < ksteps; ++st) {
-        const int s = st % T::kStages;
-        const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
-        // The ring's first pass needs no wait: those stages were never used.
-        if (st >= T::kStages && !ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
-          atomicOr(&g_status_f16, kErrProducer);
-          *abort = 1;
-          ok = false;
-          break;
+      int64_t st = 0;
+      for (int64_t p = cluster; p < pairs && ok; p += clusters) {
+        const int64_t pm = p % m_pairs, pn = p / m_pairs;
+        const int32_t a_row = static_cast<int32_t>((2 * pm + rank) * kBlockM);
+        const int32_t w_row = static_cast<int32_t>(pn * BN + rank * (BN / 2));
+        for (int j = 0; j < ksteps; ++j, ++st) {
+          const int s = static_cast<int>(st % T::kStages);
+          const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
+          // The ring's first pass needs no wait: those stages were never used.
+          if (st >= T::kStages && !ovb_wait(smem_u32(&ctl->empty[s]), ph ^ 1u, abort)) {
+            atomicOr(&g_status_f16, kErrProducer);
+            *abort = 1;
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&ctl->full[s]), 2 * T::kStageBytes);
+          const uint32_t bar = mapa_shared(smem_u32(&ctl->full[s]), 0u);  // the leader's
+          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, j * kStageKF, a_row, bar);
+          tma_load_2d_pair(sa + kABytesH, &tmap_w, j * kStageKF, w_row, bar);
         }
-        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&ctl->full[s]), 2 * T::kStageBytes);
-        const uint32_t bar = mapa_shared(smem_u32(&ctl->full[s]), 0u);  // the leader's
-        const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
-        tma_load_2d_pair(sa, &tmap_a, st * kStageKF, a_row, bar);
-        tma_load_2d_pair(sa + kABytesH, &tmap_w, st * kStageKF, w_row, bar);
       }
       if (!ok && rank == 0) {  // let the loads in flight land before the CTA can exit
-        const int first = st > T::kStages ? st - T::kStages : 0;
-        for (int j = first; j < st; ++j) {
+        const int64_t first = st > T::kStages ? st - T::kStages : 0;
+        for (int64_t j = first; j < st; ++j) {
           volatile int never = 0;
           ovb_wait(smem_u32(&ctl->full[j % T::kStages]),
                    static_cast<uint32_t>((j / T::kStages) & 1), &never);
@@ -1634,52 +1658,105 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // -------------------------------------------------------- MMA (leader)
     if (rank == 0) {
+      // ------------------------------------------------------ MMA (leader)
       const uint32_t idesc = idesc_f16(2 * kBlockM, BN);
-      for (int st = 0; st < ksteps; ++st) {
-        const int s = st % T::kStages;
-        named_sync(kBarFullH, 64);  // stage s of both CTAs has landed
-        if (lane == 0) {
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < kStageKF / 16; ++kk)
-            mma_f16_ss_pair(tmem_base, sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
-                            sw128_kmajor_desc(sa + kABytesH, static_cast<uint32_t>(kk * 32)),
-                            idesc, (st > 0 || kk > 0) ? 1u : 0u);
-          tc_commit_pair(smem_u32(&ctl->empty[s]), 0x3);
-          if (st == ksteps - 1) tc_commit_pair(smem_u32(&ctl->tfull[0]), 0x3);
+      int64_t st = 0;
+      for (int64_t t = 0; t < my_tiles; ++t) {
+        const int d = static_cast<int>(t % T::kAcc);
+        if (t >= T::kAcc) {
+          named_sync(kBarDfreeH + d, 32 * (T::kEpiW + 1));  // this CTA's epilogue read d
+          named_sync(kBarPeerH, 64);                        // and the peer's (watcher)
         }
+        const uint32_t dcol = tmem_base + static_cast<uint32_t>(d * BN);
+        for (int j = 0; j < ksteps; ++j, ++st) {
+          const int s = static_cast<int>(st % T::kStages);
+          named_sync(kBarFullH, 64);  // stage s of both CTAs has landed
+          if (lane == 0) {
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * T::kStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < kStageKF / 16; ++kk)
+              mma_f16_ss_pair(dcol, sw128_kmajor_desc(sa, static_cast<uint32_t>(kk * 32)),
+                              sw128_kmajor_desc(sa + kABytesH, static_cast<uint32_t>(kk * 32)),
+                              idesc, (j > 0 || kk > 0) ? 1u : 0u);
+            tc_commit_pair(smem_u32(&ctl->empty[s]), 0x3);
+            if (j == ksteps - 1) tc_commit_pair(smem_u32(&ctl->tfull[d]), 0x3);
+          }
+          __syncwarp();
+        }
+      }
+      if (lane == 0) {
+        tc_commit_pair(smem_u32(&ctl->drain), 0x1);
+        volatile int never = 0;
+        if (!ovb_wait(smem_u32(&ctl->drain), 0u, &never)) atomicOr(&g_status_f16, kErrDrain);
+      }
+      __syncwarp();
+    } else {
+      // ------------------------------------------- peer: accumulator release
+      // One bar.sync per tile with this CTA's epilogue, as the MMA warp does
+      // in the leader, then an arrive on the leader's pfree[d].
+      for (int64_t t = 0; t + T::kAcc < my_tiles; ++t) {
+        const int d = static_cast<int>(t % T::kAcc);
+        named_sync(kBarDfreeH + d, 32 * (T::kEpiW + 1));
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->pfree[d]), 0u));
         __syncwarp();
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------- stage watcher (leader)
+    // In lockstep with the MMA warp: per tile (from the third on) one
+    // bar.sync after the peer released the accumulator, per stage one after
+    // the stage landed -- also after a failed wait (the status word reports
+    // it).
     if (rank == 0) {
-      for (int st = 0; st < ksteps; ++st) {
-        const int s = st % T::kStages;
-        const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
-        const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
-        if (!__all_sync(0xffffffffu, got) && lane == 0) {
-          atomicOr(&g_status_f16, kErrConvert);
-          *abort = 1;
+      int64_t st = 0;
+      for (int64_t t = 0; t < my_tiles; ++t) {
+        if (t >= T::kAcc) {
+          const int d = static_cast<int>(t % T::kAcc);
+          const uint32_t ph = static_cast<uint32_t>(((t - T::kAcc) / T::kAcc) & 1);
+          const bool got = ovb_wait_cluster(smem_u32(&ctl->pfree[d]), ph, abort);
+          if (!__all_sync(0xffffffffu, got) && lane == 0) {
+            atomicOr(&g_status_f16, kErrEpilogue);
+            *abort = 1;
+          }
+          named_sync(kBarPeerH, 64);
         }
-        named_sync(kBarFullH, 64);
+        for (int j = 0; j < ksteps; ++j, ++st) {
+          const int s = static_cast<int>(st % T::kStages);
+          const uint32_t ph = static_cast<uint32_t>((st / T::kStages) & 1);
+          const bool got = ovb_wait(smem_u32(&ctl->full[s]), ph, abort);
+          if (!__all_sync(0xffffffffu, got) && lane == 0) {
+            atomicOr(&g_status_f16, kErrConvert);
+            *abort = 1;
+          }
+          named_sync(kBarFullH, 64);
+        }
       }
     }
   } else {
     // ------------------------------------------------- epilogue (both CTAs)
-    if constexpr (kSilu) {
+    const int64_t vtiles = 2 * pairs;
+    if constexpr (kRope) {
+      epilogue_rope_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                                      stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF),
+                                      stg_all + T::kEpiW * (32 * kStgStrideF) +
+                                          (warp - kFirstEpiH) * kRopeColFloats,
+                                      reinterpret_cast<uint8_t*>(stg_all + T::kEpiW * (32 * kStgStrideF +
+                                                                                   kRopeColFloats)) +
+                                          (warp - kFirstEpiH) * (2 * kRopeTabBufBytes),
+                                      warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles,
+                                      m_tiles_v, my_tiles, blockIdx.x, gridDim.x);
+    } else if constexpr (kSilu) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
-      silu_epilogue<BN, 1, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
-                                     (warp - kFirstEpiH) >> 2, kBarDfreeH, vtile + 1, m_tiles_v,
-                                     1, vtile, 1);
+      silu_epilogue<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
+                                           (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles,
+                                           m_tiles_v, my_tiles, blockIdx.x, gridDim.x);
     } else {
-      epilogue_loop<BN, 1>(args, ctl->tfull, abort, tmem_base,
-                           stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                           (warp - kFirstEpiH) >> 2, kBarDfreeH, vtile + 1, m_tiles_v, 1, vtile,
-                           1);
+      epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
+                                 stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
+                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles, m_tiles_v,
+                                 my_tiles, blockIdx.x, gridDim.x);
     }
   }
 
@@ -1694,24 +1771,16 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu>::kThreads, 1)
   }
 }
 
-template <int BN, bool kSilu>
+template <int BN, bool kSilu, bool kRope = false>
 cudaError_t launch_h2_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                            const GemmArgs& args, cudaStream_t s) {
-  using T = TileH2<BN, kSilu>;
-  auto* kernel = gemm_h2_kernel<BN, kSilu>;
+  using T = TileH2<BN, kSilu, kRope>;
+  auto* kernel = gemm_h2_kernel<BN, kSilu, kRope>;
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
-  if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(T::kSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured_dev = dev;
-  }
-  const int64_t pairs = ((args.M + 2 * kBlockM - 1) / (2 * kBlockM)) * ((args.N + BN - 1) / BN);
-  if (pairs * 8 > INT32_MAX) return cudaErrorInvalidValue;  // 32-bit tile arithmetic
+  static thread_local int max_clusters = 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   cfg.blockDim = dim3(T::kThreads);
   cfg.dynamicSmemBytes = T::kSmemBytes;
   cfg.stream = s;
@@ -1723,6 +1792,24 @@ cudaError_t launch_h2_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(T::kSmemBytes));
+    if (e != cudaSuccess) return e;
+    // The persistent grid holds as many pairs as can be resident at once
+    // (the GPCs' SM counts decide how many 2-CTA clusters fit).
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(num_sms(dev)));
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n < 1) return cudaErrorInvalidConfiguration;
+    max_clusters = n;
+    configured_dev = dev;
+  }
+  const int64_t pairs = ((args.M + 2 * kBlockM - 1) / (2 * kBlockM)) * ((args.N + BN - 1) / BN);
+  if (pairs * 8 > INT32_MAX) return cudaErrorInvalidValue;  // 32-bit tile arithmetic
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(pairs, max_clusters)));
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, tmap_a, tmap_w, args);
 }
@@ -1802,8 +1889,11 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) 
   // 64-k stage the slower of the tensor pipe (four K = 16 MMAs) and shared
   // memory at ~128 B per clock, which carries the stage twice (TMA write, MMA
   // read; a pair CTA writes half of W but serves it to both tensor cores),
-  // plus the split-K exchange; whole waves of CTAs.  CTA pairs run one tile
-  // per cluster (no epilogue overlap), so they are only used in one wave.
+  // plus the split-K exchange; whole waves of CTAs.  A CTA pair pays a
+  // one-off ~3 us more (cluster launch, paired TMEM allocation, the peer's
+  // handshakes), so it wins only with many 64-k stages per SM: measured at
+  // 15,408 rows it is 3-17 % faster than the single-CTA 128 x 256 tiles, at
+  // 400 and 1400 rows 1-2 us slower.
   const int64_t sms = num_sms(device);
   const bool silu = allowed == kHSilu;
   const int64_t m_tiles = (M + kBlockM - 1) / kBlockM;
@@ -1818,15 +1908,15 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) 
     const int64_t ctas =
         c.pair ? 2 * ((m_tiles + 1) / 2) * n_tiles : m_tiles * n_tiles * c.split;
     const int64_t waves = (ctas + sms - 1) / sms;
-    if (c.pair && waves > 1) continue;
     const int64_t box = kTileNF[c.width];  // W rows this CTA loads per stage
     const int64_t smem = c.pair ? (16384 + box * 128) + (16384 + bn * 128)
                                 : 2 * (16384 + box * 128);
     const int64_t mma = 4 * (bn <= 128 ? 64 : 128);
     const int64_t per_stage = (mma > smem / 128 ? mma : smem / 128) + (c.pair ? 30 : 0);
     const int64_t stages = (ksteps + c.split - 1) / c.split;
-    const int64_t cost = waves * (3000 + (c.pair ? 600 : 0) + (silu ? 38 : 29) * (bn / c.split) +
-                                  stages * per_stage + (c.split > 1 ? 4000 : 0));
+    const int64_t cost = waves * (3000 + (silu ? 38 : 29) * (bn / c.split) + stages * per_stage +
+                                  (c.split > 1 ? 4000 : 0)) +
+                         (c.pair ? 5000 : 0);
     if (best_cost < 0 || cost < best_cost) {
       best = i;
       best_cost = cost;
@@ -1837,9 +1927,13 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) 
 
 cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  if (args.rope_q16)  // the fused q/k norm + RoPE epilogue: two whole heads per tile
-    return config == 0 ? launch_h_impl<256, false, 1, true>(tmap_a, tmap_w, args, s)
-                       : cudaErrorInvalidValue;
+  if (args.rope_q16) {  // the fused q/k norm + RoPE epilogue: two whole heads per tile
+    switch (config) {
+      case 0: return launch_h_impl<256, false, 1, true>(tmap_a, tmap_w, args, s);
+      case 7: return launch_h2_impl<256, false, true>(tmap_a, tmap_w, args, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (args.silu_out) {
     switch (config) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
       case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);

@@ -105,6 +105,7 @@ constexpr int h_tile_n(int c) { return kTileNF[kHConfigs[c].width] * (kHConfigs[
 constexpr unsigned kHAll = (1u << kNumHConfigs) - 1;
 constexpr unsigned kHNoSplit = 0x18Fu;  // 0-3 and the pairs 7, 8
 constexpr unsigned kHSilu = 0x187u;     // BN >= 64 without split-K: 0-2, 7, 8
+constexpr unsigned kHRope = 0x81u;      // two whole heads per 128-row tile: 0, 7
 
 constexpr int kMaxSlices = 4;
 

@@ -74,6 +74,39 @@ __device__ __forceinline__ bool ovb_wait(uint32_t bar, uint32_t parity, volatile
   }
 }
 
+// Arrive once on an mbarrier of another CTA of the cluster (`bar` is a
+// shared::cluster address from mapa_shared), releasing this thread's prior
+// memory operations at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// ovb_wait for a barrier that other CTAs of the cluster arrive on: the wait
+// acquires at cluster scope.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool ovb_wait_cluster(uint32_t bar, uint32_t parity,
+                                                 volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitLimitCycles) return false;
+  }
+}
+
 // 16-byte global load that only happens when `pred` holds (else zeros);
 // predicated rather than branched, so that a batch of them is in flight
 // together.  The .cg form reads through L2 only (data written by other SMs

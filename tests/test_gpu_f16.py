@@ -304,15 +304,17 @@ def test_linear_h_unaligned_c(cuda, monkeypatch, offset, pad, tile_n, split):
 
 # ------------------------------------ CTA pairs (tcgen05 cta_group::2, M = 256)
 PAIR_SHAPES = [(400, 1024, 1024), (129, 320, 1056), (300, 4096, 1024), (1, 256, 64),
-               (1400, 6144, 1024), (600, 1000, 256)]
+               (1400, 6144, 1024), (600, 1000, 256), (3000, 4096, 1024), (2600, 1000, 512)]
 
 
 @pytest.mark.parametrize("tile_n", [256, 128])
 @pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
 def test_linear_h_pair(cuda, monkeypatch, tile_n, M, N, K):
-    """A 2-CTA cluster computes a 256-row tile with cta_group::2 MMAs, each
+    """A 2-CTA cluster computes 256-row tiles with cta_group::2 MMAs, each
     CTA loading half of the W tile.  300 rows leave the second pair's peer
-    CTA without rows; 1400 x 6144 needs several waves of clusters."""
+    CTA without rows; 1400 x 6144 and the two larger shapes give each
+    cluster of the persistent grid several tiles (both accumulators and
+    the peer's release of them in use)."""
     monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
     monkeypatch.setenv("OVB_GEMM_PAIR", "1")
     rng = np.random.default_rng(M * 3 + N + K + tile_n)

@@ -89,9 +89,15 @@ def qkv_weight(rng, H, KV, K):
     return w
 
 
+# pair 0: single-CTA 128 x 256 tiles; pair 1: the persistent cta_group::2
+# kernel (256 x 256 per 2-CTA cluster; 3000 rows give each cluster several
+# tiles, 300 rows a peer CTA without rows).
+@pytest.mark.parametrize("pair", [0, 1])
 @pytest.mark.parametrize("H,KV,K", [(16, 8, 1024), (2, 1, 256), (3, 1, 320), (4, 2, 64)])
-@pytest.mark.parametrize("M", [1, 77, 128, 300, 1000])
-def test_fused_qkv_gemm_equals_the_unfused_sequence(cuda, H, KV, K, M):
+@pytest.mark.parametrize("M", [1, 77, 128, 300, 1000, 3000])
+def test_fused_qkv_gemm_equals_the_unfused_sequence(cuda, monkeypatch, pair, H, KV, K, M):
+    monkeypatch.setenv("OVB_GEMM_TILE_N", "256")
+    monkeypatch.setenv("OVB_GEMM_PAIR", str(pair))
     rng = np.random.default_rng(M * 100 + H)
     w = qkv_weight(rng, H, KV, K)
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731

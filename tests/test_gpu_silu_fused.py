@@ -66,7 +66,7 @@ def test_q_silu_bit_exact_vs_reference(cuda, M, inter, K):
 # (tile width, CTA pair): the single-CTA widths and the cta_group::2 pairs.
 @pytest.mark.parametrize("tile_n,pair", [(256, 0), (128, 0), (64, 0), (256, 1), (128, 1)])
 @pytest.mark.parametrize("M,inter,K", [(1, 64, 64), (129, 256, 96), (400, 3072, 1024),
-                                       (300, 640, 1056)])
+                                       (300, 640, 1056), (2000, 3072, 1024)])
 def test_h_silu_agrees_with_unfused_fp16_sequence(cuda, monkeypatch, tile_n, pair, M, inter, K):
     rng = np.random.default_rng(3 * M + inter + K)
     (Wg, sg, Wu, su), g, u = weights(rng, inter, K, True)
