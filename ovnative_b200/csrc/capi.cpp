@@ -296,6 +296,14 @@ struct RopeOut {
   float eps;
 };
 
+// OVB_GEMM_TMA_OUT=0 keeps the plain fp16 epilogue on register stores (and
+// residual loads), =1 uses TMA boxes whenever the output allows; unset, the
+// launch shape decides.  A tuning and comparison switch.
+int tma_out_mode() {
+  const char* e = std::getenv("OVB_GEMM_TMA_OUT");
+  return e ? (e[0] == '0' ? 0 : 1) : -1;
+}
+
 // The plain fp16 mainloop on dequantised activations a16 [M, Kp] fp16.
 int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::SliceOut* slices,
                int n_slices, int accumulate, cudaStream_t s, const SiluOut* silu = nullptr,
@@ -343,6 +351,27 @@ int run_gemm_h(int64_t M, const ovb_weight* wc, const void* a16, const ovb::Slic
       M, w->N, w->Kb, w->device,
       rope ? ovb::kHRope
            : (silu ? ovb::kHSilu : (args.split_ws ? ovb::kHAll : ovb::kHNoSplit)));
+  // Plain outputs leave through the TMA (stores, or adds into C when
+  // accumulating) when every slice's rows are 16-byte aligned and the CTAs
+  // have several tiles each (the epilogue then runs beside the next tile's
+  // mainloop, and C's traffic no longer passes through the SM; with one tile
+  // per CTA the register stores finish sooner: 0.2 us at 400 rows).
+  const int64_t out_tiles = ((M + ovb::kBlockM - 1) / ovb::kBlockM) *
+                            ((w->N + ovb::h_tile_n(config) - 1) / ovb::h_tile_n(config));
+  const int tma_mode = tma_out_mode();
+  if (!silu && !rope &&
+      (tma_mode == 1 || (tma_mode < 0 && out_tiles > 2 * ovb::num_sms(w->device)))) {
+    bool ok = true;
+    for (int i = 0; i < n_slices; ++i)
+      ok = ok && (reinterpret_cast<uintptr_t>(slices[i].C) & 15) == 0 && (slices[i].ldc & 3) == 0;
+    for (int i = 0; ok && i < n_slices; ++i)
+      if (!ovb::encode_tmap_2d(&args.out_map[i], slices[i].C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                               static_cast<uint64_t>(slices[i].n_count), static_cast<uint64_t>(M),
+                               static_cast<uint64_t>(slices[i].ldc) * 4, 32u, 32u,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+        return OVB_ERR_INTERNAL;
+    args.out_tma = ok ? 1 : 0;
+  }
   const int width = ovb::kHConfigs[config].width;
   if (cuda_failed(ovb::launch_gemm_h(config, tmap_a, w->tmap_w16[width], args, s), "gemm launch"))
     return OVB_ERR_INTERNAL;
@@ -394,12 +423,11 @@ int check_h_args(int64_t M, const ovb_weight* w, const void* a16) {
 }
 
 int check_rope(int n_heads, int n_kv, int head_dim, const float* q_norm, const float* k_norm,
-               const float* table, const void* q16, const void* k16, const void* v16) {
+               const void* q16, const void* k16, const void* v16) {
   if (head_dim != 128) return invalid("head_dim must be 128");
   if (n_heads <= 0 || n_kv <= 0) return invalid("n_heads and n_kv must be positive");
-  if (!q_norm || !k_norm || !table || !q16 || !k16 || !v16)
-    return invalid("q_norm/k_norm/table/q16/k16/v16 must be non-null");
-  if (!aligned(table, 16)) return invalid("table must be 16-byte aligned");
+  if (!q_norm || !k_norm || !q16 || !k16 || !v16)
+    return invalid("q_norm/k_norm/q16/k16/v16 must be non-null");
   if (!aligned(q16, 16) || !aligned(k16, 16) || !aligned(v16, 16))
     return invalid("q16/k16/v16 must be 16-byte aligned");
   return OVB_OK;
@@ -919,8 +947,10 @@ int ovb_qk_norm_rope_f16(int64_t rows, const float* q, const float* k, const flo
                          const float* k_norm, float eps, const float* table, void* q16, void* k16,
                          void* v16, void* stream) {
   if (rows <= 0) return OVB_OK;
-  int st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, table, q16, k16, v16);
+  int st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, q16, k16, v16);
   if (st != OVB_OK) return st;
+  if (!table) return invalid("table must be non-null");
+  if (!aligned(table, 16)) return invalid("table must be 16-byte aligned");
   if (!q || !k || !v) return invalid("q/k/v must be non-null");
   if (rows > (int64_t{1} << 31) - 1) return invalid("rows exceeds 2^31-1");
   if (cuda_failed(ovb::launch_qk_norm_rope_f16(q, k, v, q16, k16, v16, q_norm, k_norm, table, rows,
@@ -936,8 +966,10 @@ int ovb_linear_h_qk_rope(int64_t M, const ovb_weight* w, const void* a16, int n_
   if (M <= 0) return OVB_OK;
   int st = check_h_args(M, w, a16);
   if (st != OVB_OK) return st;
-  st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, table, q16, k16, v16);
+  st = check_rope(n_heads, n_kv, head_dim, q_norm, k_norm, q16, k16, v16);
   if (st != OVB_OK) return st;
+  if (!table) return invalid("table must be non-null");
+  if (!aligned(table, 16)) return invalid("table must be 16-byte aligned");
   const int64_t qd = int64_t{n_heads} * 128, kvd = int64_t{n_kv} * 128;
   if (w->N != qd + 2 * kvd)
     return invalid("the weight's N must be (n_heads + 2 n_kv) * head_dim (a q|k|v weight)");

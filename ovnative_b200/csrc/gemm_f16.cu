@@ -86,10 +86,14 @@ constexpr uint32_t kABytesF = kBlockM * kStageKF;
 // row-per-lane float4 writes and the 4-rows-per-instruction float4 reads of
 // a 32x32 chunk are free of bank conflicts.
 constexpr int kStgStrideF = 36;
+// The plain fp16 epilogues' per-warp area: a 32 x 36-float staging chunk, or
+// (TMA output) a 4 KB box with the 128-byte swizzle plus 1 KB of wscale.
+constexpr int kStgTmaBytes = 32 * 128;
+constexpr int kStgWarpBytes = 6144;
 // Per epilogue warp of the fused q|k|v mode: one head's wscale and norm
-// weights, staged for broadcast reads.
+// weights, staged for broadcast reads, and two 2 KB buffers of the RoPE
+// table (32 rows x 8 pairs each).
 constexpr int kRopeColFloats = 256;
-// ... and two 2 KB buffers of the RoPE table (32 rows x 8 pairs each).
 constexpr int kRopeTabBufBytes = 2048;
 // named barriers (0 is __syncthreads)
 constexpr int kBarStage = 1;                    // + s: converters -> MMA warp
@@ -317,7 +321,16 @@ __device__ __forceinline__ bool rows_aligned(const SliceOut& so) {
 // after the last chunk the warps bar.sync on dfree_bar + d with the MMA warp
 // (which syncs there before reusing accumulator d).  kPipe = false loads one
 // chunk at a time (for kernels short of registers).
-template <int BN, int kAcc, bool kPipe = true>
+//
+// TMA output (kTmaOk and args.out_tma; the warp's `stg` area is then
+// kStgWarpBytes, 1 KB aligned): each lane scales its row of the chunk by the
+// columns' wscale (read as shared-memory broadcasts from the area's last
+// kilobyte), writes it into a 32 x 128-byte box with the 128-byte swizzle,
+// and lane 0 hands the box to the TMA unit: a store, or with accumulate an
+// element-wise add into C performed at L2 -- so the residual is never read
+// into the SM.  fl(fl(acc * ws) + C) either way, as the register path.
+// The TMA clips rows past M and columns past the slice.
+template <int BN, int kAcc, bool kPipe = true, bool kTmaOk = false>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull,
                                               volatile int* abort, uint32_t tmem_base,
                                               float* stg, int quarter, int eh, int dfree_bar,
@@ -328,6 +341,8 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N;
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const bool tma = kTmaOk && args.out_tma != 0;
+  float* colv = stg + kStgTmaBytes / 4;  // TMA path: the chunks' wscale values
   int64_t t = 0;
   for (int64_t tile = tile_first; tile < tiles; tile += tile_step, ++t) {
     const int d = static_cast<int>(t % kAcc);
@@ -339,6 +354,10 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     for (int i = 0; i < kMine; ++i) {
       const int64_t n = n0 + (eh + 2 * i) * 32 + lane;
       wsv[i] = (eh + 2 * i < kChunks && n < N) ? __ldg(args.wscale + n) : 0.f;
+    }
+    if (tma) {
+#pragma unroll
+      for (int i = 0; i < kMine; ++i) colv[32 * i + lane] = wsv[i];
     }
     const bool got = ovb_wait(smem_u32(&tfull[d]), ph, abort);
     if (!__all_sync(0xffffffffu, got)) {
@@ -362,6 +381,41 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
         if (!kPipe && i > 0) tmem_ld32(dcol + static_cast<uint32_t>(c * 32), cur);
         tc_wait_ld32(cur);
         if (kPipe && c + 2 < kChunks) tmem_ld32(dcol + static_cast<uint32_t>((c + 2) * 32), nxt);
+        if (kTmaOk && tma) {
+          const int64_t nc = n0 + c * 32;
+          const float4* w4 = reinterpret_cast<const float4*>(colv + 32 * i);
+          float4 o[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 w = w4[q];  // broadcast: every lane the same columns
+            o[q] = make_float4(__fmul_rn(__uint_as_float(cur[4 * q]), w.x),
+                               __fmul_rn(__uint_as_float(cur[4 * q + 1]), w.y),
+                               __fmul_rn(__uint_as_float(cur[4 * q + 2]), w.z),
+                               __fmul_rn(__uint_as_float(cur[4 * q + 3]), w.w));
+          }
+          // the previous chunk's box has left the staging area
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          float4* box = reinterpret_cast<float4*>(stg) + lane * 8;  // row `lane`
+#pragma unroll
+          for (int q = 0; q < 8; ++q) box[q ^ (lane & 7)] = o[q];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && nc < N && rows > 0) {
+            int si = 0;
+#pragma unroll
+            for (int k = 1; k < kMaxSlices; ++k)
+              if (k < args.n_slices && nc >= args.slices[k].n_begin) si = k;
+            const int32_t x = static_cast<int32_t>(nc - args.slices[si].n_begin);
+            const int32_t y = static_cast<int32_t>(r0);
+            if (args.accumulate)
+              tma_reduce_add_2d(&args.out_map[si], smem_u32(stg), x, y);
+            else
+              tma_store_2d(&args.out_map[si], smem_u32(stg), x, y);
+            bulk_commit();
+          }
+          continue;
+        }
         stage_chunk(stg, cur);
         __syncwarp();
         const int64_t nc = n0 + c * 32;  // first column of the chunk
@@ -384,6 +438,7 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     tc_fence_before();
     if (t + kAcc < my_tiles) named_sync(dfree_bar + d, 32 * (kEpiWarpsF + 1));
   }
+  if (tma && lane == 0) bulk_wait_all();  // the boxes are written before the CTA exits
 }
 
 // 16-byte asynchronous copy global -> shared (cp.async, L2 only), the group
@@ -408,6 +463,25 @@ __device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
   return (e & 3) == 0 ? q.x : (e & 3) == 1 ? q.y : (e & 3) == 2 ? q.z : q.w;
 }
 
+// Two IEEE round-to-nearest products in one packed instruction:
+// (a.x * b.x, a.y * b.y).  Only products are packed: a sum or difference of
+// products stays a scalar add.rn, so no product is ever contracted into a
+// fused multiply-add and every result rounds exactly as the scalar form.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+// Elements e, e + 1 (e even) of an 8-float register pair as a float2.
+__device__ __forceinline__ float2 f4_pair(const float4 (&v)[2], int e) {
+  const float4 q = v[e >> 2];
+  return (e & 2) == 0 ? make_float2(q.x, q.y) : make_float2(q.z, q.w);
+}
+
 // The epilogue loop of the fused q|k|v mode (args.rope_q16 non-null; BN =
 // 256, two 128-column heads per tile).  Warp (quarter, eh) takes head eh of
 // the tile for TMEM lanes 32*quarter..: each thread holds one row of the
@@ -418,7 +492,8 @@ __device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
 // at distances 16, 8, .., 1, the order of its warp tree), the same scale and
 // rotation -- so the fp16 outputs equal the unfused sequence bit for bit; v
 // heads are converted.  The per-column values (wscale, norm weight) are the
-// same for every lane: they are read as float4 broadcasts.  Two passes over
+// same for every lane: they are read as float4 broadcasts; products are
+// packed two per instruction (f32x2), sums stay scalar.  Two passes over
 // TMEM, sixteen columns at a time: the sum of squares, then the rotation of
 // set s (head elements 32s + i with 64 + 32s + i, s = 0, 1), whose 64 fp16
 // outputs are staged in shared memory (32 rows x 128 bytes, 16-byte chunks
@@ -527,12 +602,16 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                   wb[u] = *(ws4 + 16 * pr + 8 + 4 * hf + 2 * gg + u);
                 }
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
+                for (int e = 0; e < 8; e += 2) {
                   const int iv = 8 * gg + e;
-                  const float x = __fmul_rn(__uint_as_float(va[iv]), f4_at2(wa, e));
-                  const float y = __fmul_rn(__uint_as_float(vb[iv]), f4_at2(wb, e));
-                  const float q2 = __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y));
-                  s01[16 * hf + iv] = pr == 0 ? q2 : __fadd_rn(s01[16 * hf + iv], q2);
+                  const float2 x = mul2(make_float2(__uint_as_float(va[iv]), __uint_as_float(va[iv + 1])),
+                                        f4_pair(wa, e));
+                  const float2 y = mul2(make_float2(__uint_as_float(vb[iv]), __uint_as_float(vb[iv + 1])),
+                                        f4_pair(wb, e));
+                  const float2 xx = mul2(x, x), yy = mul2(y, y);
+                  const float q0 = __fadd_rn(xx.x, yy.x), q1 = __fadd_rn(xx.y, yy.y);
+                  s01[16 * hf + iv] = pr == 0 ? q0 : __fadd_rn(s01[16 * hf + iv], q0);
+                  s01[16 * hf + iv + 1] = pr == 0 ? q1 : __fadd_rn(s01[16 * hf + iv + 1], q1);
                 }
               }
             }
@@ -599,28 +678,29 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
               uint32_t lo_w[4], hi_w[4];
 #pragma unroll
               for (int e = 0; e < 8; e += 2) {
-                float lo[2], hi[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int iv = 8 * gg + e + h;  // element of va / vb
-                  const int iw = e + h;           // element of wa / wb / na / nb
-                  const float x = __fmul_rn(__uint_as_float(va[iv]), f4_at2(wa, iw));
-                  const float y = __fmul_rn(__uint_as_float(vb[iv]), f4_at2(wb, iw));
-                  if (kind < 2) {
-                    const float4 c2 = cs[(e + h) >> 1];
-                    const float cs_ = ((e + h) & 1) ? c2.z : c2.x;
-                    const float sn = ((e + h) & 1) ? c2.w : c2.y;
-                    const float a = __fmul_rn(__fmul_rn(x, scale), f4_at2(na, iw));
-                    const float b = __fmul_rn(__fmul_rn(y, scale), f4_at2(nb, iw));
-                    lo[h] = __fsub_rn(__fmul_rn(a, cs_), __fmul_rn(b, sn));
-                    hi[h] = __fadd_rn(__fmul_rn(b, cs_), __fmul_rn(a, sn));
-                  } else {
-                    lo[h] = x;
-                    hi[h] = y;
-                  }
+                // elements e, e + 1 of the step (va / vb elements 8 gg + e ..);
+                // products packed two per instruction, sums scalar
+                const int iv = 8 * gg + e;
+                const float2 x = mul2(make_float2(__uint_as_float(va[iv]), __uint_as_float(va[iv + 1])),
+                                      f4_pair(wa, e));
+                const float2 y = mul2(make_float2(__uint_as_float(vb[iv]), __uint_as_float(vb[iv + 1])),
+                                      f4_pair(wb, e));
+                float2 lo = x, hi = y;
+                if (kind < 2) {
+                  // pairs 8k + e, 8k + e + 1: (cos, sin) of both elements
+                  // (rotation pairs are columns i and 64 + i: lo and hi)
+                  const float4 c2 = cs[e >> 1];
+                  const float2 cv = make_float2(c2.x, c2.z), sv = make_float2(c2.y, c2.w);
+                  const float2 sc = make_float2(scale, scale);
+                  const float2 a = mul2(mul2(x, sc), f4_pair(na, e));
+                  const float2 b = mul2(mul2(y, sc), f4_pair(nb, e));
+                  const float2 ac = mul2(a, cv), bs = mul2(b, sv);
+                  const float2 bc = mul2(b, cv), as = mul2(a, sv);
+                  lo = make_float2(__fsub_rn(ac.x, bs.x), __fsub_rn(ac.y, bs.y));
+                  hi = make_float2(__fadd_rn(bc.x, as.x), __fadd_rn(bc.y, as.y));
                 }
-                const __half2 l2 = __floats2half2_rn(lo[0], lo[1]);
-                const __half2 h2 = __floats2half2_rn(hi[0], hi[1]);
+                const __half2 l2 = __floats2half2_rn(lo.x, lo.y);
+                const __half2 h2 = __floats2half2_rn(hi.x, hi.y);
                 lo_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
                 hi_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
                 // an fp16 output that is infinite or NaN: exponent bits all set
@@ -1087,7 +1167,7 @@ struct CtlH {
 // [kSplit - 1 senders][128 rows][kOwn floats].  A split-K CTA needs more
 // than half of the SM's shared memory, so no two of them share an SM (or a
 // workspace slot).
-template <int BN, bool kSilu, int kSplit = 1, bool kRope = false>
+template <int BN, bool kSilu, int kSplit = 1>
 struct TileH {
   static_assert(kSplit == 1 || (!kSilu && (BN / kSplit) % 32 == 0), "split-K layout");
   static constexpr uint32_t kWBytes = BN * 128;
@@ -1095,12 +1175,11 @@ struct TileH {
   static constexpr int kAcc = 2;
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
-  // epilogue staging: 32 x 32 fp32 chunks, or 32 rows x 64 bytes of the
-  // fused SiLU*up epilogue's quantised output
-  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4) +
-                                    (kRope ? static_cast<size_t>(kEpiW) *
-                                                 (kRopeColFloats * 4 + 2 * kRopeTabBufBytes)
-                                           : 0);
+  // per epilogue warp: 32 x 64 bytes of quantised rows (SiLU*up), a 32 x 36
+  // float chunk (split-K), or the plain epilogue's area
+  static constexpr size_t kStgWarp =
+      kSilu ? 32 * 64 : (kSplit > 1 ? 32 * kStgStrideF * 4 : kStgWarpBytes);
+  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * kStgWarp;
   static constexpr int kOwn = BN / kSplit;  // columns owned per rank
   static constexpr size_t kPartialFloats = static_cast<size_t>(kBlockM) * kOwn;  // per sender
   // As many stages as fit (a deeper ring hides more TMA latency; narrow
@@ -1113,6 +1192,8 @@ struct TileH {
   static_assert(kStages >= 3, "too few pipeline stages");
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert((kStageBytes % 1024 == 0 && kStgWarp % 1024 == 0) || kSilu || kSplit > 1,
+                "TMA output boxes stay 1 KB aligned");
   static_assert(kSplit == 1 || kSmemBytes > 116 * 1024, "a split-K CTA must have its SM alone");
   static_assert(kSplit == 1 || (kSplit - 1) * kPartialFloats * 4 <= kSplitSlotBytes,
                 "split-K workspace slot");
@@ -1284,12 +1365,12 @@ __device__ __forceinline__ void split_finish(const GemmArgs& args, CtlH* ctl,
   }
 }
 
-template <int BN, bool kSilu, int kSplit, bool kRope>
+template <int BN, bool kSilu, int kSplit>
 __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
     gemm_h_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ GemmArgs args) {
-  using T = TileH<BN, kSilu, kSplit, kRope>;
+  using T = TileH<BN, kSilu, kSplit>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1434,26 +1515,18 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
         split_send<BN, kSplit>(args, ctl, abort, tmem_base,
                                stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
                                (warp - kFirstEpiH) >> 2, rank);
-    } else if constexpr (kRope) {
-      epilogue_rope_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                                      stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF),
-                                      stg_all + T::kEpiW * (32 * kStgStrideF) +
-                                          (warp - kFirstEpiH) * kRopeColFloats,
-                                      reinterpret_cast<uint8_t*>(stg_all + T::kEpiW * (32 * kStgStrideF +
-                                                                                   kRopeColFloats)) +
-                                          (warp - kFirstEpiH) * (2 * kRopeTabBufBytes),
-                                      warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles,
-                                      m_tiles, my_tiles, blockIdx.x, gridDim.x);
     } else if constexpr (kSilu) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(stg_all) + (warp - kFirstEpiH) * (32 * 64);
       silu_epilogue<BN, T::kAcc, T::kEpiW>(args, ctl->tfull, abort, tmem_base, stg, warp & 3,
                                            (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles,
                                            my_tiles, blockIdx.x, gridDim.x);
     } else {
-      epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                                 stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles,
-                                 blockIdx.x, gridDim.x);
+      epilogue_loop<BN, T::kAcc, true, true>(
+          args, ctl->tfull, abort, tmem_base,
+          reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) +
+                                   (warp - kFirstEpiH) * T::kStgWarp),
+          warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, tiles, m_tiles, my_tiles, blockIdx.x,
+          gridDim.x);
     }
   }
 
@@ -1475,11 +1548,11 @@ __global__ void __launch_bounds__(TileH<BN, kSilu, kSplit>::kThreads, 1)
   }
 }
 
-template <int BN, bool kSilu, int kSplit = 1, bool kRope = false>
+template <int BN, bool kSilu, int kSplit = 1>
 cudaError_t launch_h_impl(const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  using T = TileH<BN, kSilu, kSplit, kRope>;
-  auto* kernel = gemm_h_kernel<BN, kSilu, kSplit, kRope>;
+  using T = TileH<BN, kSilu, kSplit>;
+  auto* kernel = gemm_h_kernel<BN, kSilu, kSplit>;
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
@@ -1555,10 +1628,14 @@ struct TileH2 {
   static constexpr int kAcc = 2;
   static constexpr int kEpiW = epi_warps_h<kSilu>();
   static constexpr int kThreads = 32 * (kFirstEpiH + kEpiW);
-  static constexpr size_t kStgAll = static_cast<size_t>(kEpiW) * 32 * (kSilu ? 64 : kStgStrideF * 4) +
-                                    (kRope ? static_cast<size_t>(kEpiW) *
-                                                 (kRopeColFloats * 4 + 2 * kRopeTabBufBytes)
-                                           : 0);
+  // per epilogue warp: 32 x 64 bytes of quantised rows (SiLU*up), a 32 x 36
+  // float chunk (norm + RoPE, then its column values and table buffers), or
+  // the plain epilogue's area
+  static constexpr size_t kStgWarp =
+      kSilu ? 32 * 64 : (kRope ? 32 * kStgStrideF * 4 : kStgWarpBytes);
+  static constexpr size_t kStgAll =
+      static_cast<size_t>(kEpiW) * kStgWarp +
+      (kRope ? static_cast<size_t>(kEpiW) * (kRopeColFloats * 4 + 2 * kRopeTabBufBytes) : 0);
   static constexpr int kStagesFit =
       static_cast<int>((227 * 1024 - 1024 - kStgAll - sizeof(CtlH)) / kStageBytes);
   static constexpr int kStages = kStagesFit < kMaxStagesH ? kStagesFit : kMaxStagesH;
@@ -1568,6 +1645,7 @@ struct TileH2 {
   static_assert(kAcc * BN <= static_cast<int>(kTmemColsF), "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(kStageBytes % 1024 == 0, "stage bases stay 1 KB aligned");
+  static_assert(kRope || kSilu || kStgWarp % 1024 == 0, "TMA output boxes stay 1 KB aligned");
 };
 
 template <int BN, bool kSilu, bool kRope>
@@ -1753,10 +1831,12 @@ __global__ void __launch_bounds__(TileH2<BN, kSilu, kRope>::kThreads, 1)
                                            (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles,
                                            m_tiles_v, my_tiles, blockIdx.x, gridDim.x);
     } else {
-      epilogue_loop<BN, T::kAcc>(args, ctl->tfull, abort, tmem_base,
-                                 stg_all + (warp - kFirstEpiH) * (32 * kStgStrideF), warp & 3,
-                                 (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles, m_tiles_v,
-                                 my_tiles, blockIdx.x, gridDim.x);
+      epilogue_loop<BN, T::kAcc, true, true>(
+          args, ctl->tfull, abort, tmem_base,
+          reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(stg_all) +
+                                   (warp - kFirstEpiH) * T::kStgWarp),
+          warp & 3, (warp - kFirstEpiH) >> 2, kBarDfreeH, vtiles, m_tiles_v, my_tiles, blockIdx.x,
+          gridDim.x);
     }
   }
 
@@ -1927,13 +2007,9 @@ int pick_tile_h(int64_t M, int64_t N, int64_t Kb, int device, unsigned allowed) 
 
 cudaError_t launch_gemm_h(int config, const CUtensorMap& tmap_a, const CUtensorMap& tmap_w,
                           const GemmArgs& args, cudaStream_t s) {
-  if (args.rope_q16) {  // the fused q/k norm + RoPE epilogue: two whole heads per tile
-    switch (config) {
-      case 0: return launch_h_impl<256, false, 1, true>(tmap_a, tmap_w, args, s);
-      case 7: return launch_h2_impl<256, false, true>(tmap_a, tmap_w, args, s);
-      default: return cudaErrorInvalidValue;
-    }
-  }
+  if (args.rope_q16)  // the fused q/k norm + RoPE epilogue: CTA pairs, two heads per CTA
+    return config == 7 ? launch_h2_impl<256, false, true>(tmap_a, tmap_w, args, s)
+                       : cudaErrorInvalidValue;
   if (args.silu_out) {
     switch (config) {  // the fused epilogue needs whole gate/up block pairs: BN >= 64
       case 0: return launch_h_impl<256, true>(tmap_a, tmap_w, args, s);

@@ -105,7 +105,7 @@ constexpr int h_tile_n(int c) { return kTileNF[kHConfigs[c].width] * (kHConfigs[
 constexpr unsigned kHAll = (1u << kNumHConfigs) - 1;
 constexpr unsigned kHNoSplit = 0x18Fu;  // 0-3 and the pairs 7, 8
 constexpr unsigned kHSilu = 0x187u;     // BN >= 64 without split-K: 0-2, 7, 8
-constexpr unsigned kHRope = 0x81u;      // two whole heads per 128-row tile: 0, 7
+constexpr unsigned kHRope = 0x80u;      // the norm + RoPE epilogue: the 256-wide pair, 7
 
 constexpr int kMaxSlices = 4;
 
@@ -150,6 +150,11 @@ struct GemmArgs {
   const float* rope_tab;
   int64_t rope_qd, rope_kvd;
   float rope_eps;
+  // Plain fp16-mainloop outputs written by TMA (out_tma != 0): out_map[i] is
+  // slice i's C as fp32 [M, n_count] (row stride ldc), boxes of 32 x 32 with
+  // 128-byte swizzle; stores, or element-wise adds when accumulating.
+  int out_tma;
+  alignas(64) CUtensorMap out_map[kMaxSlices];
 };
 
 // The split-K workspace: one slot per SM id (%smid < kSplitSlots), each large

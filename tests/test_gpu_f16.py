@@ -338,6 +338,62 @@ def test_linear_h_pair(cuda, monkeypatch, tile_n, M, N, K):
     w.close()
 
 
+# The plain epilogue writes C through TMA boxes (stores; element-wise adds
+# at L2 when accumulating) whenever every output slice's rows are 16-byte
+# aligned; OVB_GEMM_TMA_OUT=0 keeps the register stores and residual loads.
+# Both forms compute fl(fl(acc * wscale) + C) and must agree bit for bit.
+@pytest.mark.parametrize("tile_n,pair", [(256, 0), (128, 0), (64, 0), (32, 0), (256, 1),
+                                         (128, 1)])
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (300, 1000, 256), (2600, 1024, 1024),
+                                   (777, 4096, 512)])
+def test_tma_output_equals_register_stores(cuda, monkeypatch, tile_n, pair, M, N, K):
+    monkeypatch.setenv("OVB_GEMM_TILE_N", str(tile_n))
+    monkeypatch.setenv("OVB_GEMM_PAIR", str(pair))
+    rng = np.random.default_rng(M + N + K + tile_n + pair)
+    A, W, s = case(rng, M, N, K)
+    w = ovb.Weight.from_nk(W, s, f16=True)
+    a16, _ = ovb.s8_nk_quantize(dev(A, cuda), f16=True)
+    C0 = dev(rng.standard_normal((M, N)).astype(np.float32), cuda)
+    outs = {}
+    for tma in ("1", "0"):
+        monkeypatch.setenv("OVB_GEMM_TMA_OUT", tma)
+        plain = torch.full((M, N), float("nan"), device=cuda)
+        ovb.linear_h(a16, w, plain)
+        acc = C0.clone()
+        ovb.linear_h(a16, w, acc, accumulate=True)
+        # a row stride with padding (ldc = N + 4 keeps 16-byte rows)
+        wide = torch.full((M, N + 4), float("nan"), device=cuda)
+        ovb.linear_h(a16, w, wide[:, :N])
+        outs[tma] = (host(plain), host(acc), host(wide))
+    for a, b in zip(outs["1"], outs["0"]):
+        assert a.tobytes() == b.tobytes()
+    assert np.isnan(outs["1"][2][:, N:]).all()  # the padding is untouched
+    assert ovb.device_status() == 0
+    w.close()
+
+
+def test_tma_output_sliced(cuda, golden, monkeypatch):
+    """Three output slices (q|k|v-like): one TMA map per slice."""
+    monkeypatch.setenv("OVB_GEMM_TILE_N", "256")
+    for pair in ("0", "1"):
+        monkeypatch.setenv("OVB_GEMM_PAIR", pair)
+        for i in range(3):
+            Ns = [int(n) for n in golden[f"sliced{i}_Ns"]]
+            parts = [ovb.Weight.from_nk(golden[f"sliced{i}_W{j}"], golden[f"sliced{i}_s{j}"],
+                                        f16=True) for j in range(len(Ns))]
+            wc = ovb.Weight.concat(parts)
+            a16, _ = ovb.s8_nk_quantize(dev(golden[f"sliced{i}_A"], cuda), f16=True)
+            got = {}
+            for tma in ("1", "0"):
+                monkeypatch.setenv("OVB_GEMM_TMA_OUT", tma)
+                Cs = [torch.ones((a16.shape[0], n), device=cuda) for n in Ns]
+                ovb.linear_h_sliced(a16, wc, Cs)
+                got[tma] = [host(c) for c in Cs]
+            for a, b in zip(got["1"], got["0"]):
+                assert a.tobytes() == b.tobytes()
+    assert ovb.device_status() == 0
+
+
 def test_linear_h_pair_sliced(cuda, golden, monkeypatch):
     monkeypatch.setenv("OVB_GEMM_TILE_N", "128")
     monkeypatch.setenv("OVB_GEMM_PAIR", "1")
