@@ -1462,6 +1462,47 @@ def run_reference(args, rank: int, world: int):
     }
 
 
+# Rows of the largest batch one GPU runs at config 4 (bench.py
+# --profile-forward prints it): the GEMM shapes the forward's launch list shows.
+CONFIG4_BATCH_ROWS = 15408
+
+
+def profile_gemm(name: str) -> None:
+    """Three launches of one fp16 forward GEMM at the config-4 batch, as the LM
+    calls it: q|k|v with the fused norm + RoPE, o and down accumulating into
+    the residual stream, gate|up with the fused SiLU*up quantiser."""
+    import torch
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import layer as LY
+    dev = torch.device("cuda", 0)
+    M = CONFIG4_BATCH_ROWS
+    rng = np.random.default_rng(41)
+    lw = LY.LayerWeights.from_host(LY.random_layer_host(rng), dev, f16=True)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(42)
+    x = torch.randn((M, LY.HIDDEN), device=dev, generator=gen)
+    qh = ovb.rmsnorm_quantize_f32(x, lw.input_ln, LY.RMS_EPS, f16=True)
+    if name == "qkv":
+        tab = ovb.rope_table(torch.arange(M, device=dev, dtype=torch.int64))
+        nrm = torch.ones(128, device=dev)
+        fn = lambda: ovb.linear_h_qk_rope(qh[0], lw.qkv, LY.QD // 128, LY.KVD // 128,  # noqa: E731
+                                          nrm, nrm, LY.RMS_EPS, tab)
+    elif name == "o":
+        a = ovb.s8_nk_quantize(torch.randn((M, LY.QD), device=dev, generator=gen), f16=True)[0]
+        fn = lambda: ovb.linear_h(a, lw.o, x, accumulate=True)  # noqa: E731
+    elif name == "gate_up":
+        fn = lambda: ovb.linear_h_silu(qh[0], lw.gate_up)  # noqa: E731
+    else:
+        qi = ovb.linear_h_silu(qh[0], lw.gate_up)
+        fn = lambda: ovb.linear_h(qi[0], lw.down, x, accumulate=True)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"gemm": name, "rows": M, "status": ovb.device_status()}), flush=True)
+    lw.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1493,6 +1534,9 @@ def main():
     ap.add_argument("--profile-forward", action="store_true",
                     help="build the 28-layer LM and the largest config-4 batch of one GPU and run "
                          "two eager forwards + samplers (for an ncu launch list)")
+    ap.add_argument("--profile-gemm", choices=["qkv", "o", "gate_up", "down"], default=None,
+                    help="run one of the fp16 forward's GEMMs three times at the largest "
+                         "config-4 batch of one GPU (15,408 rows; for ncu captures)")
     ap.add_argument("--sampler-only", action="store_true",
                     help="only time the guided sampler (one plane set, 8 launches; for "
                          "profiling runs) and print its entry")
@@ -1523,6 +1567,9 @@ def main():
             m.close()
         finally:
             shutil.rmtree(tmpdir, ignore_errors=True)
+        return
+    if args.profile_gemm:
+        profile_gemm(args.profile_gemm)
         return
     if args.sampler_only:
         import torch

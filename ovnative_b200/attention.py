@@ -177,6 +177,8 @@ def qk_norm_rope_f16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm: 
         if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous float32 CUDA tensor")
     rows = q.shape[0]
+    if table.numel() < rows * HEAD_DIM:
+        raise ValueError("table must hold 64 (cos, sin) pairs per row (rope_table)")
     n_heads, n_kv = q.shape[1] // HEAD_DIM, k.shape[1] // HEAD_DIM
     q16 = torch.empty(q.shape, dtype=torch.float16, device=q.device)
     k16 = torch.empty(k.shape, dtype=torch.float16, device=q.device)

@@ -138,3 +138,24 @@ def test_fused_qkv_gemm_flags_fp16_overflow(cuda):
     assert ovb.device_status() & 16
     for p in (*parts, w):
         p.close()
+
+
+def test_table_shape_and_type_are_checked_before_the_device(cuda):
+    """A RoPE table of the wrong type or too few rows is refused on the host
+    (the kernels read 64 (cos, sin) pairs for every row)."""
+    rng = np.random.default_rng(9)
+    M, H, KV, K = 300, 2, 1, 64
+    w = qkv_weight(rng, H, KV, K)
+    a16 = torch.zeros((M, K), dtype=torch.float16, device=cuda)
+    one = torch.ones(128, device=cuda)
+    pos = torch.arange(M, device=cuda, dtype=torch.int64)
+    with pytest.raises(ValueError, match="table"):
+        ovb.linear_h_qk_rope(a16, w, H, KV, one, one, EPS, pos)
+    short = ovb.rope_table(pos[: M // 2], THETA)
+    with pytest.raises(ValueError, match="table"):
+        ovb.linear_h_qk_rope(a16, w, H, KV, one, one, EPS, short)
+    q = torch.zeros((M, H * 128), device=cuda)
+    kv = torch.zeros((M, KV * 128), device=cuda)
+    with pytest.raises(ValueError, match="table"):
+        ovb.qk_norm_rope_f16(q, kv, kv, one, one, EPS, short)
+    w.close()
