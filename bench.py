@@ -166,6 +166,17 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def load_traffic_config4(gemm: str, f16: bool) -> float | None:
+    """DRAM bytes per launch of one of the config-4 forward's fp16 GEMMs (ncu,
+    committed summary), or None."""
+    p = os.path.join(ROOT, "profiles", "gemm_traffic_config4.json")
+    if not f16 or not os.path.exists(p):
+        return None
+    with open(p) as f:
+        k = json.load(f)["kernels"].get(gemm)
+    return float(k["read"] + k["write"]) if k else None
+
+
 def load_traffic(gemm: str, f16: bool) -> float | None:
     """DRAM bytes per launch of one of the step's GEMMs (ncu dram__bytes_read
     + dram__bytes_write) from the committed summary, or None."""
@@ -1082,7 +1093,7 @@ def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
         r = gemm_roofline(name, kern, M, N_g, K_g, res, ob, us, f16)
         r["launches_per_forward"] = per_fwd
         r["us_per_forward"] = round(us * per_fwd, 1)
-        r["traffic"] = None
+        r["traffic"] = load_traffic_config4(name, f16) if M == CONFIG4_BATCH_ROWS else None
         entries.append(r)
     # attention over the batch's segments with the LM's operands: fp16 q / k /
     # v and the tile table of the CFG masks (cond: all attended; uncond: the
