@@ -37,12 +37,60 @@ __device__ __forceinline__ float emb_at(const EmbTable& t, int64_t row, int c) {
 // embeddings of ids[b][c][s] + offsets[c], accumulated in codebook order from
 // 0.  ids are [B][C][seq] (forward_cfg: B = 1, seq = rows).  One block per
 // row; an id outside its table leaves the row zero and sets status bit 128.
+// Four consecutive elements of row `row` (c % 4 == 0, cols % 4 == 0): the
+// same values as emb_at, with one 4- or 16-byte load.
+__device__ __forceinline__ float4 emb_at4(const EmbTable& t, int64_t row, int c) {
+  if (t.i8) {
+    const char4 q = *reinterpret_cast<const char4*>(t.i8 + row * t.cols + c);
+    const float sc = t.scale[row];
+    return make_float4(__fmul_rn(static_cast<float>(q.x), sc), __fmul_rn(static_cast<float>(q.y), sc),
+                       __fmul_rn(static_cast<float>(q.z), sc), __fmul_rn(static_cast<float>(q.w), sc));
+  }
+  return *reinterpret_cast<const float4*>(t.f32 + row * t.cols + c);
+}
+
+constexpr int kEmbMaxC = 32;  // codebooks the vector path stages
+
 __global__ void embed_kernel(const int64_t* ids, const uint8_t* mask, const int64_t* offsets,
                              int C, int seq, EmbTable tok, EmbTable aud, float* out, int H) {
   const int64_t r = blockIdx.x;
   const int64_t b = r / seq, s = r % seq;
   const int64_t* base = ids + b * C * seq;
   float* o = out + r * H;
+  // Vector path: the row's ids read once into shared memory, then four
+  // consecutive columns per thread and load (the row's arithmetic unchanged:
+  // the same products, summed in codebook order).
+  const bool vec = C <= kEmbMaxC && (H & 3) == 0 && (tok.cols & 3) == 0 && (aud.cols & 3) == 0;
+  if (vec) {
+    __shared__ int64_t sid[kEmbMaxC];
+    __shared__ int s_bad;
+    const bool text = !mask[r];
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    if (threadIdx.x < (text ? 1 : C)) {
+      const int cb = threadIdx.x;
+      const int64_t id = text ? base[s] : base[static_cast<int64_t>(cb) * seq + s] + offsets[cb];
+      sid[cb] = id;
+      if (!(id >= 0 && id < (text ? tok.rows : aud.rows))) atomicOr(&s_bad, 1);
+    }
+    __syncthreads();
+    const bool ok = s_bad == 0;
+    for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok && text) {
+        acc = emb_at4(tok, sid[0], c);
+      } else if (ok) {
+        for (int cb = 0; cb < C; ++cb) {
+          const float4 e = emb_at4(aud, sid[cb], c);
+          acc = make_float4(__fadd_rn(acc.x, e.x), __fadd_rn(acc.y, e.y), __fadd_rn(acc.z, e.z),
+                            __fadd_rn(acc.w, e.w));
+        }
+      }
+      *reinterpret_cast<float4*>(o + c) = acc;
+    }
+    if (!ok && threadIdx.x == 0) atomicOr(&g_status_lm, kErrLmIndex);
+    return;
+  }
   if (!mask[r]) {
     const int64_t id = base[s];
     const bool ok = id >= 0 && id < tok.rows;
