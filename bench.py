@@ -996,8 +996,9 @@ def config_utt(world: int, lengths: dict) -> dict:
                     "172-204) + guided sampler (guidance 2.0, layer_penalty 5.0)",
         "layers": LM_LAYERS, "vocab": LM_VOCAB, "audio_heads": "int8",
         "batching": f"each GPU packs its CFG pairs into forwards of <= {MAX_ROWS} rows "
-                    "(attention segments stay per pair); with two or more batches, two LM "
-                    "instances run alternate batches on two streams",
+                    "(attention segments stay per pair); with two or more batches, up to "
+                    "four LM instances (--lanes) take the batches round-robin, each on its "
+                    "own stream",
         "parallelism": f"dp{world}: utterance-parallel, LPT shards of whole CFG pairs, no "
                        "collective on the data path",
         "l2": "inputs larger than L2: every forward streams 449 MB of int8 weights (plus their "
@@ -1157,10 +1158,10 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     lengths = utterance_lengths()
     plan = shard.lpt_assign([lengths[i] for i in range(len(lengths))], world)
     m = LM.LM(path, f16=f16)
-    # with two or more batches, a second LM instance (its own forward buffers)
-    # lets two batches' forwards run on two streams at once
+    # with two or more batches, further LM instances (their own forward
+    # buffers) let batches' forwards run on several streams at once
     n_batches = len(TB.pack_batches(lengths, plan[rank], MAX_ROWS)) if plan[rank] else 0
-    extra = [LM.LM(path, f16=f16)] if n_batches >= 2 else []
+    extra = [LM.LM(path, f16=f16) for _ in range(min(args.lanes, n_batches) - 1)]
     sp = TB.Stepper(m, lengths, plan[rank], dev, stream, max_rows=MAX_ROWS, seed=rank,
                     extra_lms=extra)
     sp.warm_and_capture()
@@ -1545,6 +1546,8 @@ def main():
     ap.add_argument("--profile-forward", action="store_true",
                     help="build the 28-layer LM and the largest config-4 batch of one GPU and run "
                          "two eager forwards + samplers (for an ncu launch list)")
+    ap.add_argument("--lanes", type=int, default=4,
+                    help="LM instances per GPU whose batches' forwards run on their own streams")
     ap.add_argument("--profile-gemm", choices=["qkv", "o", "gate_up", "down"], default=None,
                     help="run one of the fp16 forward's GEMMs three times at the largest "
                          "config-4 batch of one GPU (15,408 rows; for ncu captures)")
