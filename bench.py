@@ -1059,7 +1059,8 @@ def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
     qo = ovb.s8_nk_quantize(q, f16=f16)
     qi = ovb.linear_h_silu(qh[0], layers[0].gate_up) if f16 else \
         ovb.linear_q_silu(*qh, layers[0].gate_up)
-    kern = "gemm_h (fp16 mainloop)" if f16 else "gemm_s8_tc (int8 mainloop)"
+    # at these batch sizes every fp16 GEMM runs on persistent CTA pairs
+    kern = "gemm_h2_kernel (fp16 mainloop, CTA pairs)" if f16 else "gemm_s8_tc (int8 mainloop)"
     L_ = lambda i: layers[i % n_layers]  # noqa: E731
     # the fp16 forward's q|k|v GEMM carries the q/k norm + RoPE in its
     # epilogue and writes fp16 q / k / v (the LM's path, ovb_linear_h_qk_rope)
