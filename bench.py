@@ -1209,7 +1209,8 @@ def time_utterances(args, rank: int, world: int, dev, stream, path: str, barrier
     # RMSNorm + quantise, gate|up + SiLU, down; final RMSNorm + quantise,
     # heads; then one sampler per CFG pair
     per_fwd = 3 + (7 if f16 else 8) * LM_LAYERS + 2
-    launches = int(sum_over_ranks(float(sum(per_fwd + len(b.pairs) for b in sp.batches))))
+    # one batched sampler launch per batch (V = 1025)
+    launches = int(sum_over_ranks(float(sum(per_fwd + 1 for b in sp.batches))))
     status = ovb.device_status()
     biggest = max(sp.batches, key=lambda b: b.rows) if sp.batches else None
     batches = [{"rows": b.rows, "pairs": len(b.pairs)} for b in sp.batches]

@@ -320,6 +320,26 @@ int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int 
                       float layer_penalty, int mask_id, int32_t* pred, float* scores,
                       void* stream);
 
+/* One CFG pair of ovb_guided_sample_batch: its planes and lengths. */
+typedef struct ovb_guided_pair {
+  const float* cond;
+  int cond_seq;
+  const float* uncond;
+  int uncond_seq;
+  int target_len;
+} ovb_guided_pair;
+
+/* ovb_guided_sample for n_pairs CFG pairs (n_pairs <= 64) with the same
+ * codebooks, vocab, guidance, layer_penalty and mask_id, in one launch when
+ * vocab is 1025 (the LM's audio vocabulary; one launch per pair otherwise):
+ * pair p's [codebooks, target_len] outputs follow pair p - 1's in pred and
+ * scores.  The same values as one ovb_guided_sample per pair.  A serving
+ * loop's TTS step calls it once for all the utterances of a packed forward
+ * (the reference calls LM::CudaSampleFn once per utterance, tts.cpp:278-286). */
+int ovb_guided_sample_batch(int n_pairs, const ovb_guided_pair* pairs, int codebooks, int vocab,
+                            float guidance, float layer_penalty, int mask_id, int32_t* pred,
+                            float* scores, void* stream);
+
 /* One attention segment, as the reference's AttnSegment (cpp/src/model/
  * lm.h:46-51): `rows` query rows starting at element offset q_off of q/out,
  * attending to the `rows` keys / values starting at element offset kv_off of

@@ -42,4 +42,4 @@ from .attention import (  # noqa: F401
     qk_norm_rope_f16,
     rope_table,
 )
-from .sampler import guided_sample  # noqa: F401
+from .sampler import guided_sample, guided_sample_batch  # noqa: F401

@@ -46,6 +46,12 @@ class Ovw1Tensor(C.Structure):
                 ("scales", C.c_void_p), ("n_scales", C.c_int64), ("crc", C.c_uint32)]
 
 
+class GuidedPair(C.Structure):
+    """ovb_guided_pair."""
+    _fields_ = [("cond", C.c_void_p), ("cond_seq", C.c_int), ("uncond", C.c_void_p),
+                ("uncond_seq", C.c_int), ("target_len", C.c_int)]
+
+
 class AttnSegment(C.Structure):
     """ovb_attn_segment (the reference's AttnSegment, cpp/src/model/lm.h:46-51)."""
     _fields_ = [("bias", C.c_void_p), ("rows", C.c_int32), ("q_off", C.c_int64),
@@ -86,6 +92,8 @@ SIGNATURES = {
     "ovb_block_products": ([_i64, _p, _p, _p, _p], _int),
     "ovb_guided_sample": ([_p, _int, _p, _int, _int, _int, _int, C.c_float, C.c_float, _int,
                            _p, _p, _p], _int),
+    "ovb_guided_sample_batch": ([_int, _p, _int, _int, C.c_float, C.c_float, _int, _p, _p, _p],
+                                _int),
     "ovb_ovw1_open": ([C.c_char_p, C.POINTER(_p)], _int),
     "ovb_ovw1_close": ([_p], _int),
     "ovb_ovw1_count": ([_p], _i64),

@@ -1041,6 +1041,53 @@ int ovb_guided_sample(const float* cond, int cond_seq, const float* uncond, int 
   return OVB_OK;
 }
 
+int ovb_guided_sample_batch(int n_pairs, const ovb_guided_pair* pairs, int codebooks, int vocab,
+                            float guidance, float layer_penalty, int mask_id, int32_t* pred,
+                            float* scores, void* stream) {
+  if (n_pairs == 0) return OVB_OK;
+  if (n_pairs < 0 || n_pairs > ovb::kMaxGuidedPairs) return invalid("n_pairs must be in [0, 64]");
+  if (!pairs || !pred || !scores) return invalid("pairs/pred/scores must be non-null");
+  if (codebooks <= 0 || vocab <= 0) return invalid("codebooks and vocab must be positive");
+  if (!aligned(pred, 4) || !aligned(scores, 4)) return invalid("misaligned sampler buffer");
+  ovb::GuidedBatch g = {};
+  int64_t rows = 0;
+  for (int p = 0; p < n_pairs; ++p) {
+    const ovb_guided_pair& x = pairs[p];
+    if (!x.cond || !x.uncond) return invalid("cond/uncond must be non-null");
+    if (x.target_len < 0 || x.cond_seq < x.target_len || x.uncond_seq < x.target_len)
+      return invalid("cond_seq and uncond_seq must be >= target_len >= 0");
+    if (!aligned(x.cond, 4) || !aligned(x.uncond, 4)) return invalid("misaligned sampler buffer");
+    g.cond[p] = x.cond;
+    g.uncond[p] = x.uncond;
+    g.cond_seq[p] = x.cond_seq;
+    g.T[p] = x.target_len;
+    g.out0[p] = rows;
+    rows += static_cast<int64_t>(codebooks) * x.target_len;
+    if (rows > (int64_t{1} << 31) - 1) return invalid("total output rows exceed 2^31-1");
+  }
+  g.out0[n_pairs] = rows;
+  g.n = n_pairs;
+  g.C = codebooks;
+  g.mask_id = mask_id;
+  g.guidance = guidance;
+  g.penalty = layer_penalty;
+  cudaStream_t s = as_stream(stream);
+  if (vocab == 1025) {
+    if (cuda_failed(ovb::launch_guided_sample_batch(g, pred, scores, s), "guided sample launch"))
+      return OVB_ERR_INTERNAL;
+    return OVB_OK;
+  }
+  for (int p = 0; p < n_pairs; ++p) {
+    if (g.T[p] == 0) continue;
+    if (cuda_failed(ovb::launch_guided_sample(g.cond[p], g.cond_seq[p], g.uncond[p], codebooks,
+                                              vocab, g.T[p], guidance, layer_penalty, mask_id,
+                                              pred + g.out0[p], scores + g.out0[p], s),
+                    "guided sample launch"))
+      return OVB_ERR_INTERNAL;
+  }
+  return OVB_OK;
+}
+
 int ovb_attention(const float* q, const float* k, const float* v, float* out, int64_t q_stride,
                   int64_t kv_stride, int n_heads, int n_kv, int head_dim, float scale,
                   const ovb_attn_segment* segs, int n_segs, void* stream) {

@@ -206,6 +206,23 @@ cudaError_t launch_widen_f16(const int8_t* src, int64_t n, uint16_t* dst, cudaSt
 // A kernel whose bounded wait cannot complete (status bit 64 after ~1 s).
 cudaError_t launch_wait_selftest(cudaStream_t s);
 // The guided argmax pass (sampler.cu): one warp per (codebook, frame) row.
+//
+// Up to kMaxGuidedPairs CFG pairs of V = 1025 in one launch: pair p's cond /
+// uncond planes, cond sequence and target lengths, and its first output row
+// out0[p] (out0[n] = all rows).
+constexpr int kMaxGuidedPairs = 64;
+struct GuidedBatch {
+  const float* cond[kMaxGuidedPairs];
+  const float* uncond[kMaxGuidedPairs];
+  int cond_seq[kMaxGuidedPairs];
+  int T[kMaxGuidedPairs];
+  int64_t out0[kMaxGuidedPairs + 1];
+  int n, C, mask_id;
+  float guidance, penalty;
+};
+cudaError_t launch_guided_sample_batch(const GuidedBatch& g, int32_t* pred, float* scores,
+                                       cudaStream_t s);
+// One pair, any V.
 cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
                                  int V, int T, float guidance, float penalty, int mask_id,
                                  int32_t* pred, float* scores, cudaStream_t s);

@@ -178,17 +178,16 @@ __device__ __forceinline__ void finish_row(float (&xc)[kPer], const float (&xu)[
   *idx_out = best_j;
 }
 
-// V = 32 * kFull + kTail known at compile time.
+// Row `row` of one pair's [C, T] output with V = 32 * kFull + kTail known
+// at compile time (one warp).
 template <int kFull, int kTail>
-__global__ void __launch_bounds__(32 * kSampleWarps) guided_sample_fixed_kernel(
-    const float* __restrict__ cond, int cond_seq, const float* __restrict__ uncond, int C, int T,
-    float guidance, float penalty, int mask_id, int32_t* __restrict__ pred,
-    float* __restrict__ scores) {
+__device__ __forceinline__ void fixed_row(const float* __restrict__ cond, int cond_seq,
+                                          const float* __restrict__ uncond, int C, int T,
+                                          int64_t row, float guidance, float penalty, int mask_id,
+                                          int32_t* __restrict__ pred, float* __restrict__ scores) {
   constexpr int kPer = kFull + (kTail > 0 ? 1 : 0);
   constexpr int V = 32 * kFull + kTail;
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kSampleWarps + (threadIdx.x >> 5);
-  if (row >= static_cast<int64_t>(C) * T) return;  // whole warps only
   int c;
   const float *lc, *lu;
   row_ptrs(row, cond, cond_seq, uncond, C, V, T, &c, &lc, &lu);
@@ -215,6 +214,33 @@ __global__ void __launch_bounds__(32 * kSampleWarps) guided_sample_fixed_kernel(
     pred[row] = best_j;
     scores[row] = __fsub_rn(best, __fmul_rn(static_cast<float>(c), penalty));
   }
+}
+
+template <int kFull, int kTail>
+__global__ void __launch_bounds__(32 * kSampleWarps) guided_sample_fixed_kernel(
+    const float* __restrict__ cond, int cond_seq, const float* __restrict__ uncond, int C, int T,
+    float guidance, float penalty, int mask_id, int32_t* __restrict__ pred,
+    float* __restrict__ scores) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kSampleWarps + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(C) * T) return;  // whole warps only
+  fixed_row<kFull, kTail>(cond, cond_seq, uncond, C, T, row, guidance, penalty, mask_id, pred,
+                          scores);
+}
+
+// Several CFG pairs in one launch (the same rows as one launch per pair): the
+// pairs' [C, T_p] outputs are concatenated, pair p's first at g.out0[p]; a
+// warp finds its pair by scanning those offsets.
+template <int kFull, int kTail>
+__global__ void __launch_bounds__(32 * kSampleWarps) guided_sample_batch_kernel(
+    const __grid_constant__ GuidedBatch g, int32_t* __restrict__ pred,
+    float* __restrict__ scores) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kSampleWarps + (threadIdx.x >> 5);
+  if (row >= g.out0[g.n]) return;  // whole warps only
+  int p = 0;
+  for (int i = 1; i < g.n; ++i)
+    if (row >= g.out0[i]) p = i;
+  fixed_row<kFull, kTail>(g.cond[p], g.cond_seq[p], g.uncond[p], g.C, g.T[p], row - g.out0[p],
+                          g.guidance, g.penalty, g.mask_id, pred + g.out0[p], scores + g.out0[p]);
 }
 
 // Any V <= 32 * kPer, bounds-checked per column.
@@ -307,6 +333,15 @@ __global__ void __launch_bounds__(32 * kSampleWarps) guided_sample_any_kernel(
 }
 
 }  // namespace
+
+cudaError_t launch_guided_sample_batch(const GuidedBatch& g, int32_t* pred, float* scores,
+                                       cudaStream_t s) {
+  const int64_t rows = g.out0[g.n];
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((rows + kSampleWarps - 1) / kSampleWarps));
+  return launch_plain(guided_sample_batch_kernel<32, 1>, grid, dim3(32 * kSampleWarps), 0, s, g,
+                      pred, scores);
+}
 
 cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* uncond, int C,
                                  int V, int T, float guidance, float penalty, int mask_id,

@@ -140,16 +140,14 @@ class Batch:
         self.graph = None
 
     def run(self):
-        """Enqueue the forward and the per-pair samplers on the current stream."""
+        """Enqueue the forward and the pairs' samplers (one launch for all the
+        pairs, ovb_guided_sample_batch) on the current stream."""
         lm, C = self.lm, self.lm.C
         logits = lm.forward_segments_device(self.seg_rows, self.ids, self.amask, self.masks,
                                             self.pos)
-        for p in self.pairs:
-            n = C * p.T
-            SP.guided_sample(logits[p.row0:p.row0 + p.S], logits[p.row0 + p.S:p.row0 + 2 * p.S],
-                             p.T, C, GUIDANCE, LAYER_PENALTY, MASK_ID,
-                             self.pred[p.out0:p.out0 + n].view(C, p.T),
-                             self.scores[p.out0:p.out0 + n].view(C, p.T))
+        SP.guided_sample_batch([(logits[p.row0:p.row0 + p.S],
+                                 logits[p.row0 + p.S:p.row0 + 2 * p.S], p.T) for p in self.pairs],
+                               C, GUIDANCE, LAYER_PENALTY, self.pred, self.scores, MASK_ID)
 
     def capture(self, stream: torch.cuda.Stream):
         self.graph = torch.cuda.CUDAGraph()
@@ -201,7 +199,7 @@ class Stepper:
             if mine:
                 m.reserve(max(b.rows for b in mine), max(b.mask_elems for b in mine))
         self.rows_per_step = sum(b.rows for b in self.batches)
-        self.samplers = sum(len(b.pairs) for b in self.batches)
+        self.samplers = sum(len(b.pairs) for b in self.batches)  # pairs sampled per step
 
     def _lanes(self):
         return [(self.streams[k], b) for k, b in zip(self.lane, self.batches)]

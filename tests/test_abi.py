@@ -93,3 +93,23 @@ def test_rope_entry_points_check_arguments_before_the_device():
     assert lib.ovb_linear_h_qk_rope(4, None, None, 16, 8, 128, None, None, 1e-6, None, None,
                                     None, None, None) == L.OVB_ERR_INVALID_ARG
     assert b"null" in lib.ovb_last_error()
+
+
+def test_batched_sampler_checks_arguments_before_the_device():
+    """ovb_guided_sample_batch: zero pairs are a no-op; too many pairs, null
+    buffers and lengths shorter than the target are refused on the host."""
+    lib = L.lib()
+    assert lib.ovb_guided_sample_batch(0, None, 8, 1025, 2.0, 5.0, 1024, None, None,
+                                       None) == L.OVB_OK
+    assert lib.ovb_guided_sample_batch(65, None, 8, 1025, 2.0, 5.0, 1024, None, None,
+                                       None) == L.OVB_ERR_INVALID_ARG
+    pred = C.create_string_buffer(64)
+    pairs = (L.GuidedPair * 1)(L.GuidedPair(None, 10, None, 10, 5))
+    assert lib.ovb_guided_sample_batch(1, pairs, 8, 1025, 2.0, 5.0, 1024, C.addressof(pred),
+                                       C.addressof(pred), None) == L.OVB_ERR_INVALID_ARG
+    assert b"null" in lib.ovb_last_error()
+    buf = C.create_string_buffer(64)
+    pairs = (L.GuidedPair * 1)(L.GuidedPair(C.addressof(buf), 4, C.addressof(buf), 10, 5))
+    assert lib.ovb_guided_sample_batch(1, pairs, 8, 1025, 2.0, 5.0, 1024, C.addressof(pred),
+                                       C.addressof(pred), None) == L.OVB_ERR_INVALID_ARG
+    assert b"target_len" in lib.ovb_last_error()

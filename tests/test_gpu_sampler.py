@@ -112,3 +112,29 @@ def test_guided_sample_arguments(cuda):
     pred, scores = ovb.guided_sample(cond, unc, 0, C, 1.0, 1.0)  # no work
     assert pred.shape == (C, 0)
     assert ovb.device_status() == 0
+
+
+@pytest.mark.parametrize("V", [1025, 300])
+def test_guided_sample_batch_equals_one_call_per_pair(cuda, V):
+    """ovb_guided_sample_batch over ragged pairs (one launch for V = 1025, a
+    loop for other V) writes exactly what one ovb_guided_sample per pair
+    writes, pair after pair."""
+    rng = np.random.default_rng(V)
+    C, g, pen = 8, 2.0, 5.0
+    planes, want_p, want_s = [], [], []
+    for S, T in ((60, 20), (300, 260), (45, 0), (129, 89), (7, 7)):
+        cond = torch.from_numpy((rng.standard_normal((S, C * V)) * 3).astype(np.float32)).to(cuda)
+        unc = torch.from_numpy((rng.standard_normal((S, C * V)) * 3).astype(np.float32)).to(cuda)
+        planes.append((cond, unc, T))
+        p, s = ovb.guided_sample(cond, unc, T, C, g, pen)
+        want_p.append(p.reshape(-1))
+        want_s.append(s.reshape(-1))
+    n = sum(C * T for _, _, T in planes)
+    pred = torch.full((n + 5,), -1, dtype=torch.int32, device=cuda)
+    scores = torch.full((n + 5,), float("nan"), device=cuda)
+    ovb.guided_sample_batch(planes, C, g, pen, pred, scores)
+    assert torch.equal(pred[:n], torch.cat(want_p))
+    assert torch.equal(scores[:n], torch.cat(want_s))
+    assert (pred[n:] == -1).all() and torch.isnan(scores[n:]).all()  # nothing past the outputs
+    with pytest.raises(ValueError):
+        ovb.guided_sample_batch(planes, C, g, pen, pred[: n - 1], scores)
