@@ -233,9 +233,11 @@ int ovb_linear_h(int64_t M, const ovb_weight* w, const void* a16, float* C, int6
 int ovb_linear_h_sliced(int64_t M, const ovb_weight* w, const void* a16, const ovb_slice* slices,
                         int n_slices, void* stream);
 
-/* The RoPE table of `rows` positions (device int64 pos): table [rows, 64] of
- * fp32 (cos, sin) pairs, cos / sin of fl(fl(pos[r]) * inv_freq[i]),
- * inv_freq[i] = (float) theta^(-2i/128) computed on the host as the
+/* The RoPE table of `rows` positions (device int64 pos): table [rows, 128]
+ * fp32, cos / sin of the angles a_i = fl(fl(pos[r]) * inv_freq[i]), i < 64,
+ * a row in 32 groups (cos a_2j, cos a_2j+1, sin a_2j, sin a_2j+1) so that a
+ * kernel rotating two adjacent elements reads its cosines and its sines as
+ * pairs; inv_freq[i] = (float) theta^(-2i/128) computed on the host as the
  * reference does.  The reference tabulates the same per row and keeps it
  * across layers (qk_norm_rope_f32, ops_cpu.cpp:945-986); the device LM
  * builds it once per forward.  head_dim must be 128; table 16-byte aligned. */

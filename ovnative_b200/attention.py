@@ -156,12 +156,13 @@ def attention_h_q(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, segs,
 
 def rope_table(pos: torch.Tensor, theta: float = 1e6) -> torch.Tensor:
     """The RoPE table of int64 positions ``pos`` [rows] (ovb_rope_table):
-    [rows, 64, 2] fp32 (cos, sin) of pos * inv_freq[i], inv_freq[i] =
+    [rows, 32, 2, 2] fp32, ``tab[r, j, 0, u]`` = cos and ``tab[r, j, 1, u]``
+    = sin of angle i = 2j + u, pos * inv_freq[i], inv_freq[i] =
     theta^(-2i/128) rounded to fp32 (qk_norm_rope_f32's table,
     ops_cpu.cpp:945-986)."""
     if not pos.is_cuda or pos.dtype != torch.int64 or not pos.is_contiguous():
         raise ValueError("pos must be a contiguous int64 CUDA tensor")
-    tab = torch.empty((pos.numel(), 64, 2), dtype=torch.float32, device=pos.device)
+    tab = torch.empty((pos.numel(), 32, 2, 2), dtype=torch.float32, device=pos.device)
     L.check(L.lib().ovb_rope_table(pos.data_ptr(), pos.numel(), HEAD_DIM, float(theta),
                                    tab.data_ptr(), torch.cuda.current_stream().cuda_stream))
     return tab
@@ -178,7 +179,7 @@ def qk_norm_rope_f16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm: 
             raise ValueError(f"{name} must be a contiguous float32 CUDA tensor")
     rows = q.shape[0]
     if table.numel() < rows * HEAD_DIM:
-        raise ValueError("table must hold 64 (cos, sin) pairs per row (rope_table)")
+        raise ValueError("table must hold 128 floats per row (rope_table)")
     n_heads, n_kv = q.shape[1] // HEAD_DIM, k.shape[1] // HEAD_DIM
     q16 = torch.empty(q.shape, dtype=torch.float16, device=q.device)
     k16 = torch.empty(k.shape, dtype=torch.float16, device=q.device)

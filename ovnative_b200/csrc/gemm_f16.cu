@@ -492,9 +492,7 @@ __device__ __forceinline__ float f4_at2(const float4 (&v)[2], int e) {
 }
 
 // Two IEEE round-to-nearest products in one packed instruction:
-// (a.x * b.x, a.y * b.y).  Only products are packed: a sum or difference of
-// products stays a scalar add.rn, so no product is ever contracted into a
-// fused multiply-add and every result rounds exactly as the scalar form.
+// (a.x * b.x, a.y * b.y), rounded exactly as the scalar mul.rn.
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   float2 r;
   asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
@@ -502,6 +500,31 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
       : "=f"(r.x), "=f"(r.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return r;
+}
+// (a.x + b.x, a.y + b.y), rounded as add.rn.
+// Only for operands that are not products: ptxas contracts a packed mul.rn
+// followed by a packed add.rn into one packed fma (measured on sm_100a: 16-25 %
+// of such sums then differ from the two-rounding form, even with the product
+// written as fma.rn(a, b, -0)), so a sum or difference of products stays two
+// scalar add.rn / sub.rn, which ptxas leaves alone.
+__device__ __forceinline__ float2 add2rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+// The running magnitude maximum of fp16 pairs: max(|acc|, |w|) per half, a
+// NaN in either giving NaN.  An accumulator whose half has every exponent bit
+// set has seen an fp16 infinity or NaN.
+__device__ __forceinline__ uint32_t absmax_h2(uint32_t acc, uint32_t w) {
+  uint32_t d;
+  asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(w));
+  return d;
+}
+__device__ __forceinline__ bool h2_inf_or_nan(uint32_t acc) {
+  return (acc & 0x7c00u) == 0x7c00u || (acc & 0x7c000000u) == 0x7c000000u;
 }
 
 // Elements e, e + 1 (e even) of an 8-float register pair as a float2.
@@ -520,8 +543,10 @@ __device__ __forceinline__ float2 f4_pair(const float4 (&v)[2], int e) {
 // at distances 16, 8, .., 1, the order of its warp tree), the same scale and
 // rotation -- so the fp16 outputs equal the unfused sequence bit for bit; v
 // heads are converted.  The per-column values (wscale, norm weight) are the
-// same for every lane: they are read as float4 broadcasts; products are
-// packed two per instruction (f32x2), sums stay scalar.  Two passes over
+// same for every lane: they are read as float4 broadcasts; products and the
+// sums of sums are packed two per instruction (f32x2), sums and differences
+// of products stay scalar (add2rn), and an fp16 output's overflow is found
+// from a running magnitude maximum of the packed outputs.  Two passes over
 // TMEM, sixteen columns at a time: the sum of squares, then the rotation of
 // set s (head elements 32s + i with 64 + 32s + i, s = 0, 1), whose 64 fp16
 // outputs are staged in shared memory (32 rows x 128 bytes, 16-byte chunks
@@ -605,13 +630,14 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
         const uint32_t dcol =
             tmem_base + lane_off + static_cast<uint32_t>(d * BN + 128 * eh);
         const bool row_ok = lane < rows;
-        bool bad = false;  // an fp16 output of this row overflowed (or is NaN)
+        uint32_t amax = 0u;  // this row's fp16 outputs' magnitude maximum (absmax_h2)
         const float4* ws4 = reinterpret_cast<const float4*>(colv);
         const float4* nw4 = reinterpret_cast<const float4*>(colv + 128);
         float scale = 0.f;
         if (kind < 2) {
-          // pass 1: s01 = x0^2 + x1^2 (chunks 0 and 1), then + (x2^2 + x3^2)
-          float s01[32];
+          // pass 1: s01 = x0^2 + x1^2 (chunks 0 and 1), then + (x2^2 + x3^2),
+          // element pairs (2i, 2i + 1) in s2[i]
+          float2 s2[16];
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll
@@ -636,20 +662,24 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                                         f4_pair(wa, e));
                   const float2 y = mul2(make_float2(__uint_as_float(vb[iv]), __uint_as_float(vb[iv + 1])),
                                         f4_pair(wb, e));
+                  // a sum of two products stays scalar (add2rn would be
+                  // contracted with the products); sums of sums are packed
                   const float2 xx = mul2(x, x), yy = mul2(y, y);
-                  const float q0 = __fadd_rn(xx.x, yy.x), q1 = __fadd_rn(xx.y, yy.y);
-                  s01[16 * hf + iv] = pr == 0 ? q0 : __fadd_rn(s01[16 * hf + iv], q0);
-                  s01[16 * hf + iv + 1] = pr == 0 ? q1 : __fadd_rn(s01[16 * hf + iv + 1], q1);
+                  const float2 q = make_float2(__fadd_rn(xx.x, yy.x), __fadd_rn(xx.y, yy.y));
+                  const int si = (16 * hf + iv) >> 1;
+                  s2[si] = pr == 0 ? q : add2rn(s2[si], q);
                 }
               }
             }
           }
+          // s[i] += s[i + o] for o = 16, 8, 4, 2 (pairs), then 1
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
+          for (int o = 8; o > 0; o >>= 1) {
 #pragma unroll
-            for (int i = 0; i < o; ++i) s01[i] = __fadd_rn(s01[i], s01[i + o]);
+            for (int i = 0; i < o; ++i) s2[i] = add2rn(s2[i], s2[i + o]);
           }
-          scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s01[0], 128.f), args.rope_eps)));
+          const float s01 = __fadd_rn(s2[0].x, s2[0].y);
+          scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s01, 128.f), args.rope_eps)));
         }
         // The output rows of this head.
         __half* out;
@@ -715,10 +745,10 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                                       f4_pair(wb, e));
                 float2 lo = x, hi = y;
                 if (kind < 2) {
-                  // pairs 8k + e, 8k + e + 1: (cos, sin) of both elements
-                  // (rotation pairs are columns i and 64 + i: lo and hi)
+                  // pairs 8k + e, 8k + e + 1: (cos, cos, sin, sin) of both
+                  // elements (rotation pairs are columns i and 64 + i: lo and hi)
                   const float4 c2 = cs[e >> 1];
-                  const float2 cv = make_float2(c2.x, c2.z), sv = make_float2(c2.y, c2.w);
+                  const float2 cv = make_float2(c2.x, c2.y), sv = make_float2(c2.z, c2.w);
                   const float2 sc = make_float2(scale, scale);
                   const float2 a = mul2(mul2(x, sc), f4_pair(na, e));
                   const float2 b = mul2(mul2(y, sc), f4_pair(nb, e));
@@ -731,9 +761,7 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
                 const __half2 h2 = __floats2half2_rn(hi.x, hi.y);
                 lo_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
                 hi_w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-                // an fp16 output that is infinite or NaN: exponent bits all set
-                bad = bad || __vcmpeq2(lo_w[e >> 1] & 0x7c007c00u, 0x7c007c00u) != 0u ||
-                      __vcmpeq2(hi_w[e >> 1] & 0x7c007c00u, 0x7c007c00u) != 0u;
+                amax = absmax_h2(absmax_h2(amax, lo_w[e >> 1]), hi_w[e >> 1]);
               }
               *reinterpret_cast<uint4*>(st8 + lane * 128 + 16 * (g ^ (lane & 7))) =
                   make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
@@ -754,7 +782,7 @@ __device__ __forceinline__ void epilogue_rope_loop(const GemmArgs& args, uint64_
           }
           __syncwarp();
         }
-        if (row_ok && bad) range_ok = false;  // rows past M hold no outputs
+        if (row_ok && h2_inf_or_nan(amax)) range_ok = false;  // rows past M hold no outputs
       }
     }
     tc_fence_before();

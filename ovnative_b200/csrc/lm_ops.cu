@@ -113,20 +113,31 @@ __global__ void embed_kernel(const int64_t* ids, const uint8_t* mask, const int6
   if (!ok && threadIdx.x == 0) atomicOr(&g_status_lm, kErrLmIndex);
 }
 
-// The RoPE table of a forward: tab[r, i] = (cos(angle), sin(angle)) with
-// angle = fl(fl(pos[r]) * inv_freq[i]) for i < 64, inv_freq[i] = (float)
-// theta^(-2i/D) computed on the host as the reference does.  The reference
-// tabulates the same per row and keeps the table across layers while the
-// positions do not change (qk_norm_rope_f32, ops_cpu.cpp:945-986); here it is
-// built once per forward.  cos / sin are CUDA's (not glibc's): they agree to a
-// few ulps.  One thread per (row, i).
-__global__ void rope_table_kernel(const int64_t* pos, RopeFreq f, int64_t rows, float2* tab) {
+// The RoPE table of a forward: cos and sin of angle_i = fl(fl(pos[r]) *
+// inv_freq[i]) for i < 64, inv_freq[i] = (float) theta^(-2i/D) computed on
+// the host as the reference does.  A row is 128 floats in 32 groups of four,
+// group j = (cos angle_2j, cos angle_2j+1, sin angle_2j, sin angle_2j+1), so
+// that a consumer rotating two adjacent elements reads both cosines and both
+// sines as register pairs (rope_cos_sin).  The reference tabulates the same
+// per row and keeps the table across layers while the positions do not
+// change (qk_norm_rope_f32, ops_cpu.cpp:945-986); here it is built once per
+// forward.  cos / sin are CUDA's (not glibc's): they agree to a few ulps.
+// One thread per (row, i).
+__global__ void rope_table_kernel(const int64_t* pos, RopeFreq f, int64_t rows, float* tab) {
   const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (t >= rows * 64) return;
   const int64_t r = t >> 6;
   const int i = static_cast<int>(t & 63);
   const float angle = __fmul_rn(static_cast<float>(pos[r]), f.inv_freq[i]);
-  tab[t] = make_float2(cosf(angle), sinf(angle));
+  float* g = tab + r * 128 + 4 * (i >> 1) + (i & 1);
+  g[0] = cosf(angle);
+  g[2] = sinf(angle);
+}
+
+// (cos, sin) of angle i of a table row (rope_table_kernel's grouping).
+__device__ __forceinline__ float2 rope_cos_sin(const float* row, int i) {
+  const float* g = row + 4 * (i >> 1) + (i & 1);
+  return make_float2(g[0], g[2]);
 }
 
 // qk_norm_rope_f32 (ops_cpu.cpp:945-1013) for head_dim 128, written as fp16
@@ -142,14 +153,14 @@ __global__ void rope_table_kernel(const int64_t* pos, RopeFreq f, int64_t rows, 
 // rounds to an fp16 infinity (|x| >= 65520) or is NaN sets status bit 16.
 __global__ void qk_norm_rope_f16_kernel(const float* q, const float* k, const float* v,
                                         __half* q16, __half* k16, __half* v16, const float* qw,
-                                        const float* kw, const float2* tab, int64_t rows,
+                                        const float* kw, const float* tab, int64_t rows,
                                         int n_heads, int n_kv, float eps) {
   constexpr int D = 128, half = 64;
   const int64_t r = blockIdx.x;
   if (r >= rows) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = static_cast<int>(blockDim.x >> 5);
-  const float2 cs0 = tab[r * half + lane], cs1 = tab[r * half + lane + 32];
+  const float2 cs0 = rope_cos_sin(tab + r * D, lane), cs1 = rope_cos_sin(tab + r * D, lane + 32);
   bool range_ok = true;
   // Each warp's head vectors (q, then k, then v heads), loaded in groups of
   // four before any of them is reduced, so that their loads are in flight
@@ -232,7 +243,7 @@ cudaError_t launch_rope_table(const int64_t* pos, const RopeFreq& f, int64_t row
                               cudaStream_t s) {
   const int64_t n = rows * 64;
   return launch_plain(rope_table_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256),
-                      0, s, pos, f, rows, reinterpret_cast<float2*>(tab));
+                      0, s, pos, f, rows, tab);
 }
 
 cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float* v, void* q16,
@@ -241,7 +252,7 @@ cudaError_t launch_qk_norm_rope_f16(const float* q, const float* k, const float*
                                     float eps, cudaStream_t s) {
   return launch_plain(qk_norm_rope_f16_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, s,
                       q, k, v, static_cast<__half*>(q16), static_cast<__half*>(k16),
-                      static_cast<__half*>(v16), qw, kw, reinterpret_cast<const float2*>(tab),
+                      static_cast<__half*>(v16), qw, kw, tab,
                       rows, n_heads, n_kv, eps);
 }
 

@@ -141,7 +141,7 @@ struct GemmArgs {
   // [0, rope_qd)) normalised with rope_qw and rotated, the k heads (the next
   // rope_kvd columns) likewise with rope_kw, and the v heads converted, all as
   // fp16 into rope_q16 [M, rope_qd], rope_k16 / rope_v16 [M, rope_kvd];
-  // rope_tab is the RoPE table [M, 64] of (cos, sin).  Head dim 128.
+  // rope_tab is the RoPE table (launch_rope_table) of the M rows.  Head dim 128.
   void* rope_q16;
   void* rope_k16;
   void* rope_v16;
@@ -319,7 +319,8 @@ cudaError_t launch_permute_logits(const float* src, float* dst, int B, int S, in
 struct RopeFreq {
   float inv_freq[64];
 };
-// The RoPE table of `rows` positions: tab [rows, 64] of (cos, sin) fp32 pairs.
+// The RoPE table of `rows` positions: tab [rows, 128] fp32, row r in groups
+// (cos a_2j, cos a_2j+1, sin a_2j, sin a_2j+1) of its angles a_i, j < 32.
 cudaError_t launch_rope_table(const int64_t* pos, const RopeFreq& f, int64_t rows, float* tab,
                               cudaStream_t s);
 // q / k RMSNorm + RoPE written as fp16 (q16, k16) and v converted to fp16

@@ -334,7 +334,7 @@ def linear_h_qk_rope(a16: torch.Tensor, w: Weight, n_heads: int, n_kv: int, q_no
         if not t.is_contiguous():
             raise ValueError("q_norm, k_norm, table and the outputs must be contiguous")
     if table.dtype != torch.float32 or table.numel() < M * 128:
-        raise ValueError("table must be float32 with 64 (cos, sin) pairs per row (rope_table)")
+        raise ValueError("table must be float32 with 128 floats per row (rope_table)")
     q16, k16, v16 = out
     L.check(L.lib().ovb_linear_h_qk_rope(M, w.handle, _dev_ptr(a16), n_heads, n_kv, 128,
                                          _dev_ptr(q_norm), _dev_ptr(k_norm), float(eps),

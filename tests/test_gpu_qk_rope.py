@@ -35,10 +35,17 @@ def host(t):
     return t.cpu().numpy()
 
 
+def cos_sin(tab):
+    """[rows, 64, 2] (cos, sin) per angle from the table's groups of two
+    angles (cos, cos, sin, sin)."""
+    t = np.asarray(tab).reshape(-1, 32, 2, 2)
+    return np.stack([t[:, :, 0, :].reshape(-1, 64), t[:, :, 1, :].reshape(-1, 64)], -1)
+
+
 def test_rope_table_matches_cos_sin_of_the_fp32_angles(cuda):
     rng = np.random.default_rng(1)
     pos = rng.integers(0, 4096, size=777).astype(np.int64)
-    tab = host(ovb.rope_table(torch.from_numpy(pos).to(cuda), THETA))
+    tab = cos_sin(host(ovb.rope_table(torch.from_numpy(pos).to(cuda), THETA)))
     ang = (pos.astype(np.float32)[:, None] * inv_freq()[None, :]).astype(np.float32)
     np.testing.assert_allclose(tab[..., 0], np.cos(ang.astype(np.float64)), rtol=0, atol=2e-6)
     np.testing.assert_allclose(tab[..., 1], np.sin(ang.astype(np.float64)), rtol=0, atol=2e-6)
@@ -68,7 +75,7 @@ def test_unfused_kernel_against_the_reference_formula(cuda):
     d = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     tab = ovb.rope_table(d(pos), THETA)
     q16, k16, v16 = ovb.qk_norm_rope_f16(d(q), d(k), d(v), d(qw), d(kw), EPS, tab)
-    tabh = host(tab)
+    tabh = cos_sin(host(tab))
     for got, x, w, n in ((q16, q, qw, H), (k16, k, kw, KV)):
         want = norm_rope_ref(x.reshape(rows, n, 128), w, tabh).reshape(rows, n * 128)
         g = host(got).astype(np.float64)
