@@ -11,6 +11,10 @@ q|k|v GEMM with it fused into its epilogue (ovb_linear_h_qk_rope).
   q / k / v, then ovb_qk_norm_rope_f16): bit for bit, for the LM's shape and
   for head layouts whose tiles mix q, k and v heads or end on a single head,
   over ragged row counts.
+* Both against a float32 restatement of the kernels' rounding sequence (the
+  sum of squares in the device's warp-tree order, then every product and sum
+  rounded to nearest, as numpy's float32 arithmetic does): bit for bit.  A
+  fused multiply-add anywhere in the device arithmetic shows up here.
 """
 from __future__ import annotations
 
@@ -123,6 +127,54 @@ def test_fused_qkv_gemm_equals_the_unfused_sequence(cuda, monkeypatch, pair, H, 
     got = ovb.linear_h_qk_rope(a16, w, H, KV, qw, kw, EPS, tab)
     for g, e in zip(got, want):
         np.testing.assert_array_equal(host(g).view(np.uint16), host(e).view(np.uint16))
+    assert ovb.device_status() == 0
+    w.close()
+
+
+def norm_rope_f32(x, w, cos, sin):
+    """The kernels' rounding sequence in float32 on x [rows, heads, 128]: lane
+    l's partial sum (x_l^2 + x_{l+32}^2) + (x_{l+64}^2 + x_{l+96}^2), the warp
+    tree over distances 16, 8, 4, 2, 1, scale = 1 / sqrt(sum / 128 + eps),
+    a = (x_i scale) w_i, b = (x_{i+64} scale) w_{i+64}, a cos - b sin and
+    b cos + a sin, each operation rounded to nearest; fp16 round to nearest
+    even."""
+    f = np.float32
+    x = x.astype(f)
+    sq = x * x
+    t = (sq[..., 0:32] + sq[..., 32:64]) + (sq[..., 64:96] + sq[..., 96:128])
+    for o in (16, 8, 4, 2, 1):
+        t = t[..., :o] + t[..., o:2 * o]
+    scale = (f(1) / np.sqrt(t[..., 0] / f(128) + f(EPS))).astype(f)[..., None]
+    a = (x[..., :64] * scale) * w[:64]
+    b = (x[..., 64:] * scale) * w[64:]
+    c, s = cos[:, None, :], sin[:, None, :]
+    return np.concatenate([a * c - b * s, b * c + a * s], -1).astype(np.float16)
+
+
+@pytest.mark.parametrize("M", [77, 3000])
+def test_fused_and_unfused_equal_the_float32_rounding_sequence(cuda, M):
+    H, KV, K = 16, 8, 1024
+    rng = np.random.default_rng(M + 17)
+    w = qkv_weight(rng, H, KV, K)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    x = d(rng.standard_normal((M, K)).astype(np.float32))
+    a16, _ = ovb.rmsnorm_quantize_f32(x, d(np.ones(K, np.float32)), EPS, f16=True)
+    qw_h = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kw_h = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    tab = ovb.rope_table(d(rng.permutation(4096)[:M].astype(np.int64)), THETA)
+    q = torch.empty((M, H * 128), device=cuda)
+    k = torch.empty((M, KV * 128), device=cuda)
+    v = torch.empty((M, KV * 128), device=cuda)
+    ovb.linear_h_sliced(a16, w, [q, k, v])
+    unfused = ovb.qk_norm_rope_f16(q, k, v, d(qw_h), d(kw_h), EPS, tab)
+    fused = ovb.linear_h_qk_rope(a16, w, H, KV, d(qw_h), d(kw_h), EPS, tab)
+    cs = cos_sin(host(tab))
+    for i, (src, wt, n) in enumerate(((q, qw_h, H), (k, kw_h, KV))):
+        want = norm_rope_f32(host(src).reshape(M, n, 128), wt, cs[..., 0], cs[..., 1])
+        want = want.reshape(M, n * 128).view(np.uint16)
+        np.testing.assert_array_equal(host(unfused[i]).view(np.uint16), want)
+        np.testing.assert_array_equal(host(fused[i]).view(np.uint16), want)
+    np.testing.assert_array_equal(host(fused[2]), host(v).astype(np.float16))
     assert ovb.device_status() == 0
     w.close()
 
