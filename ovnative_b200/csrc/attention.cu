@@ -515,7 +515,8 @@ struct AttnHCtl {
   int16_t act[2][kHMaxTiles];  // key tiles with something to attend, in order
   // how each active tile's scores are formed: 0 plain (every key attended and
   // inside the segment), 1 masked (class-1 bits and / or the segment's end),
-  // 2 biased (the segment's fp32 bias, no table)
+  // 2 biased (the segment's fp32 bias, no table); + 4 when the tile has
+  // class-1 mask bits to read
   int8_t kind[2][kHMaxTiles];
 };
 // Arrivals that release a list slot: the watcher warp and the 8 softmax warps.
@@ -668,8 +669,8 @@ __global__ void __launch_bounds__(kHThreads, 1)
         if (on) {
           const int at = n + __popc(m & ((1u << lane) - 1u));
           ctl->act[b][at] = static_cast<int16_t>(j);
-          ctl->kind[b][at] =
-              static_cast<int8_t>(cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > w.S ? 1 : 0));
+          ctl->kind[b][at] = static_cast<int8_t>(
+              (cls == 2 ? 2 : (cls == 1 || j * 128 + 128 > w.S ? 1 : 0)) | (cls == 1 ? 4 : 0));
         }
         n += __popc(m);
       }
@@ -899,6 +900,16 @@ __global__ void __launch_bounds__(kHThreads, 1)
       const bool mine = h < w.nh;
       float m = -INFINITY, mt = -INFINITY, l = 0.f;
       for (int i = 0; i < n_act && mine; ++i, ++tiles) {
+        const int j = ctl->act[b][i];
+        const int key0 = j * 128;
+        const int kind = ctl->kind[b][i] & 3;  // warp-uniform
+        const bool has_bits = (ctl->kind[b][i] & 4) != 0;
+        // this row's mask bits start towards L1 while S is computed
+        const uint4* bits_at =
+            has_bits ? reinterpret_cast<const uint4*>(args.tile_bits) +
+                           (static_cast<int64_t>(sg.tile0 + w.qb * w.nkt + j) * 128 + r)
+                     : nullptr;
+        if (has_bits) asm volatile("prefetch.global.L1 [%0];" ::"l"(bits_at));
         // the warp leaves together: its TMEM accesses are warp-collective
         if (!__all_sync(0xffffffffu, ovb_wait(smem_u32(&ctl->s_full[h]),
                                               static_cast<uint32_t>(tiles) & 1u, abort))) {
@@ -907,9 +918,6 @@ __global__ void __launch_bounds__(kHThreads, 1)
           break;
         }
         tc_fence_after();
-        const int j = ctl->act[b][i];
-        const int key0 = j * 128;
-        const int kind = ctl->kind[b][i];  // warp-uniform
         uint32_t u[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(s_col + static_cast<uint32_t>(c * 32), u[c]);
@@ -932,9 +940,8 @@ __global__ void __launch_bounds__(kHThreads, 1)
           mul = sl2;
         } else {
           uint32_t bw[4];
-          if (args.tile_class && args.tile_class[sg.tile0 + w.qb * w.nkt + j] == 1) {
-            const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(args.tile_bits) +
-                                   (static_cast<int64_t>(sg.tile0 + w.qb * w.nkt + j) * 128 + r));
+          if (has_bits) {
+            const uint4 b4 = __ldg(bits_at);
             bw[0] = b4.x; bw[1] = b4.y; bw[2] = b4.z; bw[3] = b4.w;
           } else {
             bw[0] = bw[1] = bw[2] = bw[3] = 0xffffffffu;
