@@ -1026,6 +1026,66 @@ def shared_checkpoint(rank: int, world: int, dist=None) -> tuple[str, str]:
     return obj[0], obj[1]
 
 
+def cfg_attention_segments(seg_rows: list, dev):
+    """The attention segments of packed CFG pairs (cond: every key attended;
+    uncond: the target slice, then the tail rows seeing themselves,
+    tts.cpp:186-198) over rows of the LM's q / k / v layout, and their tile
+    table."""
+    import torch
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import layer as LY
+    segs, r0, masks = [], 0, []
+    for si, rows in enumerate(seg_rows):
+        mk = np.ones((rows, rows), np.uint8)
+        if si % 2 == 1:
+            T = max(1, rows - 40)
+            mk[:] = 0
+            mk[:T, :T] = 1
+            mk[np.arange(T, rows), np.arange(T, rows)] = 1
+        masks.append(mk.reshape(-1))
+        segs.append((None, rows, r0 * LY.QD, r0 * LY.KVD))
+        r0 += rows
+    return segs, ovb.attention_tiles(seg_rows, torch.from_numpy(np.concatenate(masks)).to(dev))
+
+
+def config4_biggest_batch_segments() -> list:
+    """Segment rows of the largest config-4 batch one GPU runs (its CFG
+    pairs' cond and uncond halves)."""
+    from ovnative_b200 import shard
+    from ovnative_b200 import tts_batch as TB
+    lengths = utterance_lengths()
+    uids = shard.lpt_assign([lengths[i] for i in range(len(lengths))], 1)[0]
+    groups = TB.pack_batches(lengths, uids, MAX_ROWS)
+    g = max(groups, key=lambda g: sum(2 * lengths[u] for u in g))
+    return [lengths[u] for u in g for _ in range(2)]
+
+
+def profile_attention() -> None:
+    """Three launches of the forward's attention (fp16 operands, the CFG
+    masks' tile table, the o projection's quantised input written by the
+    epilogue) over the largest config-4 batch."""
+    import torch
+
+    import ovnative_b200 as ovb
+    from ovnative_b200 import layer as LY
+    dev = torch.device("cuda", 0)
+    seg_rows = config4_biggest_batch_segments()
+    M = sum(seg_rows)
+    segs, tiles = cfg_attention_segments(seg_rows, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1)
+    q = torch.randn((M, LY.QD), device=dev, generator=gen).half()
+    k = torch.randn((M, LY.KVD), device=dev, generator=gen).half()
+    v = torch.randn((M, LY.KVD), device=dev, generator=gen).half()
+    scale = 1.0 / float(np.sqrt(128))
+    for _ in range(3):
+        ovb.attention_h_q(q, k, v, segs, 16, 8, scale, tiles=tiles, f16=True)
+    torch.cuda.synchronize()
+    print(json.dumps({"attention": "config4", "rows": M, "segments": len(seg_rows),
+                      "status": ovb.device_status()}), flush=True)
+
+
 def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
                          n_layers: int = 8) -> dict:
     """Device time per launch of each GEMM and of the attention of a forward
@@ -1098,20 +1158,8 @@ def time_forward_kernels(dev, stream, f16: bool, M: int, seg_rows: list,
         r["traffic"] = load_traffic_config4(name, f16) if M == CONFIG4_BATCH_ROWS else None
         entries.append(r)
     # attention over the batch's segments with the LM's operands: fp16 q / k /
-    # v and the tile table of the CFG masks (cond: all attended; uncond: the
-    # target slice, then the tail rows seeing themselves, tts.cpp:186-198)
-    segs, r0, masks = [], 0, []
-    for si, rows in enumerate(seg_rows):
-        mk = np.ones((rows, rows), np.uint8)
-        if si % 2 == 1:
-            T = max(1, rows - 40)
-            mk[:] = 0
-            mk[:T, :T] = 1
-            mk[np.arange(T, rows), np.arange(T, rows)] = 1
-        masks.append(mk.reshape(-1))
-        segs.append((None, rows, r0 * QD, r0 * KVD))
-        r0 += rows
-    tiles = ovb.attention_tiles(seg_rows, torch.from_numpy(np.concatenate(masks)).to(dev))
+    # v and the tile table of the CFG masks
+    segs, tiles = cfg_attention_segments(seg_rows, dev)
     q16, k16, v16 = q.half(), k.half(), v.half()
     scale = 1.0 / float(np.sqrt(128))
     us = _graph_time_us(stream, lambda i: ovb.attention_h(q16, k16, v16, segs, 16, 8, scale,
@@ -1553,6 +1601,9 @@ def main():
     ap.add_argument("--profile-gemm", choices=["qkv", "o", "gate_up", "down"], default=None,
                     help="run one of the fp16 forward's GEMMs three times at the largest "
                          "config-4 batch of one GPU (15,408 rows; for ncu captures)")
+    ap.add_argument("--profile-attention", action="store_true",
+                    help="run the forward's attention three times over the largest config-4 "
+                         "batch of one GPU (32 segments, 15,408 rows; for ncu captures)")
     ap.add_argument("--sampler-only", action="store_true",
                     help="only time the guided sampler (one plane set, 8 launches; for "
                          "profiling runs) and print its entry")
@@ -1583,6 +1634,9 @@ def main():
             m.close()
         finally:
             shutil.rmtree(tmpdir, ignore_errors=True)
+        return
+    if args.profile_attention:
+        profile_attention()
         return
     if args.profile_gemm:
         profile_gemm(args.profile_gemm)
