@@ -231,6 +231,11 @@ cudaError_t launch_guided_sample(const float* cond, int cond_seq, const float* u
 // same offsets as (column, row) coordinates of the q and k/v tensor maps,
 // and the index of its first 128-row query block in the launch.
 constexpr int kAttMaxSegs = 64;
+// Launches of at most this many attention work items on at most this many
+// CTAs run a host-computed schedule (longest items first, each to the least
+// loaded CTA); larger ones walk the items round-robin.
+constexpr int kAttSchedItems = 2048;
+constexpr int kAttSchedCtas = 256;
 struct AttnSeg {
   const float* bias;  // [rows, rows] additive, or null
   int64_t q_off;      // element offset of the segment's first query row
@@ -288,6 +293,11 @@ struct AttnHArgs {
   int q_mode;
   int q_kb;
   int n_items;        // work items (segment x query block x kv head x head pair)
+  // The host's schedule (sched != 0): CTA b runs items order[cta_first[b] ..
+  // cta_first[b + 1]) in that order; otherwise CTA b runs b, b + grid, ...
+  int sched;
+  uint16_t cta_first[kAttSchedCtas + 1];
+  uint16_t order[kAttSchedItems];
   AttnHSeg segs[kAttMaxSegs];
 };
 // ctas = work items; the kernel runs persistent CTAs over them.
