@@ -1566,6 +1566,7 @@ def profile_gemm(name: str) -> None:
 
 
 def main():
+    global MAX_ROWS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
@@ -1596,6 +1597,8 @@ def main():
     ap.add_argument("--profile-forward", action="store_true",
                     help="build the 28-layer LM and the largest config-4 batch of one GPU and run "
                          "two eager forwards + samplers (for an ncu launch list)")
+    ap.add_argument("--max-rows", type=int, default=MAX_ROWS,
+                    help="rows per packed forward (at most 32 CFG pairs each)")
     ap.add_argument("--lanes", type=int, default=4,
                     help="LM instances per GPU whose batches' forwards run on their own streams")
     ap.add_argument("--profile-gemm", choices=["qkv", "o", "gate_up", "down"], default=None,
@@ -1608,6 +1611,7 @@ def main():
                     help="only time the guided sampler (one plane set, 8 launches; for "
                          "profiling runs) and print its entry")
     args = ap.parse_args()
+    MAX_ROWS = args.max_rows
     if args.profile_forward:
         import shutil
 

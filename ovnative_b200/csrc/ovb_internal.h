@@ -234,7 +234,7 @@ constexpr int kAttMaxSegs = 64;
 // Launches of at most this many attention work items on at most this many
 // CTAs run a host-computed schedule (longest items first, each to the least
 // loaded CTA); larger ones walk the items round-robin.
-constexpr int kAttSchedItems = 2048;
+constexpr int kAttSchedItems = 4096;
 constexpr int kAttSchedCtas = 256;
 struct AttnSeg {
   const float* bias;  // [rows, rows] additive, or null
