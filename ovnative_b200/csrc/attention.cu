@@ -582,9 +582,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 __device__ __forceinline__ HItem decode_item(const AttnHArgs& args, int it) {
-  int si = 0;
-  for (int i = 1; i < args.n_segs; ++i)
-    if (it >= args.segs[i].cta0) si = i;
+  // the last segment whose first item is <= it (cta0 increases with the
+  // index): a binary search, six parameter loads for 64 segments instead of
+  // a scan of all of them
+  int si = 0, hi = args.n_segs - 1;
+  while (si < hi) {
+    const int mid = (si + hi + 1) >> 1;
+    if (args.segs[mid].cta0 <= it) si = mid; else hi = mid - 1;
+  }
   const AttnHSeg& sg = args.segs[si];
   int rem = it - sg.cta0;
   const int pair = rem % args.pairs;
